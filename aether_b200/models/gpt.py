@@ -1,0 +1,153 @@
+"""GPT-style decoder (pre-RMSNorm, RoPE, SwiGLU, untied LM head) for training.
+
+This is the model family of the training benchmark: 24 layers, d_model 2048,
+16 heads, SwiGLU intermediate 5632, vocab 32000, seq 2048, random init
+N(0, 0.02), bf16 compute with fp32 master weights. The reference's trainer
+model (trainer/src/model.rs:200-670: pre-LN, GELU MLP, learned positions,
+tied head) and its GPU Qwen block stage (trainer/src/qwen_stage.rs:48-446:
+RMSNorm, QKV, RoPE, causal SDPA, O, SwiGLU) are the two shapes this class
+covers; ``AetherLMNano`` in ``nano.py`` is the exact CPU trainer model.
+
+One layer, as executed (T = B*S token rows, everything bf16 [T, *]):
+    h   = rmsnorm(x)                       (norm.cu)
+    qkv = h @ Wqkv^T ; rope(q, k)          (tcgen05 GEMM, in-place RoPE)
+    o   = attention(qkv)                   (flash attention, causal)
+    x   = x + o @ Wo^T                     (residual fused in GEMM epilogue)
+    h   = rmsnorm(x)
+    a   = swiglu(h @ Wgu^T)
+    x   = x + a @ Wd^T                     (residual fused)
+and finally loss = CE(rmsnorm(x) @ Wlm^T) with the logits gradient produced in
+the same pass.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..ops import autograd as A
+from ..ops import reference as ref
+from .arena import ParamArena
+
+
+@dataclass
+class GPTConfig:
+    vocab: int = 32000
+    d_model: int = 2048
+    n_layers: int = 24
+    n_heads: int = 16
+    n_kv_heads: int = 16
+    d_ff: int = 5632
+    max_seq: int = 2048
+    rope_theta: float = 10000.0
+    norm_eps: float = 1e-5
+    init_std: float = 0.02
+    tie_embeddings: bool = False
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.n_heads
+
+    @staticmethod
+    def gpt_24l() -> "GPTConfig":
+        return GPTConfig()
+
+    def n_params(self) -> int:
+        d, f, v, L = self.d_model, self.d_ff, self.vocab, self.n_layers
+        qkv = (self.n_heads + 2 * self.n_kv_heads) * self.head_dim * d
+        per = qkv + d * d + 2 * f * d + f * d + 2 * d
+        return L * per + v * d * (1 if self.tie_embeddings else 2) + d
+
+    def flops_per_token(self, seq: int) -> float:
+        """Training FLOPs per token (fwd + bwd = 3x fwd), causal attention counted at half."""
+        d, L = self.d_model, self.n_layers
+        mm = self.n_params() - self.vocab * d * (0 if self.tie_embeddings else 1)  # embedding gather is free
+        attn = 2 * 2 * seq * d * L / 2
+        return 6.0 * mm + 3.0 * attn
+
+
+def gpt_param_specs(cfg: GPTConfig):
+    d, f, v = cfg.d_model, cfg.d_ff, cfg.vocab
+    qkv = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
+    specs = [("tok_emb", (v, d), True)]
+    for i in range(cfg.n_layers):
+        specs += [
+            (f"l{i}.attn_norm", (d,), False),
+            (f"l{i}.wqkv", (qkv, d), True),
+            (f"l{i}.wo", (d, d), True),
+            (f"l{i}.mlp_norm", (d,), False),
+            (f"l{i}.wgu", (2 * f, d), True),
+            (f"l{i}.wd", (d, f), True),
+        ]
+    specs.append(("final_norm", (d,), False))
+    if not cfg.tie_embeddings:
+        specs.append(("lm_head", (v, d), True))
+    return specs
+
+
+class GPT:
+    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.arena = ParamArena(gpt_param_specs(cfg), self.device, pad_multiple=pad_multiple)
+        self.init_weights(seed)
+        cos, sin = ref.rope_tables(cfg.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
+        self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
+        self._pos_cache: dict[tuple, torch.Tensor] = {}
+
+    def init_weights(self, seed: int) -> None:
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        a = self.arena
+        with torch.no_grad():
+            for name, slot in a.slots.items():
+                mv = a.master_view(name)
+                if name.endswith("norm"):
+                    mv.fill_(1.0)
+                else:
+                    # generate in CPU chunks so the sequence is device-independent
+                    t = torch.empty(slot.shape, dtype=torch.float32)
+                    t.normal_(0.0, self.cfg.init_std, generator=g)
+                    mv.copy_(t.to(self.device))
+        a.sync_bf16_from_master()
+
+    def positions(self, B: int, S: int) -> torch.Tensor:
+        key = (B, S)
+        if key not in self._pos_cache:
+            self._pos_cache[key] = torch.arange(S, dtype=torch.int32, device=self.device).repeat(B)
+        return self._pos_cache[key]
+
+    def forward_hidden(self, ids: torch.Tensor) -> torch.Tensor:
+        cfg, a = self.cfg, self.arena
+        B, S = ids.shape
+        Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        scale = 1.0 / math.sqrt(D)
+        pos = self.positions(B, S)
+        x = A.embedding(a["tok_emb"], ids.reshape(-1))  # [T, d]
+        for i in range(cfg.n_layers):
+            h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
+            qkv = A.linear(h, a[f"l{i}.wqkv"])
+            qkv = A.rope_(qkv, pos, self.rope_cos, self.rope_sin, Hq + Hkv, D)
+            o = A.attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True)
+            x = A.linear(o, a[f"l{i}.wo"], residual=x)
+            h = A.rmsnorm(x, a[f"l{i}.mlp_norm"], cfg.norm_eps)
+            gu = A.linear(h, a[f"l{i}.wgu"])
+            act = A.swiglu(gu)
+            x = A.linear(act, a[f"l{i}.wd"], residual=x)
+        return A.rmsnorm(x, a["final_norm"], cfg.norm_eps)
+
+    def loss(self, ids: torch.Tensor, targets: torch.Tensor, loss_scale: float | None = None) -> torch.Tensor:
+        """Sum of per-token CE times loss_scale (default 1/num_tokens = mean)."""
+        h = self.forward_hidden(ids)
+        w = self.arena["tok_emb"] if self.cfg.tie_embeddings else self.arena["lm_head"]
+        if loss_scale is None:
+            loss_scale = 1.0 / targets.numel()
+        return A.lm_head_cross_entropy(h, w, targets.reshape(-1), loss_scale)
+
+    @torch.no_grad()
+    def logits(self, ids: torch.Tensor) -> torch.Tensor:
+        from ..ops import functional as F
+
+        h = self.forward_hidden(ids)
+        w = self.arena["tok_emb"] if self.cfg.tie_embeddings else self.arena["lm_head"]
+        return F.gemm(h, w)

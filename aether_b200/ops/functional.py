@@ -1,0 +1,308 @@
+"""Functional ops. CUDA tensors run the sm_100a kernels of ``aether_b200._C``;
+CPU tensors run the fp32 statements in ``reference`` (and return the same
+dtypes). Outputs are allocated here unless an ``out`` tensor is passed.
+"""
+from __future__ import annotations
+
+import torch
+
+from .._ext import C
+from . import reference as ref
+
+BF16 = torch.bfloat16
+
+
+def _cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+# ------------------------------------------------------------------ GEMM
+def gemm(a, b, *, a_mn=False, b_mn=False, out=None, out_dtype=BF16, bias=None, residual=None, alpha=1.0,
+         accumulate=False, alpha_t=None):
+    """out (+)= alpha * opA(a) @ opB(b)^T (+ bias) (+ residual).
+
+    a: [M, K] (a_mn=False) or [K, M] (a_mn=True); b: [N, K] (b_mn=False) or [K, N] (b_mn=True).
+    alpha_t: optional fp32 device scalar multiplied into alpha without a host sync.
+    """
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    if _cuda(a):
+        C().gemm_bf16(a, b, out, a_mn, b_mn, bias, residual, float(alpha), bool(accumulate), alpha_t)
+        return out
+    if alpha_t is not None:
+        alpha = alpha * float(alpha_t.reshape(-1)[0])
+    r = ref.gemm(a, b, a_mn, b_mn, bias, residual, alpha)
+    if accumulate:
+        out.add_(r.to(out.dtype))
+    else:
+        out.copy_(r.to(out.dtype))
+    return out
+
+
+def linear(x, w, bias=None, residual=None, out=None):
+    """y = x @ w^T (+ bias) (+ residual); x [..., K], w [N, K]."""
+    shp = x.shape
+    x2 = x.reshape(-1, shp[-1])
+    r2 = residual.reshape(-1, w.shape[0]) if residual is not None else None
+    y = gemm(x2, w, bias=bias, residual=r2, out=out)
+    return y.view(*shp[:-1], w.shape[0])
+
+
+# ------------------------------------------------------------------ norms
+def rmsnorm(x, w, eps=1e-6, res=None, want_h=False):
+    """Returns (y, h, rstd): h = x + res (the residual stream) or x."""
+    if _cuda(x):
+        y = torch.empty_like(x)
+        rstd = torch.empty(x.numel() // x.shape[-1], dtype=torch.float32, device=x.device)
+        h = torch.empty_like(x) if res is not None else x
+        C().rmsnorm_fwd(x, res, w, y, h if res is not None else None, rstd, float(eps))
+        return y, h, rstd
+    y, h, rstd = ref.rmsnorm(x, w, eps, res)
+    return y.to(x.dtype), h.to(x.dtype), rstd
+
+
+def rmsnorm_bwd(dy, h, w, rstd, dw_f32, dres=None, accumulate=True):
+    if _cuda(dy):
+        dx = torch.empty_like(dy)
+        C().rmsnorm_bwd(dy, h, w, rstd, dres, dx, dw_f32, bool(accumulate))
+        return dx
+    hf = h.float()
+    xhat = hf * rstd.view(*rstd.shape, 1)
+    g = dy.float() * w.float()
+    d = h.shape[-1]
+    dx = rstd.view(*rstd.shape, 1) * (g - xhat * (g * xhat).sum(-1, keepdim=True) / d)
+    if dres is not None:
+        dx = dx + dres.float()
+    dwp = (dy.float() * xhat).reshape(-1, d).sum(0)
+    if accumulate:
+        dw_f32.add_(dwp.detach())
+    else:
+        dw_f32.copy_(dwp.detach())
+    return dx.detach().to(dy.dtype)
+
+
+def layernorm(x, w, b=None, eps=1e-5, res=None):
+    if _cuda(x):
+        y = torch.empty_like(x)
+        rows = x.numel() // x.shape[-1]
+        mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+        rstd = torch.empty_like(mean)
+        h = torch.empty_like(x) if res is not None else x
+        C().layernorm_fwd(x, res, w, b, y, h if res is not None else None, mean, rstd, float(eps))
+        return y, h, mean, rstd
+    y, h = ref.layernorm(x, w, b, eps, res)
+    hf = h.float()
+    mean = hf.mean(-1).reshape(-1)
+    rstd = torch.rsqrt(hf.var(-1, unbiased=False) + eps).reshape(-1)
+    return y.to(x.dtype), h.to(x.dtype), mean, rstd
+
+
+def layernorm_bwd(dy, h, w, mean, rstd, dw_f32, db_f32, dres=None, accumulate=True):
+    if _cuda(dy):
+        dx = torch.empty_like(dy)
+        C().layernorm_bwd(dy, h, w, mean, rstd, dres, dx, dw_f32, db_f32, bool(accumulate))
+        return dx
+    d = h.shape[-1]
+    hf = h.float().reshape(-1, d)
+    g = dy.float().reshape(-1, d)
+    xh = (hf - mean[:, None]) * rstd[:, None]
+    gw = g * w.float()
+    dx = rstd[:, None] * (gw - gw.mean(-1, keepdim=True) - xh * (gw * xh).mean(-1, keepdim=True))
+    if dres is not None:
+        dx = dx + dres.float().reshape(-1, d)
+    if accumulate:
+        dw_f32.add_((g * xh).sum(0))
+        db_f32.add_(g.sum(0))
+    else:
+        dw_f32.copy_((g * xh).sum(0))
+        db_f32.copy_(g.sum(0))
+    return dx.view_as(dy).to(dy.dtype)
+
+
+def softmax(x, scale=1.0):
+    if _cuda(x):
+        y = torch.empty_like(x)
+        C().softmax_fwd(x, y, float(scale))
+        return y
+    return ref.softmax(x, scale).to(x.dtype)
+
+
+def softmax_bwd(y, dy, scale=1.0):
+    if _cuda(y):
+        dx = torch.empty_like(dy)
+        C().softmax_bwd(y, dy, dx, float(scale))
+        return dx
+    yf, g = y.float(), dy.float()
+    return (scale * yf * (g - (yf * g).sum(-1, keepdim=True))).to(dy.dtype)
+
+
+# ------------------------------------------------------------------ activations
+def swiglu(h):
+    F_ = h.shape[-1] // 2
+    if _cuda(h):
+        act = torch.empty(*h.shape[:-1], F_, dtype=h.dtype, device=h.device)
+        C().swiglu_fwd(h, act)
+        return act
+    return ref.swiglu(h).to(h.dtype)
+
+
+def swiglu_bwd(h, dact):
+    if _cuda(h):
+        dh = torch.empty(*dact.shape[:-1], 2 * dact.shape[-1], dtype=h.dtype, device=h.device)
+        C().swiglu_bwd(h, dact, dh)
+        return dh
+    g, u = h.float().chunk(2, dim=-1)
+    s = torch.sigmoid(g)
+    da = dact.float()
+    dg = da * u * s * (1 + g * (1 - s))
+    du = da * g * s
+    return torch.cat([dg, du], dim=-1).to(h.dtype)
+
+
+def gelu(x):
+    if _cuda(x):
+        y = torch.empty_like(x)
+        C().gelu_fwd(x, y)
+        return y
+    return ref.gelu_tanh(x).to(x.dtype)
+
+
+def gelu_bwd(x, dy):
+    if _cuda(x):
+        dx = torch.empty_like(x)
+        C().gelu_bwd(x, dy, dx)
+        return dx
+    with torch.enable_grad():
+        xf = x.detach().float().requires_grad_(True)
+        y = ref.gelu_tanh(xf)
+        (g,) = torch.autograd.grad(y, xf, dy.float())
+    return g.to(x.dtype)
+
+
+# ------------------------------------------------------------------ RoPE
+def rope_(x2d, pos, cos_t, sin_t, n_heads, head_dim, inverse=False):
+    """In-place half-split RoPE on heads [0, n_heads) of each row of x2d [T, row]."""
+    if _cuda(x2d):
+        C().rope_apply(x2d, pos, cos_t, sin_t, int(n_heads), int(head_dim), bool(inverse))
+        return x2d
+    y = ref.rope(x2d, pos, cos_t, sin_t, n_heads, head_dim, inverse)
+    x2d.copy_(y.to(x2d.dtype))
+    return x2d
+
+
+# ------------------------------------------------------------------ embedding
+def embedding(table, ids):
+    if _cuda(table):
+        out = torch.empty(*ids.shape, table.shape[1], dtype=table.dtype, device=table.device)
+        C().embedding_fwd(table, ids.long(), out.view(-1, table.shape[1]))
+        return out
+    return table[ids.long().clamp(0, table.shape[0] - 1)]
+
+
+def embedding_bwd(dy, ids, dtable_f32):
+    if _cuda(dy):
+        C().embedding_bwd(dy.reshape(-1, dy.shape[-1]).contiguous(), ids.long().reshape(-1), dtable_f32)
+        return
+    dtable_f32.index_add_(0, ids.long().reshape(-1), dy.reshape(-1, dy.shape[-1]).float())
+
+
+# ------------------------------------------------------------------ loss
+def cross_entropy_fused(logits, targets, *, grad_scale=None, scale_tensor=None, ignore_index=-100,
+                        write_grad=True, grad_out=None):
+    """Loss per row [T] fp32; when write_grad, the logits buffer is overwritten
+    in place with (softmax - onehot) * grad_scale (or written to grad_out)."""
+    T = logits.shape[0]
+    if _cuda(logits):
+        loss = torch.empty(T, dtype=torch.float32, device=logits.device)
+        lse = torch.empty(T, dtype=torch.float32, device=logits.device)
+        d = None
+        if write_grad:
+            d = logits if grad_out is None else grad_out
+        C().cross_entropy_fused(logits, targets.long().contiguous(), loss, lse, d, scale_tensor,
+                                float(grad_scale if grad_scale is not None else 1.0), int(ignore_index))
+        return loss, lse
+    loss, lse = ref.cross_entropy(logits, targets.long(), ignore_index)
+    if write_grad:
+        s = float(grad_scale if grad_scale is not None else 1.0)
+        if scale_tensor is not None:
+            s = s * float(scale_tensor.reshape(-1)[0])
+        g = ref.cross_entropy_grad(logits, targets.long(), s, ignore_index)
+        (logits if grad_out is None else grad_out).copy_(g.to(logits.dtype))
+    return loss, lse
+
+
+def argmax(x):
+    if _cuda(x):
+        out = torch.empty(x.shape[0], dtype=torch.long, device=x.device)
+        C().argmax_rows(x, out)
+        return out
+    return x.float().argmax(-1)
+
+
+# ------------------------------------------------------------------ attention
+def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=True):
+    """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] (strided views ok) -> (o [B,Sq,Hq,D], lse [B,Hq,Sq])."""
+    B, Sq, Hq, D = q.shape
+    if _cuda(q):
+        o = out if out is not None else torch.empty(B, Sq, Hq, D, dtype=q.dtype, device=q.device)
+        lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if want_lse else None
+        C().attention_fwd(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset))
+        return o, lse
+    o, lse = ref.attention(q, k, v, scale, causal, causal_offset)
+    o = o.to(q.dtype)
+    if out is not None:
+        out.copy_(o)
+        o = out
+    return o, lse
+
+
+def attention_bwd(q, k, v, o, do, lse, scale, causal=True, causal_offset=0, dq=None, dk=None, dv=None):
+    if _cuda(q):
+        dq = dq if dq is not None else torch.empty_like(q)
+        dk = dk if dk is not None else torch.empty(k.shape, dtype=k.dtype, device=k.device)
+        dv = dv if dv is not None else torch.empty(v.shape, dtype=v.dtype, device=v.device)
+        C().attention_bwd(q, k, v, o, do, lse, dq, dk, dv, float(scale), bool(causal), int(causal_offset))
+        return dq, dk, dv
+    with torch.enable_grad():
+        qf = q.detach().float().requires_grad_(True)
+        kf = k.detach().float().requires_grad_(True)
+        vf = v.detach().float().requires_grad_(True)
+        of, _ = ref.attention(qf, kf, vf, scale, causal, causal_offset)
+        gq, gk, gv = torch.autograd.grad(of, (qf, kf, vf), do.float())
+    res = []
+    for g, buf, like in ((gq, dq, q), (gk, dk, k), (gv, dv, v)):
+        if buf is not None:
+            buf.copy_(g.to(buf.dtype))
+            res.append(buf)
+        else:
+            res.append(g.to(like.dtype))
+    return tuple(res)
+
+
+# ------------------------------------------------------------------ optimiser
+def adamw_(p, g, m, v, p_bf16=None, *, lr, beta1=0.9, beta2=0.95, eps=1e-8, wd=0.0, step=1, gscale=1.0,
+           gscale_tensor=None):
+    if _cuda(p):
+        C().adamw_step(p, g, m, v, p_bf16, float(lr), float(beta1), float(beta2), float(eps), float(wd), int(step),
+                       float(gscale), gscale_tensor)
+        return p
+    s = gscale * (float(gscale_tensor.reshape(-1)[0]) if gscale_tensor is not None else 1.0)
+    ref.adamw(p, g, m, v, lr, beta1, beta2, eps, wd, step, s)
+    if p_bf16 is not None:
+        p_bf16.copy_(p.to(p_bf16.dtype))
+    return p
+
+
+def grad_norm(g, pre_scale=1.0, max_norm=0.0):
+    """Returns (norm[1], clip_coef[1]) as device tensors (no host sync)."""
+    norm = torch.empty(1, dtype=torch.float32, device=g.device)
+    clip = torch.empty(1, dtype=torch.float32, device=g.device)
+    if _cuda(g):
+        C().grad_norm(g, norm, clip, float(pre_scale), float(max_norm))
+        return norm, clip
+    n = g.float().norm() * pre_scale
+    norm.fill_(float(n))
+    clip.fill_(min(1.0, max_norm / (float(n) + 1e-6)) if max_norm > 0 else 1.0)
+    return norm, clip

@@ -1,0 +1,79 @@
+// pybind11 module `aether_b200._C`: every sm_100a kernel entry point.
+#include <torch/extension.h>
+
+#include "host_utils.h"
+
+namespace aether {
+// gemm_sm100.cu
+void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn, std::optional<at::Tensor> bias,
+               std::optional<at::Tensor> residual, double alpha, bool accumulate, std::optional<at::Tensor> alpha_t);
+// norm.cu
+void rmsnorm_fwd(at::Tensor x, std::optional<at::Tensor> res, at::Tensor w, at::Tensor y,
+                 std::optional<at::Tensor> h_out, std::optional<at::Tensor> rstd, double eps);
+void rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, std::optional<at::Tensor> dres,
+                 at::Tensor dx, at::Tensor dw_f32, bool accumulate);
+void layernorm_fwd(at::Tensor x, std::optional<at::Tensor> res, at::Tensor w, std::optional<at::Tensor> b,
+                   at::Tensor y, std::optional<at::Tensor> h_out, at::Tensor mean, at::Tensor rstd, double eps);
+void layernorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor mean, at::Tensor rstd,
+                   std::optional<at::Tensor> dres, at::Tensor dx, at::Tensor dw_f32, at::Tensor db_f32,
+                   bool accumulate);
+void softmax_fwd(at::Tensor x, at::Tensor y, double scale);
+void softmax_bwd(at::Tensor y, at::Tensor dy, at::Tensor dx, double scale);
+// elementwise.cu
+void swiglu_fwd(at::Tensor h, at::Tensor act);
+void swiglu_bwd(at::Tensor h, at::Tensor dact, at::Tensor dh);
+void gelu_fwd(at::Tensor x, at::Tensor y);
+void gelu_bwd(at::Tensor x, at::Tensor dy, at::Tensor dx);
+void rope_apply(at::Tensor x, at::Tensor pos, at::Tensor cos_t, at::Tensor sin_t, int64_t n_heads, int64_t head_dim,
+                bool inverse);
+void embedding_fwd(at::Tensor table, at::Tensor ids, at::Tensor out);
+void embedding_bwd(at::Tensor dy, at::Tensor ids, at::Tensor dtable_f32);
+// loss.cu
+void cross_entropy_fused(at::Tensor logits, at::Tensor targets, at::Tensor loss, std::optional<at::Tensor> lse,
+                         std::optional<at::Tensor> dlogits, std::optional<at::Tensor> scale_t, double scale,
+                         int64_t ignore_index);
+void argmax_rows(at::Tensor x, at::Tensor out);
+// optim.cu
+void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, std::optional<at::Tensor> p_bf16, double lr,
+                double beta1, double beta2, double eps, double wd, int64_t step, double gscale,
+                std::optional<at::Tensor> gscale_t);
+void sgd_step(at::Tensor p, at::Tensor g, std::optional<at::Tensor> buf, std::optional<at::Tensor> p_bf16, double lr,
+              double momentum, double wd, double gscale, std::optional<at::Tensor> gscale_t);
+void grad_norm(at::Tensor g, at::Tensor norm_out, std::optional<at::Tensor> clip_out, double pre_scale,
+               double max_norm);
+// attention.cu
+void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
+                   double scale, bool causal, int64_t causal_offset);
+void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
+                   at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset);
+}  // namespace aether
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  using namespace pybind11::literals;
+  m.doc() = "aether_b200 sm_100a kernels";
+  m.def("gemm_bf16", &aether::gemm_bf16, "a"_a, "b"_a, "out"_a, "a_mn"_a, "b_mn"_a, "bias"_a = pybind11::none(),
+        "residual"_a = pybind11::none(), "alpha"_a = 1.0, "accumulate"_a = false,
+        "alpha_t"_a = pybind11::none());
+  m.def("rmsnorm_fwd", &aether::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &aether::rmsnorm_bwd);
+  m.def("layernorm_fwd", &aether::layernorm_fwd);
+  m.def("layernorm_bwd", &aether::layernorm_bwd);
+  m.def("softmax_fwd", &aether::softmax_fwd);
+  m.def("softmax_bwd", &aether::softmax_bwd);
+  m.def("swiglu_fwd", &aether::swiglu_fwd);
+  m.def("swiglu_bwd", &aether::swiglu_bwd);
+  m.def("gelu_fwd", &aether::gelu_fwd);
+  m.def("gelu_bwd", &aether::gelu_bwd);
+  m.def("rope_apply", &aether::rope_apply);
+  m.def("embedding_fwd", &aether::embedding_fwd);
+  m.def("embedding_bwd", &aether::embedding_bwd);
+  m.def("cross_entropy_fused", &aether::cross_entropy_fused);
+  m.def("argmax_rows", &aether::argmax_rows);
+  m.def("adamw_step", &aether::adamw_step);
+  m.def("sgd_step", &aether::sgd_step);
+  m.def("grad_norm", &aether::grad_norm);
+  m.def("attention_fwd", &aether::attention_fwd);
+  m.def("attention_bwd", &aether::attention_bwd);
+  m.def("read_and_clear_status", &aether::read_and_clear_status,
+        "Returns (and clears) the device status word set by kernels whose bounded waits expired");
+}

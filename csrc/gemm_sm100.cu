@@ -1,0 +1,404 @@
+// Persistent, warp-specialised bf16 GEMM on the sm_100a tensor cores.
+//
+//   C[M,N] = alpha * opA(A)[M,K] . opB(B)[N,K]^T  (+ bias[N]) (+ residual[M,N])
+//
+// Replaces the reference's cuBLAS sgemm family (runtime/src/cuda.rs:7419-7760,
+// aether_op_matmul_f32_cuda / _tn_ / _nt_ / backward_lhs / backward_rhs): the
+// three training layouts (forward x.W^T, dgrad dy.W, wgrad dy^T.x) are one
+// kernel whose A/B operands are either K-major or MN-major in shared memory,
+// so no transpose kernel ever runs.
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      : TMA producer -- 128B-swizzled tiles into a 4-stage ring
+//   warp 1      : TMEM allocator + MMA issuer (one thread, tcgen05.mma M128 N256 K16)
+//   warps 2..5  : epilogue -- tcgen05.ld of the fp32 accumulator, fused bias /
+//                 residual / scale, bf16 or fp32 (optionally accumulating) stores
+// Two 128x256 fp32 accumulators (all 512 TMEM columns) let the epilogue of tile
+// i overlap the main loop of tile i+1.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <ATen/ATen.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace aether {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int kGroupM = 16;  // tile raster: groups of 16 M-tiles sweep N together (L2 reuse)
+
+enum OutMode : int { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACCUM = 2 };
+
+struct Params {
+  void* out;
+  int64_t ldo;
+  const __nv_bfloat16* bias;      // [N] or null
+  const __nv_bfloat16* residual;  // [M, N] (row stride ldr) or null
+  int64_t ldr;
+  int M, N, K;
+  float alpha;
+  const float* alpha_ptr;  // optional device scalar multiplied into alpha
+  int* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
+  const int per_group = kGroupM * num_n;
+  const int g = t / per_group;
+  const int first_m = g * kGroupM;
+  const int gsize = min(num_m - first_m, kGroupM);
+  const int r = t - g * per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+template <bool A_MN, bool B_MN, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_word)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, tm * BM);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], tm * BM + j * 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, tn * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], tn * BN + j * 64, kb * BK);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutProducer);
+        // Let the copies already in flight land before the CTA exits.
+        volatile int never = 0;
+        const uint32_t n_back = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
+        for (uint32_t j = 1; j <= n_back; ++j) {
+          const uint32_t i = issued - j;
+          mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_word)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? sdesc_sw128(a_base + kk * 2048, 8192, 1024) : sdesc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? sdesc_sw128(b_base + kk * 2048, 8192, 1024) : sdesc_sw128(b_base + kk * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutMma);
+      }
+      // Drain: every MMA this thread issued has completed before TMEM is freed.
+      volatile int never = 0;
+      umma_commit(drain);
+      mbar_wait(drain, 0, &never);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const float alpha = p.alpha * (p.alpha_ptr != nullptr ? *p.alpha_ptr : 1.f);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_word)) {
+        *abort_word = 1;
+        if (lane == 0) atomicExch(p.status, kStatusTimeoutEpilogue);
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const int m = tm * BM + row;
+      const bool row_ok = m < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = tn * BN + c * 32;
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c * 32, r);
+        tmem_ld_wait();
+        if (!row_ok || n0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+        if (p.bias != nullptr) {
+          const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (n0 + q * 8 < p.N) {
+              uint4 b = bp[q];
+              v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
+              v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
+              v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
+              v[q * 8 + 6] += bf16lo(b.w); v[q * 8 + 7] += bf16hi(b.w);
+            }
+          }
+        }
+        if (p.residual != nullptr) {
+          const uint4* rp = reinterpret_cast<const uint4*>(p.residual + (int64_t)m * p.ldr + n0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (n0 + q * 8 < p.N) {
+              uint4 b = rp[q];
+              v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
+              v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
+              v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
+              v[q * 8 + 6] += bf16lo(b.w); v[q * 8 + 7] += bf16hi(b.w);
+            }
+          }
+        }
+        if constexpr (OUT == OUT_BF16) {
+          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)m * p.ldo + n0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (n0 + q * 8 < p.N) {
+              uint4 o;
+              o.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+              o.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+              o.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+              o.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+              op[q] = o;
+            }
+          }
+        } else {
+          float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + (int64_t)m * p.ldo + n0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (n0 + q * 4 < p.N) {
+              float4 o = make_float4(v[q * 4 + 0], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+              if constexpr (OUT == OUT_F32_ACCUM) {
+                const float4 prev = op[q];
+                o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
+              }
+              op[q] = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <bool A_MN, bool B_MN, int OUT>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t stream) {
+  auto kern = gemm_bf16_kernel<A_MN, B_MN, OUT>;
+  static bool attr_set[64] = {false};
+  const int dev = current_device();
+  if (!attr_set[dev]) {
+    AETHER_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int num_tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = std::min(num_tiles, num_sms(dev));
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  AETHER_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace gemm
+
+// Python-facing entry: out (+)= alpha * opA(a) . opB(b)^T (+ bias) (+ residual).
+//   a_mn == false: a is [M, K] (row stride a.stride(0));  true: a is [K, M].
+//   b_mn == false: b is [N, K];                          true: b is [K, N].
+// out is bf16 [M, N] or fp32 [M, N]; `accumulate` (fp32 only) adds into out.
+// alpha_t (optional CUDA fp32 scalar) multiplies alpha on the device (no host sync).
+void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn,
+               std::optional<at::Tensor> bias, std::optional<at::Tensor> residual, double alpha,
+               bool accumulate, std::optional<at::Tensor> alpha_t) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm_bf16: CUDA tensors required");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm_bf16: 2-D operands");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm_bf16: inner dim must be contiguous");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm_bf16: out shape mismatch");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && (!a_mn || M % 8 == 0), "gemm_bf16: dims must be multiples of 8");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_bf16: row strides must be 16B multiples");
+  TORCH_CHECK(out.stride(0) % 8 == 0, "gemm_bf16: out row stride must be a multiple of 8 elements");
+  TORCH_CHECK(M > 0 && N > 0 && K > 0, "gemm_bf16: empty problem");
+  const bool out_f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(out_f32 || out.scalar_type() == at::kBFloat16, "gemm_bf16: out must be bf16 or fp32");
+  TORCH_CHECK(!accumulate || out_f32, "gemm_bf16: accumulate requires an fp32 output");
+  c10::cuda::CUDAGuard guard(a.device());
+
+  gemm::Params p{};
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.alpha = (float)alpha;
+  p.status = device_status_word();
+  if (alpha_t && alpha_t->defined()) {
+    TORCH_CHECK(alpha_t->is_cuda() && alpha_t->scalar_type() == at::kFloat && alpha_t->numel() >= 1, "gemm_bf16: alpha_t must be a CUDA fp32 scalar");
+    p.alpha_ptr = alpha_t->data_ptr<float>();
+  }
+  if (bias && bias->defined()) {
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N && bias->is_contiguous(), "gemm_bf16: bias must be bf16 [N]");
+    p.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (residual && residual->defined()) {
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->size(0) == M && residual->size(1) == N &&
+                    residual->stride(1) == 1 && residual->stride(0) % 8 == 0,
+                "gemm_bf16: residual must be bf16 [M, N]");
+    p.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    p.ldr = residual->stride(0);
+  }
+
+  CUtensorMap ta, tb;
+  if (!a_mn) ta = make_tmap_2d_bf16(a.data_ptr(), K, M, a.stride(0) * 2, gemm::BK, gemm::BM);
+  else ta = make_tmap_2d_bf16(a.data_ptr(), M, K, a.stride(0) * 2, 64, gemm::BK);
+  if (!b_mn) tb = make_tmap_2d_bf16(b.data_ptr(), K, N, b.stride(0) * 2, gemm::BK, gemm::BN);
+  else tb = make_tmap_2d_bf16(b.data_ptr(), N, K, b.stride(0) * 2, 64, gemm::BK);
+
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int mode = accumulate ? gemm::OUT_F32_ACCUM : (out_f32 ? gemm::OUT_F32 : gemm::OUT_BF16);
+#define AETHER_GEMM_CASE(AM, BMN, OM)                                         \
+  if (a_mn == AM && b_mn == BMN && mode == OM) {                              \
+    gemm::launch<AM, BMN, OM>(ta, tb, p, stream);                             \
+    return;                                                                   \
+  }
+  AETHER_GEMM_CASE(false, false, gemm::OUT_BF16)
+  AETHER_GEMM_CASE(false, false, gemm::OUT_F32)
+  AETHER_GEMM_CASE(false, false, gemm::OUT_F32_ACCUM)
+  AETHER_GEMM_CASE(false, true, gemm::OUT_BF16)
+  AETHER_GEMM_CASE(false, true, gemm::OUT_F32)
+  AETHER_GEMM_CASE(false, true, gemm::OUT_F32_ACCUM)
+  AETHER_GEMM_CASE(true, true, gemm::OUT_BF16)
+  AETHER_GEMM_CASE(true, true, gemm::OUT_F32)
+  AETHER_GEMM_CASE(true, true, gemm::OUT_F32_ACCUM)
+  AETHER_GEMM_CASE(true, false, gemm::OUT_BF16)
+  AETHER_GEMM_CASE(true, false, gemm::OUT_F32)
+  AETHER_GEMM_CASE(true, false, gemm::OUT_F32_ACCUM)
+#undef AETHER_GEMM_CASE
+  TORCH_CHECK(false, "gemm_bf16: unsupported configuration");
+}
+
+}  // namespace aether
