@@ -67,8 +67,21 @@ int read_and_clear_status() {
   return v;
 }
 
+// Driver calls (tensor-map encoding) need a context current on the calling
+// thread. Threads that have not made a runtime call yet (autograd's device
+// worker, for one) have none, so bind the runtime's primary context once per
+// thread.
+static void ensure_context_bound() {
+  thread_local bool bound = false;
+  if (!bound) {
+    AETHER_CUDA_CHECK(cudaFree(nullptr));
+    bound = true;
+  }
+}
+
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer) {
+  ensure_context_bound();
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
   if (row_stride_bytes % 16 != 0) throw std::runtime_error("TMA row stride must be a multiple of 16 bytes");
   CUtensorMap m;
@@ -85,6 +98,7 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, 
 
 CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t inner, uint64_t mid, uint64_t outer, uint64_t mid_stride_bytes,
                               uint64_t outer_stride_bytes, uint32_t box_inner, uint32_t box_mid, uint32_t box_outer) {
+  ensure_context_bound();
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
   if (mid_stride_bytes % 16 != 0 || outer_stride_bytes % 16 != 0)
     throw std::runtime_error("TMA strides must be multiples of 16 bytes");

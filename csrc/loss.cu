@@ -47,7 +47,9 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const __nv_bf
                                                                     float scale, int ignore_index) {
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* x = logits + row * ld;
-  const int nchunk = V / 8;
+  // 16-byte vector path only when every row (and the gradient row) starts aligned.
+  const bool vec = ((ld & 7) == 0) && (dlogits == nullptr || (ldd & 7) == 0);
+  const int nchunk = vec ? V / 8 : 0;
   const int64_t tgt = targets[row];
   const bool valid = tgt != ignore_index && tgt >= 0 && tgt < V;
   // Read the target logit before any thread can overwrite the row in pass 2.
@@ -188,7 +190,6 @@ void cross_entropy_fused(at::Tensor logits, at::Tensor targets, at::Tensor loss,
                          std::optional<at::Tensor> dlogits, std::optional<at::Tensor> scale_t, double scale,
                          int64_t ignore_index) {
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.scalar_type() == at::kBFloat16, "ce: logits [T, V] bf16");
-  TORCH_CHECK(logits.stride(0) % 8 == 0, "ce: row stride % 8");
   TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous(), "ce: targets int64");
   const int64_t T = logits.size(0);
   const int V = (int)logits.size(1);
@@ -196,7 +197,7 @@ void cross_entropy_fused(at::Tensor logits, at::Tensor targets, at::Tensor loss,
   __nv_bfloat16* dptr = nullptr;
   int64_t ldd = 0;
   if (dlogits && dlogits->defined()) {
-    TORCH_CHECK(dlogits->stride(1) == 1 && dlogits->stride(0) % 8 == 0 && dlogits->size(0) == T, "ce: dlogits layout");
+    TORCH_CHECK(dlogits->stride(1) == 1 && dlogits->size(0) == T, "ce: dlogits layout");
     dptr = reinterpret_cast<__nv_bfloat16*>(dlogits->data_ptr());
     ldd = dlogits->stride(0);
   }
