@@ -12,7 +12,10 @@
 //   warp 0      : TMA producer -- 128B-swizzled tiles into a 4-stage ring
 //   warp 1      : TMEM allocator + MMA issuer (one thread, tcgen05.mma M128 N256 K16)
 //   warps 2..5  : epilogue -- tcgen05.ld of the fp32 accumulator, fused bias /
-//                 residual / scale, bf16 or fp32 (optionally accumulating) stores
+//                 residual / scale, staged through 128B-swizzled shared memory
+//                 and written by TMA bulk-tensor stores; fp32 gradient
+//                 accumulation uses the TMA reduce-add (the L2 adds, the SM
+//                 never reads the old value)
 // Two 128x256 fp32 accumulators (all 512 TMEM columns) let the epilogue of tile
 // i overlap the main loop of tile i+1.
 #include <ATen/cuda/CUDAContext.h>
@@ -34,7 +37,9 @@ constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
-constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int kStageBytes = 32 * 128;          // one epilogue warp's 32-row x 128-byte output slab
+constexpr int kStageTotal = 4 * 2 * kStageBytes;  // 4 epilogue warps, double-buffered
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + kStageTotal + 1024 /*align slack*/ + 256 /*barriers*/;
 constexpr int kGroupM = 16;  // tile raster: groups of 16 M-tiles sweep N together (L2 reuse)
 
 enum OutMode : int { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACCUM = 2 };
@@ -63,12 +68,14 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
 
 template <bool A_MN, bool B_MN, int OUT>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sStage = sB + STAGES * B_BYTES;  // 4 warps x 2 buffers x 32 rows x 128 B
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStage + kStageTotal);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -97,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -211,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const float alpha = p.alpha * (p.alpha_ptr != nullptr ? *p.alpha_ptr : 1.f);
+    uint32_t stage_ctr = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -225,22 +234,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = tm * BM + row;
       const bool row_ok = m < p.M;
+      const int m_warp = tm * BM + quad * 32;  // first output row of this warp's slab
+      // Output chunks are 128 bytes wide per row: 32 fp32 or 64 bf16 columns.
+      constexpr int CW = (OUT == OUT_BF16) ? 64 : 32;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n0 = tn * BN + c * 32;
-        uint32_t r[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c * 32, r);
-        tmem_ld_wait();
-        if (!row_ok || n0 >= p.N) continue;
-        float v[32];
+      for (int c = 0; c < BN / CW; ++c) {
+        const int n0 = tn * BN + c * CW;
+        float v[CW];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+        for (int h = 0; h < CW / 32; ++h) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c * CW + h * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[h * 32 + j] = __uint_as_float(r[j]) * alpha;
+        }
+        if (n0 >= p.N) continue;  // whole chunk beyond N (warp-uniform)
         if (p.bias != nullptr) {
           const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < CW / 8; ++q) {
             if (n0 + q * 8 < p.N) {
-              uint4 b = bp[q];
+              const uint4 b = bp[q];
               v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
               v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
               v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
@@ -248,12 +263,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (p.residual != nullptr) {
+        if (p.residual != nullptr && row_ok) {
           const uint4* rp = reinterpret_cast<const uint4*>(p.residual + (int64_t)m * p.ldr + n0);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < CW / 8; ++q) {
             if (n0 + q * 8 < p.N) {
-              uint4 b = rp[q];
+              const uint4 b = rp[q];
               v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
               v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
               v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
@@ -261,39 +276,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if constexpr (OUT == OUT_BF16) {
-          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)m * p.ldo + n0);
+        // Stage this warp's 32 x 128-byte slab (128B-swizzled) and hand it to TMA.
+        uint8_t* stage_buf = sStage + (quad * 2 + (stage_ctr & 1)) * kStageBytes;
+        if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+        __syncwarp();
+        uint8_t* my_row = stage_buf + lane * 128;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (n0 + q * 8 < p.N) {
-              uint4 o;
-              o.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
-              o.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
-              o.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
-              o.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
-              op[q] = o;
-            }
+        for (int q = 0; q < 8; ++q) {
+          uint4 o;
+          if constexpr (OUT == OUT_BF16) {
+            o.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+            o.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+            o.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+            o.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+          } else {
+            o.x = __float_as_uint(v[q * 4 + 0]);
+            o.y = __float_as_uint(v[q * 4 + 1]);
+            o.z = __float_as_uint(v[q * 4 + 2]);
+            o.w = __float_as_uint(v[q * 4 + 3]);
           }
-        } else {
-          float4* op = reinterpret_cast<float4*>(static_cast<float*>(p.out) + (int64_t)m * p.ldo + n0);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (n0 + q * 4 < p.N) {
-              float4 o = make_float4(v[q * 4 + 0], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-              if constexpr (OUT == OUT_F32_ACCUM) {
-                const float4 prev = op[q];
-                o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
-              }
-              op[q] = o;
-            }
-          }
+          *reinterpret_cast<uint4*>(my_row + ((q ^ (lane & 7)) << 4)) = o;
         }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (OUT == OUT_F32_ACCUM) tma_reduce_add_2d(&tmC, stage_buf, n0, m_warp);
+          else tma_store_2d(&tmC, stage_buf, n0, m_warp);
+          bulk_commit();
+        }
+        ++stage_ctr;
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (lane == 0) bulk_wait<0>();  // every output store of this warp has landed
   }
 
   __syncthreads();
@@ -305,7 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <bool A_MN, bool B_MN, int OUT>
-static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t stream) {
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
+                   cudaStream_t stream) {
   auto kern = gemm_bf16_kernel<A_MN, B_MN, OUT>;
   static bool attr_set[64] = {false};
   const int dev = current_device();
@@ -315,7 +334,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
   }
   const int num_tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = std::min(num_tiles, num_sms(dev));
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tc, p);
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -378,11 +397,20 @@ void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn,
   if (!b_mn) tb = make_tmap_2d_bf16(b.data_ptr(), K, N, b.stride(0) * 2, gemm::BK, gemm::BN);
   else tb = make_tmap_2d_bf16(b.data_ptr(), N, K, b.stride(0) * 2, 64, gemm::BK);
 
+  // Output map: 128-byte wide boxes (32 fp32 or 64 bf16 columns) x 32 rows, 128B swizzle.
+  CUtensorMap tc;
+  if (out_f32)
+    tc = make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, out.stride(0) * 4, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    tc = make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, out.stride(0) * 2, 64, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int mode = accumulate ? gemm::OUT_F32_ACCUM : (out_f32 ? gemm::OUT_F32 : gemm::OUT_BF16);
 #define AETHER_GEMM_CASE(AM, BMN, OM)                                         \
   if (a_mn == AM && b_mn == BMN && mode == OM) {                              \
-    gemm::launch<AM, BMN, OM>(ta, tb, p, stream);                             \
+    gemm::launch<AM, BMN, OM>(ta, tb, tc, p, stream);                         \
     return;                                                                   \
   }
   AETHER_GEMM_CASE(false, false, gemm::OUT_BF16)

@@ -96,6 +96,25 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, 
   return m;
 }
 
+CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes, uint64_t inner,
+                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle) {
+  ensure_context_bound();
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
+  if (row_stride_bytes % 16 != 0) throw std::runtime_error("TMA row stride must be a multiple of 16 bytes");
+  if ((box_inner * elem_bytes) % 16 != 0) throw std::runtime_error("TMA box inner extent must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (2d) failed: " + std::to_string((int)r));
+  return m;
+}
+
 CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t inner, uint64_t mid, uint64_t outer, uint64_t mid_stride_bytes,
                               uint64_t outer_stride_bytes, uint32_t box_inner, uint32_t box_mid, uint32_t box_outer) {
   ensure_context_bound();

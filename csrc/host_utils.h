@@ -31,6 +31,11 @@ int read_and_clear_status();
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer);
 
+// 2-D tensor map of any element type (CU_TENSOR_MAP_DATA_TYPE_*), given swizzle.
+CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes, uint64_t inner,
+                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle);
+
 // 3-D bf16 tensor map, 128-byte swizzle: dims {inner, mid, outer}.
 CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t inner, uint64_t mid, uint64_t outer, uint64_t mid_stride_bytes,
                               uint64_t outer_stride_bytes, uint32_t box_inner, uint32_t box_mid, uint32_t box_outer);
