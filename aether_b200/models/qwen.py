@@ -1,0 +1,350 @@
+"""Qwen2 / Qwen2.5 decoder for serving (also Llama/Mistral-shaped when
+``qkv_bias=False``): batched prefill into a preallocated KV cache and a
+CUDA-graph-captured greedy decode step.
+
+Reference: QwenSession (runtime/src/serving.rs:2528-4835) and its block
+forward (serving.rs:1334-1500). Differences by design:
+  * prefill runs the whole prompt through the tensor-core GEMM and flash
+    attention at once (the reference loops the decode path token by token,
+    serving.rs:3285-3299, so its TTFT is O(prompt) decode launches);
+  * decode GEMMs are split-K swap-AB tcgen05 GEMMs over all SMs with fused
+    bias / residual / SwiGLU finalisation; decode attention is split-K over the
+    cache with one CTA per (sequence, KV head, split);
+  * positions, slots and lengths live in device buffers, so one captured CUDA
+    graph per batch bucket replays every step (the reference captures one
+    global graph, cuda.rs:8295-8380);
+  * greedy sampling runs on the device (the reference copies [vocab] fp32
+    logits to the host every step, serving.rs:3418).
+
+Weights are random-init bf16 (N(0, 0.02)) unless loaded from a
+safetensors/GGUF checkpoint through ``aether_b200.formats``.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..ops import functional as F
+from ..ops import reference as ref
+
+
+@dataclass
+class QwenConfig:
+    vocab: int = 151936
+    d_model: int = 1536
+    n_layers: int = 28
+    n_heads: int = 12
+    n_kv_heads: int = 2
+    d_ff: int = 8960
+    rope_theta: float = 1e6
+    norm_eps: float = 1e-6
+    tie_embeddings: bool = True
+    qkv_bias: bool = True
+    max_seq: int = 4096
+    init_std: float = 0.02
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.n_heads
+
+    @staticmethod
+    def qwen25_1_5b(**kw) -> "QwenConfig":
+        return QwenConfig(**kw)
+
+    @staticmethod
+    def qwen25_7b(**kw) -> "QwenConfig":
+        base = dict(vocab=152064, d_model=3584, n_layers=28, n_heads=28, n_kv_heads=4, d_ff=18944,
+                    tie_embeddings=False)
+        base.update(kw)
+        return QwenConfig(**base)
+
+    def n_params(self) -> int:
+        d, f, D = self.d_model, self.d_ff, self.head_dim
+        qkv = (self.n_heads + 2 * self.n_kv_heads) * D
+        per = qkv * d + (qkv if self.qkv_bias else 0) + self.n_heads * D * d + 3 * d * f + 2 * d
+        return self.n_layers * per + self.vocab * d * (1 if self.tie_embeddings else 2) + d
+
+
+class QwenWeights:
+    """bf16 weights. Layer tensors are stacked per kind so TP sharding and
+    checkpoint loading index one tensor per kind."""
+
+    def __init__(self, cfg: QwenConfig, device, seed: int = 0, tp_rank: int = 0, tp_size: int = 1):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        d, f, D, L = cfg.d_model, cfg.d_ff, cfg.head_dim, cfg.n_layers
+        assert cfg.n_heads % tp_size == 0 and f % tp_size == 0, "heads and d_ff must split over TP"
+        self.hq = cfg.n_heads // tp_size
+        self.hkv = max(1, cfg.n_kv_heads // tp_size)  # KV heads replicated when n_kv < tp
+        self.f = f // tp_size
+        qkv = (self.hq + 2 * self.hkv) * D
+        g = torch.Generator(device="cpu").manual_seed(seed)
+
+        def rnd(*shape):
+            t = torch.empty(*shape, dtype=torch.float32).normal_(0.0, cfg.init_std, generator=g)
+            return t.to(self.device, torch.bfloat16)
+
+        self.embed = rnd(cfg.vocab, d)
+        self.lm_head = self.embed if cfg.tie_embeddings else rnd(cfg.vocab, d)
+        self.final_norm = torch.ones(d, dtype=torch.bfloat16, device=self.device)
+        self.attn_norm = [torch.ones(d, dtype=torch.bfloat16, device=self.device) for _ in range(L)]
+        self.mlp_norm = [torch.ones(d, dtype=torch.bfloat16, device=self.device) for _ in range(L)]
+        self.wqkv = [rnd(qkv, d) for _ in range(L)]
+        self.bqkv = [rnd(qkv) if cfg.qkv_bias else None for _ in range(L)]
+        self.wo = [rnd(d, self.hq * D) for _ in range(L)]
+        self.wgu = [rnd(2 * self.f, d) for _ in range(L)]
+        self.wd = [rnd(d, self.f) for _ in range(L)]
+
+
+class KVCache:
+    def __init__(self, cfg: QwenConfig, n_kv_heads: int, slots: int, max_seq: int, device):
+        shape = (slots, max_seq, n_kv_heads, cfg.head_dim)
+        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.n_layers)]
+        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.n_layers)]
+        self.slots, self.max_seq = slots, max_seq
+
+    def bytes(self) -> int:
+        return sum(t.numel() * 2 for t in self.k + self.v)
+
+
+class QwenModel:
+    """Single-GPU (or one TP rank's) Qwen2 forward for serving.
+
+    ``tp`` (optional) is an object with ``all_reduce_(t)`` used after the
+    row-parallel o_proj and down_proj (see ``parallel/tp.py``)."""
+
+    def __init__(self, cfg: QwenConfig, device="cuda", seed: int = 0, max_batch: int = 64, max_seq: int | None = None,
+                 weights: QwenWeights | None = None, tp=None, decode_splits: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.tp = tp
+        tp_rank = tp.rank if tp is not None else 0
+        tp_size = tp.world if tp is not None else 1
+        self.w = weights or QwenWeights(cfg, device, seed, tp_rank, tp_size)
+        self.hq, self.hkv, self.f = self.w.hq, self.w.hkv, self.w.f
+        self.max_batch = max_batch
+        self.max_seq = max_seq or cfg.max_seq
+        # one extra slot absorbs the K/V writes of padded batch rows
+        self.cache = KVCache(cfg, self.hkv, max_batch + 1, self.max_seq, self.device)
+        self.scratch_slot = max_batch
+        cos, sin = ref.rope_tables(self.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
+        self.cos, self.sin = cos.contiguous(), sin.contiguous()
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.decode_splits = decode_splits or self._auto_splits()
+        self._graphs: dict[int, tuple] = {}
+        self._alloc_decode_buffers()
+
+    # ------------------------------------------------------------------ buffers
+    def _auto_splits(self) -> int:
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.device.type == "cuda" else 148
+        # enough (sequence, kv-head, split) CTAs to cover the SMs at batch 1
+        return max(1, min(32, (2 * sms) // max(1, self.hkv)))
+
+    def _alloc_decode_buffers(self):
+        cfg, B, dev = self.cfg, self.max_batch, self.device
+        D = cfg.head_dim
+        qkv_w = (self.hq + 2 * self.hkv) * D
+        widest = max(qkv_w, 2 * self.f, cfg.d_model, cfg.vocab)
+        bf = torch.bfloat16
+        self.buf = {
+            "tok": torch.zeros(B, dtype=torch.long, device=dev),
+            "pos": torch.zeros(B, dtype=torch.int32, device=dev),
+            "slot": torch.arange(B, dtype=torch.int32, device=dev),
+            "seqlen": torch.ones(B, dtype=torch.int32, device=dev),
+            "x": torch.zeros(B, cfg.d_model, dtype=bf, device=dev),
+            "x2": torch.zeros(B, cfg.d_model, dtype=bf, device=dev),
+            "h": torch.zeros(B, cfg.d_model, dtype=bf, device=dev),
+            "qkv": torch.zeros(B, qkv_w, dtype=bf, device=dev),
+            "o": torch.zeros(B, self.hq * D, dtype=bf, device=dev),
+            "act": torch.zeros(B, self.f, dtype=bf, device=dev),
+            "acc": torch.zeros(B, widest, dtype=torch.float32, device=dev),
+            "part_o": torch.empty(B * self.hq * self.decode_splits * D, dtype=torch.float32, device=dev),
+            "part_lse": torch.empty(B * self.hq * self.decode_splits, dtype=torch.float32, device=dev),
+            "next": torch.zeros(B, dtype=torch.long, device=dev),
+        }
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, tokens: torch.Tensor, slots: torch.Tensor | None = None, start_pos: int = 0) -> torch.Tensor:
+        """tokens [B, S] (one prompt per cache slot, equal lengths) -> greedy next
+        token [B]. Writes K/V for positions [start_pos, start_pos + S)."""
+        cfg, w = self.cfg, self.w
+        B, S = tokens.shape
+        D = cfg.head_dim
+        dev = self.device
+        if slots is None:
+            slots = torch.arange(B, dtype=torch.int32, device=dev)
+        T = B * S
+        pos = (torch.arange(S, dtype=torch.int32, device=dev) + start_pos).repeat(B)
+        slot_t = slots.to(dev, torch.int32).repeat_interleave(S)
+        x = F.embedding(w.embed, tokens.to(dev).reshape(-1))
+        row = (self.hq + 2 * self.hkv) * D
+        for i in range(cfg.n_layers):
+            h, _, _ = F.rmsnorm(x, w.attn_norm[i], cfg.norm_eps)
+            qkv = F.gemm(h, w.wqkv[i], bias=w.bqkv[i])
+            F.rope_kv_append(qkv, pos, slot_t, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq,
+                             self.hkv, D)
+            q = qkv.view(B, S, row)[:, :, : self.hq * D].view(B, S, self.hq, D)
+            if start_pos == 0:
+                k = qkv.view(B, S, row)[:, :, self.hq * D : (self.hq + self.hkv) * D].view(B, S, self.hkv, D)
+                v = qkv.view(B, S, row)[:, :, (self.hq + self.hkv) * D :].view(B, S, self.hkv, D)
+                o, _ = F.attention(q, k, v, self.scale, True, 0, want_lse=False)
+            else:
+                assert bool((slots == torch.arange(B, device=slots.device)).all()), "chunked prefill needs slots 0..B-1"
+                k = self.cache.k[i][:B, : start_pos + S]
+                v = self.cache.v[i][:B, : start_pos + S]
+                o, _ = F.attention(q, k, v, self.scale, True, start_pos, want_lse=False)
+            o2 = o.view(T, self.hq * D)
+            if self.tp is None:
+                x = F.gemm(o2, w.wo[i], residual=x)
+            else:
+                y = F.gemm(o2, w.wo[i])
+                self.tp.all_reduce_(y)
+                x = x + y
+            h, _, _ = F.rmsnorm(x, w.mlp_norm[i], cfg.norm_eps)
+            gu = F.gemm(h, w.wgu[i])
+            act = F.swiglu(gu)
+            if self.tp is None:
+                x = F.gemm(act, w.wd[i], residual=x)
+            else:
+                y = F.gemm(act, w.wd[i])
+                self.tp.all_reduce_(y)
+                x = x + y
+        last = x.view(B, S, cfg.d_model)[:, -1].contiguous()
+        hl, _, _ = F.rmsnorm(last, w.final_norm, cfg.norm_eps)
+        logits = F.gemm(hl, w.lm_head, out_dtype=torch.float32)
+        return F.argmax(logits)
+
+    # ------------------------------------------------------------------ decode
+    def _decode_body(self, B: int) -> None:
+        """One greedy decode step for the first B rows of the static buffers."""
+        cfg, w, b = self.cfg, self.w, self.buf
+        D = cfg.head_dim
+        x, x2, h = b["x"][:B], b["x2"][:B], b["h"][:B]
+        qkv, o, act, acc = b["qkv"][:B], b["o"][:B], b["act"][:B], b["acc"][:B]
+        pos, slot, seqlen = b["pos"][:B], b["slot"][:B], b["seqlen"][:B]
+        x.copy_(F.embedding(w.embed, b["tok"][:B]))
+        for i in range(cfg.n_layers):
+            F.rmsnorm_into(x, w.attn_norm[i], h, cfg.norm_eps)
+            F.skinny_gemm(h, w.wqkv[i], acc)
+            F.skinny_finalize(acc, qkv, bias=w.bqkv[i])
+            F.rope_kv_append(qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D)
+            F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
+                               self.decode_splits, b["part_o"], b["part_lse"])
+            F.skinny_gemm(o, w.wo[i], acc)
+            if self.tp is None:
+                F.skinny_finalize(acc, x2, res=x)
+            else:
+                F.skinny_finalize(acc, x2)
+                self.tp.all_reduce_(x2)
+                x2.add_(x)
+            F.rmsnorm_into(x2, w.mlp_norm[i], h, cfg.norm_eps)
+            F.skinny_gemm(h, w.wgu[i], acc)
+            F.skinny_finalize(acc, act, swiglu=True)
+            F.skinny_gemm(act, w.wd[i], acc)
+            if self.tp is None:
+                F.skinny_finalize(acc, x, res=x2)
+            else:
+                F.skinny_finalize(acc, x)
+                self.tp.all_reduce_(x)
+                x.add_(x2)
+        F.rmsnorm_into(x, w.final_norm, h, cfg.norm_eps)
+        F.skinny_gemm(h, w.lm_head, acc)
+        b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
+        acc.zero_()
+
+    def _bucket(self, B: int) -> int:
+        for s in (1, 2, 4, 8, 16, 32, 64):
+            if B <= s and s <= self.max_batch:
+                return s
+        return self.max_batch
+
+    @torch.no_grad()
+    def capture(self, B: int) -> None:
+        """Captures the decode step for batch bucket B as a CUDA graph."""
+        if self.device.type != "cuda" or B in self._graphs:
+            return
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm up allocations and tensor maps outside the graph
+                self._decode_body(B)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._decode_body(B)
+        self._graphs[B] = g
+
+    @torch.no_grad()
+    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor | None = None,
+                    use_graph: bool = True) -> torch.Tensor:
+        """tokens [B] at positions pos [B] (0-based) -> greedy next tokens [B]
+        (device tensor, valid until the next call)."""
+        B = tokens.shape[0]
+        Bb = self._bucket(B)
+        b = self.buf
+        b["tok"][:B].copy_(tokens, non_blocking=True)
+        b["pos"][:B].copy_(pos, non_blocking=True)
+        b["seqlen"][:B].copy_(pos + 1, non_blocking=True)
+        if slots is not None:
+            b["slot"][:B].copy_(slots, non_blocking=True)
+        if Bb > B:  # padded rows decode into spare slots and are ignored
+            b["tok"][B:Bb].zero_()
+            b["pos"][B:Bb].zero_()
+            b["seqlen"][B:Bb].fill_(1)
+            b["slot"][B:Bb].fill_(self.scratch_slot)
+        if use_graph and self.device.type == "cuda":
+            if Bb not in self._graphs:
+                self.capture(Bb)
+            self._graphs[Bb].replay()
+        else:
+            self._decode_body(Bb)
+        return b["next"][:B]
+
+    @torch.no_grad()
+    def generate(self, prompts: torch.Tensor, max_new_tokens: int, use_graph: bool = True) -> torch.Tensor:
+        """Greedy generation for B equal-length prompts [B, S] -> [B, max_new_tokens]."""
+        B, S = prompts.shape
+        assert B <= self.max_batch and S + max_new_tokens <= self.max_seq
+        out = torch.empty(B, max_new_tokens, dtype=torch.long, device=self.device)
+        nxt = self.prefill(prompts)
+        out[:, 0] = nxt
+        pos = torch.full((B,), S, dtype=torch.int32, device=self.device)
+        slots = torch.arange(B, dtype=torch.int32, device=self.device)
+        tok = nxt
+        for t in range(1, max_new_tokens):
+            tok = self.decode_step(tok, pos, slots, use_graph=use_graph).clone()
+            out[:, t] = tok
+            pos += 1
+        return out
+
+    @torch.no_grad()
+    def reference_logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        """fp32 eager forward of [B, S] tokens (no cache) for numerics checks."""
+        cfg, w = self.cfg, self.w
+        B, S = tokens.shape
+        D = cfg.head_dim
+        x = w.embed.float()[tokens.to(self.device)]
+        pos = torch.arange(S, device=self.device)
+        for i in range(cfg.n_layers):
+            h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.attn_norm[i].float()
+            qkv = h @ w.wqkv[i].float().t()
+            if w.bqkv[i] is not None:
+                qkv = qkv + w.bqkv[i].float()
+            qkv2 = qkv.reshape(B * S, -1)
+            qkv2 = ref.rope(qkv2, pos.repeat(B), self.cos, self.sin, self.hq + self.hkv, D)
+            qkv = qkv2.view(B, S, -1)
+            q = qkv[..., : self.hq * D].view(B, S, self.hq, D)
+            k = qkv[..., self.hq * D : (self.hq + self.hkv) * D].view(B, S, self.hkv, D)
+            v = qkv[..., (self.hq + self.hkv) * D :].view(B, S, self.hkv, D)
+            o, _ = ref.attention(q, k, v, self.scale, True)
+            x = x + o.reshape(B, S, -1) @ w.wo[i].float().t()
+            h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.mlp_norm[i].float()
+            gu = h @ w.wgu[i].float().t()
+            g, u = gu.chunk(2, -1)
+            x = x + (torch.nn.functional.silu(g) * u) @ w.wd[i].float().t()
+        h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.final_norm.float()
+        return h @ w.lm_head.float().t()

@@ -251,7 +251,7 @@ def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=T
         C().attention_fwd(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset))
         return o, lse
     o, lse = ref.attention(q, k, v, scale, causal, causal_offset)
-    o = o.to(q.dtype)
+    o = o.to(q.dtype).contiguous()
     if out is not None:
         out.copy_(o)
         o = out
@@ -306,3 +306,86 @@ def grad_norm(g, pre_scale=1.0, max_norm=0.0):
     norm.fill_(float(n))
     clip.fill_(min(1.0, max_norm / (float(n) + 1e-6)) if max_norm > 0 else 1.0)
     return norm, clip
+
+
+# ------------------------------------------------------------------ decode path
+def skinny_gemm(x, w, acc, splits=0):
+    """acc[M, N] += x[M, K] @ w[N, K]^T in fp32 (acc starts zeroed), M <= 64."""
+    if _cuda(x):
+        C().skinny_gemm(x, w, acc, int(splits))
+        return acc
+    acc[:, : w.shape[0]] += x.float() @ w.float().t()
+    return acc
+
+
+def skinny_finalize(acc, y, bias=None, res=None, swiglu=False):
+    """y = bf16(acc + bias + res) or swiglu(acc halves); zeroes acc."""
+    if _cuda(acc):
+        C().skinny_finalize(acc, y, bias, res, bool(swiglu))
+        return y
+    M, N = y.shape
+    if swiglu:
+        a = acc[:M, : 2 * N].clone()
+        if bias is not None:
+            a = a + bias.float()
+        g, u = a[:, :N], a[:, N:]
+        y.copy_((torch.nn.functional.silu(g) * u).to(y.dtype))
+        acc[:M, : 2 * N] = 0
+    else:
+        a = acc[:M, :N].clone()
+        if bias is not None:
+            a = a + bias.float()
+        if res is not None:
+            a = a + res.float()
+        y.copy_(a.to(y.dtype))
+        acc[:M, :N] = 0
+    return y
+
+
+def rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D):
+    """Rotates q/k of qkv [T, row] in place and writes k, v into the caches
+    [slots, max_seq, Hkv, D] at (slot[t], pos[t])."""
+    if _cuda(qkv):
+        C().rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, int(Hq), int(Hkv), int(D))
+        return qkv
+    rope_(qkv, pos, cos_t, sin_t, Hq + Hkv, D)
+    T = qkv.shape[0]
+    k = qkv[:, Hq * D : (Hq + Hkv) * D].view(T, Hkv, D)
+    v = qkv[:, (Hq + Hkv) * D : (Hq + 2 * Hkv) * D].view(T, Hkv, D)
+    k_cache[slot.long(), pos.long()] = k
+    v_cache[slot.long(), pos.long()] = v
+    return qkv
+
+
+def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8, part_o=None, part_lse=None):
+    """q [B, >=Hq*D] (one new token per sequence), caches [slots, max_seq, Hkv, D],
+    seqlen [B] = valid keys. Writes out [B, Hq*D]."""
+    B = q.shape[0]
+    D = k_cache.shape[3]
+    if _cuda(q):
+        if part_o is None:
+            part_o = torch.empty(B * Hq * splits * D, dtype=torch.float32, device=q.device)
+            part_lse = torch.empty(B * Hq * splits, dtype=torch.float32, device=q.device)
+        C().decode_attention(q, k_cache, v_cache, slot, seqlen, out, part_o, part_lse, int(Hq), int(splits),
+                             float(scale))
+        return out
+    Hkv = k_cache.shape[2]
+    for b in range(B):
+        L = int(seqlen[b])
+        s = int(slot[b])
+        qb = q[b, : Hq * D].view(1, 1, Hq, D)
+        kb = k_cache[s, :L].unsqueeze(0)
+        vb = v_cache[s, :L].unsqueeze(0)
+        o, _ = ref.attention(qb, kb, vb, scale, causal=False)
+        out[b, : Hq * D] = o.reshape(-1).to(out.dtype)
+    return out
+
+
+def rmsnorm_into(x, w, out, eps=1e-6):
+    """out = rmsnorm(x) * w into a preallocated tensor (no statistics saved)."""
+    if _cuda(x):
+        C().rmsnorm_fwd(x, None, w, out, None, None, float(eps))
+        return out
+    y, _, _ = ref.rmsnorm(x, w, eps)
+    out.copy_(y.to(out.dtype))
+    return out

@@ -46,6 +46,16 @@ void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std
                    double scale, bool causal, int64_t causal_offset);
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
                    at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset);
+// gemm_skinny.cu
+void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits);
+void skinny_finalize(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
+                     bool swiglu);
+// decode_attention.cu
+void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t,
+                    at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv, int64_t D);
+void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slot, at::Tensor seqlen,
+                      at::Tensor out, at::Tensor part_o, at::Tensor part_lse, int64_t Hq, int64_t splits,
+                      double scale);
 }  // namespace aether
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -74,6 +84,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_norm", &aether::grad_norm);
   m.def("attention_fwd", &aether::attention_fwd);
   m.def("attention_bwd", &aether::attention_bwd);
+  m.def("skinny_gemm", &aether::skinny_gemm);
+  m.def("skinny_finalize", &aether::skinny_finalize);
+  m.def("rope_kv_append", &aether::rope_kv_append);
+  m.def("decode_attention", &aether::decode_attention);
   m.def("read_and_clear_status", &aether::read_and_clear_status,
         "Returns (and clears) the device status word set by kernels whose bounded waits expired");
 }

@@ -1,0 +1,317 @@
+// Small-M ("skinny") GEMM for decode: y[M, N] = x[M, K] . W[N, K]^T with M <= 64.
+//
+// Decode multiplies a handful of token rows by every weight matrix, so the
+// work is a pure weight stream (memory-bound) and a 128-row M tile would both
+// waste the tensor core and leave most SMs idle. This kernel swaps the
+// operands -- the weight rows are the MMA's M dimension (128 per CTA) and the
+// batch rows are its N dimension (16/32/64) -- and splits K so that every SM
+// streams a slice of W:
+//
+//   grid = (N/128 weight-row tiles) x (K splits), one tile per CTA
+//   warp 0      : TMA producer, 8-deep ring of (128 x 64 W) + (BN x 64 x) tiles
+//   warp 1      : TMEM allocator + single-thread tcgen05.mma issuer (M128, N=BN)
+//   warps 2..5  : epilogue -- tcgen05.ld, then fp32 atomics into acc[M, N]
+//                 (transposed: lane = output feature, so each warp's atomics
+//                 cover 32 consecutive features = 128 contiguous bytes)
+//
+// `skinny_finalize` then turns the fp32 accumulator into bf16 with the fused
+// bias / residual / SwiGLU epilogue and writes zeros back, so the scratch is
+// ready for the next GEMM without a memset (CUDA-graph friendly).
+//
+// Reference counterpart: the decode GEMVs fused_*_matmul_seq1 and the batched
+// seqB variants (runtime/src/cuda.rs:3347-4010, 903-1001), which run one
+// thread block per output row on CUDA cores.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace aether {
+namespace skinny {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int STAGES = 8;
+constexpr int kThreads = 192;
+
+struct Params {
+  float* acc;  // [M, ldacc] fp32, pre-zeroed
+  int64_t ldacc;
+  int M, N, K;
+  int k_blocks_per_split;
+  int* status;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, Params p) {
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_n = blockIdx.x;
+  const int split = blockIdx.y;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const int kb0 = split * p.k_blocks_per_split;
+  const int kb1 = min(num_kb, kb0 + p.k_blocks_per_split);
+  const int nk = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (nk > 0) {
+    if (warp == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_word)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+        tma_load_2d(sA + stage * A_BYTES, &tmW, &full[stage], kb * BK, tile_n * BM);
+        tma_load_2d(sB + stage * B_BYTES, &tmX, &full[stage], kb * BK, 0);
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutProducer);
+        volatile int never = 0;
+        const uint32_t n_back = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
+        for (uint32_t j = 1; j <= n_back; ++j) {
+          const uint32_t i = issued - j;
+          mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < nk; ++i) {
+        if (!mbar_wait(&full[stage], phase, abort_word)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+        const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_f16(tmem_base, sdesc_sw128(a_base + kk * 32, 16, 1024), sdesc_sw128(b_base + kk * 32, 16, 1024), idesc,
+                   (i | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutMma);
+      }
+      umma_commit(tfull);  // arrives once every MMA issued above has completed
+      volatile int never = 0;
+      mbar_wait(tfull, 0, &never);  // TMEM is not freed while an MMA may still write it
+    } else if (warp >= 2) {
+      const int quad = warp & 3;
+      const int n = tile_n * BM + quad * 32 + lane;
+      if (mbar_wait(tfull, 0, abort_word)) {
+        __syncwarp();
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < (BN + 15) / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + c * 16, r);
+          tmem_ld_wait();
+          if (n < p.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = c * 16 + j;
+              if (m < p.M) atomicAdd(p.acc + (int64_t)m * p.ldacc + n, __uint_as_float(r[j]));
+            }
+          }
+        }
+      } else {
+        *abort_word = 1;
+        if (lane == 0) atomicExch(p.status, kStatusTimeoutEpilogue);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// y = bf16(acc + bias + residual) (or SwiGLU of the [gate | up] halves);
+// writes zeros back into acc.
+template <bool SWIGLU>
+__global__ void finalize_kernel(float* __restrict__ acc, int64_t ldacc, int M, int Nout,
+                                const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ res,
+                                int64_t ldr, __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // 4-wide chunk of the output
+  const int chunks = Nout / 4;
+  if (i >= (int64_t)M * chunks) return;
+  const int m = (int)(i / chunks);
+  const int n = (int)(i % chunks) * 4;
+  float* a = acc + (int64_t)m * ldacc;
+  float v[4];
+  if constexpr (SWIGLU) {
+    float4 g = *reinterpret_cast<float4*>(a + n);
+    float4 u = *reinterpret_cast<float4*>(a + Nout + n);
+    if (bias) {
+      g.x += __bfloat162float(bias[n]); g.y += __bfloat162float(bias[n + 1]);
+      g.z += __bfloat162float(bias[n + 2]); g.w += __bfloat162float(bias[n + 3]);
+      u.x += __bfloat162float(bias[Nout + n]); u.y += __bfloat162float(bias[Nout + n + 1]);
+      u.z += __bfloat162float(bias[Nout + n + 2]); u.w += __bfloat162float(bias[Nout + n + 3]);
+    }
+    const float gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = gg[j] / (1.f + __expf(-gg[j])) * uu[j];
+    *reinterpret_cast<float4*>(a + n) = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(a + Nout + n) = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    const float4 t = *reinterpret_cast<float4*>(a + n);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    if (bias) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] += __bfloat162float(bias[n + j]);
+    }
+    if (res) {
+      const uint2 r = *reinterpret_cast<const uint2*>(res + (int64_t)m * ldr + n);
+      v[0] += bf16lo(r.x); v[1] += bf16hi(r.x); v[2] += bf16lo(r.y); v[3] += bf16hi(r.y);
+    }
+    *reinterpret_cast<float4*>(a + n) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  uint2 o;
+  o.x = pack_bf16(v[0], v[1]);
+  o.y = pack_bf16(v[2], v[3]);
+  *reinterpret_cast<uint2*>(y + (int64_t)m * ldy + n) = o;
+}
+
+template <int BN>
+void launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int n_tiles, int splits,
+            cudaStream_t stream) {
+  constexpr int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  auto k = skinny_kernel<BN>;
+  static bool set[64] = {false};
+  const int dev = current_device();
+  if (!set[dev]) {
+    AETHER_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set[dev] = true;
+  }
+  k<<<dim3(n_tiles, splits), kThreads, smem, stream>>>(tw, tx, p);
+  AETHER_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace skinny
+
+// acc[M, N] += x[M, K] . w[N, K]^T (fp32, acc must start zeroed); M <= 64.
+void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && acc.is_cuda(), "skinny_gemm: CUDA tensors");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && acc.scalar_type() == at::kFloat,
+              "skinny_gemm: bf16 x/w, fp32 acc");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && acc.stride(1) == 1,
+              "skinny_gemm: row-major 2-D operands");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && acc.size(0) == M && acc.size(1) >= N, "skinny_gemm: shapes");
+  TORCH_CHECK(M >= 1 && M <= 64, "skinny_gemm: M must be in [1, 64]");
+  TORCH_CHECK(K % 8 == 0 && (x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "skinny_gemm: alignment");
+  c10::cuda::CUDAGuard g(x.device());
+  const int n_tiles = (int)((N + skinny::BM - 1) / skinny::BM);
+  const int num_kb = (int)((K + skinny::BK - 1) / skinny::BK);
+  if (splits <= 0) {
+    const int target = 2 * num_sms(current_device());
+    splits = std::max<int64_t>(1, std::min<int64_t>(num_kb / 2, (target + n_tiles - 1) / n_tiles));
+  }
+  const int kbps = (num_kb + (int)splits - 1) / (int)splits;
+  const int real_splits = (num_kb + kbps - 1) / kbps;
+  skinny::Params p{};
+  p.acc = acc.data_ptr<float>();
+  p.ldacc = acc.stride(0);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.k_blocks_per_split = kbps;
+  p.status = device_status_word();
+  const int BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  CUtensorMap tw = make_tmap_2d_bf16(w.data_ptr(), K, N, w.stride(0) * 2, skinny::BK, skinny::BM);
+  CUtensorMap tx = make_tmap_2d_bf16(x.data_ptr(), K, M, x.stride(0) * 2, skinny::BK, BN);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (BN == 16) skinny::launch<16>(tw, tx, p, n_tiles, real_splits, stream);
+  else if (BN == 32) skinny::launch<32>(tw, tx, p, n_tiles, real_splits, stream);
+  else skinny::launch<64>(tw, tx, p, n_tiles, real_splits, stream);
+}
+
+// y = bf16(acc (+bias) (+res)), or swiglu over acc's [gate | up] halves when swiglu;
+// acc is re-zeroed. y: [M, Nout] (Nout = N or N/2 for swiglu).
+void skinny_finalize(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
+                     bool swiglu) {
+  const int64_t M = y.size(0), Nout = y.size(1);
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && y.scalar_type() == at::kBFloat16 && y.stride(1) == 1, "skinny_finalize: dtypes");
+  TORCH_CHECK(Nout % 4 == 0 && acc.size(0) >= M && acc.size(1) >= (swiglu ? 2 * Nout : Nout), "skinny_finalize: shapes");
+  TORCH_CHECK(acc.stride(0) % 4 == 0 && y.stride(0) % 4 == 0, "skinny_finalize: strides");
+  const __nv_bfloat16* b = (bias && bias->defined()) ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
+  const __nv_bfloat16* r = nullptr;
+  int64_t ldr = 0;
+  if (res && res->defined()) {
+    TORCH_CHECK(!swiglu && res->stride(1) == 1 && res->stride(0) % 4 == 0, "skinny_finalize: residual layout");
+    r = reinterpret_cast<const __nv_bfloat16*>(res->data_ptr());
+    ldr = res->stride(0);
+  }
+  c10::cuda::CUDAGuard g(acc.device());
+  const int64_t n = M * (Nout / 4);
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (swiglu)
+    skinny::finalize_kernel<true><<<grid, 256, 0, stream>>>(acc.data_ptr<float>(), acc.stride(0), (int)M, (int)Nout, b,
+                                                            nullptr, 0, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+                                                            y.stride(0));
+  else
+    skinny::finalize_kernel<false><<<grid, 256, 0, stream>>>(acc.data_ptr<float>(), acc.stride(0), (int)M, (int)Nout, b,
+                                                             r, ldr, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+                                                             y.stride(0));
+  AETHER_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace aether
