@@ -26,8 +26,10 @@ class Slot:
 
 
 class ParamArena:
-    def __init__(self, specs, device, pad_multiple: int = 1):
-        """specs: list of (name, shape, decay: bool)."""
+    def __init__(self, specs, device, pad_multiple: int = 1, alloc=None):
+        """specs: list of (name, shape, decay: bool). ``alloc(numel, dtype)``
+        (optional) provides the bf16 and gradient buffers, e.g. from symmetric
+        memory so the data-parallel kernels can reach them from every GPU."""
         self.slots: dict[str, Slot] = {}
         off = 0
         for name, shape, decay in specs:
@@ -41,8 +43,14 @@ class ParamArena:
         self.n_params = sum(s.numel for s in self.slots.values())
         self.device = torch.device(device)
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        self.bf16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=self.device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        if alloc is None:
+            self.bf16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=self.device)
+            self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        else:
+            self.bf16 = alloc(self.numel, torch.bfloat16)
+            self.grad = alloc(self.numel, torch.float32)
+            self.bf16.zero_()
+            self.grad.zero_()
         self.decay_mask = torch.zeros(self.numel, dtype=torch.bool)
         for s in self.slots.values():
             if s.decay:

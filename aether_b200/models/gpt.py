@@ -87,10 +87,10 @@ def gpt_param_specs(cfg: GPTConfig):
 
 
 class GPT:
-    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1):
+    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1, alloc=None):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.arena = ParamArena(gpt_param_specs(cfg), self.device, pad_multiple=pad_multiple)
+        self.arena = ParamArena(gpt_param_specs(cfg), self.device, pad_multiple=pad_multiple, alloc=alloc)
         self.init_weights(seed)
         cos, sin = ref.rope_tables(cfg.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()

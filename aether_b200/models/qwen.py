@@ -68,35 +68,73 @@ class QwenConfig:
 
 
 class QwenWeights:
-    """bf16 weights. Layer tensors are stacked per kind so TP sharding and
-    checkpoint loading index one tensor per kind."""
+    """bf16 weights, optionally one tensor-parallel rank's shard.
+
+    Every full tensor is drawn from its own seeded generator on the target
+    device and then sliced, so all TP degrees shard the same random model:
+    q/k/v heads and the gate/up rows are split column-parallel, o_proj and
+    down_proj row-parallel (Megatron layout, reference
+    runtime/src/tensor_parallel.rs:8-29); KV heads are replicated when there
+    are fewer KV heads than ranks. Embedding, LM head and norms are replicated.
+    """
 
     def __init__(self, cfg: QwenConfig, device, seed: int = 0, tp_rank: int = 0, tp_size: int = 1):
         self.cfg = cfg
         self.device = torch.device(device)
         self.tp_rank, self.tp_size = tp_rank, tp_size
-        d, f, D, L = cfg.d_model, cfg.d_ff, cfg.head_dim, cfg.n_layers
-        assert cfg.n_heads % tp_size == 0 and f % tp_size == 0, "heads and d_ff must split over TP"
-        self.hq = cfg.n_heads // tp_size
-        self.hkv = max(1, cfg.n_kv_heads // tp_size)  # KV heads replicated when n_kv < tp
-        self.f = f // tp_size
-        qkv = (self.hq + 2 * self.hkv) * D
-        g = torch.Generator(device="cpu").manual_seed(seed)
+        d, F_, D, L = cfg.d_model, cfg.d_ff, cfg.head_dim, cfg.n_layers
+        Hq, Hkv = cfg.n_heads, cfg.n_kv_heads
+        assert Hq % tp_size == 0 and F_ % tp_size == 0, "heads and d_ff must split over TP"
+        assert Hkv % tp_size == 0 or tp_size % Hkv == 0, "KV heads must split or replicate evenly"
+        self.hq = Hq // tp_size
+        self.hkv = max(1, Hkv // tp_size)
+        self.f = F_ // tp_size
+        r = tp_rank
+        q_heads = list(range(r * self.hq, (r + 1) * self.hq))
+        kv_heads = (list(range(r * self.hkv, (r + 1) * self.hkv)) if Hkv >= tp_size
+                    else [r * Hkv // tp_size])
+        idx = [0]
 
         def rnd(*shape):
-            t = torch.empty(*shape, dtype=torch.float32).normal_(0.0, cfg.init_std, generator=g)
-            return t.to(self.device, torch.bfloat16)
+            idx[0] += 1
+            g = torch.Generator(device=self.device).manual_seed(seed * 1000003 + idx[0])
+            t = torch.randn(*shape, generator=g, device=self.device, dtype=torch.float32) * cfg.init_std
+            return t.to(torch.bfloat16)
+
+        def heads(t, hs, base):  # rows of the given heads from a [(H...)*D, ...] tensor
+            return torch.cat([t[(base + h) * D : (base + h + 1) * D] for h in hs], 0)
 
         self.embed = rnd(cfg.vocab, d)
         self.lm_head = self.embed if cfg.tie_embeddings else rnd(cfg.vocab, d)
         self.final_norm = torch.ones(d, dtype=torch.bfloat16, device=self.device)
         self.attn_norm = [torch.ones(d, dtype=torch.bfloat16, device=self.device) for _ in range(L)]
         self.mlp_norm = [torch.ones(d, dtype=torch.bfloat16, device=self.device) for _ in range(L)]
-        self.wqkv = [rnd(qkv, d) for _ in range(L)]
-        self.bqkv = [rnd(qkv) if cfg.qkv_bias else None for _ in range(L)]
-        self.wo = [rnd(d, self.hq * D) for _ in range(L)]
-        self.wgu = [rnd(2 * self.f, d) for _ in range(L)]
-        self.wd = [rnd(d, self.f) for _ in range(L)]
+        self.wqkv, self.bqkv, self.wo, self.wgu, self.wd = [], [], [], [], []
+        for _ in range(L):
+            wqkv = rnd((Hq + 2 * Hkv) * D, d)
+            bqkv = rnd((Hq + 2 * Hkv) * D) if cfg.qkv_bias else None
+            wo = rnd(d, Hq * D)
+            wgu = rnd(2 * F_, d)
+            wd = rnd(d, F_)
+            if tp_size == 1:
+                self.wqkv.append(wqkv)
+                self.bqkv.append(bqkv)
+                self.wo.append(wo)
+                self.wgu.append(wgu)
+                self.wd.append(wd)
+                continue
+            parts = [heads(wqkv, q_heads, 0), heads(wqkv, kv_heads, Hq), heads(wqkv, kv_heads, Hq + Hkv)]
+            self.wqkv.append(torch.cat(parts, 0).contiguous())
+            if bqkv is not None:
+                bp = [heads(bqkv, q_heads, 0), heads(bqkv, kv_heads, Hq), heads(bqkv, kv_heads, Hq + Hkv)]
+                self.bqkv.append(torch.cat(bp, 0).contiguous())
+            else:
+                self.bqkv.append(None)
+            self.wo.append(wo[:, r * self.hq * D : (r + 1) * self.hq * D].contiguous())
+            f0, f1 = r * self.f, (r + 1) * self.f
+            self.wgu.append(torch.cat([wgu[f0:f1], wgu[F_ + f0 : F_ + f1]], 0).contiguous())
+            self.wd.append(wd[:, f0:f1].contiguous())
+            del wqkv, bqkv, wo, wgu, wd
 
 
 class KVCache:
@@ -234,23 +272,21 @@ class QwenModel:
             F.rope_kv_append(qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
                                self.decode_splits, b["part_o"], b["part_lse"])
-            F.skinny_gemm(o, w.wo[i], acc)
             if self.tp is None:
+                F.skinny_gemm(o, w.wo[i], acc)
                 F.skinny_finalize(acc, x2, res=x)
             else:
-                F.skinny_finalize(acc, x2)
-                self.tp.all_reduce_(x2)
-                x2.add_(x)
+                racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
+                F.skinny_finalize(racc, x2, res=x)
             F.rmsnorm_into(x2, w.mlp_norm[i], h, cfg.norm_eps)
             F.skinny_gemm(h, w.wgu[i], acc)
             F.skinny_finalize(acc, act, swiglu=True)
-            F.skinny_gemm(act, w.wd[i], acc)
             if self.tp is None:
+                F.skinny_gemm(act, w.wd[i], acc)
                 F.skinny_finalize(acc, x, res=x2)
             else:
-                F.skinny_finalize(acc, x)
-                self.tp.all_reduce_(x)
-                x.add_(x2)
+                racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
+                F.skinny_finalize(racc, x, res=x2)
         F.rmsnorm_into(x, w.final_norm, h, cfg.norm_eps)
         F.skinny_gemm(h, w.lm_head, acc)
         b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))

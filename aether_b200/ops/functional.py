@@ -309,10 +309,11 @@ def grad_norm(g, pre_scale=1.0, max_norm=0.0):
 
 
 # ------------------------------------------------------------------ decode path
-def skinny_gemm(x, w, acc, splits=0):
-    """acc[M, N] += x[M, K] @ w[N, K]^T in fp32 (acc starts zeroed), M <= 64."""
+def skinny_gemm(x, w, acc, splits=0, acc_mc=0):
+    """acc[M, N] += x[M, K] @ w[N, K]^T in fp32 (acc starts zeroed), M <= 64.
+    acc_mc: NVLS multicast address of a symmetric acc (reduce into all ranks)."""
     if _cuda(x):
-        C().skinny_gemm(x, w, acc, int(splits))
+        C().skinny_gemm(x, w, acc, int(splits), int(acc_mc))
         return acc
     acc[:, : w.shape[0]] += x.float() @ w.float().t()
     return acc

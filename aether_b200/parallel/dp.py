@@ -8,15 +8,22 @@ AdamW on every rank. Here each rank owns 1/world of the flat arena:
     AdamW on the shard (gradient scaled by 1/world inside the kernel)
     bf16 shard          --all-gather------>  full bf16 compute copy
 
-so optimiser state and optimiser traffic shrink by the world size. The
-collectives run on NCCL here; ``fused_dp.py`` provides the single-kernel
-NVLink version of reduce-scatter + AdamW.
+Two implementations with the same interface:
+  * ``DataParallel``       -- the baseline: NCCL reduce-scatter, AdamW kernel,
+                              NCCL all-gather (gloo on CPU);
+  * ``FusedDataParallel``  -- the arena's gradient and bf16 buffers live in
+                              symmetric memory, and ONE kernel per step reduces
+                              the shard across GPUs (NVLS multimem.ld_reduce or
+                              P2P loads), applies AdamW, and writes the new bf16
+                              parameters into every GPU's copy (multimem.st or
+                              P2P stores), bracketed by two device barriers.
 """
 from __future__ import annotations
 
 import torch
 import torch.distributed as dist
 
+from .._ext import C
 from ..optim import FlatAdamW
 
 
@@ -41,12 +48,81 @@ class DataParallel:
             dist.broadcast(self.arena.master, src=0, group=self.group)
             self.arena.sync_bf16_from_master()
 
+    def _reduce_scatter(self) -> None:
+        a = self.arena
+        if a.grad.is_cuda:
+            dist.reduce_scatter_tensor(self.grad_shard, a.grad, op=dist.ReduceOp.SUM, group=self.group)
+        else:  # gloo has no reduce-scatter
+            full = a.grad.clone()
+            dist.all_reduce(full, group=self.group)
+            self.grad_shard.copy_(full[self.start : self.end])
+
     def step(self, lr: float | None = None) -> None:
         a = self.arena
         if self.world == 1:
             self.opt.step(lr=lr)
             return
-        dist.reduce_scatter_tensor(self.grad_shard, a.grad, op=dist.ReduceOp.SUM, group=self.group)
+        self._reduce_scatter()
         self.opt.step(lr=lr, grad=self.grad_shard, gscale=1.0 / self.world)
-        shard_bf16 = a.bf16[self.start : self.end]
-        dist.all_gather_into_tensor(a.bf16, shard_bf16, group=self.group)
+        shard_bf16 = a.bf16[self.start : self.end].clone()
+        if a.bf16.is_cuda:
+            dist.all_gather_into_tensor(a.bf16, shard_bf16, group=self.group)
+        else:
+            parts = [torch.empty_like(shard_bf16) for _ in range(self.world)]
+            dist.all_gather(parts, shard_bf16, group=self.group)
+            a.bf16.copy_(torch.cat(parts))
+
+    def state_dict(self) -> dict:
+        return {"opt": self.opt.state_dict()}
+
+
+class FusedDataParallel:
+    """One-kernel DP step over symmetric memory (see module docstring).
+
+    The model must be built with ``alloc=team_alloc(team)`` so its arena's
+    gradient and bf16 buffers are symmetric."""
+
+    def __init__(self, arena, team, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1):
+        self.arena, self.team = arena, team
+        self.world, self.rank = team.world, team.rank
+        self.lr, (self.beta1, self.beta2), self.eps, self.wd = lr, betas, eps, weight_decay
+        assert arena.numel % (self.world * 128) == 0
+        self.shard_len = arena.numel // self.world
+        self.start = self.rank * self.shard_len
+        self.end = self.start + self.shard_len
+        dev = arena.device
+        self.m = torch.zeros(self.shard_len, dtype=torch.float32, device=dev)
+        self.v = torch.zeros(self.shard_len, dtype=torch.float32, device=dev)
+        blocks = arena.decay_mask.view(-1, 128)[:, 0]
+        self.decay_blocks = blocks.to(torch.uint8).to(dev)
+        self.grad_buf = team.find(arena.grad)
+        self.param_buf = team.find(arena.bf16)
+        self.step_count = 0
+
+    def broadcast_params(self) -> None:
+        if self.world > 1:
+            dist.broadcast(self.arena.master, src=0)
+            self.arena.sync_bf16_from_master()
+
+    def step(self, lr: float | None = None) -> None:
+        self.step_count += 1
+        a = self.arena
+        gb, pb = self.grad_buf, self.param_buf
+        self.team.barrier()  # every rank's gradient is final
+        C().dp_reduce_adamw(gb.peers_dev, gb.mc_ptr, pb.peers_dev, pb.mc_ptr, a.master[self.start : self.end],
+                            self.m, self.v, self.decay_blocks, self.start, self.shard_len, self.world,
+                            float(lr if lr is not None else self.lr), self.beta1, self.beta2, self.eps, self.wd,
+                            self.step_count, 1.0 / self.world, None)
+        self.team.barrier()  # every rank's new parameters have landed everywhere
+
+    def state_dict(self) -> dict:
+        return {"m": self.m.cpu(), "v": self.v.cpu(), "step": self.step_count, "shard": (self.start, self.end)}
+
+
+def team_alloc(team):
+    """Allocator for ParamArena that places buffers in the team's symmetric memory."""
+
+    def alloc(numel, dtype):
+        return team.alloc(numel, dtype).tensor
+
+    return alloc

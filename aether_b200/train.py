@@ -16,15 +16,16 @@ from .parallel.dp import DataParallel
 
 class Trainer:
     def __init__(self, model, info, *, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
-                 micro_batch: int = 8, warmup_steps: int = 0, total_steps: int = 0, max_grad_norm: float = 0.0):
+                 micro_batch: int = 8, warmup_steps: int = 0, total_steps: int = 0, max_grad_norm: float = 0.0,
+                 dp=None):
         self.model = model
         self.info = info
         self.micro_batch = micro_batch
         self.base_lr = lr
         self.warmup = warmup_steps
         self.total = total_steps
-        self.dp = DataParallel(model.arena, info, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
-                               max_grad_norm=max_grad_norm)
+        self.dp = dp if dp is not None else DataParallel(model.arena, info, lr=lr, betas=betas, eps=eps,
+                                                         weight_decay=weight_decay, max_grad_norm=max_grad_norm)
         self.step_idx = 0
         self._loss_acc = torch.zeros(1, dtype=torch.float32, device=model.device)
 

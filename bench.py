@@ -114,6 +114,8 @@ def parse():
     ap.add_argument("--micro-batch", type=int, default=8)
     ap.add_argument("--layers", type=int, default=24, help="debug only; anything but 24 is not the benchmark config")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
+                    help="fused: one-kernel NVLink reduce + AdamW + broadcast; nccl: NCCL reduce-scatter/all-gather")
     return ap.parse_args()
 
 
@@ -143,9 +145,18 @@ def main():
     S = args.seq
     assert args.global_batch % world == 0
     per_rank = args.global_batch // world
-    model = GPT(cfg, device=dev, seed=1234, pad_multiple=world)
+    dp = None
+    if world > 1 and args.dp == "fused":
+        from aether_b200.parallel.dp import FusedDataParallel, team_alloc
+        from aether_b200.parallel.symm import SymmTeam
+
+        team = SymmTeam(info, timeout_s=60.0)
+        model = GPT(cfg, device=dev, seed=1234, pad_multiple=world, alloc=team_alloc(team))
+        dp = FusedDataParallel(model.arena, team, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    else:
+        model = GPT(cfg, device=dev, seed=1234, pad_multiple=world)
     trainer = Trainer(model, info, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
-                      micro_batch=args.micro_batch)
+                      micro_batch=args.micro_batch, dp=dp)
 
     gen = torch.Generator().manual_seed(1000 + info.rank)
     host = [torch.randint(0, cfg.vocab, (per_rank, S + 1), generator=gen, dtype=torch.int64).pin_memory()
@@ -235,7 +246,8 @@ def main():
                 "global_batch": args.global_batch,
                 "seq_len": S,
                 "micro_batch": args.micro_batch,
-                "parallelism": f"dp{world}" + (" zero1" if world > 1 else ""),
+                "parallelism": f"dp{world}" + ((" zero1 " + ("fused-nvlink" if dp is not None else "nccl"))
+                                               if world > 1 else ""),
                 "optimizer": "AdamW lr 3e-4 betas (0.9,0.95) wd 0.1, fp32 master",
                 "l2": "no flush needed: per-step working set (2.7 GB bf16 weights + activations) >> 126 MB L2",
             },

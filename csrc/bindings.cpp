@@ -47,7 +47,16 @@ void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
                    at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset);
 // gemm_skinny.cu
-void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits);
+void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc);
+// comm.cu
+void team_barrier(at::Tensor peer_sig_ptrs, at::Tensor my_sig, at::Tensor epoch, int64_t rank, int64_t world,
+                  double timeout_s);
+void allreduce_oneshot(at::Tensor peers, at::Tensor out, int64_t world);
+void allreduce_nvls(int64_t mc_ptr, int64_t numel, bool is_bf16, int64_t rank, int64_t world);
+void dp_reduce_adamw(at::Tensor grad_peers, int64_t grad_mc, at::Tensor param_peers, int64_t param_mc,
+                     at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor decay_blocks, int64_t begin, int64_t n,
+                     int64_t world, double lr, double beta1, double beta2, double eps, double wd, int64_t step,
+                     double gscale, std::optional<at::Tensor> gscale_t);
 void skinny_finalize(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
                      bool swiglu);
 // decode_attention.cu
@@ -84,7 +93,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_norm", &aether::grad_norm);
   m.def("attention_fwd", &aether::attention_fwd);
   m.def("attention_bwd", &aether::attention_bwd);
-  m.def("skinny_gemm", &aether::skinny_gemm);
+  m.def("skinny_gemm", &aether::skinny_gemm, "x"_a, "w"_a, "acc"_a, "splits"_a = 0, "acc_mc"_a = 0);
+  m.def("team_barrier", &aether::team_barrier);
+  m.def("allreduce_oneshot", &aether::allreduce_oneshot);
+  m.def("allreduce_nvls", &aether::allreduce_nvls);
+  m.def("dp_reduce_adamw", &aether::dp_reduce_adamw);
   m.def("skinny_finalize", &aether::skinny_finalize);
   m.def("rope_kv_append", &aether::rope_kv_append);
   m.def("decode_attention", &aether::decode_attention);

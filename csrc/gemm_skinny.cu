@@ -44,7 +44,10 @@ struct Params {
   int* status;
 };
 
-template <int BN>
+// With MC, `acc` is an NVLS multicast address and the epilogue's reductions go
+// through the switch into every rank's accumulator (tensor-parallel
+// row-parallel layers: GEMM and all-reduce in one kernel).
+template <int BN, bool MC>
 __global__ void __launch_bounds__(kThreads, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, Params p) {
   constexpr int A_BYTES = BM * BK * 2;
@@ -164,7 +167,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int m = c * 16 + j;
-              if (m < p.M) atomicAdd(p.acc + (int64_t)m * p.ldacc + n, __uint_as_float(r[j]));
+              if (m < p.M) {
+                float* dst = p.acc + (int64_t)m * p.ldacc + n;
+                if constexpr (MC)
+                  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(dst), "f"(__uint_as_float(r[j]))
+                               : "memory");
+                else
+                  atomicAdd(dst, __uint_as_float(r[j]));
+              }
             }
           }
         }
@@ -229,11 +239,11 @@ __global__ void finalize_kernel(float* __restrict__ acc, int64_t ldacc, int M, i
   *reinterpret_cast<uint2*>(y + (int64_t)m * ldy + n) = o;
 }
 
-template <int BN>
+template <int BN, bool MC>
 void launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int n_tiles, int splits,
             cudaStream_t stream) {
   constexpr int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
-  auto k = skinny_kernel<BN>;
+  auto k = skinny_kernel<BN, MC>;
   static bool set[64] = {false};
   const int dev = current_device();
   if (!set[dev]) {
@@ -247,14 +257,16 @@ void launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int n
 }  // namespace skinny
 
 // acc[M, N] += x[M, K] . w[N, K]^T (fp32, acc must start zeroed); M <= 64.
-void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits) {
+// acc_mc != 0: reduce into every rank's accumulator through that NVLS
+// multicast address (acc is then this rank's local view of the same buffer).
+void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && acc.is_cuda(), "skinny_gemm: CUDA tensors");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && acc.scalar_type() == at::kFloat,
               "skinny_gemm: bf16 x/w, fp32 acc");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 && acc.stride(1) == 1,
               "skinny_gemm: row-major 2-D operands");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
-  TORCH_CHECK(w.size(1) == K && acc.size(0) == M && acc.size(1) >= N, "skinny_gemm: shapes");
+  TORCH_CHECK(w.size(1) == K && acc.size(0) >= M && acc.size(1) >= N, "skinny_gemm: shapes");
   TORCH_CHECK(M >= 1 && M <= 64, "skinny_gemm: M must be in [1, 64]");
   TORCH_CHECK(K % 8 == 0 && (x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "skinny_gemm: alignment");
   c10::cuda::CUDAGuard g(x.device());
@@ -267,7 +279,7 @@ void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits) {
   const int kbps = (num_kb + (int)splits - 1) / (int)splits;
   const int real_splits = (num_kb + kbps - 1) / kbps;
   skinny::Params p{};
-  p.acc = acc.data_ptr<float>();
+  p.acc = acc_mc != 0 ? reinterpret_cast<float*>(acc_mc) : acc.data_ptr<float>();
   p.ldacc = acc.stride(0);
   p.M = (int)M;
   p.N = (int)N;
@@ -278,9 +290,13 @@ void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits) {
   CUtensorMap tw = make_tmap_2d_bf16(w.data_ptr(), K, N, w.stride(0) * 2, skinny::BK, skinny::BM);
   CUtensorMap tx = make_tmap_2d_bf16(x.data_ptr(), K, M, x.stride(0) * 2, skinny::BK, BN);
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (BN == 16) skinny::launch<16>(tw, tx, p, n_tiles, real_splits, stream);
-  else if (BN == 32) skinny::launch<32>(tw, tx, p, n_tiles, real_splits, stream);
-  else skinny::launch<64>(tw, tx, p, n_tiles, real_splits, stream);
+  const bool mc = acc_mc != 0;
+  if (BN == 16) mc ? skinny::launch<16, true>(tw, tx, p, n_tiles, real_splits, stream)
+                   : skinny::launch<16, false>(tw, tx, p, n_tiles, real_splits, stream);
+  else if (BN == 32) mc ? skinny::launch<32, true>(tw, tx, p, n_tiles, real_splits, stream)
+                        : skinny::launch<32, false>(tw, tx, p, n_tiles, real_splits, stream);
+  else mc ? skinny::launch<64, true>(tw, tx, p, n_tiles, real_splits, stream)
+          : skinny::launch<64, false>(tw, tx, p, n_tiles, real_splits, stream);
 }
 
 // y = bf16(acc (+bias) (+res)), or swiglu over acc's [gate | up] halves when swiglu;

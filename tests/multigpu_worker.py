@@ -1,0 +1,105 @@
+"""Worker for the multi-GPU tests (launched by torchrun from tests/test_multigpu.py).
+
+Checks, on N ranks over NVLink:
+  * team barrier + NVLS / P2P all-reduce (bf16 and fp32) against the plain sum;
+  * fused data-parallel step (reduce + AdamW + broadcast kernel) against the
+    NCCL reduce-scatter / AdamW / all-gather path from identical gradients;
+  * Qwen TP decode (multicast-reduce GEMM) and prefill against TP=1 tokens.
+Prints "OK <name>" lines; any mismatch raises (non-zero exit).
+"""
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from aether_b200 import _ext  # noqa: E402
+from aether_b200.parallel import dist as D  # noqa: E402
+
+
+def check_allreduce(team, info):
+    from aether_b200.parallel.symm import SymmTeam  # noqa: F401
+
+    for dtype in (torch.bfloat16, torch.float32):
+        n = 1 << 16
+        buf = team.alloc(n, dtype)
+        g = torch.Generator(device=info.device).manual_seed(100 + team.rank)
+        x = torch.randn(n, generator=g, device=info.device).to(dtype)
+        buf.tensor.copy_(x)
+        allx = [torch.empty_like(x) for _ in range(team.world)]
+        dist.all_gather(allx, x)
+        ref = torch.stack([a.float() for a in allx]).sum(0)
+        team.all_reduce_(buf)
+        torch.cuda.synchronize()
+        err = float((buf.tensor.float() - ref).norm() / ref.norm())
+        assert err < (1e-2 if dtype == torch.bfloat16 else 1e-6), (dtype, err)
+    print(f"OK allreduce mc={team.has_multicast}", flush=True)
+
+
+def check_fused_dp(info):
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.parallel.dp import DataParallel, FusedDataParallel, team_alloc
+    from aether_b200.parallel.symm import SymmTeam
+
+    cfg = GPTConfig(vocab=512, d_model=256, n_layers=2, n_heads=2, n_kv_heads=2, d_ff=512, max_seq=128)
+    team = SymmTeam(info)
+    m1 = GPT(cfg, device=info.device, seed=5, pad_multiple=info.world, alloc=team_alloc(team))
+    m2 = GPT(cfg, device=info.device, seed=5, pad_multiple=info.world)
+    fused = FusedDataParallel(m1.arena, team, lr=1e-3)
+    base = DataParallel(m2.arena, info, lr=1e-3)
+    toks = torch.randint(0, 512, (2, 129), device=info.device,
+                         generator=torch.Generator(device=info.device).manual_seed(info.rank))
+    for step in range(3):
+        m1.arena.zero_grad()
+        m1.loss(toks[:, :-1].contiguous(), toks[:, 1:].contiguous()).backward()
+        m2.arena.grad.copy_(m1.arena.grad)  # both optimisers see the same gradient
+        fused.step()
+        base.step()
+        torch.cuda.synchronize()
+        d = float((m1.arena.bf16.float() - m2.arena.bf16.float()).abs().max())
+        dm = float((m1.arena.master[fused.start:fused.end] - m2.arena.master[base.start:base.end]).abs().max())
+        assert dm < 1e-5 and d < 1e-2, (step, d, dm)
+        m2.arena.bf16.copy_(m1.arena.bf16)  # keep both forwards identical
+    assert _ext.check_status() == 0
+    print(f"OK fused_dp mc={team.has_multicast}", flush=True)
+
+
+def check_tp_qwen(info):
+    from aether_b200.models.qwen import QwenConfig, QwenModel
+    from aether_b200.parallel.tp import TensorParallel
+
+    cfg = QwenConfig(vocab=2048, d_model=1024, n_layers=2, n_heads=8, n_kv_heads=2, d_ff=2048, max_seq=512,
+                     init_std=0.05)
+    tp = TensorParallel(info)
+    mt = QwenModel(cfg, device=info.device, seed=3, max_batch=4, max_seq=512, tp=tp)
+    m1 = QwenModel(cfg, device=info.device, seed=3, max_batch=4, max_seq=512)
+    prompts = torch.randint(0, cfg.vocab, (3, 33), device=info.device, generator=torch.Generator(device=info.device).manual_seed(9))
+    out_t = mt.generate(prompts, 8, use_graph=True)
+    out_1 = m1.generate(prompts, 8, use_graph=False)
+    agree = float((out_t == out_1).float().mean())
+    assert agree > 0.9, (agree, out_t, out_1)
+    assert _ext.check_status() == 0
+    print(f"OK tp_qwen agree={agree:.3f} mc={tp.team.has_multicast}", flush=True)
+
+
+def main():
+    info = D.init(timeout_s=120)
+    from aether_b200.parallel.symm import SymmTeam
+
+    team = SymmTeam(info)
+    which = sys.argv[1:] or ["allreduce", "dp", "tp"]
+    if "allreduce" in which:
+        check_allreduce(team, info)
+    if "dp" in which:
+        check_fused_dp(info)
+    if "tp" in which:
+        check_tp_qwen(info)
+    torch.cuda.synchronize()
+    dist.barrier()
+    D.shutdown()
+
+
+if __name__ == "__main__":
+    main()
