@@ -172,6 +172,8 @@ class QwenModel:
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.decode_splits = decode_splits or self._auto_splits()
+        import os as _os
+        self.fused_decode = _os.environ.get("AETHER_UNFUSED_DECODE", "0") != "1"
         self._graphs: dict[int, tuple] = {}
         self._alloc_decode_buffers()
 
@@ -202,6 +204,7 @@ class QwenModel:
             "part_o": torch.empty(B * self.hq * self.decode_splits * D, dtype=torch.float32, device=dev),
             "part_lse": torch.empty(B * self.hq * self.decode_splits, dtype=torch.float32, device=dev),
             "next": torch.zeros(B, dtype=torch.long, device=dev),
+            "counters": torch.zeros(B * self.hkv, dtype=torch.int32, device=dev),
         }
 
     # ------------------------------------------------------------------ prefill
@@ -258,7 +261,53 @@ class QwenModel:
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int) -> None:
-        """One greedy decode step for the first B rows of the static buffers."""
+        """One greedy decode step for the first B rows of the static buffers.
+
+        Per layer (9 kernels): qkv GEMM -> fused bias+RoPE+KV-append ->
+        split-K attention with in-kernel combine -> o_proj GEMM (TP: with the
+        all-reduce fused in its epilogue) -> fused residual+RMSNorm -> gate/up
+        GEMM -> SwiGLU finalise -> down GEMM (TP: reduce fused) -> fused
+        residual+RMSNorm of the next layer. The GEMMs use programmatic
+        dependent launch, so their weight stream starts while the preceding
+        small kernel still runs."""
+        cfg, w, b = self.cfg, self.w, self.buf
+        D = cfg.head_dim
+        x, x2, h = b["x"][:B], b["x2"][:B], b["h"][:B]
+        qkv, o, act, acc = b["qkv"][:B], b["o"][:B], b["act"][:B], b["acc"][:B]
+        pos, slot, seqlen = b["pos"][:B], b["slot"][:B], b["seqlen"][:B]
+        x.copy_(F.embedding(w.embed, b["tok"][:B]))
+        F.rmsnorm_into(x, w.attn_norm[0], h, cfg.norm_eps)
+        L = cfg.n_layers
+        for i in range(L):
+            F.skinny_gemm(h, w.wqkv[i], acc)
+            F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i],
+                                self.hq, self.hkv, D)
+            F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
+                               self.decode_splits, b["part_o"], b["part_lse"], b["counters"])
+            if self.tp is None:
+                F.skinny_gemm(o, w.wo[i], acc)
+                racc = acc
+            else:
+                racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
+            F.finalize_residual_norm(racc, x2, w.mlp_norm[i], h, res=x, eps=cfg.norm_eps)
+            F.skinny_gemm(h, w.wgu[i], acc)
+            F.skinny_finalize(acc, act, swiglu=True)
+            if self.tp is None:
+                F.skinny_gemm(act, w.wd[i], acc)
+                racc = acc
+            else:
+                racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
+            nw = w.attn_norm[i + 1] if i + 1 < L else w.final_norm
+            F.finalize_residual_norm(racc, x, nw, h, res=x2, eps=cfg.norm_eps)
+        F.skinny_gemm(h, w.lm_head, acc)
+        b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
+        acc.zero_()
+
+    def _step_body(self, B: int) -> None:
+        (self._decode_body if self.fused_decode else self._decode_body_unfused)(B)
+
+    def _decode_body_unfused(self, B: int) -> None:
+        """Decode step with separate norm / RoPE / combine kernels (13 per layer)."""
         cfg, w, b = self.cfg, self.w, self.buf
         D = cfg.head_dim
         x, x2, h = b["x"][:B], b["x2"][:B], b["h"][:B]
@@ -276,7 +325,7 @@ class QwenModel:
                 F.skinny_gemm(o, w.wo[i], acc)
                 F.skinny_finalize(acc, x2, res=x)
             else:
-                racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
+                racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)
                 F.skinny_finalize(racc, x2, res=x)
             F.rmsnorm_into(x2, w.mlp_norm[i], h, cfg.norm_eps)
             F.skinny_gemm(h, w.wgu[i], acc)
@@ -307,11 +356,11 @@ class QwenModel:
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for _ in range(2):  # warm up allocations and tensor maps outside the graph
-                self._decode_body(B)
+                self._step_body(B)
         torch.cuda.current_stream(self.device).wait_stream(s)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            self._decode_body(B)
+            self._step_body(B)
         self._graphs[B] = g
 
     @torch.no_grad()
@@ -337,7 +386,7 @@ class QwenModel:
                 self.capture(Bb)
             self._graphs[Bb].replay()
         else:
-            self._decode_body(Bb)
+            self._step_body(Bb)
         return b["next"][:B]
 
     @torch.no_grad()

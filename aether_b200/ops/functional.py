@@ -358,7 +358,8 @@ def rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D):
     return qkv
 
 
-def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8, part_o=None, part_lse=None):
+def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8, part_o=None, part_lse=None,
+                     counters=None):
     """q [B, >=Hq*D] (one new token per sequence), caches [slots, max_seq, Hkv, D],
     seqlen [B] = valid keys. Writes out [B, Hq*D]."""
     B = q.shape[0]
@@ -368,7 +369,7 @@ def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8
             part_o = torch.empty(B * Hq * splits * D, dtype=torch.float32, device=q.device)
             part_lse = torch.empty(B * Hq * splits, dtype=torch.float32, device=q.device)
         C().decode_attention(q, k_cache, v_cache, slot, seqlen, out, part_o, part_lse, int(Hq), int(splits),
-                             float(scale))
+                             float(scale), counters)
         return out
     Hkv = k_cache.shape[2]
     for b in range(B):
@@ -390,3 +391,35 @@ def rmsnorm_into(x, w, out, eps=1e-6):
     y, _, _ = ref.rmsnorm(x, w, eps)
     out.copy_(y.to(out.dtype))
     return out
+
+
+def qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D):
+    """Decode QKV epilogue: qkv = rope(bf16(acc + bias)); k/v appended to the
+    caches at (slot, pos); acc zeroed."""
+    if _cuda(acc):
+        C().qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, int(Hq), int(Hkv), int(D))
+        return qkv
+    B, W = qkv.shape[0], (Hq + 2 * Hkv) * D
+    a = acc[:B, :W].clone()
+    if bias is not None:
+        a = a + bias.float()
+    qkv[:, :W].copy_(a.to(qkv.dtype))
+    acc[:B, :W] = 0
+    return rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D)
+
+
+def finalize_residual_norm(acc, y, w, h, bias=None, res=None, eps=1e-6):
+    """y = bf16(acc + bias + res) (residual stream); h = rmsnorm(y) * w; acc zeroed."""
+    if _cuda(acc):
+        C().finalize_residual_norm(acc, bias, res, y, w, h, float(eps))
+        return y, h
+    B, N = y.shape
+    a = acc[:B, :N].clone()
+    if bias is not None:
+        a = a + bias.float()
+    if res is not None:
+        a = a + res.float()
+    y.copy_(a.to(y.dtype))
+    acc[:B, :N] = 0
+    rmsnorm_into(y, w, h, eps)
+    return y, h

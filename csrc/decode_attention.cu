@@ -27,6 +27,8 @@ namespace dec {
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxGroup = 8;
+constexpr int kMaxSplits = 64;
+constexpr int kKvSmem = 2 * 128 * 256;  // staged K and V blocks
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
   v[0] = bf16lo(u.x); v[1] = bf16hi(u.x); v[2] = bf16lo(u.y); v[3] = bf16hi(u.y);
@@ -99,13 +101,26 @@ struct DecParams {
   const int* seqlen;                // [B] number of valid keys
   float* part_o;                    // [B, Hq, splits, D]
   float* part_lse;                  // [B, Hq, splits]
+  int* counters;                    // [B * Hkv] zero-initialised; the last split CTA merges
+  __nv_bfloat16* out;               // [B, out_rs]
+  int64_t out_rs;
   int Hq, Hkv, splits;
   float scale_log2;
 };
 
-// grid (splits, B * Hkv), 128 threads. D == 128.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0) : "memory");
+}
+
+// grid (splits, B * Hkv), 128 threads, D == 128. Each 128-key block of the
+// split is staged into shared memory with one burst of cp.async (K and V rows,
+// 16-byte chunks XOR-swizzled by row so the lane-per-key reads of K are
+// conflict-free), then: scores lane-per-key, online softmax per query head,
+// P.V with lanes over head dims.
 __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
   constexpr int D = 128;
+  constexpr int KB = 128;  // keys per shared-memory block
+  asm volatile("griddepcontrol.launch_dependents;");
   const int split = blockIdx.x;
   const int b = blockIdx.y / p.Hkv, hk = blockIdx.y % p.Hkv;
   const int G = p.Hq / p.Hkv;
@@ -114,9 +129,11 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
   __shared__ float sp[4][kMaxGroup][32];
   __shared__ float sm_m[4][kMaxGroup], sm_l[4][kMaxGroup];
   __shared__ float so[4][kMaxGroup][D];
+  extern __shared__ __align__(128) uint8_t kv_smem[];  // K block then V block, 128 rows x 256 B each
+  const uint32_t sK = smem_u32(kv_smem), sV = sK + KB * 256;
 
   const int len = p.seqlen[b];
-  const int per = ((len + p.splits - 1) / p.splits + 127) / 128 * 128;
+  const int per = ((len + p.splits - 1) / p.splits + KB - 1) / KB * KB;
   const int k_begin = split * per;
   const int k_end = min(len, k_begin + per);
 
@@ -124,7 +141,6 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
     const int g = i / D, d = i % D;
     sq[g][d] = __bfloat162float(p.q[(int64_t)b * p.q_rs + (int64_t)(hk * G + g) * D + d]) * p.scale_log2;
   }
-  __syncthreads();
 
   const int s = p.slot[b];
   const __nv_bfloat16* kbase = p.kc + (int64_t)s * p.slot_stride + (int64_t)hk * D;
@@ -136,36 +152,44 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
     l[g] = 0.f;
     o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
   }
-  for (int kb = k_begin + warp * 32; kb < k_end; kb += 128) {
-    const int key = kb + lane;
+  for (int blk = k_begin; blk < k_end; blk += KB) {
+    const int nblk = min(KB, k_end - blk);
+    // stage K and V rows of this block (16 chunks of 16 B per row)
+    for (int i = threadIdx.x; i < KB * 16; i += 128) {
+      const int r = i >> 4, c = i & 15;
+      const bool ok = r < nblk;
+      const uint32_t off = (uint32_t)(r * 256 + ((c ^ (r & 15)) << 4));
+      cp_async16(sK + off, kbase + (int64_t)(ok ? blk + r : blk) * p.pos_stride + c * 8, ok);
+      cp_async16(sV + (uint32_t)(r * 256 + (c << 4)), vbase + (int64_t)(ok ? blk + r : blk) * p.pos_stride + c * 8, ok);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const int r = warp * 32 + lane;  // this lane's key within the block
+    const bool valid = r < nblk;
     float sc[kMaxGroup];
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g) sc[g] = 0.f;
-    if (key < k_end) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kbase + (int64_t)key * p.pos_stride);
 #pragma unroll 4
-      for (int c = 0; c < D / 8; ++c) {
-        float kv[8];
-        unpack8(kr[c], kv);
+    for (int c = 0; c < 16; ++c) {
+      float kv[8];
+      unpack8(*reinterpret_cast<const uint4*>(kv_smem + r * 256 + ((c ^ (r & 15)) << 4)), kv);
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; ++g) {
-          if (g < G) {
+      for (int g = 0; g < kMaxGroup; ++g) {
+        if (g < G) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) sc[g] += sq[g][c * 8 + j] * kv[j];
-          }
+          for (int j = 0; j < 8; ++j) sc[g] += sq[g][c * 8 + j] * kv[j];
         }
       }
-    } else {
-#pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) sc[g] = -INFINITY;
     }
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g) {
       if (g < G) {
-        const float bm = warp_max(sc[g]);
+        const float x = valid ? sc[g] : -INFINITY;
+        const float bm = warp_max(x);
         const float mn = fmaxf(m[g], bm);
-        const float alpha = exp2f(m[g] - mn);  // m = -inf on the first block -> 0
-        const float pe = key < k_end ? exp2f(sc[g] - mn) : 0.f;
+        const float base = mn == -INFINITY ? 0.f : mn;
+        const float alpha = exp2f(m[g] - base);
+        const float pe = valid ? exp2f(x - base) : 0.f;
         l[g] = l[g] * alpha + warp_sum(pe);
         m[g] = mn;
         o[g][0] *= alpha; o[g][1] *= alpha; o[g][2] *= alpha; o[g][3] *= alpha;
@@ -173,9 +197,10 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
       }
     }
     __syncwarp();
-    const int nkeys = min(32, k_end - kb);
+    const int nkeys = min(32, nblk - warp * 32);
+    const uint8_t* vrow = kv_smem + KB * 256 + (warp * 32) * 256 + lane * 8;
     for (int j = 0; j < nkeys; ++j) {
-      const uint2 vv = *reinterpret_cast<const uint2*>(vbase + (int64_t)(kb + j) * p.pos_stride + lane * 4);
+      const uint2 vv = *reinterpret_cast<const uint2*>(vrow + j * 256);
       const float v0 = bf16lo(vv.x), v1 = bf16hi(vv.x), v2 = bf16lo(vv.y), v3 = bf16hi(vv.y);
 #pragma unroll
       for (int g = 0; g < kMaxGroup; ++g) {
@@ -185,7 +210,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
         }
       }
     }
-    __syncwarp();
+    __syncthreads();  // the next block overwrites the staged K/V
   }
   // merge the 4 warps
 #pragma unroll
@@ -221,6 +246,45 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
     p.part_o[idx * D + d] = ll > 0.f ? acc / ll : 0.f;
     if (d == 0) p.part_lse[idx] = ll > 0.f ? mm + __log2f(ll) : -INFINITY;  // log2 domain
   }
+  if (p.counters == nullptr) return;
+  // The last split CTA of this (sequence, KV head) merges all splits.
+  __threadfence();
+  __syncthreads();
+  __shared__ int s_last;
+  if (threadIdx.x == 0) s_last = atomicAdd(p.counters + blockIdx.y, 1) == p.splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // Per-split merge weights for every head of the group, computed once.
+  __shared__ float s_w[kMaxGroup][kMaxSplits];
+  for (int i = threadIdx.x; i < G * p.splits; i += 128) {
+    const int g = i / p.splits, s2 = i % p.splits;
+    s_w[g][s2] = __ldcg(p.part_lse + ((int64_t)b * p.Hq + hk * G + g) * p.splits + s2);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float mx = -INFINITY;
+    for (int s2 = 0; s2 < p.splits; ++s2) mx = fmaxf(mx, s_w[g][s2]);
+    float tot = 0.f;
+    for (int s2 = 0; s2 < p.splits; ++s2) {
+      const float w = s_w[g][s2] == -INFINITY ? 0.f : exp2f(s_w[g][s2] - mx);
+      s_w[g][s2] = w;
+      tot += w;
+    }
+    const float inv = tot > 0.f ? 1.f / tot : 0.f;
+    for (int s2 = 0; s2 < p.splits; ++s2) s_w[g][s2] *= inv;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += 128) {
+    const int g = i / D, d = i % D;
+    const int hq = hk * G + g;
+    const float* po = p.part_o + (((int64_t)b * p.Hq + hq) * p.splits) * D + d;
+    float acc = 0.f;
+    for (int s2 = 0; s2 < p.splits; ++s2) acc += s_w[g][s2] * __ldcg(po + (int64_t)s2 * D);
+    p.out[(int64_t)b * p.out_rs + (int64_t)hq * D + d] = __float2bfloat16(acc);
+  }
+  if (threadIdx.x == 0) p.counters[blockIdx.y] = 0;  // ready for the next step (graph replay)
 }
 
 // out[b, h*D + d] = sum_s w_s * part_o[b,h,s,d], w_s = 2^(lse_s - lse)
@@ -239,6 +303,113 @@ __global__ void decode_combine_kernel(const float* __restrict__ part_o, const fl
       if (lse[s] != -INFINITY) acc += exp2f(lse[s] - mx) * part_o[((int64_t)bh * splits + s) * D + d];
     }
     out[(int64_t)b * out_rs + (int64_t)h * D + d] = __float2bfloat16(tot > 0.f ? acc / tot : 0.f);
+  }
+}
+
+// Decode QKV finalisation: qkv = acc + bias, RoPE on q/k at pos, q (and k)
+// written to the bf16 qkv rows, k/v appended to the cache; acc re-zeroed.
+// One thread per (row, head, 8-wide chunk of the half head).
+__global__ void qkv_finalize_rope_kernel(float* __restrict__ acc, int64_t ldacc, const __nv_bfloat16* __restrict__ bias,
+                                         __nv_bfloat16* __restrict__ qkv, int64_t row, const int* __restrict__ pos,
+                                         const int* __restrict__ slot, const float* __restrict__ cos_t,
+                                         const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ kc,
+                                         __nv_bfloat16* __restrict__ vc, int B, int Hq, int Hkv, int D,
+                                         int64_t slot_stride, int64_t pos_stride) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int half = D / 2, chunks = half / 8;
+  const int H = Hq + 2 * Hkv;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)B * H * chunks) return;
+  const int c = (int)(i % chunks) * 8;
+  const int h = (int)((i / chunks) % H);
+  const int b = (int)(i / ((int64_t)chunks * H));
+  float* ar = acc + (int64_t)b * ldacc + (int64_t)h * D;
+  float a[8], bb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    a[j] = ar[c + j];
+    bb[j] = ar[half + c + j];
+    ar[c + j] = 0.f;
+    ar[half + c + j] = 0.f;
+  }
+  if (bias) {
+    const __nv_bfloat16* br = bias + (int64_t)h * D;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      a[j] += __bfloat162float(br[c + j]);
+      bb[j] += __bfloat162float(br[half + c + j]);
+    }
+  }
+  // round to bf16 first (the values the prefill path stores), then rotate
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    a[j] = __bfloat162float(__float2bfloat16(a[j]));
+    bb[j] = __bfloat162float(__float2bfloat16(bb[j]));
+  }
+  const int p_ = pos[b];
+  if (h < Hq + Hkv) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float cs = cos_t[(int64_t)p_ * half + c + j], sn = sin_t[(int64_t)p_ * half + c + j];
+      const float x1 = a[j], x2 = bb[j];
+      a[j] = x1 * cs - x2 * sn;
+      bb[j] = x2 * cs + x1 * sn;
+    }
+  }
+  const uint4 ua = pack8(a), ub = pack8(bb);
+  __nv_bfloat16* qr = qkv + (int64_t)b * row + (int64_t)h * D;
+  *reinterpret_cast<uint4*>(qr + c) = ua;
+  *reinterpret_cast<uint4*>(qr + half + c) = ub;
+  if (h >= Hq) {
+    const bool is_k = h < Hq + Hkv;
+    const int hk = is_k ? h - Hq : h - Hq - Hkv;
+    __nv_bfloat16* dst = (is_k ? kc : vc) + (int64_t)slot[b] * slot_stride + (int64_t)p_ * pos_stride + (int64_t)hk * D;
+    *reinterpret_cast<uint4*>(dst + c) = ua;
+    *reinterpret_cast<uint4*>(dst + half + c) = ub;
+  }
+}
+
+// y = bf16(acc + bias + res) (the residual stream), h = rmsnorm(y) * w; acc
+// re-zeroed. One CTA per row.
+__global__ void __launch_bounds__(1024) finalize_residual_norm_kernel(float* __restrict__ acc, int64_t ldacc, int N,
+                                                                     const __nv_bfloat16* __restrict__ bias,
+                                                                     const __nv_bfloat16* __restrict__ res,
+                                                                     __nv_bfloat16* __restrict__ y,
+                                                                     const __nv_bfloat16* __restrict__ w,
+                                                                     __nv_bfloat16* __restrict__ h, float eps) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  constexpr int kMaxPer = 8;  // N <= 1024 * 8 = 8192
+  const int r = blockIdx.x;
+  float* ar = acc + (int64_t)r * ldacc;
+  float v[kMaxPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int c = threadIdx.x + k * 1024;
+    v[k] = 0.f;
+    if (c < N) {
+      float x = ar[c];
+      ar[c] = 0.f;
+      if (bias) x += __bfloat162float(bias[c]);
+      if (res) x += __bfloat162float(res[(int64_t)r * N + c]);
+      const __nv_bfloat16 xb = __float2bfloat16(x);
+      y[(int64_t)r * N + c] = xb;
+      v[k] = __bfloat162float(xb);
+      ss += v[k] * v[k];
+    }
+  }
+  ss = warp_sum(ss);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) tot += red[k];
+  const float rstd = rsqrtf(tot / N + eps);
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int c = threadIdx.x + k * 1024;
+    if (c < N) h[(int64_t)r * N + c] = __float2bfloat16(v[k] * rstd * __bfloat162float(w[c]));
   }
 }
 
@@ -270,7 +441,7 @@ void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor 
 // q: [B, q_rs] (head h at h*D); out: [B, out_rs]; part buffers sized [B*Hq*splits*(D+1)].
 void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slot, at::Tensor seqlen,
                       at::Tensor out, at::Tensor part_o, at::Tensor part_lse, int64_t Hq, int64_t splits,
-                      double scale) {
+                      double scale, std::optional<at::Tensor> counters) {
   const int64_t B = q.size(0);
   const int64_t Hkv = k_cache.size(2), D = k_cache.size(3);
   TORCH_CHECK(D == 128, "decode_attention: head_dim 128");
@@ -294,12 +465,70 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
   p.Hkv = (int)Hkv;
   p.splits = (int)splits;
   p.scale_log2 = (float)scale * dec::kLog2e;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_rs = out.stride(0);
   auto stream = at::cuda::getCurrentCUDAStream();
-  dec::decode_attn_kernel<<<dim3((unsigned)splits, (unsigned)(B * Hkv)), 128, 0, stream>>>(p);
+  static bool attr_set[64] = {false};
+  const int dev = current_device();
+  if (!attr_set[dev]) {
+    AETHER_CUDA_CHECK(cudaFuncSetAttribute(dec::decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kKvSmem));
+    attr_set[dev] = true;
+  }
+  if (counters && counters->defined()) {
+    TORCH_CHECK(counters->scalar_type() == at::kInt && counters->numel() >= B * Hkv, "decode_attention: counters");
+    TORCH_CHECK(splits <= dec::kMaxSplits, "decode_attention: at most 64 splits with the fused combine");
+    p.counters = counters->data_ptr<int>();
+    dec::decode_attn_kernel<<<dim3((unsigned)splits, (unsigned)(B * Hkv)), 128, dec::kKvSmem, stream>>>(p);
+    AETHER_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
+  dec::decode_attn_kernel<<<dim3((unsigned)splits, (unsigned)(B * Hkv)), 128, dec::kKvSmem, stream>>>(p);
   AETHER_CUDA_CHECK(cudaGetLastError());
   dec::decode_combine_kernel<<<(unsigned)(B * Hq), 128, 0, stream>>>(
       p.part_o, p.part_lse, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), (int)Hq, (int)splits,
       (int)D);
+  AETHER_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace aether
+
+namespace aether {
+
+// Decode QKV epilogue: qkv rows = rope(acc + bias); k/v appended to the caches; acc zeroed.
+void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tensor qkv, at::Tensor pos, at::Tensor slot,
+                       at::Tensor cos_t, at::Tensor sin_t, at::Tensor k_cache, at::Tensor v_cache, int64_t Hq,
+                       int64_t Hkv, int64_t D) {
+  const int64_t B = qkv.size(0);
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.size(1) >= (Hq + 2 * Hkv) * D, "qkv_finalize_rope: acc");
+  TORCH_CHECK(qkv.stride(1) == 1 && qkv.stride(0) % 8 == 0 && D % 16 == 0, "qkv_finalize_rope: qkv layout");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "qkv_finalize_rope: caches");
+  c10::cuda::CUDAGuard g(acc.device());
+  const int64_t n = B * (Hq + 2 * Hkv) * (D / 16);
+  if (n == 0) return;
+  dec::qkv_finalize_rope_kernel<<<(unsigned)((n + 127) / 128), 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      acc.data_ptr<float>(), acc.stride(0),
+      (bias && bias->defined()) ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
+      reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), pos.data_ptr<int>(), slot.data_ptr<int>(),
+      cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), (int)B, (int)Hq, (int)Hkv, (int)D, k_cache.stride(0),
+      k_cache.stride(1));
+  AETHER_CUDA_CHECK(cudaGetLastError());
+}
+
+// y = bf16(acc + bias + res); h = rmsnorm(y) * w; acc zeroed. y/h/res: [B, N] contiguous.
+void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
+                            at::Tensor y, at::Tensor w, at::Tensor h, double eps) {
+  const int64_t B = y.size(0), N = y.size(1);
+  TORCH_CHECK(N <= 8192 && y.is_contiguous() && h.is_contiguous(), "finalize_residual_norm: rows up to 8192, contiguous");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.size(1) >= N, "finalize_residual_norm: acc");
+  c10::cuda::CUDAGuard g(acc.device());
+  if (B == 0) return;
+  dec::finalize_residual_norm_kernel<<<(unsigned)B, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      acc.data_ptr<float>(), acc.stride(0), (int)N,
+      (bias && bias->defined()) ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
+      (res && res->defined()) ? reinterpret_cast<const __nv_bfloat16*>(res->data_ptr()) : nullptr,
+      reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), (float)eps);
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 

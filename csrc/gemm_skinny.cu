@@ -7,7 +7,7 @@
 // batch rows are its N dimension (16/32/64) -- and splits K so that every SM
 // streams a slice of W:
 //
-//   grid = (N/128 weight-row tiles) x (K splits), one tile per CTA
+//   grid = one wave of CTAs; stream-K over (weight-row tile, K block) units
 //   warp 0      : TMA producer, 8-deep ring of (128 x 64 W) + (BN x 64 x) tiles
 //   warp 1      : TMEM allocator + single-thread tcgen05.mma issuer (M128, N=BN)
 //   warps 2..5  : epilogue -- tcgen05.ld, then fp32 atomics into acc[M, N]
@@ -21,6 +21,8 @@
 // Reference counterpart: the decode GEMVs fused_*_matmul_seq1 and the batched
 // seqB variants (runtime/src/cuda.rs:3347-4010, 903-1001), which run one
 // thread block per output row on CUDA cores.
+#include <cstdlib>
+
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -37,13 +39,19 @@ constexpr int STAGES = 8;
 constexpr int kThreads = 192;
 
 struct Params {
-  float* acc;  // [M, ldacc] fp32, pre-zeroed
+  float* acc;  // [M, ldacc] fp32, pre-zeroed (or an NVLS multicast address)
   int64_t ldacc;
   int M, N, K;
-  int k_blocks_per_split;
+  int num_kb;      // K blocks of 64
+  int64_t units;   // (weight-row tile, K block) pairs: n_tiles * num_kb
   int* status;
 };
 
+// Stream-K partition: CTA c owns units [c*U/G, (c+1)*U/G) in tile-major order
+// (u = tile * num_kb + kb) and walks them as per-tile segments; every segment
+// ends in an accumulator hand-off to the epilogue, which adds the partial sums
+// into the fp32 output with atomics. One wave of CTAs, equal weight bytes each.
+//
 // With MC, `acc` is an NVLS multicast address and the epilogue's reductions go
 // through the switch into every rank's accumulator (tensor-parallel
 // row-parallel layers: GEMM and all-reduce in one kernel).
@@ -53,7 +61,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  constexpr int ACC_COLS = BN < 32 ? 32 : BN;
+  constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered accumulator
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -61,23 +70,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_n = blockIdx.x;
-  const int split = blockIdx.y;
-  const int num_kb = (p.K + BK - 1) / BK;
-  const int kb0 = split * p.k_blocks_per_split;
-  const int kb1 = min(num_kb, kb0 + p.k_blocks_per_split);
-  const int nk = kb1 - kb0;
+  const int64_t u0 = (int64_t)blockIdx.x * p.units / gridDim.x;
+  const int64_t u1 = (int64_t)(blockIdx.x + 1) * p.units / gridDim.x;
+  const int nkb = p.num_kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tfull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
     *abort_word = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
@@ -92,42 +104,70 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (nk > 0) {
-    if (warp == 0 && lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued = 0;
-      bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_word)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-        tma_load_2d(sA + stage * A_BYTES, &tmW, &full[stage], kb * BK, tile_n * BM);
-        tma_load_2d(sB + stage * B_BYTES, &tmX, &full[stage], kb * BK, 0);
-        ++issued;
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    // The weights do not depend on the previous kernel: with programmatic
+    // dependent launch this CTA may start while that kernel still runs, so
+    // the first ring of weight tiles is requested before waiting for it; only
+    // the activation tiles (x) are loaded after griddepcontrol.wait.
+    const int pre = (int)((u1 - u0) < (int64_t)STAGES ? (u1 - u0) : (int64_t)STAGES);
+    for (int i = 0; i < pre; ++i) {
+      const int64_t u = u0 + i;
+      asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&full[i])),
+                   "r"((uint32_t)STAGE_BYTES)
+                   : "memory");
+      tma_load_2d(sA + i * A_BYTES, &tmW, &full[i], (int)(u % nkb) * BK, (int)(u / nkb) * BM);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int i = 0; i < pre; ++i) {
+      tma_load_2d(sB + i * B_BYTES, &tmX, &full[i], (int)((u0 + i) % nkb) * BK, 0);
+      mbar_arrive(&full[i]);
+    }
+    int stage = pre % STAGES;
+    uint32_t phase = pre == STAGES ? 1u : 0u;
+    uint32_t issued = pre;
+    bool ok = true;
+    for (int64_t u = u0 + pre; u < u1; ++u) {
+      if (!mbar_wait(&empty[stage], phase ^ 1u, abort_word)) {
+        ok = false;
+        break;
       }
-      if (!ok) {
-        *abort_word = 1;
-        atomicExch(p.status, kStatusTimeoutProducer);
-        volatile int never = 0;
-        const uint32_t n_back = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
-        for (uint32_t j = 1; j <= n_back; ++j) {
-          const uint32_t i = issued - j;
-          mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never);
-        }
+      mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+      tma_load_2d(sA + stage * A_BYTES, &tmW, &full[stage], (int)(u % nkb) * BK, (int)(u / nkb) * BM);
+      tma_load_2d(sB + stage * B_BYTES, &tmX, &full[stage], (int)(u % nkb) * BK, 0);
+      ++issued;
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
       }
-    } else if (warp == 1 && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int i = 0; i < nk; ++i) {
+    }
+    if (!ok) {
+      *abort_word = 1;
+      atomicExch(p.status, kStatusTimeoutProducer);
+      volatile int never = 0;
+      const uint32_t n_back = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
+      for (uint32_t j = 1; j <= n_back; ++j) {
+        const uint32_t i = issued - j;
+        mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int64_t u = u0; u < u1 && ok;) {
+      const int64_t seg_end = min(u1, (u / nkb + 1) * nkb);
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_word)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+      for (int64_t v = u; v < seg_end; ++v) {
         if (!mbar_wait(&full[stage], phase, abort_word)) {
           ok = false;
           break;
@@ -137,51 +177,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          umma_f16(tmem_base, sdesc_sw128(a_base + kk * 32, 16, 1024), sdesc_sw128(b_base + kk * 32, 16, 1024), idesc,
-                   (i | kk) != 0 ? 1u : 0u);
+          umma_f16(d_tmem, sdesc_sw128(a_base + kk * 32, 16, 1024), sdesc_sw128(b_base + kk * 32, 16, 1024), idesc,
+                   (v != u || kk != 0) ? 1u : 0u);
         umma_commit(&empty[stage]);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
         }
       }
-      if (!ok) {
+      if (!ok) break;
+      umma_commit(&tfull[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+      u = seg_end;
+    }
+    if (!ok) {
+      *abort_word = 1;
+      atomicExch(p.status, kStatusTimeoutMma);
+    }
+    volatile int never = 0;
+    umma_commit(drain);  // TMEM is not freed while an MMA may still write it
+    mbar_wait(drain, 0, &never);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t u = u0; u < u1;) {
+      const int64_t tile = u / nkb;
+      const int64_t seg_end = min(u1, (tile + 1) * nkb);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_word)) {
         *abort_word = 1;
-        atomicExch(p.status, kStatusTimeoutMma);
+        if (lane == 0) atomicExch(p.status, kStatusTimeoutEpilogue);
+        break;
       }
-      umma_commit(tfull);  // arrives once every MMA issued above has completed
-      volatile int never = 0;
-      mbar_wait(tfull, 0, &never);  // TMEM is not freed while an MMA may still write it
-    } else if (warp >= 2) {
-      const int quad = warp & 3;
-      const int n = tile_n * BM + quad * 32 + lane;
-      if (mbar_wait(tfull, 0, abort_word)) {
-        __syncwarp();
-        tc_fence_after();
+      __syncwarp();
+      tc_fence_after();
+      const int n = (int)tile * BM + quad * 32 + lane;
 #pragma unroll
-        for (int c = 0; c < (BN + 15) / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + c * 16, r);
-          tmem_ld_wait();
-          if (n < p.N) {
+      for (int c = 0; c < (BN + 15) / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * ACC_COLS + c * 16, r);
+        tmem_ld_wait();
+        if (n < p.N) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = c * 16 + j;
-              if (m < p.M) {
-                float* dst = p.acc + (int64_t)m * p.ldacc + n;
-                if constexpr (MC)
-                  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(dst), "f"(__uint_as_float(r[j]))
-                               : "memory");
-                else
-                  atomicAdd(dst, __uint_as_float(r[j]));
-              }
+          for (int j = 0; j < 16; ++j) {
+            const int m = c * 16 + j;
+            if (m < p.M) {
+              float* dst = p.acc + (int64_t)m * p.ldacc + n;
+              if constexpr (MC)
+                asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(dst), "f"(__uint_as_float(r[j]))
+                             : "memory");
+              else
+                atomicAdd(dst, __uint_as_float(r[j]));
             }
           }
         }
-      } else {
-        *abort_word = 1;
-        if (lane == 0) atomicExch(p.status, kStatusTimeoutEpilogue);
       }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+      u = seg_end;
     }
   }
   tc_fence_before();
@@ -199,6 +256,7 @@ template <bool SWIGLU>
 __global__ void finalize_kernel(float* __restrict__ acc, int64_t ldacc, int M, int Nout,
                                 const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ res,
                                 int64_t ldr, __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // 4-wide chunk of the output
   const int chunks = Nout / 4;
   if (i >= (int64_t)M * chunks) return;
@@ -240,8 +298,7 @@ __global__ void finalize_kernel(float* __restrict__ acc, int64_t ldacc, int M, i
 }
 
 template <int BN, bool MC>
-void launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int n_tiles, int splits,
-            cudaStream_t stream) {
+void launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int grid, cudaStream_t stream) {
   constexpr int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   auto k = skinny_kernel<BN, MC>;
   static bool set[64] = {false};
@@ -250,8 +307,20 @@ void launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int n
     AETHER_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     set[dev] = true;
   }
-  k<<<dim3(n_tiles, splits), kThreads, smem, stream>>>(tw, tx, p);
-  AETHER_CUDA_CHECK(cudaGetLastError());
+  // Programmatic dependent launch: the kernel may begin (TMEM, barriers,
+  // weight prefetch) before the previous kernel in the stream has finished.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  static const bool pdl = std::getenv("AETHER_NO_PDL") == nullptr;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  AETHER_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, tw, tx, p));
 }
 
 }  // namespace skinny
@@ -272,31 +341,28 @@ void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int
   c10::cuda::CUDAGuard g(x.device());
   const int n_tiles = (int)((N + skinny::BM - 1) / skinny::BM);
   const int num_kb = (int)((K + skinny::BK - 1) / skinny::BK);
-  if (splits <= 0) {
-    const int target = 2 * num_sms(current_device());
-    splits = std::max<int64_t>(1, std::min<int64_t>(num_kb / 2, (target + n_tiles - 1) / n_tiles));
-  }
-  const int kbps = (num_kb + (int)splits - 1) / (int)splits;
-  const int real_splits = (num_kb + kbps - 1) / kbps;
+  const int64_t units = (int64_t)n_tiles * num_kb;
+  // one wave; at least 4 K blocks per CTA so the fixed per-CTA cost is amortised
+  int64_t grid = splits > 0 ? splits : std::min<int64_t>(num_sms(current_device()), (units + 3) / 4);
+  grid = std::max<int64_t>(1, std::min<int64_t>(grid, units));
   skinny::Params p{};
   p.acc = acc_mc != 0 ? reinterpret_cast<float*>(acc_mc) : acc.data_ptr<float>();
   p.ldacc = acc.stride(0);
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
-  p.k_blocks_per_split = kbps;
+  p.num_kb = num_kb;
+  p.units = units;
   p.status = device_status_word();
   const int BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
   CUtensorMap tw = make_tmap_2d_bf16(w.data_ptr(), K, N, w.stride(0) * 2, skinny::BK, skinny::BM);
   CUtensorMap tx = make_tmap_2d_bf16(x.data_ptr(), K, M, x.stride(0) * 2, skinny::BK, BN);
   auto stream = at::cuda::getCurrentCUDAStream();
   const bool mc = acc_mc != 0;
-  if (BN == 16) mc ? skinny::launch<16, true>(tw, tx, p, n_tiles, real_splits, stream)
-                   : skinny::launch<16, false>(tw, tx, p, n_tiles, real_splits, stream);
-  else if (BN == 32) mc ? skinny::launch<32, true>(tw, tx, p, n_tiles, real_splits, stream)
-                        : skinny::launch<32, false>(tw, tx, p, n_tiles, real_splits, stream);
-  else mc ? skinny::launch<64, true>(tw, tx, p, n_tiles, real_splits, stream)
-          : skinny::launch<64, false>(tw, tx, p, n_tiles, real_splits, stream);
+  const int ng = (int)grid;
+  if (BN == 16) mc ? skinny::launch<16, true>(tw, tx, p, ng, stream) : skinny::launch<16, false>(tw, tx, p, ng, stream);
+  else if (BN == 32) mc ? skinny::launch<32, true>(tw, tx, p, ng, stream) : skinny::launch<32, false>(tw, tx, p, ng, stream);
+  else mc ? skinny::launch<64, true>(tw, tx, p, ng, stream) : skinny::launch<64, false>(tw, tx, p, ng, stream);
 }
 
 // y = bf16(acc (+bias) (+res)), or swiglu over acc's [gate | up] halves when swiglu;
