@@ -4,6 +4,8 @@ dtypes). Outputs are allocated here unless an ``out`` tensor is passed.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .._ext import C
@@ -242,13 +244,33 @@ def argmax(x):
 
 
 # ------------------------------------------------------------------ attention
-def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=True):
-    """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] (strided views ok) -> (o [B,Sq,Hq,D], lse [B,Hq,Sq])."""
+_FA2_ONLY = os.environ.get("AETHER_FA2", "0") == "1"
+
+
+def _tc_ok(q, k, v):
+    """The tcgen05 forward handles head_dim 128 with [B, S, H, D] views whose
+    batch stride is S * row stride (e.g. slices of one packed qkv buffer)."""
+    if _FA2_ONLY or q.shape[-1] != 128:
+        return False
+    for t in (q, k, v):
+        if t.stride(0) != t.shape[1] * t.stride(1) or t.stride(3) != 1 or t.stride(2) != 128:
+            return False
+    return True
+
+
+def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=True, impl="auto"):
+    """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] (strided views ok) -> (o [B,Sq,Hq,D], lse [B,Hq,Sq]).
+
+    impl: "auto" (tcgen05 kernel when it applies, else the mma.sync kernel),
+    "tc" or "fa2"."""
     B, Sq, Hq, D = q.shape
     if _cuda(q):
         o = out if out is not None else torch.empty(B, Sq, Hq, D, dtype=q.dtype, device=q.device)
         lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if want_lse else None
-        C().attention_fwd(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset))
+        if impl == "tc" or (impl == "auto" and _tc_ok(q, k, v)):
+            C().attention_fwd_tc(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset))
+        else:
+            C().attention_fwd(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset))
         return o, lse
     o, lse = ref.attention(q, k, v, scale, causal, causal_offset)
     o = o.to(q.dtype).contiguous()

@@ -1,0 +1,391 @@
+// Flash-attention forward on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// One CTA computes 128 query rows of one head (head_dim 128):
+//   warp 0      : TMA producer -- the Q tile once, then K and V tiles of 128
+//                 keys through a 2-stage ring (128B-swizzled, no multicast)
+//   warp 1      : TMEM allocator + single-thread MMA issuer:
+//                   S_j = Q K_j^T        (SS MMA, M128 N128, into TMEM S[j%2])
+//                   O  += P_{j-1} V_{j-1} (TS MMA: P read from TMEM, V from smem)
+//                 QK_j is issued before PV_{j-1}, so the tensor core computes
+//                 the next scores while the softmax warps work on this tile
+//   warps 2..5  : one thread per query row: tcgen05.ld of its S row, masking,
+//                 online softmax (max / exp2 / sum in registers), P written back
+//                 as bf16 over the S columns (tcgen05.st), and O rescaled in
+//                 TMEM only when the row maximum actually grew
+// TMEM: S double buffer (2 x 128 columns) + O (128 columns).
+//
+// Reference counterpart: sdpa_causal_fwd (runtime/src/cuda.rs:6736-6786), one
+// thread per query row materialising the [bh, s, s] probability matrix.
+// Same semantics as attention.cu's attention_fwd (GQA, causal offset, LSE out).
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace aether {
+namespace fa {
+
+constexpr int BM = 128;   // query rows per CTA
+constexpr int BN = 128;   // keys per tile
+constexpr int D = 128;    // head dim
+constexpr int KV_STAGES = 2;
+constexpr int kThreads = 192;
+constexpr int TILE_BYTES = 128 * D * 2;  // 32 KB: [128 rows][128 d] as two 128B-swizzled halves
+constexpr int kSmem = TILE_BYTES * (1 + 2 * KV_STAGES) + 1024 + 256;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Params {
+  __nv_bfloat16* out;
+  int64_t o_bs, o_rs;
+  float* lse;  // [B, Hq, Sq] or null
+  int B, Hq, Hkv, Sq, Sk;
+  float scale_log2;
+  int causal, causal_offset;
+  int* status;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Loads one [128 rows][128 d] tile as two 64-column boxes (128B swizzle).
+__device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int x0, int y0) {
+  tma_load_2d(dst, map, bar, x0, y0);
+  tma_load_2d(dst + TILE_BYTES / 2, map, bar, x0 + 64, y0);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + TILE_BYTES;
+  uint8_t* sV = sK + KV_STAGES * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KV_STAGES * TILE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;                // [KV_STAGES]
+  uint64_t* v_full = k_full + KV_STAGES;      // [KV_STAGES]
+  uint64_t* kv_empty = v_full + KV_STAGES;    // [KV_STAGES]
+  uint64_t* s_full = kv_empty + KV_STAGES;    // [2]
+  uint64_t* p_full = s_full + 2;              // [2]
+  uint64_t* o_done = p_full + 2;              // PV completions
+  uint64_t* drain = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int q0 = qb * BM;
+  int kv_end = p.Sk;
+  if (p.causal) kv_end = min(p.Sk, q0 + BM + p.causal_offset);
+  const int n_kv = kv_end > 0 ? (kv_end + BN - 1) / BN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;          // S buffers at columns [0,128) and [128,256)
+  const uint32_t tO = tmem + 256;    // O at columns [256, 384)
+
+  if (warp == 0) {
+    if (lane == 0 && n_kv > 0) {
+      // ------------------------------------------------------------ producer
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      load_tile(sQ, &tmQ, q_full, h * D, b * p.Sq + q0);
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1u;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_word)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+        load_tile(sK + st * TILE_BYTES, &tmK, &k_full[st], hk * D, b * p.Sk + j * BN);
+        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+        load_tile(sV + st * TILE_BYTES, &tmV, &v_full[st], hk * D, b * p.Sk + j * BN);
+      }
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_kv > 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(BM, BN, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(BM, D, false, true);
+      bool ok = mbar_wait(q_full, 0, abort_word);
+      tc_fence_after();
+      const uint32_t q_addr = smem_u32(sQ);
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(&k_full[st], (j / KV_STAGES) & 1u, abort_word)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
+          umma_f16(tS + (j & 1) * BN, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
+                   idesc_qk, kk != 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[j & 1]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1u, abort_word)) return false;
+        if (!mbar_wait(&v_full[st], (j / KV_STAGES) & 1u, abort_word)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + st * TILE_BYTES);
+        const uint32_t p_tmem = tS + (j & 1) * BN;  // bf16 P packed in the first 64 columns
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16_ts(tO, p_tmem + kk * 8, sdesc_sw128(v_addr + kk * 2048, TILE_BYTES / 2, 1024), idesc_pv,
+                      (j != 0 || kk != 0) ? 1u : 0u);
+        umma_commit(o_done);
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      for (int j = 1; j < n_kv && ok; ++j) {
+        ok = issue_qk(j);
+        if (ok) ok = issue_pv(j - 1);
+      }
+      if (ok) ok = issue_pv(n_kv - 1);
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutMma);
+      }
+      volatile int never = 0;
+      umma_commit(drain);
+      mbar_wait(drain, 0, &never);
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;  // query row within the tile = TMEM lane
+    const int qpos = q0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    uint32_t o_phase = 0;
+    int pv_waited = 0;  // PV completions observed so far
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1u, abort_word)) {
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + lane_off + (j & 1) * BN + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(r[t]) * p.scale_log2;
+      }
+      const int key0 = j * BN;
+      const bool need_mask = (key0 + BN > p.Sk) || (p.causal && key0 + BN - 1 > q0 + p.causal_offset);
+      if (need_mask) {
+        const int lim = p.causal ? min(p.Sk, qpos + p.causal_offset + 1) : p.Sk;
+#pragma unroll
+        for (int t = 0; t < BN; ++t)
+          if (key0 + t >= lim) s[t] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < BN; ++t) mx = fmaxf(mx, s[t]);
+      const float mn = fmaxf(m, mx);
+      const float base = mn == -INFINITY ? 0.f : mn;
+      const float alpha = exp2f(m - base);
+      float rs = 0.f;
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int t = 0; t < BN; t += 2) {
+        const float a0 = exp2f(s[t] - base), a1 = exp2f(s[t + 1] - base);
+        rs += a0 + a1;
+        pk[t / 2] = pack_bf16(a0, a1);
+      }
+      l = l * alpha + rs;
+      m = mn;
+      // PV_{j-1} must have landed before O may be touched; every PV completion
+      // is awaited in order so the o_done barrier never runs two phases ahead.
+      if (j > 0) {
+        if (!mbar_wait(o_done, o_phase, abort_word)) {
+          ok = false;
+          break;
+        }
+        o_phase ^= 1u;
+        ++pv_waited;
+      }
+      // Rescale O only if some row of this warp saw its maximum grow.
+      const bool need = (j > 0) && (alpha != 1.f);
+      if (__any_sync(0xffffffffu, need)) {
+        __syncwarp();
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + lane_off + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+          tmem_st32(tO + lane_off + c * 32, r);
+        }
+      }
+      // P (bf16) over the first 64 columns of this S buffer
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) r[t] = pk[t];
+        tmem_st32(tS + lane_off + (j & 1) * BN, r);
+#pragma unroll
+        for (int t = 0; t < 32; ++t) r[t] = pk[32 + t];
+        tmem_st32(tS + lane_off + (j & 1) * BN + 32, r);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[j & 1]);
+    }
+    if (ok && n_kv > 0) {
+      while (pv_waited < n_kv) {
+        if (!mbar_wait(o_done, o_phase, abort_word)) {
+          ok = false;
+          break;
+        }
+        o_phase ^= 1u;
+        ++pv_waited;
+      }
+    }
+    if (!ok) {
+      *abort_word = 1;
+      if (lane == 0) atomicExch(p.status, kStatusTimeoutEpilogue);
+    } else {
+      __syncwarp();
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.out + (int64_t)b * p.o_bs + (int64_t)qpos * p.o_rs + (int64_t)h * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (n_kv > 0) {
+          tmem_ld32(tO + lane_off + c * 32, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) r[t] = 0u;
+        }
+        if (qpos < p.Sq) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 o;
+            o.x = pack_bf16(__uint_as_float(r[q * 8 + 0]) * inv, __uint_as_float(r[q * 8 + 1]) * inv);
+            o.y = pack_bf16(__uint_as_float(r[q * 8 + 2]) * inv, __uint_as_float(r[q * 8 + 3]) * inv);
+            o.z = pack_bf16(__uint_as_float(r[q * 8 + 4]) * inv, __uint_as_float(r[q * 8 + 5]) * inv);
+            o.w = pack_bf16(__uint_as_float(r[q * 8 + 6]) * inv, __uint_as_float(r[q * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) = o;
+          }
+        }
+      }
+      if (p.lse != nullptr && qpos < p.Sq)
+        p.lse[((int64_t)b * p.Hq + h) * p.Sq + qpos] = l > 0.f ? (m + __log2f(l)) / kLog2e : INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fa
+
+// Same contract as attention_fwd (head_dim 128 only): q [B,Sq,Hq,128], k/v
+// [B,Sk,Hkv,128] with unit head-dim stride, head stride 128 and any token-row
+// stride that is a multiple of 8 elements; lse optional fp32 [B,Hq,Sq].
+void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
+                      double scale, bool causal, int64_t causal_offset) {
+  const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), D = q.size(3);
+  const int64_t Sk = k.size(1), Hkv = k.size(2);
+  TORCH_CHECK(D == 128 && k.size(3) == 128, "attention_fwd_tc: head_dim 128");
+  for (const at::Tensor* t : {&q, &k, &v, &out}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 4, "attention_fwd_tc: bf16 [B,S,H,D]");
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == 128 && t->stride(1) % 8 == 0, "attention_fwd_tc: layout");
+  }
+  // the 2-D tensor maps flatten (batch, token): each batch's rows must follow the previous batch's
+  TORCH_CHECK(q.stride(0) == Sq * q.stride(1) && k.stride(0) == Sk * k.stride(1) && v.stride(0) == Sk * v.stride(1),
+              "attention_fwd_tc: batch stride must equal S * row stride");
+  TORCH_CHECK(Hq % Hkv == 0, "attention_fwd_tc: GQA group");
+  c10::cuda::CUDAGuard guard(q.device());
+  if (B == 0 || Sq == 0) return;
+  const CUtensorMap tq = make_tmap_2d_bf16(q.data_ptr(), q.stride(1), B * Sq, q.stride(1) * 2, 64, 128);
+  const CUtensorMap tk = make_tmap_2d_bf16(k.data_ptr(), k.stride(1), B * Sk, k.stride(1) * 2, 64, 128);
+  const CUtensorMap tv = make_tmap_2d_bf16(v.data_ptr(), v.stride(1), B * Sk, v.stride(1) * 2, 64, 128);
+  fa::Params p{};
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.o_bs = out.stride(0);
+  p.o_rs = out.stride(1);
+  p.lse = (lse && lse->defined()) ? lse->data_ptr<float>() : nullptr;
+  p.B = (int)B;
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.Sq = (int)Sq;
+  p.Sk = (int)Sk;
+  p.scale_log2 = (float)scale * fa::kLog2e;
+  p.causal = causal ? 1 : 0;
+  p.causal_offset = (int)causal_offset;
+  p.status = device_status_word();
+  static bool attr_set[64] = {false};
+  const int dev = current_device();
+  if (!attr_set[dev]) {
+    AETHER_CUDA_CHECK(cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmem));
+    attr_set[dev] = true;
+  }
+  dim3 grid((unsigned)((Sq + 127) / 128), (unsigned)(B * Hq));
+  fa::fa_fwd_kernel<<<grid, fa::kThreads, fa::kSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  AETHER_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace aether

@@ -46,6 +46,9 @@ void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std
                    double scale, bool causal, int64_t causal_offset);
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
                    at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset);
+// attention_sm100.cu
+void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
+                      double scale, bool causal, int64_t causal_offset);
 // gemm_skinny.cu
 void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc);
 // comm.cu
@@ -98,6 +101,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_norm", &aether::grad_norm);
   m.def("attention_fwd", &aether::attention_fwd);
   m.def("attention_bwd", &aether::attention_bwd);
+  m.def("attention_fwd_tc", &aether::attention_fwd_tc);
   m.def("skinny_gemm", &aether::skinny_gemm, "x"_a, "w"_a, "acc"_a, "splits"_a = 0, "acc_mc"_a = 0);
   m.def("team_barrier", &aether::team_barrier);
   m.def("allreduce_oneshot", &aether::allreduce_oneshot);

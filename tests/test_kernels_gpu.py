@@ -221,6 +221,21 @@ def test_attention_fwd_bwd(B, Sq, Sk, Hq, Hkv, D, causal):
     assert_close(dv, vf.grad, 2e-2, "dv")
 
 
+@pytest.mark.parametrize("impl", ["tc", "fa2"])
+@pytest.mark.parametrize("B,Sq,Sk,Hq,Hkv,causal", [
+    (2, 256, 256, 4, 4, True), (1, 300, 300, 4, 2, True), (2, 128, 384, 6, 2, True), (1, 200, 333, 2, 1, False),
+    (1, 1000, 1000, 2, 2, True),
+])
+def test_attention_fwd_impls(impl, B, Sq, Sk, Hq, Hkv, causal):
+    D = 128
+    q, k, v = bf(B, Sq, Hq, D, seed=5), bf(B, Sk, Hkv, D, seed=6), bf(B, Sk, Hkv, D, seed=7)
+    off = Sk - Sq
+    o, lse = F.attention(q, k, v, D ** -0.5, causal, off, impl=impl)
+    o_r, lse_r = ref.attention(q, k, v, D ** -0.5, causal, off)
+    assert_close(o, o_r, 1e-2, f"attention {impl}")
+    assert_close(lse, lse_r, 1e-4, f"lse {impl}")
+
+
 def test_attention_packed_strided():
     """q/k/v as strided views of one packed qkv buffer (the model's layout)."""
     B, S, H, D = 2, 512, 4, 128
