@@ -280,12 +280,14 @@ def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=T
     return o, lse
 
 
-def attention_bwd(q, k, v, o, do, lse, scale, causal=True, causal_offset=0, dq=None, dk=None, dv=None):
+def attention_bwd(q, k, v, o, do, lse, scale, causal=True, causal_offset=0, dq=None, dk=None, dv=None,
+                  impl="auto"):
     if _cuda(q):
         dq = dq if dq is not None else torch.empty_like(q)
         dk = dk if dk is not None else torch.empty(k.shape, dtype=k.dtype, device=k.device)
         dv = dv if dv is not None else torch.empty(v.shape, dtype=v.dtype, device=v.device)
-        C().attention_bwd(q, k, v, o, do, lse, dq, dk, dv, float(scale), bool(causal), int(causal_offset))
+        use_tc = impl == "tc" or (impl == "auto" and _tc_ok(q, k, v) and _tc_ok(do, dk, dv))
+        C().attention_bwd(q, k, v, o, do, lse, dq, dk, dv, float(scale), bool(causal), int(causal_offset), use_tc)
         return dq, dk, dv
     with torch.enable_grad():
         qf = q.detach().float().requires_grad_(True)

@@ -608,9 +608,16 @@ void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
-// Gradients of attention_fwd. dq/dk/dv are written (not accumulated).
+void attention_bwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor dout, at::Tensor lse, at::Tensor dsum,
+                      at::Tensor dq_acc, at::Tensor dk, at::Tensor dv, double scale, bool causal,
+                      int64_t causal_offset);
+
+// Gradients of attention_fwd. dq/dk/dv are written (not accumulated). With
+// use_tc (head_dim 128) the main pass runs on the tcgen05 kernel of
+// attention_bwd_sm100.cu; the rowsum(dO*O) pre-pass and the dQ conversion are shared.
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
-                   at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset) {
+                   at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset,
+                   bool use_tc) {
   const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), D = q.size(3);
   const int64_t Sk = k.size(1), Hkv = k.size(2);
   attn::check_bshd(q, Hq, D, "attention_bwd q");
@@ -640,6 +647,10 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at:
         dsum.data_ptr<float>(), out.stride(0), out.stride(1), dout.stride(0), dout.stride(1), (int)B, (int)Hq, (int)Sq);
   AETHER_CUDA_CHECK(cudaGetLastError());
 
+  if (use_tc) {
+    TORCH_CHECK(D == 128, "attention_bwd: the tcgen05 path needs head_dim 128");
+    attention_bwd_tc(q, k, v, dout, lse, dsum, dq_acc, dk, dv, scale, causal, causal_offset);
+  } else {
   attn::BwdParams p{};
   p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   p.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
@@ -672,6 +683,7 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at:
     attn::attn_bwd_kernel<64><<<grid, 256, sm, stream>>>(p);
   }
   AETHER_CUDA_CHECK(cudaGetLastError());
+  }
   const int64_t n4 = B * Sq * Hq * D / 4;
   const unsigned cgrid = (unsigned)((n4 + 255) / 256);
   if (D == 128)

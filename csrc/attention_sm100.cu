@@ -1,6 +1,6 @@
 // Flash-attention forward on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA computes 128 query rows of one head (head_dim 128):
+// One CTA computes 256 query rows (two 128-row sub-tiles) of one head (head_dim 128):
 //   warp 0      : TMA producer -- the Q tile once, then K and V tiles of 128
 //                 keys through a 2-stage ring (128B-swizzled, no multicast)
 //   warp 1      : TMEM allocator + single-thread MMA issuer:
@@ -8,11 +8,14 @@
 //                   O  += P_{j-1} V_{j-1} (TS MMA: P read from TMEM, V from smem)
 //                 QK_j is issued before PV_{j-1}, so the tensor core computes
 //                 the next scores while the softmax warps work on this tile
-//   warps 2..5  : one thread per query row: tcgen05.ld of its S row, masking,
+//   warps 2..9  : two softmax warpgroups, one per sub-tile, one thread per query
+//                 row: tcgen05.ld of its S row, masking,
 //                 online softmax (max / exp2 / sum in registers), P written back
 //                 as bf16 over the S columns (tcgen05.st), and O rescaled in
 //                 TMEM only when the row maximum actually grew
-// TMEM: S double buffer (2 x 128 columns) + O (128 columns).
+// TMEM: per sub-tile an S/P region (128 columns) and an O accumulator (128).
+// The MMA issuer interleaves the sub-tiles (PV of one, QK of the other) so the
+// tensor core stays busy while each warpgroup runs its softmax.
 //
 // Reference counterpart: sdpa_causal_fwd (runtime/src/cuda.rs:6736-6786), one
 // thread per query row materialising the [bh, s, s] probability matrix.
@@ -27,13 +30,13 @@
 namespace aether {
 namespace fa {
 
-constexpr int BM = 128;   // query rows per CTA
+constexpr int BM = 256;   // query rows per CTA (two 128-row sub-tiles)
 constexpr int BN = 128;   // keys per tile
 constexpr int D = 128;    // head dim
 constexpr int KV_STAGES = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA, two softmax warpgroups
 constexpr int TILE_BYTES = 128 * D * 2;  // 32 KB: [128 rows][128 d] as two 128B-swizzled halves
-constexpr int kSmem = TILE_BYTES * (1 + 2 * KV_STAGES) + 1024 + 256;
+constexpr int kSmem = TILE_BYTES * (2 + 2 * KV_STAGES) + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Params {
@@ -69,18 +72,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap tmV, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + TILE_BYTES;
+  uint8_t* sQ = smem;                       // [2 sub-tiles]
+  uint8_t* sK = sQ + 2 * TILE_BYTES;        // [KV_STAGES]
   uint8_t* sV = sK + KV_STAGES * TILE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KV_STAGES * TILE_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;                // [KV_STAGES]
   uint64_t* v_full = k_full + KV_STAGES;      // [KV_STAGES]
   uint64_t* kv_empty = v_full + KV_STAGES;    // [KV_STAGES]
-  uint64_t* s_full = kv_empty + KV_STAGES;    // [2]
-  uint64_t* p_full = s_full + 2;              // [2]
-  uint64_t* o_done = p_full + 2;              // PV completions
-  uint64_t* drain = o_done + 1;
+  uint64_t* s_full = kv_empty + KV_STAGES;    // [2 groups]
+  uint64_t* p_full = s_full + 2;              // [2 groups]
+  uint64_t* o_done = p_full + 2;              // [2 groups]
+  uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -90,9 +93,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int hk = h / (p.Hq / p.Hkv);
   const int q0 = qb * BM;
-  int kv_end = p.Sk;
-  if (p.causal) kv_end = min(p.Sk, q0 + BM + p.causal_offset);
-  const int n_kv = kv_end > 0 ? (kv_end + BN - 1) / BN : 0;
+  // KV tiles each 128-row sub-tile needs (causal rows see keys <= row + offset)
+  int nkv[2];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    int kv_end = p.Sk;
+    if (p.causal) kv_end = min(p.Sk, q0 + 128 * (g + 1) + p.causal_offset);
+    nkv[g] = kv_end > 0 ? (kv_end + BN - 1) / BN : 0;
+  }
+  const int n_kv = max(nkv[0], nkv[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -101,11 +110,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], 128);
+      mbar_init(&o_done[g], 1);
     }
-    mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_word = 0;
     fence_mbar_init();
@@ -120,15 +129,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;          // S buffers at columns [0,128) and [128,256)
-  const uint32_t tO = tmem + 256;    // O at columns [256, 384)
+  const uint32_t tmem = *tmem_slot;  // group g: S at 256g, O at 256g + 128
 
   if (warp == 0) {
     if (lane == 0 && n_kv > 0) {
       // ------------------------------------------------------------ producer
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
       load_tile(sQ, &tmQ, q_full, h * D, b * p.Sq + q0);
+      load_tile(sQ + TILE_BYTES, &tmQ, q_full, h * D, b * p.Sq + q0 + 128);
       bool ok = true;
       for (int j = 0; j < n_kv && ok; ++j) {
         const int st = j % KV_STAGES;
@@ -150,46 +158,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && n_kv > 0) {
       // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc_qk = idesc_bf16_f32(BM, BN, false, false);
-      constexpr uint32_t idesc_pv = idesc_bf16_f32(BM, D, false, true);
+      // Order: QK(0,0) QK(1,0) | PV(0,j) QK(0,j+1) PV(1,j) QK(1,j+1) | ...
+      // so the tensor core works on one sub-tile while the other's softmax runs.
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(128, BN, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(128, D, false, true);
       bool ok = mbar_wait(q_full, 0, abort_word);
       tc_fence_after();
-      const uint32_t q_addr = smem_u32(sQ);
-      auto issue_qk = [&](int j) -> bool {
+      auto issue_qk = [&](int g, int j) -> bool {
         const int st = j % KV_STAGES;
         if (!mbar_wait(&k_full[st], (j / KV_STAGES) & 1u, abort_word)) return false;
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + g * TILE_BYTES);
         const uint32_t k_addr = smem_u32(sK + st * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
-          umma_f16(tS + (j & 1) * BN, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
-                   idesc_qk, kk != 0 ? 1u : 0u);
+          umma_f16(tmem + 256 * g, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024), idesc_qk,
+                   kk != 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[g]);
         return true;
       };
-      auto issue_pv = [&](int j) -> bool {
+      auto issue_pv = [&](int g, int j) -> bool {
         const int st = j % KV_STAGES;
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1u, abort_word)) return false;
+        if (!mbar_wait(&p_full[g], j & 1u, abort_word)) return false;
         if (!mbar_wait(&v_full[st], (j / KV_STAGES) & 1u, abort_word)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + st * TILE_BYTES);
-        const uint32_t p_tmem = tS + (j & 1) * BN;  // bf16 P packed in the first 64 columns
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16_ts(tO, p_tmem + kk * 8, sdesc_sw128(v_addr + kk * 2048, TILE_BYTES / 2, 1024), idesc_pv,
-                      (j != 0 || kk != 0) ? 1u : 0u);
-        umma_commit(o_done);
-        umma_commit(&kv_empty[st]);
+          umma_f16_ts(tmem + 256 * g + 128, tmem + 256 * g + kk * 8,
+                      sdesc_sw128(v_addr + kk * 2048, TILE_BYTES / 2, 1024), idesc_pv, (j != 0 || kk != 0) ? 1u : 0u);
+        umma_commit(&o_done[g]);
         return true;
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 1; j < n_kv && ok; ++j) {
-        ok = issue_qk(j);
-        if (ok) ok = issue_pv(j - 1);
+      for (int g = 0; g < 2 && ok; ++g)
+        if (nkv[g] > 0) ok = issue_qk(g, 0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j < nkv[0]) ok = issue_pv(0, j);
+        if (ok && j + 1 < nkv[0]) ok = issue_qk(0, j + 1);
+        if (ok && j < nkv[1]) ok = issue_pv(1, j);
+        if (ok && j + 1 < nkv[1]) ok = issue_qk(1, j + 1);
+        if (ok) umma_commit(&kv_empty[j % KV_STAGES]);  // K_j and V_j consumed by every MMA issued so far
       }
-      if (ok) ok = issue_pv(n_kv - 1);
       if (!ok) {
         *abort_word = 1;
         atomicExch(p.status, kStatusTimeoutMma);
@@ -199,17 +210,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0, &never);
     }
   } else {
-    // -------------------------------------------------------------- softmax
+    // -------------------------------------------------------------- softmax groups
+    const int grp = (warp - 2) >> 2;
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;  // query row within the tile = TMEM lane
-    const int qpos = q0 + row;
+    const int row = quad * 32 + lane;  // row within the sub-tile = TMEM lane
+    const int qpos = q0 + 128 * grp + row;
+    const int qsub0 = q0 + 128 * grp;  // first row of this sub-tile
+    const int my_kv = nkv[grp];
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + 256 * grp, tO = tS + 128;
     float m = -INFINITY, l = 0.f;
     uint32_t o_phase = 0;
-    int pv_waited = 0;  // PV completions observed so far
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1u, abort_word)) {
+    for (int j = 0; j < my_kv; ++j) {
+      if (!mbar_wait(&s_full[grp], j & 1u, abort_word)) {
         ok = false;
         break;
       }
@@ -219,13 +233,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tS + lane_off + (j & 1) * BN + c * 32, r);
+        tmem_ld32(tS + lane_off + c * 32, r);
         tmem_ld_wait();
 #pragma unroll
         for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(r[t]) * p.scale_log2;
       }
       const int key0 = j * BN;
-      const bool need_mask = (key0 + BN > p.Sk) || (p.causal && key0 + BN - 1 > q0 + p.causal_offset);
+      const bool need_mask = (key0 + BN > p.Sk) || (p.causal && key0 + BN - 1 > qsub0 + p.causal_offset);
       if (need_mask) {
         const int lim = p.causal ? min(p.Sk, qpos + p.causal_offset + 1) : p.Sk;
 #pragma unroll
@@ -251,12 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // PV_{j-1} must have landed before O may be touched; every PV completion
       // is awaited in order so the o_done barrier never runs two phases ahead.
       if (j > 0) {
-        if (!mbar_wait(o_done, o_phase, abort_word)) {
+        if (!mbar_wait(&o_done[grp], o_phase, abort_word)) {
           ok = false;
           break;
         }
         o_phase ^= 1u;
-        ++pv_waited;
       }
       // Rescale O only if some row of this warp saw its maximum grow.
       const bool need = (j > 0) && (alpha != 1.f);
@@ -273,29 +286,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(tO + lane_off + c * 32, r);
         }
       }
-      // P (bf16) over the first 64 columns of this S buffer
       {
         uint32_t r[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) r[t] = pk[t];
-        tmem_st32(tS + lane_off + (j & 1) * BN, r);
+        tmem_st32(tS + lane_off, r);
 #pragma unroll
         for (int t = 0; t < 32; ++t) r[t] = pk[32 + t];
-        tmem_st32(tS + lane_off + (j & 1) * BN + 32, r);
+        tmem_st32(tS + lane_off + 32, r);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
+      mbar_arrive(&p_full[grp]);
     }
-    if (ok && n_kv > 0) {
-      while (pv_waited < n_kv) {
-        if (!mbar_wait(o_done, o_phase, abort_word)) {
-          ok = false;
-          break;
-        }
-        o_phase ^= 1u;
-        ++pv_waited;
-      }
+    if (ok && my_kv > 0) {
+      if (!mbar_wait(&o_done[grp], o_phase, abort_word)) ok = false;
     }
     if (!ok) {
       *abort_word = 1;
@@ -308,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
-        if (n_kv > 0) {
+        if (my_kv > 0) {
           tmem_ld32(tO + lane_off + c * 32, r);
           tmem_ld_wait();
         } else {
@@ -383,7 +388,7 @@ void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, 
     AETHER_CUDA_CHECK(cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmem));
     attr_set[dev] = true;
   }
-  dim3 grid((unsigned)((Sq + 127) / 128), (unsigned)(B * Hq));
+  dim3 grid((unsigned)((Sq + fa::BM - 1) / fa::BM), (unsigned)(B * Hq));
   fa::fa_fwd_kernel<<<grid, fa::kThreads, fa::kSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
   AETHER_CUDA_CHECK(cudaGetLastError());
 }

@@ -45,7 +45,8 @@ void grad_norm(at::Tensor g, at::Tensor norm_out, std::optional<at::Tensor> clip
 void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
                    double scale, bool causal, int64_t causal_offset);
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
-                   at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset);
+                   at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset,
+                   bool use_tc);
 // attention_sm100.cu
 void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
                       double scale, bool causal, int64_t causal_offset);
@@ -100,7 +101,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sgd_step", &aether::sgd_step);
   m.def("grad_norm", &aether::grad_norm);
   m.def("attention_fwd", &aether::attention_fwd);
-  m.def("attention_bwd", &aether::attention_bwd);
+  m.def("attention_bwd", &aether::attention_bwd, "q"_a, "k"_a, "v"_a, "out"_a, "dout"_a, "lse"_a, "dq"_a, "dk"_a,
+        "dv"_a, "scale"_a, "causal"_a, "causal_offset"_a, "use_tc"_a = false);
   m.def("attention_fwd_tc", &aether::attention_fwd_tc);
   m.def("skinny_gemm", &aether::skinny_gemm, "x"_a, "w"_a, "acc"_a, "splits"_a = 0, "acc_mc"_a = 0);
   m.def("team_barrier", &aether::team_barrier);

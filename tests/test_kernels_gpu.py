@@ -236,6 +236,26 @@ def test_attention_fwd_impls(impl, B, Sq, Sk, Hq, Hkv, causal):
     assert_close(lse, lse_r, 1e-4, f"lse {impl}")
 
 
+@pytest.mark.parametrize("impl", ["tc", "fa2"])
+@pytest.mark.parametrize("B,Sq,Sk,Hq,Hkv,causal", [
+    (2, 256, 256, 4, 4, True), (1, 300, 300, 4, 2, True), (2, 128, 384, 6, 2, True), (1, 200, 333, 2, 1, False),
+    (1, 700, 700, 2, 2, True),
+])
+def test_attention_bwd_impls(impl, B, Sq, Sk, Hq, Hkv, causal):
+    D = 128
+    q, k, v = bf(B, Sq, Hq, D, seed=8), bf(B, Sk, Hkv, D, seed=9), bf(B, Sk, Hkv, D, seed=10)
+    off = Sk - Sq
+    o, lse = F.attention(q, k, v, D ** -0.5, causal, off)
+    do = bf(B, Sq, Hq, D, seed=11)
+    dq, dk, dv = F.attention_bwd(q, k, v, o, do, lse, D ** -0.5, causal, off, impl=impl)
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    of, _ = ref.attention(qf, kf, vf, D ** -0.5, causal, off)
+    of.backward(do.float())
+    assert_close(dq, qf.grad, 2e-2, f"dq {impl}")
+    assert_close(dk, kf.grad, 2e-2, f"dk {impl}")
+    assert_close(dv, vf.grad, 2e-2, f"dv {impl}")
+
+
 def test_attention_packed_strided():
     """q/k/v as strided views of one packed qkv buffer (the model's layout)."""
     B, S, H, D = 2, 512, 4, 128
