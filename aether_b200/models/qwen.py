@@ -205,13 +205,17 @@ class QwenModel:
             "part_lse": torch.empty(B * self.hq * self.decode_splits, dtype=torch.float32, device=dev),
             "next": torch.zeros(B, dtype=torch.long, device=dev),
             "counters": torch.zeros(B * self.hkv, dtype=torch.int32, device=dev),
+            "logits": torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev),
         }
+        self._want_logits = False
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, tokens: torch.Tensor, slots: torch.Tensor | None = None, start_pos: int = 0) -> torch.Tensor:
+    def prefill(self, tokens: torch.Tensor, slots: torch.Tensor | None = None, start_pos: int = 0,
+                return_logits: bool = False):
         """tokens [B, S] (one prompt per cache slot, equal lengths) -> greedy next
-        token [B]. Writes K/V for positions [start_pos, start_pos + S)."""
+        token [B] (and the fp32 last-position logits with return_logits).
+        Writes K/V for positions [start_pos, start_pos + S)."""
         cfg, w = self.cfg, self.w
         B, S = tokens.shape
         D = cfg.head_dim
@@ -257,7 +261,8 @@ class QwenModel:
         last = x.view(B, S, cfg.d_model)[:, -1].contiguous()
         hl, _, _ = F.rmsnorm(last, w.final_norm, cfg.norm_eps)
         logits = F.gemm(hl, w.lm_head, out_dtype=torch.float32)
-        return F.argmax(logits)
+        nxt = F.argmax(logits)
+        return (nxt, logits) if return_logits else nxt
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int) -> None:
@@ -300,6 +305,8 @@ class QwenModel:
             nw = w.attn_norm[i + 1] if i + 1 < L else w.final_norm
             F.finalize_residual_norm(racc, x, nw, h, res=x2, eps=cfg.norm_eps)
         F.skinny_gemm(h, w.lm_head, acc)
+        if self._want_logits:
+            b["logits"][:B].copy_(acc[:, : cfg.vocab])
         b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
         acc.zero_()
 
@@ -338,6 +345,8 @@ class QwenModel:
                 F.skinny_finalize(racc, x, res=x2)
         F.rmsnorm_into(x, w.final_norm, h, cfg.norm_eps)
         F.skinny_gemm(h, w.lm_head, acc)
+        if self._want_logits:
+            b["logits"][:B].copy_(acc[:, : cfg.vocab])
         b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
         acc.zero_()
 
@@ -348,10 +357,13 @@ class QwenModel:
         return self.max_batch
 
     @torch.no_grad()
-    def capture(self, B: int) -> None:
-        """Captures the decode step for batch bucket B as a CUDA graph."""
-        if self.device.type != "cuda" or B in self._graphs:
+    def capture(self, B: int, want_logits: bool = False) -> None:
+        """Captures the decode step for batch bucket B as a CUDA graph (the
+        variant with want_logits also copies the fp32 logits out)."""
+        key = (B, want_logits)
+        if self.device.type != "cuda" or key in self._graphs:
             return
+        self._want_logits = want_logits
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
@@ -361,13 +373,15 @@ class QwenModel:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             self._step_body(B)
-        self._graphs[B] = g
+        self._graphs[key] = g
+        self._want_logits = False
 
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor | None = None,
-                    use_graph: bool = True) -> torch.Tensor:
+                    use_graph: bool = True, want_logits: bool = False) -> torch.Tensor:
         """tokens [B] at positions pos [B] (0-based) -> greedy next tokens [B]
-        (device tensor, valid until the next call)."""
+        (device tensor, valid until the next call). With want_logits the fp32
+        logits of the step are left in ``self.buf["logits"][:B]``."""
         B = tokens.shape[0]
         Bb = self._bucket(B)
         b = self.buf
@@ -382,11 +396,13 @@ class QwenModel:
             b["seqlen"][B:Bb].fill_(1)
             b["slot"][B:Bb].fill_(self.scratch_slot)
         if use_graph and self.device.type == "cuda":
-            if Bb not in self._graphs:
-                self.capture(Bb)
-            self._graphs[Bb].replay()
+            if (Bb, want_logits) not in self._graphs:
+                self.capture(Bb, want_logits)
+            self._graphs[(Bb, want_logits)].replay()
         else:
+            self._want_logits = want_logits
             self._step_body(Bb)
+            self._want_logits = False
         return b["next"][:B]
 
     @torch.no_grad()

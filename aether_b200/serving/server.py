@@ -1,0 +1,178 @@
+"""OpenAI-compatible HTTP server.
+
+Reference: aether-serve (trainer/src/bin/serve.rs): routes GET /v1/models,
+POST /v1/chat/completions, POST /v1/completions, POST /v1/embeddings, SSE
+streaming, Prometheus metrics; its own HTTP/1.1 + h2 + TLS 1.3 stack. Here the
+HTTP layer is FastAPI/uvicorn (HTTP/1.1; TLS via uvicorn's ssl options) in
+front of the continuous-batching ``Engine``.
+
+    python -m aether_b200.serving.server --model 1.5b --max-concurrent 8 --port 8000
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import time
+import uuid
+
+from fastapi import FastAPI, HTTPException, Request as HTTPRequest
+from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+from .sampling import SamplingParams
+from .tokenizer import chat_template
+
+
+def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: str = "chatml") -> FastAPI:
+    app = FastAPI(title="aether_b200")
+
+    @app.get("/health")
+    def health():
+        return {"status": "ok", "active": len(engine.active), "queue": engine.pending.qsize()}
+
+    @app.get("/v1/models")
+    def models():
+        data = [{"id": model_name, "object": "model", "owned_by": "aether_b200", "created": 0}]
+        if embedder is not None:
+            data.append({"id": embedder.name, "object": "model", "owned_by": "aether_b200", "created": 0})
+        return {"object": "list", "data": data}
+
+    @app.get("/metrics")
+    def metrics():
+        return PlainTextResponse(engine.metrics.prometheus())
+
+    def _usage(r):
+        return {"prompt_tokens": len(r.prompt_ids), "completion_tokens": len(r.tokens),
+                "total_tokens": len(r.prompt_ids) + len(r.tokens)}
+
+    async def _collect(r):
+        loop = asyncio.get_running_loop()
+        toks = []
+        while True:
+            t = await loop.run_in_executor(None, r.out.get)
+            if t is None:
+                return toks
+            toks.append(t)
+
+    def _trim(text: str, stops) -> str:
+        for s in stops or []:
+            i = text.find(s)
+            if i >= 0:
+                text = text[:i]
+        return text
+
+    async def _sse(r, make_chunk, stops):
+        loop = asyncio.get_running_loop()
+        sent = ""
+        toks = []
+        while True:
+            t = await loop.run_in_executor(None, r.out.get)
+            if t is None:
+                break
+            toks.append(t)
+            text = _trim(engine.tok.decode(toks), stops)
+            delta, sent = text[len(sent):], text
+            if delta:
+                yield f"data: {json.dumps(make_chunk(delta, None))}\n\n"
+        yield f"data: {json.dumps(make_chunk('', r.finish_reason or 'stop'))}\n\n"
+        yield "data: [DONE]\n\n"
+
+    @app.post("/v1/completions")
+    async def completions(req: HTTPRequest):
+        body = await req.json()
+        prompt = body.get("prompt", "")
+        if isinstance(prompt, list):
+            prompt = prompt[0] if prompt and isinstance(prompt[0], str) else prompt
+        ids = engine.tok.encode(prompt) if isinstance(prompt, str) else list(prompt)
+        params = SamplingParams.from_openai(body)
+        try:
+            r = engine.submit(ids, params)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        cid = f"cmpl-{uuid.uuid4().hex[:24]}"
+        created = int(time.time())
+        if body.get("stream"):
+            def chunk(delta, fin):
+                return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
+                        "choices": [{"index": 0, "text": delta, "finish_reason": fin}]}
+            return StreamingResponse(_sse(r, chunk, params.stop), media_type="text/event-stream")
+        toks = await _collect(r)
+        text = _trim(engine.tok.decode(toks), params.stop)
+        return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
+                "choices": [{"index": 0, "text": text, "finish_reason": r.finish_reason or "stop"}],
+                "usage": _usage(r)}
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: HTTPRequest):
+        body = await req.json()
+        messages = body.get("messages") or []
+        if not messages:
+            raise HTTPException(400, "messages required")
+        prompt = chat_template(messages, template)
+        ids = engine.tok.encode(prompt)
+        params = SamplingParams.from_openai(body)
+        try:
+            r = engine.submit(ids, params)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        cid = f"chatcmpl-{uuid.uuid4().hex[:24]}"
+        created = int(time.time())
+        if body.get("stream"):
+            def chunk(delta, fin):
+                d = {"content": delta} if delta else {}
+                return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
+                        "choices": [{"index": 0, "delta": d, "finish_reason": fin}]}
+            return StreamingResponse(_sse(r, chunk, params.stop), media_type="text/event-stream")
+        toks = await _collect(r)
+        text = _trim(engine.tok.decode(toks), params.stop)
+        return {"id": cid, "object": "chat.completion", "created": created, "model": model_name,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                             "finish_reason": r.finish_reason or "stop"}],
+                "usage": _usage(r)}
+
+    @app.post("/v1/embeddings")
+    async def embeddings(req: HTTPRequest):
+        if embedder is None:
+            return JSONResponse({"error": {"message": "no embedding model loaded"}}, status_code=501)
+        body = await req.json()
+        inputs = body.get("input", [])
+        if isinstance(inputs, str):
+            inputs = [inputs]
+        vecs = embedder.embed_texts(inputs)
+        return {"object": "list", "model": embedder.name,
+                "data": [{"object": "embedding", "index": i, "embedding": v} for i, v in enumerate(vecs)],
+                "usage": {"prompt_tokens": 0, "total_tokens": 0}}
+
+    return app
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="1.5b", choices=["1.5b", "7b", "tiny"])
+    ap.add_argument("--tokenizer", default=None, help="tokenizer.json (default: byte tokenizer)")
+    ap.add_argument("--max-concurrent", type=int, default=8)
+    ap.add_argument("--max-seq", type=int, default=4096)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--device", default="cuda")
+    args = ap.parse_args()
+    import uvicorn
+
+    from ..models.qwen import QwenConfig, QwenModel
+    from .engine import Engine
+    from .tokenizer import BPETokenizer, ByteTokenizer
+
+    if args.model == "7b":
+        cfg = QwenConfig.qwen25_7b()
+    elif args.model == "tiny":
+        cfg = QwenConfig(vocab=1024, d_model=256, n_layers=2, n_heads=2, n_kv_heads=1, d_ff=512, max_seq=args.max_seq)
+    else:
+        cfg = QwenConfig.qwen25_1_5b()
+    tok = BPETokenizer.from_file(args.tokenizer) if args.tokenizer else ByteTokenizer()
+    model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq)
+    engine = Engine(model, tok, max_concurrent=args.max_concurrent, use_graph=args.device != "cpu")
+    uvicorn.run(build_app(engine, f"qwen2.5-{args.model}"), host=args.host, port=args.port, log_level="warning")
+
+
+if __name__ == "__main__":
+    main()

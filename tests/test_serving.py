@@ -1,0 +1,152 @@
+"""Serving stack on CPU with a tiny random Qwen: tokenizers, the continuous
+batching engine (results equal per-request greedy generation), sampling
+parameters, and the OpenAI-compatible HTTP routes on a live server."""
+import json
+import socket
+import threading
+import time
+import urllib.request
+
+import pytest
+import torch
+
+from aether_b200.models.qwen import QwenConfig, QwenModel
+from aether_b200.serving.engine import Engine
+from aether_b200.serving.sampling import SamplingParams
+from aether_b200.serving.tokenizer import BPETokenizer, ByteTokenizer, bytes_to_unicode, chat_template
+
+TINY = dict(vocab=300, d_model=128, n_layers=2, n_heads=2, n_kv_heads=1, d_ff=256, max_seq=128, init_std=0.08)
+
+
+def _model(seed=0, max_batch=4):
+    return QwenModel(QwenConfig(**TINY), device="cpu", seed=seed, max_batch=max_batch, max_seq=128)
+
+
+def test_byte_tokenizer_roundtrip():
+    t = ByteTokenizer()
+    s = "héllo <|im_start|>user\nhi<|im_end|>"
+    ids = t.encode(s)
+    assert t.special["<|im_start|>"] in ids
+    assert t.decode(ids) == s
+
+
+def test_bpe_tokenizer_merges():
+    be = bytes_to_unicode()
+    sp = be[ord(" ")]
+    vocab = {c: i for i, c in enumerate(sorted(set(be.values())))}
+    n = len(vocab)
+    vocab.update({"h" + "e": n, "he" + "l": n + 1, "hel" + "l": n + 2, "hell" + "o": n + 3, sp + "w": n + 4})
+    merges = ["h e", "he l", "hel l", "hell o", sp + " w"]
+    tok = BPETokenizer(vocab, merges, {"<|endoftext|>": n + 10})
+    ids = tok.encode("hello world<|endoftext|>")
+    assert ids[0] == n + 3 and ids[1] == n + 4 and ids[-1] == n + 10
+    assert tok.decode(ids) == "hello world<|endoftext|>"
+
+
+def test_chat_template():
+    p = chat_template([{"role": "user", "content": "hi"}])
+    assert p == "<|im_start|>user\nhi<|im_end|>\n<|im_start|>assistant\n"
+
+
+def test_engine_matches_individual_generation():
+    m = _model(seed=3, max_batch=4)
+    ref = _model(seed=3, max_batch=4)
+    eng = Engine(m, ByteTokenizer(), max_concurrent=3, eos_ids=[], use_graph=False)
+    prompts = [list(range(5, 5 + n)) for n in (7, 11, 4, 9)]
+    reqs = [eng.submit(p, SamplingParams(max_tokens=6)) for p in prompts]
+    outs = []
+    for r in reqs:
+        toks = list(eng.stream(r, timeout=120))
+        outs.append(toks)
+    eng.shutdown()
+    for p, got in zip(prompts, outs):
+        want = ref.generate(torch.tensor([p]), 6, use_graph=False)[0].tolist()
+        assert got == want, (p, got, want)
+    assert eng.metrics.counters["requests_finished"] == 4
+
+
+def test_sampling_params():
+    m = _model(seed=4)
+    eng = Engine(m, ByteTokenizer(), max_concurrent=2, eos_ids=[], use_graph=False)
+    prompt = list(range(20, 30))
+    a = eng.generate(prompt, SamplingParams(temperature=0.8, top_k=20, seed=123, max_tokens=5))[1]
+    b = eng.generate(prompt, SamplingParams(temperature=0.8, top_k=20, seed=123, max_tokens=5))[1]
+    assert a == b
+    g = eng.generate(prompt, SamplingParams(max_tokens=5))[1]
+    k1 = eng.generate(prompt, SamplingParams(temperature=1.0, top_k=1, seed=1, max_tokens=5))[1]
+    assert g == k1
+    forced = eng.generate(prompt, SamplingParams(temperature=0.7, logit_bias={42: 100.0}, seed=1, max_tokens=3))[1]
+    assert forced == [42, 42, 42]
+    eng.shutdown()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _post(url, body):
+    req = urllib.request.Request(url, data=json.dumps(body).encode(), headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=60) as r:
+        return r.read().decode()
+
+
+def test_http_server_routes():
+    import uvicorn
+
+    from aether_b200.serving.server import build_app
+
+    m = _model(seed=5)
+    eng = Engine(m, ByteTokenizer(), max_concurrent=2, use_graph=False)
+    port = _free_port()
+    server = uvicorn.Server(uvicorn.Config(build_app(eng, "tiny"), host="127.0.0.1", port=port, log_level="error"))
+    th = threading.Thread(target=server.run, daemon=True)
+    th.start()
+    base = f"http://127.0.0.1:{port}"
+    for _ in range(200):
+        try:
+            urllib.request.urlopen(base + "/health", timeout=1)
+            break
+        except Exception:  # noqa: BLE001
+            time.sleep(0.05)
+    try:
+        models = json.loads(urllib.request.urlopen(base + "/v1/models", timeout=10).read())
+        assert models["data"][0]["id"] == "tiny"
+        out = json.loads(_post(base + "/v1/completions", {"prompt": "abc", "max_tokens": 4}))
+        assert out["object"] == "text_completion" and out["usage"]["completion_tokens"] >= 1
+        chat = json.loads(_post(base + "/v1/chat/completions",
+                                {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3}))
+        assert chat["choices"][0]["message"]["role"] == "assistant"
+        sse = _post(base + "/v1/chat/completions",
+                    {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3, "stream": True})
+        assert sse.strip().endswith("data: [DONE]")
+        metrics = urllib.request.urlopen(base + "/metrics", timeout=10).read().decode()
+        assert "aether_requests_total" in metrics
+        emb = urllib.request.Request(base + "/v1/embeddings", data=b'{"input": "x"}',
+                                     headers={"Content-Type": "application/json"})
+        with pytest.raises(urllib.error.HTTPError):
+            urllib.request.urlopen(emb, timeout=10)
+    finally:
+        server.should_exit = True
+        th.join(timeout=10)
+        eng.shutdown()
+
+
+@pytest.mark.gpu
+def test_gpu_engine_batched_graph_decode():
+    cfg = QwenConfig(**dict(TINY, d_model=256, n_heads=2, n_kv_heads=1, d_ff=512))
+    m = QwenModel(cfg, device="cuda", seed=6, max_batch=4, max_seq=128)
+    ref = QwenModel(cfg, device="cuda", seed=6, max_batch=4, max_seq=128)
+    eng = Engine(m, ByteTokenizer(), max_concurrent=4, eos_ids=[], use_graph=True)
+    prompts = [list(range(3, 3 + n)) for n in (5, 13, 8)]
+    reqs = [eng.submit(p, SamplingParams(max_tokens=8)) for p in prompts]
+    outs = [list(eng.stream(r, timeout=120)) for r in reqs]
+    eng.shutdown()
+    agree = 0
+    for p, got in zip(prompts, outs):
+        want = ref.generate(torch.tensor([p], device="cuda"), 8, use_graph=False)[0].tolist()
+        agree += sum(int(a == b) for a, b in zip(got, want))
+    assert agree >= 0.9 * 24, (outs,)
