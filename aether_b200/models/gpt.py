@@ -67,11 +67,14 @@ class GPTConfig:
         return 6.0 * mm + 3.0 * attn
 
 
-def gpt_param_specs(cfg: GPTConfig):
+def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool = True):
+    """Parameter specs (name, shape, weight_decay). ``layers`` / ``first`` /
+    ``last`` select one pipeline stage's share of the model."""
     d, f, v = cfg.d_model, cfg.d_ff, cfg.vocab
     qkv = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
-    specs = [("tok_emb", (v, d), True)]
-    for i in range(cfg.n_layers):
+    layers = range(cfg.n_layers) if layers is None else layers
+    specs = [("tok_emb", (v, d), True)] if (first or (last and cfg.tie_embeddings)) else []
+    for i in layers:
         specs += [
             (f"l{i}.attn_norm", (d,), False),
             (f"l{i}.wqkv", (qkv, d), True),
@@ -80,24 +83,36 @@ def gpt_param_specs(cfg: GPTConfig):
             (f"l{i}.wgu", (2 * f, d), True),
             (f"l{i}.wd", (d, f), True),
         ]
-    specs.append(("final_norm", (d,), False))
-    if not cfg.tie_embeddings:
-        specs.append(("lm_head", (v, d), True))
+    if last:
+        specs.append(("final_norm", (d,), False))
+        if not cfg.tie_embeddings:
+            specs.append(("lm_head", (v, d), True))
     return specs
 
 
 class GPT:
-    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1, alloc=None):
+    """The whole model, or one pipeline stage of it (``layers``, ``first``,
+    ``last``): a first stage embeds token ids, a last stage ends in the final
+    norm, LM head and loss, other stages map hidden states to hidden states."""
+
+    def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1, alloc=None,
+                 layers=None, first: bool = True, last: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.arena = ParamArena(gpt_param_specs(cfg), self.device, pad_multiple=pad_multiple, alloc=alloc)
+        self.layers = list(range(cfg.n_layers) if layers is None else layers)
+        self.first, self.last = first, last
+        self.arena = ParamArena(gpt_param_specs(cfg, self.layers, first, last), self.device,
+                                pad_multiple=pad_multiple, alloc=alloc)
         self.init_weights(seed)
         cos, sin = ref.rope_tables(cfg.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
         self._pos_cache: dict[tuple, torch.Tensor] = {}
 
     def init_weights(self, seed: int) -> None:
-        g = torch.Generator(device="cpu").manual_seed(seed)
+        """N(0, init_std) weights, unit norms. Every tensor has its own CPU
+        generator keyed by its index in the full model, so any pipeline split
+        (and any device) produces the same values as the unsplit model."""
+        index = {name: i for i, (name, _, _) in enumerate(gpt_param_specs(self.cfg))}
         a = self.arena
         with torch.no_grad():
             for name, slot in a.slots.items():
@@ -105,7 +120,7 @@ class GPT:
                 if name.endswith("norm"):
                     mv.fill_(1.0)
                 else:
-                    # generate in CPU chunks so the sequence is device-independent
+                    g = torch.Generator(device="cpu").manual_seed(seed * 1000003 + index[name])
                     t = torch.empty(slot.shape, dtype=torch.float32)
                     t.normal_(0.0, self.cfg.init_std, generator=g)
                     mv.copy_(t.to(self.device))
@@ -117,14 +132,19 @@ class GPT:
             self._pos_cache[key] = torch.arange(S, dtype=torch.int32, device=self.device).repeat(B)
         return self._pos_cache[key]
 
-    def forward_hidden(self, ids: torch.Tensor) -> torch.Tensor:
+    def forward_hidden(self, ids: torch.Tensor, x: torch.Tensor | None = None, B: int | None = None,
+                       S: int | None = None) -> torch.Tensor:
+        """First stage: ids [B, S] -> hidden; later stages: x [B*S, d] -> hidden.
+        The last stage applies the final RMSNorm."""
         cfg, a = self.cfg, self.arena
-        B, S = ids.shape
+        if ids is not None:
+            B, S = ids.shape
         Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         scale = 1.0 / math.sqrt(D)
         pos = self.positions(B, S)
-        x = A.embedding(a["tok_emb"], ids.reshape(-1))  # [T, d]
-        for i in range(cfg.n_layers):
+        if self.first:
+            x = A.embedding(a["tok_emb"], ids.reshape(-1))  # [T, d]
+        for i in self.layers:
             h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
             qkv = A.linear(h, a[f"l{i}.wqkv"])
             qkv = A.rope_(qkv, pos, self.rope_cos, self.rope_sin, Hq + Hkv, D)
@@ -134,11 +154,15 @@ class GPT:
             gu = A.linear(h, a[f"l{i}.wgu"])
             act = A.swiglu(gu)
             x = A.linear(act, a[f"l{i}.wd"], residual=x)
-        return A.rmsnorm(x, a["final_norm"], cfg.norm_eps)
+        return A.rmsnorm(x, a["final_norm"], cfg.norm_eps) if self.last else x
 
-    def loss(self, ids: torch.Tensor, targets: torch.Tensor, loss_scale: float | None = None) -> torch.Tensor:
-        """Sum of per-token CE times loss_scale (default 1/num_tokens = mean)."""
-        h = self.forward_hidden(ids)
+    def loss(self, ids: torch.Tensor, targets: torch.Tensor, loss_scale: float | None = None,
+             x: torch.Tensor | None = None) -> torch.Tensor:
+        """Sum of per-token CE times loss_scale (default 1/num_tokens = mean).
+        A last pipeline stage passes its input hidden states as ``x``."""
+        assert self.last, "loss needs the last stage"
+        B, S = targets.shape
+        h = self.forward_hidden(ids, x=x, B=B, S=S)
         w = self.arena["tok_emb"] if self.cfg.tie_embeddings else self.arena["lm_head"]
         if loss_scale is None:
             loss_scale = 1.0 / targets.numel()

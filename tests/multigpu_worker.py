@@ -84,18 +84,57 @@ def check_tp_qwen(info):
     print(f"OK tp_qwen agree={agree:.3f} mc={tp.team.has_multicast}", flush=True)
 
 
+def check_pp(info):
+    """1F1B pipeline over NCCL p2p (one stage per rank) against one GPU."""
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.optim import FlatAdamW
+    from aether_b200.parallel.pp import GPTPipelineStage, run_1f1b
+
+    cfg = GPTConfig(vocab=512, d_model=256, n_layers=2 * info.world, n_heads=2, n_kv_heads=2, d_ff=512, max_seq=128)
+    st = GPTPipelineStage(cfg, info.rank, info.world, info.device, seed=11, lr=1e-3, weight_decay=0.0)
+    g = torch.Generator().manual_seed(5)
+    toks = torch.randint(0, 512, (4, 2, 129), generator=g)
+    batches = [(t[:, :-1].contiguous(), t[:, 1:].contiguous()) for t in toks]
+    losses = []
+    for _ in range(2):
+        st.zero_grad()
+        loss = run_1f1b(st, batches)
+        st.step()
+        if loss is not None:
+            losses.append(float(loss))
+    t = torch.tensor(losses or [0.0, 0.0], device=info.device)
+    dist.broadcast(t, src=info.world - 1)
+    if info.rank == 0:
+        ref = GPT(cfg, device=info.device, seed=11)
+        opt = FlatAdamW(ref.arena, lr=1e-3, weight_decay=0.0)
+        n_tok = sum(tg.numel() for _, tg in batches)
+        for step in range(2):
+            ref.arena.zero_grad()
+            tot = 0.0
+            for ids, tg in batches:
+                l = ref.loss(ids.to(info.device), tg.to(info.device), 1.0 / n_tok)
+                l.backward()
+                tot += float(l)
+            opt.step()
+            assert abs(tot - float(t[step])) < 2e-2 * abs(tot), (step, tot, float(t[step]))
+    dist.barrier()
+    print(f"OK pp losses={[round(float(x), 4) for x in t]}", flush=True)
+
+
 def main():
     info = D.init(timeout_s=120)
     from aether_b200.parallel.symm import SymmTeam
 
     team = SymmTeam(info)
-    which = sys.argv[1:] or ["allreduce", "dp", "tp"]
+    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp"]
     if "allreduce" in which:
         check_allreduce(team, info)
     if "dp" in which:
         check_fused_dp(info)
     if "tp" in which:
         check_tp_qwen(info)
+    if "pp" in which:
+        check_pp(info)
     torch.cuda.synchronize()
     dist.barrier()
     D.shutdown()
