@@ -23,7 +23,8 @@ from .sampling import SamplingParams
 from .tokenizer import chat_template
 
 
-def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: str = "chatml") -> FastAPI:
+def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: str = "chatml",
+              vision=None) -> FastAPI:
     app = FastAPI(title="aether_b200")
 
     @app.get("/health")
@@ -143,6 +144,27 @@ def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: 
                 "data": [{"object": "embedding", "index": i, "embedding": v} for i, v in enumerate(vecs)],
                 "usage": {"prompt_tokens": 0, "total_tokens": 0}}
 
+    @app.post("/v1/vision/embed")
+    async def vision_embed(req: HTTPRequest):
+        """Body: {"image": [3][H][W] floats} or {"image_b64": raw little-endian
+        float32 bytes, "shape": [3, H, W]} -> L2-normalised CLS embedding."""
+        if vision is None:
+            return JSONResponse({"error": {"message": "no vision model loaded"}}, status_code=501)
+        import base64
+
+        import numpy as np
+        import torch
+
+        body = await req.json()
+        if "image_b64" in body:
+            arr = np.frombuffer(base64.b64decode(body["image_b64"]), dtype="<f4").reshape(body["shape"])
+            img = torch.from_numpy(arr.copy())
+        else:
+            img = torch.tensor(body["image"], dtype=torch.float32)
+        if tuple(img.shape) != (3, vision.cfg.img, vision.cfg.img):
+            raise HTTPException(400, f"image must be [3, {vision.cfg.img}, {vision.cfg.img}]")
+        return {"object": "embedding", "model": vision.name, "embedding": vision.embed(img).tolist()}
+
     return app
 
 
@@ -155,6 +177,8 @@ def main():
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--device", default="cuda")
+    ap.add_argument("--embeddings", action="store_true", help="also serve a BGE-large-shape /v1/embeddings model")
+    ap.add_argument("--vision", action="store_true", help="also serve a DINOv3 ViT-L/16-shape /v1/vision/embed")
     args = ap.parse_args()
     import uvicorn
 
@@ -171,7 +195,17 @@ def main():
     tok = BPETokenizer.from_file(args.tokenizer) if args.tokenizer else ByteTokenizer()
     model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq)
     engine = Engine(model, tok, max_concurrent=args.max_concurrent, use_graph=args.device != "cpu")
-    uvicorn.run(build_app(engine, f"qwen2.5-{args.model}"), host=args.host, port=args.port, log_level="warning")
+    embedder = vision = None
+    if args.embeddings:
+        from ..models.encoders import BertConfig, BertEncoder, TextEmbedder
+
+        embedder = TextEmbedder(BertEncoder(BertConfig.bge_large(), device=args.device), tok)
+    if args.vision:
+        from ..models.encoders import VitConfig, VitEncoder
+
+        vision = VitEncoder(VitConfig.vitl16(), device=args.device)
+    app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, vision=vision)
+    uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
 
 
 if __name__ == "__main__":

@@ -99,10 +99,16 @@ def test_http_server_routes():
 
     from aether_b200.serving.server import build_app
 
+    from aether_b200.models.encoders import BertConfig, BertEncoder, TextEmbedder, VitConfig, VitEncoder
+
     m = _model(seed=5)
     eng = Engine(m, ByteTokenizer(), max_concurrent=2, use_graph=False)
+    emb = TextEmbedder(BertEncoder(BertConfig(vocab=500, d_model=64, n_layers=1, n_heads=2, d_ff=128, max_pos=64),
+                                   device="cpu"), ByteTokenizer())
+    vis = VitEncoder(VitConfig(d=64, n_layers=1, n_heads=2, d_ff=128, patch=8, img=16), device="cpu")
     port = _free_port()
-    server = uvicorn.Server(uvicorn.Config(build_app(eng, "tiny"), host="127.0.0.1", port=port, log_level="error"))
+    app = build_app(eng, "tiny", embedder=emb, vision=vis)
+    server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="error"))
     th = threading.Thread(target=server.run, daemon=True)
     th.start()
     base = f"http://127.0.0.1:{port}"
@@ -125,10 +131,10 @@ def test_http_server_routes():
         assert sse.strip().endswith("data: [DONE]")
         metrics = urllib.request.urlopen(base + "/metrics", timeout=10).read().decode()
         assert "aether_requests_total" in metrics
-        emb = urllib.request.Request(base + "/v1/embeddings", data=b'{"input": "x"}',
-                                     headers={"Content-Type": "application/json"})
-        with pytest.raises(urllib.error.HTTPError):
-            urllib.request.urlopen(emb, timeout=10)
+        e = json.loads(_post(base + "/v1/embeddings", {"input": ["hello", "world"]}))
+        assert len(e["data"]) == 2 and len(e["data"][0]["embedding"]) == 64
+        v = json.loads(_post(base + "/v1/vision/embed", {"image": torch.randn(3, 16, 16).tolist()}))
+        assert len(v["embedding"]) == 64
     finally:
         server.should_exit = True
         th.join(timeout=10)
