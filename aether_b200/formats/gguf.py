@@ -1,0 +1,300 @@
+"""GGUF reader, writer (for tests and exports) and load-time dequantisation.
+
+Reference: aether_gguf_* (runtime/src/lib.rs:8647-9030 -- header, metadata
+key/values including arrays, tensor table), the CPU dequantisers
+(lib.rs:217, 9218-9404) and GGUF-metadata-driven model configs
+(runtime/src/serving.rs:459-900). The reference keeps weights quantised on the
+GPU and multiplies with per-format GEMV kernels; this build dequantises at
+load time to bf16 (the tensor-core GEMMs want bf16 operands), so the block
+formats only need a correct unpacking, done here in vectorised numpy.
+
+Block layouts (the published GGUF/ggml formats, reproduced because files must
+decode identically):
+  Q8_0  32 values: f16 d, 32 x int8            x = d * q
+  Q4_0  32 values: f16 d, 16 bytes of nibbles  x = d * (q - 8); low nibbles are
+        elements 0..15, high nibbles 16..31
+  Q4_K  256 values: f16 d, f16 dmin, 12 bytes of 6-bit (scale, min) pairs for 8
+        sub-blocks of 32, 128 bytes of nibbles; x = d*sc*q - dmin*mn
+  Q6_K  256 values: 128 bytes low 4 bits, 64 bytes high 2 bits, 16 x int8
+        scales, f16 d; x = d * scale * (q - 32) over 16 sub-blocks of 16
+"""
+from __future__ import annotations
+
+import struct
+
+import numpy as np
+import torch
+
+GGUF_MAGIC = 0x46554747
+(T_U8, T_I8, T_U16, T_I16, T_U32, T_I32, T_F32, T_BOOL, T_STR, T_ARR, T_U64, T_I64, T_F64) = range(13)
+_SCALAR = {T_U8: "<B", T_I8: "<b", T_U16: "<H", T_I16: "<h", T_U32: "<I", T_I32: "<i", T_F32: "<f", T_BOOL: "<?",
+           T_U64: "<Q", T_I64: "<q", T_F64: "<d"}
+
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 14, 30
+# (block elements, block bytes)
+_BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_0: (32, 18), Q4_K: (256, 144), Q6_K: (256, 210)}
+
+
+class GGUFFile:
+    def __init__(self, path: str):
+        self.path = path
+        with open(path, "rb") as f:
+            self.data = f.read()
+        self.pos = 0
+        magic, self.version = self._u("<I"), self._u("<I")
+        if magic != GGUF_MAGIC:
+            raise ValueError(f"{path}: not a GGUF file")
+        n_tensors, n_kv = self._u("<Q"), self._u("<Q")
+        self.meta = {}
+        for _ in range(n_kv):
+            k = self._str()
+            self.meta[k] = self._val(self._u("<I"))
+        self.tensors = {}
+        for _ in range(n_tensors):
+            name = self._str()
+            nd = self._u("<I")
+            dims = [self._u("<Q") for _ in range(nd)]
+            typ = self._u("<I")
+            off = self._u("<Q")
+            self.tensors[name] = (dims, typ, off)
+        align = int(self.meta.get("general.alignment", 32))
+        self.data_start = (self.pos + align - 1) // align * align
+
+    def _u(self, fmt):
+        v = struct.unpack_from(fmt, self.data, self.pos)[0]
+        self.pos += struct.calcsize(fmt)
+        return v
+
+    def _str(self):
+        n = self._u("<Q")
+        s = self.data[self.pos : self.pos + n].decode("utf-8", errors="replace")
+        self.pos += n
+        return s
+
+    def _val(self, t):
+        if t == T_STR:
+            return self._str()
+        if t == T_ARR:
+            et, n = self._u("<I"), self._u("<Q")
+            return [self._val(et) for _ in range(n)]
+        return self._u(_SCALAR[t])
+
+    def raw(self, name: str) -> tuple:
+        dims, typ, off = self.tensors[name]
+        n = int(np.prod(dims)) if dims else 1
+        be, bb = _BLOCK[typ]
+        nbytes = n // be * bb
+        start = self.data_start + off
+        return np.frombuffer(self.data, dtype=np.uint8, count=nbytes, offset=start), dims, typ
+
+    def tensor(self, name: str, dtype=torch.bfloat16) -> torch.Tensor:
+        """Dequantised tensor in torch (row-major) shape: GGUF dims are listed
+        fastest-first, so dims [K, N] become [N, K]."""
+        buf, dims, typ = self.raw(name)
+        x = dequantize(buf, typ, int(np.prod(dims)))
+        return torch.from_numpy(x.reshape(list(reversed(dims)))).to(dtype)
+
+
+def _f16(b):
+    return b.view(np.float16).astype(np.float32)
+
+
+def dequantize(buf: np.ndarray, typ: int, n: int) -> np.ndarray:
+    if typ == F32:
+        return buf.view(np.float32)[:n].copy()
+    if typ == F16:
+        return buf.view(np.float16)[:n].astype(np.float32)
+    if typ == BF16:
+        u = buf.view(np.uint16)[:n].astype(np.uint32) << 16
+        return u.view(np.float32)
+    if typ == Q8_0:
+        b = buf.reshape(-1, 34)
+        d = _f16(b[:, :2].copy())
+        q = b[:, 2:].view(np.int8).astype(np.float32)
+        return (q * d).reshape(-1)[:n]
+    if typ == Q4_0:
+        b = buf.reshape(-1, 18)
+        d = _f16(b[:, :2].copy())
+        qs = b[:, 2:]
+        q = np.concatenate([qs & 0x0F, qs >> 4], axis=1).astype(np.float32) - 8.0
+        return (q * d).reshape(-1)[:n]
+    if typ == Q4_K:
+        b = buf.reshape(-1, 144)
+        d = _f16(b[:, 0:2].copy())
+        dmin = _f16(b[:, 2:4].copy())
+        sc = b[:, 4:16].astype(np.uint32)
+        qs = b[:, 16:144]
+        scales = np.empty((b.shape[0], 8), np.float32)
+        mins = np.empty((b.shape[0], 8), np.float32)
+        for j in range(8):
+            if j < 4:
+                s, m = sc[:, j] & 63, sc[:, j + 4] & 63
+            else:
+                s = (sc[:, j + 4] & 0x0F) | ((sc[:, j - 4] >> 6) << 4)
+                m = (sc[:, j + 4] >> 4) | ((sc[:, j] >> 6) << 4)
+            scales[:, j], mins[:, j] = s, m
+        out = np.empty((b.shape[0], 256), np.float32)
+        for g in range(4):  # 4 groups of 64: low nibbles -> sub-block 2g, high -> 2g+1
+            q = qs[:, g * 32 : (g + 1) * 32]
+            lo, hi = (q & 0x0F).astype(np.float32), (q >> 4).astype(np.float32)
+            out[:, g * 64 : g * 64 + 32] = d * scales[:, 2 * g : 2 * g + 1] * lo - dmin * mins[:, 2 * g : 2 * g + 1]
+            out[:, g * 64 + 32 : g * 64 + 64] = d * scales[:, 2 * g + 1 : 2 * g + 2] * hi - dmin * mins[:, 2 * g + 1 : 2 * g + 2]
+        return out.reshape(-1)[:n]
+    if typ == Q6_K:
+        b = buf.reshape(-1, 210)
+        ql, qh = b[:, 0:128], b[:, 128:192]
+        scales = b[:, 192:208].view(np.int8).astype(np.float32)
+        d = _f16(b[:, 208:210].copy())
+        out = np.empty((b.shape[0], 256), np.float32)
+        for half in range(2):  # two 128-value halves
+            l = ql[:, half * 64 : half * 64 + 64]
+            h = qh[:, half * 32 : half * 32 + 32]
+            for part in range(4):
+                if part == 0:
+                    q = (l[:, 0:32] & 0xF) | (((h >> 0) & 3) << 4)
+                elif part == 1:
+                    q = (l[:, 32:64] & 0xF) | (((h >> 2) & 3) << 4)
+                elif part == 2:
+                    q = (l[:, 0:32] >> 4) | (((h >> 4) & 3) << 4)
+                else:
+                    q = (l[:, 32:64] >> 4) | (((h >> 6) & 3) << 4)
+                q = q.astype(np.float32) - 32.0
+                base = half * 128 + part * 32
+                for sub in range(2):  # each 32-run spans two 16-value sub-blocks
+                    si = half * 8 + part * 2 + sub
+                    out[:, base + sub * 16 : base + sub * 16 + 16] = d * scales[:, si : si + 1] * q[:, sub * 16 : sub * 16 + 16]
+        return out.reshape(-1)[:n]
+    raise NotImplementedError(f"GGUF tensor type {typ} is not supported by the load-time dequantiser")
+
+
+# ---------------------------------------------------------------------------- writer
+def _quant_q8_0(x: np.ndarray) -> bytes:
+    b = x.reshape(-1, 32).astype(np.float32)
+    d = np.abs(b).max(axis=1) / 127.0
+    d16 = d.astype(np.float16)
+    inv = np.where(d16.astype(np.float32) > 0, 1.0 / d16.astype(np.float32), 0.0)
+    q = np.clip(np.rint(b * inv[:, None]), -127, 127).astype(np.int8)
+    out = np.empty((b.shape[0], 34), np.uint8)
+    out[:, :2] = d16.view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q.view(np.uint8)
+    return out.tobytes()
+
+
+def _quant_q4_0(x: np.ndarray) -> bytes:
+    b = x.reshape(-1, 32).astype(np.float32)
+    idx = np.abs(b).argmax(axis=1)
+    mx = b[np.arange(b.shape[0]), idx]
+    d = mx / -8.0
+    d16 = d.astype(np.float16)
+    inv = np.where(d16.astype(np.float32) != 0, 1.0 / d16.astype(np.float32), 0.0)
+    q = np.clip(np.rint(b * inv[:, None]) + 8, 0, 15).astype(np.uint8)
+    out = np.empty((b.shape[0], 18), np.uint8)
+    out[:, :2] = d16.view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q[:, :16] | (q[:, 16:] << 4)
+    return out.tobytes()
+
+
+def write_gguf(path: str, metadata: dict, tensors: dict, alignment: int = 32) -> None:
+    """tensors: name -> (torch tensor [.., K], ggml type in {F32, F16, Q8_0, Q4_0})."""
+    def s(x: str) -> bytes:
+        e = x.encode()
+        return struct.pack("<Q", len(e)) + e
+
+    def val(v) -> bytes:
+        if isinstance(v, bool):
+            return struct.pack("<I", T_BOOL) + struct.pack("<?", v)
+        if isinstance(v, int):
+            return struct.pack("<I", T_U32) + struct.pack("<I", v) if 0 <= v < 2**32 else struct.pack("<I", T_I64) + struct.pack("<q", v)
+        if isinstance(v, float):
+            return struct.pack("<I", T_F32) + struct.pack("<f", v)
+        if isinstance(v, str):
+            return struct.pack("<I", T_STR) + s(v)
+        if isinstance(v, list):
+            if all(isinstance(i, str) for i in v):
+                return struct.pack("<I", T_ARR) + struct.pack("<IQ", T_STR, len(v)) + b"".join(s(i) for i in v)
+            return struct.pack("<I", T_ARR) + struct.pack("<IQ", T_I32, len(v)) + b"".join(struct.pack("<i", i) for i in v)
+        raise TypeError(type(v))
+
+    meta = dict(metadata)
+    meta["general.alignment"] = alignment
+    head = struct.pack("<IIQQ", GGUF_MAGIC, 3, len(tensors), len(meta))
+    head += b"".join(s(k) + val(v) for k, v in meta.items())
+    blobs, infos, off = [], b"", 0
+    for name, (t, typ) in tensors.items():
+        x = t.detach().float().cpu().numpy().reshape(-1)
+        if typ == F32:
+            raw = x.astype(np.float32).tobytes()
+        elif typ == F16:
+            raw = x.astype(np.float16).tobytes()
+        elif typ == Q8_0:
+            raw = _quant_q8_0(x)
+        elif typ == Q4_0:
+            raw = _quant_q4_0(x)
+        else:
+            raise NotImplementedError(typ)
+        dims = list(reversed(t.shape))
+        infos += s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
+        infos += struct.pack("<IQ", typ, off)
+        pad = (-len(raw)) % alignment
+        blobs.append(raw + b"\0" * pad)
+        off += len(raw) + pad
+    body = head + infos
+    body += b"\0" * ((-len(body)) % alignment)
+    with open(path, "wb") as f:
+        f.write(body)
+        for b in blobs:
+            f.write(b)
+
+
+# ---------------------------------------------------------------------------- Qwen2 mapping
+def qwen_config_from_gguf(g: GGUFFile):
+    from ..models.qwen import QwenConfig
+
+    arch = g.meta.get("general.architecture", "qwen2")
+    m = lambda k, d=None: g.meta.get(f"{arch}.{k}", d)  # noqa: E731
+    vocab = len(g.meta.get("tokenizer.ggml.tokens", [])) or int(g.tensors["token_embd.weight"][0][1])
+    return QwenConfig(vocab=vocab, d_model=int(m("embedding_length")), n_layers=int(m("block_count")),
+                      n_heads=int(m("attention.head_count")), n_kv_heads=int(m("attention.head_count_kv")),
+                      d_ff=int(m("feed_forward_length")), rope_theta=float(m("rope.freq_base", 1e6)),
+                      norm_eps=float(m("attention.layer_norm_rms_epsilon", 1e-6)),
+                      tie_embeddings="output.weight" not in g.tensors,
+                      qkv_bias="blk.0.attn_q.bias" in g.tensors)
+
+
+def load_qwen_weights(path: str, device="cuda"):
+    """GGUF (llama.cpp tensor names) -> QwenWeights on `device` (bf16)."""
+    from ..models.qwen import QwenWeights
+
+    g = GGUFFile(path)
+    cfg = qwen_config_from_gguf(g)
+    w = QwenWeights.__new__(QwenWeights)
+    w.cfg, w.device, w.tp_rank, w.tp_size = cfg, torch.device(device), 0, 1
+    w.hq, w.hkv, w.f = cfg.n_heads, cfg.n_kv_heads, cfg.d_ff
+    t = lambda n: g.tensor(n).to(device)  # noqa: E731
+    w.embed = t("token_embd.weight")
+    w.lm_head = w.embed if cfg.tie_embeddings else t("output.weight")
+    w.final_norm = t("output_norm.weight")
+    w.attn_norm, w.mlp_norm, w.wqkv, w.bqkv, w.wo, w.wgu, w.wd = [], [], [], [], [], [], []
+    for i in range(cfg.n_layers):
+        p = f"blk.{i}."
+        w.attn_norm.append(t(p + "attn_norm.weight"))
+        w.mlp_norm.append(t(p + "ffn_norm.weight"))
+        w.wqkv.append(torch.cat([t(p + "attn_q.weight"), t(p + "attn_k.weight"), t(p + "attn_v.weight")]).contiguous())
+        w.bqkv.append(torch.cat([t(p + "attn_q.bias"), t(p + "attn_k.bias"), t(p + "attn_v.bias")]).contiguous()
+                      if cfg.qkv_bias else None)
+        w.wo.append(t(p + "attn_output.weight"))
+        w.wgu.append(torch.cat([t(p + "ffn_gate.weight"), t(p + "ffn_up.weight")]).contiguous())
+        w.wd.append(t(p + "ffn_down.weight"))
+    return cfg, w
+
+
+def tokenizer_from_gguf(g: GGUFFile):
+    from ..serving.tokenizer import BPETokenizer
+
+    toks = g.meta.get("tokenizer.ggml.tokens", [])
+    merges = g.meta.get("tokenizer.ggml.merges", [])
+    types = g.meta.get("tokenizer.ggml.token_type", [1] * len(toks))
+    vocab, added = {}, {}
+    for i, (tok, ty) in enumerate(zip(toks, types)):
+        (added if ty in (3, 4) else vocab)[tok] = i
+    return BPETokenizer(vocab, merges, added)
