@@ -371,7 +371,9 @@ class QwenModel:
                 self._step_body(B)
         torch.cuda.current_stream(self.device).wait_stream(s)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        # thread_local: the serving engine captures on its worker thread while
+        # other threads may still issue CUDA calls
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
             self._step_body(B)
         self._graphs[key] = g
         self._want_logits = False

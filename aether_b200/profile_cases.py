@@ -1,0 +1,96 @@
+"""Small, self-terminating cases of the hot kernels for Nsight Compute.
+
+Each case builds inputs larger than the 126 MB L2 (so DRAM counters mean
+something) but only a few hundred MB in total, runs the kernel a few times and
+exits. Meant to be run under ``ncu -k regex:<kernel> -c 1`` after it has run
+once on its own:
+
+    python -m aether_b200.profile_cases gemm        # tcgen05 GEMM 8192x8192x4096
+    python -m aether_b200.profile_cases attn_fwd    # tcgen05 flash attention fwd, B2 H16 S4096 D128 causal
+    python -m aether_b200.profile_cases attn_bwd    # tcgen05 flash attention bwd, same shape
+    python -m aether_b200.profile_cases skinny      # decode GEMM 1 x 3584 -> 37888 (Qwen-7B gate/up)
+    python -m aether_b200.profile_cases decode_attn # split-K decode attention B8 Hq28 Hkv4 S8192
+    python -m aether_b200.profile_cases adamw       # fused AdamW over 64M fp32 params
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from .ops import functional as F
+
+
+def gemm(reps):
+    a = torch.randn(8192, 4096, device="cuda").bfloat16()
+    b = torch.randn(8192, 4096, device="cuda").bfloat16()
+    for _ in range(reps):
+        F.gemm(a, b)
+
+
+def _qkv():
+    B, S, H, D = 2, 4096, 16, 128
+    q = torch.randn(B, S, H, D, device="cuda").bfloat16()
+    return q, torch.randn_like(q), torch.randn_like(q), D ** -0.5
+
+
+def attn_fwd(reps):
+    q, k, v, s = _qkv()
+    for _ in range(reps):
+        F.attention(q, k, v, s, True, impl="tc")
+
+
+def attn_bwd(reps):
+    q, k, v, s = _qkv()
+    o, lse = F.attention(q, k, v, s, True, impl="tc")
+    do = torch.randn_like(q)
+    for _ in range(reps):
+        F.attention_bwd(q, k, v, o, do, lse, s, True, impl="tc")
+
+
+def skinny(reps):
+    x = torch.randn(1, 3584, device="cuda").bfloat16()
+    w = torch.randn(37888, 3584, device="cuda").bfloat16()
+    acc = torch.zeros(1, 37888, device="cuda")
+    for _ in range(reps):
+        F.skinny_gemm(x, w, acc)
+        acc.zero_()
+
+
+def decode_attn(reps):
+    B, Hq, Hkv, D, S = 8, 28, 4, 128, 8192
+    kc = torch.randn(B, S, Hkv, D, device="cuda").bfloat16()
+    vc = torch.randn_like(kc)
+    q = torch.randn(B, Hq * D, device="cuda").bfloat16()
+    slot = torch.arange(B, dtype=torch.int32, device="cuda")
+    seqlen = torch.full((B,), S, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hq * D, dtype=torch.bfloat16, device="cuda")
+    counters = torch.zeros(B * Hkv, dtype=torch.int32, device="cuda")
+    for _ in range(reps):
+        F.decode_attention(q, kc, vc, slot, seqlen, out, Hq, D ** -0.5, splits=8, counters=counters)
+
+
+def adamw(reps):
+    n = 64 * 1024 * 1024
+    p, g = torch.randn(n, device="cuda"), torch.randn(n, device="cuda")
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    pb = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    for i in range(reps):
+        F.adamw_(p, g, m, v, pb, lr=1e-4, beta1=0.9, beta2=0.95, eps=1e-8, wd=0.1, step=i + 1)
+
+
+CASES = {f.__name__: f for f in (gemm, attn_fwd, attn_bwd, skinny, decode_attn, adamw)}
+
+
+def main():
+    name = sys.argv[1] if len(sys.argv) > 1 else ""
+    if name not in CASES:
+        raise SystemExit(f"usage: python -m aether_b200.profile_cases {{{','.join(CASES)}}} [reps]")
+    reps = int(sys.argv[2]) if len(sys.argv) > 2 else 3
+    CASES[name](reps)
+    torch.cuda.synchronize()
+    print(f"{name}: ok")
+
+
+if __name__ == "__main__":
+    main()

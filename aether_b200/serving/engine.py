@@ -84,6 +84,7 @@ class Engine:
         self._stop = threading.Event()
         self._wake = threading.Condition()
         self._gens: dict = {}
+        self.errors: list = []  # formatted tracebacks of worker-side failures
         self.worker = threading.Thread(target=self._loop, name="aether-engine", daemon=True)
         self.worker.start()
 
@@ -177,12 +178,12 @@ class Engine:
             r = self.pending.get()
             slot = self.free_slots.pop(0)
             r.slot = slot
+            self.active[slot] = r  # from here on an error path finishes it
             dev = self.model.device
             ids = torch.tensor([r.prompt_ids], dtype=torch.long, device=dev)
             nxt, logits = self.model.prefill(ids, slots=torch.tensor([slot], dtype=torch.int32, device=dev),
                                              return_logits=True)
             tok = int(sample_rows(logits, [r.params], [[]], [self._gen(r)])[0]) if not r.params.greedy else int(nxt[0])
-            self.active[slot] = r
             if self._emit(r, tok):
                 self._finish(r)
 
@@ -219,6 +220,11 @@ class Engine:
                         if self.pending.empty() and not self._stop.is_set():
                             self._wake.wait(timeout=0.05)
             except Exception as e:  # noqa: BLE001 -- fail every request instead of dying silently
+                import sys
+                import traceback
+
+                self.errors.append(traceback.format_exc())
+                print(f"aether engine: {self.errors[-1]}", file=sys.stderr, flush=True)
                 for r in list(self.active.values()):
                     r.finish_reason = f"error: {e}"
                     self._finish(r)

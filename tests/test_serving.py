@@ -151,6 +151,8 @@ def test_gpu_engine_batched_graph_decode():
     reqs = [eng.submit(p, SamplingParams(max_tokens=8)) for p in prompts]
     outs = [list(eng.stream(r, timeout=120)) for r in reqs]
     eng.shutdown()
+    assert not eng.errors, eng.errors
+    assert all(r.finish_reason == "length" for r in reqs), [r.finish_reason for r in reqs]
     agree = 0
     for p, got in zip(prompts, outs):
         want = ref.generate(torch.tensor([p], device="cuda"), 8, use_graph=False)[0].tolist()
