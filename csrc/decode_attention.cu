@@ -533,3 +533,92 @@ void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std:
 }
 
 }  // namespace aether
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of decode_attention (fused combine). Declared, with
+// its rules and limits, in aether_noalloc.h. It has no counterpart in the
+// reference. Same kernel as above; only where the scratch comes from differs.
+#include <mutex>
+
+#include "aether_noalloc.h"
+
+namespace aether {
+namespace noalloc {
+
+constexpr int kMaxRows = AETHER_NOALLOC_MAX_PARTIAL_ROWS;
+constexpr int kMaxCounters = AETHER_NOALLOC_MAX_COUNTERS;
+constexpr int kMaxDevices = 64;
+
+// One scratch block per device: split partial outputs [rows, 128] fp32, their
+// log-sum-exps [rows] fp32, and the last-CTA counters [kMaxCounters] int32
+// (must be zero before a launch; every launch leaves them zero again).
+static __device__ __align__(256) float g_part_o[kMaxRows * 128];
+static __device__ __align__(256) float g_part_lse[kMaxRows];
+static __device__ __align__(256) int g_counters[kMaxCounters];
+
+struct DeviceScratch {
+  float* part_o = nullptr;
+  float* part_lse = nullptr;
+  int* counters = nullptr;
+  int status = AETHER_NOALLOC_ECUDA;
+};
+static DeviceScratch g_dev[kMaxDevices];
+static std::once_flag g_once[kMaxDevices];
+
+static void setup(int dev) {
+  DeviceScratch s;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_o), g_part_o) != cudaSuccess ||
+      cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_lse), g_part_lse) != cudaSuccess ||
+      cudaGetSymbolAddress(reinterpret_cast<void**>(&s.counters), g_counters) != cudaSuccess ||
+      cudaFuncSetAttribute(dec::decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kKvSmem) !=
+          cudaSuccess ||
+      cudaMemset(s.counters, 0, sizeof(int) * kMaxCounters) != cudaSuccess) {
+    g_dev[dev].status = AETHER_NOALLOC_ECUDA;
+    return;
+  }
+  s.status = AETHER_NOALLOC_OK;
+  g_dev[dev] = s;
+}
+
+}  // namespace noalloc
+}  // namespace aether
+
+extern "C" __attribute__((visibility("default"))) int aether_decode_attention_noalloc(
+    const void* q, int64_t q_rs, const void* k_cache, const void* v_cache, int64_t slot_stride, int64_t pos_stride,
+    const int* slot, const int* seqlen, void* out, int64_t out_rs, int B, int Hq, int Hkv, int D, int splits,
+    float scale, void* stream) {
+  using namespace aether;
+  if (!q || !k_cache || !v_cache || !slot || !seqlen || !out) return AETHER_NOALLOC_EINVAL;
+  if (B < 0 || D != 128 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0 || Hq / Hkv > dec::kMaxGroup || splits < 1 ||
+      splits > dec::kMaxSplits)
+    return AETHER_NOALLOC_EINVAL;
+  if ((int64_t)B * Hq * splits > noalloc::kMaxRows || (int64_t)B * Hkv > noalloc::kMaxCounters)
+    return AETHER_NOALLOC_ETOOBIG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= noalloc::kMaxDevices) return AETHER_NOALLOC_ECUDA;
+  std::call_once(noalloc::g_once[dev], noalloc::setup, dev);
+  const noalloc::DeviceScratch& s = noalloc::g_dev[dev];
+  if (s.status != AETHER_NOALLOC_OK) return s.status;
+  if (B == 0) return AETHER_NOALLOC_OK;
+  dec::DecParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_rs = q_rs;
+  p.kc = static_cast<const __nv_bfloat16*>(k_cache);
+  p.vc = static_cast<const __nv_bfloat16*>(v_cache);
+  p.slot_stride = slot_stride;
+  p.pos_stride = pos_stride;
+  p.slot = slot;
+  p.seqlen = seqlen;
+  p.part_o = s.part_o;
+  p.part_lse = s.part_lse;
+  p.counters = s.counters;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_rs = out_rs;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.splits = splits;
+  p.scale_log2 = scale * dec::kLog2e;
+  dec::decode_attn_kernel<<<dim3((unsigned)splits, (unsigned)(B * Hkv)), 128, dec::kKvSmem,
+                            static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? AETHER_NOALLOC_OK : AETHER_NOALLOC_ECUDA;
+}
