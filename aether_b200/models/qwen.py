@@ -260,9 +260,24 @@ class QwenModel:
                 x = x + y
         last = x.view(B, S, cfg.d_model)[:, -1].contiguous()
         hl, _, _ = F.rmsnorm(last, w.final_norm, cfg.norm_eps)
-        logits = F.gemm(hl, w.lm_head, out_dtype=torch.float32)
+        head = self._prefill_head()
+        logits = F.gemm(hl, head, out_dtype=torch.float32)
+        if head.shape[0] != cfg.vocab:
+            logits = logits[:, : cfg.vocab].contiguous()
         nxt = F.argmax(logits)
         return (nxt, logits) if return_logits else nxt
+
+    def _prefill_head(self) -> torch.Tensor:
+        """LM head for the tensor-core GEMM, whose N must be a multiple of 8:
+        vocabularies that are not get a zero-padded copy (made once)."""
+        V = self.cfg.vocab
+        if V % 8 == 0 or self.device.type != "cuda":
+            return self.w.lm_head
+        if getattr(self, "_head_p", None) is None:
+            hp = torch.zeros((V + 7) // 8 * 8, self.cfg.d_model, dtype=torch.bfloat16, device=self.device)
+            hp[:V].copy_(self.w.lm_head)
+            self._head_p = hp
+        return self._head_p
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int) -> None:

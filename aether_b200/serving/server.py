@@ -23,9 +23,36 @@ from .sampling import SamplingParams
 from .tokenizer import chat_template
 
 
+class RateLimiter:
+    """Token bucket per client address: ``rate`` requests per second with
+    bursts of ``burst`` (reference: the rate limiter of
+    runtime/src/lib.rs:6186-6210)."""
+
+    def __init__(self, rate: float, burst: int, clock=time.monotonic):
+        self.rate, self.burst, self.clock = rate, burst, clock
+        self.buckets: dict = {}
+
+    def allow(self, key: str) -> bool:
+        now = self.clock()
+        tokens, last = self.buckets.get(key, (float(self.burst), now))
+        tokens = min(float(self.burst), tokens + (now - last) * self.rate)
+        ok = tokens >= 1.0
+        self.buckets[key] = (tokens - 1.0 if ok else tokens, now)
+        return ok
+
+
 def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: str = "chatml",
-              vision=None) -> FastAPI:
+              vision=None, rate_limit: RateLimiter | None = None) -> FastAPI:
     app = FastAPI(title="aether_b200")
+
+    if rate_limit is not None:
+        @app.middleware("http")
+        async def _limit(req: HTTPRequest, call_next):
+            if req.method == "POST" and not rate_limit.allow(req.client.host if req.client else "?"):
+                engine.metrics.inc("rate_limited")
+                return JSONResponse({"error": {"message": "rate limit exceeded", "type": "rate_limit"}},
+                                    status_code=429)
+            return await call_next(req)
 
     @app.get("/health")
     def health():
@@ -179,6 +206,9 @@ def main():
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--embeddings", action="store_true", help="also serve a BGE-large-shape /v1/embeddings model")
     ap.add_argument("--vision", action="store_true", help="also serve a DINOv3 ViT-L/16-shape /v1/vision/embed")
+    ap.add_argument("--rate-limit", type=float, default=0.0, help="POST requests per second per client (0 = off)")
+    ap.add_argument("--gguf", default=None, help="load Qwen2 weights (and tokenizer) from a GGUF file")
+    ap.add_argument("--hf", default=None, help="load Qwen2 weights from a Hugging Face directory")
     args = ap.parse_args()
     import uvicorn
 
@@ -193,7 +223,22 @@ def main():
     else:
         cfg = QwenConfig.qwen25_1_5b()
     tok = BPETokenizer.from_file(args.tokenizer) if args.tokenizer else ByteTokenizer()
-    model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq)
+    weights = None
+    if args.gguf:
+        from ..formats import gguf
+
+        cfg, weights = gguf.load_qwen_weights(args.gguf, device=args.device)
+        if not args.tokenizer:
+            tok = gguf.tokenizer_from_gguf(gguf.GGUFFile(args.gguf))
+    elif args.hf:
+        import os
+
+        from ..formats import hf
+
+        cfg, weights = hf.load_qwen_hf(args.hf, device=args.device)
+        if not args.tokenizer and os.path.exists(os.path.join(args.hf, "tokenizer.json")):
+            tok = BPETokenizer.from_file(os.path.join(args.hf, "tokenizer.json"))
+    model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq, weights=weights)
     engine = Engine(model, tok, max_concurrent=args.max_concurrent, use_graph=args.device != "cpu")
     embedder = vision = None
     if args.embeddings:
@@ -204,7 +249,8 @@ def main():
         from ..models.encoders import VitConfig, VitEncoder
 
         vision = VitEncoder(VitConfig.vitl16(), device=args.device)
-    app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, vision=vision)
+    limiter = RateLimiter(args.rate_limit, max(1, int(args.rate_limit))) if args.rate_limit > 0 else None
+    app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, vision=vision, rate_limit=limiter)
     uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
 
 

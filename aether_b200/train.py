@@ -17,8 +17,12 @@ from .parallel.dp import DataParallel
 class Trainer:
     def __init__(self, model, info, *, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
                  micro_batch: int = 8, warmup_steps: int = 0, total_steps: int = 0, max_grad_norm: float = 0.0,
-                 dp=None):
+                 dp=None, tracer=None, crash_dir: str | None = None):
+        """tracer: optional ``utils.trace.Tracer`` (sections fwd_bwd / optimizer);
+        crash_dir: write ``crash_<pid>_<step>.dump`` there if a step raises."""
         self.model = model
+        self.tracer = tracer
+        self.crash_dir = crash_dir
         self.info = info
         self.micro_batch = micro_batch
         self.base_lr = lr
@@ -37,6 +41,19 @@ class Trainer:
     def train_step(self, tokens: torch.Tensor) -> torch.Tensor:
         """tokens: [b, S+1] int64 (this rank's sequences). Returns the mean loss
         of this rank as a device tensor (no host sync)."""
+        if self.crash_dir is None:
+            return self._train_step(tokens)
+        from .utils.crash import crash_guard
+
+        with crash_guard(lambda: self.step_idx, self.crash_dir):
+            return self._train_step(tokens)
+
+    def _section(self, name):
+        import contextlib
+
+        return self.tracer.section(name) if self.tracer is not None else contextlib.nullcontext()
+
+    def _train_step(self, tokens: torch.Tensor) -> torch.Tensor:
         dev = self.model.device
         b = tokens.shape[0]
         mb = min(self.micro_batch, b)
@@ -44,15 +61,17 @@ class Trainer:
         n_tok = b * (tokens.shape[1] - 1)
         self.model.arena.zero_grad()
         self._loss_acc.zero_()
-        for i in range(n_mb):
-            chunk = tokens[i * mb : (i + 1) * mb]
-            if chunk.device != dev:
-                chunk = chunk.to(dev, non_blocking=True)
-            ids = chunk[:, :-1]
-            tgt = chunk[:, 1:]
-            loss = self.model.loss(ids.contiguous(), tgt.contiguous(), loss_scale=1.0 / n_tok)
-            loss.backward()
-            self._loss_acc += loss.detach()
-        self.dp.step(lr=self.lr_at(self.step_idx))
+        with self._section("fwd_bwd"):
+            for i in range(n_mb):
+                chunk = tokens[i * mb : (i + 1) * mb]
+                if chunk.device != dev:
+                    chunk = chunk.to(dev, non_blocking=True)
+                ids = chunk[:, :-1]
+                tgt = chunk[:, 1:]
+                loss = self.model.loss(ids.contiguous(), tgt.contiguous(), loss_scale=1.0 / n_tok)
+                loss.backward()
+                self._loss_acc += loss.detach()
+        with self._section("optimizer"):
+            self.dp.step(lr=self.lr_at(self.step_idx))
         self.step_idx += 1
         return self._loss_acc

@@ -178,3 +178,14 @@ def test_gguf_qwen_loader_logits(tmp_path):
     a = QwenModel(cfg, device="cpu", weights=w, max_batch=1).reference_logits(toks)
     b = QwenModel(cfg2, device="cpu", weights=w2, max_batch=1).reference_logits(toks)
     assert torch.equal(a, b)
+
+
+def test_tokenizer_from_gguf_metadata(tmp_path):
+    toks = ["a", "b", "c", "ab", "abc", "<|im_end|>"]
+    meta = {"general.architecture": "qwen2", "tokenizer.ggml.tokens": toks, "tokenizer.ggml.merges": ["a b", "ab c"],
+            "tokenizer.ggml.token_type": [1, 1, 1, 1, 1, 3]}
+    p = str(tmp_path / "tok.gguf")
+    gguf.write_gguf(p, meta, {"x": (torch.zeros(8), gguf.F32)})
+    tok = gguf.tokenizer_from_gguf(gguf.GGUFFile(p))
+    assert tok.encode("abc<|im_end|>") == [4, 5]
+    assert tok.decode([3, 2]) == "abc" and tok.eos_id == 5

@@ -158,3 +158,14 @@ def test_gpu_engine_batched_graph_decode():
         want = ref.generate(torch.tensor([p], device="cuda"), 8, use_graph=False)[0].tolist()
         agree += sum(int(a == b) for a, b in zip(got, want))
     assert agree >= 0.9 * 24, (outs,)
+
+
+def test_rate_limiter_token_bucket():
+    from aether_b200.serving.server import RateLimiter
+
+    now = [0.0]
+    rl = RateLimiter(rate=2.0, burst=3, clock=lambda: now[0])
+    assert [rl.allow("x") for _ in range(4)] == [True, True, True, False]
+    assert rl.allow("y")  # buckets are per client
+    now[0] += 0.5  # one token back at 2/s
+    assert rl.allow("x") and not rl.allow("x")
