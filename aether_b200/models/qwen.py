@@ -155,7 +155,11 @@ class QwenModel:
     row-parallel o_proj and down_proj (see ``parallel/tp.py``)."""
 
     def __init__(self, cfg: QwenConfig, device="cuda", seed: int = 0, max_batch: int = 64, max_seq: int | None = None,
-                 weights: QwenWeights | None = None, tp=None, decode_splits: int = 0):
+                 weights: QwenWeights | None = None, tp=None, decode_splits: int = 0, kv_pages: int = 0,
+                 page_size: int = 64):
+        """kv_pages > 0 selects the paged KV cache (``serving.kv.PagedKVCache``)
+        with that many pages of ``page_size`` tokens shared by all sequences;
+        otherwise every batch slot owns a contiguous max_seq cache."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.tp = tp
@@ -166,7 +170,16 @@ class QwenModel:
         self.max_batch = max_batch
         self.max_seq = max_seq or cfg.max_seq
         # one extra slot absorbs the K/V writes of padded batch rows
-        self.cache = KVCache(cfg, self.hkv, max_batch + 1, self.max_seq, self.device)
+        if kv_pages > 0:
+            from ..serving.kv import PagedKVCache
+
+            self.cache = PagedKVCache(cfg.n_layers, self.hkv, cfg.head_dim, kv_pages, page_size, max_batch + 1,
+                                      self.max_seq, self.device)
+            self.page_table = self.cache.table
+        else:
+            self.cache = KVCache(cfg, self.hkv, max_batch + 1, self.max_seq, self.device)
+            self.page_table = None
+        self.paged = self.page_table is not None
         self.scratch_slot = max_batch
         cos, sin = ref.rope_tables(self.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
@@ -231,16 +244,22 @@ class QwenModel:
             h, _, _ = F.rmsnorm(x, w.attn_norm[i], cfg.norm_eps)
             qkv = F.gemm(h, w.wqkv[i], bias=w.bqkv[i])
             F.rope_kv_append(qkv, pos, slot_t, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq,
-                             self.hkv, D)
+                             self.hkv, D, page_table=self.page_table)
             q = qkv.view(B, S, row)[:, :, : self.hq * D].view(B, S, self.hq, D)
             if start_pos == 0:
                 k = qkv.view(B, S, row)[:, :, self.hq * D : (self.hq + self.hkv) * D].view(B, S, self.hkv, D)
                 v = qkv.view(B, S, row)[:, :, (self.hq + self.hkv) * D :].view(B, S, self.hkv, D)
                 o, _ = F.attention(q, k, v, self.scale, True, 0, want_lse=False)
             else:
-                assert bool((slots == torch.arange(B, device=slots.device)).all()), "chunked prefill needs slots 0..B-1"
-                k = self.cache.k[i][:B, : start_pos + S]
-                v = self.cache.v[i][:B, : start_pos + S]
+                Lk = start_pos + S
+                if self.paged:
+                    rows = [int(r) for r in slots.tolist()]
+                    k = torch.stack([F.gather_kv(self.cache.k[i], r, Lk, self.page_table) for r in rows])
+                    v = torch.stack([F.gather_kv(self.cache.v[i], r, Lk, self.page_table) for r in rows])
+                else:
+                    assert bool((slots == torch.arange(B, device=slots.device)).all()), "chunked prefill needs slots 0..B-1"
+                    k = self.cache.k[i][:B, :Lk]
+                    v = self.cache.v[i][:B, :Lk]
                 o, _ = F.attention(q, k, v, self.scale, True, start_pos, want_lse=False)
             o2 = o.view(T, self.hq * D)
             if self.tp is None:
@@ -301,9 +320,9 @@ class QwenModel:
         for i in range(L):
             F.skinny_gemm(h, w.wqkv[i], acc)
             F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i],
-                                self.hq, self.hkv, D)
+                                self.hq, self.hkv, D, page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
-                               self.decode_splits, b["part_o"], b["part_lse"], b["counters"])
+                               self.decode_splits, b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table)
             if self.tp is None:
                 F.skinny_gemm(o, w.wo[i], acc)
                 racc = acc
@@ -340,9 +359,10 @@ class QwenModel:
             F.rmsnorm_into(x, w.attn_norm[i], h, cfg.norm_eps)
             F.skinny_gemm(h, w.wqkv[i], acc)
             F.skinny_finalize(acc, qkv, bias=w.bqkv[i])
-            F.rope_kv_append(qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D)
+            F.rope_kv_append(qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D,
+                             page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
-                               self.decode_splits, b["part_o"], b["part_lse"])
+                               self.decode_splits, b["part_o"], b["part_lse"], page_table=self.page_table)
             if self.tp is None:
                 F.skinny_gemm(o, w.wo[i], acc)
                 F.skinny_finalize(acc, x2, res=x)
@@ -428,6 +448,10 @@ class QwenModel:
         B, S = prompts.shape
         assert B <= self.max_batch and S + max_new_tokens <= self.max_seq
         out = torch.empty(B, max_new_tokens, dtype=torch.long, device=self.device)
+        if self.paged:
+            for r in range(B):
+                self.cache.release(r)
+                self.cache.ensure(r, S + max_new_tokens)
         nxt = self.prefill(prompts)
         out[:, 0] = nxt
         pos = torch.full((B,), S, dtype=torch.int32, device=self.device)

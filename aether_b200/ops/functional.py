@@ -367,25 +367,46 @@ def skinny_finalize(acc, y, bias=None, res=None, swiglu=False):
     return y
 
 
-def rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D):
+def _kv_index(slot, pos, k_cache, page_table):
+    """(dim-0 index, dim-1 index) of (sequence row, position) in a cache: the
+    slot and position, or with a page table the physical page and its row."""
+    if page_table is None:
+        return slot.long(), pos.long()
+    P = k_cache.shape[1]
+    pos = pos.long()
+    return page_table[slot.long(), pos // P].long(), pos % P
+
+
+def rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D, page_table=None):
     """Rotates q/k of qkv [T, row] in place and writes k, v into the caches
-    [slots, max_seq, Hkv, D] at (slot[t], pos[t])."""
+    [slots, max_seq, Hkv, D] at (slot[t], pos[t]) -- or, with ``page_table``
+    [rows, max_pages] int32, into page pools [pages, page_size, Hkv, D]."""
     if _cuda(qkv):
-        C().rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, int(Hq), int(Hkv), int(D))
+        C().rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, int(Hq), int(Hkv), int(D), page_table)
         return qkv
     rope_(qkv, pos, cos_t, sin_t, Hq + Hkv, D)
     T = qkv.shape[0]
     k = qkv[:, Hq * D : (Hq + Hkv) * D].view(T, Hkv, D)
     v = qkv[:, (Hq + Hkv) * D : (Hq + 2 * Hkv) * D].view(T, Hkv, D)
-    k_cache[slot.long(), pos.long()] = k
-    v_cache[slot.long(), pos.long()] = v
+    i0, i1 = _kv_index(slot, pos, k_cache, page_table)
+    k_cache[i0, i1] = k
+    v_cache[i0, i1] = v
     return qkv
 
 
+def gather_kv(cache, slot: int, L: int, page_table=None):
+    """Keys (or values) [L, Hkv, D] of one sequence row as a contiguous tensor."""
+    if page_table is None:
+        return cache[slot, :L]
+    P = cache.shape[1]
+    pages = page_table[slot, : (L + P - 1) // P].long()
+    return cache[pages].reshape(-1, cache.shape[2], cache.shape[3])[:L]
+
+
 def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8, part_o=None, part_lse=None,
-                     counters=None):
-    """q [B, >=Hq*D] (one new token per sequence), caches [slots, max_seq, Hkv, D],
-    seqlen [B] = valid keys. Writes out [B, Hq*D]."""
+                     counters=None, page_table=None):
+    """q [B, >=Hq*D] (one new token per sequence), caches [slots, max_seq, Hkv, D]
+    (or page pools with ``page_table``), seqlen [B] = valid keys. Writes out [B, Hq*D]."""
     B = q.shape[0]
     D = k_cache.shape[3]
     if _cuda(q):
@@ -393,15 +414,15 @@ def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8
             part_o = torch.empty(B * Hq * splits * D, dtype=torch.float32, device=q.device)
             part_lse = torch.empty(B * Hq * splits, dtype=torch.float32, device=q.device)
         C().decode_attention(q, k_cache, v_cache, slot, seqlen, out, part_o, part_lse, int(Hq), int(splits),
-                             float(scale), counters)
+                             float(scale), counters, page_table)
         return out
     Hkv = k_cache.shape[2]
     for b in range(B):
         L = int(seqlen[b])
         s = int(slot[b])
         qb = q[b, : Hq * D].view(1, 1, Hq, D)
-        kb = k_cache[s, :L].unsqueeze(0)
-        vb = v_cache[s, :L].unsqueeze(0)
+        kb = gather_kv(k_cache, s, L, page_table).unsqueeze(0)
+        vb = gather_kv(v_cache, s, L, page_table).unsqueeze(0)
         o, _ = ref.attention(qb, kb, vb, scale, causal=False)
         out[b, : Hq * D] = o.reshape(-1).to(out.dtype)
     return out
@@ -417,11 +438,12 @@ def rmsnorm_into(x, w, out, eps=1e-6):
     return out
 
 
-def qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D):
+def qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D, page_table=None):
     """Decode QKV epilogue: qkv = rope(bf16(acc + bias)); k/v appended to the
     caches at (slot, pos); acc zeroed."""
     if _cuda(acc):
-        C().qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, int(Hq), int(Hkv), int(D))
+        C().qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, int(Hq), int(Hkv), int(D),
+                              page_table)
         return qkv
     B, W = qkv.shape[0], (Hq + 2 * Hkv) * D
     a = acc[:B, :W].clone()
@@ -429,7 +451,7 @@ def qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache,
         a = a + bias.float()
     qkv[:, :W].copy_(a.to(qkv.dtype))
     acc[:B, :W] = 0
-    return rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D)
+    return rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D, page_table)
 
 
 def finalize_residual_norm(acc, y, w, h, bias=None, res=None, eps=1e-6):

@@ -10,6 +10,7 @@ tensor cores.
 """
 from __future__ import annotations
 
+import collections
 import itertools
 import queue
 import threading
@@ -85,6 +86,8 @@ class Engine:
         self._wake = threading.Condition()
         self._gens: dict = {}
         self.errors: list = []  # formatted tracebacks of worker-side failures
+        self._deferred: collections.deque = collections.deque()  # admitted later, when KV pages free up
+        self.paged = bool(getattr(model, "paged", False))
         self.worker = threading.Thread(target=self._loop, name="aether-engine", daemon=True)
         self.worker.start()
 
@@ -96,6 +99,10 @@ class Engine:
             raise ValueError("empty prompt")
         if len(prompt_ids) + params.max_tokens > limit:
             params.max_tokens = max(1, limit - len(prompt_ids))
+        if self.paged:
+            c = self.model.cache
+            if c.pages_for(len(prompt_ids) + params.max_tokens) > c.alloc.num_pages - 1:
+                raise ValueError("request needs more KV pages than the pool holds")
         r = Request(list(prompt_ids), params, id=next(self._ids), t_submit=time.perf_counter())
         self.metrics.inc("requests_total")
         self.metrics.inc("prompt_tokens", len(prompt_ids))
@@ -170,19 +177,47 @@ class Engine:
         self._gens.pop(r.id, None)
         if r.slot >= 0:
             self.active.pop(r.slot, None)
+            if self.paged:
+                self.model.cache.release(r.slot)
             self.free_slots.append(r.slot)
+
+    def _reserve_pages(self, r: Request, slot: int):
+        """Paged cache: shares cached prefix pages and reserves the pages the
+        whole request can reach. Returns the number of prompt tokens whose K/V
+        are already cached, or None (request deferred) if the pool is full."""
+        from .kv import NoPages
+
+        c = self.model.cache
+        try:
+            n = c.match_prefix(slot, r.prompt_ids)
+            c.ensure(slot, len(r.prompt_ids) + r.params.max_tokens)
+        except NoPages:
+            c.release(slot)
+            return None
+        if n:
+            self.metrics.inc("prefix_cached_tokens", n)
+        return n
 
     @torch.no_grad()
     def _admit(self):
-        while self.free_slots and not self.pending.empty():
-            r = self.pending.get()
+        while self.free_slots and (self._deferred or not self.pending.empty()):
+            r = self._deferred.popleft() if self._deferred else self.pending.get()
             slot = self.free_slots.pop(0)
+            cached = 0
+            if self.paged:
+                cached = self._reserve_pages(r, slot)
+                if cached is None:  # wait for running requests to release pages
+                    self.free_slots.insert(0, slot)
+                    self._deferred.appendleft(r)
+                    return
             r.slot = slot
             self.active[slot] = r  # from here on an error path finishes it
             dev = self.model.device
-            ids = torch.tensor([r.prompt_ids], dtype=torch.long, device=dev)
+            ids = torch.tensor([r.prompt_ids[cached:]], dtype=torch.long, device=dev)
             nxt, logits = self.model.prefill(ids, slots=torch.tensor([slot], dtype=torch.int32, device=dev),
-                                             return_logits=True)
+                                             start_pos=cached, return_logits=True)
+            if self.paged:
+                self.model.cache.register_prompt(slot, r.prompt_ids)
             tok = int(sample_rows(logits, [r.params], [[]], [self._gen(r)])[0]) if not r.params.greedy else int(nxt[0])
             if self._emit(r, tok):
                 self._finish(r)
@@ -211,7 +246,7 @@ class Engine:
         while not self._stop.is_set():
             try:
                 self._admit()
-                self.metrics.queue_depth = self.pending.qsize()
+                self.metrics.queue_depth = self.pending.qsize() + len(self._deferred)
                 self.metrics.active = len(self.active)
                 if self.active:
                     self._tick()
@@ -228,7 +263,7 @@ class Engine:
                 for r in list(self.active.values()):
                     r.finish_reason = f"error: {e}"
                     self._finish(r)
-                while not self.pending.empty():
-                    r = self.pending.get()
+                while self._deferred or not self.pending.empty():
+                    r = self._deferred.popleft() if self._deferred else self.pending.get()
                     r.finish_reason = f"error: {e}"
                     r.out.put(None)

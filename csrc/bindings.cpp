@@ -65,13 +65,14 @@ void skinny_finalize(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bia
                      bool swiglu);
 // decode_attention.cu
 void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t,
-                    at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv, int64_t D);
+                    at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv, int64_t D,
+                    std::optional<at::Tensor> page_table);
 void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slot, at::Tensor seqlen,
                       at::Tensor out, at::Tensor part_o, at::Tensor part_lse, int64_t Hq, int64_t splits,
-                      double scale, std::optional<at::Tensor> counters);
+                      double scale, std::optional<at::Tensor> counters, std::optional<at::Tensor> page_table);
 void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tensor qkv, at::Tensor pos, at::Tensor slot,
                        at::Tensor cos_t, at::Tensor sin_t, at::Tensor k_cache, at::Tensor v_cache, int64_t Hq,
-                       int64_t Hkv, int64_t D);
+                       int64_t Hkv, int64_t D, std::optional<at::Tensor> page_table);
 void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
                             at::Tensor y, at::Tensor w, at::Tensor h, double eps);
 }  // namespace aether
@@ -110,10 +111,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("allreduce_nvls", &aether::allreduce_nvls);
   m.def("dp_reduce_adamw", &aether::dp_reduce_adamw);
   m.def("skinny_finalize", &aether::skinny_finalize);
-  m.def("rope_kv_append", &aether::rope_kv_append);
+  m.def("rope_kv_append", &aether::rope_kv_append, "qkv"_a, "pos"_a, "slot"_a, "cos_t"_a, "sin_t"_a, "k_cache"_a,
+        "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
   m.def("decode_attention", &aether::decode_attention, "q"_a, "k_cache"_a, "v_cache"_a, "slot"_a, "seqlen"_a, "out"_a,
-        "part_o"_a, "part_lse"_a, "Hq"_a, "splits"_a, "scale"_a, "counters"_a = pybind11::none());
-  m.def("qkv_finalize_rope", &aether::qkv_finalize_rope);
+        "part_o"_a, "part_lse"_a, "Hq"_a, "splits"_a, "scale"_a, "counters"_a = pybind11::none(),
+        "page_table"_a = pybind11::none());
+  m.def("qkv_finalize_rope", &aether::qkv_finalize_rope, "acc"_a, "bias"_a, "qkv"_a, "pos"_a, "slot"_a, "cos_t"_a,
+        "sin_t"_a, "k_cache"_a, "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
   m.def("finalize_residual_norm", &aether::finalize_residual_norm);
   m.def("read_and_clear_status", &aether::read_and_clear_status,
         "Returns (and clears) the device status word set by kernels whose bounded waits expired");

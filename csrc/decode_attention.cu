@@ -41,13 +41,31 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return u;
 }
 
+// Paged KV: with a page table, a cache is a pool [pages, page_size, Hkv, D]
+// and key t of the sequence in table row `seq` lives in physical page
+// table[seq * stride + t / page_size] at row t % page_size (page_size a power of
+// two). Without one, the cache is [slots, max_seq, Hkv, D] indexed by slot.
+struct PageMap {
+  const int* table = nullptr;
+  int stride = 0;
+  int shift = 0;
+};
+
+// element offset of (sequence row `seq`, position t) -- head 0, dim 0
+__device__ __forceinline__ int64_t kv_offset(const PageMap& pm, int seq, int t, int64_t slot_stride,
+                                             int64_t pos_stride) {
+  if (pm.table == nullptr) return (int64_t)seq * slot_stride + (int64_t)t * pos_stride;
+  const int64_t phys = pm.table[(int64_t)seq * pm.stride + (t >> pm.shift)];
+  return ((phys << pm.shift) | (int64_t)(t & ((1 << pm.shift) - 1))) * pos_stride;
+}
+
 // qkv: [T, row] with q heads [0,Hq), k heads [Hq, Hq+Hkv), v heads after.
 // One thread per (token, head, 8-wide chunk of the half head).
 __global__ void rope_kv_append_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row, const int* __restrict__ pos,
                                       const int* __restrict__ slot, const float* __restrict__ cos_t,
                                       const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ kc,
                                       __nv_bfloat16* __restrict__ vc, int64_t T, int Hq, int Hkv, int D,
-                                      int64_t slot_stride, int64_t pos_stride) {
+                                      int64_t slot_stride, int64_t pos_stride, PageMap pm) {
   const int half = D / 2, chunks = half / 8;
   const int H = Hq + 2 * Hkv;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -82,7 +100,7 @@ __global__ void rope_kv_append_kernel(__nv_bfloat16* __restrict__ qkv, int64_t r
   const int s = slot[t];
   const bool is_k = h < Hq + Hkv;
   const int hk = is_k ? h - Hq : h - Hq - Hkv;
-  __nv_bfloat16* dst = (is_k ? kc : vc) + (int64_t)s * slot_stride + (int64_t)p * pos_stride + (int64_t)hk * D;
+  __nv_bfloat16* dst = (is_k ? kc : vc) + kv_offset(pm, s, p, slot_stride, pos_stride) + (int64_t)hk * D;
   *reinterpret_cast<uint4*>(dst + c) = ua;
   *reinterpret_cast<uint4*>(dst + half + c) = ub;
   if (is_k) {  // keep the rotated k in qkv too (prefill attention reads it there)
@@ -106,6 +124,7 @@ struct DecParams {
   int64_t out_rs;
   int Hq, Hkv, splits;
   float scale_log2;
+  PageMap pm;  // table == nullptr: contiguous per-slot caches
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
@@ -143,8 +162,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
   }
 
   const int s = p.slot[b];
-  const __nv_bfloat16* kbase = p.kc + (int64_t)s * p.slot_stride + (int64_t)hk * D;
-  const __nv_bfloat16* vbase = p.vc + (int64_t)s * p.slot_stride + (int64_t)hk * D;
+  const __nv_bfloat16* kbase = p.kc + (int64_t)hk * D;
+  const __nv_bfloat16* vbase = p.vc + (int64_t)hk * D;
   float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][4];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g) {
@@ -159,8 +178,9 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
       const int r = i >> 4, c = i & 15;
       const bool ok = r < nblk;
       const uint32_t off = (uint32_t)(r * 256 + ((c ^ (r & 15)) << 4));
-      cp_async16(sK + off, kbase + (int64_t)(ok ? blk + r : blk) * p.pos_stride + c * 8, ok);
-      cp_async16(sV + (uint32_t)(r * 256 + (c << 4)), vbase + (int64_t)(ok ? blk + r : blk) * p.pos_stride + c * 8, ok);
+      const int64_t ro = kv_offset(p.pm, s, ok ? blk + r : blk, p.slot_stride, p.pos_stride);
+      cp_async16(sK + off, kbase + ro + c * 8, ok);
+      cp_async16(sV + (uint32_t)(r * 256 + (c << 4)), vbase + ro + c * 8, ok);
     }
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
@@ -314,7 +334,7 @@ __global__ void qkv_finalize_rope_kernel(float* __restrict__ acc, int64_t ldacc,
                                          const int* __restrict__ slot, const float* __restrict__ cos_t,
                                          const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ kc,
                                          __nv_bfloat16* __restrict__ vc, int B, int Hq, int Hkv, int D,
-                                         int64_t slot_stride, int64_t pos_stride) {
+                                         int64_t slot_stride, int64_t pos_stride, PageMap pm) {
   asm volatile("griddepcontrol.launch_dependents;");
   const int half = D / 2, chunks = half / 8;
   const int H = Hq + 2 * Hkv;
@@ -363,7 +383,7 @@ __global__ void qkv_finalize_rope_kernel(float* __restrict__ acc, int64_t ldacc,
   if (h >= Hq) {
     const bool is_k = h < Hq + Hkv;
     const int hk = is_k ? h - Hq : h - Hq - Hkv;
-    __nv_bfloat16* dst = (is_k ? kc : vc) + (int64_t)slot[b] * slot_stride + (int64_t)p_ * pos_stride + (int64_t)hk * D;
+    __nv_bfloat16* dst = (is_k ? kc : vc) + kv_offset(pm, slot[b], p_, slot_stride, pos_stride) + (int64_t)hk * D;
     *reinterpret_cast<uint4*>(dst + c) = ua;
     *reinterpret_cast<uint4*>(dst + half + c) = ub;
   }
@@ -415,10 +435,31 @@ __global__ void __launch_bounds__(1024) finalize_residual_norm_kernel(float* __r
 
 }  // namespace dec
 
+namespace {
+// page_table: CUDA int32 [rows, max_pages] (rows indexed by `slot`), caches
+// [pages, page_size, Hkv, D] with page_size a power of two.
+dec::PageMap page_map(const std::optional<at::Tensor>& page_table, const at::Tensor& cache) {
+  dec::PageMap pm;
+  if (!page_table || !page_table->defined()) return pm;
+  TORCH_CHECK(page_table->is_cuda() && page_table->scalar_type() == at::kInt && page_table->dim() == 2 &&
+                  page_table->stride(1) == 1,
+              "page_table: CUDA int32 [rows, max_pages] with unit inner stride");
+  const int64_t P = cache.size(1);
+  TORCH_CHECK(P > 0 && (P & (P - 1)) == 0, "paged cache: page size must be a power of two");
+  pm.table = page_table->data_ptr<int>();
+  pm.stride = (int)page_table->stride(0);
+  int shift = 0;
+  while ((int64_t(1) << shift) < P) ++shift;
+  pm.shift = shift;
+  return pm;
+}
+}  // namespace
+
 // qkv [T, row] bf16 (rotated in place), pos/slot int32 [T], cos/sin [max_pos, D/2],
-// k_cache/v_cache [slots, max_seq, Hkv, D].
+// k_cache/v_cache [slots, max_seq, Hkv, D] (or page pools with page_table).
 void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t,
-                    at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv, int64_t D) {
+                    at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv, int64_t D,
+                    std::optional<at::Tensor> page_table) {
   TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.scalar_type() == at::kBFloat16, "rope_kv_append: qkv");
   TORCH_CHECK(qkv.size(1) >= (Hq + 2 * Hkv) * D && qkv.stride(0) % 8 == 0, "rope_kv_append: qkv row");
   TORCH_CHECK(pos.scalar_type() == at::kInt && slot.scalar_type() == at::kInt, "rope_kv_append: int32 pos/slot");
@@ -434,14 +475,14 @@ void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor 
       reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), pos.data_ptr<int>(), slot.data_ptr<int>(),
       cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), T, (int)Hq, (int)Hkv, (int)D, k_cache.stride(0),
-      k_cache.stride(1));
+      k_cache.stride(1), page_map(page_table, k_cache));
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
 // q: [B, q_rs] (head h at h*D); out: [B, out_rs]; part buffers sized [B*Hq*splits*(D+1)].
 void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slot, at::Tensor seqlen,
                       at::Tensor out, at::Tensor part_o, at::Tensor part_lse, int64_t Hq, int64_t splits,
-                      double scale, std::optional<at::Tensor> counters) {
+                      double scale, std::optional<at::Tensor> counters, std::optional<at::Tensor> page_table) {
   const int64_t B = q.size(0);
   const int64_t Hkv = k_cache.size(2), D = k_cache.size(3);
   TORCH_CHECK(D == 128, "decode_attention: head_dim 128");
@@ -467,6 +508,7 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
   p.scale_log2 = (float)scale * dec::kLog2e;
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.out_rs = out.stride(0);
+  p.pm = page_map(page_table, k_cache);
   auto stream = at::cuda::getCurrentCUDAStream();
   static bool attr_set[64] = {false};
   const int dev = current_device();
@@ -497,7 +539,7 @@ namespace aether {
 // Decode QKV epilogue: qkv rows = rope(acc + bias); k/v appended to the caches; acc zeroed.
 void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tensor qkv, at::Tensor pos, at::Tensor slot,
                        at::Tensor cos_t, at::Tensor sin_t, at::Tensor k_cache, at::Tensor v_cache, int64_t Hq,
-                       int64_t Hkv, int64_t D) {
+                       int64_t Hkv, int64_t D, std::optional<at::Tensor> page_table) {
   const int64_t B = qkv.size(0);
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.size(1) >= (Hq + 2 * Hkv) * D, "qkv_finalize_rope: acc");
   TORCH_CHECK(qkv.stride(1) == 1 && qkv.stride(0) % 8 == 0 && D % 16 == 0, "qkv_finalize_rope: qkv layout");
@@ -511,7 +553,7 @@ void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tenso
       reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), pos.data_ptr<int>(), slot.data_ptr<int>(),
       cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), (int)B, (int)Hq, (int)Hkv, (int)D, k_cache.stride(0),
-      k_cache.stride(1));
+      k_cache.stride(1), page_map(page_table, k_cache));
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
