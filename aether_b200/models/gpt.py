@@ -126,6 +126,19 @@ class GPT:
                     mv.copy_(t.to(self.device))
         a.sync_bf16_from_master()
 
+    def _linear(self, i: int, name: str, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """The projection ``name`` of layer i (adapters replace this hook)."""
+        return A.linear(x, self.arena[f"l{i}.{name}"], residual=residual)
+
+    def freeze(self) -> None:
+        """Stops gradients to every base parameter (adapter fine-tuning): the
+        weight-gradient GEMMs are skipped and the flat gradient stays unused."""
+        for name in self.arena.names():
+            v = self.arena[name]
+            v.requires_grad_(False)
+            if hasattr(v, "main_grad"):
+                del v.main_grad
+
     def positions(self, B: int, S: int) -> torch.Tensor:
         key = (B, S)
         if key not in self._pos_cache:
@@ -144,16 +157,17 @@ class GPT:
         pos = self.positions(B, S)
         if self.first:
             x = A.embedding(a["tok_emb"], ids.reshape(-1))  # [T, d]
+        lin = self._linear
         for i in self.layers:
             h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
-            qkv = A.linear(h, a[f"l{i}.wqkv"])
+            qkv = lin(i, "wqkv", h)
             qkv = A.rope_(qkv, pos, self.rope_cos, self.rope_sin, Hq + Hkv, D)
             o = A.attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True)
-            x = A.linear(o, a[f"l{i}.wo"], residual=x)
+            x = lin(i, "wo", o, residual=x)
             h = A.rmsnorm(x, a[f"l{i}.mlp_norm"], cfg.norm_eps)
-            gu = A.linear(h, a[f"l{i}.wgu"])
+            gu = lin(i, "wgu", h)
             act = A.swiglu(gu)
-            x = A.linear(act, a[f"l{i}.wd"], residual=x)
+            x = lin(i, "wd", act, residual=x)
         return A.rmsnorm(x, a["final_norm"], cfg.norm_eps) if self.last else x
 
     def loss(self, ids: torch.Tensor, targets: torch.Tensor, loss_scale: float | None = None,

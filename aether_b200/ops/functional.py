@@ -469,3 +469,40 @@ def finalize_residual_norm(acc, y, w, h, bias=None, res=None, eps=1e-6):
     acc[:B, :N] = 0
     rmsnorm_into(y, w, h, eps)
     return y, h
+
+
+# ------------------------------------------------------------------ block quantisation (QLoRA base weights)
+Q8_0, Q4_0 = 8, 2  # GGUF type ids
+_QBYTES = {Q8_0: 34, Q4_0: 18}
+
+
+def quantize_blocks(x, fmt=Q8_0):
+    """bf16 tensor (numel % 32 == 0) -> uint8 GGUF blocks (Q8_0 or Q4_0)."""
+    n = x.numel()
+    assert n % 32 == 0
+    if _cuda(x):
+        out = torch.empty(n // 32 * _QBYTES[fmt], dtype=torch.uint8, device=x.device)
+        C().quantize_blocks(x.contiguous(), out, int(fmt))
+        return out
+    from ..formats import gguf
+
+    q = gguf._quant_q8_0 if fmt == Q8_0 else gguf._quant_q4_0
+    return torch.frombuffer(bytearray(q(x.float().numpy().reshape(-1))), dtype=torch.uint8)
+
+
+def dequantize_blocks(q, shape, fmt=Q8_0, out=None):
+    """uint8 GGUF blocks -> bf16 tensor of ``shape``."""
+    n = 1
+    for s_ in shape:
+        n *= int(s_)
+    if _cuda(q):
+        out = out if out is not None else torch.empty(shape, dtype=torch.bfloat16, device=q.device)
+        C().dequantize_blocks(q, out, int(fmt))
+        return out
+    from ..formats import gguf
+
+    x = torch.from_numpy(gguf.dequantize(q.numpy(), fmt, n)).reshape(shape).to(torch.bfloat16)
+    if out is not None:
+        out.copy_(x)
+        return out
+    return x

@@ -75,6 +75,9 @@ void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tenso
                        int64_t Hkv, int64_t D, std::optional<at::Tensor> page_table);
 void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
                             at::Tensor y, at::Tensor w, at::Tensor h, double eps);
+// quant.cu
+void quantize_blocks(at::Tensor x, at::Tensor out, int64_t fmt);
+void dequantize_blocks(at::Tensor in, at::Tensor y, int64_t fmt);
 }  // namespace aether
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -119,6 +122,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_finalize_rope", &aether::qkv_finalize_rope, "acc"_a, "bias"_a, "qkv"_a, "pos"_a, "slot"_a, "cos_t"_a,
         "sin_t"_a, "k_cache"_a, "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
   m.def("finalize_residual_norm", &aether::finalize_residual_norm);
+  m.def("quantize_blocks", &aether::quantize_blocks, "bf16 -> GGUF Q8_0 (fmt 8) or Q4_0 (fmt 2) blocks");
+  m.def("dequantize_blocks", &aether::dequantize_blocks, "GGUF Q8_0 / Q4_0 blocks -> bf16");
   m.def("read_and_clear_status", &aether::read_and_clear_status,
         "Returns (and clears) the device status word set by kernels whose bounded waits expired");
 }
