@@ -67,9 +67,10 @@ class GPTConfig:
         return 6.0 * mm + 3.0 * attn
 
 
-def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool = True):
+def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool = True, tp_size: int = 1):
     """Parameter specs (name, shape, weight_decay). ``layers`` / ``first`` /
-    ``last`` select one pipeline stage's share of the model."""
+    ``last`` select one pipeline stage's share of the model, ``tp_size`` one
+    tensor-parallel rank's shard shapes."""
     d, f, v = cfg.d_model, cfg.d_ff, cfg.vocab
     qkv = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
     layers = range(cfg.n_layers) if layers is None else layers
@@ -87,6 +88,10 @@ def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool 
         specs.append(("final_norm", (d,), False))
         if not cfg.tie_embeddings:
             specs.append(("lm_head", (v, d), True))
+    if tp_size > 1:
+        from ..parallel.tp_train import shard_shape
+
+        specs = [(n, shard_shape(cfg, n, shp, tp_size), dec) for n, shp, dec in specs]
     return specs
 
 
@@ -96,12 +101,18 @@ class GPT:
     norm, LM head and loss, other stages map hidden states to hidden states."""
 
     def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1, alloc=None,
-                 layers=None, first: bool = True, last: bool = True):
+                 layers=None, first: bool = True, last: bool = True, tp=None):
+        """tp: a ``parallel.tp_train.TPGroup`` -- this rank then holds its
+        Megatron shard of every layer (and the same values as the matching
+        slice of the unsharded model with the same seed)."""
         self.cfg = cfg
+        self.tp = tp if tp is not None and tp.world > 1 else None
+        tp_size = self.tp.world if self.tp else 1
+        assert cfg.n_heads % tp_size == 0 and cfg.n_kv_heads % tp_size == 0 and cfg.d_ff % tp_size == 0
         self.device = torch.device(device)
         self.layers = list(range(cfg.n_layers) if layers is None else layers)
         self.first, self.last = first, last
-        self.arena = ParamArena(gpt_param_specs(cfg, self.layers, first, last), self.device,
+        self.arena = ParamArena(gpt_param_specs(cfg, self.layers, first, last, tp_size), self.device,
                                 pad_multiple=pad_multiple, alloc=alloc)
         self.init_weights(seed)
         cos, sin = ref.rope_tables(cfg.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
@@ -112,7 +123,9 @@ class GPT:
         """N(0, init_std) weights, unit norms. Every tensor has its own CPU
         generator keyed by its index in the full model, so any pipeline split
         (and any device) produces the same values as the unsplit model."""
-        index = {name: i for i, (name, _, _) in enumerate(gpt_param_specs(self.cfg))}
+        full = gpt_param_specs(self.cfg)
+        index = {name: i for i, (name, _, _) in enumerate(full)}
+        full_shape = {name: shp for name, shp, _ in full}
         a = self.arena
         with torch.no_grad():
             for name, slot in a.slots.items():
@@ -121,14 +134,29 @@ class GPT:
                     mv.fill_(1.0)
                 else:
                     g = torch.Generator(device="cpu").manual_seed(seed * 1000003 + index[name])
-                    t = torch.empty(slot.shape, dtype=torch.float32)
+                    t = torch.empty(full_shape[name], dtype=torch.float32)
                     t.normal_(0.0, self.cfg.init_std, generator=g)
+                    if self.tp is not None:
+                        from ..parallel.tp_train import shard_tensor
+
+                        t = shard_tensor(self.cfg, name, t, self.tp.rank, self.tp.world)
                     mv.copy_(t.to(self.device))
         a.sync_bf16_from_master()
 
     def _linear(self, i: int, name: str, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
-        """The projection ``name`` of layer i (adapters replace this hook)."""
-        return A.linear(x, self.arena[f"l{i}.{name}"], residual=residual)
+        """The projection ``name`` of layer i (adapters replace this hook).
+        Under TP: column-parallel projections see the input through
+        ``tp_copy``; row-parallel ones all-reduce their partial sums, with the
+        residual added once (by TP rank 0's GEMM epilogue)."""
+        w = self.arena[f"l{i}.{name}"]
+        if self.tp is None:
+            return A.linear(x, w, residual=residual)
+        from ..parallel import tp_train as T
+
+        if name in T.COLUMN:
+            return A.linear(T.tp_copy(x, self.tp), w)
+        y = A.linear(x, w, residual=residual.detach() if (residual is not None and self.tp.rank == 0) else None)
+        return T.tp_reduce_residual(y, residual, self.tp)
 
     def freeze(self) -> None:
         """Stops gradients to every base parameter (adapter fine-tuning): the
@@ -152,7 +180,8 @@ class GPT:
         cfg, a = self.cfg, self.arena
         if ids is not None:
             B, S = ids.shape
-        Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        tpw = self.tp.world if self.tp else 1
+        Hq, Hkv, D = cfg.n_heads // tpw, cfg.n_kv_heads // tpw, cfg.head_dim
         scale = 1.0 / math.sqrt(D)
         pos = self.positions(B, S)
         if self.first:

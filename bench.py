@@ -116,6 +116,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
                     help="fused: one-kernel NVLink reduce + AdamW + broadcast; nccl: NCCL reduce-scatter/all-gather")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (TP x DP mesh, e.g. --gpus 8 --tp 4)")
+    ap.add_argument("--tp-comm", default="symm", choices=["symm", "nccl"],
+                    help="TP all-reduce: in-kernel symmetric-memory (NVLS / peer loads) or NCCL")
     return ap.parse_args()
 
 
@@ -143,22 +146,38 @@ def main():
 
     cfg = GPTConfig(n_layers=args.layers)
     S = args.seq
-    assert args.global_batch % world == 0
-    per_rank = args.global_batch // world
+    tp = args.tp
+    assert world % tp == 0, "--gpus must be a multiple of --tp"
+    dp_world = world // tp
+    assert args.global_batch % dp_world == 0
+    per_rank = args.global_batch // dp_world  # sequences per DP replica (shared by its TP ranks)
     dp = None
-    if world > 1 and args.dp == "fused":
+    mesh = None
+    dinfo = info
+    if tp > 1:
+        from aether_b200.parallel.tp_train import make_mesh
+
+        mesh = make_mesh(tp, use_symm=args.tp_comm == "symm")
+        dinfo = D.DistInfo(mesh.dp_rank, dp_world, info.local_rank, dev, info.backend)
+    if dp_world > 1 and args.dp == "fused":
         from aether_b200.parallel.dp import FusedDataParallel, team_alloc
         from aether_b200.parallel.symm import SymmTeam
 
-        team = SymmTeam(info, timeout_s=60.0)
-        model = GPT(cfg, device=dev, seed=1234, pad_multiple=world, alloc=team_alloc(team))
+        team = SymmTeam(info, group=mesh.dp_group if mesh else None, timeout_s=60.0)
+        model = GPT(cfg, device=dev, seed=1234, pad_multiple=dp_world, alloc=team_alloc(team),
+                    tp=mesh.tp if mesh else None)
         dp = FusedDataParallel(model.arena, team, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
     else:
-        model = GPT(cfg, device=dev, seed=1234, pad_multiple=world)
-    trainer = Trainer(model, info, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+        model = GPT(cfg, device=dev, seed=1234, pad_multiple=dp_world, tp=mesh.tp if mesh else None)
+        if mesh is not None:
+            from aether_b200.parallel.dp import DataParallel
+
+            dp = DataParallel(model.arena, dinfo, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                              group=mesh.dp_group)
+    trainer = Trainer(model, dinfo, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
                       micro_batch=args.micro_batch, dp=dp)
 
-    gen = torch.Generator().manual_seed(1000 + info.rank)
+    gen = torch.Generator().manual_seed(1000 + (mesh.dp_rank if mesh else info.rank))
     host = [torch.randint(0, cfg.vocab, (per_rank, S + 1), generator=gen, dtype=torch.int64).pin_memory()
             for _ in range(2)]
     dev_batch = host[0].to(dev)
@@ -246,8 +265,9 @@ def main():
                 "global_batch": args.global_batch,
                 "seq_len": S,
                 "micro_batch": args.micro_batch,
-                "parallelism": f"dp{world}" + ((" zero1 " + ("fused-nvlink" if dp is not None else "nccl"))
-                                               if world > 1 else ""),
+                "parallelism": (f"tp{tp}x" if tp > 1 else "") + f"dp{dp_world}"
+                + ((" zero1 " + ("fused-nvlink" if args.dp == "fused" else "nccl")) if dp_world > 1 else "")
+                + (f" tp-allreduce-{args.tp_comm}" if tp > 1 else ""),
                 "optimizer": "AdamW lr 3e-4 betas (0.9,0.95) wd 0.1, fp32 master",
                 "l2": "no flush needed: per-step working set (2.7 GB bf16 weights + activations) >> 126 MB L2",
             },

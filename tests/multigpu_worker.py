@@ -121,12 +121,40 @@ def check_pp(info):
     print(f"OK pp losses={[round(float(x), 4) for x in t]}", flush=True)
 
 
+def check_tp_train(info):
+    """Megatron TP over all ranks (in-kernel symmetric-memory all-reduce) against one GPU."""
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.parallel.tp_train import make_mesh, shard_tensor
+
+    w = info.world
+    cfg = GPTConfig(vocab=512, d_model=128 * w, n_layers=2, n_heads=w, n_kv_heads=w, d_ff=256 * w, max_seq=128)
+    mesh = make_mesh(w, use_symm=True)
+    m = GPT(cfg, device=info.device, seed=13, tp=mesh.tp)
+    ref = GPT(cfg, device=info.device, seed=13)
+    toks = torch.randint(0, 512, (2, 129), generator=torch.Generator().manual_seed(2))
+    ids, tg = toks[:, :-1].contiguous().to(info.device), toks[:, 1:].contiguous().to(info.device)
+    lt = m.loss(ids, tg)
+    lt.backward()
+    lr = ref.loss(ids, tg)
+    lr.backward()
+    assert abs(float(lt.detach()) - float(lr.detach())) < 1e-2 * abs(float(lr.detach()))
+    for n, s in m.arena.slots.items():
+        g = m.arena.grad[s.offset : s.offset + s.numel].view(s.shape)
+        rs = ref.arena.slots[n]
+        want = shard_tensor(cfg, n, ref.arena.grad[rs.offset : rs.offset + rs.numel].view(rs.shape), mesh.tp.rank, w)
+        err = float((g - want).norm() / want.norm().clamp(min=1e-12))
+        assert err < 5e-2, (n, err)
+    torch.cuda.synchronize()
+    assert _ext.check_status() == 0
+    print(f"OK tp_train loss={float(lt.detach()):.4f}", flush=True)
+
+
 def main():
     info = D.init(timeout_s=120)
     from aether_b200.parallel.symm import SymmTeam
 
     team = SymmTeam(info)
-    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp"]
+    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train"]
     if "allreduce" in which:
         check_allreduce(team, info)
     if "dp" in which:
@@ -135,6 +163,8 @@ def main():
         check_tp_qwen(info)
     if "pp" in which:
         check_pp(info)
+    if "tp_train" in which:
+        check_tp_train(info)
     torch.cuda.synchronize()
     dist.barrier()
     D.shutdown()
