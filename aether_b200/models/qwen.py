@@ -184,17 +184,22 @@ class QwenModel:
         cos, sin = ref.rope_tables(self.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
-        self.decode_splits = decode_splits or self._auto_splits()
+        self._fixed_splits = decode_splits
+        self.decode_splits = decode_splits or self._auto_splits(1)  # the most any batch size uses
         import os as _os
         self.fused_decode = _os.environ.get("AETHER_UNFUSED_DECODE", "0") != "1"
         self._graphs: dict[int, tuple] = {}
         self._alloc_decode_buffers()
 
     # ------------------------------------------------------------------ buffers
-    def _auto_splits(self) -> int:
+    def _auto_splits(self, B: int) -> int:
+        """Key splits of the decode attention for batch size B: enough
+        (sequence, KV head, split) CTAs for about two per SM, and no more --
+        fewer splits mean longer pipelined runs per CTA and a cheaper merge."""
+        if self._fixed_splits:
+            return self._fixed_splits
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.device.type == "cuda" else 148
-        # enough (sequence, kv-head, split) CTAs to cover the SMs at batch 1
-        return max(1, min(32, (2 * sms) // max(1, self.hkv)))
+        return max(1, min(32, -(-2 * sms // max(1, B * self.hkv))))
 
     def _alloc_decode_buffers(self):
         cfg, B, dev = self.cfg, self.max_batch, self.device
@@ -322,7 +327,7 @@ class QwenModel:
             F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i],
                                 self.hq, self.hkv, D, page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
-                               self.decode_splits, b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table)
+                               self._auto_splits(B), b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table)
             if self.tp is None:
                 F.skinny_gemm(o, w.wo[i], acc)
                 racc = acc
@@ -362,7 +367,7 @@ class QwenModel:
             F.rope_kv_append(qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D,
                              page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
-                               self.decode_splits, b["part_o"], b["part_lse"], page_table=self.page_table)
+                               self._auto_splits(B), b["part_o"], b["part_lse"], page_table=self.page_table)
             if self.tp is None:
                 F.skinny_gemm(o, w.wo[i], acc)
                 F.skinny_finalize(acc, x2, res=x)

@@ -10,7 +10,11 @@ once on its own:
     python -m aether_b200.profile_cases attn_bwd    # tcgen05 flash attention bwd, same shape
     python -m aether_b200.profile_cases skinny      # decode GEMM 1 x 3584 -> 37888 (Qwen-7B gate/up)
     python -m aether_b200.profile_cases decode_attn # split-K decode attention B8 Hq28 Hkv4 S8192
+    python -m aether_b200.profile_cases decode_attn_b1  # the same at batch 1, 2048 keys, 32 splits
     python -m aether_b200.profile_cases adamw       # fused AdamW over 64M fp32 params
+    python -m aether_b200.profile_cases decode7b    # eager Qwen2.5-7B-shape decode steps (batch 1, 2048 cached)
+                                                    # inside NVTX range "decode": for the launch list only
+                                                    # (ncu --nvtx --nvtx-include "decode/" --metrics gpu__time_duration.sum)
 """
 from __future__ import annotations
 
@@ -70,6 +74,21 @@ def decode_attn(reps):
         F.decode_attention(q, kc, vc, slot, seqlen, out, Hq, D ** -0.5, splits=8, counters=counters)
 
 
+def decode_attn_b1(reps):
+    """The decode attention of one Qwen2.5-7B-shape layer at batch 1 with 2048
+    cached keys and the serving path's 32 splits."""
+    Hq, Hkv, D, S = 28, 4, 128, 2048
+    kc = torch.randn(2, 4096, Hkv, D, device="cuda").bfloat16()
+    vc = torch.randn_like(kc)
+    q = torch.randn(1, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+    slot = torch.zeros(1, dtype=torch.int32, device="cuda")
+    seqlen = torch.full((1,), S, dtype=torch.int32, device="cuda")
+    out = torch.empty(1, Hq * D, dtype=torch.bfloat16, device="cuda")
+    counters = torch.zeros(Hkv, dtype=torch.int32, device="cuda")
+    for _ in range(reps):
+        F.decode_attention(q, kc, vc, slot, seqlen, out, Hq, D ** -0.5, splits=32, counters=counters)
+
+
 def adamw(reps):
     n = 64 * 1024 * 1024
     p, g = torch.randn(n, device="cuda"), torch.randn(n, device="cuda")
@@ -79,7 +98,24 @@ def adamw(reps):
         F.adamw_(p, g, m, v, pb, lr=1e-4, beta1=0.9, beta2=0.95, eps=1e-8, wd=0.1, step=i + 1)
 
 
-CASES = {f.__name__: f for f in (gemm, attn_fwd, attn_bwd, skinny, decode_attn, adamw)}
+def decode7b(reps):
+    from .models.qwen import QwenConfig, QwenModel
+
+    cfg = QwenConfig.qwen25_7b()
+    m = QwenModel(cfg, device="cuda", seed=1, max_batch=1, max_seq=4096)
+    prompt = torch.randint(0, cfg.vocab, (1, 2048), device="cuda")
+    tok = m.prefill(prompt)
+    pos = torch.full((1,), 2048, dtype=torch.int32, device="cuda")
+    slots = torch.zeros(1, dtype=torch.int32, device="cuda")
+    m.decode_step(tok, pos, slots, use_graph=False)
+    torch.cuda.synchronize()
+    for _ in range(reps):
+        torch.cuda.nvtx.range_push("decode")
+        tok = m.decode_step(tok, pos, slots, use_graph=False)
+        torch.cuda.nvtx.range_pop()
+
+
+CASES = {f.__name__: f for f in (gemm, attn_fwd, attn_bwd, skinny, decode_attn, decode_attn_b1, adamw, decode7b)}
 
 
 def main():

@@ -20,7 +20,8 @@
 //     B * Hkv <= AETHER_NOALLOC_MAX_COUNTERS (1024); larger problems are
 //     rejected with AETHER_NOALLOC_ETOOBIG before anything is launched.
 //     The scratch costs 8192 * 129 * 4 bytes + 4 KB, about 4.2 MB per GPU.
-//   * D must be 128, Hq a multiple of Hkv with Hq / Hkv <= 8, 1 <= splits <= 64.
+//   * D must be 128, Hq a multiple of Hkv with Hq / Hkv <= 8, 1 <= splits <= 64;
+//     out must be 8-byte aligned with out_rs a multiple of 4.
 //   * The first call on each device does one-time set-up for that device: it
 //     looks up the scratch address, raises the kernel's shared-memory limit and
 //     clears the counters (a synchronous memset). Make that first call before

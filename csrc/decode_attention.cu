@@ -28,7 +28,10 @@ namespace dec {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxGroup = 8;
 constexpr int kMaxSplits = 64;
-constexpr int kKvSmem = 2 * 128 * 256;  // staged K and V blocks
+constexpr int kKeysPerBlock = 64;                      // keys per pipeline stage
+constexpr int kStages = 3;
+constexpr int kStageBytes = 2 * kKeysPerBlock * 256;   // K and V rows of one block
+constexpr int kKvSmem = kStages * kStageBytes;         // 96 KB
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
   v[0] = bf16lo(u.x); v[1] = bf16hi(u.x); v[2] = bf16lo(u.y); v[3] = bf16hi(u.y);
@@ -131,134 +134,186 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool p
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0) : "memory");
 }
 
-// grid (splits, B * Hkv), 128 threads, D == 128. Each 128-key block of the
-// split is staged into shared memory with one burst of cp.async (K and V rows,
-// 16-byte chunks XOR-swizzled by row so the lane-per-key reads of K are
-// conflict-free), then: scores lane-per-key, online softmax per query head,
-// P.V with lanes over head dims.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+// c += a(16x16, rows 8..15 zero) * b(16x8)
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+// grid (splits, B * Hkv), 128 threads, D == 128.
+// A CTA owns one (sequence, KV head, split). The G <= 8 query heads of the KV
+// head's GQA group are the M rows of warp-level tensor-core MMAs (m16n8k16,
+// rows G..15 zero), so every K/V row is read once for the whole group:
+//   S = Q K^T over 64-key blocks (each warp takes 16 keys of the block),
+//   online softmax in registers, O += P V with P re-packed from the S
+//   accumulators straight into the A operand.
+// K/V blocks stream through a 3-stage cp.async ring (16-byte chunks
+// XOR-swizzled by row for conflict-free ldmatrix); the four warps' partial
+// (max, sum, O) are merged through shared memory at the end.
 __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
   constexpr int D = 128;
-  constexpr int KB = 128;  // keys per shared-memory block
   asm volatile("griddepcontrol.launch_dependents;");
   const int split = blockIdx.x;
   const int b = blockIdx.y / p.Hkv, hk = blockIdx.y % p.Hkv;
   const int G = p.Hq / p.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float sq[kMaxGroup][D];
-  __shared__ float sp[4][kMaxGroup][32];
-  __shared__ float sm_m[4][kMaxGroup], sm_l[4][kMaxGroup];
-  __shared__ float so[4][kMaxGroup][D];
-  extern __shared__ __align__(128) uint8_t kv_smem[];  // K block then V block, 128 rows x 256 B each
-  const uint32_t sK = smem_u32(kv_smem), sV = sK + KB * 256;
+  const int row = lane >> 2;        // query head of this thread's accumulator rows
+  const int quad = lane & 3;
+  extern __shared__ __align__(128) uint8_t kv_smem[];  // kStages x (K block, V block), 64 rows x 256 B each
+  const uint32_t sbase = smem_u32(kv_smem);
 
   const int len = p.seqlen[b];
-  const int per = ((len + p.splits - 1) / p.splits + KB - 1) / KB * KB;
+  const int per = ((len + p.splits - 1) / p.splits + kKeysPerBlock - 1) / kKeysPerBlock * kKeysPerBlock;
   const int k_begin = split * per;
   const int k_end = min(len, k_begin + per);
-
-  for (int i = threadIdx.x; i < G * D; i += 128) {
-    const int g = i / D, d = i % D;
-    sq[g][d] = __bfloat162float(p.q[(int64_t)b * p.q_rs + (int64_t)(hk * G + g) * D + d]) * p.scale_log2;
-  }
-
+  const int nb = k_end > k_begin ? (k_end - k_begin + kKeysPerBlock - 1) / kKeysPerBlock : 0;
   const int s = p.slot[b];
   const __nv_bfloat16* kbase = p.kc + (int64_t)hk * D;
   const __nv_bfloat16* vbase = p.vc + (int64_t)hk * D;
-  float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][4];
-#pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-    o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
-  }
-  for (int blk = k_begin; blk < k_end; blk += KB) {
-    const int nblk = min(KB, k_end - blk);
-    // stage K and V rows of this block (16 chunks of 16 B per row)
-    for (int i = threadIdx.x; i < KB * 16; i += 128) {
+
+  auto stage_load = [&](int blk_i, int st) {
+    const int blk = k_begin + blk_i * kKeysPerBlock;
+    const int nblk = min(kKeysPerBlock, k_end - blk);
+    const uint32_t sK = sbase + st * kStageBytes, sV = sK + kKeysPerBlock * 256;
+    for (int i = threadIdx.x; i < kKeysPerBlock * 16; i += 128) {
       const int r = i >> 4, c = i & 15;
       const bool ok = r < nblk;
-      const uint32_t off = (uint32_t)(r * 256 + ((c ^ (r & 15)) << 4));
       const int64_t ro = kv_offset(p.pm, s, ok ? blk + r : blk, p.slot_stride, p.pos_stride);
+      const uint32_t off = (uint32_t)(r * 256 + ((c ^ (r & 7)) << 4));
       cp_async16(sK + off, kbase + ro + c * 8, ok);
-      cp_async16(sV + (uint32_t)(r * 256 + (c << 4)), vbase + ro + c * 8, ok);
+      cp_async16(sV + off, vbase + ro + c * 8, ok);
     }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    const int r = warp * 32 + lane;  // this lane's key within the block
-    const bool valid = r < nblk;
-    float sc[kMaxGroup];
+  };
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) sc[g] = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < 16; ++c) {
-      float kv[8];
-      unpack8(*reinterpret_cast<const uint4*>(kv_smem + r * 256 + ((c ^ (r & 15)) << 4)), kv);
-#pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) {
-        if (g < G) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) sc[g] += sq[g][c * 8 + j] * kv[j];
-        }
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g < G) {
-        const float x = valid ? sc[g] : -INFINITY;
-        const float bm = warp_max(x);
-        const float mn = fmaxf(m[g], bm);
-        const float base = mn == -INFINITY ? 0.f : mn;
-        const float alpha = exp2f(m[g] - base);
-        const float pe = valid ? exp2f(x - base) : 0.f;
-        l[g] = l[g] * alpha + warp_sum(pe);
-        m[g] = mn;
-        o[g][0] *= alpha; o[g][1] *= alpha; o[g][2] *= alpha; o[g][3] *= alpha;
-        sp[warp][g][lane] = pe;
-      }
-    }
-    __syncwarp();
-    const int nkeys = min(32, nblk - warp * 32);
-    const uint8_t* vrow = kv_smem + KB * 256 + (warp * 32) * 256 + lane * 8;
-    for (int j = 0; j < nkeys; ++j) {
-      const uint2 vv = *reinterpret_cast<const uint2*>(vrow + j * 256);
-      const float v0 = bf16lo(vv.x), v1 = bf16hi(vv.x), v2 = bf16lo(vv.y), v3 = bf16hi(vv.y);
-#pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) {
-        if (g < G) {
-          const float pj = sp[warp][g][j];
-          o[g][0] += pj * v0; o[g][1] += pj * v1; o[g][2] += pj * v2; o[g][3] += pj * v3;
-        }
-      }
-    }
-    __syncthreads();  // the next block overwrites the staged K/V
+  for (int st = 0; st < kStages - 1; ++st) {
+    if (st < nb) stage_load(st, st);
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  // merge the 4 warps
+
+  // Q as A fragments (rows = heads of the group, pre-scaled into the log2 domain)
+  uint32_t qa[8][2];
+  {
+    const bool ok = row < G;
+    const __nv_bfloat16* qr = p.q + (int64_t)b * p.q_rs + (int64_t)(hk * G + (ok ? row : 0)) * D;
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    if (g < G) {
-      if (lane == 0) {
-        sm_m[warp][g] = m[g];
-        sm_l[warp][g] = l[g];
-      }
-      so[warp][g][lane * 4 + 0] = o[g][0];
-      so[warp][g][lane * 4 + 1] = o[g][1];
-      so[warp][g][lane * 4 + 2] = o[g][2];
-      so[warp][g][lane * 4 + 3] = o[g][3];
+    for (int kk = 0; kk < 8; ++kk) {
+      const int d0 = kk * 16 + quad * 2;
+      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(qr + d0));
+      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(qr + d0 + 8));
+      qa[kk][0] = ok ? pack_bf16(lo.x, lo.y) : 0u;
+      qa[kk][1] = ok ? pack_bf16(hi.x, hi.y) : 0u;
     }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  const int kw = warp * 16;  // this warp's keys within a block
+
+  for (int it = 0; it < nb; ++it) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 2) : "memory");
+    __syncthreads();  // block `it` landed everywhere; stage (it-1) % kStages is free again
+    if (it + kStages - 1 < nb) stage_load(it + kStages - 1, (it + kStages - 1) % kStages);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t sK = sbase + (it % kStages) * kStageBytes, sV = sK + kKeysPerBlock * 256;
+    const int blk = k_begin + it * kKeysPerBlock;
+
+    // S (16 x 16 keys) = Q K^T
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      const int mi = lane >> 3, r8 = lane & 7;
+      const int krow = kw + (mi >> 1) * 8 + r8;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int c = 2 * kk + (mi & 1);
+        uint32_t bq[4];
+        ldsm_x4(sK + (uint32_t)(krow * 256 + ((c ^ (krow & 7)) << 4)), bq);
+        mma16816(sc[0], qa[kk][0], qa[kk][1], bq[0], bq[1]);
+        mma16816(sc[1], qa[kk][0], qa[kk][1], bq[2], bq[3]);
+      }
+    }
+    // online softmax on this thread's row (keys kw + 8j + 2*quad + e)
+    float x[4];
+    float bm = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = blk + kw + 8 * j + 2 * quad + e;
+        const float v = key < k_end ? sc[j][e] * p.scale_log2 : -INFINITY;
+        x[j * 2 + e] = v;
+        bm = fmaxf(bm, v);
+      }
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+    const float mn = fmaxf(m_run, bm);
+    const float base = mn == -INFINITY ? 0.f : mn;
+    const float alpha = exp2f(m_run - base);
+    float pe[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pe[i] = exp2f(x[i] - base);
+    l_run = l_run * alpha + (pe[0] + pe[1] + pe[2] + pe[3]);
+    m_run = mn;
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      o[t][0] *= alpha;
+      o[t][1] *= alpha;
+    }
+    // O += P V (k = this warp's 16 keys)
+    const uint32_t pa0 = pack_bf16(pe[0], pe[1]), pa2 = pack_bf16(pe[2], pe[3]);
+    {
+      const int mi = lane >> 3, r8 = lane & 7;
+      const int vrow = kw + (mi & 1) * 8 + r8;
+#pragma unroll
+      for (int nn = 0; nn < 8; ++nn) {
+        const int c = 2 * nn + (mi >> 1);
+        uint32_t bv[4];
+        ldsm_x4_t(sV + (uint32_t)(vrow * 256 + ((c ^ (vrow & 7)) << 4)), bv);
+        mma16816(o[2 * nn], pa0, pa2, bv[0], bv[1]);
+        mma16816(o[2 * nn + 1], pa0, pa2, bv[2], bv[3]);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  __syncthreads();  // every warp is done with the ring; reuse it for the merge
+  // merge the 4 warps (rows >= G are padding)
+  float* sm_m = reinterpret_cast<float*>(kv_smem);        // [4][8]
+  float* sm_l = sm_m + 32;                                // [4][8]
+  float* so = sm_m + 64;                                  // [4][8][D]
+  if (quad == 0) {
+    sm_m[warp * 8 + row] = m_run;
+    sm_l[warp * 8 + row] = l_run;
+  }
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    so[(warp * 8 + row) * D + 8 * t + 2 * quad] = o[t][0];
+    so[(warp * 8 + row) * D + 8 * t + 2 * quad + 1] = o[t][1];
   }
   __syncthreads();
   for (int i = threadIdx.x; i < G * D; i += 128) {
     const int g = i / D, d = i % D;
     float mm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sm_m[w][g]);
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sm_m[w * 8 + g]);
     float ll = 0.f, acc = 0.f;
     if (mm != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
-        const float f = exp2f(sm_m[w][g] - mm);
-        ll += sm_l[w][g] * f;
-        acc += so[w][g][d] * f;
+        const float f = exp2f(sm_m[w * 8 + g] - mm);
+        ll += sm_l[w * 8 + g] * f;
+        acc += so[(w * 8 + g) * D + d] * f;
       }
     }
     const int hq = hk * G + g;
@@ -275,34 +330,57 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // Only the splits that own keys take part: split s covers [s * per, ...),
+  // so the first ceil(len / per) are non-empty.
+  const int n_act = per > 0 ? min(p.splits, (len + per - 1) / per) : 0;
   // Per-split merge weights for every head of the group, computed once.
   __shared__ float s_w[kMaxGroup][kMaxSplits];
-  for (int i = threadIdx.x; i < G * p.splits; i += 128) {
-    const int g = i / p.splits, s2 = i % p.splits;
+  for (int i = threadIdx.x; i < G * n_act; i += 128) {
+    const int g = i / n_act, s2 = i % n_act;
     s_w[g][s2] = __ldcg(p.part_lse + ((int64_t)b * p.Hq + hk * G + g) * p.splits + s2);
   }
   __syncthreads();
   if (threadIdx.x < G) {
     const int g = threadIdx.x;
     float mx = -INFINITY;
-    for (int s2 = 0; s2 < p.splits; ++s2) mx = fmaxf(mx, s_w[g][s2]);
+    for (int s2 = 0; s2 < n_act; ++s2) mx = fmaxf(mx, s_w[g][s2]);
     float tot = 0.f;
-    for (int s2 = 0; s2 < p.splits; ++s2) {
+    for (int s2 = 0; s2 < n_act; ++s2) {
       const float w = s_w[g][s2] == -INFINITY ? 0.f : exp2f(s_w[g][s2] - mx);
       s_w[g][s2] = w;
       tot += w;
     }
     const float inv = tot > 0.f ? 1.f / tot : 0.f;
-    for (int s2 = 0; s2 < p.splits; ++s2) s_w[g][s2] *= inv;
+    for (int s2 = 0; s2 < n_act; ++s2) s_w[g][s2] *= inv;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += 128) {
-    const int g = i / D, d = i % D;
+  // out = sum_s w_s * part_o[s]: float4 loads, four splits in flight per step
+  constexpr int D4 = D / 4;
+  for (int i = threadIdx.x; i < G * D4; i += 128) {
+    const int g = i / D4, d4 = i % D4;
     const int hq = hk * G + g;
-    const float* po = p.part_o + (((int64_t)b * p.Hq + hq) * p.splits) * D + d;
-    float acc = 0.f;
-    for (int s2 = 0; s2 < p.splits; ++s2) acc += s_w[g][s2] * __ldcg(po + (int64_t)s2 * D);
-    p.out[(int64_t)b * p.out_rs + (int64_t)hq * D + d] = __float2bfloat16(acc);
+    const float4* po = reinterpret_cast<const float4*>(p.part_o + (((int64_t)b * p.Hq + hq) * p.splits) * D) + d4;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int s2 = 0;
+    for (; s2 + 4 <= n_act; s2 += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(po + (int64_t)(s2 + u) * D4);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = s_w[g][s2 + u];
+        a0 += w * v[u].x; a1 += w * v[u].y; a2 += w * v[u].z; a3 += w * v[u].w;
+      }
+    }
+    for (; s2 < n_act; ++s2) {
+      const float4 v = __ldcg(po + (int64_t)s2 * D4);
+      const float w = s_w[g][s2];
+      a0 += w * v.x; a1 += w * v.y; a2 += w * v.z; a3 += w * v.w;
+    }
+    uint2 packed;
+    packed.x = pack_bf16(a0, a1);
+    packed.y = pack_bf16(a2, a3);
+    *reinterpret_cast<uint2*>(p.out + (int64_t)b * p.out_rs + (int64_t)hq * D + d4 * 4) = packed;
   }
   if (threadIdx.x == 0) p.counters[blockIdx.y] = 0;  // ready for the next step (graph replay)
 }
@@ -488,6 +566,8 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
   TORCH_CHECK(D == 128, "decode_attention: head_dim 128");
   TORCH_CHECK(Hq % Hkv == 0 && Hq / Hkv <= dec::kMaxGroup, "decode_attention: GQA group must be <= 8");
   TORCH_CHECK(q.stride(1) == 1 && out.stride(1) == 1, "decode_attention: rows");
+  TORCH_CHECK(out.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 8 == 0,
+              "decode_attention: out rows must start on 8-byte boundaries");
   TORCH_CHECK(part_o.numel() >= B * Hq * splits * D && part_lse.numel() >= B * Hq * splits, "decode_attention: scratch");
   c10::cuda::CUDAGuard g(q.device());
   if (B == 0) return;
@@ -631,6 +711,7 @@ extern "C" __attribute__((visibility("default"))) int aether_decode_attention_no
     float scale, void* stream) {
   using namespace aether;
   if (!q || !k_cache || !v_cache || !slot || !seqlen || !out) return AETHER_NOALLOC_EINVAL;
+  if (out_rs % 4 != 0 || reinterpret_cast<uintptr_t>(out) % 8 != 0) return AETHER_NOALLOC_EINVAL;
   if (B < 0 || D != 128 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0 || Hq / Hkv > dec::kMaxGroup || splits < 1 ||
       splits > dec::kMaxSplits)
     return AETHER_NOALLOC_EINVAL;

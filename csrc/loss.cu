@@ -134,28 +134,58 @@ __global__ void __launch_bounds__(kCeThreads) cross_entropy_kernel(const __nv_bf
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 
-// Row argmax over the first V columns of a bf16 or fp32 matrix.
+// Row argmax over the first V columns of a bf16 or fp32 matrix. One CTA per
+// row; each thread keeps 4 independent 16-byte loads in flight (64 bytes per
+// trip) so a single row of a 152K vocabulary is read at many bytes per clock
+// instead of one dependent load chain per thread. Ties go to the lowest index.
+__device__ __forceinline__ void argmax_take(float v, int c, float& best, int& idx) {
+  if (v > best || (v == best && c < idx)) {
+    best = v;
+    idx = c;
+  }
+}
+__device__ __forceinline__ void argmax_vec(const uint4& u, int c0, const float*, float& best, int& idx) {
+  const float f[4] = {__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w)};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) argmax_take(f[j], c0 + j, best, idx);
+}
+__device__ __forceinline__ void argmax_vec(const uint4& u, int c0, const __nv_bfloat16*, float& best, int& idx) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    argmax_take(__uint_as_float(w[j] << 16), c0 + 2 * j, best, idx);
+    argmax_take(__uint_as_float(w[j] & 0xffff0000u), c0 + 2 * j + 1, best, idx);
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, int64_t ld, int V,
-                                                      int64_t* __restrict__ out) {
+                                                      int64_t* __restrict__ out, bool vec) {
   const T* row = x + (int64_t)blockIdx.x * ld;
   float best = -INFINITY;
-  int idx = 0;
-  for (int c = threadIdx.x; c < V; c += blockDim.x) {
-    const float v = to_f(row[c]);
-    if (v > best) {
-      best = v;
-      idx = c;
+  int idx = 0x7fffffff;
+  constexpr int E = 16 / sizeof(T);  // elements per 16-byte load
+  constexpr int U = 4;               // loads in flight per thread
+  int done = 0;
+  if (vec) {
+    const int per_trip = 1024 * E * U;
+    const int full = V / per_trip * per_trip;
+    for (int base = 0; base < full; base += per_trip) {
+      uint4 u[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        u[k] = __ldg(reinterpret_cast<const uint4*>(row + base + (k * 1024 + threadIdx.x) * E));
+#pragma unroll
+      for (int k = 0; k < U; ++k) argmax_vec(u[k], base + (k * 1024 + threadIdx.x) * E, row, best, idx);
     }
+    done = full;
   }
+  for (int c = done + threadIdx.x; c < V; c += blockDim.x) argmax_take(to_f(row[c]), c, best, idx);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
     const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (b2 > best || (b2 == best && i2 < idx)) {
-      best = b2;
-      idx = i2;
-    }
+    argmax_take(b2, i2, best, idx);
   }
   __shared__ float sb[32];
   __shared__ int si[32];
@@ -173,12 +203,9 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, i
     for (int o = 16; o > 0; o >>= 1) {
       const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
       const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-      if (b2 > best || (b2 == best && i2 < idx)) {
-        best = b2;
-        idx = i2;
-      }
+      argmax_take(b2, i2, best, idx);
     }
-    if (lane == 0) out[blockIdx.x] = idx;
+    if (lane == 0) out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
   }
 }
 
@@ -216,12 +243,13 @@ void argmax_rows(at::Tensor x, at::Tensor out) {
   const unsigned rows = (unsigned)x.size(0);
   if (rows == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
+  const bool vec = reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && (x.stride(0) * x.element_size()) % 16 == 0;
   if (x.scalar_type() == at::kBFloat16)
     argmax_kernel<__nv_bfloat16><<<rows, 1024, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-                                                            x.stride(0), (int)x.size(1), out.data_ptr<int64_t>());
+                                                            x.stride(0), (int)x.size(1), out.data_ptr<int64_t>(), vec);
   else if (x.scalar_type() == at::kFloat)
     argmax_kernel<float><<<rows, 1024, 0, stream>>>(x.data_ptr<float>(), x.stride(0), (int)x.size(1),
-                                                    out.data_ptr<int64_t>());
+                                                    out.data_ptr<int64_t>(), vec);
   else
     TORCH_CHECK(false, "argmax: bf16 or fp32");
   AETHER_CUDA_CHECK(cudaGetLastError());

@@ -177,6 +177,13 @@ def test_cross_entropy(V):
 def test_argmax():
     x = bf(7, 151936)
     assert torch.equal(F.argmax(x), x.float().argmax(-1))
+    y = torch.randn(3, 152064, device=dev)  # fp32, vectorised path
+    assert torch.equal(F.argmax(y), y.argmax(-1))
+    z = torch.randn(3, 1003, device=dev)[:, :1001]  # odd stride: scalar path
+    assert torch.equal(F.argmax(z), z.argmax(-1))
+    t = torch.zeros(2, 70000, device=dev)
+    t[0, 5] = t[0, 60000] = 1.0  # ties go to the lowest index
+    assert F.argmax(t).tolist() == [5, 0]
 
 
 def test_adamw():
