@@ -274,14 +274,7 @@ class QwenModel:
                 self.tp.all_reduce_(y)
                 x = x + y
             h, _, _ = F.rmsnorm(x, w.mlp_norm[i], cfg.norm_eps)
-            gu = F.gemm(h, w.wgu[i])
-            act = F.swiglu(gu)
-            if self.tp is None:
-                x = F.gemm(act, w.wd[i], residual=x)
-            else:
-                y = F.gemm(act, w.wd[i])
-                self.tp.all_reduce_(y)
-                x = x + y
+            x = self._ffn(i, h, x)
         last = x.view(B, S, cfg.d_model)[:, -1].contiguous()
         hl, _, _ = F.rmsnorm(last, w.final_norm, cfg.norm_eps)
         head = self._prefill_head()
@@ -290,6 +283,16 @@ class QwenModel:
             logits = logits[:, : cfg.vocab].contiguous()
         nxt = F.argmax(logits)
         return (nxt, logits) if return_logits else nxt
+
+    def _ffn(self, i: int, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        """x + FFN(h) for token rows (prefill); subclasses swap the FFN."""
+        w = self.w
+        act = F.swiglu(F.gemm(h, w.wgu[i]))
+        if self.tp is None:
+            return F.gemm(act, w.wd[i], residual=x)
+        y = F.gemm(act, w.wd[i])
+        self.tp.all_reduce_(y)
+        return x + y
 
     def _prefill_head(self) -> torch.Tensor:
         """LM head for the tensor-core GEMM, whose N must be a multiple of 8:
@@ -375,20 +378,25 @@ class QwenModel:
                 racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)
                 F.skinny_finalize(racc, x2, res=x)
             F.rmsnorm_into(x2, w.mlp_norm[i], h, cfg.norm_eps)
-            F.skinny_gemm(h, w.wgu[i], acc)
-            F.skinny_finalize(acc, act, swiglu=True)
-            if self.tp is None:
-                F.skinny_gemm(act, w.wd[i], acc)
-                F.skinny_finalize(acc, x, res=x2)
-            else:
-                racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
-                F.skinny_finalize(racc, x, res=x2)
+            self._decode_ffn(i, h, x2, x, act, acc)
         F.rmsnorm_into(x, w.final_norm, h, cfg.norm_eps)
         F.skinny_gemm(h, w.lm_head, acc)
         if self._want_logits:
             b["logits"][:B].copy_(acc[:, : cfg.vocab])
         b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
         acc.zero_()
+
+    def _decode_ffn(self, i, h, x2, x, act, acc) -> None:
+        """x = x2 + FFN(h) on the decode rows (static buffers)."""
+        w = self.w
+        F.skinny_gemm(h, w.wgu[i], acc)
+        F.skinny_finalize(acc, act, swiglu=True)
+        if self.tp is None:
+            F.skinny_gemm(act, w.wd[i], acc)
+            F.skinny_finalize(acc, x, res=x2)
+        else:
+            racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
+            F.skinny_finalize(racc, x, res=x2)
 
     def _bucket(self, B: int) -> int:
         for s in (1, 2, 4, 8, 16, 32, 64):
@@ -490,8 +498,11 @@ class QwenModel:
             o, _ = ref.attention(q, k, v, self.scale, True)
             x = x + o.reshape(B, S, -1) @ w.wo[i].float().t()
             h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.mlp_norm[i].float()
-            gu = h @ w.wgu[i].float().t()
-            g, u = gu.chunk(2, -1)
-            x = x + (torch.nn.functional.silu(g) * u) @ w.wd[i].float().t()
+            x = x + self._reference_ffn(i, h)
         h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.final_norm.float()
         return h @ w.lm_head.float().t()
+
+    def _reference_ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:
+        w = self.w
+        g, u = (h @ w.wgu[i].float().t()).chunk(2, -1)
+        return (torch.nn.functional.silu(g) * u) @ w.wd[i].float().t()

@@ -506,3 +506,107 @@ def dequantize_blocks(q, shape, fmt=Q8_0, out=None):
         out.copy_(x)
         return out
     return x
+
+
+# ------------------------------------------------------------------ mixture of experts
+MOE_TILE = 128
+
+
+def moe_route(logits, k, softmax_all=True, renorm=False):
+    """fp32 router logits [T, E] -> (expert ids int32 [T, k], weights fp32 [T, k]).
+    softmax_all: softmax over all experts then top-k (renorm: weights / their sum);
+    otherwise softmax over the k selected logits."""
+    T, E = logits.shape
+    if _cuda(logits):
+        idx = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+        wt = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+        lg = logits if logits.dtype == torch.float32 and logits.stride(1) == 1 else logits.float().contiguous()
+        C().moe_route(lg, idx, wt, int(k), bool(softmax_all), bool(renorm))
+        return idx, wt
+    lf = logits.float()
+    if softmax_all:
+        pr = torch.softmax(lf, -1)
+        wt, idx = torch.topk(pr, k, dim=-1)
+        if renorm:
+            wt = wt / wt.sum(-1, keepdim=True)
+    else:
+        top, idx = torch.topk(lf, k, dim=-1)
+        wt = torch.softmax(top, -1)
+    return idx.to(torch.int32), wt
+
+
+def moe_rows(T, k, E):
+    """Rows of the permuted buffer: every expert segment padded to 128 rows."""
+    n = T * k + E * (MOE_TILE - 1)
+    return (n + MOE_TILE - 1) // MOE_TILE * MOE_TILE
+
+
+def moe_permute(idx, E):
+    """-> (row_of int32 [T*k], src_row int32 [Mpad], tile_group int32 [Mpad/128])."""
+    T, k = idx.shape
+    Mpad = moe_rows(T, k, E)
+    dev = idx.device
+    if _cuda(idx):
+        row_of = torch.empty(T * k, dtype=torch.int32, device=dev)
+        src_row = torch.empty(Mpad, dtype=torch.int32, device=dev)
+        tile_group = torch.empty(Mpad // MOE_TILE, dtype=torch.int32, device=dev)
+        C().moe_permute(idx.contiguous(), int(E), row_of, src_row, tile_group)
+        return row_of, src_row, tile_group
+    flat = idx.reshape(-1).long()
+    counts = torch.bincount(flat, minlength=E)
+    seg = (counts + MOE_TILE - 1) // MOE_TILE * MOE_TILE
+    off = torch.zeros(E + 1, dtype=torch.long)
+    off[1:] = torch.cumsum(seg, 0)
+    row_of = torch.empty(T * k, dtype=torch.int32)
+    src_row = torch.full((Mpad,), -1, dtype=torch.int32)
+    cur = off[:-1].clone()
+    for i, e in enumerate(flat.tolist()):
+        row_of[i] = int(cur[e])
+        src_row[int(cur[e])] = i // k
+        cur[e] += 1
+    tile_group = torch.full((Mpad // MOE_TILE,), -1, dtype=torch.int32)
+    for e in range(E):
+        tile_group[int(off[e]) // MOE_TILE : int(off[e + 1]) // MOE_TILE] = e
+    return row_of, src_row, tile_group
+
+
+def moe_gather(x, src_row):
+    Mpad = src_row.numel()
+    if _cuda(x):
+        X = torch.empty(Mpad, x.shape[1], dtype=x.dtype, device=x.device)
+        C().moe_gather(x, src_row, X)
+        return X
+    X = torch.zeros(Mpad, x.shape[1], dtype=x.dtype)
+    ok = src_row >= 0
+    X[ok] = x[src_row[ok].long()]
+    return X
+
+
+def gemm_grouped(X, w, tile_group):
+    """X [Mpad, K] bf16 (expert segments on 128-row boundaries), w [E, N, K] ->
+    [Mpad, N]; rows of unused tiles are left undefined."""
+    E, N, K = w.shape
+    if _cuda(X):
+        out = torch.empty(X.shape[0], N, dtype=torch.bfloat16, device=X.device)
+        C().gemm_grouped(X, w, out, tile_group)
+        return out
+    out = torch.zeros(X.shape[0], N, dtype=torch.bfloat16)
+    for t, e in enumerate(tile_group.tolist()):
+        if e >= 0:
+            rows = slice(t * MOE_TILE, (t + 1) * MOE_TILE)
+            out[rows] = (X[rows].float() @ w[e].float().t()).to(torch.bfloat16)
+    return out
+
+
+def moe_combine(Y, row_of, wt, res=None, extra=None):
+    """out[t] = sum_j wt[t, j] * Y[row_of[t, j]] (+ res) (+ extra), bf16 [T, d]."""
+    T, k = wt.shape
+    if _cuda(Y):
+        out = torch.empty(T, Y.shape[1], dtype=torch.bfloat16, device=Y.device)
+        C().moe_combine(Y, row_of, wt, int(k), res, extra, out)
+        return out
+    acc = (Y[row_of.long()].float().view(T, k, -1) * wt.unsqueeze(-1)).sum(1)
+    for a in (res, extra):
+        if a is not None:
+            acc = acc + a.float()
+    return acc.to(torch.bfloat16)

@@ -75,6 +75,13 @@ void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tenso
                        int64_t Hkv, int64_t D, std::optional<at::Tensor> page_table);
 void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
                             at::Tensor y, at::Tensor w, at::Tensor h, double eps);
+// gemm_sm100.cu (grouped) and moe.cu
+void gemm_grouped(at::Tensor a, at::Tensor w, at::Tensor out, at::Tensor tile_group);
+void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool softmax_all, bool renorm);
+void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_row, at::Tensor tile_group);
+void moe_gather(at::Tensor x, at::Tensor src_row, at::Tensor X);
+void moe_combine(at::Tensor Y, at::Tensor row_of, at::Tensor wt, int64_t k, std::optional<at::Tensor> res,
+                 std::optional<at::Tensor> extra, at::Tensor out);
 // quant.cu
 void quantize_blocks(at::Tensor x, at::Tensor out, int64_t fmt);
 void dequantize_blocks(at::Tensor in, at::Tensor y, int64_t fmt);
@@ -122,6 +129,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_finalize_rope", &aether::qkv_finalize_rope, "acc"_a, "bias"_a, "qkv"_a, "pos"_a, "slot"_a, "cos_t"_a,
         "sin_t"_a, "k_cache"_a, "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
   m.def("finalize_residual_norm", &aether::finalize_residual_norm);
+  m.def("gemm_grouped", &aether::gemm_grouped, "grouped (MoE) tcgen05 GEMM over 128-row expert tiles");
+  m.def("moe_route", &aether::moe_route);
+  m.def("moe_permute", &aether::moe_permute);
+  m.def("moe_gather", &aether::moe_gather);
+  m.def("moe_combine", &aether::moe_combine);
   m.def("quantize_blocks", &aether::quantize_blocks, "bf16 -> GGUF Q8_0 (fmt 8) or Q4_0 (fmt 2) blocks");
   m.def("dequantize_blocks", &aether::dequantize_blocks, "GGUF Q8_0 / Q4_0 blocks -> bf16");
   m.def("read_and_clear_status", &aether::read_and_clear_status,

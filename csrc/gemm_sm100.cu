@@ -54,7 +54,18 @@ struct Params {
   float alpha;
   const float* alpha_ptr;  // optional device scalar multiplied into alpha
   int* status;
+  // Grouped (mixture-of-experts) mode: M-tile tm multiplies A's rows by group
+  // tile_group[tm]'s B rows [g * N, (g + 1) * N) of a [groups * N, K] B; a
+  // negative entry marks an unused tile, which every role skips.
+  const int* tile_group;
 };
+
+// B row of the tile's first output column (-1: tile skipped).
+__device__ __forceinline__ int b_row(const Params& p, int tm, int tn) {
+  if (p.tile_group == nullptr) return tn * BN;
+  const int g = p.tile_group[tm];
+  return g < 0 ? -1 : g * p.N + tn * BN;
+}
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
   const int per_group = kGroupM * num_n;
@@ -125,6 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
         tile_coords(t, num_m, num_n, tm, tn);
+        const int brow = b_row(p, tm, tn);
+        if (brow < 0) continue;
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_word)) {
             ok = false;
@@ -140,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], tm * BM + j * 64, kb * BK);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, tn * BN);
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, brow);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], tn * BN + j * 64, kb * BK);
@@ -174,6 +187,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (p.tile_group != nullptr) {
+          int tm, tn;
+          tile_coords(t, num_m, num_n, tm, tn);
+          if (b_row(p, tm, tn) < 0) continue;
+        }
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_word)) {
           ok = false;
           break;
@@ -225,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, num_m, num_n, tm, tn);
+      if (b_row(p, tm, tn) < 0) continue;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_word)) {
         *abort_word = 1;
         if (lane == 0) atomicExch(p.status, kStatusTimeoutEpilogue);
@@ -427,6 +446,43 @@ void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn,
   AETHER_GEMM_CASE(true, false, gemm::OUT_F32_ACCUM)
 #undef AETHER_GEMM_CASE
   TORCH_CHECK(false, "gemm_bf16: unsupported configuration");
+}
+
+// Grouped GEMM for mixture-of-experts layers: out[Mpad, N] = a[Mpad, K] .
+// w[g]^T with g = tile_group[m / 128] for every 128-row tile of a (rows of
+// one expert are contiguous and start on a 128-row boundary; -1 skips the
+// tile). w: [groups, N, K] (or [groups * N, K]) bf16, K-major.
+void gemm_grouped(at::Tensor a, at::Tensor w, at::Tensor out, at::Tensor tile_group) {
+  TORCH_CHECK(a.is_cuda() && w.is_cuda() && out.is_cuda() && tile_group.is_cuda(), "gemm_grouped: CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16,
+              "gemm_grouped: bf16 operands and output");
+  TORCH_CHECK(tile_group.scalar_type() == at::kInt && tile_group.is_contiguous(), "gemm_grouped: int32 tile_group");
+  TORCH_CHECK(a.dim() == 2 && a.stride(1) == 1 && w.is_contiguous() && out.dim() == 2 && out.stride(1) == 1,
+              "gemm_grouped: layouts");
+  const int64_t M = a.size(0), K = a.size(1);
+  const int64_t N = out.size(1);
+  const int64_t rows_w = w.numel() / K;
+  TORCH_CHECK(w.size(-1) == K && rows_w % N == 0, "gemm_grouped: w must be [groups, N, K]");
+  TORCH_CHECK(out.size(0) == M && M % gemm::BM == 0 && tile_group.numel() >= M / gemm::BM,
+              "gemm_grouped: M must be a multiple of 128 with one tile_group entry per 128 rows");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && (a.stride(0) * 2) % 16 == 0 && out.stride(0) % 8 == 0,
+              "gemm_grouped: dims / strides must be multiples of 8 elements");
+  c10::cuda::CUDAGuard guard(a.device());
+  gemm::Params p{};
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.alpha = 1.f;
+  p.status = device_status_word();
+  p.tile_group = tile_group.data_ptr<int>();
+  CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), K, M, a.stride(0) * 2, gemm::BK, gemm::BM);
+  CUtensorMap tb = make_tmap_2d_bf16(w.data_ptr(), K, rows_w, K * 2, gemm::BK, gemm::BN);
+  CUtensorMap tc = make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, out.stride(0) * 2, 64, 32,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  gemm::launch<false, false, gemm::OUT_BF16>(ta, tb, tc, p, at::cuda::getCurrentCUDAStream());
 }
 
 }  // namespace aether
