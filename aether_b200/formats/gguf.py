@@ -253,16 +253,21 @@ def qwen_config_from_gguf(g: GGUFFile):
     arch = g.meta.get("general.architecture", "qwen2")
     m = lambda k, d=None: g.meta.get(f"{arch}.{k}", d)  # noqa: E731
     vocab = len(g.meta.get("tokenizer.ggml.tokens", [])) or int(g.tensors["token_embd.weight"][0][1])
-    return QwenConfig(vocab=vocab, d_model=int(m("embedding_length")), n_layers=int(m("block_count")),
-                      n_heads=int(m("attention.head_count")), n_kv_heads=int(m("attention.head_count_kv")),
+    d, H = int(m("embedding_length")), int(m("attention.head_count"))
+    head_dim = int(m("attention.key_length", d // H))
+    return QwenConfig(vocab=vocab, d_model=d, n_layers=int(m("block_count")), n_heads=H,
+                      n_kv_heads=int(m("attention.head_count_kv", H)),
                       d_ff=int(m("feed_forward_length")), rope_theta=float(m("rope.freq_base", 1e6)),
                       norm_eps=float(m("attention.layer_norm_rms_epsilon", 1e-6)),
                       tie_embeddings="output.weight" not in g.tensors,
-                      qkv_bias="blk.0.attn_q.bias" in g.tensors)
+                      qkv_bias="blk.0.attn_q.bias" in g.tensors,
+                      qk_norm="blk.0.attn_q_norm.weight" in g.tensors,
+                      head_dim_=head_dim if head_dim != d // H else 0)
 
 
 def load_qwen_weights(path: str, device="cuda"):
-    """GGUF (llama.cpp tensor names) -> QwenWeights on `device` (bf16)."""
+    """GGUF (llama.cpp tensor names; architectures qwen2, qwen3, llama, mistral)
+    -> QwenWeights on `device` (bf16)."""
     from ..models.qwen import QwenWeights
 
     g = GGUFFile(path)
@@ -275,8 +280,13 @@ def load_qwen_weights(path: str, device="cuda"):
     w.lm_head = w.embed if cfg.tie_embeddings else t("output.weight")
     w.final_norm = t("output_norm.weight")
     w.attn_norm, w.mlp_norm, w.wqkv, w.bqkv, w.wo, w.wgu, w.wd = [], [], [], [], [], [], []
+    w.q_norm = [] if cfg.qk_norm else None
+    w.k_norm = [] if cfg.qk_norm else None
     for i in range(cfg.n_layers):
         p = f"blk.{i}."
+        if cfg.qk_norm:
+            w.q_norm.append(t(p + "attn_q_norm.weight"))
+            w.k_norm.append(t(p + "attn_k_norm.weight"))
         w.attn_norm.append(t(p + "attn_norm.weight"))
         w.mlp_norm.append(t(p + "ffn_norm.weight"))
         w.wqkv.append(torch.cat([t(p + "attn_q.weight"), t(p + "attn_k.weight"), t(p + "attn_v.weight")]).contiguous())

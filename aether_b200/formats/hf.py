@@ -20,13 +20,15 @@ from . import safetensors as st
 def qwen_config_from_hf(cfg_json: dict):
     from ..models.qwen import QwenConfig
 
-    return QwenConfig(vocab=cfg_json["vocab_size"], d_model=cfg_json["hidden_size"],
-                      n_layers=cfg_json["num_hidden_layers"], n_heads=cfg_json["num_attention_heads"],
-                      n_kv_heads=cfg_json.get("num_key_value_heads", cfg_json["num_attention_heads"]),
-                      d_ff=cfg_json["intermediate_size"], rope_theta=float(cfg_json.get("rope_theta", 1e6)),
+    d, H = cfg_json["hidden_size"], cfg_json["num_attention_heads"]
+    hd = int(cfg_json.get("head_dim") or d // H)
+    return QwenConfig(vocab=cfg_json["vocab_size"], d_model=d, n_layers=cfg_json["num_hidden_layers"], n_heads=H,
+                      n_kv_heads=cfg_json.get("num_key_value_heads", H), d_ff=cfg_json["intermediate_size"],
+                      rope_theta=float(cfg_json.get("rope_theta", 1e6)),
                       norm_eps=float(cfg_json.get("rms_norm_eps", 1e-6)),
                       tie_embeddings=bool(cfg_json.get("tie_word_embeddings", False)),
-                      qkv_bias=True, max_seq=int(cfg_json.get("max_position_embeddings", 4096)))
+                      qkv_bias=True, max_seq=int(cfg_json.get("max_position_embeddings", 4096)),
+                      head_dim_=hd if hd != d // H else 0)
 
 
 def _all_tensors(path: str) -> dict:
@@ -47,6 +49,7 @@ def load_qwen_hf(path: str, device="cuda"):
     cfg = qwen_config_from_hf(json.load(open(os.path.join(path, "config.json"))))
     t = _all_tensors(path)
     cfg.qkv_bias = "model.layers.0.self_attn.q_proj.bias" in t
+    cfg.qk_norm = "model.layers.0.self_attn.q_norm.weight" in t
     g = lambda n: t[n].to(device=device, dtype=torch.bfloat16).contiguous()  # noqa: E731
     w = QwenWeights.__new__(QwenWeights)
     w.cfg, w.device, w.tp_rank, w.tp_size = cfg, torch.device(device), 0, 1
@@ -55,9 +58,14 @@ def load_qwen_hf(path: str, device="cuda"):
     w.lm_head = w.embed if cfg.tie_embeddings or "lm_head.weight" not in t else g("lm_head.weight")
     w.final_norm = g("model.norm.weight")
     w.attn_norm, w.mlp_norm, w.wqkv, w.bqkv, w.wo, w.wgu, w.wd = [], [], [], [], [], [], []
+    w.q_norm = [] if cfg.qk_norm else None
+    w.k_norm = [] if cfg.qk_norm else None
     for i in range(cfg.n_layers):
         p = f"model.layers.{i}."
         a = p + "self_attn."
+        if cfg.qk_norm:
+            w.q_norm.append(g(a + "q_norm.weight"))
+            w.k_norm.append(g(a + "k_norm.weight"))
         w.attn_norm.append(g(p + "input_layernorm.weight"))
         w.mlp_norm.append(g(p + "post_attention_layernorm.weight"))
         w.wqkv.append(torch.cat([g(a + "q_proj.weight"), g(a + "k_proj.weight"), g(a + "v_proj.weight")]).contiguous())
@@ -89,9 +97,12 @@ def save_qwen_hf(cfg, w, path: str) -> None:
         t[a + "o_proj.weight"] = w.wo[i]
         t[p + "mlp.gate_proj.weight"], t[p + "mlp.up_proj.weight"] = w.wgu[i].split([cfg.d_ff, cfg.d_ff])
         t[p + "mlp.down_proj.weight"] = w.wd[i]
+        if cfg.qk_norm:
+            t[a + "q_norm.weight"], t[a + "k_norm.weight"] = w.q_norm[i], w.k_norm[i]
     st.save_file(t, os.path.join(path, "model.safetensors"), metadata={"format": "pt"})
     json.dump({"vocab_size": cfg.vocab, "hidden_size": cfg.d_model, "num_hidden_layers": cfg.n_layers,
                "num_attention_heads": cfg.n_heads, "num_key_value_heads": cfg.n_kv_heads,
                "intermediate_size": cfg.d_ff, "rope_theta": cfg.rope_theta, "rms_norm_eps": cfg.norm_eps,
                "tie_word_embeddings": cfg.tie_embeddings, "max_position_embeddings": cfg.max_seq,
+               "head_dim": cfg.head_dim,
                "architectures": ["Qwen2ForCausalLM"]}, open(os.path.join(path, "config.json"), "w"))

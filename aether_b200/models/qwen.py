@@ -44,10 +44,12 @@ class QwenConfig:
     qkv_bias: bool = True
     max_seq: int = 4096
     init_std: float = 0.02
+    qk_norm: bool = False  # Qwen3: per-head RMSNorm of q and k before RoPE
+    head_dim_: int = 0     # 0: d_model / n_heads
 
     @property
     def head_dim(self) -> int:
-        return self.d_model // self.n_heads
+        return self.head_dim_ or self.d_model // self.n_heads
 
     @staticmethod
     def qwen25_1_5b(**kw) -> "QwenConfig":
@@ -57,6 +59,27 @@ class QwenConfig:
     def qwen25_7b(**kw) -> "QwenConfig":
         base = dict(vocab=152064, d_model=3584, n_layers=28, n_heads=28, n_kv_heads=4, d_ff=18944,
                     tie_embeddings=False)
+        base.update(kw)
+        return QwenConfig(**base)
+
+    @staticmethod
+    def qwen3_8b(**kw) -> "QwenConfig":
+        base = dict(vocab=151936, d_model=4096, n_layers=36, n_heads=32, n_kv_heads=8, d_ff=12288, qkv_bias=False,
+                    qk_norm=True, tie_embeddings=False)
+        base.update(kw)
+        return QwenConfig(**base)
+
+    @staticmethod
+    def llama3_8b(**kw) -> "QwenConfig":
+        base = dict(vocab=128256, d_model=4096, n_layers=32, n_heads=32, n_kv_heads=8, d_ff=14336, qkv_bias=False,
+                    tie_embeddings=False, rope_theta=500000.0, norm_eps=1e-5)
+        base.update(kw)
+        return QwenConfig(**base)
+
+    @staticmethod
+    def mistral_7b(**kw) -> "QwenConfig":
+        base = dict(vocab=32000, d_model=4096, n_layers=32, n_heads=32, n_kv_heads=8, d_ff=14336, qkv_bias=False,
+                    tie_embeddings=False, rope_theta=1e6, norm_eps=1e-5)
         base.update(kw)
         return QwenConfig(**base)
 
@@ -108,6 +131,8 @@ class QwenWeights:
         self.lm_head = self.embed if cfg.tie_embeddings else rnd(cfg.vocab, d)
         self.final_norm = torch.ones(d, dtype=torch.bfloat16, device=self.device)
         self.attn_norm = [torch.ones(d, dtype=torch.bfloat16, device=self.device) for _ in range(L)]
+        self.q_norm = [torch.ones(D, dtype=torch.bfloat16, device=self.device) for _ in range(L)] if cfg.qk_norm else None
+        self.k_norm = [torch.ones(D, dtype=torch.bfloat16, device=self.device) for _ in range(L)] if cfg.qk_norm else None
         self.mlp_norm = [torch.ones(d, dtype=torch.bfloat16, device=self.device) for _ in range(L)]
         self.wqkv, self.bqkv, self.wo, self.wgu, self.wd = [], [], [], [], []
         for _ in range(L):
@@ -187,7 +212,8 @@ class QwenModel:
         self._fixed_splits = decode_splits
         self.decode_splits = decode_splits or self._auto_splits(1)  # the most any batch size uses
         import os as _os
-        self.fused_decode = _os.environ.get("AETHER_UNFUSED_DECODE", "0") != "1"
+        # the fused decode epilogue has no slot for Qwen3's q/k norm
+        self.fused_decode = _os.environ.get("AETHER_UNFUSED_DECODE", "0") != "1" and not cfg.qk_norm
         self._graphs: dict[int, tuple] = {}
         self._alloc_decode_buffers()
 
@@ -248,6 +274,7 @@ class QwenModel:
         for i in range(cfg.n_layers):
             h, _, _ = F.rmsnorm(x, w.attn_norm[i], cfg.norm_eps)
             qkv = F.gemm(h, w.wqkv[i], bias=w.bqkv[i])
+            self._qk_norm(i, qkv)
             F.rope_kv_append(qkv, pos, slot_t, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq,
                              self.hkv, D, page_table=self.page_table)
             q = qkv.view(B, S, row)[:, :, : self.hq * D].view(B, S, self.hq, D)
@@ -283,6 +310,12 @@ class QwenModel:
             logits = logits[:, : cfg.vocab].contiguous()
         nxt = F.argmax(logits)
         return (nxt, logits) if return_logits else nxt
+
+    def _qk_norm(self, i: int, qkv: torch.Tensor) -> None:
+        if self.cfg.qk_norm:
+            D, eps = self.cfg.head_dim, self.cfg.norm_eps
+            F.head_rmsnorm_(qkv, 0, self.hq, D, self.w.q_norm[i], eps)
+            F.head_rmsnorm_(qkv, self.hq, self.hkv, D, self.w.k_norm[i], eps)
 
     def _ffn(self, i: int, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         """x + FFN(h) for token rows (prefill); subclasses swap the FFN."""
@@ -367,6 +400,7 @@ class QwenModel:
             F.rmsnorm_into(x, w.attn_norm[i], h, cfg.norm_eps)
             F.skinny_gemm(h, w.wqkv[i], acc)
             F.skinny_finalize(acc, qkv, bias=w.bqkv[i])
+            self._qk_norm(i, qkv)
             F.rope_kv_append(qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D,
                              page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
@@ -489,6 +523,12 @@ class QwenModel:
             qkv = h @ w.wqkv[i].float().t()
             if w.bqkv[i] is not None:
                 qkv = qkv + w.bqkv[i].float()
+            if cfg.qk_norm:
+                qkv = qkv.clone()
+                for (h0, nh, wn) in ((0, self.hq, w.q_norm[i]), (self.hq, self.hkv, w.k_norm[i])):
+                    v = qkv[..., h0 * D : (h0 + nh) * D].reshape(B, S, nh, D)
+                    v = v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * wn.float()
+                    qkv[..., h0 * D : (h0 + nh) * D] = v.reshape(B, S, nh * D)
             qkv2 = qkv.reshape(B * S, -1)
             qkv2 = ref.rope(qkv2, pos.repeat(B), self.cos, self.sin, self.hq + self.hkv, D)
             qkv = qkv2.view(B, S, -1)

@@ -610,3 +610,14 @@ def moe_combine(Y, row_of, wt, res=None, extra=None):
         if a is not None:
             acc = acc + a.float()
     return acc.to(torch.bfloat16)
+
+
+def head_rmsnorm_(x, h0, nh, D, w, eps=1e-6):
+    """In place: RMSNorm (weight [D]) of heads [h0, h0+nh) of every row of x [T, row]."""
+    if _cuda(x):
+        C().head_rmsnorm(x, int(h0), int(nh), int(D), w, float(eps))
+        return x
+    v = x[:, h0 * D : (h0 + nh) * D].float().view(x.shape[0], nh, D)
+    v = v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    x[:, h0 * D : (h0 + nh) * D] = v.reshape(x.shape[0], -1).to(x.dtype)
+    return x

@@ -197,7 +197,8 @@ def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--model", default="1.5b", choices=["1.5b", "7b", "tiny"])
+    ap.add_argument("--model", default="1.5b",
+                    choices=["1.5b", "7b", "qwen3-8b", "llama3-8b", "mistral-7b", "qwen2-moe", "mixtral", "tiny"])
     ap.add_argument("--tokenizer", default=None, help="tokenizer.json (default: byte tokenizer)")
     ap.add_argument("--max-concurrent", type=int, default=8)
     ap.add_argument("--max-seq", type=int, default=4096)
@@ -216,12 +217,15 @@ def main():
     from .engine import Engine
     from .tokenizer import BPETokenizer, ByteTokenizer
 
-    if args.model == "7b":
-        cfg = QwenConfig.qwen25_7b()
-    elif args.model == "tiny":
+    from ..models.moe import MoEConfig, MoEQwenModel
+
+    presets = {"7b": QwenConfig.qwen25_7b, "qwen3-8b": QwenConfig.qwen3_8b, "llama3-8b": QwenConfig.llama3_8b,
+               "mistral-7b": QwenConfig.mistral_7b, "qwen2-moe": MoEConfig.qwen2_moe_a2_7b,
+               "mixtral": MoEConfig.mixtral_8x7b, "1.5b": QwenConfig.qwen25_1_5b}
+    if args.model == "tiny":
         cfg = QwenConfig(vocab=1024, d_model=256, n_layers=2, n_heads=2, n_kv_heads=1, d_ff=512, max_seq=args.max_seq)
     else:
-        cfg = QwenConfig.qwen25_1_5b()
+        cfg = presets[args.model]()
     tok = BPETokenizer.from_file(args.tokenizer) if args.tokenizer else ByteTokenizer()
     weights = None
     if args.gguf:
@@ -238,7 +242,11 @@ def main():
         cfg, weights = hf.load_qwen_hf(args.hf, device=args.device)
         if not args.tokenizer and os.path.exists(os.path.join(args.hf, "tokenizer.json")):
             tok = BPETokenizer.from_file(os.path.join(args.hf, "tokenizer.json"))
-    model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq, weights=weights)
+    if isinstance(cfg, MoEConfig):
+        model = MoEQwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq)
+    else:
+        model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq,
+                          weights=weights)
     engine = Engine(model, tok, max_concurrent=args.max_concurrent, use_graph=args.device != "cpu")
     embedder = vision = None
     if args.embeddings:

@@ -82,6 +82,7 @@ void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_ro
 void moe_gather(at::Tensor x, at::Tensor src_row, at::Tensor X);
 void moe_combine(at::Tensor Y, at::Tensor row_of, at::Tensor wt, int64_t k, std::optional<at::Tensor> res,
                  std::optional<at::Tensor> extra, at::Tensor out);
+void head_rmsnorm(at::Tensor x, int64_t h0, int64_t nh, int64_t D, at::Tensor w, double eps);
 // quant.cu
 void quantize_blocks(at::Tensor x, at::Tensor out, int64_t fmt);
 void dequantize_blocks(at::Tensor in, at::Tensor y, int64_t fmt);
@@ -134,6 +135,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &aether::moe_permute);
   m.def("moe_gather", &aether::moe_gather);
   m.def("moe_combine", &aether::moe_combine);
+  m.def("head_rmsnorm", &aether::head_rmsnorm, "in-place per-head RMSNorm (Qwen3 q/k norm)");
   m.def("quantize_blocks", &aether::quantize_blocks, "bf16 -> GGUF Q8_0 (fmt 8) or Q4_0 (fmt 2) blocks");
   m.def("dequantize_blocks", &aether::dequantize_blocks, "GGUF Q8_0 / Q4_0 blocks -> bf16");
   m.def("read_and_clear_status", &aether::read_and_clear_status,

@@ -547,4 +547,45 @@ void softmax_bwd(at::Tensor y, at::Tensor dy, at::Tensor dx, double scale) {
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
+
+namespace {
+// In-place RMSNorm of heads [h0, h0 + nh) of every row of x [T, ld] (head h at
+// h * D), with a weight [D] shared by all heads (Qwen3 q/k norm). One warp per
+// (row, head); D a multiple of 64 up to 256.
+__global__ void head_rmsnorm_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int T, int h0, int nh, int D,
+                                    const __nv_bfloat16* __restrict__ w, float eps) {
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (int64_t)T * nh) return;
+  const int t = (int)(wid / nh), h = h0 + (int)(wid % nh);
+  __nv_bfloat16* row = x + (int64_t)t * ld + (int64_t)h * D;
+  const int per = D / 32;  // 2, 4 or 8 elements per lane
+  float v[8];
+  float ss = 0.f;
+  for (int j = 0; j < per; ++j) {
+    v[j] = __bfloat162float(row[lane * per + j]);
+    ss += v[j] * v[j];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / D + eps);
+  for (int j = 0; j < per; ++j)
+    row[lane * per + j] = __float2bfloat16(v[j] * r * __bfloat162float(w[lane * per + j]));
+}
+}  // namespace
+
+void head_rmsnorm(at::Tensor x, int64_t h0, int64_t nh, int64_t D, at::Tensor w, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "head_rmsnorm: bf16 [T, row]");
+  TORCH_CHECK(D % 64 == 0 && D <= 256 && w.numel() == D && w.is_contiguous() && (h0 + nh) * D <= x.size(1),
+              "head_rmsnorm: D in {64, 128, 192, 256}, weight [D]");
+  c10::cuda::CUDAGuard g(x.device());
+  const int64_t warps = x.size(0) * nh;
+  if (warps == 0) return;
+  head_rmsnorm_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)x.size(0), (int)h0, (int)nh, (int)D,
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (float)eps);
+  AETHER_CUDA_CHECK(cudaGetLastError());
+}
+
 }  // namespace aether

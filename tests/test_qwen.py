@@ -73,3 +73,46 @@ def test_gpu_skinny_gemm_and_decode_attention():
         o, _ = ref.attention(q[bi].view(1, 1, Hq, D), kc[s, :L][None], vc[s, :L][None], D ** -0.5, causal=False)
         e = (out[bi].float() - o.reshape(-1)).norm() / o.norm()
         assert e < 1e-2, (bi, float(e))
+
+
+QWEN3 = dict(TINY, qkv_bias=False, qk_norm=True, head_dim_=128, tie_embeddings=False)  # head_dim != d / H
+
+
+def _random_qk_norms(m, seed):
+    g = torch.Generator().manual_seed(seed)
+    for lst in (m.w.q_norm, m.w.k_norm):
+        for t in lst:
+            t.copy_((1 + 0.3 * torch.randn(t.shape, generator=g)).to(t.dtype))
+
+
+def test_cpu_qwen3_qk_norm_decode_matches_full_forward():
+    cfg = QwenConfig(**QWEN3)
+    m = QwenModel(cfg, device="cpu", seed=3, max_batch=2, max_seq=128)
+    _random_qk_norms(m, 0)
+    toks = torch.randint(0, cfg.vocab, (2, 10), generator=torch.Generator().manual_seed(4))
+    nxt, logits = m.prefill(toks, return_logits=True)
+    ref = m.reference_logits(toks)[:, -1]
+    assert float((logits - ref).norm() / ref.norm()) < 2e-2
+    out = m.generate(toks, 4, use_graph=False)
+    seq = torch.cat([toks, out[:, :3]], dim=1)
+    assert torch.equal(out[:, 3], m.reference_logits(seq)[:, -1].argmax(-1))
+
+
+def test_model_family_presets():
+    for cfg, params in ((QwenConfig.qwen3_8b(), 8.19e9), (QwenConfig.llama3_8b(), 8.03e9),
+                        (QwenConfig.mistral_7b(), 7.24e9)):
+        assert abs(cfg.n_params() - params) / params < 0.02, (cfg, cfg.n_params())
+
+
+@pytest.mark.gpu
+def test_gpu_qwen3_qk_norm_graph_decode():
+    cfg = QwenConfig(**QWEN3)
+    m = QwenModel(cfg, device="cuda", seed=3, max_batch=4, max_seq=256)
+    _random_qk_norms(m, 0)
+    toks = torch.randint(0, cfg.vocab, (2, 24), generator=torch.Generator().manual_seed(5)).cuda()
+    _, logits = m.prefill(toks, return_logits=True)
+    ref = m.reference_logits(toks)[:, -1]
+    assert float((logits - ref).norm() / ref.norm()) < 3e-2
+    out_g = m.generate(toks, 5, use_graph=True)
+    out_e = m.generate(toks, 5, use_graph=False)
+    assert float((out_g == out_e).float().mean()) > 0.9
