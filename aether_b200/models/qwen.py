@@ -90,6 +90,25 @@ class QwenConfig:
         return self.n_layers * per + self.vocab * d * (1 if self.tie_embeddings else 2) + d
 
 
+def tp_heads(Hq: int, Hkv: int, rank: int, tp: int) -> tuple:
+    """(query heads, KV heads) of one TP rank. With at least as many KV heads as
+    ranks every rank takes whole GQA groups; with fewer, each KV head is
+    replicated on tp / Hkv ranks, which split its group's query heads as evenly
+    as they go -- so Qwen2.5-7B (28 q / 4 KV heads) runs at TP = 8 with 4 or 3
+    query heads per rank."""
+    if tp <= Hkv:
+        assert Hkv % tp == 0 and Hq % tp == 0, "heads must split evenly over TP"
+        hq, hkv = Hq // tp, Hkv // tp
+        return list(range(rank * hq, (rank + 1) * hq)), list(range(rank * hkv, (rank + 1) * hkv))
+    assert tp % Hkv == 0, "KV heads must replicate evenly over TP"
+    per_kv, G = tp // Hkv, Hq // Hkv
+    j, sub = divmod(rank, per_kv)
+    sizes = [G // per_kv + (1 if s < G % per_kv else 0) for s in range(per_kv)]
+    assert min(sizes) > 0, "more ranks than query heads per KV head"
+    start = j * G + sum(sizes[:sub])
+    return list(range(start, start + sizes[sub])), [j]
+
+
 class QwenWeights:
     """bf16 weights, optionally one tensor-parallel rank's shard.
 
@@ -107,15 +126,12 @@ class QwenWeights:
         self.tp_rank, self.tp_size = tp_rank, tp_size
         d, F_, D, L = cfg.d_model, cfg.d_ff, cfg.head_dim, cfg.n_layers
         Hq, Hkv = cfg.n_heads, cfg.n_kv_heads
-        assert Hq % tp_size == 0 and F_ % tp_size == 0, "heads and d_ff must split over TP"
-        assert Hkv % tp_size == 0 or tp_size % Hkv == 0, "KV heads must split or replicate evenly"
-        self.hq = Hq // tp_size
-        self.hkv = max(1, Hkv // tp_size)
+        assert F_ % tp_size == 0, "d_ff must split over TP"
+        q_heads, kv_heads = tp_heads(Hq, Hkv, tp_rank, tp_size)
+        self.hq = len(q_heads)
+        self.hkv = len(kv_heads)
         self.f = F_ // tp_size
         r = tp_rank
-        q_heads = list(range(r * self.hq, (r + 1) * self.hq))
-        kv_heads = (list(range(r * self.hkv, (r + 1) * self.hkv)) if Hkv >= tp_size
-                    else [r * Hkv // tp_size])
         idx = [0]
 
         def rnd(*shape):
@@ -155,7 +171,7 @@ class QwenWeights:
                 self.bqkv.append(torch.cat(bp, 0).contiguous())
             else:
                 self.bqkv.append(None)
-            self.wo.append(wo[:, r * self.hq * D : (r + 1) * self.hq * D].contiguous())
+            self.wo.append(wo[:, q_heads[0] * D : (q_heads[-1] + 1) * D].contiguous())
             f0, f1 = r * self.f, (r + 1) * self.f
             self.wgu.append(torch.cat([wgu[f0:f1], wgu[F_ + f0 : F_ + f1]], 0).contiguous())
             self.wd.append(wd[:, f0:f1].contiguous())
