@@ -1,0 +1,218 @@
+"""ctypes bindings to ``libaether_rt.so`` -- the C ABI that compiled Aether
+programs link against (CPU op bodies, autodiff tape, AetherLM-Nano trainer,
+checkpoint I/O, serving structures, observability).
+
+    from aether_b200 import runtime as rt
+    rt.call("aether_op_matmul_f32", rt.ptr(a), rt.ptr(b), rt.ptr(c), m, k, n)
+    nano = rt.Nano(vocab=256, d_model=64, n_layers=2, n_heads=4, d_ff=128, seq_len=32, seed=42)
+
+Argument and return types come from ``SIGNATURES`` (floats must be declared
+for ctypes to pass them correctly); functions not listed default to int
+arguments and an int result.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG, "libaether_rt.so")
+_LIB = None
+
+P, I, L, Fl, U64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_uint64
+
+SIGNATURES = {
+    # core ops
+    "aether_op_matmul_f32": (I, [P, P, P, I, I, I]),
+    "aether_op_softmax_f32": (I, [P, I, I, I]),
+    "aether_op_layer_norm_f32": (I, [P, P, P, Fl, P, P, P, I, I]),
+    "aether_op_cross_entropy_f32": (Fl, [P, P, P, I, I]),
+    "aether_op_adamw_step_f32": (I, [P, P, P, P, Fl, Fl, Fl, Fl, Fl, L, I]),
+    "aether_op_clip_grad_norm_f32": (Fl, [P, Fl, I]),
+    "aether_rt_self_check": (I, []),
+    "aether_alloc_f32": (L, [I]),
+    "aether_free": (None, [L]),
+    # extended ops
+    "aether_op_pow_f32": (I, [P, Fl, I]),
+    "aether_op_clamp_f32": (I, [P, Fl, Fl, I]),
+    "aether_op_sum_f32": (Fl, [P, I]),
+    "aether_op_mean_f32": (Fl, [P, I]),
+    "aether_op_var_f32": (Fl, [P, I]),
+    "aether_op_std_f32": (Fl, [P, I]),
+    "aether_op_argmax_f32": (L, [P, I]),
+    "aether_op_lion_step_f32": (I, [P, P, P, I, Fl, Fl, Fl, Fl]),
+    "aether_op_lamb_step_f32": (I, [P, P, P, P, I, Fl, Fl, Fl, Fl, Fl, Fl, Fl]),
+    "aether_op_adafactor_step_f32": (I, [P, P, P, P, I, I, Fl, Fl, Fl]),
+    "aether_op_sgd_momentum_step_f32": (I, [P, P, P, Fl, Fl, Fl, I]),
+    "aether_op_rmsprop_step_f32": (I, [P, P, P, Fl, Fl, Fl, I]),
+    "aether_op_adagrad_step_f32": (I, [P, P, P, Fl, Fl, I]),
+    "aether_op_max_pool_2d_f32": (I, [P, P] + [I] * 10),
+    "aether_op_avg_pool_2d_f32": (I, [P, P] + [I] * 10),
+    "aether_op_adaptive_avg_pool_2d_f32": (I, [P, P] + [I] * 6),
+    "aether_op_embedding_bag_f32": (I, [P, P, P, P, I, I, I, I, I]),
+    "aether_op_masked_fill_f32": (I, [P, P, Fl, I]),
+    "aether_op_mish_backward_f32": (I, [P, P, I]),
+    # dtype conversions and dequantisers
+    "aether_f32_to_bf16": (I, [Fl]),
+    "aether_bf16_to_f32": (Fl, [I]),
+    "aether_f32_to_f16": (I, [Fl]),
+    "aether_f16_to_f32": (Fl, [I]),
+    "aether_op_matmul_bf16_f32_out": (I, [L, L, L, I, I, I]),
+    "aether_pack_f32_to_bf16": (I, [L, L, I]),
+    "aether_dequant_q4_0": (I, [P, P, I]),
+    "aether_dequant_q8_0": (I, [P, P, I]),
+    "aether_dequant_q4_k_m": (I, [P, P, I]),
+    "aether_dequant_q6_k": (I, [P, P, I]),
+    # serving structures
+    "aether_pkv_new": (L, [I, I]),
+    "aether_pkv_destroy": (I, [L]),
+    "aether_pkv_allocate": (I, [L]),
+    "aether_pkv_touch": (I, [L, I]),
+    "aether_pkv_free_block": (I, [L, I]),
+    "aether_pkv_evict_lru": (I, [L]),
+    "aether_pkv_n_allocated": (I, [L]),
+    "aether_pkv_pagetable_new": (L, [I]),
+    "aether_pkv_pagetable_set": (I, [L, I, I]),
+    "aether_pkv_pagetable_get": (L, [L, I]),
+    "aether_pkv_pagetable_translate": (L, [L, I, I]),
+    "aether_batch_sched_new": (L, [L, I, I]),
+    "aether_batch_sched_destroy": (L, [L]),
+    "aether_batch_sched_admit": (L, [L, I, I, I]),
+    "aether_batch_sched_record_token": (L, [L, I, I]),
+    "aether_batch_sched_finish": (L, [L, I]),
+    "aether_batch_sched_reap": (L, [L]),
+    "aether_batch_sched_n_active": (L, [L]),
+    "aether_batch_sched_position": (L, [L, I]),
+    "aether_batch_sched_pagetable_for": (L, [L, I]),
+    "aether_cb_new": (L, [I]),
+    "aether_cb_admit": (I, [L, I]),
+    "aether_cb_step": (I, [L]),
+    "aether_cb_complete": (I, [L, I]),
+    "aether_cb_n_active": (I, [L]),
+    "aether_specdec_accept": (I, [Fl, Fl, Fl]),
+    "aether_mm_new": (L, []),
+    "aether_mm_register": (I, [L, P, I, I]),
+    "aether_mm_lookup": (I, [L, P, I]),
+    "aether_mm_total_vram_mb": (I, [L]),
+    "aether_rl_new": (L, [I, I]),
+    "aether_rl_check": (I, [L, P, I, L]),
+    # observability
+    "aether_obs_counter_inc": (I, [P, I, I]),
+    "aether_obs_counter_get": (L, [P, I]),
+    "aether_obs_dump_prometheus": (I, [P, I]),
+    "aether_crash_dump": (I, [P, L, L]),
+    "aether_gpu_alloc_track": (L, [L]),
+    "aether_gpu_free_track": (L, [L]),
+    "aether_gpu_live_bytes": (L, []),
+    "aether_oom_signal": (L, [L]),
+    "aether_oom_check": (L, []),
+    "aether_prof_alloc_total": (L, []),
+    "aether_prof_alloc_live": (L, []),
+    "aether_prof_alloc_peak": (L, []),
+    "aether_prof_reset": (I, []),
+    "aether_timer_start": (L, []),
+    "aether_timer_elapsed_us": (L, [L]),
+    # AetherLM-Nano
+    "aether_nano_create": (P, [I, I, I, I, I, I, U64]),
+    "aether_nano_destroy": (None, [P]),
+    "aether_nano_num_params": (L, [P]),
+    "aether_nano_params": (C.POINTER(C.c_float), [P]),
+    "aether_nano_train_step": (Fl, [P, P, P, I, Fl, Fl, Fl, L]),
+    "aether_nano_loss": (Fl, [P, P, P, I]),
+    "aether_nano_generate": (I, [P, P, I, I, P]),
+    "aether_nano_synthetic_corpus": (L, [P, L, U64, I]),
+    "aether_nano_pattern_corpus": (L, [P, L]),
+    "aether_nano_sample_batch": (None, [P, L, I, I, P, P, P]),
+    "aether_nano_cosine_lr": (Fl, [I, I, Fl, I]),
+    "aether_nano_save": (I, [P, C.c_char_p]),
+    "aether_nano_load_weights": (I, [P, C.c_char_p]),
+}
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            from .._build import build_runtime
+
+            build_runtime()  # plain g++ / make: seconds, no GPU needed
+        _LIB = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(_LIB, name)
+            fn.restype, fn.argtypes = res, args
+    return _LIB
+
+
+def call(name: str, *args):
+    return getattr(lib(), name)(*args)
+
+
+def ptr(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Nano:
+    """AetherLM-Nano on the native CPU trainer (reference trainer/src/model.rs)."""
+
+    def __init__(self, vocab=256, d_model=64, n_layers=2, n_heads=4, d_ff=128, seq_len=32, seed=42):
+        self.seq_len = seq_len
+        self.step = 0
+        self.h = call("aether_nano_create", vocab, d_model, n_layers, n_heads, d_ff, seq_len, seed)
+
+    def __del__(self):
+        if getattr(self, "h", None) and _LIB is not None:
+            try:
+                _LIB.aether_nano_destroy(self.h)
+            except Exception:  # noqa: BLE001 -- interpreter shutdown
+                pass
+            self.h = None
+
+    @property
+    def n_params(self) -> int:
+        return int(call("aether_nano_num_params", self.h))
+
+    def params(self) -> np.ndarray:
+        return np.ctypeslib.as_array(call("aether_nano_params", self.h), shape=(self.n_params,)).copy()
+
+    def train_step(self, ids: np.ndarray, labels: np.ndarray, lr: float, wd: float = 0.0, clip: float = 1.0) -> float:
+        B = ids.shape[0]
+        self.step += 1
+        return float(call("aether_nano_train_step", self.h, ptr(ids), ptr(labels), B, lr, wd, clip, self.step))
+
+    def loss(self, ids, labels) -> float:
+        return float(call("aether_nano_loss", self.h, ptr(ids), ptr(labels), ids.shape[0]))
+
+    def generate(self, prompt, max_new: int) -> list:
+        p = np.asarray(prompt, dtype=np.int32)
+        out = np.zeros(max_new, dtype=np.int32)
+        n = call("aether_nano_generate", self.h, ptr(p), len(p), max_new, ptr(out))
+        return out[:n].tolist()
+
+    def save(self, stem: str) -> int:
+        return int(call("aether_nano_save", self.h, stem.encode()))
+
+    def load(self, path: str) -> int:
+        return int(call("aether_nano_load_weights", self.h, path.encode()))
+
+
+def synthetic_corpus(n_bytes: int, seed: int = 42, n_words: int = 200) -> np.ndarray:
+    buf = np.zeros(n_bytes, dtype=np.uint8)
+    n = call("aether_nano_synthetic_corpus", ptr(buf), n_bytes, seed, n_words)
+    return buf[:n]
+
+
+def pattern_corpus(n_bytes: int) -> np.ndarray:
+    """The reference trainer's default smoke corpus (one sentence repeated)."""
+    buf = np.zeros(n_bytes, dtype=np.uint8)
+    call("aether_nano_pattern_corpus", ptr(buf), n_bytes)
+    return buf
+
+
+def sample_batch(data: np.ndarray, B: int, S: int, rng_state: np.ndarray):
+    ids = np.zeros((B, S), dtype=np.int32)
+    labels = np.zeros((B, S), dtype=np.int32)
+    call("aether_nano_sample_batch", ptr(data), data.size, B, S, ptr(rng_state), ptr(ids), ptr(labels))
+    return ids, labels

@@ -68,10 +68,27 @@ int aether_autodiff_partial_count() {
 }
 
 // ------------------------------------------------------------------ host memory
-int64_t aether_alloc_f32(int n) { return (int64_t)(intptr_t)std::calloc((size_t)std::max(n, 1), sizeof(float)); }
-int64_t aether_alloc_i32(int n) { return (int64_t)(intptr_t)std::calloc((size_t)std::max(n, 1), sizeof(int32_t)); }
-int64_t aether_alloc_bytes(int64_t n) { return (int64_t)(intptr_t)std::calloc((size_t)std::max<int64_t>(n, 1), 1); }
-void aether_free(int64_t p) { std::free((void*)(intptr_t)p); }
+// Every block carries a 16-byte header with its size, so the allocation
+// probes (aether_prof_alloc_{total,live,peak}) can track frees too.
+void aether_prof_note_alloc(int64_t bytes);  // ext.cpp
+void aether_prof_note_free(int64_t bytes);
+static int64_t rt_alloc(int64_t bytes) {
+  bytes = std::max<int64_t>(bytes, 1);
+  uint8_t* p = static_cast<uint8_t*>(std::calloc((size_t)bytes + 16, 1));
+  if (!p) return 0;
+  *reinterpret_cast<int64_t*>(p) = bytes;
+  aether_prof_note_alloc(bytes);
+  return (int64_t)(intptr_t)(p + 16);
+}
+int64_t aether_alloc_f32(int n) { return rt_alloc((int64_t)std::max(n, 1) * (int64_t)sizeof(float)); }
+int64_t aether_alloc_i32(int n) { return rt_alloc((int64_t)std::max(n, 1) * (int64_t)sizeof(int32_t)); }
+int64_t aether_alloc_bytes(int64_t n) { return rt_alloc(n); }
+void aether_free(int64_t p) {
+  if (p == 0) return;
+  uint8_t* base = reinterpret_cast<uint8_t*>((intptr_t)p) - 16;
+  aether_prof_note_free(*reinterpret_cast<int64_t*>(base));
+  std::free(base);
+}
 
 // SplitMix64 + Box-Muller normal fill (same generator as the trainer).
 int aether_init_normal_f32(void* buf, int n, float mean, float std, uint64_t seed) {

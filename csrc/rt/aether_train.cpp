@@ -20,6 +20,7 @@ void aether_nano_destroy(void*);
 int64_t aether_nano_num_params(void*);
 float aether_nano_train_step(void*, const int32_t*, const int32_t*, int, float, float, float, int64_t);
 int64_t aether_nano_synthetic_corpus(uint8_t*, int64_t, uint64_t, int);
+int64_t aether_nano_pattern_corpus(uint8_t*, int64_t);
 void aether_nano_sample_batch(const uint8_t*, int64_t, int, int, uint64_t*, int32_t*, int32_t*);
 float aether_nano_cosine_lr(int, int, float, int);
 int aether_nano_save(void*, const char*);
@@ -27,7 +28,7 @@ int aether_nano_generate(void*, const int32_t*, int, int, int32_t*);
 }
 
 int main(int argc, char** argv) {
-  std::string config = "nano", data, out = "checkpoints/aether_lm";
+  std::string config = "nano", data, out = "checkpoints/aether_lm", synthetic = "pattern";
   int steps = 60, batch = 8, seq = 0, log_every = 10, warmup = 10, gen = 60;
   float lr = 3e-3f, wd = 0.f, clip = 1.f;
   uint64_t seed = 42;
@@ -44,6 +45,7 @@ int main(int argc, char** argv) {
     else if (a == "--log-every") log_every = std::max(1, std::atoi(next().c_str()));
     else if (a == "--data") data = next();
     else if (a == "--synth-bytes") synth = std::atoll(next().c_str());
+    else if (a == "--synthetic") synthetic = next();  // pattern (reference default) | words
     else if (a == "--out") out = next();
     else if (a == "--warmup") warmup = std::atoi(next().c_str());
     else if (a == "--wd") wd = std::atof(next().c_str());
@@ -77,7 +79,10 @@ int main(int argc, char** argv) {
     corpus.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
   } else {
     corpus.resize((size_t)synth);
-    aether_nano_synthetic_corpus(corpus.data(), synth, seed, 200);
+    if (synthetic == "words")
+      aether_nano_synthetic_corpus(corpus.data(), synth, seed, 200);
+    else
+      aether_nano_pattern_corpus(corpus.data(), synth);
   }
   void* m = aether_nano_create(V, D, L, H, F, S, seed);
   std::fprintf(stderr, "[aether-train] config=%s params=%lld corpus=%zu bytes\n", config.c_str(),

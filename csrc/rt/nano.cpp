@@ -380,6 +380,15 @@ int64_t aether_nano_synthetic_corpus(uint8_t* out, int64_t n_bytes, uint64_t see
   return (int64_t)v.size();
 }
 
+// The reference trainer's default smoke corpus: one English sentence repeated
+// (trainer/src/data.rs ByteDataset::synthetic). Learnable in tens of steps.
+int64_t aether_nano_pattern_corpus(uint8_t* out, int64_t n_bytes) {
+  static const char kPat[] = "the quick brown fox jumps over the lazy dog. ";
+  const int64_t m = (int64_t)sizeof(kPat) - 1;
+  for (int64_t i = 0; i < n_bytes; ++i) out[i] = (uint8_t)kPat[i % m];
+  return n_bytes;
+}
+
 // Random windows of a byte corpus: ids/labels [B, S].
 void aether_nano_sample_batch(const uint8_t* data, int64_t n, int B, int S, uint64_t* rng_state, int32_t* ids,
                               int32_t* labels) {
