@@ -117,6 +117,7 @@ def parse():
     ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
                     help="fused: one-kernel NVLink reduce + AdamW + broadcast; nccl: NCCL reduce-scatter/all-gather")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (TP x DP mesh, e.g. --gpus 8 --tp 4)")
+    ap.add_argument("--pp", type=int, default=1, help="pipeline stages (1F1B over NCCL p2p); --gpus must equal --pp")
     ap.add_argument("--tp-comm", default="symm", choices=["symm", "nccl"],
                     help="TP all-reduce: in-kernel symmetric-memory (NVLS / peer loads) or NCCL")
     return ap.parse_args()
@@ -146,6 +147,8 @@ def main():
 
     cfg = GPTConfig(n_layers=args.layers)
     S = args.seq
+    if args.pp > 1:
+        return run_pp(args, info, cfg)
     tp = args.tp
     assert world % tp == 0, "--gpus must be a multiple of --tp"
     dp_world = world // tp
@@ -279,6 +282,86 @@ def main():
             "impl": "aether",
         }
         print(json.dumps(out), flush=True)
+    D.barrier()
+    D.shutdown()
+    return 0
+
+
+def run_pp(args, info, cfg):
+    """GPT-24L as a 1F1B pipeline: one stage per GPU, the global batch split
+    into micro-batches, activations and gradients over NCCL p2p."""
+    import torch
+
+    from aether_b200 import _ext
+    from aether_b200.parallel import dist as D
+    from aether_b200.parallel.pp import GPTPipelineStage, run_1f1b
+
+    world, S = info.world, args.seq
+    assert world == args.pp, "--gpus must equal --pp (pure pipeline)"
+    st = GPTPipelineStage(cfg, info.rank, world, info.device, seed=1234, lr=3e-4, weight_decay=0.1)
+    gen = torch.Generator().manual_seed(1000)  # every rank sees the same micro-batches
+    toks = torch.randint(0, cfg.vocab, (args.global_batch, S + 1), generator=gen, dtype=torch.int64)
+    n_mb = args.global_batch // args.micro_batch
+    host = [(toks[i * args.micro_batch : (i + 1) * args.micro_batch, :-1].contiguous().pin_memory(),
+             toks[i * args.micro_batch : (i + 1) * args.micro_batch, 1:].contiguous().pin_memory()) for i in range(n_mb)]
+    dev = [(a.to(info.device), b.to(info.device)) for a, b in host]
+
+    def step(batches):
+        st.zero_grad()
+        loss = run_1f1b(st, batches)
+        st.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step(dev)
+    torch.cuda.synchronize()
+    D.barrier()
+    sampler = ClockSampler(range(torch.cuda.device_count())) if info.is_main else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    D.barrier()
+    torch.cuda.synchronize()
+    _ext.count_launches(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(dev)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = _ext.count_launches(False)
+    D.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = D.all_reduce_max(e0.elapsed_time(e1) / args.steps, info.device)
+    tokens = args.global_batch * S
+    value = tokens / (ms / 1e3)
+    e2e = None
+    if not args.no_e2e:
+        torch.cuda.synchronize()
+        D.barrier()
+        t0 = time.perf_counter()
+        k2 = max(2, args.steps // 2)
+        for _ in range(k2):
+            loss = step(host)  # pinned host -> device inside the schedule
+            if loss is not None:
+                float(loss.item())
+        torch.cuda.synchronize()
+        wall = D.all_reduce_max((time.perf_counter() - t0) / k2 * 1e3, info.device)
+        e2e = {"value": tokens / (wall / 1e3), "unit": "tokens/s", "ms_per_step": wall, "steps": k2,
+               "h2d_bytes_per_step": 2 * args.global_batch * S * 8 * world, "d2h_bytes_per_step": 4,
+               "timing": "host wall clock around run_1f1b + step + loss.item(), max over ranks"}
+    if info.is_main:
+        tflops = value * cfg.flops_per_token(S) / world / 1e12
+        print(json.dumps({
+            "metric": "train_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: uniform-random token ids, random-init weights",
+            "config": {"model": f"GPT-{cfg.n_layers}L d{cfg.d_model} {cfg.n_heads}H SwiGLU-{cfg.d_ff} vocab{cfg.vocab}",
+                       "params": cfg.n_params(), "global_batch": args.global_batch, "seq_len": S,
+                       "micro_batch": args.micro_batch, "parallelism": f"pp{world} 1f1b nccl-p2p",
+                       "l2": "no flush needed: per-step working set >> 126 MB L2"},
+            "model_tflops_per_gpu": tflops, "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "impl": "aether"}),
+            flush=True)
     D.barrier()
     D.shutdown()
     return 0
