@@ -13,8 +13,8 @@
    (multicast once) on the egress side.
 2. Tensor-parallel decode reduction (Qwen2.5-7B o_proj shape, batch 1 / 64):
    the decode GEMM whose epilogue reduces through multimem.red into every
-   rank's accumulator, plus the device barrier, against the same GEMM followed
-   by an NCCL all-reduce. Roofline: max(weight bytes / HBM bandwidth,
+   rank's accumulator and whose last CTA signals completion to the consuming
+   finalize kernel, against the same GEMM followed by an NCCL all-reduce. Roofline: max(weight bytes / HBM bandwidth,
    output bytes over NVLink / link bandwidth).
 Times are CUDA-event device times, max over ranks, after warm-up.
 """
@@ -95,7 +95,7 @@ def tp_reduce(info, out):
         x = torch.randn(B, K, device=dev).bfloat16()
 
         def fused():
-            F.skinny_finalize(tp.reduce_gemm(x, w, 0), y[:B])
+            F.skinny_finalize(tp.reduce_gemm(x, w, 0), y[:B], wait=tp.finalize_wait())
 
         def nccl():
             F.skinny_gemm(x, w, acc_local[:B])

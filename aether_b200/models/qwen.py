@@ -385,7 +385,7 @@ class QwenModel:
                 racc = acc
             else:
                 racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
-            F.finalize_residual_norm(racc, x2, w.mlp_norm[i], h, res=x, eps=cfg.norm_eps)
+            F.finalize_residual_norm(racc, x2, w.mlp_norm[i], h, res=x, eps=cfg.norm_eps, wait=self._tp_wait())
             F.skinny_gemm(h, w.wgu[i], acc)
             F.skinny_finalize(acc, act, swiglu=True)
             if self.tp is None:
@@ -394,7 +394,7 @@ class QwenModel:
             else:
                 racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
             nw = w.attn_norm[i + 1] if i + 1 < L else w.final_norm
-            F.finalize_residual_norm(racc, x, nw, h, res=x2, eps=cfg.norm_eps)
+            F.finalize_residual_norm(racc, x, nw, h, res=x2, eps=cfg.norm_eps, wait=self._tp_wait())
         F.skinny_gemm(h, w.lm_head, acc)
         if self._want_logits:
             b["logits"][:B].copy_(acc[:, : cfg.vocab])
@@ -426,7 +426,7 @@ class QwenModel:
                 F.skinny_finalize(acc, x2, res=x)
             else:
                 racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)
-                F.skinny_finalize(racc, x2, res=x)
+                F.skinny_finalize(racc, x2, res=x, wait=self._tp_wait())
             F.rmsnorm_into(x2, w.mlp_norm[i], h, cfg.norm_eps)
             self._decode_ffn(i, h, x2, x, act, acc)
         F.rmsnorm_into(x, w.final_norm, h, cfg.norm_eps)
@@ -435,6 +435,9 @@ class QwenModel:
             b["logits"][:B].copy_(acc[:, : cfg.vocab])
         b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
         acc.zero_()
+
+    def _tp_wait(self):
+        return self.tp.finalize_wait() if self.tp is not None else None
 
     def _decode_ffn(self, i, h, x2, x, act, acc) -> None:
         """x = x2 + FFN(h) on the decode rows (static buffers)."""
@@ -446,7 +449,7 @@ class QwenModel:
             F.skinny_finalize(acc, x, res=x2)
         else:
             racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
-            F.skinny_finalize(racc, x, res=x2)
+            F.skinny_finalize(racc, x, res=x2, wait=self._tp_wait())
 
     def _bucket(self, B: int) -> int:
         for s in (1, 2, 4, 8, 16, 32, 64):

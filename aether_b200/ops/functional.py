@@ -333,20 +333,31 @@ def grad_norm(g, pre_scale=1.0, max_norm=0.0):
 
 
 # ------------------------------------------------------------------ decode path
-def skinny_gemm(x, w, acc, splits=0, acc_mc=0):
+def skinny_gemm(x, w, acc, splits=0, acc_mc=0, signal=None):
     """acc[M, N] += x[M, K] @ w[N, K]^T in fp32 (acc starts zeroed), M <= 64.
-    acc_mc: NVLS multicast address of a symmetric acc (reduce into all ranks)."""
+    acc_mc: NVLS multicast address of a symmetric acc (reduce into all ranks).
+    signal: (peer slot pointers, epoch, done counter, rank, world) -- the
+    kernel's last CTA announces to every rank that its reductions landed."""
     if _cuda(x):
-        C().skinny_gemm(x, w, acc, int(splits), int(acc_mc))
+        if signal is None:
+            C().skinny_gemm(x, w, acc, int(splits), int(acc_mc))
+        else:
+            peers, epoch, done, rank, world = signal
+            C().skinny_gemm(x, w, acc, int(splits), int(acc_mc), peers, epoch, done, int(rank), int(world))
         return acc
     acc[:, : w.shape[0]] += x.float() @ w.float().t()
     return acc
 
 
-def skinny_finalize(acc, y, bias=None, res=None, swiglu=False):
-    """y = bf16(acc + bias + res) or swiglu(acc halves); zeroes acc."""
+def skinny_finalize(acc, y, bias=None, res=None, swiglu=False, wait=None):
+    """y = bf16(acc + bias + res) or swiglu(acc halves); zeroes acc.
+    wait: (signal slots, epoch, rank, world, timeout_s) -- first wait until
+    every rank has announced its reductions into acc (see skinny_gemm)."""
     if _cuda(acc):
-        C().skinny_finalize(acc, y, bias, res, bool(swiglu))
+        if wait is None:
+            C().skinny_finalize(acc, y, bias, res, bool(swiglu))
+        else:
+            C().skinny_finalize(acc, y, bias, res, bool(swiglu), *wait)
         return y
     M, N = y.shape
     if swiglu:
@@ -454,10 +465,14 @@ def qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache,
     return rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D, page_table)
 
 
-def finalize_residual_norm(acc, y, w, h, bias=None, res=None, eps=1e-6):
-    """y = bf16(acc + bias + res) (residual stream); h = rmsnorm(y) * w; acc zeroed."""
+def finalize_residual_norm(acc, y, w, h, bias=None, res=None, eps=1e-6, wait=None):
+    """y = bf16(acc + bias + res) (residual stream); h = rmsnorm(y) * w; acc zeroed.
+    wait: as in skinny_finalize."""
     if _cuda(acc):
-        C().finalize_residual_norm(acc, bias, res, y, w, h, float(eps))
+        if wait is None:
+            C().finalize_residual_norm(acc, bias, res, y, w, h, float(eps))
+        else:
+            C().finalize_residual_norm(acc, bias, res, y, w, h, float(eps), *wait)
         return y, h
     B, N = y.shape
     a = acc[:B, :N].clone()

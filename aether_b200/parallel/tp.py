@@ -5,10 +5,12 @@ executes on one GPU only): q/k/v heads and gate/up rows column-parallel,
 o_proj and down_proj row-parallel, two reductions of [tokens, d_model] per
 block. Decode runs each row-parallel layer as ONE kernel: the split-K
 swap-AB tcgen05 GEMM's epilogue reduces its fp32 partials through the
-NVSwitch multicast address (``multimem.red``) into every rank's accumulator,
-followed by a device barrier and the finalising kernel (bias / residual ->
-bf16). Without multicast the partials go to a local accumulator and a P2P
-one-shot all-reduce. Prefill uses the NVLS two-shot all-reduce kernel.
+NVSwitch multicast address (``multimem.red``) into every rank's accumulator;
+its last CTA then raises this rank's epoch in every peer's signal slot, and
+the finalising kernel (bias / residual (+ RMSNorm) -> bf16) waits for all
+ranks' slots before it reads -- no separate barrier launch. Without multicast
+the partials go to a local accumulator and a P2P one-shot all-reduce. Prefill
+uses the NVLS two-shot all-reduce kernel.
 """
 from __future__ import annotations
 
@@ -27,6 +29,10 @@ class TensorParallel:
         self.device = info.device
         self._stage = None
         self._acc = []
+        self._done = torch.zeros(4, dtype=torch.int32, device=self.device)  # CTA counters of the signalling GEMMs
+        t = self.team
+        # finalize kernels pass this to F.skinny_finalize / F.finalize_residual_norm(wait=...)
+        self.wait = (t.sig.tensor, t.epoch, self.rank, self.world, float(t.timeout_s)) if self.world > 1 else None
 
     # ------------------------------------------------------------------ prefill
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
@@ -55,12 +61,19 @@ class TensorParallel:
         b, cols = self._acc_buf(which, M, N)
         acc = b.tensor.view(-1, cols)
         if b.mc_ptr:
-            F.skinny_gemm(x, w, acc, acc_mc=b.mc_ptr)
-            self.team.barrier()
+            t = self.team
+            F.skinny_gemm(x, w, acc, acc_mc=b.mc_ptr,
+                          signal=(t.peer_sig, t.epoch, self._done[which % 2], self.rank, self.world))
         else:
             F.skinny_gemm(x, w, acc)
             self.team.all_reduce_(b, acc.numel())
         return acc[:M]
+
+    def finalize_wait(self):
+        """The ``wait`` argument for the kernel that consumes reduce_gemm's
+        output: with multicast the GEMM signals completion itself; without,
+        the all-reduce already synchronised."""
+        return self.wait if (self._acc and self._acc[0][0].mc_ptr) else None
 
     def _init_acc(self, M: int, N: int) -> None:
         rows = max(M, 64)

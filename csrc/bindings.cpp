@@ -51,7 +51,9 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at:
 void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
                       double scale, bool causal, int64_t causal_offset);
 // gemm_skinny.cu
-void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc);
+void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc,
+                 std::optional<at::Tensor> sig_peers, std::optional<at::Tensor> sig_epoch,
+                 std::optional<at::Tensor> sig_done, int64_t sig_rank, int64_t sig_world);
 // comm.cu
 void team_barrier(at::Tensor peer_sig_ptrs, at::Tensor my_sig, at::Tensor epoch, int64_t rank, int64_t world,
                   double timeout_s);
@@ -62,7 +64,8 @@ void dp_reduce_adamw(at::Tensor grad_peers, int64_t grad_mc, at::Tensor param_pe
                      int64_t world, double lr, double beta1, double beta2, double eps, double wd, int64_t step,
                      double gscale, std::optional<at::Tensor> gscale_t);
 void skinny_finalize(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
-                     bool swiglu);
+                     bool swiglu, std::optional<at::Tensor> wait_sig, std::optional<at::Tensor> wait_epoch,
+                     int64_t wait_rank, int64_t wait_world, double wait_timeout_s);
 // decode_attention.cu
 void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t,
                     at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv, int64_t D,
@@ -74,7 +77,9 @@ void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tenso
                        at::Tensor cos_t, at::Tensor sin_t, at::Tensor k_cache, at::Tensor v_cache, int64_t Hq,
                        int64_t Hkv, int64_t D, std::optional<at::Tensor> page_table);
 void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
-                            at::Tensor y, at::Tensor w, at::Tensor h, double eps);
+                            at::Tensor y, at::Tensor w, at::Tensor h, double eps,
+                            std::optional<at::Tensor> wait_sig, std::optional<at::Tensor> wait_epoch,
+                            int64_t wait_rank, int64_t wait_world, double wait_timeout_s);
 // gemm_sm100.cu (grouped) and moe.cu
 void gemm_grouped(at::Tensor a, at::Tensor w, at::Tensor out, at::Tensor tile_group);
 void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool softmax_all, bool renorm);
@@ -116,12 +121,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_bwd", &aether::attention_bwd, "q"_a, "k"_a, "v"_a, "out"_a, "dout"_a, "lse"_a, "dq"_a, "dk"_a,
         "dv"_a, "scale"_a, "causal"_a, "causal_offset"_a, "use_tc"_a = false);
   m.def("attention_fwd_tc", &aether::attention_fwd_tc);
-  m.def("skinny_gemm", &aether::skinny_gemm, "x"_a, "w"_a, "acc"_a, "splits"_a = 0, "acc_mc"_a = 0);
+  m.def("skinny_gemm", &aether::skinny_gemm, "x"_a, "w"_a, "acc"_a, "splits"_a = 0, "acc_mc"_a = 0,
+        "sig_peers"_a = pybind11::none(), "sig_epoch"_a = pybind11::none(), "sig_done"_a = pybind11::none(),
+        "sig_rank"_a = 0, "sig_world"_a = 0);
   m.def("team_barrier", &aether::team_barrier);
   m.def("allreduce_oneshot", &aether::allreduce_oneshot);
   m.def("allreduce_nvls", &aether::allreduce_nvls);
   m.def("dp_reduce_adamw", &aether::dp_reduce_adamw);
-  m.def("skinny_finalize", &aether::skinny_finalize);
+  m.def("skinny_finalize", &aether::skinny_finalize, "acc"_a, "y"_a, "bias"_a, "res"_a, "swiglu"_a,
+        "wait_sig"_a = pybind11::none(), "wait_epoch"_a = pybind11::none(), "wait_rank"_a = 0, "wait_world"_a = 0,
+        "wait_timeout_s"_a = 10.0);
   m.def("rope_kv_append", &aether::rope_kv_append, "qkv"_a, "pos"_a, "slot"_a, "cos_t"_a, "sin_t"_a, "k_cache"_a,
         "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
   m.def("decode_attention", &aether::decode_attention, "q"_a, "k_cache"_a, "v_cache"_a, "slot"_a, "seqlen"_a, "out"_a,
@@ -129,7 +138,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "page_table"_a = pybind11::none());
   m.def("qkv_finalize_rope", &aether::qkv_finalize_rope, "acc"_a, "bias"_a, "qkv"_a, "pos"_a, "slot"_a, "cos_t"_a,
         "sin_t"_a, "k_cache"_a, "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
-  m.def("finalize_residual_norm", &aether::finalize_residual_norm);
+  m.def("finalize_residual_norm", &aether::finalize_residual_norm, "acc"_a, "bias"_a, "res"_a, "y"_a, "w"_a, "h"_a,
+        "eps"_a, "wait_sig"_a = pybind11::none(), "wait_epoch"_a = pybind11::none(), "wait_rank"_a = 0,
+        "wait_world"_a = 0, "wait_timeout_s"_a = 10.0);
   m.def("gemm_grouped", &aether::gemm_grouped, "grouped (MoE) tcgen05 GEMM over 128-row expert tiles");
   m.def("moe_route", &aether::moe_route);
   m.def("moe_permute", &aether::moe_permute);

@@ -287,4 +287,70 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------- cross-GPU completion flags
+// A kernel that reduced into every rank's buffer (multimem / peer stores)
+// announces completion with PeerSignal; the consumer kernel on each rank
+// gates itself with PeerWait. Same epoch protocol as the team barrier of
+// comm.cu: slot q of a rank's signal array holds the last epoch rank q
+// reached; the epoch is a device counter, so the pair is CUDA-graph safe.
+struct PeerSignal {
+  uint64_t peer_sig[8];  // every rank's signal array, as seen from this rank
+  uint32_t* epoch;       // this rank's epoch counter
+  int* done;             // CTA completion counter of the signalling launch (returns to 0)
+  int rank, world;       // world == 0: no signal
+};
+struct PeerWait {
+  const uint32_t* my_sig;  // this rank's signal array
+  const uint32_t* epoch;
+  int rank, world;         // world == 0: no wait
+  uint64_t timeout_ns;
+  int* status;
+};
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Called by every thread of a CTA after its last global/multimem write. The
+// last CTA of the grid bumps the epoch and releases it to every peer.
+__device__ __forceinline__ void peer_signal_done(const PeerSignal& s) {
+  if (s.world == 0) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.sc.sys;" ::: "memory");  // this CTA's writes before its count
+    if (atomicAdd(s.done, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
+      *s.done = 0;
+      asm volatile("fence.sc.sys;" ::: "memory");  // every CTA's writes before the flags
+      const uint32_t e = *s.epoch + 1;
+      *s.epoch = e;
+      for (int q = 0; q < s.world; ++q)
+        if (q != s.rank) st_release_sys_u32(reinterpret_cast<uint32_t*>(s.peer_sig[q]) + s.rank, e);
+    }
+  }
+}
+
+// Called by every thread of a CTA before it reads the reduced data: thread q
+// waits (bounded) until rank q has reached this rank's current epoch.
+__device__ __forceinline__ void peer_wait(const PeerWait& w) {
+  if (w.world == 0) return;
+  const int q = threadIdx.x;
+  if (q < w.world && q != w.rank) {
+    const uint32_t e = *w.epoch;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while ((int32_t)(ld_acquire_sys_u32(w.my_sig + q) - e) < 0) {
+      if ((++it & 255u) == 0 && globaltimer_ns() - t0 > w.timeout_ns) {
+        atomicExch(w.status, kStatusTimeoutPeer);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 }  // namespace aether

@@ -23,6 +23,8 @@
 #include "host_utils.h"
 
 namespace aether {
+PeerWait make_peer_wait(const std::optional<at::Tensor>& my_sig, const std::optional<at::Tensor>& epoch, int64_t rank,
+                        int64_t world, double timeout_s);
 namespace dec {
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -474,8 +476,10 @@ __global__ void __launch_bounds__(1024) finalize_residual_norm_kernel(float* __r
                                                                      const __nv_bfloat16* __restrict__ res,
                                                                      __nv_bfloat16* __restrict__ y,
                                                                      const __nv_bfloat16* __restrict__ w,
-                                                                     __nv_bfloat16* __restrict__ h, float eps) {
+                                                                     __nv_bfloat16* __restrict__ h, float eps,
+                                                                     PeerWait wait) {
   asm volatile("griddepcontrol.launch_dependents;");
+  peer_wait(wait);  // tensor parallel: every rank's reductions into acc have landed
   constexpr int kMaxPer = 8;  // N <= 1024 * 8 = 8192
   const int r = blockIdx.x;
   float* ar = acc + (int64_t)r * ldacc;
@@ -639,7 +643,9 @@ void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tenso
 
 // y = bf16(acc + bias + res); h = rmsnorm(y) * w; acc zeroed. y/h/res: [B, N] contiguous.
 void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
-                            at::Tensor y, at::Tensor w, at::Tensor h, double eps) {
+                            at::Tensor y, at::Tensor w, at::Tensor h, double eps,
+                            std::optional<at::Tensor> wait_sig, std::optional<at::Tensor> wait_epoch,
+                            int64_t wait_rank, int64_t wait_world, double wait_timeout_s) {
   const int64_t B = y.size(0), N = y.size(1);
   TORCH_CHECK(N <= 8192 && y.is_contiguous() && h.is_contiguous(), "finalize_residual_norm: rows up to 8192, contiguous");
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.size(1) >= N, "finalize_residual_norm: acc");
@@ -650,7 +656,8 @@ void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std:
       (bias && bias->defined()) ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
       (res && res->defined()) ? reinterpret_cast<const __nv_bfloat16*>(res->data_ptr()) : nullptr,
       reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), (float)eps);
+      reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), (float)eps,
+      make_peer_wait(wait_sig, wait_epoch, wait_rank, wait_world, wait_timeout_s));
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 

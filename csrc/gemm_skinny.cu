@@ -45,6 +45,7 @@ struct Params {
   int num_kb;      // K blocks of 64
   int64_t units;   // (weight-row tile, K block) pairs: n_tiles * num_kb
   int* status;
+  PeerSignal sig;  // tensor parallel: announce that this rank's reductions have landed
 };
 
 // Stream-K partition: CTA c owns units [c*U/G, (c+1)*U/G) in tile-major order
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+  if constexpr (MC) peer_signal_done(p.sig);
 }
 
 // y = bf16(acc + bias + residual) (or SwiGLU of the [gate | up] halves);
@@ -255,8 +257,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <bool SWIGLU>
 __global__ void finalize_kernel(float* __restrict__ acc, int64_t ldacc, int M, int Nout,
                                 const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ res,
-                                int64_t ldr, __nv_bfloat16* __restrict__ y, int64_t ldy) {
+                                int64_t ldr, __nv_bfloat16* __restrict__ y, int64_t ldy, PeerWait wait) {
   asm volatile("griddepcontrol.launch_dependents;");
+  peer_wait(wait);  // tensor parallel: every rank's reductions into acc have landed
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // 4-wide chunk of the output
   const int chunks = Nout / 4;
   if (i >= (int64_t)M * chunks) return;
@@ -328,7 +331,39 @@ void launch(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int g
 // acc[M, N] += x[M, K] . w[N, K]^T (fp32, acc must start zeroed); M <= 64.
 // acc_mc != 0: reduce into every rank's accumulator through that NVLS
 // multicast address (acc is then this rank's local view of the same buffer).
-void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc) {
+PeerSignal make_peer_signal(const std::optional<at::Tensor>& peers, const std::optional<at::Tensor>& epoch,
+                            const std::optional<at::Tensor>& done, int64_t rank, int64_t world) {
+  PeerSignal s{};
+  if (world <= 0) return s;
+  TORCH_CHECK(world <= 8 && peers && peers->numel() == world && !peers->is_cuda() &&
+                  peers->scalar_type() == at::kLong && epoch && done,
+              "peer signal: CPU int64 [world] peer slot pointers, CUDA epoch and done counters");
+  auto acc = peers->accessor<int64_t, 1>();
+  for (int q = 0; q < world; ++q) s.peer_sig[q] = (uint64_t)acc[q];
+  s.epoch = reinterpret_cast<uint32_t*>(epoch->data_ptr());
+  s.done = done->data_ptr<int>();
+  s.rank = (int)rank;
+  s.world = (int)world;
+  return s;
+}
+
+PeerWait make_peer_wait(const std::optional<at::Tensor>& my_sig, const std::optional<at::Tensor>& epoch, int64_t rank,
+                        int64_t world, double timeout_s) {
+  PeerWait w{};
+  if (world <= 0) return w;
+  TORCH_CHECK(my_sig && epoch && my_sig->is_cuda() && epoch->is_cuda(), "peer wait: CUDA signal array and epoch");
+  w.my_sig = reinterpret_cast<const uint32_t*>(my_sig->data_ptr());
+  w.epoch = reinterpret_cast<const uint32_t*>(epoch->data_ptr());
+  w.rank = (int)rank;
+  w.world = (int)world;
+  w.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  w.status = device_status_word();
+  return w;
+}
+
+void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc,
+                 std::optional<at::Tensor> sig_peers, std::optional<at::Tensor> sig_epoch,
+                 std::optional<at::Tensor> sig_done, int64_t sig_rank, int64_t sig_world) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && acc.is_cuda(), "skinny_gemm: CUDA tensors");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && acc.scalar_type() == at::kFloat,
               "skinny_gemm: bf16 x/w, fp32 acc");
@@ -354,6 +389,8 @@ void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int
   p.num_kb = num_kb;
   p.units = units;
   p.status = device_status_word();
+  p.sig = make_peer_signal(sig_peers, sig_epoch, sig_done, sig_rank, sig_world);
+  TORCH_CHECK(p.sig.world == 0 || acc_mc != 0, "skinny_gemm: the completion signal needs the multicast reduction");
   const int BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
   CUtensorMap tw = make_tmap_2d_bf16(w.data_ptr(), K, N, w.stride(0) * 2, skinny::BK, skinny::BM);
   CUtensorMap tx = make_tmap_2d_bf16(x.data_ptr(), K, M, x.stride(0) * 2, skinny::BK, BN);
@@ -368,7 +405,8 @@ void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int
 // y = bf16(acc (+bias) (+res)), or swiglu over acc's [gate | up] halves when swiglu;
 // acc is re-zeroed. y: [M, Nout] (Nout = N or N/2 for swiglu).
 void skinny_finalize(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
-                     bool swiglu) {
+                     bool swiglu, std::optional<at::Tensor> wait_sig, std::optional<at::Tensor> wait_epoch,
+                     int64_t wait_rank, int64_t wait_world, double wait_timeout_s) {
   const int64_t M = y.size(0), Nout = y.size(1);
   TORCH_CHECK(acc.scalar_type() == at::kFloat && y.scalar_type() == at::kBFloat16 && y.stride(1) == 1, "skinny_finalize: dtypes");
   TORCH_CHECK(Nout % 4 == 0 && acc.size(0) >= M && acc.size(1) >= (swiglu ? 2 * Nout : Nout), "skinny_finalize: shapes");
@@ -385,14 +423,15 @@ void skinny_finalize(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bia
   const int64_t n = M * (Nout / 4);
   const unsigned grid = (unsigned)((n + 255) / 256);
   auto stream = at::cuda::getCurrentCUDAStream();
+  const PeerWait pw = make_peer_wait(wait_sig, wait_epoch, wait_rank, wait_world, wait_timeout_s);
   if (swiglu)
     skinny::finalize_kernel<true><<<grid, 256, 0, stream>>>(acc.data_ptr<float>(), acc.stride(0), (int)M, (int)Nout, b,
                                                             nullptr, 0, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
-                                                            y.stride(0));
+                                                            y.stride(0), pw);
   else
     skinny::finalize_kernel<false><<<grid, 256, 0, stream>>>(acc.data_ptr<float>(), acc.stride(0), (int)M, (int)Nout, b,
                                                              r, ldr, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
-                                                             y.stride(0));
+                                                             y.stride(0), pw);
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
