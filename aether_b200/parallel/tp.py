@@ -6,9 +6,10 @@ o_proj and down_proj row-parallel, two reductions of [tokens, d_model] per
 block. Decode runs each row-parallel layer as ONE kernel: the split-K
 swap-AB tcgen05 GEMM's epilogue reduces its fp32 partials through the
 NVSwitch multicast address (``multimem.red``) into every rank's accumulator;
-its last CTA then raises this rank's epoch in every peer's signal slot, and
-the finalising kernel (bias / residual (+ RMSNorm) -> bf16) waits for all
-ranks' slots before it reads -- no separate barrier launch. Without multicast
+at two ranks its last CTA then raises this rank's epoch in every peer's signal
+slot and the finalising kernel (bias / residual (+ RMSNorm) -> bf16) waits for
+all ranks' slots before it reads (no separate barrier launch); at more ranks a
+device barrier kernel sits between the two, which measured faster there. Without multicast
 the partials go to a local accumulator and a P2P one-shot all-reduce. Prefill
 uses the NVLS two-shot all-reduce kernel.
 """
@@ -30,6 +31,14 @@ class TensorParallel:
         self._stage = None
         self._acc = []
         self._done = torch.zeros(4, dtype=torch.int32, device=self.device)  # CTA counters of the signalling GEMMs
+        # Completion signal from the GEMM's last CTA instead of a separate barrier
+        # launch. Measured (7B o_proj, batch 1): TP2 16.9 vs 19.0 us per reduction,
+        # TP8 26.8 vs 19.7 us -- the signalling GEMM's tail waits for its multimem
+        # reductions to reach all 8 ranks -- so it is the default up to 2 ranks.
+        import os
+
+        env = os.environ.get("AETHER_TP_SIGNAL")
+        self.signal = (env == "1") if env is not None else self.world <= 2
         t = self.team
         # finalize kernels pass this to F.skinny_finalize / F.finalize_residual_norm(wait=...)
         self.wait = (t.sig.tensor, t.epoch, self.rank, self.world, float(t.timeout_s)) if self.world > 1 else None
@@ -60,10 +69,13 @@ class TensorParallel:
             self._init_acc(M, N)
         b, cols = self._acc_buf(which, M, N)
         acc = b.tensor.view(-1, cols)
-        if b.mc_ptr:
+        if b.mc_ptr and self.signal:
             t = self.team
             F.skinny_gemm(x, w, acc, acc_mc=b.mc_ptr,
                           signal=(t.peer_sig, t.epoch, self._done[which % 2], self.rank, self.world))
+        elif b.mc_ptr:
+            F.skinny_gemm(x, w, acc, acc_mc=b.mc_ptr)
+            self.team.barrier()
         else:
             F.skinny_gemm(x, w, acc)
             self.team.all_reduce_(b, acc.numel())
@@ -73,7 +85,7 @@ class TensorParallel:
         """The ``wait`` argument for the kernel that consumes reduce_gemm's
         output: with multicast the GEMM signals completion itself; without,
         the all-reduce already synchronised."""
-        return self.wait if (self._acc and self._acc[0][0].mc_ptr) else None
+        return self.wait if (self.signal and self._acc and self._acc[0][0].mc_ptr) else None
 
     def _init_acc(self, M: int, N: int) -> None:
         rows = max(M, 64)

@@ -322,10 +322,13 @@ __device__ __forceinline__ void peer_signal_done(const PeerSignal& s) {
   if (s.world == 0) return;
   __syncthreads();
   if (threadIdx.x == 0) {
-    asm volatile("fence.sc.sys;" ::: "memory");  // this CTA's writes before its count
+    // GPU-scope release per CTA (cheap), one system-scope fence in the last CTA
+    // before the flags leave -- the same ordering a kernel boundary followed by
+    // a barrier kernel provides, without the extra launch.
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     if (atomicAdd(s.done, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
       *s.done = 0;
-      asm volatile("fence.sc.sys;" ::: "memory");  // every CTA's writes before the flags
+      asm volatile("fence.sc.sys;" ::: "memory");
       const uint32_t e = *s.epoch + 1;
       *s.epoch = e;
       for (int q = 0; q < s.world; ++q)
