@@ -175,3 +175,59 @@ def test_observability(tmp_path):
     assert "label=train" in text and "step=17" in text and "oom_flag=1" in text
     t0 = rt.call("aether_timer_start")
     assert rt.call("aether_timer_elapsed_us", t0) >= 0
+
+
+def test_tcp_transport_and_tools(tmp_path):
+    import subprocess
+    import threading
+
+    lib = rt.lib()
+    for name, res, args in (("aether_tcp_listen", ctypes.c_int64, [ctypes.c_int64]),
+                            ("aether_tcp_listener_port", ctypes.c_int64, [ctypes.c_int64]),
+                            ("aether_tcp_accept_one", ctypes.c_int64, [ctypes.c_int64]),
+                            ("aether_tcp_connect", ctypes.c_int64, [ctypes.c_int64]),
+                            ("aether_tcp_send_all", ctypes.c_int64, [ctypes.c_int64] * 3),
+                            ("aether_tcp_recv_all", ctypes.c_int64, [ctypes.c_int64] * 3),
+                            ("aether_tcp_stream_close", ctypes.c_int, [ctypes.c_int64]),
+                            ("aether_tcp_close", ctypes.c_int, [ctypes.c_int64])):
+        getattr(lib, name).restype, getattr(lib, name).argtypes = res, args
+    lst = lib.aether_tcp_listen(0)  # ephemeral port
+    port = lib.aether_tcp_listener_port(lst)
+    assert lst >= 0 and port > 0
+    got = {}
+
+    def server():
+        s = lib.aether_tcp_accept_one(lst)
+        buf = np.zeros(1000, np.float32)
+        got["n"] = lib.aether_tcp_recv_all(s, buf.ctypes.data, buf.nbytes)
+        got["buf"] = buf
+        lib.aether_tcp_stream_close(s)
+
+    th = threading.Thread(target=server)
+    th.start()
+    c = lib.aether_tcp_connect(port)
+    data = np.arange(1000, dtype=np.float32)
+    assert lib.aether_tcp_send_all(c, data.ctypes.data, data.nbytes) == data.nbytes
+    th.join(timeout=30)
+    lib.aether_tcp_stream_close(c)
+    lib.aether_tcp_close(lst)
+    assert got["n"] == 4000 and np.array_equal(got["buf"], data)
+
+    # star all-reduce across three processes
+    bind = os.path.join(os.path.dirname(rt.LIB_PATH), "bin")
+    p = 29000 + os.getpid() % 1000
+    procs = [subprocess.Popen([os.path.join(bind, "aether-allreduce"), "--role", "server" if r == 0 else "client",
+                               "--port", str(p), "--world-size", "3", "--rank", str(r), "--n", "8", "--value",
+                               str(1 << r)], stdout=subprocess.PIPE, text=True) for r in range(3)]
+    outs = [q.communicate(timeout=60)[0] for q in procs]
+    assert all(q.returncode == 0 for q in procs) and all("sum[0..4]=7,7,7,7" in o for o in outs), outs
+
+    # corpus preparation: copies bytes, refuses paths outside the working directory
+    src = tmp_path / "raw.txt"
+    src.write_text("hello aether\n")
+    ok = subprocess.run([os.path.join(bind, "aether-prepare"), "--in", str(src), "--out", "data/corpus.bin"],
+                        cwd=tmp_path, capture_output=True)
+    assert ok.returncode == 0 and (tmp_path / "data" / "corpus.bin").read_bytes() == b"hello aether\n"
+    bad = subprocess.run([os.path.join(bind, "aether-prepare"), "--in", str(src), "--out", "../escape.bin"],
+                         cwd=tmp_path, capture_output=True)
+    assert bad.returncode != 0
