@@ -101,12 +101,15 @@ class GPT:
     norm, LM head and loss, other stages map hidden states to hidden states."""
 
     def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1, alloc=None,
-                 layers=None, first: bool = True, last: bool = True, tp=None):
+                 layers=None, first: bool = True, last: bool = True, tp=None, cp=None):
         """tp: a ``parallel.tp_train.TPGroup`` -- this rank then holds its
         Megatron shard of every layer (and the same values as the matching
         slice of the unsharded model with the same seed)."""
         self.cfg = cfg
         self.tp = tp if tp is not None and tp.world > 1 else None
+        # context parallel (parallel.cp.CPGroup): this rank holds one contiguous
+        # chunk of every sequence; attention all-gathers K/V over the group
+        self.cp = cp if cp is not None and cp.world > 1 else None
         tp_size = self.tp.world if self.tp else 1
         assert cfg.n_heads % tp_size == 0 and cfg.n_kv_heads % tp_size == 0 and cfg.d_ff % tp_size == 0
         self.device = torch.device(device)
@@ -168,9 +171,11 @@ class GPT:
                 del v.main_grad
 
     def positions(self, B: int, S: int) -> torch.Tensor:
+        """Global positions of this rank's tokens (offset by the CP chunk)."""
         key = (B, S)
         if key not in self._pos_cache:
-            self._pos_cache[key] = torch.arange(S, dtype=torch.int32, device=self.device).repeat(B)
+            off = self.cp.rank * S if self.cp is not None else 0
+            self._pos_cache[key] = (torch.arange(S, dtype=torch.int32, device=self.device) + off).repeat(B)
         return self._pos_cache[key]
 
     def forward_hidden(self, ids: torch.Tensor, x: torch.Tensor | None = None, B: int | None = None,
@@ -191,7 +196,12 @@ class GPT:
             h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
             qkv = lin(i, "wqkv", h)
             qkv = A.rope_(qkv, pos, self.rope_cos, self.rope_sin, Hq + Hkv, D)
-            o = A.attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True)
+            if self.cp is None:
+                o = A.attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True)
+            else:
+                from ..parallel.cp import cp_attention
+
+                o = cp_attention(qkv, B, S, Hq, Hkv, D, scale, self.cp)
             x = lin(i, "wo", o, residual=x)
             h = A.rmsnorm(x, a[f"l{i}.mlp_norm"], cfg.norm_eps)
             gu = lin(i, "wgu", h)
