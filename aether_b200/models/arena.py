@@ -69,6 +69,10 @@ class ParamArena:
         s = self.slots[name]
         return self.master[s.offset : s.offset + s.numel].view(s.shape)
 
+    def set_full(self, name: str, t: torch.Tensor) -> None:
+        """Initialise parameter ``name`` from its full fp32 value."""
+        self.master_view(name).copy_(t.to(self.device, torch.float32))
+
     def names(self):
         return list(self.slots.keys())
 

@@ -101,10 +101,12 @@ class GPT:
     norm, LM head and loss, other stages map hidden states to hidden states."""
 
     def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1, alloc=None,
-                 layers=None, first: bool = True, last: bool = True, tp=None, cp=None):
+                 layers=None, first: bool = True, last: bool = True, tp=None, cp=None, shard=None):
         """tp: a ``parallel.tp_train.TPGroup`` -- this rank then holds its
         Megatron shard of every layer (and the same values as the matching
-        slice of the unsharded model with the same seed)."""
+        slice of the unsharded model with the same seed).
+        shard: a ``parallel.fsdp.ShardSpec`` -- ZeRO-2 / ZeRO-3 (FSDP) storage:
+        the arena holds only this rank's slice of every layer."""
         self.cfg = cfg
         self.tp = tp if tp is not None and tp.world > 1 else None
         # context parallel (parallel.cp.CPGroup): this rank holds one contiguous
@@ -115,8 +117,13 @@ class GPT:
         self.device = torch.device(device)
         self.layers = list(range(cfg.n_layers) if layers is None else layers)
         self.first, self.last = first, last
-        self.arena = ParamArena(gpt_param_specs(cfg, self.layers, first, last, tp_size), self.device,
-                                pad_multiple=pad_multiple, alloc=alloc)
+        specs = gpt_param_specs(cfg, self.layers, first, last, tp_size)
+        if shard is not None:
+            from ..parallel.fsdp import ShardedArena
+
+            self.arena = ShardedArena(specs, self.device, shard)
+        else:
+            self.arena = ParamArena(specs, self.device, pad_multiple=pad_multiple, alloc=alloc)
         self.init_weights(seed)
         cos, sin = ref.rope_tables(cfg.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
@@ -131,19 +138,18 @@ class GPT:
         full_shape = {name: shp for name, shp, _ in full}
         a = self.arena
         with torch.no_grad():
-            for name, slot in a.slots.items():
-                mv = a.master_view(name)
+            for name in a.names():
                 if name.endswith("norm"):
-                    mv.fill_(1.0)
+                    t = torch.ones(full_shape[name], dtype=torch.float32)
                 else:
                     g = torch.Generator(device="cpu").manual_seed(seed * 1000003 + index[name])
                     t = torch.empty(full_shape[name], dtype=torch.float32)
                     t.normal_(0.0, self.cfg.init_std, generator=g)
-                    if self.tp is not None:
-                        from ..parallel.tp_train import shard_tensor
+                if self.tp is not None:
+                    from ..parallel.tp_train import shard_tensor
 
-                        t = shard_tensor(self.cfg, name, t, self.tp.rank, self.tp.world)
-                    mv.copy_(t.to(self.device))
+                    t = shard_tensor(self.cfg, name, t, self.tp.rank, self.tp.world)
+                a.set_full(name, t)
         a.sync_bf16_from_master()
 
     def _linear(self, i: int, name: str, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
@@ -209,10 +215,7 @@ class GPT:
             x = lin(i, "wd", act, residual=x)
         return A.rmsnorm(x, a["final_norm"], cfg.norm_eps) if self.last else x
 
-    def loss(self, ids: torch.Tensor, targets: torch.Tensor, loss_scale: float | None = None,
-             x: torch.Tensor | None = None) -> torch.Tensor:
-        """Sum of per-token CE times loss_scale (default 1/num_tokens = mean).
-        A last pipeline stage passes its input hidden states as ``x``."""
+    def _loss(self, ids, targets, loss_scale, x):
         assert self.last, "loss needs the last stage"
         B, S = targets.shape
         h = self.forward_hidden(ids, x=x, B=B, S=S)
@@ -220,6 +223,16 @@ class GPT:
         if loss_scale is None:
             loss_scale = 1.0 / targets.numel()
         return A.lm_head_cross_entropy(h, w, targets.reshape(-1), loss_scale)
+
+    def loss(self, ids: torch.Tensor, targets: torch.Tensor, loss_scale: float | None = None,
+             x: torch.Tensor | None = None) -> torch.Tensor:
+        """Sum of per-token CE times loss_scale (default 1/num_tokens = mean).
+        A last pipeline stage passes its input hidden states as ``x``."""
+        hooks = getattr(self.arena, "autograd_hooks", None)
+        if hooks is None:
+            return self._loss(ids, targets, loss_scale, x)
+        with hooks():
+            return self._loss(ids, targets, loss_scale, x)
 
     @torch.no_grad()
     def logits(self, ids: torch.Tensor) -> torch.Tensor:

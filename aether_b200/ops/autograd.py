@@ -14,8 +14,17 @@ import torch
 from . import functional as F
 
 
+# Gradient buffers of parameters that autograd re-creates on unpack (sharded
+# parameters gathered again by a saved-tensor hook): the unpacked tensor is a
+# new object, so its buffer is found by (data_ptr, numel).
+MAIN_GRADS: dict = {}
+
+
 def _main_grad(w: torch.Tensor) -> torch.Tensor | None:
-    return getattr(w, "main_grad", None)
+    mg = getattr(w, "main_grad", None)
+    if mg is None and MAIN_GRADS:
+        mg = MAIN_GRADS.get((w.data_ptr(), w.numel()))
+    return mg
 
 
 class LinearFn(torch.autograd.Function):

@@ -149,12 +149,76 @@ def check_tp_train(info):
     print(f"OK tp_train loss={float(lt.detach()):.4f}", flush=True)
 
 
+def check_fsdp(info):
+    """ZeRO-2 and ZeRO-3 over all ranks: the gathered gradient shards equal the
+    all-reduced gradients of the flat arena, and one step keeps the loss finite."""
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.parallel.fsdp import ShardedDataParallel, ShardSpec
+
+    w, r = info.world, info.rank
+    cfg = GPTConfig(vocab=512, d_model=256, n_layers=3, n_heads=4, n_kv_heads=4, d_ff=512, max_seq=128)
+    g = torch.Generator().manual_seed(40 + r)
+    toks = [torch.randint(0, 512, (2, 129), generator=g).to(info.device) for _ in range(2)]
+    ref = GPT(cfg, device=info.device, seed=5)
+    for t in toks:
+        ref.loss(t[:, :-1].contiguous(), t[:, 1:].contiguous()).backward()
+    dist.all_reduce(ref.arena.grad)
+    for stage in (2, 3):
+        m = GPT(cfg, device=info.device, seed=5, shard=ShardSpec(r, w, stage))
+        for t in toks:
+            m.loss(t[:, :-1].contiguous(), t[:, 1:].contiguous()).backward()
+        a = m.arena
+        a._finish_grads()
+        for u, unit in a.units.items():
+            full = torch.empty(unit.numel, dtype=torch.float32, device=info.device)
+            a._all_gather(full, a._shard_of(u, a.grad).contiguous(), False)
+            for n, s in unit.slots.items():
+                o = ref.arena.slots[n].offset
+                want = ref.arena.grad[o : o + s.numel]
+                err = float((full[s.offset : s.offset + s.numel] - want).norm() / want.norm().clamp(min=1e-12))
+                assert err < 1e-4, (stage, n, err)
+        eng = ShardedDataParallel(a, lr=1e-3)
+        eng.step()
+        loss = m.loss(toks[0][:, :-1].contiguous(), toks[0][:, 1:].contiguous())
+        assert torch.isfinite(loss)
+    torch.cuda.synchronize()
+    print(f"OK fsdp stages=2,3 world={w}", flush=True)
+
+
+def check_cp(info):
+    """Context parallelism over all ranks (K/V all-gather) against the whole sequence on one GPU."""
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.parallel.cp import CPGroup, shard_sequence
+
+    w, r = info.world, info.rank
+    S = 128 * w
+    cfg = GPTConfig(vocab=512, d_model=256, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=512, max_seq=S)
+    toks = torch.randint(0, 512, (2, S + 1), generator=torch.Generator().manual_seed(9)).to(info.device)
+    cp = CPGroup(r, w, None)
+    m = GPT(cfg, device=info.device, seed=8, cp=cp)
+    ids, tg = shard_sequence(toks, cp)
+    lc = m.loss(ids, tg)
+    lc.backward()
+    dist.all_reduce(m.arena.grad)
+    m.arena.grad /= w
+    lsum = lc.detach().clone()
+    dist.all_reduce(lsum)
+    ref = GPT(cfg, device=info.device, seed=8)
+    lr = ref.loss(toks[:, :-1].contiguous(), toks[:, 1:].contiguous())
+    lr.backward()
+    assert abs(float(lsum) / w - float(lr.detach())) < 1e-2 * abs(float(lr.detach()))
+    err = float((m.arena.grad - ref.arena.grad).norm() / ref.arena.grad.norm())
+    assert err < 5e-2, err
+    torch.cuda.synchronize()
+    print(f"OK cp world={w} grad_err={err:.2e}", flush=True)
+
+
 def main():
     info = D.init(timeout_s=120)
     from aether_b200.parallel.symm import SymmTeam
 
     team = SymmTeam(info)
-    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train"]
+    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train", "fsdp", "cp"]
     if "allreduce" in which:
         check_allreduce(team, info)
     if "dp" in which:
@@ -165,6 +229,10 @@ def main():
         check_pp(info)
     if "tp_train" in which:
         check_tp_train(info)
+    if "fsdp" in which:
+        check_fsdp(info)
+    if "cp" in which:
+        check_cp(info)
     torch.cuda.synchronize()
     dist.barrier()
     D.shutdown()
