@@ -12,6 +12,14 @@ Qwen2-MoE routes with softmax over all experts then top-k (not renormalised)
 and adds a gated shared expert; Mixtral takes softmax over the top-k logits
 and has no shared expert.
 
+Expert parallelism: under tensor parallelism the token rows are replicated on
+every rank, so the experts are partitioned over the same ranks (rank r holds
+experts [r E / w, (r+1) E / w)) and need no all-to-all. Each rank routes all
+tokens, permutes only the pairs routed to its experts (the others get row -1),
+runs its grouped GEMMs and combines its share together with its TP slice of
+the shared expert; one all-reduce of that partial sum finishes the block, the
+same reduction as a dense row-parallel FFN.
+
 Reference: the MoE fields of the serving ModelConfig
 (runtime/src/serving.rs:459-900), host-side top-k routing (serving.rs:2335)
 and one expert GEMV per (token, expert)
@@ -53,14 +61,22 @@ class MoEConfig(QwenConfig):
         return MoEConfig(**base)
 
 
+def expert_range(E: int, rank: int, world: int) -> tuple[int, int]:
+    """Experts [e0, e1) of rank ``rank`` out of ``world`` (sizes differ by at most one)."""
+    return rank * E // world, (rank + 1) * E // world
+
+
 class MoEWeights:
     """Router [E, d], experts gate|up [E, 2F, d] and down [E, d, F], and the
     shared expert's gate vector [1, d] (its MLP is the dense FFN of the base
     weights, with d_ff = shared_ff)."""
 
-    def __init__(self, cfg: MoEConfig, device, seed: int = 0):
+    def __init__(self, cfg: MoEConfig, device, seed: int = 0, ep_rank: int = 0, ep_size: int = 1):
+        """ep_rank / ep_size: keep only this rank's experts [e0, e1) (same
+        values as the matching slice of the unpartitioned weights)."""
         dev = torch.device(device)
         E, F_, d = cfg.n_experts, cfg.d_expert, cfg.d_model
+        self.e0, self.e1 = expert_range(E, ep_rank, ep_size)
 
         def rnd(idx, *shape, std=cfg.init_std):
             g = torch.Generator(device=dev).manual_seed(seed * 7919 + 104729 + idx)
@@ -72,37 +88,45 @@ class MoEWeights:
             r = torch.zeros(Ep, d, dtype=torch.bfloat16, device=dev)
             r[:E] = rnd(4 * i, E, d)
             self.router.append(r)
-            self.wgu.append(rnd(4 * i + 1, E, 2 * F_, d).contiguous())
-            self.wd.append(rnd(4 * i + 2, E, d, F_).contiguous())
+            self.wgu.append(rnd(4 * i + 1, E, 2 * F_, d)[self.e0 : self.e1].contiguous())
+            self.wd.append(rnd(4 * i + 2, E, d, F_)[self.e0 : self.e1].contiguous())
             self.shared_gate.append(rnd(4 * i + 3, 8, d) if cfg.shared_ff else None)  # row 0 used; 8 rows for the GEMM
 
 
 class MoEQwenModel(QwenModel):
     def __init__(self, cfg: MoEConfig, device="cuda", seed: int = 0, max_batch: int = 64, max_seq: int | None = None,
-                 kv_pages: int = 0, page_size: int = 64, moe_weights: MoEWeights | None = None):
+                 kv_pages: int = 0, page_size: int = 64, moe_weights: MoEWeights | None = None, tp=None):
+        """tp: tensor-parallel group (``all_reduce_``, ``rank``, ``world``):
+        attention and the shared expert are TP-sharded, the routed experts
+        are partitioned over the same ranks (expert parallelism)."""
         import dataclasses
 
-        dense = dataclasses.replace(cfg, d_ff=cfg.shared_ff or 8)  # the shared expert is the dense FFN
-        weights = QwenWeights(dense, device, seed)
+        r, w = (tp.rank, tp.world) if tp is not None else (0, 1)
+        dense = dataclasses.replace(cfg, d_ff=cfg.shared_ff or 8 * w)  # the shared expert is the dense FFN
+        weights = QwenWeights(dense, device, seed, r, w)
         super().__init__(cfg, device=device, seed=seed, max_batch=max_batch, max_seq=max_seq, weights=weights,
-                         kv_pages=kv_pages, page_size=page_size)
+                         kv_pages=kv_pages, page_size=page_size, tp=tp)
         self.fused_decode = False  # decode runs the MoE block through the generic path
-        self.moe = moe_weights or MoEWeights(cfg, device, seed)
+        self.moe = moe_weights or MoEWeights(cfg, device, seed, r, w)
 
     def _moe(self, i: int, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         cfg, m = self.cfg, self.moe
         logits = F.gemm(h, m.router[i], out_dtype=torch.float32)[:, : cfg.n_experts]
         idx, wt = F.moe_route(logits, cfg.top_k, cfg.router_softmax_all, cfg.norm_topk)
-        row_of, src_row, tile_group = F.moe_permute(idx, cfg.n_experts)
+        row_of, src_row, tile_group = F.moe_permute(idx, m.e1 - m.e0, m.e0)
         X = F.moe_gather(h, src_row)
         act = F.swiglu(F.gemm_grouped(X, m.wgu[i], tile_group))
         Y = F.gemm_grouped(act, m.wd[i], tile_group)
         extra = None
-        if cfg.shared_ff:
+        if cfg.shared_ff:  # under TP: this rank's slice of the shared expert (a partial sum)
             g = F.gemm(h, m.shared_gate[i], out_dtype=torch.float32)[:, :1]
             s = F.gemm(F.swiglu(F.gemm(h, self.w.wgu[i])), self.w.wd[i])
             extra = (torch.sigmoid(g) * s.float()).to(torch.bfloat16)
-        return F.moe_combine(Y, row_of, wt, res=x, extra=extra)
+        if self.tp is None:
+            return F.moe_combine(Y, row_of, wt, res=x, extra=extra)
+        y = F.moe_combine(Y, row_of, wt, extra=extra)  # this rank's experts + shared slice
+        self.tp.all_reduce_(y)
+        return x + y
 
     def _ffn(self, i, h, x):
         return self._moe(i, h, x)
@@ -111,8 +135,9 @@ class MoEQwenModel(QwenModel):
         x.copy_(self._moe(i, h, x2))
 
     def _reference_ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:
-        """fp32 per-token loop over the selected experts (numerics oracle)."""
+        """fp32 per-token loop over the selected experts (numerics oracle; one rank)."""
         cfg, m = self.cfg, self.moe
+        assert m.e0 == 0 and m.e1 == cfg.n_experts, "the oracle needs every expert"
         shp = h.shape
         h2 = h.reshape(-1, shp[-1])
         logits = h2 @ m.router[i][: cfg.n_experts].float().t()

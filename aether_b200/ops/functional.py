@@ -556,8 +556,10 @@ def moe_rows(T, k, E):
     return (n + MOE_TILE - 1) // MOE_TILE * MOE_TILE
 
 
-def moe_permute(idx, E):
-    """-> (row_of int32 [T*k], src_row int32 [Mpad], tile_group int32 [Mpad/128])."""
+def moe_permute(idx, E, e0=0):
+    """-> (row_of int32 [T*k], src_row int32 [Mpad], tile_group int32 [Mpad/128]).
+    Experts [e0, e0 + E) are local (tile groups 0..E-1); pairs routed to any
+    other expert get row -1 (expert parallelism)."""
     T, k = idx.shape
     Mpad = moe_rows(T, k, E)
     dev = idx.device
@@ -565,10 +567,11 @@ def moe_permute(idx, E):
         row_of = torch.empty(T * k, dtype=torch.int32, device=dev)
         src_row = torch.empty(Mpad, dtype=torch.int32, device=dev)
         tile_group = torch.empty(Mpad // MOE_TILE, dtype=torch.int32, device=dev)
-        C().moe_permute(idx.contiguous(), int(E), row_of, src_row, tile_group)
+        C().moe_permute(idx.contiguous(), int(E), row_of, src_row, tile_group, int(e0))
         return row_of, src_row, tile_group
-    flat = idx.reshape(-1).long()
-    counts = torch.bincount(flat, minlength=E)
+    flat = idx.reshape(-1).long() - e0
+    local = (flat >= 0) & (flat < E)
+    counts = torch.bincount(flat[local], minlength=E)
     seg = (counts + MOE_TILE - 1) // MOE_TILE * MOE_TILE
     off = torch.zeros(E + 1, dtype=torch.long)
     off[1:] = torch.cumsum(seg, 0)
@@ -576,6 +579,9 @@ def moe_permute(idx, E):
     src_row = torch.full((Mpad,), -1, dtype=torch.int32)
     cur = off[:-1].clone()
     for i, e in enumerate(flat.tolist()):
+        if e < 0 or e >= E:
+            row_of[i] = -1
+            continue
         row_of[i] = int(cur[e])
         src_row[int(cur[e])] = i // k
         cur[e] += 1
@@ -620,7 +626,9 @@ def moe_combine(Y, row_of, wt, res=None, extra=None):
         out = torch.empty(T, Y.shape[1], dtype=torch.bfloat16, device=Y.device)
         C().moe_combine(Y, row_of, wt, int(k), res, extra, out)
         return out
-    acc = (Y[row_of.long()].float().view(T, k, -1) * wt.unsqueeze(-1)).sum(1)
+    r = row_of.long()
+    w = torch.where(r >= 0, wt.reshape(-1), torch.zeros(())).view(T, k, 1)
+    acc = (Y[r.clamp(min=0)].float().view(T, k, -1) * w).sum(1)
     for a in (res, extra):
         if a is not None:
             acc = acc + a.float()

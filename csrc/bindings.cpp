@@ -83,7 +83,8 @@ void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std:
 // gemm_sm100.cu (grouped) and moe.cu
 void gemm_grouped(at::Tensor a, at::Tensor w, at::Tensor out, at::Tensor tile_group);
 void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool softmax_all, bool renorm);
-void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_row, at::Tensor tile_group);
+void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_row, at::Tensor tile_group,
+                 int64_t e0);
 void moe_gather(at::Tensor x, at::Tensor src_row, at::Tensor X);
 void moe_combine(at::Tensor Y, at::Tensor row_of, at::Tensor wt, int64_t k, std::optional<at::Tensor> res,
                  std::optional<at::Tensor> extra, at::Tensor out);
@@ -143,7 +144,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "wait_world"_a = 0, "wait_timeout_s"_a = 10.0);
   m.def("gemm_grouped", &aether::gemm_grouped, "grouped (MoE) tcgen05 GEMM over 128-row expert tiles");
   m.def("moe_route", &aether::moe_route);
-  m.def("moe_permute", &aether::moe_permute);
+  m.def("moe_permute", &aether::moe_permute, "idx"_a, "E"_a, "row_of"_a, "src_row"_a, "tile_group"_a, "e0"_a = 0);
   m.def("moe_gather", &aether::moe_gather);
   m.def("moe_combine", &aether::moe_combine);
   m.def("head_rmsnorm", &aether::head_rmsnorm, "in-place per-head RMSNorm (Qwen3 q/k norm)");

@@ -9,9 +9,11 @@
 //                128-row GEMM tile belongs to one expert: writes the row of
 //                each pair, the source token of each permuted row (-1 for
 //                padding) and the expert of each 128-row tile (-1: unused).
+//                With an expert range [e0, e0 + E) (expert parallelism: this
+//                GPU holds E of the experts) pairs routed elsewhere get row -1.
 //                One CTA; everything stays on the device (CUDA-graph safe).
 //   moe_gather   permuted activations X[r] = x[src_row[r]] (zero rows for padding)
-//   moe_combine  out[t] = sum_j w[t, j] * Y[row_of[t, j]] (+ residual)
+//   moe_combine  out[t] = sum_j w[t, j] * Y[row_of[t, j]] (+ residual); rows -1 skipped
 //
 // Reference: the MoE fields of the serving ModelConfig and the host-side top-k
 // routing (runtime/src/serving.rs:2335, 459-900) with one expert GEMV per
@@ -114,7 +116,7 @@ __global__ void route_kernel(const float* __restrict__ logits, int64_t ld, int T
 }
 
 // One CTA of 1024 threads.
-__global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ idx, int TK, int E, int Mpad,
+__global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ idx, int TK, int E, int e0, int Mpad,
                                                        int* __restrict__ row_of, int* __restrict__ src_row,
                                                        int* __restrict__ tile_group, int k) {
   __shared__ int cnt[kMaxExperts];
@@ -125,7 +127,10 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ i
     cur[e] = 0;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < TK; i += blockDim.x) atomicAdd(&cnt[idx[i]], 1);
+  for (int i = threadIdx.x; i < TK; i += blockDim.x) {
+    const int e = idx[i] - e0;
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int o = 0;
@@ -155,7 +160,11 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ i
   }
   __syncthreads();
   for (int i = threadIdx.x; i < TK; i += blockDim.x) {
-    const int e = idx[i];
+    const int e = idx[i] - e0;
+    if (e < 0 || e >= E) {  // routed to an expert on another GPU
+      row_of[i] = -1;
+      continue;
+    }
     const int r = off[e] + atomicAdd(&cur[e], 1);
     row_of[i] = r;
     src_row[r] = i / k;
@@ -185,8 +194,10 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ Y, int64_t ldy,
   const int t = (int)(i / per_row), c = (int)(i % per_row) * 8;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int j = 0; j < k; ++j) {
+    const int r = row_of[(int64_t)t * k + j];
+    if (r < 0) continue;
     const float w = wt[(int64_t)t * k + j];
-    const uint4 u = *reinterpret_cast<const uint4*>(Y + (int64_t)row_of[(int64_t)t * k + j] * ldy + c);
+    const uint4 u = *reinterpret_cast<const uint4*>(Y + (int64_t)r * ldy + c);
     acc[0] += w * bf16lo(u.x); acc[1] += w * bf16hi(u.x); acc[2] += w * bf16lo(u.y); acc[3] += w * bf16hi(u.y);
     acc[4] += w * bf16lo(u.z); acc[5] += w * bf16hi(u.z); acc[6] += w * bf16lo(u.w); acc[7] += w * bf16hi(u.w);
   }
@@ -224,7 +235,8 @@ void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
-void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_row, at::Tensor tile_group) {
+void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_row, at::Tensor tile_group,
+                 int64_t e0) {
   TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kInt && idx.dim() == 2, "moe_permute: int32 [T, k] experts");
   const int TK = (int)idx.numel(), k = (int)idx.size(1);
   const int Mpad = (int)src_row.numel();
@@ -233,7 +245,7 @@ void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_ro
   TORCH_CHECK(row_of.numel() == TK && tile_group.numel() >= Mpad / moe::kTile, "moe_permute: output sizes");
   c10::cuda::CUDAGuard g(idx.device());
   moe::permute_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
-      idx.data_ptr<int>(), TK, (int)E, Mpad, row_of.data_ptr<int>(), src_row.data_ptr<int>(),
+      idx.data_ptr<int>(), TK, (int)E, (int)e0, Mpad, row_of.data_ptr<int>(), src_row.data_ptr<int>(),
       tile_group.data_ptr<int>(), k);
   AETHER_CUDA_CHECK(cudaGetLastError());
 }

@@ -213,12 +213,33 @@ def check_cp(info):
     print(f"OK cp world={w} grad_err={err:.2e}", flush=True)
 
 
+def check_ep(info):
+    """MoE with experts partitioned over all ranks (attention and shared expert TP-sharded) against one GPU."""
+    from aether_b200.models.moe import MoEConfig, MoEQwenModel
+    from aether_b200.parallel.tp import TensorParallel
+
+    w = info.world
+    cfg = MoEConfig(vocab=512, d_model=256, n_layers=2, n_heads=2 * w, n_kv_heads=w, d_ff=8, max_seq=64,
+                    init_std=0.05, n_experts=4 * w, top_k=2, d_expert=128, shared_ff=128 * w)
+    tp = TensorParallel(info)
+    m = MoEQwenModel(cfg, device=info.device, seed=1, max_batch=2, max_seq=64, tp=tp)
+    ref = MoEQwenModel(cfg, device=info.device, seed=1, max_batch=2, max_seq=64)
+    toks = torch.randint(0, 512, (2, 16), generator=torch.Generator().manual_seed(2)).to(info.device)
+    _, lt = m.prefill(toks, return_logits=True)
+    _, lr = ref.prefill(toks, return_logits=True)
+    err = float((lt - lr).norm() / lr.norm())
+    assert err < 3e-2, err
+    torch.cuda.synchronize()
+    tp.close()
+    print(f"OK ep world={w} err={err:.2e}", flush=True)
+
+
 def main():
     info = D.init(timeout_s=120)
     from aether_b200.parallel.symm import SymmTeam
 
     team = SymmTeam(info)
-    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train", "fsdp", "cp"]
+    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train", "fsdp", "cp", "ep"]
     if "allreduce" in which:
         check_allreduce(team, info)
     if "dp" in which:
@@ -233,6 +254,8 @@ def main():
         check_fsdp(info)
     if "cp" in which:
         check_cp(info)
+    if "ep" in which:
+        check_ep(info)
     torch.cuda.synchronize()
     dist.barrier()
     D.shutdown()
