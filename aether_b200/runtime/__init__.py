@@ -26,6 +26,14 @@ P, I, L, Fl, U64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_uint64
 SIGNATURES = {
     # core ops
     "aether_op_matmul_f32": (I, [P, P, P, I, I, I]),
+    # distributed layout arithmetic
+    "aether_tp_simulate_column_parallel_linear_f32": (I, [P, P, P, I, I, I, I]),
+    "aether_pp_simulate_2stage_forward_f32": (I, [P, P, P, P, I, I, I, I]),
+    "aether_zero_simulate_stage_bytes_f32": (L, [I, I, I]),
+    "aether_overlap_simulate_overlapped_us": (I, [I, I]),
+    "aether_overlap_simulate_serial_us": (I, [I, I]),
+    "aether_grad_compress_lowrank_f32": (I, [P, P, I, I, I]),
+    "aether_fsdp_simulate_shard_alltoall_f32": (I, [P, P, I, I]),
     "aether_op_softmax_f32": (I, [P, I, I, I]),
     "aether_op_layer_norm_f32": (I, [P, P, P, Fl, P, P, P, I, I]),
     "aether_op_cross_entropy_f32": (Fl, [P, P, P, I, I]),

@@ -985,4 +985,104 @@ AE_API int aether_op_all_to_all_f32(const void* src, void* dst, int n, int /*wor
   return 0;
 }
 
+// ------------------------------------------------------------------ distributed algorithm shapes
+// Single-process versions of the parallel layouts, with the reference's
+// names and argument order (runtime/src/lib.rs:3418-3650). Their real
+// multi-GPU counterparts are the torch.distributed engines of the Python
+// package (tensor / pipeline / ZeRO-2/3 / PowerSGD); these check a layout's
+// arithmetic on the host.
+
+// Column-parallel linear: W (k x n) split into world column blocks, each
+// block's product X W_b written into its columns of out (m x n).
+AE_API int aether_tp_simulate_column_parallel_linear_f32(const void* x, const void* w, void* out, int m, int k, int n,
+                                                         int world) {
+  if (!x || !w || !out) return 1;
+  if (m <= 0 || k <= 0 || n <= 0 || world <= 0) return 2;
+  if (n % world) return 3;
+  const float* X = static_cast<const float*>(x);
+  const float* W = static_cast<const float*>(w);
+  float* O = static_cast<float*>(out);
+  const int nb = n / world;
+  for (int b = 0; b < world; ++b)
+    for (int r = 0; r < m; ++r)
+      for (int c = b * nb; c < (b + 1) * nb; ++c) {
+        float acc = 0.f;
+        for (int j = 0; j < k; ++j) acc += X[(size_t)r * k + j] * W[(size_t)j * n + c];
+        O[(size_t)r * n + c] = acc;
+      }
+  return 0;
+}
+
+// Pipeline of n_blocks affine blocks (y = y * scale[b] + bias[b]) over
+// n_stages stages, every micro-batch passing every stage in order.
+AE_API int aether_pp_simulate_2stage_forward_f32(const void* input, const void* scales, const void* biases, void* out,
+                                                 int microbatches, int d, int n_blocks, int n_stages) {
+  if (!input || !scales || !biases || !out) return 1;
+  if (microbatches <= 0 || d <= 0 || n_blocks <= 0 || n_stages <= 0) return 2;
+  if (n_blocks % n_stages) return 3;
+  const float* in = static_cast<const float*>(input);
+  const float* sc = static_cast<const float*>(scales);
+  const float* bi = static_cast<const float*>(biases);
+  float* o = static_cast<float*>(out);
+  const size_t n = (size_t)microbatches * d;
+  std::vector<float> act(in, in + n);  // the activation that would cross each stage boundary
+  const int per = n_blocks / n_stages;
+  for (int st = 0; st < n_stages; ++st)
+    for (int b = st * per; b < (st + 1) * per; ++b)
+      for (size_t i = 0; i < n; ++i) act[i] = act[i] * sc[b] + bi[b];
+  std::memcpy(o, act.data(), n * sizeof(float));
+  return 0;
+}
+
+// Per-rank bytes of fp32 parameters + gradients + two AdamW moments under
+// ZeRO stage 1 (moments sharded), 2 (+ gradients) and 3 (+ parameters).
+AE_API int64_t aether_zero_simulate_stage_bytes_f32(int n_params, int world, int stage) {
+  if (n_params <= 0 || world <= 0) return -1;
+  if (stage < 1 || stage > 3) return -2;
+  const int64_t p = 4LL * n_params, g = 4LL * n_params, o = 8LL * n_params;
+  if (stage == 1) return p + g + o / world;
+  if (stage == 2) return p + (g + o) / world;
+  return (p + g + o) / world;
+}
+
+// Step time with the collective hidden under compute versus run after it.
+AE_API int aether_overlap_simulate_overlapped_us(int compute_us, int comm_us) {
+  if (compute_us < 0 || comm_us < 0) return -1;
+  return std::max(compute_us, comm_us);
+}
+AE_API int aether_overlap_simulate_serial_us(int compute_us, int comm_us) {
+  if (compute_us < 0 || comm_us < 0) return -1;
+  return compute_us + comm_us;
+}
+
+// Rank-k projection with P = the first k columns of G and Q = the first k
+// unit vectors: the reconstruction keeps G's first k columns and zeroes the
+// rest ((m + n) k values would travel instead of m n). The PowerSGD engine of
+// the Python package is the real compressor.
+AE_API int aether_grad_compress_lowrank_f32(const void* grad, void* reconstructed, int m, int n, int k) {
+  if (!grad || !reconstructed) return 1;
+  if (m <= 0 || n <= 0 || k <= 0) return 2;
+  if (k > n) return 3;
+  const float* g = static_cast<const float*>(grad);
+  float* r = static_cast<float*>(reconstructed);
+  for (int i = 0; i < m; ++i)
+    for (int j = 0; j < n; ++j) r[(size_t)i * n + j] = j < k ? g[(size_t)i * n + j] : 0.f;
+  return 0;
+}
+
+// FSDP round trip: shard a flat parameter vector over world ranks and
+// all-gather the shards back in rank order.
+AE_API int aether_fsdp_simulate_shard_alltoall_f32(const void* params, void* out, int n, int world) {
+  if (!params || !out) return 1;
+  if (n <= 0 || world <= 0) return 2;
+  if (n % world) return 3;
+  const float* p = static_cast<const float*>(params);
+  float* o = static_cast<float*>(out);
+  const int len = n / world;
+  std::vector<std::vector<float>> shards((size_t)world);
+  for (int r = 0; r < world; ++r) shards[(size_t)r].assign(p + (size_t)r * len, p + (size_t)(r + 1) * len);
+  for (int r = 0; r < world; ++r) std::memcpy(o + (size_t)r * len, shards[(size_t)r].data(), len * sizeof(float));
+  return 0;
+}
+
 }  // extern "C"

@@ -231,3 +231,42 @@ def test_tcp_transport_and_tools(tmp_path):
     bad = subprocess.run([os.path.join(bind, "aether-prepare"), "--in", str(src), "--out", "../escape.bin"],
                          cwd=tmp_path, capture_output=True)
     assert bad.returncode != 0
+
+
+def test_distributed_layout_abi():
+    """The reference's single-process layout checks: column-parallel linear =
+    full matmul, pipelined affine blocks = sequential, ZeRO bytes, overlap,
+    rank-k projection, FSDP round trip."""
+    import numpy as np
+
+    from aether_b200 import runtime as R
+
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((3, 5)).astype(np.float32)
+    w = rng.standard_normal((5, 8)).astype(np.float32)
+    out = np.zeros((3, 8), np.float32)
+    assert R.call("aether_tp_simulate_column_parallel_linear_f32", R.ptr(x), R.ptr(w), R.ptr(out), 3, 5, 8, 4) == 0
+    assert np.allclose(out, x @ w, atol=1e-5)
+    assert R.call("aether_tp_simulate_column_parallel_linear_f32", R.ptr(x), R.ptr(w), R.ptr(out), 3, 5, 8, 3) == 3
+    inp = rng.standard_normal((4, 6)).astype(np.float32)
+    sc = rng.standard_normal(6).astype(np.float32)
+    bi = rng.standard_normal(6).astype(np.float32)
+    o = np.zeros_like(inp)
+    assert R.call("aether_pp_simulate_2stage_forward_f32", R.ptr(inp), R.ptr(sc), R.ptr(bi), R.ptr(o), 4, 6, 6, 2) == 0
+    want = inp.copy()
+    for b in range(6):
+        want = want * sc[b] + bi[b]
+    assert np.allclose(o, want, atol=1e-4)
+    z = [R.call("aether_zero_simulate_stage_bytes_f32", 1000, 4, s) for s in (1, 2, 3)]
+    assert z == [4000 + 4000 + 8000 // 4, 4000 + 12000 // 4, 16000 // 4]
+    assert R.call("aether_zero_simulate_stage_bytes_f32", 1000, 4, 4) == -2
+    assert R.call("aether_overlap_simulate_overlapped_us", 30, 20) == 30
+    assert R.call("aether_overlap_simulate_serial_us", 30, 20) == 50
+    g = rng.standard_normal((4, 6)).astype(np.float32)
+    rec = np.zeros_like(g)
+    assert R.call("aether_grad_compress_lowrank_f32", R.ptr(g), R.ptr(rec), 4, 6, 2) == 0
+    assert np.array_equal(rec[:, :2], g[:, :2]) and not rec[:, 2:].any()
+    p = rng.standard_normal(12).astype(np.float32)
+    q = np.zeros_like(p)
+    assert R.call("aether_fsdp_simulate_shard_alltoall_f32", R.ptr(p), R.ptr(q), 12, 4) == 0
+    assert np.array_equal(p, q)
