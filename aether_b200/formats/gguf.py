@@ -262,7 +262,11 @@ def qwen_config_from_gguf(g: GGUFFile):
                       tie_embeddings="output.weight" not in g.tensors,
                       qkv_bias="blk.0.attn_q.bias" in g.tensors,
                       qk_norm="blk.0.attn_q_norm.weight" in g.tensors,
-                      head_dim_=head_dim if head_dim != d // H else 0)
+                      head_dim_=head_dim if head_dim != d // H else 0,
+                      sliding_window=int(m("attention.sliding_window", 0)),
+                      sliding_window_pattern=int(m("attention.sliding_window_pattern", 0)),
+                      rope_theta_swa=float(m("rope.freq_base_swa", 0.0)),
+                      attn_softcap=float(m("attn_logit_softcapping", 0.0)))
 
 
 def load_qwen_weights(path: str, device="cuda"):

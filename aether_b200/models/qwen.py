@@ -46,6 +46,23 @@ class QwenConfig:
     init_std: float = 0.02
     qk_norm: bool = False  # Qwen3: per-head RMSNorm of q and k before RoPE
     head_dim_: int = 0     # 0: d_model / n_heads
+    # flex attention: a sliding window of `sliding_window` keys (0: full); with
+    # `sliding_window_pattern` p > 0 only layers i % p != p - 1 are windowed
+    # (the others attend globally) and windowed layers use rope_theta_swa when
+    # set; attn_softcap > 0 soft-caps the logits (softcap * tanh(s / softcap))
+    sliding_window: int = 0
+    sliding_window_pattern: int = 0
+    rope_theta_swa: float = 0.0
+    attn_softcap: float = 0.0
+
+    def layer_window(self, i: int) -> tuple[int, float]:
+        """(sliding window, RoPE base) of layer i (reference: ModelConfig::attn_layer_params)."""
+        if self.sliding_window_pattern > 0:
+            p = self.sliding_window_pattern
+            if i % p != p - 1:
+                return self.sliding_window, self.rope_theta_swa or self.rope_theta
+            return 0, self.rope_theta
+        return self.sliding_window, self.rope_theta
 
     @property
     def head_dim(self) -> int:
@@ -80,6 +97,14 @@ class QwenConfig:
     def mistral_7b(**kw) -> "QwenConfig":
         base = dict(vocab=32000, d_model=4096, n_layers=32, n_heads=32, n_kv_heads=8, d_ff=14336, qkv_bias=False,
                     tie_embeddings=False, rope_theta=1e6, norm_eps=1e-5)
+        base.update(kw)
+        return QwenConfig(**base)
+
+    @staticmethod
+    def mistral_7b_v01(**kw) -> "QwenConfig":
+        """Mistral-7B v0.1: every layer attends over a 4096-key sliding window."""
+        base = dict(vocab=32000, d_model=4096, n_layers=32, n_heads=32, n_kv_heads=8, d_ff=14336, qkv_bias=False,
+                    tie_embeddings=False, rope_theta=1e4, norm_eps=1e-5, sliding_window=4096)
         base.update(kw)
         return QwenConfig(**base)
 
@@ -224,6 +249,17 @@ class QwenModel:
         self.scratch_slot = max_batch
         cos, sin = ref.rope_tables(self.max_seq, cfg.head_dim, cfg.rope_theta, device=self.device)
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
+        # per-layer flex attention parameters: window and RoPE tables
+        self.win, self.rope_cs = [], []
+        tables = {cfg.rope_theta: (self.cos, self.sin)}
+        for i in range(cfg.n_layers):
+            wnd, base = cfg.layer_window(i)
+            if base not in tables:
+                c2, s2 = ref.rope_tables(self.max_seq, cfg.head_dim, base, device=self.device)
+                tables[base] = (c2.contiguous(), s2.contiguous())
+            self.win.append(wnd)
+            self.rope_cs.append(tables[base])
+        self.softcap = cfg.attn_softcap
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self._fixed_splits = decode_splits
         self.decode_splits = decode_splits or self._auto_splits(1)  # the most any batch size uses
@@ -291,13 +327,14 @@ class QwenModel:
             h, _, _ = F.rmsnorm(x, w.attn_norm[i], cfg.norm_eps)
             qkv = F.gemm(h, w.wqkv[i], bias=w.bqkv[i])
             self._qk_norm(i, qkv)
-            F.rope_kv_append(qkv, pos, slot_t, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq,
+            F.rope_kv_append(qkv, pos, slot_t, *self.rope_cs[i], self.cache.k[i], self.cache.v[i], self.hq,
                              self.hkv, D, page_table=self.page_table)
             q = qkv.view(B, S, row)[:, :, : self.hq * D].view(B, S, self.hq, D)
             if start_pos == 0:
                 k = qkv.view(B, S, row)[:, :, self.hq * D : (self.hq + self.hkv) * D].view(B, S, self.hkv, D)
                 v = qkv.view(B, S, row)[:, :, (self.hq + self.hkv) * D :].view(B, S, self.hkv, D)
-                o, _ = F.attention(q, k, v, self.scale, True, 0, want_lse=False)
+                o, _ = F.attention(q, k, v, self.scale, True, 0, want_lse=False, window=self.win[i],
+                                   softcap=self.softcap)
             else:
                 Lk = start_pos + S
                 if self.paged:
@@ -308,7 +345,8 @@ class QwenModel:
                     assert bool((slots == torch.arange(B, device=slots.device)).all()), "chunked prefill needs slots 0..B-1"
                     k = self.cache.k[i][:B, :Lk]
                     v = self.cache.v[i][:B, :Lk]
-                o, _ = F.attention(q, k, v, self.scale, True, start_pos, want_lse=False)
+                o, _ = F.attention(q, k, v, self.scale, True, start_pos, want_lse=False, window=self.win[i],
+                                   softcap=self.softcap)
             o2 = o.view(T, self.hq * D)
             if self.tp is None:
                 x = F.gemm(o2, w.wo[i], residual=x)
@@ -376,10 +414,11 @@ class QwenModel:
         L = cfg.n_layers
         for i in range(L):
             F.skinny_gemm(h, w.wqkv[i], acc)
-            F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i],
+            F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, *self.rope_cs[i], self.cache.k[i], self.cache.v[i],
                                 self.hq, self.hkv, D, page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
-                               self._auto_splits(B), b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table)
+                               self._auto_splits(B), b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table,
+                               window=self.win[i], softcap=self.softcap)
             if self.tp is None:
                 F.skinny_gemm(o, w.wo[i], acc)
                 racc = acc
@@ -417,10 +456,11 @@ class QwenModel:
             F.skinny_gemm(h, w.wqkv[i], acc)
             F.skinny_finalize(acc, qkv, bias=w.bqkv[i])
             self._qk_norm(i, qkv)
-            F.rope_kv_append(qkv, pos, slot, self.cos, self.sin, self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D,
+            F.rope_kv_append(qkv, pos, slot, *self.rope_cs[i], self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D,
                              page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
-                               self._auto_splits(B), b["part_o"], b["part_lse"], page_table=self.page_table)
+                               self._auto_splits(B), b["part_o"], b["part_lse"], page_table=self.page_table,
+                               window=self.win[i], softcap=self.softcap)
             if self.tp is None:
                 F.skinny_gemm(o, w.wo[i], acc)
                 F.skinny_finalize(acc, x2, res=x)
@@ -549,12 +589,12 @@ class QwenModel:
                     v = v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * wn.float()
                     qkv[..., h0 * D : (h0 + nh) * D] = v.reshape(B, S, nh * D)
             qkv2 = qkv.reshape(B * S, -1)
-            qkv2 = ref.rope(qkv2, pos.repeat(B), self.cos, self.sin, self.hq + self.hkv, D)
+            qkv2 = ref.rope(qkv2, pos.repeat(B), *self.rope_cs[i], self.hq + self.hkv, D)
             qkv = qkv2.view(B, S, -1)
             q = qkv[..., : self.hq * D].view(B, S, self.hq, D)
             k = qkv[..., self.hq * D : (self.hq + self.hkv) * D].view(B, S, self.hkv, D)
             v = qkv[..., (self.hq + self.hkv) * D :].view(B, S, self.hkv, D)
-            o, _ = ref.attention(q, k, v, self.scale, True)
+            o, _ = ref.attention(q, k, v, self.scale, True, 0, self.win[i], self.softcap)
             x = x + o.reshape(B, S, -1) @ w.wo[i].float().t()
             h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.mlp_norm[i].float()
             x = x + self._reference_ffn(i, h)

@@ -258,21 +258,26 @@ def _tc_ok(q, k, v):
     return True
 
 
-def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=True, impl="auto"):
+def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=True, impl="auto", window=0,
+              softcap=0.0):
     """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] (strided views ok) -> (o [B,Sq,Hq,D], lse [B,Hq,Sq]).
 
     impl: "auto" (tcgen05 kernel when it applies, else the mma.sync kernel),
-    "tc" or "fa2"."""
+    "tc" or "fa2". Flex attention: ``window`` > 0 (sliding window: query i
+    sees keys (i + offset - window, i + offset]) and ``softcap`` > 0 (logits
+    soft-capped by softcap * tanh(s / softcap)); forward only."""
     B, Sq, Hq, D = q.shape
     if _cuda(q):
         o = out if out is not None else torch.empty(B, Sq, Hq, D, dtype=q.dtype, device=q.device)
         lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device) if want_lse else None
         if impl == "tc" or (impl == "auto" and _tc_ok(q, k, v)):
-            C().attention_fwd_tc(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset))
+            C().attention_fwd_tc(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset), int(window),
+                                 float(softcap))
         else:
-            C().attention_fwd(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset))
+            C().attention_fwd(q, k, v, o, lse, float(scale), bool(causal), int(causal_offset), int(window),
+                              float(softcap))
         return o, lse
-    o, lse = ref.attention(q, k, v, scale, causal, causal_offset)
+    o, lse = ref.attention(q, k, v, scale, causal, causal_offset, window, softcap)
     o = o.to(q.dtype).contiguous()
     if out is not None:
         out.copy_(o)
@@ -415,9 +420,10 @@ def gather_kv(cache, slot: int, L: int, page_table=None):
 
 
 def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8, part_o=None, part_lse=None,
-                     counters=None, page_table=None):
+                     counters=None, page_table=None, window=0, softcap=0.0):
     """q [B, >=Hq*D] (one new token per sequence), caches [slots, max_seq, Hkv, D]
-    (or page pools with ``page_table``), seqlen [B] = valid keys. Writes out [B, Hq*D]."""
+    (or page pools with ``page_table``), seqlen [B] = valid keys. Writes out [B, Hq*D].
+    window > 0: only the last ``window`` keys; softcap > 0: soft-capped logits."""
     B = q.shape[0]
     D = k_cache.shape[3]
     if _cuda(q):
@@ -425,7 +431,7 @@ def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8
             part_o = torch.empty(B * Hq * splits * D, dtype=torch.float32, device=q.device)
             part_lse = torch.empty(B * Hq * splits, dtype=torch.float32, device=q.device)
         C().decode_attention(q, k_cache, v_cache, slot, seqlen, out, part_o, part_lse, int(Hq), int(splits),
-                             float(scale), counters, page_table)
+                             float(scale), counters, page_table, int(window), float(softcap))
         return out
     Hkv = k_cache.shape[2]
     for b in range(B):
@@ -434,7 +440,7 @@ def decode_attention(q, k_cache, v_cache, slot, seqlen, out, Hq, scale, splits=8
         qb = q[b, : Hq * D].view(1, 1, Hq, D)
         kb = gather_kv(k_cache, s, L, page_table).unsqueeze(0)
         vb = gather_kv(v_cache, s, L, page_table).unsqueeze(0)
-        o, _ = ref.attention(qb, kb, vb, scale, causal=False)
+        o, _ = ref.attention(qb, kb, vb, scale, True, L - 1, window, softcap)
         out[b, : Hq * D] = o.reshape(-1).to(out.dtype)
     return out
 

@@ -75,8 +75,10 @@ def rope(x, pos, cos_t, sin_t, n_heads, head_dim, inverse=False):
     return y
 
 
-def attention(q, k, v, scale, causal=True, causal_offset=0):
-    """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] -> (out [B,Sq,Hq,D], lse [B,Hq,Sq])."""
+def attention(q, k, v, scale, causal=True, causal_offset=0, window=0, softcap=0.0):
+    """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] -> (out [B,Sq,Hq,D], lse [B,Hq,Sq]).
+    window > 0: query i sees keys (i + offset - window, i + offset];
+    softcap > 0: logits -> softcap * tanh(logits / softcap)."""
     B, Sq, Hq, D = q.shape
     Sk, Hkv = k.shape[1], k.shape[2]
     g = Hq // Hkv
@@ -84,10 +86,14 @@ def attention(q, k, v, scale, causal=True, causal_offset=0):
     kf = k.float().permute(0, 2, 1, 3).repeat_interleave(g, dim=1)
     vf = v.float().permute(0, 2, 1, 3).repeat_interleave(g, dim=1)
     s = (qf @ kf.transpose(-1, -2)) * scale
+    if softcap > 0:
+        s = softcap * torch.tanh(s / softcap)
+    i = torch.arange(Sq, device=q.device)[:, None]
+    j = torch.arange(Sk, device=q.device)[None, :]
     if causal:
-        i = torch.arange(Sq, device=q.device)[:, None]
-        j = torch.arange(Sk, device=q.device)[None, :]
         s = s.masked_fill(j > i + causal_offset, float("-inf"))
+    if window > 0:
+        s = s.masked_fill(j < i + causal_offset - window + 1, float("-inf"))
     lse = torch.logsumexp(s, dim=-1)
     p = torch.softmax(s, dim=-1)
     o = p @ vf

@@ -13,7 +13,10 @@
 //     adds dQ with fp32 atomics (converted to bf16 by a small epilogue kernel);
 //   * GQA is native (kv_head = q_head / group) -- no K/V copies;
 //   * `causal_offset` lets query i see keys <= i + offset (prefill on top of a
-//     KV cache).
+//     KV cache);
+//   * flex attention (forward): `window` > 0 also hides keys < i + offset -
+//     window + 1 (sliding window), `softcap` > 0 maps the scaled logits
+//     through cap * tanh(s / cap).
 // Tiles live in shared memory with a 16-byte-chunk XOR swizzle so every
 // ldmatrix is conflict-free. Matrix products use mma.sync m16n8k16 bf16.
 #include <ATen/ATen.h>
@@ -88,6 +91,8 @@ struct FwdParams {
   float scale_log2;  // softmax scale * log2(e)
   int causal;
   int causal_offset;
+  int window;            // > 0: sliding window (forward only)
+  float cap_in, cap_out;  // softcap > 0: scale / cap and cap * log2(e) (forward only)
 };
 
 // ============================================================== forward
@@ -174,16 +179,19 @@ __global__ void __launch_bounds__(256, 1) attn_fwd_kernel(FwdParams p) {
     }
     // scale + mask
     const int key0 = j * BC;
-    const bool need_mask = (key0 + BC > p.Sk) || (p.causal && key0 + BC - 1 > q0 + warp * 16 + p.causal_offset);
+    const bool need_mask = (key0 + BC > p.Sk) || (p.causal && key0 + BC - 1 > q0 + warp * 16 + p.causal_offset) ||
+                           (p.window > 0 && key0 < q0 + warp * 16 + 15 + p.causal_offset - p.window + 1);
 #pragma unroll
     for (int nt = 0; nt < BC / 8; ++nt) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float x = s[nt][e] * p.scale_log2;
+        float x = p.cap_in > 0.f ? p.cap_out * tanh_sfu(s[nt][e] * p.cap_in) : s[nt][e] * p.scale_log2;
         if (need_mask) {
           const int col = key0 + nt * 8 + 2 * t + (e & 1);
           const int row = row0 + (e >> 1) * 8;
-          if (col >= p.Sk || (p.causal && col > row + p.causal_offset)) x = -INFINITY;
+          if (col >= p.Sk || (p.causal && col > row + p.causal_offset) ||
+              (p.window > 0 && col < row + p.causal_offset - p.window + 1))
+            x = -INFINITY;
         }
         s[nt][e] = x;
       }
@@ -569,7 +577,7 @@ void check_bshd(const at::Tensor& x, int64_t H, int64_t D, const char* what) {
 // q: [B, Sq, Hq, D], k/v: [B, Sk, Hkv, D] (strided views allowed), out: [B, Sq, Hq, D].
 // lse: optional fp32 [B, Hq, Sq].
 void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
-                   double scale, bool causal, int64_t causal_offset) {
+                   double scale, bool causal, int64_t causal_offset, int64_t window, double softcap) {
   const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), D = q.size(3);
   const int64_t Sk = k.size(1), Hkv = k.size(2);
   attn::check_bshd(q, Hq, D, "attention q");
@@ -593,6 +601,11 @@ void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std
   p.scale_log2 = (float)scale * attn::kLog2e;
   p.causal = causal ? 1 : 0;
   p.causal_offset = (int)causal_offset;
+  p.window = (int)window;
+  if (softcap > 0.0) {
+    p.cap_in = (float)(scale / softcap);
+    p.cap_out = (float)softcap * attn::kLog2e;
+  }
   if (B == 0 || Sq == 0) return;
   dim3 grid((unsigned)((Sq + 127) / 128), (unsigned)(B * Hq));
   auto stream = at::cuda::getCurrentCUDAStream();

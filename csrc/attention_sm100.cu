@@ -19,7 +19,8 @@
 //
 // Reference counterpart: sdpa_causal_fwd (runtime/src/cuda.rs:6736-6786), one
 // thread per query row materialising the [bh, s, s] probability matrix.
-// Same semantics as attention.cu's attention_fwd (GQA, causal offset, LSE out).
+// Same semantics as attention.cu's attention_fwd (GQA, causal offset, LSE out,
+// sliding window and logit softcap).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -46,6 +47,8 @@ struct Params {
   int B, Hq, Hkv, Sq, Sk;
   float scale_log2;
   int causal, causal_offset;
+  int window;             // > 0: keys < row + offset - window + 1 are hidden
+  float cap_in, cap_out;  // softcap > 0: s' = cap tanh(s scale / cap), in the log2 domain
   int* status;
 };
 
@@ -235,8 +238,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld32(tS + lane_off + c * 32, r);
         tmem_ld_wait();
+        if (p.cap_in > 0.f) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(r[t]) * p.scale_log2;
+          for (int t = 0; t < 32; ++t) s[c * 32 + t] = p.cap_out * tanh_sfu(__uint_as_float(r[t]) * p.cap_in);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(r[t]) * p.scale_log2;
+        }
       }
       const int key0 = j * BN;
       const bool need_mask = (key0 + BN > p.Sk) || (p.causal && key0 + BN - 1 > qsub0 + p.causal_offset);
@@ -245,6 +253,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < BN; ++t)
           if (key0 + t >= lim) s[t] = -INFINITY;
+      }
+      if (p.window > 0) {
+        const int lo = qpos + p.causal_offset - p.window + 1;  // first visible key of this row
+        if (key0 < lo) {
+#pragma unroll
+          for (int t = 0; t < BN; ++t)
+            if (key0 + t < lo) s[t] = -INFINITY;
+        }
       }
       float mx = -INFINITY;
 #pragma unroll
@@ -351,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // [B,Sk,Hkv,128] with unit head-dim stride, head stride 128 and any token-row
 // stride that is a multiple of 8 elements; lse optional fp32 [B,Hq,Sq].
 void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
-                      double scale, bool causal, int64_t causal_offset) {
+                      double scale, bool causal, int64_t causal_offset, int64_t window, double softcap) {
   const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), D = q.size(3);
   const int64_t Sk = k.size(1), Hkv = k.size(2);
   TORCH_CHECK(D == 128 && k.size(3) == 128, "attention_fwd_tc: head_dim 128");
@@ -381,6 +397,11 @@ void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, 
   p.scale_log2 = (float)scale * fa::kLog2e;
   p.causal = causal ? 1 : 0;
   p.causal_offset = (int)causal_offset;
+  p.window = (int)window;
+  if (softcap > 0.0) {
+    p.cap_in = (float)(scale / softcap);
+    p.cap_out = (float)softcap * fa::kLog2e;
+  }
   p.status = device_status_word();
   static bool attr_set[64] = {false};
   const int dev = current_device();

@@ -43,13 +43,13 @@ void grad_norm(at::Tensor g, at::Tensor norm_out, std::optional<at::Tensor> clip
                double max_norm);
 // attention.cu
 void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
-                   double scale, bool causal, int64_t causal_offset);
+                   double scale, bool causal, int64_t causal_offset, int64_t window, double softcap);
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
                    at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset,
                    bool use_tc);
 // attention_sm100.cu
 void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
-                      double scale, bool causal, int64_t causal_offset);
+                      double scale, bool causal, int64_t causal_offset, int64_t window, double softcap);
 // gemm_skinny.cu
 void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc,
                  std::optional<at::Tensor> sig_peers, std::optional<at::Tensor> sig_epoch,
@@ -72,7 +72,8 @@ void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor 
                     std::optional<at::Tensor> page_table);
 void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slot, at::Tensor seqlen,
                       at::Tensor out, at::Tensor part_o, at::Tensor part_lse, int64_t Hq, int64_t splits,
-                      double scale, std::optional<at::Tensor> counters, std::optional<at::Tensor> page_table);
+                      double scale, std::optional<at::Tensor> counters, std::optional<at::Tensor> page_table,
+                      int64_t window, double softcap);
 void qkv_finalize_rope(at::Tensor acc, std::optional<at::Tensor> bias, at::Tensor qkv, at::Tensor pos, at::Tensor slot,
                        at::Tensor cos_t, at::Tensor sin_t, at::Tensor k_cache, at::Tensor v_cache, int64_t Hq,
                        int64_t Hkv, int64_t D, std::optional<at::Tensor> page_table);
@@ -118,10 +119,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &aether::adamw_step);
   m.def("sgd_step", &aether::sgd_step);
   m.def("grad_norm", &aether::grad_norm);
-  m.def("attention_fwd", &aether::attention_fwd);
+  m.def("attention_fwd", &aether::attention_fwd, "q"_a, "k"_a, "v"_a, "out"_a, "lse"_a, "scale"_a, "causal"_a,
+        "causal_offset"_a, "window"_a = 0, "softcap"_a = 0.0);
   m.def("attention_bwd", &aether::attention_bwd, "q"_a, "k"_a, "v"_a, "out"_a, "dout"_a, "lse"_a, "dq"_a, "dk"_a,
         "dv"_a, "scale"_a, "causal"_a, "causal_offset"_a, "use_tc"_a = false);
-  m.def("attention_fwd_tc", &aether::attention_fwd_tc);
+  m.def("attention_fwd_tc", &aether::attention_fwd_tc, "q"_a, "k"_a, "v"_a, "out"_a, "lse"_a, "scale"_a, "causal"_a,
+        "causal_offset"_a, "window"_a = 0, "softcap"_a = 0.0);
   m.def("skinny_gemm", &aether::skinny_gemm, "x"_a, "w"_a, "acc"_a, "splits"_a = 0, "acc_mc"_a = 0,
         "sig_peers"_a = pybind11::none(), "sig_epoch"_a = pybind11::none(), "sig_done"_a = pybind11::none(),
         "sig_rank"_a = 0, "sig_world"_a = 0);
@@ -136,7 +139,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
   m.def("decode_attention", &aether::decode_attention, "q"_a, "k_cache"_a, "v_cache"_a, "slot"_a, "seqlen"_a, "out"_a,
         "part_o"_a, "part_lse"_a, "Hq"_a, "splits"_a, "scale"_a, "counters"_a = pybind11::none(),
-        "page_table"_a = pybind11::none());
+        "page_table"_a = pybind11::none(), "window"_a = 0, "softcap"_a = 0.0);
   m.def("qkv_finalize_rope", &aether::qkv_finalize_rope, "acc"_a, "bias"_a, "qkv"_a, "pos"_a, "slot"_a, "cos_t"_a,
         "sin_t"_a, "k_cache"_a, "v_cache"_a, "Hq"_a, "Hkv"_a, "D"_a, "page_table"_a = pybind11::none());
   m.def("finalize_residual_norm", &aether::finalize_residual_norm, "acc"_a, "bias"_a, "res"_a, "y"_a, "w"_a, "h"_a,

@@ -130,7 +130,12 @@ struct DecParams {
   int Hq, Hkv, splits;
   float scale_log2;
   PageMap pm;  // table == nullptr: contiguous per-slot caches
+  // flex attention: window > 0 keeps the last `window` keys; cap_in > 0 soft-caps
+  // the logits, s' = cap * tanh(s * scale / cap) (cap_in = scale / cap, cap_out = cap * log2 e)
+  int window;
+  float cap_in, cap_out;
 };
+
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0) : "memory");
@@ -175,8 +180,10 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
   const uint32_t sbase = smem_u32(kv_smem);
 
   const int len = p.seqlen[b];
-  const int per = ((len + p.splits - 1) / p.splits + kKeysPerBlock - 1) / kKeysPerBlock * kKeysPerBlock;
-  const int k_begin = split * per;
+  const int lo = p.window > 0 ? max(0, len - p.window) : 0;  // sliding window: keys [lo, len)
+  const int span = len - lo;
+  const int per = ((span + p.splits - 1) / p.splits + kKeysPerBlock - 1) / kKeysPerBlock * kKeysPerBlock;
+  const int k_begin = lo + split * per;
   const int k_end = min(len, k_begin + per);
   const int nb = k_end > k_begin ? (k_end - k_begin + kKeysPerBlock - 1) / kKeysPerBlock : 0;
   const int s = p.slot[b];
@@ -252,7 +259,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int key = blk + kw + 8 * j + 2 * quad + e;
-        const float v = key < k_end ? sc[j][e] * p.scale_log2 : -INFINITY;
+        const float sv = p.cap_in > 0.f ? p.cap_out * tanh_sfu(sc[j][e] * p.cap_in) : sc[j][e] * p.scale_log2;
+        const float v = key < k_end ? sv : -INFINITY;
         x[j * 2 + e] = v;
         bm = fmaxf(bm, v);
       }
@@ -334,7 +342,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecParams p) {
   __threadfence();
   // Only the splits that own keys take part: split s covers [s * per, ...),
   // so the first ceil(len / per) are non-empty.
-  const int n_act = per > 0 ? min(p.splits, (len + per - 1) / per) : 0;
+  const int n_act = per > 0 ? min(p.splits, (span + per - 1) / per) : 0;
   // Per-split merge weights for every head of the group, computed once.
   __shared__ float s_w[kMaxGroup][kMaxSplits];
   for (int i = threadIdx.x; i < G * n_act; i += 128) {
@@ -564,7 +572,8 @@ void rope_kv_append(at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor 
 // q: [B, q_rs] (head h at h*D); out: [B, out_rs]; part buffers sized [B*Hq*splits*(D+1)].
 void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slot, at::Tensor seqlen,
                       at::Tensor out, at::Tensor part_o, at::Tensor part_lse, int64_t Hq, int64_t splits,
-                      double scale, std::optional<at::Tensor> counters, std::optional<at::Tensor> page_table) {
+                      double scale, std::optional<at::Tensor> counters, std::optional<at::Tensor> page_table,
+                      int64_t window, double softcap) {
   const int64_t B = q.size(0);
   const int64_t Hkv = k_cache.size(2), D = k_cache.size(3);
   TORCH_CHECK(D == 128, "decode_attention: head_dim 128");
@@ -593,6 +602,11 @@ void decode_attention(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.out_rs = out.stride(0);
   p.pm = page_map(page_table, k_cache);
+  p.window = (int)window;
+  if (softcap > 0.0) {
+    p.cap_in = (float)(scale / softcap);
+    p.cap_out = (float)softcap * dec::kLog2e;
+  }
   auto stream = at::cuda::getCurrentCUDAStream();
   static bool attr_set[64] = {false};
   const int dev = current_device();

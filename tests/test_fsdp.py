@@ -102,6 +102,8 @@ def _one_rank(n_layers, stage, device):
     from aether_b200.parallel.fsdp import ShardSpec
 
     cfg = dict(CFG, n_layers=n_layers)
+    if device == "cuda":  # the attention kernels take head_dim 64 or 128
+        cfg.update(d_model=128, d_ff=256)
     g = torch.Generator().manual_seed(5)
     ts = [torch.randint(0, 128, (2, 17), generator=g).to(device) for _ in range(2)]
     m1 = GPT(GPTConfig(**cfg), device=device, seed=3)
