@@ -26,6 +26,14 @@ P, I, L, Fl, U64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_uint64
 SIGNATURES = {
     # core ops
     "aether_op_matmul_f32": (I, [P, P, P, I, I, I]),
+    # chat templates and tool calls
+    "aether_template_new": (L, []),
+    "aether_template_free": (I, [L]),
+    "aether_template_set_var": (I, [L, P, I, P, I]),
+    "aether_template_push_message": (I, [L, P, I, P, I]),
+    "aether_template_render": (I, [L, P, I, P, I]),
+    "aether_template_render_from_file": (I, [L, L, I, P, I]),
+    "aether_tool_render_call": (I, [P, I, P, I, P, I]),
     # distributed layout arithmetic
     "aether_tp_simulate_column_parallel_linear_f32": (I, [P, P, P, I, I, I, I]),
     "aether_pp_simulate_2stage_forward_f32": (I, [P, P, P, P, I, I, I, I]),
@@ -224,3 +232,34 @@ def sample_batch(data: np.ndarray, B: int, S: int, rng_state: np.ndarray):
     labels = np.zeros((B, S), dtype=np.int32)
     call("aether_nano_sample_batch", ptr(data), data.size, B, S, ptr(rng_state), ptr(ids), ptr(labels))
     return ids, labels
+
+
+def render_template(template: str, messages, variables=None, max_out: int = 1 << 20) -> str:
+    """Render a chat template (the native Jinja subset) over (role, content) messages."""
+    h = call("aether_template_new")
+    try:
+        for k, v in (variables or {}).items():
+            kb, vb = k.encode(), str(v).encode()
+            if call("aether_template_set_var", h, kb, len(kb), vb, len(vb)) != 0:
+                raise ValueError(f"bad variable {k!r}")
+        for role, content in messages:
+            rb, cb = role.encode(), content.encode()
+            if call("aether_template_push_message", h, rb, len(rb), cb, len(cb)) != 0:
+                raise ValueError("bad message")
+        tb = template.encode()
+        out = C.create_string_buffer(max_out)
+        n = call("aether_template_render", h, tb, len(tb), out, max_out)
+        if n < 0:
+            raise ValueError("template render failed (malformed template or output too large)")
+        return out.raw[:n].decode()
+    finally:
+        call("aether_template_free", h)
+
+
+def render_tool_call(name: str, arguments: str, max_out: int = 1 << 16) -> str:
+    nb, ab = name.encode(), arguments.encode()
+    out = C.create_string_buffer(max_out)
+    n = call("aether_tool_render_call", nb, len(nb), ab, len(ab), out, max_out)
+    if n < 0:
+        raise ValueError("tool call render failed")
+    return out.raw[:n].decode()

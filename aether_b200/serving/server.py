@@ -41,8 +41,11 @@ class RateLimiter:
         return ok
 
 
-def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: str = "chatml",
+def build_app(engine, model_name: str = "aether-qwen", embedder=None, template="chatml",
               vision=None, rate_limit: RateLimiter | None = None) -> FastAPI:
+    """template: a built-in style name ("chatml", "llama3", ...) or a
+    ``templates.JinjaChatTemplate`` (the model's own chat template, which also
+    renders ``tools`` and tool-call turns)."""
     app = FastAPI(title="aether_b200")
 
     if rate_limit is not None:
@@ -136,7 +139,14 @@ def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: 
         messages = body.get("messages") or []
         if not messages:
             raise HTTPException(400, "messages required")
-        prompt = chat_template(messages, template)
+        tools = body.get("tools")
+        if isinstance(template, str):
+            prompt = chat_template(messages, template)
+        else:
+            try:
+                prompt = template.render(messages, tools=tools, add_generation_prompt=True)
+            except Exception as e:  # a template's raise_exception or a sandbox violation
+                raise HTTPException(400, f"chat template: {e}") from e
         ids = engine.tok.encode(prompt)
         params = SamplingParams.from_openai(body)
         try:
@@ -153,9 +163,17 @@ def build_app(engine, model_name: str = "aether-qwen", embedder=None, template: 
             return StreamingResponse(_sse(r, chunk, params.stop), media_type="text/event-stream")
         toks = await _collect(r)
         text = _trim(engine.tok.decode(toks), params.stop)
+        msg = {"role": "assistant", "content": text}
+        finish = r.finish_reason or "stop"
+        if tools:
+            from .templates import parse_tool_calls
+
+            content, calls = parse_tool_calls(text)
+            if calls:
+                msg = {"role": "assistant", "content": content or None, "tool_calls": calls}
+                finish = "tool_calls"
         return {"id": cid, "object": "chat.completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
-                             "finish_reason": r.finish_reason or "stop"}],
+                "choices": [{"index": 0, "message": msg, "finish_reason": finish}],
                 "usage": _usage(r)}
 
     @app.post("/v1/embeddings")
@@ -228,20 +246,27 @@ def main():
         cfg = presets[args.model]()
     tok = BPETokenizer.from_file(args.tokenizer) if args.tokenizer else ByteTokenizer()
     weights = None
+    template = "chatml"
     if args.gguf:
         from ..formats import gguf
+        from .templates import JinjaChatTemplate
 
         cfg, weights = gguf.load_qwen_weights(args.gguf, device=args.device)
+        g = gguf.GGUFFile(args.gguf)
         if not args.tokenizer:
-            tok = gguf.tokenizer_from_gguf(gguf.GGUFFile(args.gguf))
+            tok = gguf.tokenizer_from_gguf(g)
+        template = JinjaChatTemplate.from_gguf(g) or template
     elif args.hf:
         import os
 
         from ..formats import hf
 
+        from .templates import JinjaChatTemplate
+
         cfg, weights = hf.load_qwen_hf(args.hf, device=args.device)
         if not args.tokenizer and os.path.exists(os.path.join(args.hf, "tokenizer.json")):
             tok = BPETokenizer.from_file(os.path.join(args.hf, "tokenizer.json"))
+        template = JinjaChatTemplate.from_hf_dir(args.hf) or template
     if isinstance(cfg, MoEConfig):
         model = MoEQwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq)
     else:
@@ -258,7 +283,8 @@ def main():
 
         vision = VitEncoder(VitConfig.vitl16(), device=args.device)
     limiter = RateLimiter(args.rate_limit, max(1, int(args.rate_limit))) if args.rate_limit > 0 else None
-    app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, vision=vision, rate_limit=limiter)
+    app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, template=template, vision=vision,
+                    rate_limit=limiter)
     uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
 
 

@@ -270,3 +270,25 @@ def test_distributed_layout_abi():
     q = np.zeros_like(p)
     assert R.call("aether_fsdp_simulate_shard_alltoall_f32", R.ptr(p), R.ptr(q), 12, 4) == 0
     assert np.array_equal(p, q)
+
+
+def test_chat_template_subset_and_tool_call():
+    import json
+
+    from aether_b200 import runtime as R
+
+    tpl = ("{% for m in messages %}<|im_start|>{{ m.role }}\n{{ m.content }}<|im_end|>\n{% endfor %}"
+           "{% if add_generation_prompt %}<|im_start|>assistant\n{% endif %}")
+    msgs = [("system", "be brief"), ("user", "hi")]
+    out = R.render_template(tpl, msgs, {"add_generation_prompt": "true"})
+    assert out == "<|im_start|>system\nbe brief<|im_end|>\n<|im_start|>user\nhi<|im_end|>\n<|im_start|>assistant\n"
+    assert R.render_template(tpl, msgs, {"add_generation_prompt": "false"}).endswith("hi<|im_end|>\n")
+    assert R.render_template("[{{ missing }}]", []) == "[]"
+    for bad in ("{% for m in messages %}x", "{% endif %}", "{% while x %}{% endwhile %}", "{{ x"):
+        try:
+            R.render_template(bad, msgs)
+            raise AssertionError(bad)
+        except ValueError:
+            pass
+    call = json.loads(R.render_tool_call("get_weather", '{"city": "Paris"}'))
+    assert call == {"type": "function", "function": {"name": "get_weather", "arguments": '{"city": "Paris"}'}}

@@ -169,3 +169,43 @@ def test_rate_limiter_token_bucket():
     assert rl.allow("y")  # buckets are per client
     now[0] += 0.5  # one token back at 2/s
     assert rl.allow("x") and not rl.allow("x")
+
+
+QWEN_STYLE = (
+    "{%- if tools %}<|im_start|>system\n# Tools\n<tools>\n{%- for tool in tools %}\n{{ tool | tojson }}\n{%- endfor %}\n"
+    "</tools><|im_end|>\n{%- endif %}\n"
+    "{%- for message in messages %}\n"
+    "{%- if message.role == 'assistant' and message.tool_calls %}<|im_start|>assistant\n"
+    "{%- for tc in message.tool_calls %}<tool_call>\n{\"name\": \"{{ tc.function.name }}\", \"arguments\": "
+    "{{ tc.function.arguments }}}\n</tool_call>{%- endfor %}<|im_end|>\n"
+    "{%- elif message.role == 'tool' %}<|im_start|>user\n<tool_response>\n{{ message.content }}\n</tool_response>"
+    "<|im_end|>\n"
+    "{%- else %}<|im_start|>{{ message.role }}\n{{ message.content }}<|im_end|>\n{%- endif %}\n"
+    "{%- endfor %}\n{%- if add_generation_prompt %}<|im_start|>assistant\n{%- endif %}")
+
+
+def test_jinja_chat_template_tools_and_tool_call_parsing():
+    from aether_b200.serving.templates import JinjaChatTemplate, TemplateError, parse_tool_calls
+
+    t = JinjaChatTemplate(QWEN_STYLE)
+    tools = [{"type": "function", "function": {"name": "get_weather", "parameters": {"type": "object"}}}]
+    msgs = [{"role": "user", "content": "weather in Paris?"},
+            {"role": "assistant", "content": None,
+             "tool_calls": [{"type": "function", "function": {"name": "get_weather",
+                                                               "arguments": "{\"city\": \"Paris\"}"}}]},
+            {"role": "tool", "content": "18C"}]
+    out = t.render(msgs, tools=tools)
+    assert '"name": "get_weather"' in out and "<tool_response>\n18C" in out
+    assert out.endswith("<|im_start|>assistant")  # "{%-" also strips the newline before it
+    gen = 'Let me check.<tool_call>\n{"name": "get_weather", "arguments": {"city": "Oslo"}}\n</tool_call>'
+    content, calls = parse_tool_calls(gen)
+    assert content == "Let me check." and len(calls) == 1
+    assert calls[0]["function"]["name"] == "get_weather"
+    assert json.loads(calls[0]["function"]["arguments"]) == {"city": "Oslo"}
+    assert parse_tool_calls("no calls here") == ("no calls here", [])
+    bad = JinjaChatTemplate("{{ raise_exception('only user/assistant roles') }}")
+    with pytest.raises(TemplateError):
+        bad.render(msgs)
+    # the sandbox refuses attribute access into Python internals
+    with pytest.raises(Exception):
+        JinjaChatTemplate("{{ messages.__class__.__mro__ }}").render(msgs)
