@@ -533,18 +533,29 @@ def dequantize_blocks(q, shape, fmt=Q8_0, out=None):
 MOE_TILE = 128
 
 
-def moe_route(logits, k, softmax_all=True, renorm=False):
+def moe_route(logits, k, softmax_all=True, renorm=False, sigmoid=False, scale=1.0):
     """fp32 router logits [T, E] -> (expert ids int32 [T, k], weights fp32 [T, k]).
     softmax_all: softmax over all experts then top-k (renorm: weights / their sum);
-    otherwise softmax over the k selected logits."""
+    sigmoid: per-expert sigmoid scores then top-k (renorm likewise); otherwise
+    softmax over the k selected logits. Weights are multiplied by ``scale``."""
     T, E = logits.shape
     if _cuda(logits):
         idx = torch.empty(T, k, dtype=torch.int32, device=logits.device)
         wt = torch.empty(T, k, dtype=torch.float32, device=logits.device)
         lg = logits if logits.dtype == torch.float32 and logits.stride(1) == 1 else logits.float().contiguous()
-        C().moe_route(lg, idx, wt, int(k), bool(softmax_all), bool(renorm))
+        C().moe_route(lg, idx, wt, int(k), bool(softmax_all), bool(renorm), bool(sigmoid), float(scale))
         return idx, wt
+    idx, wt = _moe_route_cpu(logits, k, softmax_all, renorm, sigmoid)
+    return idx, wt * scale
+
+
+def _moe_route_cpu(logits, k, softmax_all, renorm, sigmoid):
     lf = logits.float()
+    if sigmoid:
+        wt, idx = torch.topk(torch.sigmoid(lf), k, dim=-1)
+        if renorm:
+            wt = wt / wt.sum(-1, keepdim=True)
+        return idx.to(torch.int32), wt
     if softmax_all:
         pr = torch.softmax(lf, -1)
         wt, idx = torch.topk(pr, k, dim=-1)
@@ -554,6 +565,48 @@ def moe_route(logits, k, softmax_all=True, renorm=False):
         top, idx = torch.topk(lf, k, dim=-1)
         wt = torch.softmax(top, -1)
     return idx.to(torch.int32), wt
+
+
+# ------------------------------------------------------------------ multi-head latent attention
+MLA_LAT, MLA_ROPE = 512, 64
+
+
+def mla_attention(q_abs, cache, slot, seqlen, out, scale, splits=1, part_o=None, part_lse=None):
+    """Absorbed MLA: q_abs [N, H, 576], latent cache [slots, max_seq, 576],
+    query n sees cache rows [0, seqlen[n]) of slot[n]; out [N, H, 512] =
+    softmax(scale q_abs . cache) cache[:, :512]."""
+    N, H, _ = q_abs.shape
+    if _cuda(q_abs):
+        if part_o is None:
+            part_o = torch.empty(N * H * splits * MLA_LAT, dtype=torch.float32, device=q_abs.device)
+            part_lse = torch.empty(N * H * splits, dtype=torch.float32, device=q_abs.device)
+        C().mla_attention(q_abs, cache, slot, seqlen, out, part_o, part_lse, int(splits), float(scale))
+        return out
+    for n in range(N):
+        L = int(seqlen[n])
+        kv = cache[int(slot[n]), :L].float()
+        pr = torch.softmax(q_abs[n].float() @ kv.t() * scale, -1)
+        out[n] = (pr @ kv[:, :MLA_LAT]).to(out.dtype)
+    return out
+
+
+def mla_prep(kv_a, norm_w, eps, q, H, q_hd, nope, pos, slot, cos_t, sin_t, cache, q_abs):
+    """Per token: cache[slot, pos] = [RMSNorm(kv_a[:512]) * w, rope(kv_a[512:576])]
+    and q_abs[:, h, 512:] = rope(q[:, h, nope:nope + 64])."""
+    if _cuda(kv_a):
+        C().mla_prep(kv_a, norm_w, float(eps), q, int(H), int(q_hd), int(nope), pos, slot, cos_t, sin_t, cache,
+                     q_abs)
+        return
+    T = kv_a.shape[0]
+    c = kv_a[:, :MLA_LAT].float()
+    c = c * torch.rsqrt(c.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float()
+    kpe = ref.rope(kv_a[:, MLA_LAT : MLA_LAT + MLA_ROPE].float().contiguous(), pos, cos_t, sin_t, 1, MLA_ROPE)
+    qpe = q.view(T, H, q_hd)[:, :, nope : nope + MLA_ROPE].float().reshape(T, H * MLA_ROPE)
+    qpe = ref.rope(qpe, pos, cos_t, sin_t, H, MLA_ROPE).view(T, H, MLA_ROPE)
+    for t in range(T):
+        cache[int(slot[t]), int(pos[t]), :MLA_LAT] = c[t].to(cache.dtype)
+        cache[int(slot[t]), int(pos[t]), MLA_LAT:] = kpe[t].to(cache.dtype)
+    q_abs[:, :, MLA_LAT:] = qpe.to(q_abs.dtype)
 
 
 def moe_rows(T, k, E):

@@ -83,7 +83,14 @@ void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std:
                             int64_t wait_rank, int64_t wait_world, double wait_timeout_s);
 // gemm_sm100.cu (grouped) and moe.cu
 void gemm_grouped(at::Tensor a, at::Tensor w, at::Tensor out, at::Tensor tile_group);
-void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool softmax_all, bool renorm);
+void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool softmax_all, bool renorm,
+               bool sigmoid, double scale);
+// mla.cu
+void mla_attention(at::Tensor q_abs, at::Tensor cache, at::Tensor slot, at::Tensor seqlen, at::Tensor out,
+                   at::Tensor part_o, at::Tensor part_lse, int64_t splits, double scale);
+void mla_prep(at::Tensor kv_a, at::Tensor norm_w, double eps, at::Tensor q, int64_t H, int64_t q_hd, int64_t nope,
+              at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t, at::Tensor cache,
+              at::Tensor q_abs);
 void moe_permute(at::Tensor idx, int64_t E, at::Tensor row_of, at::Tensor src_row, at::Tensor tile_group,
                  int64_t e0);
 void moe_gather(at::Tensor x, at::Tensor src_row, at::Tensor X);
@@ -146,7 +153,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "eps"_a, "wait_sig"_a = pybind11::none(), "wait_epoch"_a = pybind11::none(), "wait_rank"_a = 0,
         "wait_world"_a = 0, "wait_timeout_s"_a = 10.0);
   m.def("gemm_grouped", &aether::gemm_grouped, "grouped (MoE) tcgen05 GEMM over 128-row expert tiles");
-  m.def("moe_route", &aether::moe_route);
+  m.def("moe_route", &aether::moe_route, "logits"_a, "idx"_a, "wt"_a, "k"_a, "softmax_all"_a, "renorm"_a,
+        "sigmoid"_a = false, "scale"_a = 1.0);
+  m.def("mla_attention", &aether::mla_attention);
+  m.def("mla_prep", &aether::mla_prep);
   m.def("moe_permute", &aether::moe_permute, "idx"_a, "E"_a, "row_of"_a, "src_row"_a, "tile_group"_a, "e0"_a = 0);
   m.def("moe_gather", &aether::moe_gather);
   m.def("moe_combine", &aether::moe_combine);

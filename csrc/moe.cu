@@ -2,8 +2,11 @@
 //
 //   moe_route    router logits [T, E] -> top-k experts and weights per token
 //                (softmax over all experts, then top-k, optionally renormalised
-//                -- Qwen-MoE / DeepSeek style -- or softmax over the top-k
-//                logits only -- Mixtral style); one warp per token.
+//                -- Qwen-MoE / DeepSeek-V2 style -- or softmax over the top-k
+//                logits only -- Mixtral style -- or per-expert sigmoid scores,
+//                optionally renormalised -- DeepSeek-V3 / GLM-4.7-flash
+//                style); weights times a routed scaling factor; one warp per
+//                token.
 //   moe_permute  counting sort of the T*k (token, expert) pairs by expert into
 //                expert segments that start on 128-row boundaries, so every
 //                128-row GEMM tile belongs to one expert: writes the row of
@@ -34,7 +37,7 @@ constexpr int kMaxTopK = 16;
 constexpr int kTile = 128;
 
 __global__ void route_kernel(const float* __restrict__ logits, int64_t ld, int T, int E, int k, bool softmax_all,
-                             bool renorm, int* __restrict__ idx, float* __restrict__ wt) {
+                             bool renorm, bool sigmoid, float scale, int* __restrict__ idx, float* __restrict__ wt) {
   const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -51,7 +54,11 @@ __global__ void route_kernel(const float* __restrict__ logits, int64_t ld, int T
   for (int i = 0; i < PER; ++i) mx = fmaxf(mx, v[i]);
   mx = warp_max(mx);
   float denom = 1.f;
-  if (softmax_all) {
+  if (sigmoid) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (v[i] != -INFINITY) v[i] = 1.f / (1.f + __expf(-v[i]));
+  } else if (softmax_all) {
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
@@ -94,7 +101,7 @@ __global__ void route_kernel(const float* __restrict__ logits, int64_t ld, int T
   if (lane == 0) {
     float w[kMaxTopK];
     float tot = 0.f;
-    if (softmax_all) {
+    if (softmax_all || sigmoid) {
       for (int j = 0; j < k; ++j) {
         w[j] = sel_v[j];
         tot += w[j];
@@ -110,7 +117,7 @@ __global__ void route_kernel(const float* __restrict__ logits, int64_t ld, int T
     }
     for (int j = 0; j < k; ++j) {
       idx[(int64_t)t * k + j] = sel_e[j];
-      wt[(int64_t)t * k + j] = w[j];
+      wt[(int64_t)t * k + j] = w[j] * scale;
     }
   }
 }
@@ -219,7 +226,8 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ Y, int64_t ldy,
 
 }  // namespace moe
 
-void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool softmax_all, bool renorm) {
+void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool softmax_all, bool renorm,
+               bool sigmoid, double scale) {
   TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
               "moe_route: fp32 [T, E] logits (rows may be strided)");
   const int T = (int)logits.size(0), E = (int)logits.size(1);
@@ -230,7 +238,8 @@ void moe_route(at::Tensor logits, at::Tensor idx, at::Tensor wt, int64_t k, bool
   c10::cuda::CUDAGuard g(logits.device());
   if (T == 0) return;
   moe::route_kernel<<<(T + 3) / 4, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      logits.data_ptr<float>(), logits.stride(0), T, E, (int)k, softmax_all, renorm, idx.data_ptr<int>(),
+      logits.data_ptr<float>(), logits.stride(0), T, E, (int)k, softmax_all, renorm, sigmoid, (float)scale,
+      idx.data_ptr<int>(),
       wt.data_ptr<float>());
   AETHER_CUDA_CHECK(cudaGetLastError());
 }

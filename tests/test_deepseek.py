@@ -1,0 +1,108 @@
+"""DeepSeek-V2 family: absorbed multi-head latent attention against the
+standard (decompressed) MLA oracle, YaRN tables, DeepSeek MoE routing; CPU
+and the GPU kernels."""
+import math
+
+import pytest
+import torch
+
+from aether_b200.models.deepseek import DeepSeekConfig, DeepSeekModel, yarn_rope_tables
+from aether_b200.ops import functional as F
+
+TINY = dict(vocab=256, d_model=128, n_layers=2, n_heads=4, d_ff=256, first_dense=1, n_experts=8, top_k=2,
+            d_expert=64, n_shared=1, max_seq=64, init_std=0.05, yarn_factor=4.0, yarn_orig_ctx=16,
+            yarn_mscale=0.707, yarn_mscale_all_dim=0.707)
+
+
+def test_yarn_tables():
+    plain = DeepSeekConfig(**dict(TINY, yarn_factor=0.0))
+    c0, s0 = yarn_rope_tables(plain, 8)
+    assert torch.allclose(c0[:, 0], torch.cos(torch.arange(8.0)), atol=1e-6)
+    cfg = DeepSeekConfig(**TINY)
+    c, s = yarn_rope_tables(cfg, 64)
+    # the highest frequency keeps its original rate, the lowest is divided by the factor
+    assert torch.allclose(c[:, 0], c0[:, 0].new_tensor(torch.cos(torch.arange(64.0)).tolist()), atol=1e-5)
+    inv_last = 10000.0 ** (-(62 / 64))
+    assert torch.allclose(s[:8, -1], torch.sin(torch.arange(8.0) * inv_last / 4.0), atol=1e-6)
+    assert cfg.softmax_scale() > 1 / math.sqrt(192)
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(q_lora_rank=64, router="sigmoid", norm_topk=True, routed_scale=1.8)])
+def test_mla_model_matches_oracle_cpu(kw):
+    cfg = DeepSeekConfig(**dict(TINY, **kw))
+    m = DeepSeekModel(cfg, device="cpu", seed=1, max_batch=2, max_seq=64)
+    toks = torch.randint(0, 256, (2, 9), generator=torch.Generator().manual_seed(2))
+    _, logits = m.prefill(toks, return_logits=True)
+    ref = m.reference_logits(toks)[:, -1]
+    err = float((logits - ref).norm() / ref.norm())
+    assert err < 3e-2, err
+    out = m.generate(toks, 3, use_graph=False)
+    full = torch.cat([toks, out[:, :1]], 1)
+    ref2 = m.reference_logits(full)[:, -1]
+    _, l2 = DeepSeekModel(cfg, device="cpu", seed=1, max_batch=2, max_seq=64).prefill(full, return_logits=True)
+    assert float((l2 - ref2).norm() / ref2.norm()) < 3e-2
+
+
+def test_sigmoid_route_cpu():
+    lg = torch.randn(5, 8, generator=torch.Generator().manual_seed(0))
+    idx, wt = F.moe_route(lg, 3, sigmoid=True, renorm=True, scale=2.0)
+    want = torch.topk(torch.sigmoid(lg), 3, -1)
+    assert torch.equal(idx.long(), want.indices)
+    assert torch.allclose(wt, 2.0 * want.values / want.values.sum(-1, keepdim=True), atol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,splits", [(16, 1), (16, 4), (20, 3), (4, 1)])
+def test_gpu_mla_attention_matches_cpu(H, splits):
+    g = torch.Generator().manual_seed(H + splits)
+    N = 5
+    cache = (torch.randn(3, 300, 576, generator=g) * 0.5).bfloat16()
+    q = (torch.randn(N, H, 576, generator=g) * 0.5).bfloat16()
+    slot = torch.tensor([0, 2, 1, 0, 2], dtype=torch.int32)
+    seqlen = torch.tensor([300, 1, 65, 128, 200], dtype=torch.int32)
+    out = torch.empty(N, H, 512, dtype=torch.bfloat16)
+    F.mla_attention(q, cache, slot, seqlen, out, 0.07)
+    og = torch.empty(N, H, 512, dtype=torch.bfloat16, device="cuda")
+    F.mla_attention(q.cuda(), cache.cuda(), slot.cuda(), seqlen.cuda(), og, 0.07, splits=splits)
+    err = float((og.float().cpu() - out.float()).norm() / out.float().norm())
+    assert err < 1e-2, err
+
+
+@pytest.mark.gpu
+def test_gpu_mla_prep_and_sigmoid_route():
+    g = torch.Generator().manual_seed(7)
+    T, H = 6, 4
+    kv_a = torch.randn(T, 576, generator=g).bfloat16()
+    q = torch.randn(T, H * 192, generator=g).bfloat16()
+    w = torch.rand(512, generator=g) + 0.5
+    pos = torch.tensor([0, 1, 2, 5, 9, 3], dtype=torch.int32)
+    slot = torch.tensor([0, 0, 0, 1, 1, 2], dtype=torch.int32)
+    cfg = DeepSeekConfig(**TINY)
+    cos, sin = yarn_rope_tables(cfg, 16)
+    outs = []
+    for dev in ("cpu", "cuda"):
+        cache = torch.zeros(3, 16, 576, dtype=torch.bfloat16, device=dev)
+        q_abs = torch.zeros(T, H, 576, dtype=torch.bfloat16, device=dev)
+        F.mla_prep(kv_a.to(dev), w.to(dev), 1e-6, q.to(dev), H, 192, 128, pos.to(dev), slot.to(dev), cos.to(dev),
+                   sin.to(dev), cache, q_abs)
+        outs.append((cache.float().cpu(), q_abs.float().cpu()))
+    assert torch.allclose(outs[0][0], outs[1][0], atol=2e-2, rtol=2e-2)
+    assert torch.allclose(outs[0][1], outs[1][1], atol=2e-2, rtol=2e-2)
+    lg = torch.randn(33, 64, generator=g)
+    ic, wc = F.moe_route(lg, 6, sigmoid=True, renorm=True, scale=1.8)
+    ig, wg = F.moe_route(lg.cuda(), 6, sigmoid=True, renorm=True, scale=1.8)
+    assert torch.equal(ig.cpu(), ic) and torch.allclose(wg.cpu(), wc, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kw", [dict(n_heads=16), dict(n_heads=4, q_lora_rank=64, router="sigmoid", norm_topk=True)])
+def test_gpu_mla_model_prefill_and_graph_decode(kw):
+    cfg = DeepSeekConfig(**dict(TINY, d_model=256, **kw))
+    m = DeepSeekModel(cfg, device="cuda", seed=1, max_batch=2, max_seq=64)
+    toks = torch.randint(0, 256, (2, 20), generator=torch.Generator().manual_seed(2)).cuda()
+    _, logits = m.prefill(toks, return_logits=True)
+    ref = m.reference_logits(toks)[:, -1]
+    assert float((logits - ref).norm() / ref.norm()) < 3e-2
+    eager = m.generate(toks, 6, use_graph=False)
+    graph = m.generate(toks, 6, use_graph=True)
+    assert float((eager == graph).float().mean()) > 0.9
