@@ -312,3 +312,108 @@ def tokenizer_from_gguf(g: GGUFFile):
     for i, (tok, ty) in enumerate(zip(toks, types)):
         (added if ty in (3, 4) else vocab)[tok] = i
     return BPETokenizer(vocab, merges, added)
+
+
+# ---------------------------------------------------------------------------- DeepSeek-V2 / GLM-4.7-flash mapping
+def _rope_rows_to_halves(n: int = 64) -> torch.Tensor:
+    """Row order that turns interleaved RoPE pairs (0,1), (2,3), ... -- the
+    GGUF / Hugging Face layout of DeepSeek-V2's q_pe / k_pe -- into the
+    half-split pairs (i, i + n/2) the kernels rotate: dot products of q_pe and
+    k_pe are unchanged when both are reordered the same way."""
+    return torch.cat([torch.arange(0, n, 2), torch.arange(1, n, 2)])
+
+
+def deepseek_config_from_gguf(g: GGUFFile):
+    from ..models.deepseek import DeepSeekConfig
+
+    arch = g.meta.get("general.architecture", "deepseek2")
+    m = lambda k, d=None: g.meta.get(f"{arch}.{k}", d)  # noqa: E731
+    vocab = len(g.meta.get("tokenizer.ggml.tokens", [])) or int(g.tensors["token_embd.weight"][0][1])
+    H = int(m("attention.head_count"))
+    rope_d = int(m("rope.dimension_count", 64))
+    qk = int(m("attention.key_length", 192))
+    gating = int(m("expert_gating_func", 1))
+    factor = float(m("rope.scaling.factor", 0.0))
+    log_mul = float(m("rope.scaling.yarn_log_multiplier", 0.0))  # 0.1 * mscale_all_dim
+    return DeepSeekConfig(
+        vocab=vocab, d_model=int(m("embedding_length")), n_layers=int(m("block_count")), n_heads=H,
+        q_lora_rank=int(m("attention.q_lora_rank", 0)), kv_lora_rank=int(m("attention.kv_lora_rank", 512)),
+        qk_nope=qk - rope_d, qk_rope=rope_d, v_head=int(m("attention.value_length", 128)),
+        d_ff=int(m("feed_forward_length")), first_dense=int(m("leading_dense_block_count", 1)),
+        n_experts=int(m("expert_count", 0)), top_k=int(m("expert_used_count", 0)),
+        d_expert=int(m("expert_feed_forward_length", 0)), n_shared=int(m("expert_shared_count", 0)),
+        router="sigmoid" if gating == 2 else "softmax", norm_topk=bool(m("expert_weights_norm", False)),
+        routed_scale=float(m("expert_weights_scale", 1.0)), rope_theta=float(m("rope.freq_base", 10000.0)),
+        yarn_factor=factor if m("rope.scaling.type", "yarn") == "yarn" else 0.0,
+        yarn_orig_ctx=int(m("rope.scaling.original_context_length", 4096)),
+        yarn_mscale=log_mul / 0.1 if log_mul else 1.0, yarn_mscale_all_dim=log_mul / 0.1 if log_mul else 0.0,
+        norm_eps=float(m("attention.layer_norm_rms_epsilon", 1e-6)),
+        tie_embeddings="output.weight" not in g.tensors)
+
+
+def load_deepseek_weights(path: str, device="cuda"):
+    """GGUF (llama.cpp ``deepseek2`` tensor names) -> (DeepSeekConfig, DeepSeekWeights)."""
+    from ..models.deepseek import DeepSeekWeights
+
+    g = GGUFFile(path)
+    cfg = deepseek_config_from_gguf(g)
+    dev = torch.device(device)
+    t = lambda n: g.tensor(n).to(dev)  # noqa: E731
+    w = DeepSeekWeights.__new__(DeepSeekWeights)
+    w.cfg, w.device = cfg, dev
+    H, qh, nope = cfg.n_heads, cfg.qk_head, cfg.qk_nope
+    perm = _rope_rows_to_halves(cfg.qk_rope).to(dev)
+
+    def fix_q(wq):  # rows [H, qh]: reorder each head's RoPE rows
+        v = wq.view(H, qh, -1)
+        return torch.cat([v[:, :nope], v[:, nope:][:, perm]], 1).reshape(H * qh, -1).contiguous()
+
+    w.embed = t("token_embd.weight")
+    w.lm_head = w.embed if cfg.tie_embeddings else t("output.weight")
+    w.final_norm = t("output_norm.weight")
+    names = ("attn_norm", "mlp_norm", "wq", "wq_a", "q_a_norm", "wq_b", "wkv_a", "kv_norm", "w_uk", "w_uv", "wo",
+             "dense_gu", "dense_d", "router", "exp_gu", "exp_d", "sh_gu", "sh_d")
+    for n in names:
+        setattr(w, n, [])
+    for i in range(cfg.n_layers):
+        p = f"blk.{i}."
+        w.attn_norm.append(t(p + "attn_norm.weight"))
+        w.mlp_norm.append(t(p + "ffn_norm.weight"))
+        if cfg.q_lora_rank:
+            w.wq.append(None)
+            w.wq_a.append(t(p + "attn_q_a.weight"))
+            w.q_a_norm.append(t(p + "attn_q_a_norm.weight"))
+            w.wq_b.append(fix_q(t(p + "attn_q_b.weight")))
+        else:
+            w.wq.append(fix_q(t(p + "attn_q.weight")))
+            for lst in (w.wq_a, w.q_a_norm, w.wq_b):
+                lst.append(None)
+        kva = t(p + "attn_kv_a_mqa.weight")
+        w.wkv_a.append(torch.cat([kva[: cfg.kv_lora_rank], kva[cfg.kv_lora_rank :][perm]]).contiguous())
+        w.kv_norm.append(g.tensor(p + "attn_kv_a_norm.weight", torch.float32).to(dev))
+        kvb = t(p + "attn_kv_b.weight").view(H, nope + cfg.v_head, cfg.kv_lora_rank)
+        w.w_uk.append(kvb[:, :nope].contiguous())
+        w.w_uv.append(kvb[:, nope:].contiguous())
+        w.wo.append(t(p + "attn_output.weight"))
+        if i < cfg.first_dense:
+            w.dense_gu.append(torch.cat([t(p + "ffn_gate.weight"), t(p + "ffn_up.weight")]).contiguous())
+            w.dense_d.append(t(p + "ffn_down.weight"))
+            for lst in (w.router, w.exp_gu, w.exp_d, w.sh_gu, w.sh_d):
+                lst.append(None)
+            continue
+        w.dense_gu.append(None)
+        w.dense_d.append(None)
+        r = t(p + "ffn_gate_inp.weight")
+        Ep = (cfg.n_experts + 7) // 8 * 8
+        rp = torch.zeros(Ep, r.shape[1], dtype=r.dtype, device=dev)
+        rp[: cfg.n_experts] = r
+        w.router.append(rp)
+        w.exp_gu.append(torch.cat([t(p + "ffn_gate_exps.weight"), t(p + "ffn_up_exps.weight")], 1).contiguous())
+        w.exp_d.append(t(p + "ffn_down_exps.weight").contiguous())
+        if cfg.n_shared:
+            w.sh_gu.append(torch.cat([t(p + "ffn_gate_shexp.weight"), t(p + "ffn_up_shexp.weight")]).contiguous())
+            w.sh_d.append(t(p + "ffn_down_shexp.weight"))
+        else:
+            w.sh_gu.append(None)
+            w.sh_d.append(None)
+    return cfg, w

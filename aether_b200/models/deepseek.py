@@ -187,18 +187,21 @@ class DeepSeekModel:
         self.max_batch = max_batch
         self.max_seq = max_seq or cfg.max_seq
         self.scratch_slot = max_batch
+        self.paged = False  # per-slot contiguous latent caches
         # the latent cache: one 576-wide row per token for all heads
         self.cache = [torch.zeros(max_batch + 1, self.max_seq, F.MLA_LAT + F.MLA_ROPE, dtype=torch.bfloat16,
                                   device=self.device) for _ in range(cfg.n_layers)]
         self.cos, self.sin = yarn_rope_tables(cfg, self.max_seq, self.device)
         self.scale = cfg.softmax_scale()
         self.hgroups = (cfg.n_heads + 15) // 16
-        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
         B = max_batch
         self.buf = {"tok": torch.zeros(B, dtype=torch.long, device=self.device),
                     "pos": torch.zeros(B, dtype=torch.int32, device=self.device),
                     "slot": torch.arange(B, dtype=torch.int32, device=self.device),
-                    "next": torch.zeros(B, dtype=torch.long, device=self.device)}
+                    "next": torch.zeros(B, dtype=torch.long, device=self.device),
+                    "logits": torch.zeros(B, cfg.vocab, dtype=torch.float32, device=self.device)}
+        self._want_logits = False
 
     # ------------------------------------------------------------------ blocks
     def _attention(self, i: int, h: torch.Tensor, x: torch.Tensor, pos, slot, splits: int) -> torch.Tensor:
@@ -252,12 +255,14 @@ class DeepSeekModel:
 
     # ------------------------------------------------------------------ serving API
     @torch.no_grad()
-    def prefill(self, tokens: torch.Tensor, slots: torch.Tensor | None = None, return_logits: bool = False):
-        """tokens [B, S] -> greedy next token [B] (and fp32 logits [B, vocab])."""
+    def prefill(self, tokens: torch.Tensor, slots: torch.Tensor | None = None, start_pos: int = 0,
+                return_logits: bool = False):
+        """tokens [B, S] at positions start_pos.. (the cache of each slot already
+        holds the earlier ones) -> greedy next token [B] (and fp32 logits)."""
         B, S = tokens.shape
         dev = self.device
         slots = torch.arange(B, dtype=torch.int32, device=dev) if slots is None else slots.to(dev, torch.int32)
-        pos = torch.arange(S, dtype=torch.int32, device=dev).repeat(B)
+        pos = (torch.arange(S, dtype=torch.int32, device=dev) + start_pos).repeat(B)
         h = self._forward(tokens.to(dev).reshape(-1), pos, slots.repeat_interleave(S), 1)
         last = h.view(B, S, -1)[:, -1].contiguous()
         logits = F.gemm(last, self.w.lm_head, out_dtype=torch.float32)
@@ -267,7 +272,10 @@ class DeepSeekModel:
     def _decode_body(self, B: int) -> None:
         b = self.buf
         h = self._forward(b["tok"][:B], b["pos"][:B], b["slot"][:B], self._splits(B))
-        b["next"][:B].copy_(F.gemm(h, self.w.lm_head, out_dtype=torch.float32).argmax(-1))
+        logits = F.gemm(h, self.w.lm_head, out_dtype=torch.float32)
+        if self._want_logits:
+            b["logits"][:B].copy_(logits)
+        b["next"][:B].copy_(logits.argmax(-1))
 
     def _bucket(self, B: int) -> int:
         for s in (1, 2, 4, 8, 16, 32, 64):
@@ -277,7 +285,9 @@ class DeepSeekModel:
 
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor | None = None,
-                    use_graph: bool = True) -> torch.Tensor:
+                    use_graph: bool = True, want_logits: bool = False) -> torch.Tensor:
+        """tokens [B] at positions pos [B] -> greedy next tokens [B]; with
+        want_logits the fp32 logits are left in ``buf["logits"][:B]``."""
         B = tokens.shape[0]
         Bb = self._bucket(B)
         b = self.buf
@@ -289,8 +299,10 @@ class DeepSeekModel:
             b["tok"][B:Bb].zero_()
             b["pos"][B:Bb].zero_()
             b["slot"][B:Bb].fill_(self.scratch_slot)
+        self._want_logits = want_logits
         if use_graph and self.device.type == "cuda":
-            if Bb not in self._graphs:
+            key = (Bb, want_logits)
+            if key not in self._graphs:
                 s = torch.cuda.Stream(self.device)
                 s.wait_stream(torch.cuda.current_stream(self.device))
                 with torch.cuda.stream(s):
@@ -300,10 +312,11 @@ class DeepSeekModel:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, capture_error_mode="thread_local"):
                     self._decode_body(Bb)
-                self._graphs[Bb] = g
-            self._graphs[Bb].replay()
+                self._graphs[key] = g
+            self._graphs[key].replay()
         else:
             self._decode_body(Bb)
+        self._want_logits = False
         return b["next"][:B]
 
     @torch.no_grad()

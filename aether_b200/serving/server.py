@@ -216,7 +216,8 @@ def build_app(engine, model_name: str = "aether-qwen", embedder=None, template="
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="1.5b",
-                    choices=["1.5b", "7b", "qwen3-8b", "llama3-8b", "mistral-7b", "qwen2-moe", "mixtral", "tiny"])
+                    choices=["1.5b", "7b", "qwen3-8b", "llama3-8b", "mistral-7b", "mistral-7b-v0.1", "qwen2-moe",
+                             "mixtral", "deepseek-v2-lite", "tiny"])
     ap.add_argument("--tokenizer", default=None, help="tokenizer.json (default: byte tokenizer)")
     ap.add_argument("--max-concurrent", type=int, default=8)
     ap.add_argument("--max-seq", type=int, default=4096)
@@ -237,9 +238,12 @@ def main():
 
     from ..models.moe import MoEConfig, MoEQwenModel
 
+    from ..models.deepseek import DeepSeekConfig, DeepSeekModel
+
     presets = {"7b": QwenConfig.qwen25_7b, "qwen3-8b": QwenConfig.qwen3_8b, "llama3-8b": QwenConfig.llama3_8b,
-               "mistral-7b": QwenConfig.mistral_7b, "qwen2-moe": MoEConfig.qwen2_moe_a2_7b,
-               "mixtral": MoEConfig.mixtral_8x7b, "1.5b": QwenConfig.qwen25_1_5b}
+               "mistral-7b": QwenConfig.mistral_7b, "mistral-7b-v0.1": QwenConfig.mistral_7b_v01,
+               "qwen2-moe": MoEConfig.qwen2_moe_a2_7b, "mixtral": MoEConfig.mixtral_8x7b,
+               "deepseek-v2-lite": DeepSeekConfig.deepseek_v2_lite, "1.5b": QwenConfig.qwen25_1_5b}
     if args.model == "tiny":
         cfg = QwenConfig(vocab=1024, d_model=256, n_layers=2, n_heads=2, n_kv_heads=1, d_ff=512, max_seq=args.max_seq)
     else:
@@ -251,8 +255,11 @@ def main():
         from ..formats import gguf
         from .templates import JinjaChatTemplate
 
-        cfg, weights = gguf.load_qwen_weights(args.gguf, device=args.device)
         g = gguf.GGUFFile(args.gguf)
+        if g.meta.get("general.architecture") == "deepseek2":  # DeepSeek-V2 / GLM-4.7-flash (MLA + MoE)
+            cfg, weights = gguf.load_deepseek_weights(args.gguf, device=args.device)
+        else:
+            cfg, weights = gguf.load_qwen_weights(args.gguf, device=args.device)
         if not args.tokenizer:
             tok = gguf.tokenizer_from_gguf(g)
         template = JinjaChatTemplate.from_gguf(g) or template
@@ -267,7 +274,10 @@ def main():
         if not args.tokenizer and os.path.exists(os.path.join(args.hf, "tokenizer.json")):
             tok = BPETokenizer.from_file(os.path.join(args.hf, "tokenizer.json"))
         template = JinjaChatTemplate.from_hf_dir(args.hf) or template
-    if isinstance(cfg, MoEConfig):
+    if isinstance(cfg, DeepSeekConfig):
+        model = DeepSeekModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq,
+                              weights=weights)
+    elif isinstance(cfg, MoEConfig):
         model = MoEQwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq)
     else:
         model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq,

@@ -106,3 +106,84 @@ def test_gpu_mla_model_prefill_and_graph_decode(kw):
     eager = m.generate(toks, 6, use_graph=False)
     graph = m.generate(toks, 6, use_graph=True)
     assert float((eager == graph).float().mean()) > 0.9
+
+
+def test_deepseek_gguf_roundtrip(tmp_path):
+    """A deepseek2 GGUF written with llama.cpp tensor names and interleaved
+    RoPE rows loads back into the same model (same logits)."""
+    from aether_b200.formats import gguf as G
+
+    cfg = DeepSeekConfig(**dict(TINY, q_lora_rank=64, router="sigmoid", norm_topk=True, routed_scale=1.5))
+    m = DeepSeekModel(cfg, device="cpu", seed=3, max_batch=2, max_seq=64)
+    w = m.w
+    inv = torch.argsort(G._rope_rows_to_halves(64))  # back to interleaved rows
+
+    def unfix_q(wq):
+        v = wq.view(cfg.n_heads, cfg.qk_head, -1)
+        return torch.cat([v[:, : cfg.qk_nope], v[:, cfg.qk_nope :][:, inv]], 1).reshape(wq.shape)
+
+    T = {"token_embd.weight": w.embed, "output_norm.weight": w.final_norm, "output.weight": w.lm_head}
+    for i in range(cfg.n_layers):
+        p = f"blk.{i}."
+        T[p + "attn_norm.weight"] = w.attn_norm[i]
+        T[p + "ffn_norm.weight"] = w.mlp_norm[i]
+        T[p + "attn_q_a.weight"] = w.wq_a[i]
+        T[p + "attn_q_a_norm.weight"] = w.q_a_norm[i]
+        T[p + "attn_q_b.weight"] = unfix_q(w.wq_b[i])
+        T[p + "attn_kv_a_mqa.weight"] = torch.cat([w.wkv_a[i][:512], w.wkv_a[i][512:][inv]])
+        T[p + "attn_kv_a_norm.weight"] = w.kv_norm[i]
+        T[p + "attn_kv_b.weight"] = torch.cat([w.w_uk[i], w.w_uv[i]], 1).reshape(-1, 512)
+        T[p + "attn_output.weight"] = w.wo[i]
+        if i < cfg.first_dense:
+            g_, u_ = w.dense_gu[i].chunk(2)
+            T[p + "ffn_gate.weight"], T[p + "ffn_up.weight"], T[p + "ffn_down.weight"] = g_, u_, w.dense_d[i]
+        else:
+            T[p + "ffn_gate_inp.weight"] = w.router[i][: cfg.n_experts]
+            g_, u_ = w.exp_gu[i].chunk(2, 1)
+            T[p + "ffn_gate_exps.weight"], T[p + "ffn_up_exps.weight"] = g_, u_
+            T[p + "ffn_down_exps.weight"] = w.exp_d[i]
+            g_, u_ = w.sh_gu[i].chunk(2)
+            T[p + "ffn_gate_shexp.weight"], T[p + "ffn_up_shexp.weight"] = g_, u_
+            T[p + "ffn_down_shexp.weight"] = w.sh_d[i]
+    a = "deepseek2."
+    meta = {"general.architecture": "deepseek2", a + "block_count": cfg.n_layers, a + "embedding_length": 128,
+            a + "feed_forward_length": cfg.d_ff, a + "attention.head_count": cfg.n_heads,
+            a + "attention.q_lora_rank": 64, a + "attention.kv_lora_rank": 512, a + "attention.key_length": 192,
+            a + "attention.value_length": 128, a + "rope.dimension_count": 64, a + "leading_dense_block_count": 1,
+            a + "expert_count": 8, a + "expert_used_count": 2, a + "expert_feed_forward_length": 64,
+            a + "expert_shared_count": 1, a + "expert_gating_func": 2, a + "expert_weights_norm": True,
+            a + "expert_weights_scale": 1.5, a + "rope.freq_base": 10000.0, a + "rope.scaling.type": "yarn",
+            a + "rope.scaling.factor": 4.0, a + "rope.scaling.original_context_length": 16,
+            a + "rope.scaling.yarn_log_multiplier": 0.0707, a + "attention.layer_norm_rms_epsilon": 1e-6}
+    path = str(tmp_path / "ds.gguf")
+    G.write_gguf(path, meta, {k: (v, G.F32) for k, v in T.items()})
+    cfg2, w2 = G.load_deepseek_weights(path, device="cpu")
+    assert (cfg2.q_lora_rank, cfg2.router, cfg2.routed_scale, cfg2.n_shared) == (64, "sigmoid", 1.5, 1)
+    assert abs(cfg2.yarn_mscale_all_dim - 0.707) < 1e-4 and cfg2.yarn_factor == 4.0
+    m2 = DeepSeekModel(cfg2, device="cpu", max_batch=2, max_seq=64, weights=w2)
+    toks = torch.randint(0, 256, (2, 7), generator=torch.Generator().manual_seed(5))
+    _, l1 = m.prefill(toks, return_logits=True)
+    _, l2 = m2.prefill(toks, return_logits=True)
+    assert float((l1 - l2).norm() / l1.norm()) < 1e-2
+
+
+def test_engine_serves_mla_model_cpu():
+    """The continuous-batching engine drives the MLA model (prefill per slot, batched decode)."""
+    from aether_b200.serving.engine import Engine
+    from aether_b200.serving.sampling import SamplingParams
+    from aether_b200.serving.tokenizer import ByteTokenizer
+
+    cfg = DeepSeekConfig(**TINY)
+    m = DeepSeekModel(cfg, device="cpu", seed=1, max_batch=2, max_seq=64)
+    eng = Engine(m, ByteTokenizer(), max_concurrent=2, use_graph=False)
+    try:
+        rs = [eng.submit(list(b"hello"), SamplingParams(max_tokens=4)),
+              eng.submit(list(b"abc"), SamplingParams(max_tokens=3, temperature=0.7, seed=1))]
+        for r in rs:  # each request streams its tokens, then None
+            while r.out.get(timeout=120) is not None:
+                pass
+        assert len(rs[0].tokens) == 4 and len(rs[1].tokens) == 3
+        want = m.generate(torch.tensor([list(b"hello")]), 4, use_graph=False)[0].tolist()
+        assert rs[0].tokens == want
+    finally:
+        eng.shutdown()
