@@ -31,8 +31,15 @@ _SCALAR = {T_U8: "<B", T_I8: "<b", T_U16: "<H", T_I16: "<h", T_U32: "<I", T_I32:
            T_U64: "<Q", T_I64: "<q", T_F64: "<d"}
 
 F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 14, 30
+Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, IQ4_NL, IQ4_XS = 3, 6, 7, 10, 11, 13, 20, 23
+# (block elements, block bytes) of every type the load-time dequantiser reads
+BLOCKS = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24),
+          Q8_0: (32, 34), Q2_K: (256, 84), Q3_K: (256, 110), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
+          IQ4_NL: (32, 18), IQ4_XS: (256, 136)}
+# the 16 non-uniform levels of the IQ4_NL / IQ4_XS formats
+IQ4_LEVELS = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.float32)
 # (block elements, block bytes)
-_BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_0: (32, 18), Q4_K: (256, 144), Q6_K: (256, 210)}
+_BLOCK = BLOCKS
 
 
 class GGUFFile:
@@ -164,7 +171,122 @@ def dequantize(buf: np.ndarray, typ: int, n: int) -> np.ndarray:
                     si = half * 8 + part * 2 + sub
                     out[:, base + sub * 16 : base + sub * 16 + 16] = d * scales[:, si : si + 1] * q[:, sub * 16 : sub * 16 + 16]
         return out.reshape(-1)[:n]
+    if typ in (Q4_1, Q5_0, Q5_1, IQ4_NL):
+        return _dequant_32(buf, typ)[:n]
+    if typ in (Q2_K, Q3_K, Q5_K, IQ4_XS):
+        return _dequant_k(buf, typ)[:n]
     raise NotImplementedError(f"GGUF tensor type {typ} is not supported by the load-time dequantiser")
+
+
+def _k4_scales(sc: np.ndarray):
+    """The 8 six-bit (scale, min) pairs packed in 12 bytes (Q4_K / Q5_K)."""
+    sc = sc.astype(np.uint32)
+    scales = np.empty((sc.shape[0], 8), np.float32)
+    mins = np.empty((sc.shape[0], 8), np.float32)
+    for j in range(8):
+        if j < 4:
+            s_, m_ = sc[:, j] & 63, sc[:, j + 4] & 63
+        else:
+            s_ = (sc[:, j + 4] & 0x0F) | ((sc[:, j - 4] >> 6) << 4)
+            m_ = (sc[:, j + 4] >> 4) | ((sc[:, j] >> 6) << 4)
+        scales[:, j], mins[:, j] = s_, m_
+    return scales, mins
+
+
+def _dequant_32(buf: np.ndarray, typ: int) -> np.ndarray:
+    """32-element blocks: Q4_1 (d, m, nibbles), Q5_0 (d, 32 high bits, nibbles;
+    offset 16), Q5_1 (d, m, high bits, nibbles), IQ4_NL (d, nibbles indexing
+    the 16 IQ4 levels). Nibble j of byte i is element i (low) / i + 16 (high)."""
+    ne, nb = BLOCKS[typ]
+    b = buf.reshape(-1, nb)
+    d = _f16(b[:, 0:2].copy())
+    if typ == IQ4_NL:
+        qs = b[:, 2:18]
+        q = np.concatenate([qs & 0x0F, qs >> 4], axis=1)
+        return (IQ4_LEVELS[q] * d).reshape(-1)
+    has_m = typ in (Q4_1, Q5_1)
+    m = _f16(b[:, 2:4].copy()) if has_m else 0.0
+    o = 4 if has_m else 2
+    if typ == Q4_1:
+        qs = b[:, o : o + 16]
+        q = np.concatenate([qs & 0x0F, qs >> 4], axis=1).astype(np.float32)
+        return (q * d + m).reshape(-1)
+    qh = b[:, o : o + 4].copy().view(np.uint32)  # [blocks, 1]
+    qs = b[:, o + 4 : o + 20]
+    bits = (qh >> np.arange(32, dtype=np.uint32)[None, :]) & 1  # bit j -> element j
+    q = np.concatenate([qs & 0x0F, qs >> 4], axis=1).astype(np.uint32) | (bits << 4)
+    q = q.astype(np.float32)
+    if typ == Q5_0:
+        return ((q - 16.0) * d).reshape(-1)
+    return (q * d + m).reshape(-1)
+
+
+def _dequant_k(buf: np.ndarray, typ: int) -> np.ndarray:
+    """256-element super-blocks: Q2_K, Q3_K, Q5_K, IQ4_XS."""
+    ne, nb = BLOCKS[typ]
+    b = buf.reshape(-1, nb)
+    nbk = b.shape[0]
+    out = np.empty((nbk, 256), np.float32)
+    if typ == Q2_K:
+        # scales[16] (low nibble scale, high nibble min), qs[64] (2 bits), d, dmin
+        sc, qs = b[:, 0:16], b[:, 16:80]
+        d, dmin = _f16(b[:, 80:82].copy()), _f16(b[:, 82:84].copy())
+        dl = d * (sc & 0x0F).astype(np.float32)
+        ml = dmin * (sc >> 4).astype(np.float32)
+        for half in range(2):
+            q = qs[:, half * 32 : half * 32 + 32]
+            for j in range(4):  # shift 2j
+                v = ((q >> (2 * j)) & 3).astype(np.float32)
+                for part in range(2):
+                    si = half * 8 + j * 2 + part
+                    o = half * 128 + j * 32 + part * 16
+                    out[:, o : o + 16] = dl[:, si : si + 1] * v[:, part * 16 : part * 16 + 16] - ml[:, si : si + 1]
+        return out.reshape(-1)
+    if typ == Q3_K:
+        # hmask[32] (third bit, 0 means -4), qs[64] (low 2 bits), 16 six-bit scales in 12 bytes, d
+        hm, qs, sb = b[:, 0:32], b[:, 32:96], b[:, 96:108].astype(np.uint32)
+        d = _f16(b[:, 108:110].copy())
+        a = [sb[:, 4 * i] | (sb[:, 4 * i + 1] << 8) | (sb[:, 4 * i + 2] << 16) | (sb[:, 4 * i + 3] << 24)
+             for i in range(3)]
+        k1, k2 = np.uint32(0x03030303), np.uint32(0x0F0F0F0F)
+        words = [(a[0] & k2) | (((a[2] >> 0) & k1) << 4), (a[1] & k2) | (((a[2] >> 2) & k1) << 4),
+                 ((a[0] >> 4) & k2) | (((a[2] >> 4) & k1) << 4), ((a[1] >> 4) & k2) | (((a[2] >> 6) & k1) << 4)]
+        scales = np.stack([((w >> (8 * k)) & 0xFF) for w in words for k in range(4)], 1).astype(np.float32) - 32.0
+        for half in range(2):
+            q = qs[:, half * 32 : half * 32 + 32]
+            for j in range(4):
+                m = 1 << (half * 4 + j)
+                v = ((q >> (2 * j)) & 3).astype(np.float32) - np.where(hm & m, 0.0, 4.0)
+                for part in range(2):
+                    si = half * 8 + j * 2 + part
+                    o = half * 128 + j * 32 + part * 16
+                    out[:, o : o + 16] = d * scales[:, si : si + 1] * v[:, part * 16 : part * 16 + 16]
+        return out.reshape(-1)
+    if typ == Q5_K:
+        d, dmin = _f16(b[:, 0:2].copy()), _f16(b[:, 2:4].copy())
+        scales, mins = _k4_scales(b[:, 4:16])
+        qh, qs = b[:, 16:48], b[:, 48:176]
+        for g in range(4):
+            q = qs[:, g * 32 : g * 32 + 32]
+            lo = (q & 0x0F).astype(np.float32) + np.where(qh & (1 << (2 * g)), 16.0, 0.0)
+            hi = (q >> 4).astype(np.float32) + np.where(qh & (1 << (2 * g + 1)), 16.0, 0.0)
+            out[:, g * 64 : g * 64 + 32] = d * scales[:, 2 * g : 2 * g + 1] * lo - dmin * mins[:, 2 * g : 2 * g + 1]
+            out[:, g * 64 + 32 : g * 64 + 64] = (d * scales[:, 2 * g + 1 : 2 * g + 2] * hi
+                                                 - dmin * mins[:, 2 * g + 1 : 2 * g + 2])
+        return out.reshape(-1)
+    if typ == IQ4_XS:
+        # d, scales_h (u16: 2 high bits per sub-block), scales_l[4] (nibbles), qs[128]
+        d = _f16(b[:, 0:2].copy())
+        sh = b[:, 2:4].copy().view(np.uint16).astype(np.uint32)
+        sl, qs = b[:, 4:8], b[:, 8:136]
+        for ib in range(8):
+            ls = ((sl[:, ib // 2] >> (4 * (ib % 2))) & 0x0F).astype(np.uint32) | (((sh[:, 0] >> (2 * ib)) & 3) << 4)
+            dl = d[:, 0] * (ls.astype(np.float32) - 32.0)
+            q = qs[:, ib * 16 : ib * 16 + 16]
+            out[:, ib * 32 : ib * 32 + 16] = dl[:, None] * IQ4_LEVELS[q & 0x0F]
+            out[:, ib * 32 + 16 : ib * 32 + 32] = dl[:, None] * IQ4_LEVELS[q >> 4]
+        return out.reshape(-1)
+    raise NotImplementedError(typ)
 
 
 # ---------------------------------------------------------------------------- writer

@@ -81,6 +81,7 @@ SIGNATURES = {
     "aether_dequant_q8_0": (I, [P, P, I]),
     "aether_dequant_q4_k_m": (I, [P, P, I]),
     "aether_dequant_q6_k": (I, [P, P, I]),
+    "aether_dequant_q3_k": (I, [P, P, I]),
     # serving structures
     "aether_pkv_new": (L, [I, I]),
     "aether_pkv_destroy": (I, [L]),

@@ -575,6 +575,34 @@ AE_API int aether_dequant_q6_k(const void* blocks, void* out, int n_blocks) {
   return 0;
 }
 
+// Q3_K super-block (256 values): 32 bytes of third bits (a clear bit
+// subtracts 4), 64 bytes of 2-bit values, 16 six-bit scales (low nibbles in
+// bytes 0..7, high bit pairs in bytes 8..11, offset 32), f16 d. Value e of
+// 128-value half h, pair-shift j, sub-block s uses scale h*8 + j*2 + s.
+AE_API int aether_dequant_q3_k(const void* blocks, void* out, int n_blocks) {
+  if (!blocks || !out) return 1;
+  if (n_blocks <= 0) return 2;
+  const uint8_t* b = static_cast<const uint8_t*>(blocks);
+  for (int i = 0; i < n_blocks; ++i, b += 110) {
+    const uint8_t* hm = b;
+    const uint8_t* qs = b + 32;
+    const uint8_t* raw = b + 96;
+    const float d = half_at(b + 108);
+    int sc[16];
+    for (int k = 0; k < 16; ++k)
+      sc[k] = (((raw[k % 8] >> (4 * (k / 8))) & 0xf) | (((raw[8 + k % 4] >> (2 * (k / 4))) & 3) << 4)) - 32;
+    float* o = F(out) + (size_t)i * 256;
+    for (int half = 0; half < 2; ++half)
+      for (int j = 0; j < 4; ++j)
+        for (int l = 0; l < 32; ++l) {
+          int q = (qs[half * 32 + l] >> (2 * j)) & 3;
+          if (!((hm[l] >> (half * 4 + j)) & 1)) q -= 4;
+          o[half * 128 + j * 32 + l] = d * (float)sc[half * 8 + j * 2 + l / 16] * (float)q;
+        }
+  }
+  return 0;
+}
+
 // ------------------------------------------------------------------ paged-KV block pool + page tables
 struct Pool {
   std::vector<uint8_t> used;
