@@ -589,10 +589,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&dq_read[s]);  // the TMEM columns may now take the next dP^T
       if (lane == 0) bulk_wait_read<0>();  // the previous reduce has read this slab
       __syncwarp();
-      // slab: 32 query rows x 32 head dims (128 B), 16 B granules XOR (row & 7)
+      // slab: 32 query rows x 32 head dims (128 B), 16 B granules XOR (row & 7);
+      // the eight per-lane granule offsets are computed once
+      uint32_t* gofs[8];
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
-        *reinterpret_cast<uint32_t*>(slab + t * 128 + (((lane >> 2) ^ (t & 7)) << 4) + (lane & 3) * 4) = rq[t];
+      for (int g8 = 0; g8 < 8; ++g8)
+        gofs[g8] = reinterpret_cast<uint32_t*>(slab + ((((lane >> 2) ^ g8)) << 4) + (lane & 3) * 4);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) gofs[t & 7][t * 32] = rq[t];
       fence_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -640,13 +644,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tS + lane_off + half * 32, rs);
       tmem_ld_wait();
       float pv[32];
+      // this thread's 32 queries are q0 + half*32 + [0, 32); visible ones form [lo, hi)
+      const int qb = q0 + half * 32;
+      const int lo = p.causal ? key - p.causal_offset - qb : 0;  // first visible (causal)
+      const int hi = key < p.Sk ? p.Sq - qb : 0;                    // past the last query
+      const float4* l4 = reinterpret_cast<const float4*>(lse_s + half * 32);
+      if (lo <= 0 && hi >= 32) {  // the whole row chunk is visible: no per-element masks
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const int ql = half * 32 + t;
-        const int q = q0 + ql;
-        bool valid = q < p.Sq && key < p.Sk;
-        if (p.causal && key > q + p.causal_offset) valid = false;
-        pv[t] = valid ? ex2_sfu(__uint_as_float(rs[t]) * p.scale_log2 - lse_s[ql]) : 0.f;
+        for (int t4 = 0; t4 < 8; ++t4) {
+          const float4 l = l4[t4];
+          pv[4 * t4 + 0] = ex2_sfu(__uint_as_float(rs[4 * t4 + 0]) * p.scale_log2 - l.x);
+          pv[4 * t4 + 1] = ex2_sfu(__uint_as_float(rs[4 * t4 + 1]) * p.scale_log2 - l.y);
+          pv[4 * t4 + 2] = ex2_sfu(__uint_as_float(rs[4 * t4 + 2]) * p.scale_log2 - l.z);
+          pv[4 * t4 + 3] = ex2_sfu(__uint_as_float(rs[4 * t4 + 3]) * p.scale_log2 - l.w);
+        }
+      } else {
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4) {
+          const float4 l = l4[t4];
+          const float lv[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int t = 4 * t4 + u;
+            pv[t] = (t >= lo && t < hi) ? ex2_sfu(__uint_as_float(rs[t]) * p.scale_log2 - lv[u]) : 0.f;
+          }
+        }
       }
 #pragma unroll
       for (int t = 0; t < 32; t += 2) pp[t / 2] = pack_bf16(pv[t], pv[t + 1]);
@@ -660,10 +682,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t rd[32], pd[16];
       tmem_ld32(tDP + lane_off + half * 32, rd);
       tmem_ld_wait();
+      const float4* d4 = reinterpret_cast<const float4*>(dsum_s + half * 32);
 #pragma unroll
-      for (int t = 0; t < 32; t += 2)
-        pd[t / 2] = pack_bf16(pv[t] * (__uint_as_float(rd[t]) - dsum_s[half * 32 + t]),
-                              pv[t + 1] * (__uint_as_float(rd[t + 1]) - dsum_s[half * 32 + t + 1]));
+      for (int t4 = 0; t4 < 8; ++t4) {
+        const float4 d = d4[t4];
+        const int t = 4 * t4;
+        pd[t / 2] = pack_bf16(pv[t] * (__uint_as_float(rd[t]) - d.x), pv[t + 1] * (__uint_as_float(rd[t + 1]) - d.y));
+        pd[t / 2 + 1] =
+            pack_bf16(pv[t + 2] * (__uint_as_float(rd[t + 2]) - d.z), pv[t + 3] * (__uint_as_float(rd[t + 3]) - d.w));
+      }
       tmem_st16b(tDP + lane_off + half * 32, pd);
       // dS^T row (this key) into the [128 keys][64 queries] tile: 16 B granules XOR (r & 7)
       uint8_t* dst = sDS + s * DSTILE + r * 128;
