@@ -120,6 +120,14 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __nv_bfl
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  // dw: a lane owns the same columns in every row, so up to 2048 wide the
+  // partial sums stay in registers and meet in shared memory once per CTA
+  constexpr bool kRegDw = VPT <= 8;
+  float dwr[kRegDw ? VPT : 1][8];
+#pragma unroll
+  for (int i = 0; i < (kRegDw ? VPT : 1); ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwr[i][j] = 0.f;
   for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
     uint4 rx[VPT], rg[VPT];
     load_raw<VPT>(x + (int64_t)row * d, d, lane, rx);
@@ -137,7 +145,11 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __nv_bfl
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float xh = a[j] * rs;
-          atomicAdd(&sdw[c + j], g[j] * xh);
+          if constexpr (kRegDw) {
+            dwr[i][j] += g[j] * xh;
+          } else {
+            atomicAdd(&sdw[c + j], g[j] * xh);
+          }
           dot += g[j] * wv[j] * xh;
         }
       }
@@ -160,6 +172,16 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const __nv_bfl
           for (int j = 0; j < 8; ++j) g[j] += q[j];
         }
         *reinterpret_cast<uint4*>(dx + (int64_t)row * d + c) = pack8(g);
+      }
+    }
+  }
+  if constexpr (kRegDw) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < d) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) atomicAdd(&sdw[c + j], dwr[i][j]);
       }
     }
   }
