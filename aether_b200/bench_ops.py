@@ -119,6 +119,46 @@ def bench_sdpa(iters):
         torch.cuda.empty_cache()
 
 
+def bench_attn_bwd(iters):
+    """The flash-attention backward call at the profiled shape (B 2, H 16, S 4096,
+    D 128, causal): dsum kernel + tcgen05 backward + dQ convert."""
+    hbm, tf, src = peaks()
+    B, H, S, D = 2, 16, 4096, 128
+    q, k, v, do = (torch.randn(B, S, H, D, device="cuda").bfloat16() for _ in range(4))
+    sc = D ** -0.5
+    o, lse = F.attention(q, k, v, sc, True, impl="tc")
+    t = time_fn(lambda: F.attention_bwd(q, k, v, o, do, lse, sc, True, impl="tc"), max(iters, 20))
+    fl = 2.5 * 4 * B * H * S * S * D / 2
+    emit({"op": "attention_bwd_call", "shape": [B, S, H, D], "ms": t, "tflops": fl / t / 1e9,
+          "frac_of_peak": fl / t / 1e9 / tf, "peak": src})
+
+
+def bench_rms_bwd(iters):
+    """RMSNorm backward at the GPT-24L training rows (micro-batch 8 x 2048, d 2048)."""
+    hbm, tf, src = peaks()
+    R, Dm = 8 * 2048, 2048
+    x = torch.randn(R, Dm, device="cuda").bfloat16()
+    w = torch.randn(Dm, device="cuda").bfloat16()
+    dy = torch.randn_like(x)
+    _, h, rstd = F.rmsnorm(x, w)
+    dw = torch.zeros(Dm, device="cuda")
+    t = time_fn(lambda: F.rmsnorm_bwd(dy, h, w, rstd, dw), iters)
+    nb = 3 * R * Dm * 2
+    emit({"op": "rms_norm_bwd", "shape": [R, Dm], "ms": t, "gbs": nb / t / 1e6, "frac_of_hbm": nb / t / 1e6 / hbm,
+          "peak": src})
+    # LayerNorm backward at the encoder width (BERT-large / ViT-L, d 1024)
+    R2, D2 = 16384, 1024
+    x2 = torch.randn(R2, D2, device="cuda").bfloat16()
+    w2, b2 = torch.randn(D2, device="cuda").bfloat16(), torch.randn(D2, device="cuda").bfloat16()
+    _, _, mean2, rstd2 = F.layernorm(x2, w2, b2)
+    dy2 = torch.randn_like(x2)
+    dw2, db2 = torch.zeros(D2, device="cuda"), torch.zeros(D2, device="cuda")
+    t = time_fn(lambda: F.layernorm_bwd(dy2, x2, w2, mean2, rstd2, dw2, db2), iters)
+    nb = 3 * R2 * D2 * 2
+    emit({"op": "layer_norm_bwd", "shape": [R2, D2], "ms": t, "gbs": nb / t / 1e6, "frac_of_hbm": nb / t / 1e6 / hbm,
+          "peak": src})
+
+
 def bench_rows(iters):
     hbm, tf, src = peaks()
     R, Dm = 8 * 2048, 4096
@@ -200,13 +240,13 @@ def bench_adamw(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default="gemm,sdpa,rows,ce,adamw")
+    ap.add_argument("--only", default="gemm,sdpa,attn_bwd,rows,rms_bwd,ce,adamw")
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args()
     _ext.C()
     sel = set(args.only.split(","))
-    for name, fn in (("gemm", bench_gemm), ("sdpa", bench_sdpa), ("rows", bench_rows), ("ce", bench_ce),
-                     ("adamw", bench_adamw)):
+    for name, fn in (("gemm", bench_gemm), ("sdpa", bench_sdpa), ("attn_bwd", bench_attn_bwd), ("rows", bench_rows),
+                     ("rms_bwd", bench_rms_bwd), ("ce", bench_ce), ("adamw", bench_adamw)):
         if name in sel:
             fn(args.iters)
             torch.cuda.empty_cache()

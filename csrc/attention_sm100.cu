@@ -25,6 +25,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
+#include <string>
+
 #include "common.cuh"
 #include "host_utils.h"
 
@@ -70,6 +73,27 @@ __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, 
   tma_load_2d(dst + TILE_BYTES / 2, map, bar, x0 + 64, y0);
 }
 
+// 2^x on the SFU (ex2.approx.ftz.f32); probabilities are rounded to bf16 next.
+__device__ __forceinline__ float ex2_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x for x <= 0 on the FMA / integer pipes, so the softmax is not bound by
+// the SFU's 16 results per clock: x = n + f with n = round(x) taken from the
+// low mantissa bits of x + 1.5 * 2^23, 2^f for f in [-0.5, 0.5] from a cubic
+// fitted here (least squares reweighted to the minimax relative error,
+// max 1.0e-4 -- bf16 keeps 2^-9), and n added to the exponent field.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.055008791f, f, 0.24221075f), f, 0.69328290f), f, 1.f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+template <bool kPoly>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, Params p) {
@@ -262,20 +286,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (key0 + t < lo) s[t] = -INFINITY;
         }
       }
-      float mx = -INFINITY;
+      // row max and sum over eight independent accumulators (a single chain
+      // would serialise 128 dependent max / 64 dependent adds per tile)
+      float m8[8];
 #pragma unroll
-      for (int t = 0; t < BN; ++t) mx = fmaxf(mx, s[t]);
+      for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < BN; ++t) m8[t & 7] = fmaxf(m8[t & 7], s[t]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float mn = fmaxf(m, mx);
       const float base = mn == -INFINITY ? 0.f : mn;
-      const float alpha = exp2f(m - base);
-      float rs = 0.f;
+      const float alpha = ex2_sfu(m - base);
+      float r8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) r8[u] = 0.f;
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int t = 0; t < BN; t += 2) {
-        const float a0 = exp2f(s[t] - base), a1 = exp2f(s[t + 1] - base);
-        rs += a0 + a1;
+        float a0, a1;
+        if (kPoly && ((t >> 1) & 3) == 3) {  // a quarter of the exponentials on the FMA pipe
+          a0 = ex2_poly(s[t] - base);
+          a1 = ex2_poly(s[t + 1] - base);
+        } else {
+          a0 = ex2_sfu(s[t] - base);
+          a1 = ex2_sfu(s[t + 1] - base);
+        }
+        r8[(t >> 1) & 7] += a0 + a1;
         pk[t / 2] = pack_bf16(a0, a1);
       }
+      const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       l = l * alpha + rs;
       m = mn;
       // PV_{j-1} must have landed before O may be touched; every PV completion
@@ -406,11 +446,23 @@ void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, 
   static bool attr_set[64] = {false};
   const int dev = current_device();
   if (!attr_set[dev]) {
-    AETHER_CUDA_CHECK(cudaFuncSetAttribute(fa::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmem));
+    AETHER_CUDA_CHECK(
+        cudaFuncSetAttribute(fa::fa_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmem));
+    AETHER_CUDA_CHECK(
+        cudaFuncSetAttribute(fa::fa_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::kSmem));
     attr_set[dev] = true;
   }
   dim3 grid((unsigned)((Sq + fa::BM - 1) / fa::BM), (unsigned)(B * Hq));
-  fa::fa_fwd_kernel<<<grid, fa::kThreads, fa::kSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  // AETHER_FA_FWD_POLY=1 moves a quarter of the exponentials to the FMA pipe
+  // (measured slower here: the SFU is not the limiter; kept for A/B runs)
+  static const bool poly = [] {
+    const char* e = std::getenv("AETHER_FA_FWD_POLY");
+    return e != nullptr && std::string(e) == "1";
+  }();
+  if (poly)
+    fa::fa_fwd_kernel<true><<<grid, fa::kThreads, fa::kSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  else
+    fa::fa_fwd_kernel<false><<<grid, fa::kThreads, fa::kSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 

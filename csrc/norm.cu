@@ -286,6 +286,14 @@ __global__ void __launch_bounds__(kWarps * 32) layernorm_bwd_kernel(const __nv_b
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  // dw / db partials in registers across the warp's rows up to 1024 wide
+  // (BERT / ViT widths); wider rows add into shared memory per element
+  constexpr bool kRegDw = VPT <= 4;
+  float dwr[kRegDw ? VPT : 1][8], dbr[kRegDw ? VPT : 1][8];
+#pragma unroll
+  for (int i = 0; i < (kRegDw ? VPT : 1); ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwr[i][j] = dbr[i][j] = 0.f;
   for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
     uint4 rx[VPT], rg[VPT];
     load_raw<VPT>(x + (int64_t)row * d, d, lane, rx);
@@ -303,8 +311,13 @@ __global__ void __launch_bounds__(kWarps * 32) layernorm_bwd_kernel(const __nv_b
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float xh = (a[j] - mu) * rs;
-          atomicAdd(&sdw[c + j], g[j] * xh);
-          atomicAdd(&sdw[d + c + j], g[j]);
+          if constexpr (kRegDw) {
+            dwr[i][j] += g[j] * xh;
+            dbr[i][j] += g[j];
+          } else {
+            atomicAdd(&sdw[c + j], g[j] * xh);
+            atomicAdd(&sdw[d + c + j], g[j]);
+          }
           const float gw = g[j] * wv[j];
           sg += gw;
           sgx += gw * xh;
@@ -330,6 +343,19 @@ __global__ void __launch_bounds__(kWarps * 32) layernorm_bwd_kernel(const __nv_b
           for (int j = 0; j < 8; ++j) g[j] += q[j];
         }
         *reinterpret_cast<uint4*>(dx + (int64_t)row * d + c) = pack8(g);
+      }
+    }
+  }
+  if constexpr (kRegDw) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < d) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          atomicAdd(&sdw[c + j], dwr[i][j]);
+          atomicAdd(&sdw[d + c + j], dbr[i][j]);
+        }
       }
     }
   }
