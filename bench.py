@@ -111,7 +111,8 @@ def parse():
     ap.add_argument("--impl", default="aether", choices=["aether", "reference"])
     ap.add_argument("--global-batch", type=int, default=256)
     ap.add_argument("--seq", type=int, default=2048)
-    ap.add_argument("--micro-batch", type=int, default=8)
+    ap.add_argument("--micro-batch", type=int, default=16,
+                    help="sequences per forward/backward pass (16: ~56 GB of activations on one GPU)")
     ap.add_argument("--layers", type=int, default=24, help="debug only; anything but 24 is not the benchmark config")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
