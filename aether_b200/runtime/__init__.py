@@ -26,6 +26,38 @@ P, I, L, Fl, U64 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_uint64
 SIGNATURES = {
     # core ops
     "aether_op_matmul_f32": (I, [P, P, P, I, I, I]),
+    # developer tooling, host communicator, autotune, audio
+    "aether_hot_reload_arm": (I, [P, L]),
+    "aether_hot_reload_check": (I, [P, L]),
+    "aether_sbom_reset": (I, []),
+    "aether_sbom_add": (I, [P, L, P, L]),
+    "aether_sbom_count": (L, []),
+    "aether_sbom_emit": (I, [P, L]),
+    "aether_autotune_matmul_tile_f32": (L, [L, L, L]),
+    "aether_autotune_unpack_tile_m": (L, [L]),
+    "aether_autotune_unpack_tile_n": (L, [L]),
+    "aether_autotune_unpack_tile_k": (L, [L]),
+    "aether_autotune_unpack_unroll": (L, [L]),
+    "aether_cov_record": (I, [L, L]),
+    "aether_cov_hits": (L, [L, L]),
+    "aether_cov_reset": (I, []),
+    "aether_cov_dump": (I, []),
+    "aether_pgo_record_branch": (I, [L, L]),
+    "aether_pgo_record_call": (I, [L]),
+    "aether_pgo_branch_freq": (Fl, [L]),
+    "aether_pgo_call_count": (L, [L]),
+    "aether_pgo_reset": (I, []),
+    "aether_prefetch_t0": (I, [L]),
+    "aether_nccl_init": (I, []),
+    "aether_nccl_init_count": (I, []),
+    "aether_nccl_finalize": (I, []),
+    "aether_nccl_comm_create": (L, [I, I]),
+    "aether_nccl_comm_destroy": (I, [L]),
+    "aether_nccl_comm_world_size": (I, [L]),
+    "aether_nccl_comm_rank": (I, [L]),
+    "aether_nccl_all_reduce_f32": (I, [P, P, I, I, L]),
+    "aether_audio_hann_window": (I, [P, I]),
+    "aether_audio_dft_magnitude_f32": (I, [P, I, P, I]),
     # chat templates and tool calls
     "aether_template_new": (L, []),
     "aether_template_free": (I, [L]),
