@@ -44,6 +44,7 @@ class GPTConfig:
     norm_eps: float = 1e-5
     init_std: float = 0.02
     tie_embeddings: bool = False
+    qk_norm: bool = False  # Qwen3: per-head RMSNorm of q and k before RoPE
 
     @property
     def head_dim(self) -> int:
@@ -79,6 +80,10 @@ def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool 
         specs += [
             (f"l{i}.attn_norm", (d,), False),
             (f"l{i}.wqkv", (qkv, d), True),
+        ]
+        if cfg.qk_norm:
+            specs += [(f"l{i}.q_norm", (cfg.head_dim,), False), (f"l{i}.k_norm", (cfg.head_dim,), False)]
+        specs += [
             (f"l{i}.wo", (d, d), True),
             (f"l{i}.mlp_norm", (d,), False),
             (f"l{i}.wgu", (2 * f, d), True),
@@ -113,6 +118,8 @@ class GPT:
         # chunk of every sequence; attention all-gathers K/V over the group
         self.cp = cp if cp is not None and cp.world > 1 else None
         tp_size = self.tp.world if self.tp else 1
+        # the shared q/k norm weights would get only this rank's heads' gradient
+        assert not (cfg.qk_norm and self.tp is not None), "qk_norm with tensor parallelism is not supported"
         assert cfg.n_heads % tp_size == 0 and cfg.n_kv_heads % tp_size == 0 and cfg.d_ff % tp_size == 0
         self.device = torch.device(device)
         self.layers = list(range(cfg.n_layers) if layers is None else layers)
@@ -167,6 +174,16 @@ class GPT:
         y = A.linear(x, w, residual=residual.detach() if (residual is not None and self.tp.rank == 0) else None)
         return T.tp_reduce_residual(y, residual, self.tp)
 
+    def _qk_norm(self, i: int, qkv: torch.Tensor, Hq: int, Hkv: int, D: int) -> torch.Tensor:
+        """Qwen3's per-head RMSNorm of the q and k heads (one shared weight of
+        head_dim per layer each): the heads become the rows of the row-norm
+        kernels, and the normalised q, k and the untouched v are reassembled."""
+        T, a = qkv.shape[0], self.arena
+        eps = self.cfg.norm_eps
+        q = A.rmsnorm(qkv[:, : Hq * D].reshape(T * Hq, D), a[f"l{i}.q_norm"], eps).view(T, Hq * D)
+        k = A.rmsnorm(qkv[:, Hq * D : (Hq + Hkv) * D].reshape(T * Hkv, D), a[f"l{i}.k_norm"], eps).view(T, Hkv * D)
+        return torch.cat([q, k, qkv[:, (Hq + Hkv) * D :]], 1)
+
     def freeze(self) -> None:
         """Stops gradients to every base parameter (adapter fine-tuning): the
         weight-gradient GEMMs are skipped and the flat gradient stays unused."""
@@ -201,6 +218,8 @@ class GPT:
         for i in self.layers:
             h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
             qkv = lin(i, "wqkv", h)
+            if cfg.qk_norm:
+                qkv = self._qk_norm(i, qkv, Hq, Hkv, D)
             qkv = A.rope_(qkv, pos, self.rope_cos, self.rope_sin, Hq + Hkv, D)
             if self.cp is None:
                 o = A.attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True)
