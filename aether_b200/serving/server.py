@@ -191,8 +191,10 @@ def build_app(engine, model_name: str = "aether-qwen", embedder=None, template="
 
     @app.post("/v1/vision/embed")
     async def vision_embed(req: HTTPRequest):
-        """Body: {"image": [3][H][W] floats} or {"image_b64": raw little-endian
-        float32 bytes, "shape": [3, H, W]} -> L2-normalised CLS embedding."""
+        """Body: {"image": [3][H][W] floats}, {"image_b64": raw little-endian
+        float32 bytes, "shape": [3, H, W]}, or {"image_u8_b64": raw 8-bit RGB
+        bytes, "shape": [H, W, 3]} (normalised with the ImageNet mean / std
+        per channel) -> L2-normalised CLS embedding."""
         if vision is None:
             return JSONResponse({"error": {"message": "no vision model loaded"}}, status_code=501)
         import base64
@@ -201,7 +203,18 @@ def build_app(engine, model_name: str = "aether-qwen", embedder=None, template="
         import torch
 
         body = await req.json()
-        if "image_b64" in body:
+        if "image_u8_b64" in body:
+            from ..runtime import call, ptr
+
+            hwc = np.frombuffer(base64.b64decode(body["image_u8_b64"]), dtype=np.uint8).reshape(body["shape"])
+            if hwc.ndim != 3 or hwc.shape[2] != 3:
+                raise HTTPException(400, "image_u8_b64 must be [H, W, 3] uint8")
+            chw = np.empty((3, hwc.shape[0], hwc.shape[1]), np.float32)
+            for c, (mu, sd) in enumerate(((0.485, 0.229), (0.456, 0.224), (0.406, 0.225))):
+                plane = np.ascontiguousarray(hwc[:, :, c])
+                call("aether_img_normalize_f32", ptr(plane), ptr(chw[c]), plane.size, mu, sd)
+            img = torch.from_numpy(chw)
+        elif "image_b64" in body:
             arr = np.frombuffer(base64.b64decode(body["image_b64"]), dtype="<f4").reshape(body["shape"])
             img = torch.from_numpy(arr.copy())
         else:

@@ -1,11 +1,12 @@
 // libaether_rt: developer-tooling hooks, the NCCL-shaped host communicator,
-// the CPU matmul tile autotuner and two audio preprocessing primitives.
+// the CPU matmul tile autotuner and the image / audio preprocessing primitives.
 //
 // Reference ABI (runtime/src/lib.rs): aether_hot_reload_{arm,check} (:2152),
 // aether_sbom_{reset,add,count,emit} (:2217), aether_autotune_matmul_tile_f32
 // + unpack helpers (:2295), aether_cov_{record,hits,reset,dump} (:2352),
 // aether_prefetch_{t0,t1,nta} (:2425), aether_nccl_* (:3336),
-// aether_pgo_* (:3879), aether_audio_{hann_window,dft_magnitude_f32} (:6352).
+// aether_pgo_* (:3879), aether_img_{normalize,patchify}_f32 (:6302),
+// aether_audio_{hann_window,dft_magnitude_f32} (:6352).
 //
 // The NCCL-shaped communicator is real across processes here: world_size 1
 // is the identity; for world_size > 1 every rank passes the same rendezvous
@@ -398,6 +399,36 @@ AE_API int aether_nccl_all_reduce_f32(const void* send, void* recv, int n, int o
     if (aether_tcp_recv_all(s, (int64_t)(intptr_t)out, bytes) != bytes) return 3;
   }
   return 0;
+}
+
+// ------------------------------------------------------------------ vision preprocessing
+// out = (px / 255 - mean) / std for n 8-bit pixel values of one channel.
+AE_API int aether_img_normalize_f32(const void* px_u8, void* out_f32, int n_pixels, float mean, float stdv) {
+  if (!px_u8 || !out_f32 || n_pixels <= 0 || stdv == 0.f) return -1;
+  const uint8_t* p = static_cast<const uint8_t*>(px_u8);
+  float* o = static_cast<float*>(out_f32);
+  const float inv = 1.f / stdv;
+  for (int i = 0; i < n_pixels; ++i) o[i] = ((float)p[i] * (1.f / 255.f) - mean) * inv;
+  return 0;
+}
+
+// (h, w) single-channel image -> (h / patch * w / patch) row-major patches of
+// patch * patch values, patches in raster order; returns the patch count.
+AE_API int aether_img_patchify_f32(const void* img, void* out, int h, int w, int patch) {
+  if (!img || !out) return -1;
+  if (h <= 0 || w <= 0 || patch <= 0) return -2;
+  if (h % patch || w % patch) return -3;
+  const float* x = static_cast<const float*>(img);
+  float* o = static_cast<float*>(out);
+  const int pr = h / patch, pc = w / patch;
+  for (int py = 0; py < pr; ++py)
+    for (int px = 0; px < pc; ++px) {
+      float* dst = o + (size_t)(py * pc + px) * patch * patch;
+      for (int iy = 0; iy < patch; ++iy)
+        std::memcpy(dst + (size_t)iy * patch, x + (size_t)(py * patch + iy) * w + (size_t)px * patch,
+                    sizeof(float) * (size_t)patch);
+    }
+  return pr * pc;
 }
 
 // ------------------------------------------------------------------ audio preprocessing

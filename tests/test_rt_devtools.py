@@ -111,3 +111,17 @@ def test_nccl_surface_two_processes():
         assert [o[0] for o in outs] == [0, 0, 0, 0]
         assert outs[0][1] == [6.0] * 5 and outs[1][1] == [3.0] * 5 and outs[2][1] == [1.0] * 5
         assert outs[3][1] == [6.0] * 5  # 1 * 2 * 3
+
+
+def test_image_preprocess():
+    rng = np.random.default_rng(1)
+    px = rng.integers(0, 256, 48, dtype=np.uint8)
+    out = np.zeros(48, np.float32)
+    assert R.call("aether_img_normalize_f32", R.ptr(px), R.ptr(out), 48, 0.485, 0.229) == 0
+    assert np.allclose(out, (px / 255.0 - 0.485) / 0.229, atol=1e-5)
+    img = rng.standard_normal((8, 12)).astype(np.float32)
+    pat = np.zeros(6 * 16, np.float32)
+    assert R.call("aether_img_patchify_f32", R.ptr(img), R.ptr(pat), 8, 12, 4) == 6
+    want = img.reshape(2, 4, 3, 4).transpose(0, 2, 1, 3).reshape(6, 16)
+    assert np.array_equal(pat.reshape(6, 16), want)
+    assert R.call("aether_img_patchify_f32", R.ptr(img), R.ptr(pat), 8, 12, 5) == -3

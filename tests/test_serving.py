@@ -135,6 +135,14 @@ def test_http_server_routes():
         assert len(e["data"]) == 2 and len(e["data"][0]["embedding"]) == 64
         v = json.loads(_post(base + "/v1/vision/embed", {"image": torch.randn(3, 16, 16).tolist()}))
         assert len(v["embedding"]) == 64
+        import base64
+
+        import numpy as np
+
+        raw = np.random.default_rng(0).integers(0, 256, (16, 16, 3), dtype=np.uint8)
+        v8 = json.loads(_post(base + "/v1/vision/embed", {"image_u8_b64": base64.b64encode(raw.tobytes()).decode(),
+                                                          "shape": [16, 16, 3]}))
+        assert len(v8["embedding"]) == 64 and abs(sum(x * x for x in v8["embedding"]) - 1.0) < 1e-3
     finally:
         server.should_exit = True
         th.join(timeout=10)
