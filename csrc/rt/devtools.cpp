@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -398,6 +399,80 @@ AE_API int aether_nccl_all_reduce_f32(const void* send, void* recv, int n, int o
     if (aether_tcp_send_all(s, (int64_t)(intptr_t)out, bytes) != bytes) return 3;
     if (aether_tcp_recv_all(s, (int64_t)(intptr_t)out, bytes) != bytes) return 3;
   }
+  return 0;
+}
+
+// ------------------------------------------------------------------ LLM inference bench entry points
+// Forward passes per second of a pre-LayerNorm decoder (LN -> Q/K/V -> causal
+// attention -> O + residual -> LN -> up -> SiLU -> down + residual) over a
+// seq_len-token block, fp32 on this CPU through the C ABI's own ops; weights
+// are drawn once from a fixed-seed SplitMix64 stream, scaled to +-0.01. GPU
+// serving throughput is measured by the Python package (bench_serve): the
+// cuBLAS-routed and device-resident variants return 0 (not built into the
+// host library).
+int aether_op_matmul_f32(const void*, const void*, void*, int, int, int);
+int aether_op_layer_norm_f32(const void*, const void*, const void*, float, void*, void*, void*, int, int);
+int aether_op_sdpa_causal_f32(const void*, const void*, const void*, void*, void*, int, int, int);
+int aether_op_silu_f32(void*, int);
+
+AE_API float aether_llm_inference_bench_tps(int n_iters, int d_model, int n_layers, int ff, int seq_len) {
+  if (n_iters <= 0 || d_model <= 0 || n_layers <= 0 || ff <= 0 || seq_len <= 0) return 0.f;
+  const size_t d = (size_t)d_model, f = (size_t)ff, s = (size_t)seq_len;
+  uint64_t st = 0x2545F4914F6CDD1DULL;
+  auto rnd = [&]() {
+    st += 0x9E3779B97F4A7C15ULL;
+    uint64_t z = st;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    z ^= z >> 31;
+    return ((float)(z >> 40) / (float)(1 << 24) - 0.5f) * 0.02f;
+  };
+  struct Layer {
+    std::vector<float> wq, wk, wv, wo, up, down;
+  };
+  std::vector<Layer> L((size_t)n_layers);
+  for (auto& l : L) {
+    for (auto* w : {&l.wq, &l.wk, &l.wv, &l.wo}) {
+      w->resize(d * d);
+      for (auto& e : *w) e = rnd();
+    }
+    l.up.resize(d * f);
+    for (auto& e : l.up) e = rnd();
+    l.down.resize(f * d);
+    for (auto& e : l.down) e = rnd();
+  }
+  std::vector<float> ones(d, 1.f), zeros(d, 0.f), x(s * d), h(s * d), q(s * d), k(s * d), v(s * d), o(s * d),
+      proj(s * d), att(s * s), up(s * f), mean(s), rstd(s);
+  for (auto& e : x) e = rnd();
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0; it < n_iters; ++it)
+    for (auto& l : L) {
+      aether_op_layer_norm_f32(x.data(), ones.data(), zeros.data(), 1e-5f, h.data(), mean.data(), rstd.data(),
+                               (int)s, (int)d);
+      aether_op_matmul_f32(h.data(), l.wq.data(), q.data(), (int)s, (int)d, (int)d);
+      aether_op_matmul_f32(h.data(), l.wk.data(), k.data(), (int)s, (int)d, (int)d);
+      aether_op_matmul_f32(h.data(), l.wv.data(), v.data(), (int)s, (int)d, (int)d);
+      aether_op_sdpa_causal_f32(q.data(), k.data(), v.data(), o.data(), att.data(), 1, (int)s, (int)d);
+      aether_op_matmul_f32(o.data(), l.wo.data(), proj.data(), (int)s, (int)d, (int)d);
+      for (size_t i = 0; i < s * d; ++i) x[i] += proj[i];
+      aether_op_layer_norm_f32(x.data(), ones.data(), zeros.data(), 1e-5f, h.data(), mean.data(), rstd.data(),
+                               (int)s, (int)d);
+      aether_op_matmul_f32(h.data(), l.up.data(), up.data(), (int)s, (int)d, (int)f);
+      aether_op_silu_f32(up.data(), (int)(s * f));
+      aether_op_matmul_f32(up.data(), l.down.data(), proj.data(), (int)s, (int)f, (int)d);
+      for (size_t i = 0; i < s * d; ++i) x[i] += proj[i];
+    }
+  const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  return sec > 0 ? (float)(n_iters / sec) : 0.f;
+}
+AE_API float aether_llm_inference_bench_tps_cuda(int, int, int, int, int) { return 0.f; }
+AE_API float aether_llm_inference_bench_tps_cuda_resident(int, int, int, int, int) { return 0.f; }
+
+// One bench line: "cpu|gpu  M= N= K= iters= us=".
+AE_API int aether_print_bench(int64_t which, int m, int n, int k, int iters, int64_t us) {
+  std::printf("%-3s  M=%4d  N=%4d  K=%4d  iters=%4d  us=%10lld\n", which == 0 ? "cpu" : "gpu", m, n, k, iters,
+              (long long)us);
+  std::fflush(stdout);
   return 0;
 }
 

@@ -125,3 +125,12 @@ def test_image_preprocess():
     want = img.reshape(2, 4, 3, 4).transpose(0, 2, 1, 3).reshape(6, 16)
     assert np.array_equal(pat.reshape(6, 16), want)
     assert R.call("aether_img_patchify_f32", R.ptr(img), R.ptr(pat), 8, 12, 5) == -3
+
+
+def test_llm_inference_bench_entry_point(capfd):
+    tps = R.call("aether_llm_inference_bench_tps", 3, 64, 2, 128, 16)
+    assert tps > 0
+    assert R.call("aether_llm_inference_bench_tps", 0, 64, 2, 128, 16) == 0.0
+    assert R.call("aether_llm_inference_bench_tps_cuda", 3, 64, 2, 128, 16) == 0.0  # GPU numbers come from bench_serve
+    R.call("aether_print_bench", 0, 64, 64, 64, 10, 1234)
+    assert "cpu  M=  64" in capfd.readouterr().out
