@@ -10,7 +10,10 @@ checkpoint readable.
 
 Loading concatenates all ranks' shards into the full master / moment vectors
 and slices the caller's own shard out of them, so a checkpoint written at one
-DP degree resumes at another. The bf16 compute copy is rebuilt from the fp32
+DP degree resumes at another. ZeRO-2 / ZeRO-3 arenas (``parallel.fsdp``)
+save their per-layer-unit shards with the unit layout; loading rebuilds every
+parameter's full master and moments by name, so either kind of checkpoint
+resumes into either kind of arena at any world size. The bf16 compute copy is rebuilt from the fp32
 master (bf16 = round(master), which is how every optimiser step writes it), so
 the continuation is bit-identical to an uninterrupted run.
 
@@ -47,12 +50,19 @@ def _opt_state(opt):
     return inner.m, inner.v, get, put, start, end
 
 
+def _sharded(arena) -> bool:
+    return hasattr(arena, "units") and hasattr(arena, "scatter_full")
+
+
 def save(path: str, arena, opt, step: int, rank: int = 0, world: int = 1, extra: dict | None = None) -> None:
     os.makedirs(path, exist_ok=True)
     m, v, get_step, _, start, end = _opt_state(opt)
     end = arena.numel if end is None else end
     meta = {"step": step, "opt_step": get_step(), "start": start, "end": end, "numel": arena.numel,
             "rank": rank, "world": world, "cpu_rng": torch.get_rng_state().tolist()}
+    if _sharded(arena):
+        meta.update(kind="sharded", layout=arena.layout(), start=0, end=arena.numel)
+        start, end = 0, arena.numel
     if arena.device.type == "cuda":
         meta["cuda_rng"] = torch.cuda.get_rng_state(arena.device).tolist()
     st.save_file({"master": arena.master[start:end], "m": m, "v": v}, os.path.join(path, f"rank{rank:05d}.safetensors"),
@@ -61,16 +71,52 @@ def save(path: str, arena, opt, step: int, rank: int = 0, world: int = 1, extra:
         info = {"world": world, "numel": arena.numel, "step": step,
                 "slots": {n: [list(s.shape), s.offset, s.numel, s.decay] for n, s in arena.slots.items()},
                 "extra": extra or {}}
+        if _sharded(arena):
+            info.update(kind="sharded", slots={})
         tmp = os.path.join(path, "meta.json.tmp")
         with open(tmp, "w") as f:
             json.dump(info, f)
         os.replace(tmp, os.path.join(path, "meta.json"))
 
 
+def named_state(path: str) -> tuple:
+    """(info, {name: {"master", "m", "v": full fp32 tensors}}, [per-rank meta])
+    of a checkpoint of either kind."""
+    info = json.load(open(os.path.join(path, "meta.json")))
+    metas, shards = [], []
+    for r in range(info["world"]):
+        f = os.path.join(path, f"rank{r:05d}.safetensors")
+        metas.append(json.loads(st.metadata(f)["aether"]))
+        shards.append(st.load_file(f))
+    out = {}
+    if info.get("kind") == "sharded":
+        for uid, (_, _, unit_numel, slots) in metas[0]["layout"].items():
+            full = {k: torch.cat([sh[k][me["layout"][uid][0] : me["layout"][uid][0] + me["layout"][uid][1]]
+                                  for sh, me in zip(shards, metas)])[:unit_numel] for k in ("master", "m", "v")}
+            for n, (shape, off, numel, _) in slots.items():
+                out[n] = {k: full[k][off : off + numel].view(shape).clone() for k in full}
+        return info, out, metas
+    full = {k: torch.zeros(info["numel"], dtype=torch.float32) for k in ("master", "m", "v")}
+    for me, sh in zip(metas, shards):
+        for k in full:
+            full[k][me["start"] : me["end"]] = sh[k]
+    for n, (shape, off, numel, _) in info["slots"].items():
+        out[n] = {k: full[k][off : off + numel].view(shape).clone() for k in full}
+    return info, out, metas
+
+
+def _restore_rng(meta, device) -> None:
+    torch.set_rng_state(torch.tensor(meta["cpu_rng"], dtype=torch.uint8))
+    if "cuda_rng" in meta and device.type == "cuda":
+        torch.cuda.set_rng_state(torch.tensor(meta["cuda_rng"], dtype=torch.uint8), device)
+
+
 def load(path: str, arena, opt, restore_rng: bool = True) -> int:
     """Restore ``arena`` (master + bf16) and ``opt`` (moments, step count) from
     a checkpoint directory; returns the saved training step."""
     info = json.load(open(os.path.join(path, "meta.json")))
+    if info.get("kind") == "sharded" or _sharded(arena):
+        return _load_by_name(path, arena, opt, restore_rng)
     if info["numel"] != arena.numel:
         # a different DP degree pads the arena differently; the slots must agree
         for n, s in arena.slots.items():
@@ -100,4 +146,40 @@ def load(path: str, arena, opt, restore_rng: bool = True) -> int:
         torch.set_rng_state(torch.tensor(my_rank_meta["cpu_rng"], dtype=torch.uint8))
         if "cuda_rng" in my_rank_meta and arena.device.type == "cuda":
             torch.cuda.set_rng_state(torch.tensor(my_rank_meta["cuda_rng"], dtype=torch.uint8), arena.device)
+    return int(info["step"])
+
+
+def _load_by_name(path: str, arena, opt, restore_rng: bool) -> int:
+    """Resume through named full tensors (a ZeRO-2/3 checkpoint, or any
+    checkpoint into a ZeRO-2/3 arena)."""
+    info, named, metas = named_state(path)
+    missing = [n for n in arena.slots if n not in named]
+    if missing:
+        raise ValueError(f"checkpoint lacks parameters {missing[:4]}")
+    m, v, _, put_step, start, end = _opt_state(opt)
+    with torch.no_grad():
+        if _sharded(arena):
+            for n, t in named.items():
+                if n in arena.slots:
+                    arena.scatter_full(n, t["master"], arena.master)
+                    arena.scatter_full(n, t["m"], m)
+                    arena.scatter_full(n, t["v"], v)
+        else:
+            end = arena.numel if end is None else end
+            fm = torch.zeros(arena.numel, dtype=torch.float32)
+            fv = torch.zeros(arena.numel, dtype=torch.float32)
+            for n, t in named.items():
+                if n in arena.slots:
+                    s = arena.slots[n]
+                    arena.master_view(n).copy_(t["master"].to(arena.master.device))
+                    fm[s.offset : s.offset + s.numel] = t["m"].reshape(-1)
+                    fv[s.offset : s.offset + s.numel] = t["v"].reshape(-1)
+            m.copy_(fm[start:end].to(m.device))
+            v.copy_(fv[start:end].to(v.device))
+        arena.sync_bf16_from_master()
+    rank = getattr(arena, "rank", 0)
+    me = metas[rank] if rank < len(metas) else metas[0]
+    put_step(int(me["opt_step"]))
+    if restore_rng:
+        _restore_rng(me, arena.device)
     return int(info["step"])

@@ -161,14 +161,25 @@ class ShardedArena:
     def set_full(self, name: str, t: torch.Tensor) -> None:
         """Initialise parameter ``name`` from its full fp32 value (every rank
         passes the same tensor and keeps its slice)."""
+        self.scatter_full(name, t, self.master)
+
+    def scatter_full(self, name: str, t: torch.Tensor, buf: torch.Tensor) -> None:
+        """Write this rank's slice of parameter ``name`` (full value ``t``) into
+        ``buf``, a shard-layout buffer (master weights or optimiser moments)."""
         u = self.unit_of[name]
         unit, s = self.units[u], self.slots[name]
         lo = self.rank * unit.shard
         flat = t.reshape(-1).to(torch.float32)
         a, b = max(s.offset, lo), min(s.offset + s.numel, lo + unit.shard)
         if a < b:
-            dst = self.master[unit.offset + a - lo : unit.offset + b - lo]
-            dst.copy_(flat[a - s.offset : b - s.offset].to(self.device))
+            buf[unit.offset + a - lo : unit.offset + b - lo].copy_(flat[a - s.offset : b - s.offset].to(buf.device))
+
+    def layout(self) -> dict:
+        """Unit id -> [offset in this rank's shard, shard length, unit length,
+        {name: [shape, offset in unit, numel, decay]}] (checkpoint metadata)."""
+        return {str(u): [unit.offset, unit.shard, unit.numel,
+                         {n: [list(sl.shape), sl.offset, sl.numel, sl.decay] for n, sl in unit.slots.items()}]
+                for u, unit in self.units.items()}
 
     def sync_bf16_from_master(self) -> None:
         with torch.no_grad():

@@ -135,3 +135,68 @@ def test_sharded_grads_accumulate_one_rank_gpu(stage):
     """The same on the GPU kernels: the weight-gradient GEMMs reduce into the
     rotating unit buffers found through the autograd gradient-buffer table."""
     _one_rank(3, stage, "cuda")
+
+
+def _ckpt_worker(rank, world, port, path, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    sys.path.insert(0, ROOT)
+    from aether_b200 import checkpoint
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.parallel import dist as D
+    from aether_b200.parallel.fsdp import ShardedDataParallel, ShardSpec
+    from aether_b200.train import Trainer
+
+    info = D.init(device="cpu", timeout_s=60)
+    g = torch.Generator().manual_seed(200 + rank)
+    batches = [torch.randint(0, 128, (4, 17), generator=g) for _ in range(3)]
+
+    def build():
+        m = GPT(GPTConfig(**CFG), device="cpu", seed=3, shard=ShardSpec(rank, world, 3))
+        eng = ShardedDataParallel(m.arena, lr=1e-2)
+        return m, eng, Trainer(m, info, micro_batch=4, dp=eng, lr=1e-2)
+
+    m, eng, tr = build()
+    for b in batches[:2]:
+        tr.train_step(b)
+    checkpoint.save(path, m.arena, eng, step=2, rank=rank, world=world)
+    straight = float(tr.train_step(batches[2]))
+    want = m.arena.full_state()
+    m2, eng2, tr2 = build()
+    step = checkpoint.load(path, m2.arena, eng2)
+    tr2.step_idx = step
+    resumed = float(tr2.train_step(batches[2]))
+    got = m2.arena.full_state()
+    same = all(torch.equal(want[n], got[n]) for n in want)
+    q.put((rank, step, straight, resumed, same))
+    D.shutdown()
+
+
+def test_zero3_checkpoint_resume_bitwise_and_into_plain_arena(tmp_path):
+    import multiprocessing as mp
+
+    from aether_b200 import checkpoint
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.optim import FlatAdamW
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    path = str(tmp_path / "ck")
+    ps = [ctx.Process(target=_ckpt_worker, args=(r, 2, port, path, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = [q.get(timeout=300) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, step, straight, resumed, same in out:
+        assert step == 2 and straight == resumed and same, (rank, straight, resumed, same)
+    # the world-2 ZeRO-3 checkpoint resumes into a one-process flat arena
+    info, named, _ = checkpoint.named_state(path)
+    m = GPT(GPTConfig(**CFG), device="cpu", seed=99)
+    opt = FlatAdamW(m.arena, lr=1e-2)
+    assert checkpoint.load(path, m.arena, opt) == 2
+    for n in m.arena.names():
+        assert torch.equal(m.arena.master_view(n), named[n]["master"]), n
+    assert opt.step_count == 2 and float(opt.m.abs().sum()) > 0
