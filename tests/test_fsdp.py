@@ -97,11 +97,11 @@ def test_stage_bytes():
     assert stage_bytes(n, 1, 3) == stage_bytes(n, 1, 1) == 18 * n
 
 
-def _one_rank(n_layers, stage, device):
+def _one_rank(n_layers, stage, device, tie=False):
     from aether_b200.models.gpt import GPT, GPTConfig
     from aether_b200.parallel.fsdp import ShardSpec
 
-    cfg = dict(CFG, n_layers=n_layers)
+    cfg = dict(CFG, n_layers=n_layers, tie_embeddings=tie)
     if device == "cuda":  # the attention kernels take head_dim 64 or 128
         cfg.update(d_model=128, d_ff=256)
     g = torch.Generator().manual_seed(5)
@@ -127,6 +127,13 @@ def test_sharded_grads_accumulate_one_rank(n_layers, stage):
     """World 1: two backward passes accumulate the same gradients as the flat
     arena (exercises the rotating unit buffers and their recycling)."""
     _one_rank(n_layers, stage, "cpu")
+
+
+@pytest.mark.parametrize("stage", [2, 3])
+def test_sharded_tied_embeddings_one_rank(stage):
+    """The tied embedding / LM head weight lives in the root unit and gets
+    both its gradients."""
+    _one_rank(2, stage, "cpu", tie=True)
 
 
 @pytest.mark.gpu
