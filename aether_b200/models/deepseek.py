@@ -15,6 +15,12 @@ where W_uk[h] / W_uv[h] are head h's key / value blocks of Wkv_b. Only the
 decode run the same per-token path: a prefill token is a query whose length
 is its position + 1.
 
+Tensor parallelism (``tp``: ``rank``, ``world``, ``all_reduce_``): the heads
+are split over the ranks (their q rows, W_uk / W_uv blocks and W_o columns),
+the shared latent is computed and cached on every rank, the routed experts are
+partitioned over the same ranks and the dense / shared-expert FFNs are split
+by columns / rows; each block ends in one all-reduce of its partial output.
+
 FFN: the first ``first_dense`` layers are dense SwiGLU; the others route
 each token to ``top_k`` of ``n_experts`` (grouped tcgen05 GEMMs over tokens
 sorted by expert, as in ``models/moe.py``) and add the shared experts (one
@@ -123,10 +129,15 @@ def yarn_rope_tables(cfg: DeepSeekConfig, max_pos: int, device=None):
 
 
 class DeepSeekWeights:
-    def __init__(self, cfg: DeepSeekConfig, device, seed: int = 0):
+    def __init__(self, cfg: DeepSeekConfig, device, seed: int = 0, tp_rank: int = 0, tp_size: int = 1):
+        """tp_rank / tp_size: keep this rank's heads, experts and FFN slices
+        (the same values as the matching slices of the unsplit weights)."""
         assert cfg.kv_lora_rank == F.MLA_LAT and cfg.qk_rope == F.MLA_ROPE, "MLA kernels: latent 512, rope 64"
+        assert cfg.n_heads % tp_size == 0 and cfg.d_ff % tp_size == 0, "heads and d_ff must split over TP"
+        assert (cfg.n_shared * cfg.d_expert) % tp_size == 0, "the shared experts must split over TP"
         dev = torch.device(device)
         self.cfg, self.device = cfg, dev
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         d, H = cfg.d_model, cfg.n_heads
         idx = [0]
 
@@ -134,6 +145,25 @@ class DeepSeekWeights:
             idx[0] += 1
             g = torch.Generator(device=dev).manual_seed(seed * 7919 + 31 * idx[0])
             return (torch.randn(*shape, generator=g, device=dev) * std).to(torch.bfloat16)
+
+        r, w = tp_rank, tp_size
+        Hl = H // w
+        h0 = r * Hl
+
+        def rows(t, n):  # this rank's n-row block
+            return t[r * n : (r + 1) * n].contiguous()
+
+        def cols(t, n):
+            return t[:, r * n : (r + 1) * n].contiguous()
+
+        def gu_rows(t, f):  # gate and up halves each split into w blocks
+            g_, u_ = t[:f], t[f:]
+            return torch.cat([rows(g_, f // w), rows(u_, f // w)]).contiguous()
+
+        from .moe import expert_range
+
+        e0, e1 = expert_range(cfg.n_experts, r, w)
+        self.e0, self.e1 = e0, e1
 
         ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
         self.embed = rnd(cfg.vocab, d)
@@ -151,39 +181,42 @@ class DeepSeekWeights:
                 self.wq.append(None)
                 self.wq_a.append(rnd(cfg.q_lora_rank, d))
                 self.q_a_norm.append(ones(cfg.q_lora_rank))
-                self.wq_b.append(rnd(H * qh, cfg.q_lora_rank))
+                self.wq_b.append(rows(rnd(H * qh, cfg.q_lora_rank), Hl * qh))
             else:
-                self.wq.append(rnd(H * qh, d))
-            self.wkv_a.append(rnd(F.MLA_LAT + F.MLA_ROPE, d))
+                self.wq.append(rows(rnd(H * qh, d), Hl * qh))
+            self.wkv_a.append(rnd(F.MLA_LAT + F.MLA_ROPE, d))  # the shared latent: every rank
             self.kv_norm.append(torch.ones(F.MLA_LAT, dtype=torch.float32, device=dev))
             wkv_b = rnd(H * (cfg.qk_nope + cfg.v_head), F.MLA_LAT).view(H, cfg.qk_nope + cfg.v_head, F.MLA_LAT)
-            self.w_uk.append(wkv_b[:, : cfg.qk_nope].contiguous())   # [H, 128, 512]
-            self.w_uv.append(wkv_b[:, cfg.qk_nope :].contiguous())   # [H, v_head, 512]
-            self.wo.append(rnd(d, H * cfg.v_head))
+            self.w_uk.append(wkv_b[h0 : h0 + Hl, : cfg.qk_nope].contiguous())   # [Hl, 128, 512]
+            self.w_uv.append(wkv_b[h0 : h0 + Hl, cfg.qk_nope :].contiguous())   # [Hl, v_head, 512]
+            self.wo.append(cols(rnd(d, H * cfg.v_head), Hl * cfg.v_head))
             if i < cfg.first_dense:
-                self.dense_gu.append(rnd(2 * cfg.d_ff, d))
-                self.dense_d.append(rnd(d, cfg.d_ff))
+                self.dense_gu.append(gu_rows(rnd(2 * cfg.d_ff, d), cfg.d_ff))
+                self.dense_d.append(cols(rnd(d, cfg.d_ff), cfg.d_ff // w))
                 for lst in (self.router, self.exp_gu, self.exp_d, self.sh_gu, self.sh_d):
                     lst.append(None)
             else:
                 self.dense_gu.append(None)
                 self.dense_d.append(None)
-                r = torch.zeros(Ep, d, dtype=torch.bfloat16, device=dev)
-                r[: cfg.n_experts] = rnd(cfg.n_experts, d)
-                self.router.append(r)
-                self.exp_gu.append(rnd(cfg.n_experts, 2 * cfg.d_expert, d).contiguous())
-                self.exp_d.append(rnd(cfg.n_experts, d, cfg.d_expert).contiguous())
+                rt = torch.zeros(Ep, d, dtype=torch.bfloat16, device=dev)
+                rt[: cfg.n_experts] = rnd(cfg.n_experts, d)
+                self.router.append(rt)
+                self.exp_gu.append(rnd(cfg.n_experts, 2 * cfg.d_expert, d)[e0:e1].contiguous())
+                self.exp_d.append(rnd(cfg.n_experts, d, cfg.d_expert)[e0:e1].contiguous())
                 fs = cfg.n_shared * cfg.d_expert
-                self.sh_gu.append(rnd(2 * fs, d) if fs else None)
-                self.sh_d.append(rnd(d, fs) if fs else None)
+                self.sh_gu.append(gu_rows(rnd(2 * fs, d), fs) if fs else None)
+                self.sh_d.append(cols(rnd(d, fs), fs // w) if fs else None)
 
 
 class DeepSeekModel:
     def __init__(self, cfg: DeepSeekConfig, device="cuda", seed: int = 0, max_batch: int = 16,
-                 max_seq: int | None = None, weights: DeepSeekWeights | None = None):
+                 max_seq: int | None = None, weights: DeepSeekWeights | None = None, tp=None):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.w = weights or DeepSeekWeights(cfg, device, seed)
+        self.tp = tp if tp is not None and tp.world > 1 else None
+        r, w = (tp.rank, tp.world) if self.tp is not None else (0, 1)
+        self.w = weights or DeepSeekWeights(cfg, device, seed, r, w)
+        self.heads = cfg.n_heads // w  # this rank's heads
         self.max_batch = max_batch
         self.max_seq = max_seq or cfg.max_seq
         self.scratch_slot = max_batch
@@ -193,7 +226,7 @@ class DeepSeekModel:
                                   device=self.device) for _ in range(cfg.n_layers)]
         self.cos, self.sin = yarn_rope_tables(cfg, self.max_seq, self.device)
         self.scale = cfg.softmax_scale()
-        self.hgroups = (cfg.n_heads + 15) // 16
+        self.hgroups = (self.heads + 15) // 16
         self._graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
         B = max_batch
         self.buf = {"tok": torch.zeros(B, dtype=torch.long, device=self.device),
@@ -206,7 +239,7 @@ class DeepSeekModel:
     # ------------------------------------------------------------------ blocks
     def _attention(self, i: int, h: torch.Tensor, x: torch.Tensor, pos, slot, splits: int) -> torch.Tensor:
         cfg, w = self.cfg, self.w
-        T, H = h.shape[0], cfg.n_heads
+        T, H = h.shape[0], self.heads
         if cfg.q_lora_rank:
             qa = F.gemm(h, w.wq_a[i])
             qa, _, _ = F.rmsnorm(qa, w.q_a_norm[i], cfg.norm_eps)
@@ -222,20 +255,33 @@ class DeepSeekModel:
         o_lat = torch.empty(T, H, F.MLA_LAT, dtype=torch.bfloat16, device=h.device)
         F.mla_attention(q_abs, self.cache[i], slot, pos + 1, o_lat, self.scale, splits)
         o = torch.bmm(o_lat.transpose(0, 1), w.w_uv[i].transpose(1, 2)).transpose(0, 1).reshape(T, H * cfg.v_head)
-        return F.gemm(o.contiguous(), w.wo[i], residual=x)
+        if self.tp is None:
+            return F.gemm(o.contiguous(), w.wo[i], residual=x)
+        y = F.gemm(o.contiguous(), w.wo[i])  # this rank's heads' share
+        self.tp.all_reduce_(y)
+        return x + y
 
     def _ffn(self, i: int, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         cfg, w = self.cfg, self.w
         if w.dense_gu[i] is not None:
-            return F.gemm(F.swiglu(F.gemm(h, w.dense_gu[i])), w.dense_d[i], residual=x)
+            if self.tp is None:
+                return F.gemm(F.swiglu(F.gemm(h, w.dense_gu[i])), w.dense_d[i], residual=x)
+            y = F.gemm(F.swiglu(F.gemm(h, w.dense_gu[i])), w.dense_d[i])
+            self.tp.all_reduce_(y)
+            return x + y
         logits = F.gemm(h, w.router[i], out_dtype=torch.float32)[:, : cfg.n_experts]
         idx, wt = F.moe_route(logits, cfg.top_k, softmax_all=cfg.router == "softmax", renorm=cfg.norm_topk,
                               sigmoid=cfg.router == "sigmoid", scale=cfg.routed_scale)
-        row_of, src_row, tile_group = F.moe_permute(idx, cfg.n_experts)
+        e0, e1 = getattr(w, "e0", 0), getattr(w, "e1", cfg.n_experts)
+        row_of, src_row, tile_group = F.moe_permute(idx, e1 - e0, e0)
         X = F.moe_gather(h, src_row)
         Y = F.gemm_grouped(F.swiglu(F.gemm_grouped(X, w.exp_gu[i], tile_group)), w.exp_d[i], tile_group)
         extra = F.gemm(F.swiglu(F.gemm(h, w.sh_gu[i])), w.sh_d[i]) if w.sh_gu[i] is not None else None
-        return F.moe_combine(Y, row_of, wt, res=x, extra=extra)
+        if self.tp is None:
+            return F.moe_combine(Y, row_of, wt, res=x, extra=extra)
+        y = F.moe_combine(Y, row_of, wt, extra=extra)  # this rank's experts + shared-expert slice
+        self.tp.all_reduce_(y)
+        return x + y
 
     def _forward(self, tok: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, splits: int) -> torch.Tensor:
         """Token rows (any mix of sequences and positions) -> final hidden [T, d];
@@ -339,7 +385,8 @@ class DeepSeekModel:
     def reference_logits(self, tokens: torch.Tensor) -> torch.Tensor:
         """fp32 forward of [B, S] tokens in the standard (non-absorbed) MLA form:
         per-head keys / values decompressed from the latent, causal attention
-        over 192-dim queries / keys, 128-dim values."""
+        over 192-dim queries / keys, 128-dim values (one rank)."""
+        assert self.tp is None, "the oracle needs the unsplit weights"
         cfg, w = self.cfg, self.w
         B, S = tokens.shape
         H, nope, rope_d, vh = cfg.n_heads, cfg.qk_nope, cfg.qk_rope, cfg.v_head

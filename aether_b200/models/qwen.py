@@ -202,6 +202,41 @@ class QwenWeights:
             self.wd.append(wd[:, f0:f1].contiguous())
             del wqkv, bqkv, wo, wgu, wd
 
+    @staticmethod
+    def shard(full: "QwenWeights", tp_rank: int, tp_size: int, device) -> "QwenWeights":
+        """One rank's shard of full (e.g. GGUF- or HF-loaded) weights, in the
+        same layout as the random-init shards, moved to ``device``."""
+        cfg = full.cfg
+        dev = torch.device(device)
+        D, Hq, Hkv, F_ = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.d_ff
+        q_heads, kv_heads = tp_heads(Hq, Hkv, tp_rank, tp_size)
+        w = QwenWeights.__new__(QwenWeights)
+        w.cfg, w.device, w.tp_rank, w.tp_size = cfg, dev, tp_rank, tp_size
+        w.hq, w.hkv, w.f = len(q_heads), len(kv_heads), F_ // tp_size
+        f0, f1 = tp_rank * w.f, (tp_rank + 1) * w.f
+
+        def heads(t, hs, base):
+            return torch.cat([t[(base + h) * D : (base + h + 1) * D] for h in hs], 0)
+
+        def qkv(t):
+            return torch.cat([heads(t, q_heads, 0), heads(t, kv_heads, Hq), heads(t, kv_heads, Hq + Hkv)],
+                             0).contiguous().to(dev)
+
+        to = lambda t: None if t is None else t.to(dev)  # noqa: E731
+        w.embed = to(full.embed)
+        w.lm_head = w.embed if cfg.tie_embeddings else to(full.lm_head)
+        w.final_norm = to(full.final_norm)
+        w.attn_norm = [to(t) for t in full.attn_norm]
+        w.mlp_norm = [to(t) for t in full.mlp_norm]
+        w.q_norm = [to(t) for t in full.q_norm] if full.q_norm is not None else None
+        w.k_norm = [to(t) for t in full.k_norm] if full.k_norm is not None else None
+        w.wqkv = [qkv(t) for t in full.wqkv]
+        w.bqkv = [None if t is None else qkv(t) for t in full.bqkv]
+        w.wo = [t[:, q_heads[0] * D : (q_heads[-1] + 1) * D].contiguous().to(dev) for t in full.wo]
+        w.wgu = [torch.cat([t[f0:f1], t[F_ + f0 : F_ + f1]], 0).contiguous().to(dev) for t in full.wgu]
+        w.wd = [t[:, f0:f1].contiguous().to(dev) for t in full.wd]
+        return w
+
 
 class KVCache:
     def __init__(self, cfg: QwenConfig, n_kv_heads: int, slots: int, max_seq: int, device):

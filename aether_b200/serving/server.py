@@ -242,10 +242,12 @@ def main():
     ap.add_argument("--rate-limit", type=float, default=0.0, help="POST requests per second per client (0 = off)")
     ap.add_argument("--gguf", default=None, help="load Qwen2 weights (and tokenizer) from a GGUF file")
     ap.add_argument("--hf", default=None, help="load Qwen2 weights from a Hugging Face directory")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel degree; launch with torchrun --nproc-per-node N (rank 0 serves HTTP)")
     args = ap.parse_args()
     import uvicorn
 
-    from ..models.qwen import QwenConfig, QwenModel
+    from ..models.qwen import QwenConfig, QwenModel, QwenWeights
     from .engine import Engine
     from .tokenizer import BPETokenizer, ByteTokenizer
 
@@ -269,10 +271,13 @@ def main():
         from .templates import JinjaChatTemplate
 
         g = gguf.GGUFFile(args.gguf)
+        load_dev = "cpu" if args.tp > 1 else args.device  # TP: each rank moves only its shard
         if g.meta.get("general.architecture") == "deepseek2":  # DeepSeek-V2 / GLM-4.7-flash (MLA + MoE)
+            if args.tp > 1:
+                raise SystemExit("--tp with a deepseek2 GGUF is not supported yet (random-init presets are)")
             cfg, weights = gguf.load_deepseek_weights(args.gguf, device=args.device)
         else:
-            cfg, weights = gguf.load_qwen_weights(args.gguf, device=args.device)
+            cfg, weights = gguf.load_qwen_weights(args.gguf, device=load_dev)
         if not args.tokenizer:
             tok = gguf.tokenizer_from_gguf(g)
         template = JinjaChatTemplate.from_gguf(g) or template
@@ -283,18 +288,41 @@ def main():
 
         from .templates import JinjaChatTemplate
 
-        cfg, weights = hf.load_qwen_hf(args.hf, device=args.device)
+        cfg, weights = hf.load_qwen_hf(args.hf, device="cpu" if args.tp > 1 else args.device)
         if not args.tokenizer and os.path.exists(os.path.join(args.hf, "tokenizer.json")):
             tok = BPETokenizer.from_file(os.path.join(args.hf, "tokenizer.json"))
         template = JinjaChatTemplate.from_hf_dir(args.hf) or template
+    tp = None
+    if args.tp > 1:  # one process per GPU; every rank builds its shard, rank 0 serves
+        import torch.distributed as dist
+
+        from ..parallel import dist as D
+        from ..parallel.tp import TensorParallel
+        from .tp_serve import BroadcastModel, follow
+
+        info = D.init(timeout_s=600)
+        if info.world != args.tp:
+            raise SystemExit(f"--tp {args.tp} needs {args.tp} processes (got {info.world})")
+        args.device = str(info.device)
+        tp = TensorParallel(info)
+        ctrl = dist.new_group(backend="gloo")
+        if weights is not None and not isinstance(cfg, (DeepSeekConfig, MoEConfig)):
+            weights = QwenWeights.shard(weights, info.rank, info.world, info.device)
     if isinstance(cfg, DeepSeekConfig):
         model = DeepSeekModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq,
-                              weights=weights)
+                              weights=weights, tp=tp)
     elif isinstance(cfg, MoEConfig):
-        model = MoEQwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq)
+        model = MoEQwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq, tp=tp)
     else:
         model = QwenModel(cfg, device=args.device, max_batch=args.max_concurrent, max_seq=args.max_seq,
-                          weights=weights)
+                          weights=weights, tp=tp)
+    if tp is not None:
+        if info.rank != 0:
+            follow(model, ctrl)  # until rank 0 stops
+            tp.close()
+            D.shutdown()
+            return
+        model = BroadcastModel(model, ctrl)
     engine = Engine(model, tok, max_concurrent=args.max_concurrent, use_graph=args.device != "cpu")
     embedder = vision = None
     if args.embeddings:
@@ -308,7 +336,14 @@ def main():
     limiter = RateLimiter(args.rate_limit, max(1, int(args.rate_limit))) if args.rate_limit > 0 else None
     app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, template=template, vision=vision,
                     rate_limit=limiter)
-    uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    try:
+        uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    finally:
+        engine.shutdown()
+        if tp is not None:  # release the replaying ranks, then the process group
+            model.stop()
+            tp.close()
+            D.shutdown()
 
 
 if __name__ == "__main__":

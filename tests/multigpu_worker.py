@@ -234,12 +234,33 @@ def check_ep(info):
     print(f"OK ep world={w} err={err:.2e}", flush=True)
 
 
+def check_mla_tp(info):
+    """DeepSeek-V2-family MLA model with heads, experts and FFNs split over all ranks against one GPU."""
+    from aether_b200.models.deepseek import DeepSeekConfig, DeepSeekModel
+    from aether_b200.parallel.tp import TensorParallel
+
+    w = info.world
+    cfg = DeepSeekConfig(vocab=512, d_model=256, n_layers=2, n_heads=4 * w, d_ff=256 * w, first_dense=1,
+                         n_experts=4 * w, top_k=2, d_expert=64, n_shared=w, max_seq=64, init_std=0.05)
+    tp = TensorParallel(info)
+    m = DeepSeekModel(cfg, device=info.device, seed=1, max_batch=2, max_seq=64, tp=tp)
+    ref = DeepSeekModel(cfg, device=info.device, seed=1, max_batch=2, max_seq=64)
+    toks = torch.randint(0, 512, (2, 16), generator=torch.Generator().manual_seed(2)).to(info.device)
+    _, lt = m.prefill(toks, return_logits=True)
+    _, lr = ref.prefill(toks, return_logits=True)
+    err = float((lt - lr).norm() / lr.norm())
+    assert err < 3e-2, err
+    torch.cuda.synchronize()
+    tp.close()
+    print(f"OK mla_tp world={w} err={err:.2e}", flush=True)
+
+
 def main():
     info = D.init(timeout_s=120)
     from aether_b200.parallel.symm import SymmTeam
 
     team = SymmTeam(info)
-    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train", "fsdp", "cp", "ep"]
+    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train", "fsdp", "cp", "ep", "mla_tp"]
     if "allreduce" in which:
         check_allreduce(team, info)
     if "dp" in which:
@@ -256,6 +277,8 @@ def main():
         check_cp(info)
     if "ep" in which:
         check_ep(info)
+    if "mla_tp" in which:
+        check_mla_tp(info)
     torch.cuda.synchronize()
     dist.barrier()
     D.shutdown()

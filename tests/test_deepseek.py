@@ -187,3 +187,59 @@ def test_engine_serves_mla_model_cpu():
         assert rs[0].tokens == want
     finally:
         eng.shutdown()
+
+
+def _tp_worker(rank, world, port, kw, q):
+    import os
+
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+
+    class GlooTP:
+        def __init__(self):
+            self.rank, self.world = rank, world
+
+        def all_reduce_(self, t):
+            f = t.float()
+            dist.all_reduce(f)
+            t.copy_(f)
+            return t
+
+    cfg = DeepSeekConfig(**dict(TINY, **kw))
+    m = DeepSeekModel(cfg, device="cpu", seed=1, max_batch=2, max_seq=64, tp=GlooTP())
+    toks = torch.randint(0, 256, (2, 9), generator=torch.Generator().manual_seed(2))
+    _, logits = m.prefill(toks, return_logits=True)
+    nxt = m.generate(toks, 3, use_graph=False)
+    q.put((rank, logits, nxt))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(q_lora_rank=64, router="sigmoid", norm_topk=True)])
+def test_mla_tensor_parallel_matches_one_rank_cpu(kw):
+    """Heads, experts and FFN slices over 2 gloo ranks give the single-rank logits."""
+    import multiprocessing as mp
+    import socket
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, kw, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = {r: (lg, nx) for r, lg, nx in (q.get(timeout=300) for _ in ps)}
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    cfg = DeepSeekConfig(**dict(TINY, **kw))
+    m = DeepSeekModel(cfg, device="cpu", seed=1, max_batch=2, max_seq=64)
+    toks = torch.randint(0, 256, (2, 9), generator=torch.Generator().manual_seed(2))
+    _, ref = m.prefill(toks, return_logits=True)
+    for r in (0, 1):
+        lg, nx = got[r]
+        assert float((lg - ref).norm() / ref.norm()) < 3e-2, r
+    assert torch.equal(got[0][1], got[1][1])  # ranks agree on the generated tokens

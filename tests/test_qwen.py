@@ -116,3 +116,19 @@ def test_gpu_qwen3_qk_norm_graph_decode():
     out_g = m.generate(toks, 5, use_graph=True)
     out_e = m.generate(toks, 5, use_graph=False)
     assert float((out_g == out_e).float().mean()) > 0.9
+
+
+def test_shard_of_full_weights_equals_random_init_shard():
+    """QwenWeights.shard of the unsplit weights gives the same tensors as the
+    random-init TP shard (the path checkpoints take into TP serving)."""
+    from aether_b200.models.qwen import QwenConfig, QwenWeights
+
+    cfg = QwenConfig(vocab=256, d_model=128, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=256, max_seq=32)
+    full = QwenWeights(cfg, "cpu", seed=5)
+    for r in range(2):
+        a = QwenWeights(cfg, "cpu", seed=5, tp_rank=r, tp_size=2)
+        b = QwenWeights.shard(full, r, 2, "cpu")
+        for name in ("wqkv", "bqkv", "wo", "wgu", "wd"):
+            for x, y in zip(getattr(a, name), getattr(b, name)):
+                assert (x is None and y is None) or torch.equal(x, y), (r, name)
+        assert (a.hq, a.hkv, a.f) == (b.hq, b.hkv, b.f)
