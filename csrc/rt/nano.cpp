@@ -348,6 +348,22 @@ float aether_nano_train_step(void* h, const int32_t* ids, const int32_t* labels,
   return loss;
 }
 
+// Data-parallel halves of a step: forward + backward (gradient left in
+// aether_nano_grads, loss returned), and the update once the caller has
+// replaced the gradient with its mean over ranks.
+float aether_nano_forward_backward(void* h, const int32_t* ids, const int32_t* labels, int B) {
+  Nano* n = static_cast<Nano*>(h);
+  const float loss = n->forward(ids, labels, B, n->c.S);
+  n->backward(ids, labels, n->c.S);
+  return loss;
+}
+
+void aether_nano_apply_update(void* h, float lr, float wd, float clip, int64_t step) {
+  Nano* n = static_cast<Nano*>(h);
+  if (clip > 0.f) aether_rt::clip_grad_norm(n->g.data(), clip, n->total);
+  aether_rt::adamw(n->p.data(), n->g.data(), n->m.data(), n->v.data(), lr, 0.9f, 0.95f, 1e-8f, wd, step, n->total);
+}
+
 float aether_nano_loss(void* h, const int32_t* ids, const int32_t* labels, int B) {
   Nano* n = static_cast<Nano*>(h);
   return n->forward(ids, labels, B, n->c.S);

@@ -292,3 +292,35 @@ def test_chat_template_subset_and_tool_call():
             pass
     call = json.loads(R.render_tool_call("get_weather", '{"city": "Paris"}'))
     assert call == {"type": "function", "function": {"name": "get_weather", "arguments": '{"city": "Paris"}'}}
+
+
+def test_aether_train_data_parallel_in_process_equals_multi_process(tmp_path):
+    """aether-train --world-size 2: the in-process replicas and two processes
+    meeting over TCP train the same model (byte-identical checkpoints)."""
+    import json
+    import os
+    import socket
+    import subprocess
+
+    from aether_b200 import runtime as R
+
+    R.lib()
+    exe = os.path.join(os.path.dirname(R.LIB_PATH), "bin", "aether-train")
+    common = ["--world-size", "2", "--steps", "12", "--batch", "4", "--log-every", "100", "--gen", "4"]
+    a = subprocess.run([exe, *common, "--out", str(tmp_path / "inproc")], capture_output=True, text=True, timeout=300)
+    assert a.returncode == 0, a.stderr
+    assert "replicas identical" in a.stderr
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = dict(os.environ, AETHER_COMM_ADDR=f"127.0.0.1:{port}")
+    procs = [subprocess.Popen([exe, *common, "--rank", str(r), "--out", str(tmp_path / f"mp{r}")], env=env,
+                              stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True) for r in range(2)]
+    outs = [p.communicate(timeout=300) for p in procs]
+    assert all(p.returncode == 0 for p in procs), [o[1][-500:] for o in outs]
+    assert json.loads(outs[0][0])["final_loss"] == json.loads(a.stdout)["final_loss"]
+    w_in = open(str(tmp_path / "inproc") + ".weights", "rb").read()
+    w_mp = open(str(tmp_path / "mp0") + ".weights", "rb").read()
+    assert w_in == w_mp
+    assert not os.path.exists(str(tmp_path / "mp1") + ".weights")  # rank 0 writes the checkpoint
