@@ -180,8 +180,10 @@ class GPT:
         kernels, and the normalised q, k and the untouched v are reassembled."""
         T, a = qkv.shape[0], self.arena
         eps = self.cfg.norm_eps
-        q = A.rmsnorm(qkv[:, : Hq * D].reshape(T * Hq, D), a[f"l{i}.q_norm"], eps).view(T, Hq * D)
-        k = A.rmsnorm(qkv[:, Hq * D : (Hq + Hkv) * D].reshape(T * Hkv, D), a[f"l{i}.k_norm"], eps).view(T, Hkv * D)
+        # contiguous head rows (with one head a reshape would keep the qkv row stride)
+        q = A.rmsnorm(qkv[:, : Hq * D].contiguous().view(T * Hq, D), a[f"l{i}.q_norm"], eps).view(T, Hq * D)
+        k = A.rmsnorm(qkv[:, Hq * D : (Hq + Hkv) * D].contiguous().view(T * Hkv, D), a[f"l{i}.k_norm"],
+                      eps).view(T, Hkv * D)
         return torch.cat([q, k, qkv[:, (Hq + Hkv) * D :]], 1)
 
     def freeze(self) -> None:
