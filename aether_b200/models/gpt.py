@@ -120,6 +120,9 @@ class GPT:
         tp_size = self.tp.world if self.tp else 1
         # the shared q/k norm weights would get only this rank's heads' gradient
         assert not (cfg.qk_norm and self.tp is not None), "qk_norm with tensor parallelism is not supported"
+        if self.tp is not None and self.tp.sp:
+            assert first and last and self.cp is None and shard is None, \
+                "sequence parallelism needs the whole model on a flat arena, without CP"
         assert cfg.n_heads % tp_size == 0 and cfg.n_kv_heads % tp_size == 0 and cfg.d_ff % tp_size == 0
         self.device = torch.device(device)
         self.layers = list(range(cfg.n_layers) if layers is None else layers)
@@ -169,6 +172,10 @@ class GPT:
             return A.linear(x, w, residual=residual)
         from ..parallel import tp_train as T
 
+        if self.tp.sp:  # x and the residual are this rank's token rows
+            if name in T.COLUMN:
+                return T.sp_column_linear(x, w, self.tp)
+            return T.sp_row_linear(x, w, residual, self.tp)
         if name in T.COLUMN:
             return A.linear(T.tp_copy(x, self.tp), w)
         y = A.linear(x, w, residual=residual.detach() if (residual is not None and self.tp.rank == 0) else None)
@@ -214,8 +221,14 @@ class GPT:
         Hq, Hkv, D = cfg.n_heads // tpw, cfg.n_kv_heads // tpw, cfg.head_dim
         scale = 1.0 / math.sqrt(D)
         pos = self.positions(B, S)
+        sp = self.tp is not None and self.tp.sp
         if self.first:
             x = A.embedding(a["tok_emb"], ids.reshape(-1))  # [T, d]
+        if sp:
+            from ..parallel import tp_train as T
+
+            assert x.shape[0] % self.tp.world == 0, "sequence parallelism needs B*S divisible by the TP degree"
+            x = T.sp_split(x, self.tp)
         lin = self._linear
         for i in self.layers:
             h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
@@ -234,7 +247,28 @@ class GPT:
             gu = lin(i, "wgu", h)
             act = A.swiglu(gu)
             x = lin(i, "wd", act, residual=x)
+        if sp:
+            x = T.sp_gather(x, self.tp)
         return A.rmsnorm(x, a["final_norm"], cfg.norm_eps) if self.last else x
+
+    def finish_grads(self) -> None:
+        """After the last backward of a step: under sequence parallelism each
+        TP rank holds the per-layer norm gradients of its own tokens only, so
+        they are summed over the TP group (one all-reduce of 2 * layers * d
+        floats). Everything else already holds the full gradient."""
+        if self.tp is None or not self.tp.sp:
+            return
+        gs = [getattr(self.arena[f"l{i}.{n}"], "main_grad", None) for i in self.layers
+              for n in ("attn_norm", "mlp_norm")]
+        gs = [g for g in gs if g is not None]  # frozen base weights (adapters) have none
+        if not gs:
+            return
+        flat = torch.cat([g.reshape(-1) for g in gs])
+        self.tp.all_reduce_(flat)
+        off = 0
+        for g in gs:
+            g.view(-1).copy_(flat[off : off + g.numel()])
+            off += g.numel()
 
     def _loss(self, ids, targets, loss_scale, x):
         assert self.last, "loss needs the last stage"

@@ -13,6 +13,16 @@ backward) sits in front of each column-parallel projection, ``tp_reduce``
 residual is added by TP rank 0's GEMM epilogue only, so the sum carries it
 once. Two all-reduces per layer forward and two backward.
 
+Sequence parallelism (``make_mesh(..., sequence_parallel=True)``): between
+the projections the [T, d] residual stream, its norms and their saved
+activations are split by token over the TP ranks; each all-reduce becomes a
+reduce-scatter after the row-parallel GEMM plus an all-gather before the next
+column-parallel one (the column GEMM keeps only its local rows and gathers them
+again in backward, overlapped with the input-gradient GEMM). The per-layer norm
+weights then see only their rank's tokens, so ``GPT.finish_grads`` sums their
+gradients over the TP group; the embedding output is split after the lookup
+and the final norm, LM head and loss run on the all-gathered rows.
+
 The all-reduce is pluggable: NCCL over the TP process group (the baseline), or
 the in-kernel symmetric-memory all-reduce (``parallel.symm.SymmTeam``, NVLS
 ``multimem.ld_reduce`` / ``multimem.st`` or one-shot peer loads).
@@ -20,7 +30,9 @@ the in-kernel symmetric-memory all-reduce (``parallel.symm.SymmTeam``, NVLS
 Reference: the Megatron plan of runtime/src/tensor_parallel.rs:8-29
 (column-parallel QKV and gate/up, row-parallel o_proj and down_proj, 2
 all-reduces per block, KV heads replicated below TP = n_kv) -- which the
-reference only executes on one GPU -- and the TP4 x DP2 training target.
+reference only executes on one GPU -- and the TP4 x DP2 training target. The
+reference has no sequence parallelism (its long-context features are paged KV
+and split-K decode attention); the split here is Megatron's.
 """
 from __future__ import annotations
 
@@ -37,6 +49,7 @@ class TPGroup:
     group: object = None
     team: object = None  # SymmTeam for the in-kernel all-reduce (None: NCCL / gloo)
     _bufs: dict = None
+    sp: bool = False  # sequence parallelism: the residual stream split by token
 
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -66,7 +79,7 @@ class Mesh:
     dp_group: object
 
 
-def make_mesh(tp_size: int, use_symm: bool = False) -> Mesh:
+def make_mesh(tp_size: int, use_symm: bool = False, sequence_parallel: bool = False) -> Mesh:
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
     assert world % tp_size == 0, "world size must be a multiple of the TP degree"
@@ -88,7 +101,8 @@ def make_mesh(tp_size: int, use_symm: bool = False) -> Mesh:
 
         info = DistInfo(rank, world, rank, torch.device("cuda", torch.cuda.current_device()), "nccl")
         team = SymmTeam(info, group=tp_group)
-    return Mesh(TPGroup(rank % tp_size, tp_size, tp_group, team), rank // tp_size, dp_size, dp_group)
+    return Mesh(TPGroup(rank % tp_size, tp_size, tp_group, team, sp=sequence_parallel and tp_size > 1),
+                rank // tp_size, dp_size, dp_group)
 
 
 class _Copy(torch.autograd.Function):
@@ -138,6 +152,155 @@ def tp_copy(x, tp):
 
 def tp_reduce(y, tp):
     return _Reduce.apply(y, tp) if tp is not None and tp.world > 1 else y
+
+
+# ---------------------------------------------------------------------------- sequence parallelism
+# The residual stream (and with it the norms and their saved activations) is
+# split by token over the TP ranks: rank r holds rows [r*Tl, (r+1)*Tl) of the
+# [T, d] hidden state. A column-parallel projection all-gathers its input rows
+# (and reduce-scatters the input gradient), a row-parallel one reduce-scatters
+# its partial sums (and all-gathers the output gradient): the same bytes as the
+# two all-reduces, split into their halves, with 1/tp of the activations kept.
+def _gather_tokens(t: torch.Tensor, tp: TPGroup, async_op: bool = False):
+    """[Tl, ...] on every TP rank -> [tp*Tl, ...] (rank r's rows at r*Tl)."""
+    t = t.contiguous()
+    out = torch.empty((tp.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    if t.is_cuda:
+        work = dist.all_gather_into_tensor(out, t, group=tp.group, async_op=async_op)
+    else:
+        work = dist.all_gather(list(out.chunk(tp.world)), t, group=tp.group, async_op=async_op)
+    return out, work
+
+
+def _scatter_tokens(t: torch.Tensor, tp: TPGroup, async_op: bool = False):
+    """[tp*Tl, ...] partial sums on every rank -> this rank's rows of the sum."""
+    t = t.contiguous()
+    Tl = t.shape[0] // tp.world
+    if t.is_cuda:
+        out = torch.empty((Tl,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        work = dist.reduce_scatter_tensor(out, t, group=tp.group, async_op=async_op)
+        return out, work
+    full = t.clone()  # gloo has no reduce-scatter
+    dist.all_reduce(full, group=tp.group)
+    return full[tp.rank * Tl : (tp.rank + 1) * Tl].clone(), None
+
+
+def _wgrad(dy, x, w):
+    """dW = dy^T x, accumulated into w's fp32 main gradient when it has one."""
+    from ..ops import functional as F
+    from ..ops.autograd import _main_grad
+
+    mg = _main_grad(w)
+    if mg is not None:
+        F.gemm(dy, x, a_mn=True, b_mn=True, out=mg, accumulate=True)
+        return None
+    return F.gemm(dy, x, a_mn=True, b_mn=True, out_dtype=torch.float32).to(w.dtype)
+
+
+class _SPColumnLinear(torch.autograd.Function):
+    """y = all_gather(h) @ w^T. Only the local rows h are saved: backward
+    gathers them again on the communication stream while the input-gradient
+    GEMM runs, and reduce-scatters that gradient while the weight-gradient
+    GEMM runs."""
+
+    @staticmethod
+    def forward(ctx, h, w, tp):
+        from ..ops import functional as F
+
+        hf, _ = _gather_tokens(h, tp)
+        ctx.tp = tp
+        ctx.save_for_backward(h, w)
+        return F.gemm(hf, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..ops import functional as F
+
+        h, w = ctx.saved_tensors
+        tp = ctx.tp
+        dy = dy.contiguous()
+        hf, gwork = _gather_tokens(h, tp, async_op=True)
+        dhf = F.gemm(dy, w, b_mn=True)
+        dh, swork = _scatter_tokens(dhf, tp, async_op=True)
+        if gwork is not None:
+            gwork.wait()
+        dw = _wgrad(dy, hf, w) if ctx.needs_input_grad[1] else None
+        if swork is not None:
+            swork.wait()
+        return dh, dw, None
+
+
+class _SPRowLinear(torch.autograd.Function):
+    """x_out = reduce_scatter(o @ w^T) + r: o holds this rank's heads / FFN
+    columns for all T tokens, r and x_out this rank's token rows."""
+
+    @staticmethod
+    def forward(ctx, o, w, r, tp):
+        from ..ops import functional as F
+
+        y, _ = _scatter_tokens(F.gemm(o, w), tp)
+        ctx.tp = tp
+        ctx.has_r = r is not None
+        ctx.save_for_backward(o, w)
+        return y.add_(r) if r is not None else y
+
+    @staticmethod
+    def backward(ctx, dx):
+        from ..ops import functional as F
+
+        o, w = ctx.saved_tensors
+        dyf, _ = _gather_tokens(dx, ctx.tp)
+        do = F.gemm(dyf, w, b_mn=True) if ctx.needs_input_grad[0] else None
+        dw = _wgrad(dyf, o, w) if ctx.needs_input_grad[1] else None
+        return do, dw, (dx if ctx.has_r else None), None
+
+
+class _SPSplit(torch.autograd.Function):
+    """Full rows computed identically on every rank -> this rank's rows; the
+    gradient of the full tensor is the all-gather of the row gradients."""
+
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        Tl = x.shape[0] // tp.world
+        return x[tp.rank * Tl : (tp.rank + 1) * Tl].clone()
+
+    @staticmethod
+    def backward(ctx, dx):
+        return _gather_tokens(dx, ctx.tp)[0], None
+
+
+class _SPGather(torch.autograd.Function):
+    """This rank's rows -> all rows, followed by work that every rank repeats
+    on the full tensor (final norm, LM head, loss): the incoming gradient is
+    the same on every rank, so each keeps its own rows of it."""
+
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        return _gather_tokens(x, tp)[0]
+
+    @staticmethod
+    def backward(ctx, dx):
+        tp = ctx.tp
+        Tl = dx.shape[0] // tp.world
+        return dx[tp.rank * Tl : (tp.rank + 1) * Tl].contiguous(), None
+
+
+def sp_column_linear(h, w, tp):
+    return _SPColumnLinear.apply(h, w, tp)
+
+
+def sp_row_linear(o, w, r, tp):
+    return _SPRowLinear.apply(o, w, r, tp)
+
+
+def sp_split(x, tp):
+    return _SPSplit.apply(x, tp)
+
+
+def sp_gather(x, tp):
+    return _SPGather.apply(x, tp)
 
 
 # ---------------------------------------------------------------------------- sharding of full tensors

@@ -71,6 +71,9 @@ class Trainer:
                 loss = self.model.loss(ids.contiguous(), tgt.contiguous(), loss_scale=1.0 / n_tok)
                 loss.backward()
                 self._loss_acc += loss.detach()
+            finish = getattr(self.model, "finish_grads", None)
+            if finish is not None:  # gradients that the model reduces itself (sequence parallelism)
+                finish()
         with self._section("optimizer"):
             self.dp.step(lr=self.lr_at(self.step_idx))
         self.step_idx += 1

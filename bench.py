@@ -119,6 +119,8 @@ def parse():
                     help="fused: one-kernel NVLink reduce + AdamW + broadcast; nccl: NCCL reduce-scatter/all-gather")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (TP x DP mesh, e.g. --gpus 8 --tp 4)")
     ap.add_argument("--pp", type=int, default=1, help="pipeline stages (1F1B over NCCL p2p); --gpus must equal --pp")
+    ap.add_argument("--sp", action="store_true",
+                    help="sequence parallelism inside TP (residual stream split by token over the TP ranks)")
     ap.add_argument("--tp-comm", default="symm", choices=["symm", "nccl"],
                     help="TP all-reduce: in-kernel symmetric-memory (NVLS / peer loads) or NCCL")
     return ap.parse_args()
@@ -161,7 +163,7 @@ def main():
     if tp > 1:
         from aether_b200.parallel.tp_train import make_mesh
 
-        mesh = make_mesh(tp, use_symm=args.tp_comm == "symm")
+        mesh = make_mesh(tp, use_symm=args.tp_comm == "symm", sequence_parallel=args.sp)
         dinfo = D.DistInfo(mesh.dp_rank, dp_world, info.local_rank, dev, info.backend)
     if dp_world > 1 and args.dp == "fused":
         from aether_b200.parallel.dp import FusedDataParallel, team_alloc
@@ -271,7 +273,7 @@ def main():
                 "micro_batch": args.micro_batch,
                 "parallelism": (f"tp{tp}x" if tp > 1 else "") + f"dp{dp_world}"
                 + ((" zero1 " + ("fused-nvlink" if args.dp == "fused" else "nccl")) if dp_world > 1 else "")
-                + (f" tp-allreduce-{args.tp_comm}" if tp > 1 else ""),
+                + (f" tp-allreduce-{args.tp_comm}" if tp > 1 else "") + (" sp" if tp > 1 and args.sp else ""),
                 "optimizer": "AdamW lr 3e-4 betas (0.9,0.95) wd 0.1, fp32 master",
                 "l2": "no flush needed: per-step working set (2.7 GB bf16 weights + activations) >> 126 MB L2",
             },

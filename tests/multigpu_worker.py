@@ -121,20 +121,23 @@ def check_pp(info):
     print(f"OK pp losses={[round(float(x), 4) for x in t]}", flush=True)
 
 
-def check_tp_train(info):
-    """Megatron TP over all ranks (in-kernel symmetric-memory all-reduce) against one GPU."""
+def check_tp_train(info, sp=False):
+    """Megatron TP over all ranks (in-kernel symmetric-memory all-reduce; with
+    sp, NCCL reduce-scatter / all-gather around a token-split residual) against
+    one GPU."""
     from aether_b200.models.gpt import GPT, GPTConfig
     from aether_b200.parallel.tp_train import make_mesh, shard_tensor
 
     w = info.world
     cfg = GPTConfig(vocab=512, d_model=128 * w, n_layers=2, n_heads=w, n_kv_heads=w, d_ff=256 * w, max_seq=128)
-    mesh = make_mesh(w, use_symm=True)
+    mesh = make_mesh(w, use_symm=True, sequence_parallel=sp)
     m = GPT(cfg, device=info.device, seed=13, tp=mesh.tp)
     ref = GPT(cfg, device=info.device, seed=13)
     toks = torch.randint(0, 512, (2, 129), generator=torch.Generator().manual_seed(2))
     ids, tg = toks[:, :-1].contiguous().to(info.device), toks[:, 1:].contiguous().to(info.device)
     lt = m.loss(ids, tg)
     lt.backward()
+    m.finish_grads()
     lr = ref.loss(ids, tg)
     lr.backward()
     assert abs(float(lt.detach()) - float(lr.detach())) < 1e-2 * abs(float(lr.detach()))
@@ -146,7 +149,7 @@ def check_tp_train(info):
         assert err < 5e-2, (n, err)
     torch.cuda.synchronize()
     assert _ext.check_status() == 0
-    print(f"OK tp_train loss={float(lt.detach()):.4f}", flush=True)
+    print(f"OK tp_train{'_sp' if sp else ''} loss={float(lt.detach()):.4f}", flush=True)
 
 
 def check_fsdp(info):
@@ -271,6 +274,7 @@ def main():
         check_pp(info)
     if "tp_train" in which:
         check_tp_train(info)
+        check_tp_train(info, sp=True)
     if "fsdp" in which:
         check_fsdp(info)
     if "cp" in which:

@@ -1,6 +1,8 @@
 """Tensor-parallel training on gloo ranks (CPU): a TP=2 GPT gives the loss and
 (sharded) gradients of the unsharded model, and a TP=2 x DP=2 mesh trains to
-the same parameters as one process over the same global batch."""
+the same parameters as one process over the same global batch -- with the
+residual stream replicated over the TP ranks and with it split by token
+(sequence parallelism)."""
 import os
 import socket
 import sys
@@ -23,7 +25,7 @@ def _tokens(step, n=4):
     return torch.randint(0, 128, (n, 17), generator=torch.Generator().manual_seed(50 + step))
 
 
-def _worker(rank, world, tp, port, q):
+def _worker(rank, world, tp, port, q, sp=False):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
                       MASTER_PORT=str(port))
     sys.path.insert(0, ROOT)
@@ -34,12 +36,14 @@ def _worker(rank, world, tp, port, q):
     from aether_b200.train import Trainer
 
     D.init(device="cpu", timeout_s=60)
-    mesh = make_mesh(tp)
+    mesh = make_mesh(tp, sequence_parallel=sp)
+    assert mesh.tp.sp == sp
     m = GPT(GPTConfig(**CFG), device="cpu", seed=9, tp=mesh.tp, pad_multiple=mesh.dp_world)
     # one gradient for the checks against the unsharded model
     toks = _tokens(0)
     loss = m.loss(toks[:, :-1].contiguous(), toks[:, 1:].contiguous())
     loss.backward()
+    m.finish_grads()
     grads = {n: m.arena.grad[s.offset : s.offset + s.numel].view(s.shape).clone().numpy() for n, s in m.arena.slots.items()}
     m.arena.zero_grad()
     # then a few training steps over the mesh: each DP rank takes its half of the global batch
@@ -57,13 +61,13 @@ def _worker(rank, world, tp, port, q):
     D.shutdown()
 
 
-def _run(world, tp):
+def _run(world, tp, sp=False):
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, tp, port, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, tp, port, q, sp)) for r in range(world)]
     for p in ps:
         p.start()
     got = {}
@@ -130,3 +134,11 @@ def test_tp2_matches_single_process():
 
 def test_tp2_dp2_mesh_matches_single_process():
     _check(_run(4, 2), 2)
+
+
+def test_tp2_sequence_parallel_matches_single_process():
+    _check(_run(2, 2, sp=True), 2)
+
+
+def test_tp2_dp2_sequence_parallel_mesh_matches_single_process():
+    _check(_run(4, 2, sp=True), 2)
