@@ -1,0 +1,1504 @@
+// libaether_dev: the device-handle C ABI (aether_dev_* / aether_op_*_cuda).
+//
+// Programs written against the reference runtime (and the code its language
+// compiler emits for Tensor method calls) drive the GPU through i64 handles:
+// allocate a buffer, copy host data in, call ops by handle, copy results out.
+// This library keeps those names, argument orders and return conventions
+// (0 = ok, negative = error; handles are slot + 1, 0 = allocation failed) but
+// none of the reference's machinery:
+//   * one handle table for every element kind (f32 / i32 / u8), each entry
+//     holding a stream-ordered allocation (cudaMallocAsync) and its device;
+//   * a context per device (stream, cuBLAS handle, captured graph) instead of
+//     one global device-0 context, so several GPUs can be driven from one
+//     process (aether_dev_set_device);
+//   * every op checks each handle's kind and that the extents it is about to
+//     touch fit the allocation, and returns -1 instead of launching;
+//   * ahead-of-time sm_100a kernels (no runtime compilation). GEMMs are plain
+//     f32 library GEMMs (cuBLAS, row-major through the transposed view; TF32
+//     tensor cores with AETHER_DEV_TF32=1); everything else is a kernel in
+//     this file: one CTA per row with shuffle reductions for norms / softmax /
+//     cross-entropy, column-tiled deterministic reductions for parameter
+//     gradients, and quantised mat-vecs that dequantise GGUF blocks in
+//     registers (one warp per output row, 32-value chunks per lane).
+//
+// Reference: runtime/src/cuda.rs:7230-7410 (registry), 7419-8420 (GEMM family,
+// training ops, graphs, sync), 8442-8480 (RoPE), 10185-10380 (GQA, embedding,
+// SiLU, transpose, in-place ops), 10388-11120 (dequant and fused quantised
+// mat-vecs), 11553 (d2d), 11609-11680 (KV append and one-token attention).
+#include <cublas_v2.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#define AE_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+enum Kind { KF32 = 0, KI32 = 1, KU8 = 2 };
+
+struct Buf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  int dev = -1;
+  int kind = 0;
+};
+
+struct Ctx {
+  bool ready = false;
+  cudaStream_t s = nullptr;
+  cublasHandle_t blas = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+constexpr int kMaxDev = 64;
+std::mutex g_mu;
+std::vector<Buf> g_bufs;
+std::vector<int64_t> g_free;
+Ctx g_ctx[kMaxDev];
+thread_local char g_err[256] = "";
+
+void set_err(const char* what, cudaError_t e) {
+  snprintf(g_err, sizeof(g_err), "%s: %s", what, cudaGetErrorString(e));
+}
+
+int cur_dev() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+Ctx* ctx_for(int d) {
+  if (d < 0 || d >= kMaxDev) return nullptr;
+  Ctx& c = g_ctx[d];
+  if (c.ready) return &c;
+  std::lock_guard<std::mutex> l(g_mu);
+  if (c.ready) return &c;
+  cudaError_t e = cudaStreamCreateWithFlags(&c.s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    set_err("stream", e);
+    return nullptr;
+  }
+  if (cublasCreate(&c.blas) != CUBLAS_STATUS_SUCCESS) {
+    snprintf(g_err, sizeof(g_err), "cublasCreate failed");
+    return nullptr;
+  }
+  cublasSetStream(c.blas, c.s);
+  const char* tf32 = getenv("AETHER_DEV_TF32");
+  cublasSetMathMode(c.blas, (tf32 && tf32[0] == '1') ? CUBLAS_TF32_TENSOR_OP_MATH : CUBLAS_DEFAULT_MATH);
+  c.ready = true;
+  return &c;
+}
+
+Ctx* ctx() { return ctx_for(cur_dev()); }
+
+// The buffer behind handle h if it has the given kind and holds at least
+// `need` elements of size `esz`; nullptr otherwise.
+void* lookup(int64_t h, int kind, size_t need, size_t esz) {
+  std::lock_guard<std::mutex> l(g_mu);
+  if (h <= 0 || (size_t)h > g_bufs.size()) return nullptr;
+  const Buf& b = g_bufs[h - 1];
+  if (!b.p || b.kind != kind || need * esz > b.bytes) return nullptr;
+  return b.p;
+}
+
+size_t capacity(int64_t h, size_t esz) {
+  std::lock_guard<std::mutex> l(g_mu);
+  if (h <= 0 || (size_t)h > g_bufs.size() || !g_bufs[h - 1].p) return 0;
+  return g_bufs[h - 1].bytes / esz;
+}
+
+float* F(int64_t h, size_t need) { return (float*)lookup(h, KF32, need, 4); }
+int* I(int64_t h, size_t need) { return (int*)lookup(h, KI32, need, 4); }
+uint8_t* U(int64_t h, size_t need) { return (uint8_t*)lookup(h, KU8, need, 1); }
+
+int64_t alloc(size_t n, size_t esz, int kind) {
+  Ctx* c = ctx();
+  if (!c || n == 0) return 0;
+  void* p = nullptr;
+  cudaError_t e = cudaMallocAsync(&p, n * esz, c->s);
+  if (e != cudaSuccess) {
+    set_err("alloc", e);
+    return 0;
+  }
+  cudaMemsetAsync(p, 0, n * esz, c->s);  // handles start zeroed, like the reference's alloc_zeros
+  std::lock_guard<std::mutex> l(g_mu);
+  Buf b{p, n * esz, cur_dev(), kind};
+  if (!g_free.empty()) {
+    int64_t h = g_free.back();
+    g_free.pop_back();
+    g_bufs[h - 1] = b;
+    return h;
+  }
+  g_bufs.push_back(b);
+  return (int64_t)g_bufs.size();
+}
+
+int release(int64_t h, int kind) {
+  Buf b;
+  {
+    std::lock_guard<std::mutex> l(g_mu);
+    if (h <= 0 || (size_t)h > g_bufs.size() || !g_bufs[h - 1].p || g_bufs[h - 1].kind != kind) return 0;
+    b = g_bufs[h - 1];
+    g_bufs[h - 1] = Buf{};
+    g_free.push_back(h);
+  }
+  Ctx* c = ctx_for(b.dev);
+  if (c) cudaFreeAsync(b.p, c->s);
+  return 0;
+}
+
+int copy(void* dst, const void* src, size_t bytes, cudaMemcpyKind k) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, k, c->s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->s);  // the host buffer is the caller's again on return
+  if (e != cudaSuccess) {
+    set_err("copy", e);
+    return -2;
+  }
+  return 0;
+}
+
+int launched(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(what, e);
+    return -2;
+  }
+  return 0;
+}
+
+unsigned blocks(size_t n, unsigned t = 256) { return (unsigned)((n + t - 1) / t); }
+
+// ---------------------------------------------------------------------------------------------- reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Sum over the CTA (blockDim.x a multiple of 32, at most 1024); every thread gets the result.
+__device__ float block_sum(float v) {
+  __shared__ float sh[32];
+  __shared__ float total;
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float t = l < (int)(blockDim.x >> 5) ? sh[l] : 0.f;
+    t = warp_sum(t);
+    if (l == 0) total = t;
+  }
+  __syncthreads();
+  return total;
+}
+
+__device__ float block_max(float v) {
+  __shared__ float sh[32];
+  __shared__ float total;
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float t = l < (int)(blockDim.x >> 5) ? sh[l] : -INFINITY;
+    t = warp_max(t);
+    if (l == 0) total = t;
+  }
+  __syncthreads();
+  return total;
+}
+
+constexpr int kRowThreads = 256;
+
+// ---------------------------------------------------------------------------------------------- elementwise
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))  (Hendrycks & Gimpel's approximation)
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.f + tanhf(u));
+}
+
+__device__ __forceinline__ float gelu_tanh_grad(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  const float t = tanhf(u);
+  const float du = 0.7978845608028654f * (1.f + 3.f * 0.044715f * x * x);
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * du;
+}
+
+__global__ void k_add(const float* a, const float* b, float* o, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) o[i] = a[i] + b[i];
+}
+__global__ void k_add_inplace(float* x, const float* y, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) x[i] += y[i];
+}
+__global__ void k_mul_inplace(float* x, const float* y, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) x[i] *= y[i];
+}
+__global__ void k_scale(float* x, float s, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) x[i] *= s;
+}
+__global__ void k_gelu(const float* x, float* y, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) y[i] = gelu_tanh(x[i]);
+}
+__global__ void k_gelu_bwd(const float* x, const float* dy, float* dx, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) dx[i] = dy[i] * gelu_tanh_grad(x[i]);
+}
+__global__ void k_gelu_erf(const float* x, float* y, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) y[i] = 0.5f * x[i] * (1.f + erff(x[i] * 0.7071067811865476f));
+}
+__global__ void k_silu(float* x, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) x[i] = x[i] / (1.f + expf(-x[i]));
+}
+__global__ void k_silu_bwd(const float* x, const float* dy, float* dx, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float s = 1.f / (1.f + expf(-x[i]));
+    dx[i] = dy[i] * s * (1.f + x[i] * (1.f - s));
+  }
+}
+__global__ void k_bias_add(float* x, const float* b, size_t rows, int cols) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < rows * cols) x[i] += b[i % cols];
+}
+__global__ void k_transpose_021(const float* in, float* out, int d0, int d1, int d2) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;  // index into out [d1, d0, d2]
+  size_t n = (size_t)d0 * d1 * d2;
+  if (i >= n) return;
+  const int k = (int)(i % d2);
+  const size_t r = i / d2;
+  const int a = (int)(r % d0), b = (int)(r / d0);
+  out[i] = in[((size_t)a * d1 + b) * d2 + k];
+}
+__global__ void k_embed(const float* table, const int* ids, float* out, int t, int d, int vocab) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)t * d) return;
+  const int r = (int)(i / d), j = (int)(i % d);
+  const int id = ids[r];
+  out[i] = (id >= 0 && id < vocab) ? table[(size_t)id * d + j] : 0.f;
+}
+__global__ void k_embed_scatter(const float* dout, const int* ids, float* dtable, int t, int d, int vocab) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)t * d) return;
+  const int r = (int)(i / d), j = (int)(i % d);
+  const int id = ids[r];
+  if (id >= 0 && id < vocab) atomicAdd(&dtable[(size_t)id * d + j], dout[i]);
+}
+__global__ void k_gqa_repeat(const float* in, float* out, int seq, int hkv, int hd, int hq) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)seq * hq * hd) return;
+  const int k = (int)(i % hd);
+  const size_t r = i / hd;
+  const int h = (int)(r % hq), s = (int)(r / hq);
+  out[i] = in[((size_t)s * hkv + h / (hq / hkv)) * hd + k];
+}
+__global__ void k_gqa_reduce(const float* dout, float* din, int seq, int hkv, int hd, int hq) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)seq * hkv * hd) return;
+  const int k = (int)(i % hd);
+  const size_t r = i / hd;
+  const int h = (int)(r % hkv), s = (int)(r / hkv);
+  const int g = hq / hkv;
+  float acc = 0.f;
+  for (int j = 0; j < g; ++j) acc += dout[((size_t)s * hq + h * g + j) * hd + k];
+  din[i] = acc;
+}
+__global__ void k_append_kv(const float* kn, const float* vn, float* kc, float* vc, int pos, int dkv) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < dkv) {
+    kc[(size_t)pos * dkv + i] = kn[i];
+    vc[(size_t)pos * dkv + i] = vn[i];
+  }
+}
+__global__ void k_adamw(float* p, const float* g, float* m, float* v, float lr, float b1, float b2, float eps, float wd,
+                        float bc1, float bc2, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gi = g[i];
+  const float mi = b1 * m[i] + (1.f - b1) * gi;
+  const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+  m[i] = mi;
+  v[i] = vi;
+  p[i] -= lr * ((mi * bc1) / (sqrtf(vi * bc2) + eps) + wd * p[i]);
+}
+
+// RoPE on x [seq, heads, hd], pairs (i, i + hd/2), angle (pos_start + t) * base^(-2i/hd);
+// dir = -1 rotates back (the backward pass).
+__global__ void k_rope(float* x, int seq, int heads, int hd, float base, int pos0, float dir) {
+  const int half = hd / 2;
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)seq * heads * half) return;
+  const int j = (int)(i % half);
+  const size_t r = i / half;
+  const int t = (int)(r / heads);
+  const float ang = (float)(t + pos0) * powf(base, -2.f * (float)j / (float)hd);
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  sn *= dir;
+  float* row = x + r * hd;
+  const float a = row[j], b = row[j + half];
+  row[j] = a * cs - b * sn;
+  row[j + half] = a * sn + b * cs;
+}
+
+// ---------------------------------------------------------------------------------------------- row kernels
+__global__ void k_softmax(const float* x, float* y, int d) {
+  const float* xr = x + (size_t)blockIdx.x * d;
+  float* yr = y + (size_t)blockIdx.x * d;
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) m = fmaxf(m, xr[j]);
+  m = block_max(m);
+  float s = 0.f;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) s += expf(xr[j] - m);
+  s = block_sum(s);
+  const float inv = 1.f / s;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) yr[j] = expf(xr[j] - m) * inv;
+}
+
+// dx = scale * y * (dy - sum(dy * y))
+__global__ void k_softmax_bwd(const float* y, const float* dy, float* dx, int d, float scale) {
+  const size_t o = (size_t)blockIdx.x * d;
+  float dot = 0.f;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) dot += y[o + j] * dy[o + j];
+  dot = block_sum(dot);
+  for (int j = threadIdx.x; j < d; j += blockDim.x) dx[o + j] = scale * y[o + j] * (dy[o + j] - dot);
+}
+
+// Causal softmax of pre-scaled scores, row i of each [s, s] matrix keeps columns <= i.
+__global__ void k_causal_softmax(float* a, int s) {
+  const int i = blockIdx.x % s;
+  float* r = a + (size_t)blockIdx.x * s;
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j <= i; j += blockDim.x) m = fmaxf(m, r[j]);
+  m = block_max(m);
+  float sum = 0.f;
+  for (int j = threadIdx.x; j <= i; j += blockDim.x) sum += expf(r[j] - m);
+  sum = block_sum(sum);
+  const float inv = 1.f / sum;
+  for (int j = threadIdx.x; j < s; j += blockDim.x) r[j] = j <= i ? expf(r[j] - m) * inv : 0.f;
+}
+
+// x (+ res, written back into x when res != null) -> layer norm; mean / rstd cached per row
+__global__ void k_layernorm(const float* a, const float* b, const float* g, const float* beta, float* y, float* mean,
+                            float* rstd, float eps, int d) {
+  const size_t o = (size_t)blockIdx.x * d;
+  float s = 0.f;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) s += a[o + j] + (b ? b[o + j] : 0.f);
+  const float mu = block_sum(s) / d;
+  float v = 0.f;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    const float t = a[o + j] + (b ? b[o + j] : 0.f) - mu;
+    v += t * t;
+  }
+  const float rs = rsqrtf(block_sum(v) / d + eps);
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    const float t = a[o + j] + (b ? b[o + j] : 0.f) - mu;
+    y[o + j] = t * rs * g[j] + (beta ? beta[j] : 0.f);
+  }
+  if (threadIdx.x == 0) {
+    if (mean) mean[blockIdx.x] = mu;
+    if (rstd) rstd[blockIdx.x] = rs;
+  }
+}
+
+__global__ void k_layernorm_bwd_dx(const float* x, const float* g, const float* mean, const float* rstd, const float* dy,
+                                   float* dx, int d) {
+  const size_t o = (size_t)blockIdx.x * d;
+  const float mu = mean[blockIdx.x], rs = rstd[blockIdx.x];
+  float s1 = 0.f, s2 = 0.f;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    const float gy = dy[o + j] * g[j];
+    s1 += gy;
+    s2 += gy * (x[o + j] - mu) * rs;
+  }
+  s1 = block_sum(s1) / d;
+  s2 = block_sum(s2) / d;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    const float xh = (x[o + j] - mu) * rs;
+    dx[o + j] = rs * (dy[o + j] * g[j] - s1 - xh * s2);
+  }
+}
+
+__global__ void k_rmsnorm(float* x, const float* res, const float* g, float* y, float eps, int d) {
+  const size_t o = (size_t)blockIdx.x * d;
+  float s = 0.f;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    float v = x[o + j];
+    if (res) {
+      v += res[o + j];
+      x[o + j] = v;  // fused residual add writes the sum back
+    }
+    s += v * v;
+  }
+  const float inv = rsqrtf(block_sum(s) / d + eps);
+  for (int j = threadIdx.x; j < d; j += blockDim.x) y[o + j] = x[o + j] * inv * g[j];
+}
+
+__global__ void k_rmsnorm_bwd_dx(const float* x, const float* g, const float* dy, float* dx, float* inv_rms, float eps,
+                                 int d) {
+  const size_t o = (size_t)blockIdx.x * d;
+  float ss = 0.f, dot = 0.f;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    ss += x[o + j] * x[o + j];
+    dot += dy[o + j] * g[j] * x[o + j];
+  }
+  const float inv = rsqrtf(block_sum(ss) / d + eps);
+  dot = block_sum(dot) / d;
+  for (int j = threadIdx.x; j < d; j += blockDim.x)
+    dx[o + j] = inv * (dy[o + j] * g[j] - x[o + j] * inv * inv * dot);
+  if (threadIdx.x == 0) inv_rms[blockIdx.x] = inv;
+}
+
+// Parameter gradients: sum over rows of a per-element product, per column.
+// 32 columns x 8 row stripes per CTA, fixed summation order (deterministic).
+// mode 0: dgamma = sum dy * (x - mean) * rstd and dbeta = sum dy (layer norm);
+// mode 1: dgamma = sum dy * x * inv_rms (RMSNorm).
+__global__ void k_colsum(const float* x, const float* dy, const float* mean, const float* rstd, float* dg, float* db,
+                         int rows, int d, int mode) {
+  __shared__ float sg[8][33], sb[8][33];
+  const int j = blockIdx.x * 32 + threadIdx.x;
+  float ag = 0.f, ab = 0.f;
+  if (j < d) {
+    for (int r = threadIdx.y; r < rows; r += 8) {
+      const size_t o = (size_t)r * d + j;
+      const float xh = mode == 0 ? (x[o] - mean[r]) * rstd[r] : x[o] * rstd[r];
+      ag += dy[o] * xh;
+      ab += dy[o];
+    }
+  }
+  sg[threadIdx.y][threadIdx.x] = ag;
+  sb[threadIdx.y][threadIdx.x] = ab;
+  __syncthreads();
+  if (threadIdx.y == 0 && j < d) {
+    float tg = 0.f, tb = 0.f;
+    for (int k = 0; k < 8; ++k) {
+      tg += sg[k][threadIdx.x];
+      tb += sb[k][threadIdx.x];
+    }
+    dg[j] = tg;
+    if (db) db[j] = tb;
+  }
+}
+
+// Cross-entropy: per-row softmax probabilities and -log p[label] (0 for labels outside [0, v)).
+__global__ void k_ce_fwd(const float* logits, const int* labels, float* probs, float* loss, int v) {
+  const size_t o = (size_t)blockIdx.x * v;
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < v; j += blockDim.x) m = fmaxf(m, logits[o + j]);
+  m = block_max(m);
+  float s = 0.f;
+  for (int j = threadIdx.x; j < v; j += blockDim.x) s += expf(logits[o + j] - m);
+  s = block_sum(s);
+  const float inv = 1.f / s;
+  for (int j = threadIdx.x; j < v; j += blockDim.x) probs[o + j] = expf(logits[o + j] - m) * inv;
+  if (threadIdx.x == 0) {
+    const int lab = labels[blockIdx.x];
+    loss[blockIdx.x] = (lab >= 0 && lab < v) ? -(logits[o + lab] - m - logf(s)) : 0.f;
+  }
+}
+
+__global__ void k_ce_bwd(const float* probs, const int* labels, float* dl, int b, int v) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)b * v) return;
+  const int r = (int)(i / v), c = (int)(i % v);
+  const float inv_b = 1.f / (float)b;
+  dl[i] = probs[i] * inv_b - (c == labels[r] ? inv_b : 0.f);
+}
+
+// One query token against a [cur_seq, n_kv * hd] KV cache: one CTA per query
+// head, scores in shared memory.
+__global__ void k_attn_seq1(const float* q, const float* kc, const float* vc, float* out, int cur, int hq, int hkv, int hd,
+                            float scale) {
+  extern __shared__ float sc[];
+  const int h = blockIdx.x, kvh = h / (hq / hkv), dkv = hkv * hd;
+  const float* qh = q + (size_t)h * hd;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int t = w; t < cur; t += nw) {  // one warp per key
+    const float* kr = kc + (size_t)t * dkv + (size_t)kvh * hd;
+    float acc = 0.f;
+    for (int k = l; k < hd; k += 32) acc += qh[k] * kr[k];
+    acc = warp_sum(acc);
+    if (l == 0) sc[t] = acc * scale;
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int t = threadIdx.x; t < cur; t += blockDim.x) m = fmaxf(m, sc[t]);
+  m = block_max(m);
+  float s = 0.f;
+  for (int t = threadIdx.x; t < cur; t += blockDim.x) {
+    const float e = expf(sc[t] - m);
+    sc[t] = e;
+    s += e;
+  }
+  s = block_sum(s);
+  const float inv = 1.f / s;
+  for (int k = threadIdx.x; k < hd; k += blockDim.x) {
+    float acc = 0.f;
+    for (int t = 0; t < cur; ++t) acc += sc[t] * vc[(size_t)t * dkv + (size_t)kvh * hd + k];
+    out[(size_t)h * hd + k] = acc * inv;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- GGUF blocks
+// Element types by their GGML numbers; block = (elements, bytes).
+enum Q { TF32 = 0, TF16 = 1, TQ4_0 = 2, TQ5_0 = 6, TQ8_0 = 8, TQ3_K = 11, TQ4_K = 12, TQ5_K = 13, TQ6_K = 14,
+         TIQ4_NL = 20, TIQ4_XS = 23 };
+
+bool block_of(int t, int* ne, int* nb) {
+  switch (t) {
+    case TF32: *ne = 1; *nb = 4; return true;
+    case TF16: *ne = 1; *nb = 2; return true;
+    case TQ4_0: *ne = 32; *nb = 18; return true;
+    case TQ5_0: *ne = 32; *nb = 22; return true;
+    case TQ8_0: *ne = 32; *nb = 34; return true;
+    case TIQ4_NL: *ne = 32; *nb = 18; return true;
+    case TQ3_K: *ne = 256; *nb = 110; return true;
+    case TQ4_K: *ne = 256; *nb = 144; return true;
+    case TQ5_K: *ne = 256; *nb = 176; return true;
+    case TQ6_K: *ne = 256; *nb = 210; return true;
+    case TIQ4_XS: *ne = 256; *nb = 136; return true;
+    default: return false;
+  }
+}
+
+__constant__ float c_iq4[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+__device__ __forceinline__ float h2f(const uint8_t* p) {
+  __half_raw r;
+  r.x = (unsigned short)(p[0] | (p[1] << 8));
+  return __half2float(__half(r));
+}
+
+// Six-bit (scale, min) pair j of the 12 packed bytes of a Q4_K / Q5_K super-block.
+__device__ __forceinline__ void k4_scale(const uint8_t* s, int j, float* sc, float* mn) {
+  if (j < 4) {
+    *sc = (float)(s[j] & 63);
+    *mn = (float)(s[j + 4] & 63);
+  } else {
+    *sc = (float)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
+    *mn = (float)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+  }
+}
+
+// The 32 values of chunk c (elements 32c .. 32c+31) of a row of type t.
+template <int T>
+__device__ __forceinline__ void chunk32(const uint8_t* row, int c, float* v) {
+  if constexpr (T == TF32) {
+    const float* p = (const float*)row + c * 32;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = p[i];
+  } else if constexpr (T == TF16) {
+    const uint8_t* p = row + c * 64;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = h2f(p + 2 * i);
+  } else if constexpr (T == TQ8_0) {
+    const uint8_t* b = row + c * 34;
+    const float d = h2f(b);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = d * (float)(int8_t)b[2 + i];
+  } else if constexpr (T == TQ4_0 || T == TIQ4_NL) {
+    const uint8_t* b = row + c * 18;
+    const float d = h2f(b);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int lo = b[2 + i] & 0x0F, hi = b[2 + i] >> 4;
+      if constexpr (T == TQ4_0) {
+        v[i] = d * (float)(lo - 8);
+        v[i + 16] = d * (float)(hi - 8);
+      } else {
+        v[i] = d * c_iq4[lo];
+        v[i + 16] = d * c_iq4[hi];
+      }
+    }
+  } else if constexpr (T == TQ5_0) {
+    const uint8_t* b = row + c * 22;
+    const float d = h2f(b);
+    const uint32_t qh = b[2] | (b[3] << 8) | (b[4] << 16) | ((uint32_t)b[5] << 24);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int lo = (b[6 + i] & 0x0F) | (((qh >> i) & 1) << 4);
+      const int hi = (b[6 + i] >> 4) | (((qh >> (i + 16)) & 1) << 4);
+      v[i] = d * (float)(lo - 16);
+      v[i + 16] = d * (float)(hi - 16);
+    }
+  } else if constexpr (T == TQ4_K || T == TQ5_K) {
+    const int j = c & 7;
+    const uint8_t* b = row + (size_t)(c >> 3) * (T == TQ4_K ? 144 : 176);
+    const float d = h2f(b), dmin = h2f(b + 2);
+    float sc, mn;
+    k4_scale(b + 4, j, &sc, &mn);
+    const float a = d * sc, o = dmin * mn;
+    const uint8_t* qs = b + (T == TQ4_K ? 16 : 48) + (j >> 1) * 32;
+    const int sh = (j & 1) * 4;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      int q = (qs[i] >> sh) & 0x0F;
+      if constexpr (T == TQ5_K) q += ((b[16 + i] >> j) & 1) << 4;
+      v[i] = a * (float)q - o;
+    }
+  } else if constexpr (T == TQ6_K) {
+    const int j = c & 7, half = j >> 2, part = j & 3;
+    const uint8_t* b = row + (size_t)(c >> 3) * 210;
+    const uint8_t* ql = b + half * 64 + (part & 1) * 32;
+    const uint8_t* qh = b + 128 + half * 32;
+    const int8_t* scl = (const int8_t*)(b + 192);
+    const float d = h2f(b + 208);
+    const int lsh = (part >> 1) * 4, hsh = part * 2;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int q = (((ql[i] >> lsh) & 0x0F) | (((qh[i] >> hsh) & 3) << 4)) - 32;
+      v[i] = d * (float)scl[half * 8 + part * 2 + (i >> 4)] * (float)q;
+    }
+  } else if constexpr (T == TQ3_K) {
+    const int j = c & 7, half = j >> 2, sh = j & 3;
+    const uint8_t* b = row + (size_t)(c >> 3) * 110;
+    const uint8_t* hm = b;
+    const uint8_t* qs = b + 32 + half * 32;
+    const uint8_t* s = b + 96;
+    const float d = h2f(b + 108);
+    float scl[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {  // sixteen 6-bit scales: low nibbles in bytes 0-7, high pairs in 8-11
+      const int si = half * 8 + sh * 2 + u;
+      const int lo = si < 8 ? (s[si] & 0x0F) : (s[si - 8] >> 4);
+      const int hi = (s[8 + (si & 3)] >> (2 * (si >> 2))) & 3;
+      scl[u] = (float)((lo | (hi << 4)) - 32);
+    }
+    const int m = 1 << (half * 4 + sh);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int q = ((qs[i] >> (2 * sh)) & 3) - ((hm[i] & m) ? 0 : 4);
+      v[i] = d * scl[i >> 4] * (float)q;
+    }
+  } else if constexpr (T == TIQ4_XS) {
+    const int j = c & 7;
+    const uint8_t* b = row + (size_t)(c >> 3) * 136;
+    const float d = h2f(b);
+    const int sh = b[2] | (b[3] << 8);
+    const int ls = ((b[4 + j / 2] >> (4 * (j & 1))) & 0x0F) | (((sh >> (2 * j)) & 3) << 4);
+    const float dl = d * (float)(ls - 32);
+    const uint8_t* qs = b + 8 + j * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = dl * c_iq4[qs[i] & 0x0F];
+      v[i + 16] = dl * c_iq4[qs[i] >> 4];
+    }
+  }
+}
+
+// Row-major dequantisation: thread per 32-value chunk (rows are whole blocks,
+// so chunk c of the flat tensor is chunk c of the flat block stream).
+template <int T>
+__global__ void k_dequant_flat(const uint8_t* w, float* out, size_t chunks) {
+  size_t c = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (c >= chunks) return;
+  float v[32];
+  if constexpr (T == TQ4_K || T == TQ5_K || T == TQ6_K || T == TQ3_K || T == TIQ4_XS) {
+    chunk32<T>(w, (int)c, v);  // super-block c / 8, sub-block c % 8
+  } else {
+    const int nb = T == TQ8_0 ? 34 : T == TQ5_0 ? 22 : 18;  // one 32-value block per chunk
+    chunk32<T>(w + c * nb, 0, v);
+  }
+  float4* o = (float4*)(out + c * 32);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+// y[r] = sum_k x[k] * W[r, k] (* silu gate variant): one warp per output row,
+// lane l takes 32-value chunks l, l+32, ...
+template <int T>
+__global__ void k_matvec(const float* x, const uint8_t* w, float* y, int rows, int chunks, size_t row_bytes,
+                         const uint8_t* w2) {
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int l = threadIdx.x & 31;
+  if (r >= rows) return;
+  const uint8_t* wr = w + (size_t)r * row_bytes;
+  const uint8_t* wr2 = w2 ? w2 + (size_t)r * row_bytes : nullptr;
+  float acc = 0.f, acc2 = 0.f;
+  float v[32];
+  for (int c = l; c < chunks; c += 32) {
+    const float4* xv = (const float4*)(x + (size_t)c * 32);
+    float xs[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 t = __ldg(xv + i);
+      xs[4 * i] = t.x;
+      xs[4 * i + 1] = t.y;
+      xs[4 * i + 2] = t.z;
+      xs[4 * i + 3] = t.w;
+    }
+    chunk32<T>(wr, c, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc += xs[i] * v[i];
+    if (wr2) {
+      chunk32<T>(wr2, c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc2 += xs[i] * v[i];
+    }
+  }
+  acc = warp_sum(acc);
+  if (wr2) acc2 = warp_sum(acc2);
+  if (l == 0) y[r] = wr2 ? acc / (1.f + expf(-acc)) * acc2 : acc;  // silu(gate) * up
+}
+
+// ---------------------------------------------------------------------------------------------- GEMM
+// Row-major C[M,N] = alpha op(A) op(B) + beta C through cuBLAS's column-major
+// view (C^T = op(B)^T op(A)^T, the row-major buffers read as their transposes).
+int gemm_rm(bool ta, bool tb, int M, int N, int K, float alpha, const float* A, int lda, const float* B, int ldb,
+            float beta, float* C, int ldc, int batch = 1, long long sA = 0, long long sB = 0, long long sC = 0) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  const cublasOperation_t oa = ta ? CUBLAS_OP_T : CUBLAS_OP_N, ob = tb ? CUBLAS_OP_T : CUBLAS_OP_N;
+  cublasStatus_t st;
+  if (batch == 1)
+    st = cublasSgemm(c->blas, ob, oa, N, M, K, &alpha, B, ldb, A, lda, &beta, C, ldc);
+  else
+    st = cublasSgemmStridedBatched(c->blas, ob, oa, N, M, K, &alpha, B, ldb, sB, A, lda, sA, &beta, C, ldc, sC, batch);
+  if (st != CUBLAS_STATUS_SUCCESS) {
+    snprintf(g_err, sizeof(g_err), "cublas status %d", (int)st);
+    return -2;
+  }
+  return 0;
+}
+
+template <int T>
+int matvec_launch(const float* x, const uint8_t* w, float* y, int rows, int chunks, size_t row_bytes,
+                  const uint8_t* w2 = nullptr) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  k_matvec<T><<<blocks(rows, 8), 256, 0, c->s>>>(x, w, y, rows, chunks, row_bytes, w2);
+  return launched("matvec");
+}
+
+int matvec_typed(int t, const float* x, const uint8_t* w, float* y, int rows, int chunks, size_t row_bytes,
+                 const uint8_t* w2 = nullptr) {
+  switch (t) {
+    case TF32: return matvec_launch<TF32>(x, w, y, rows, chunks, row_bytes, w2);
+    case TF16: return matvec_launch<TF16>(x, w, y, rows, chunks, row_bytes, w2);
+    case TQ4_0: return matvec_launch<TQ4_0>(x, w, y, rows, chunks, row_bytes, w2);
+    case TQ5_0: return matvec_launch<TQ5_0>(x, w, y, rows, chunks, row_bytes, w2);
+    case TQ8_0: return matvec_launch<TQ8_0>(x, w, y, rows, chunks, row_bytes, w2);
+    case TIQ4_NL: return matvec_launch<TIQ4_NL>(x, w, y, rows, chunks, row_bytes, w2);
+    case TQ3_K: return matvec_launch<TQ3_K>(x, w, y, rows, chunks, row_bytes, w2);
+    case TQ4_K: return matvec_launch<TQ4_K>(x, w, y, rows, chunks, row_bytes, w2);
+    case TQ5_K: return matvec_launch<TQ5_K>(x, w, y, rows, chunks, row_bytes, w2);
+    case TQ6_K: return matvec_launch<TQ6_K>(x, w, y, rows, chunks, row_bytes, w2);
+    case TIQ4_XS: return matvec_launch<TIQ4_XS>(x, w, y, rows, chunks, row_bytes, w2);
+    default: return -2;
+  }
+}
+
+// Quantised mat-vec by handle: `rows` output rows of `nblk` blocks each, the
+// weight starting `expert` whole matrices into the buffer.
+int qmatvec(int t, int64_t xh, int64_t wh, int64_t yh, int rows, int nblk, int expert = 0, int64_t w2h = 0) {
+  int ne, nb;
+  if (!block_of(t, &ne, &nb) || rows <= 0 || nblk <= 0 || expert < 0) return -1;
+  const size_t k = (size_t)nblk * ne;
+  if (k % 32) return -1;
+  const size_t row_bytes = (size_t)nblk * nb, mat = row_bytes * rows;
+  const float* x = F(xh, k);
+  const uint8_t* w = U(wh, mat * (expert + 1));
+  float* y = F(yh, rows);
+  const uint8_t* w2 = w2h ? U(w2h, mat) : nullptr;
+  if (!x || !w || !y || (w2h && !w2)) return -1;
+  return matvec_typed(t, x, w + mat * expert, y, rows, (int)(k / 32), row_bytes, w2);
+}
+
+template <int T>
+int dequant_launch(const uint8_t* w, float* out, size_t chunks) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  k_dequant_flat<T><<<blocks(chunks), 256, 0, c->s>>>(w, out, chunks);
+  return launched("dequant");
+}
+
+int dequant_typed(int t, const uint8_t* w, float* out, size_t chunks) {
+  switch (t) {
+    case TQ4_K: return dequant_launch<TQ4_K>(w, out, chunks);
+    case TQ6_K: return dequant_launch<TQ6_K>(w, out, chunks);
+    case TQ8_0: return dequant_launch<TQ8_0>(w, out, chunks);
+    case TQ4_0: return dequant_launch<TQ4_0>(w, out, chunks);
+    case TQ5_0: return dequant_launch<TQ5_0>(w, out, chunks);
+    case TQ5_K: return dequant_launch<TQ5_K>(w, out, chunks);
+    case TQ3_K: return dequant_launch<TQ3_K>(w, out, chunks);
+    case TIQ4_NL: return dequant_launch<TIQ4_NL>(w, out, chunks);
+    case TIQ4_XS: return dequant_launch<TIQ4_XS>(w, out, chunks);
+    default: return -2;
+  }
+}
+
+int dequant_handle(int t, int64_t wh, int64_t oh, int nblk) {
+  int ne, nb;
+  if (!block_of(t, &ne, &nb) || nblk <= 0 || ne < 32) return -1;
+  const uint8_t* w = U(wh, (size_t)nblk * nb);
+  float* o = F(oh, (size_t)nblk * ne);
+  if (!w || !o) return -1;
+  return dequant_typed(t, w, o, (size_t)nblk * ne / 32);
+}
+
+}  // namespace
+
+// ================================================================================================ registry
+AE_API int aether_dev_init() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return -1;
+  return ctx() ? 0 : -1;
+}
+
+// Select the device later calls (allocations, ops, graphs) run on.
+AE_API int aether_dev_set_device(int d) {
+  if (cudaSetDevice(d) != cudaSuccess) return -1;
+  return ctx() ? 0 : -1;
+}
+
+AE_API int aether_dev_count() {
+  int n = 0;
+  return cudaGetDeviceCount(&n) == cudaSuccess ? n : 0;
+}
+
+AE_API const char* aether_dev_last_error() { return g_err; }
+
+AE_API int64_t aether_dev_mem_free_bytes() {
+  size_t f = 0, t = 0;
+  if (!ctx() || cudaMemGetInfo(&f, &t) != cudaSuccess) return -1;
+  return (int64_t)f;
+}
+
+AE_API int64_t aether_dev_alloc_f32(int n) { return n > 0 ? alloc((size_t)n, 4, KF32) : 0; }
+AE_API int64_t aether_dev_alloc_i32(int n) { return n > 0 ? alloc((size_t)n, 4, KI32) : 0; }
+AE_API int64_t aether_dev_alloc_u8(int n) { return n > 0 ? alloc((size_t)n, 1, KU8) : 0; }
+AE_API int aether_dev_free_f32(int64_t h) { return release(h, KF32); }
+AE_API int aether_dev_free_i32(int64_t h) { return release(h, KI32); }
+AE_API int aether_dev_free_u8(int64_t h) { return release(h, KU8); }
+
+AE_API int aether_dev_h2d_f32(int64_t host, int64_t dev, int n) {
+  float* d = n > 0 ? F(dev, n) : nullptr;
+  return (!d || !host) ? -1 : copy(d, (const void*)host, (size_t)n * 4, cudaMemcpyHostToDevice);
+}
+AE_API int aether_dev_d2h_f32(int64_t dev, int64_t host, int n) {
+  float* d = n > 0 ? F(dev, n) : nullptr;
+  return (!d || !host) ? -1 : copy((void*)host, d, (size_t)n * 4, cudaMemcpyDeviceToHost);
+}
+AE_API int aether_dev_h2d_i32(int64_t host, int64_t dev, int n) {
+  int* d = n > 0 ? I(dev, n) : nullptr;
+  return (!d || !host) ? -1 : copy(d, (const void*)host, (size_t)n * 4, cudaMemcpyHostToDevice);
+}
+AE_API int aether_dev_d2h_i32(int64_t dev, int64_t host, int n) {
+  int* d = n > 0 ? I(dev, n) : nullptr;
+  return (!d || !host) ? -1 : copy((void*)host, d, (size_t)n * 4, cudaMemcpyDeviceToHost);
+}
+AE_API int aether_dev_h2d_u8(int64_t host, int64_t dev, int n) {
+  uint8_t* d = n > 0 ? U(dev, n) : nullptr;
+  return (!d || !host) ? -1 : copy(d, (const void*)host, (size_t)n, cudaMemcpyHostToDevice);
+}
+AE_API int aether_dev_d2h_u8(int64_t dev, int64_t host, int n) {
+  uint8_t* d = n > 0 ? U(dev, n) : nullptr;
+  return (!d || !host) ? -1 : copy((void*)host, d, (size_t)n, cudaMemcpyDeviceToHost);
+}
+// The first n elements of a possibly larger buffer (the plain forms already allow that here).
+AE_API int aether_dev_h2d_f32_n(int64_t host, int64_t dev, int n) { return aether_dev_h2d_f32(host, dev, n); }
+AE_API int aether_dev_d2h_f32_n(int64_t dev, int64_t host, int n) { return aether_dev_d2h_f32(dev, host, n); }
+AE_API int aether_dev_h2d_i32_n(int64_t host, int64_t dev, int n) { return aether_dev_h2d_i32(host, dev, n); }
+
+AE_API int aether_dev_d2d_f32_offset(int64_t src, int src_off, int64_t dst, int dst_off, int n) {
+  if (n <= 0 || src_off < 0 || dst_off < 0) return -1;
+  float* s = F(src, (size_t)src_off + n);
+  float* d = F(dst, (size_t)dst_off + n);
+  Ctx* c = ctx();
+  if (!s || !d || !c) return -1;
+  cudaError_t e = cudaMemcpyAsync(d + dst_off, s + src_off, (size_t)n * 4, cudaMemcpyDeviceToDevice, c->s);
+  if (e != cudaSuccess) {
+    set_err("d2d", e);
+    return -2;
+  }
+  return 0;
+}
+
+AE_API int64_t aether_wall_us() {
+  using namespace std::chrono;
+  return duration_cast<microseconds>(steady_clock::now().time_since_epoch()).count();
+}
+
+AE_API int aether_dev_sync() {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  cudaError_t e = cudaStreamSynchronize(c->s);
+  if (e != cudaSuccess) {
+    set_err("sync", e);
+    return -2;
+  }
+  return 0;
+}
+
+// ================================================================================================ graphs
+// One captured graph per device: begin/end capture the device stream (thread-
+// local mode), launch replays it, destroy frees it.
+AE_API int aether_dev_graph_begin() {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  return cudaStreamBeginCapture(c->s, cudaStreamCaptureModeThreadLocal) == cudaSuccess ? 0 : -2;
+}
+
+AE_API int aether_dev_graph_end() {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  cudaGraph_t g = nullptr;
+  if (cudaStreamEndCapture(c->s, &g) != cudaSuccess || !g) return -2;
+  if (c->exec) cudaGraphExecDestroy(c->exec);
+  if (c->graph) cudaGraphDestroy(c->graph);
+  c->graph = g;
+  c->exec = nullptr;
+  return cudaGraphInstantiate(&c->exec, g, 0) == cudaSuccess ? 0 : -2;
+}
+
+AE_API int aether_dev_graph_launch() {
+  Ctx* c = ctx();
+  if (!c || !c->exec) return -1;
+  return cudaGraphLaunch(c->exec, c->s) == cudaSuccess ? 0 : -2;
+}
+
+AE_API int aether_dev_graph_destroy() {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  if (c->exec) cudaGraphExecDestroy(c->exec);
+  if (c->graph) cudaGraphDestroy(c->graph);
+  c->exec = nullptr;
+  c->graph = nullptr;
+  return 0;
+}
+
+// ================================================================================================ GEMMs
+#define NEED3(pa, na, pb, nb, pc, nc)                     \
+  const float* pa##_ = F(pa, (size_t)(na));               \
+  const float* pb##_ = F(pb, (size_t)(nb));               \
+  float* pc##_ = F(pc, (size_t)(nc));                     \
+  if (!pa##_ || !pb##_ || !pc##_ || m <= 0 || k <= 0 || n <= 0) return -1;
+
+// out[m,n] = a[m,k] b[k,n]
+AE_API int aether_op_matmul_f32_cuda(int64_t a, int64_t b, int64_t out, int m, int k, int n) {
+  NEED3(a, (size_t)m * k, b, (size_t)k * n, out, (size_t)m * n);
+  return gemm_rm(false, false, m, n, k, 1.f, a_, k, b_, n, 0.f, out_, n);
+}
+// out[m,n] = a[k,m]^T b[k,n]
+AE_API int aether_op_matmul_tn_f32_cuda(int64_t a, int64_t b, int64_t out, int m, int k, int n) {
+  NEED3(a, (size_t)k * m, b, (size_t)k * n, out, (size_t)m * n);
+  return gemm_rm(true, false, m, n, k, 1.f, a_, m, b_, n, 0.f, out_, n);
+}
+// out[m,n] = a[m,k] b[n,k]^T
+AE_API int aether_op_matmul_nt_f32_cuda(int64_t a, int64_t b, int64_t out, int m, int k, int n) {
+  NEED3(a, (size_t)m * k, b, (size_t)n * k, out, (size_t)m * n);
+  return gemm_rm(false, true, m, n, k, 1.f, a_, k, b_, k, 0.f, out_, n);
+}
+// out = gelu(a b), the GELU launched right behind the GEMM on the same stream
+AE_API int aether_op_matmul_gelu_f32_cuda(int64_t a, int64_t b, int64_t out, int m, int k, int n) {
+  int r = aether_op_matmul_f32_cuda(a, b, out, m, k, n);
+  if (r) return r;
+  float* o = F(out, (size_t)m * n);
+  size_t cnt = (size_t)m * n;
+  k_gelu<<<blocks(cnt), 256, 0, ctx()->s>>>(o, o, cnt);
+  return launched("gelu");
+}
+// matmul timed with events on the device stream; prints the time and rate to stderr
+AE_API int aether_op_matmul_f32_cuda_profile(int64_t a, int64_t b, int64_t out, int m, int k, int n) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, c->s);
+  int r = aether_op_matmul_f32_cuda(a, b, out, m, k, n);
+  cudaEventRecord(e1, c->s);
+  cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (!r)
+    fprintf(stderr, "[aether_dev] matmul %dx%dx%d: %.3f ms, %.2f TFLOP/s\n", m, k, n, ms,
+            2.0 * m * k * n / (ms * 1e-3) / 1e12);
+  return r;
+}
+// db[k,n] = a[m,k]^T dy[m,n]
+AE_API int aether_op_matmul_backward_rhs_f32_cuda(int64_t a, int64_t dy, int64_t db, int m, int k, int n) {
+  NEED3(a, (size_t)m * k, dy, (size_t)m * n, db, (size_t)k * n);
+  return gemm_rm(true, false, k, n, m, 1.f, a_, k, dy_, n, 0.f, db_, n);
+}
+// da[m,k] = dy[m,n] b[k,n]^T
+AE_API int aether_op_matmul_backward_lhs_f32_cuda(int64_t dy, int64_t b, int64_t da, int m, int k, int n) {
+  NEED3(dy, (size_t)m * n, b, (size_t)k * n, da, (size_t)m * k);
+  return gemm_rm(false, true, m, k, n, 1.f, dy_, n, b_, n, 0.f, da_, k);
+}
+// Enqueue `iters` matmuls with no sync between them; prints enqueue and drain time.
+AE_API int aether_bench_matmul_batch(int64_t a, int64_t b, int64_t out, int m, int k, int n, int iters) {
+  if (iters <= 0) return -1;
+  const int64_t t0 = aether_wall_us();
+  for (int i = 0; i < iters; ++i) {
+    int r = aether_op_matmul_f32_cuda(a, b, out, m, k, n);
+    if (r) return r;
+  }
+  const int64_t t1 = aether_wall_us();
+  int r = aether_dev_sync();
+  const int64_t t2 = aether_wall_us();
+  fprintf(stderr, "[aether_dev] %d x matmul %dx%dx%d: enqueue %lld us, drain %lld us, %.1f us/call\n", iters, m, k, n,
+          (long long)(t1 - t0), (long long)(t2 - t1), (double)(t2 - t0) / iters);
+  return r;
+}
+// dx[n_in] = W^T dy for a frozen quantised W [n_out, n_in] (Q4_K = 12, Q6_K = 14):
+// W is dequantised into a transient buffer and multiplied.
+AE_API int aether_op_quant_matmul_backward_lhs_f32_cuda(int64_t w, int dt, int64_t dy, int64_t dx, int n_out,
+                                                        int n_in) {
+  if (dt != TQ4_K && dt != TQ6_K) return -2;
+  if (n_out <= 0 || n_in <= 0 || n_in % 256) return -1;
+  int ne, nb;
+  block_of(dt, &ne, &nb);
+  const size_t nblk = (size_t)n_out * (n_in / 256);
+  const uint8_t* wq = U(w, nblk * nb);
+  const float* g = F(dy, n_out);
+  float* o = F(dx, n_in);
+  Ctx* c = ctx();
+  if (!wq || !g || !o || !c) return -1;
+  float* wf = nullptr;
+  if (cudaMallocAsync(&wf, nblk * 256 * 4, c->s) != cudaSuccess) return -2;
+  int r = dequant_typed(dt, wq, wf, nblk * 8);
+  if (!r) r = gemm_rm(false, false, 1, n_in, n_out, 1.f, g, n_out, wf, n_in, 0.f, o, n_in);
+  cudaFreeAsync(wf, c->s);
+  return r;
+}
+
+// ================================================================================================ elementwise ops
+#define EW_LAUNCH(kern, n, ...)                                   \
+  do {                                                            \
+    Ctx* c_ = ctx();                                              \
+    if (!c_) return -1;                                           \
+    kern<<<blocks(n), 256, 0, c_->s>>>(__VA_ARGS__);              \
+    return launched(#kern);                                       \
+  } while (0)
+
+AE_API int aether_op_add_f32_cuda(int64_t a, int64_t b, int64_t out, int n) {
+  const float *pa = F(a, n), *pb = F(b, n);
+  float* po = F(out, n);
+  if (n <= 0 || !pa || !pb || !po) return -1;
+  EW_LAUNCH(k_add, n, pa, pb, po, (size_t)n);
+}
+AE_API int aether_op_add_inplace_f32_cuda(int64_t x, int64_t y, int n) {
+  float* px = F(x, n);
+  const float* py = F(y, n);
+  if (n <= 0 || !px || !py) return -1;
+  EW_LAUNCH(k_add_inplace, n, px, py, (size_t)n);
+}
+AE_API int aether_op_mul_inplace_f32_cuda(int64_t x, int64_t y, int n) {
+  float* px = F(x, n);
+  const float* py = F(y, n);
+  if (n <= 0 || !px || !py) return -1;
+  EW_LAUNCH(k_mul_inplace, n, px, py, (size_t)n);
+}
+AE_API int aether_op_scale_f32_cuda(int64_t x, float s, int n) {
+  float* px = F(x, n);
+  if (n <= 0 || !px) return -1;
+  EW_LAUNCH(k_scale, n, px, s, (size_t)n);
+}
+AE_API int aether_op_gelu_f32_cuda(int64_t x, int64_t y, int n) {
+  const float* px = F(x, n);
+  float* py = F(y, n);
+  if (n <= 0 || !px || !py) return -1;
+  EW_LAUNCH(k_gelu, n, px, py, (size_t)n);
+}
+AE_API int aether_op_gelu_backward_f32_cuda(int64_t x, int64_t dy, int64_t dx, int n) {
+  const float *px = F(x, n), *pg = F(dy, n);
+  float* po = F(dx, n);
+  if (n <= 0 || !px || !pg || !po) return -1;
+  EW_LAUNCH(k_gelu_bwd, n, px, pg, po, (size_t)n);
+}
+AE_API int aether_op_gelu_erf_f32_cuda(int64_t x, int64_t y, int n) {
+  const float* px = F(x, n);
+  float* py = F(y, n);
+  if (n <= 0 || !px || !py) return -1;
+  EW_LAUNCH(k_gelu_erf, n, px, py, (size_t)n);
+}
+AE_API int aether_op_silu_f32_cuda(int64_t x, int n) {
+  float* px = F(x, n);
+  if (n <= 0 || !px) return -1;
+  EW_LAUNCH(k_silu, n, px, (size_t)n);
+}
+AE_API int aether_op_silu_backward_f32_cuda(int64_t x, int64_t dy, int64_t dx, int n) {
+  const float *px = F(x, n), *pg = F(dy, n);
+  float* po = F(dx, n);
+  if (n <= 0 || !px || !pg || !po) return -1;
+  EW_LAUNCH(k_silu_bwd, n, px, pg, po, (size_t)n);
+}
+AE_API int aether_op_bias_add_f32_cuda(int64_t x, int64_t bias, int rows, int cols) {
+  const size_t n = (size_t)rows * cols;
+  float* px = F(x, n);
+  const float* pb = F(bias, cols);
+  if (rows <= 0 || cols <= 0 || !px || !pb) return -1;
+  EW_LAUNCH(k_bias_add, n, px, pb, (size_t)rows, cols);
+}
+AE_API int aether_op_transpose_021_f32_cuda(int64_t in, int64_t out, int d0, int d1, int d2) {
+  const size_t n = (size_t)d0 * d1 * d2;
+  const float* pi = F(in, n);
+  float* po = F(out, n);
+  if (d0 <= 0 || d1 <= 0 || d2 <= 0 || !pi || !po || pi == po) return -1;
+  EW_LAUNCH(k_transpose_021, n, pi, po, d0, d1, d2);
+}
+AE_API int aether_op_embed_lookup_f32_cuda(int64_t table, int64_t ids, int64_t out, int t, int d) {
+  if (t <= 0 || d <= 0) return -1;
+  const int vocab = (int)(capacity(table, 4) / d);
+  const float* pt = F(table, (size_t)vocab * d);
+  const int* pi = I(ids, t);
+  float* po = F(out, (size_t)t * d);
+  if (vocab <= 0 || !pt || !pi || !po) return -1;
+  EW_LAUNCH(k_embed, (size_t)t * d, pt, pi, po, t, d, vocab);
+}
+AE_API int aether_op_embed_scatter_add_f32_cuda(int64_t dout, int64_t ids, int64_t dtable, int t, int d) {
+  if (t <= 0 || d <= 0) return -1;
+  const int vocab = (int)(capacity(dtable, 4) / d);
+  const float* pg = F(dout, (size_t)t * d);
+  const int* pi = I(ids, t);
+  float* pt = F(dtable, (size_t)vocab * d);
+  if (vocab <= 0 || !pg || !pi || !pt) return -1;
+  EW_LAUNCH(k_embed_scatter, (size_t)t * d, pg, pi, pt, t, d, vocab);
+}
+AE_API int aether_op_gqa_repeat_kv_f32_cuda(int64_t kv_in, int64_t kv_out, int seq, int hkv, int hd, int hq) {
+  if (seq <= 0 || hkv <= 0 || hd <= 0 || hq <= 0 || hq % hkv) return -1;
+  const float* pi = F(kv_in, (size_t)seq * hkv * hd);
+  float* po = F(kv_out, (size_t)seq * hq * hd);
+  if (!pi || !po) return -1;
+  EW_LAUNCH(k_gqa_repeat, (size_t)seq * hq * hd, pi, po, seq, hkv, hd, hq);
+}
+AE_API int aether_op_gqa_reduce_kv_grad_f32_cuda(int64_t dkv_out, int64_t dkv_in, int seq, int hkv, int hd, int hq) {
+  if (seq <= 0 || hkv <= 0 || hd <= 0 || hq <= 0 || hq % hkv) return -1;
+  const float* pg = F(dkv_out, (size_t)seq * hq * hd);
+  float* po = F(dkv_in, (size_t)seq * hkv * hd);
+  if (!pg || !po) return -1;
+  EW_LAUNCH(k_gqa_reduce, (size_t)seq * hkv * hd, pg, po, seq, hkv, hd, hq);
+}
+AE_API int aether_op_append_kv_f32_cuda(int64_t kn, int64_t vn, int64_t kc, int64_t vc, int pos, int dkv) {
+  if (pos < 0 || dkv <= 0) return -1;
+  const float *pk = F(kn, dkv), *pv = F(vn, dkv);
+  float *ck = F(kc, (size_t)(pos + 1) * dkv), *cv = F(vc, (size_t)(pos + 1) * dkv);
+  if (!pk || !pv || !ck || !cv) return -1;
+  EW_LAUNCH(k_append_kv, dkv, pk, pv, ck, cv, pos, dkv);
+}
+// AdamW with decoupled weight decay inside the step (p -= lr (m^ / (sqrt(v^) + eps) + wd p)),
+// bias corrections 1 / (1 - beta^step).
+AE_API int aether_op_adamw_step_f32_cuda(int64_t param, int64_t grad, int64_t m, int64_t v, float lr, float b1, float b2,
+                                         float eps, float wd, int64_t step, int n) {
+  float* pp = F(param, n);
+  const float* pg = F(grad, n);
+  float *pm = F(m, n), *pv = F(v, n);
+  if (n <= 0 || step <= 0 || !pp || !pg || !pm || !pv) return -1;
+  const float bc1 = (float)(1.0 / (1.0 - std::pow((double)b1, (double)step)));
+  const float bc2 = (float)(1.0 / (1.0 - std::pow((double)b2, (double)step)));
+  EW_LAUNCH(k_adamw, n, pp, pg, pm, pv, lr, b1, b2, eps, wd, bc1, bc2, (size_t)n);
+}
+AE_API int aether_op_rope_apply_f32_cuda(int64_t x, int seq, int heads, int hd, float base, int pos0) {
+  if (seq <= 0 || heads <= 0 || hd <= 0 || hd % 2) return -1;
+  float* px = F(x, (size_t)seq * heads * hd);
+  if (!px) return -1;
+  EW_LAUNCH(k_rope, (size_t)seq * heads * (hd / 2), px, seq, heads, hd, base, pos0, 1.f);
+}
+AE_API int aether_op_rope_apply_backward_f32_cuda(int64_t g, int seq, int heads, int hd, float base, int pos0) {
+  if (seq <= 0 || heads <= 0 || hd <= 0 || hd % 2) return -1;
+  float* px = F(g, (size_t)seq * heads * hd);
+  if (!px) return -1;
+  EW_LAUNCH(k_rope, (size_t)seq * heads * (hd / 2), px, seq, heads, hd, base, pos0, -1.f);
+}
+
+// ================================================================================================ row ops
+#define ROW_LAUNCH(kern, rows, ...)                                     \
+  do {                                                                  \
+    Ctx* c_ = ctx();                                                    \
+    if (!c_) return -1;                                                 \
+    kern<<<(unsigned)(rows), kRowThreads, 0, c_->s>>>(__VA_ARGS__);     \
+    return launched(#kern);                                             \
+  } while (0)
+
+AE_API int aether_op_softmax_f32_cuda(int64_t x, int64_t y, int b, int d) {
+  const size_t n = (size_t)b * d;
+  const float* px = F(x, n);
+  float* py = F(y, n);
+  if (b <= 0 || d <= 0 || !px || !py) return -1;
+  ROW_LAUNCH(k_softmax, b, px, py, d);
+}
+AE_API int aether_op_softmax_backward_scaled_f32_cuda(int64_t y, int64_t dy, int64_t dx, float s, int b, int d) {
+  const size_t n = (size_t)b * d;
+  const float *py = F(y, n), *pg = F(dy, n);
+  float* po = F(dx, n);
+  if (b <= 0 || d <= 0 || !py || !pg || !po) return -1;
+  ROW_LAUNCH(k_softmax_bwd, b, py, pg, po, d, s);
+}
+AE_API int aether_op_softmax_backward_f32_cuda(int64_t y, int64_t dy, int64_t dx, int b, int d) {
+  return aether_op_softmax_backward_scaled_f32_cuda(y, dy, dx, 1.f, b, d);
+}
+AE_API int aether_op_layer_norm_f32_cuda(int64_t x, int64_t gamma, int64_t beta, int64_t y, int64_t mean, int64_t rstd,
+                                         float eps, int b, int d) {
+  const size_t n = (size_t)b * d;
+  const float *px = F(x, n), *pg = F(gamma, d), *pb = F(beta, d);
+  float *py = F(y, n), *pm = F(mean, b), *pr = F(rstd, b);
+  if (b <= 0 || d <= 0 || !px || !pg || !pb || !py || !pm || !pr) return -1;
+  ROW_LAUNCH(k_layernorm, b, px, nullptr, pg, pb, py, pm, pr, eps, d);
+}
+AE_API int aether_op_add_layer_norm_f32_cuda(int64_t a, int64_t bb, int64_t gamma, int64_t beta, int64_t y, int64_t mean,
+                                             int64_t rstd, float eps, int b, int d) {
+  const size_t n = (size_t)b * d;
+  const float *pa = F(a, n), *p2 = F(bb, n), *pg = F(gamma, d), *pb = F(beta, d);
+  float *py = F(y, n), *pm = F(mean, b), *pr = F(rstd, b);
+  if (b <= 0 || d <= 0 || !pa || !p2 || !pg || !pb || !py || !pm || !pr) return -1;
+  ROW_LAUNCH(k_layernorm, b, pa, p2, pg, pb, py, pm, pr, eps, d);
+}
+AE_API int aether_op_layer_norm_backward_dx_f32_cuda(int64_t x, int64_t gamma, int64_t mean, int64_t rstd, int64_t dy,
+                                                     int64_t dx, int b, int d) {
+  const size_t n = (size_t)b * d;
+  const float *px = F(x, n), *pg = F(gamma, d), *pm = F(mean, b), *pr = F(rstd, b), *pd = F(dy, n);
+  float* po = F(dx, n);
+  if (b <= 0 || d <= 0 || !px || !pg || !pm || !pr || !pd || !po) return -1;
+  ROW_LAUNCH(k_layernorm_bwd_dx, b, px, pg, pm, pr, pd, po, d);
+}
+AE_API int aether_op_layer_norm_backward_params_f32_cuda(int64_t x, int64_t mean, int64_t rstd, int64_t dy,
+                                                         int64_t dgamma, int64_t dbeta, int b, int d) {
+  const size_t n = (size_t)b * d;
+  const float *px = F(x, n), *pm = F(mean, b), *pr = F(rstd, b), *pd = F(dy, n);
+  float *pg = F(dgamma, d), *pb = F(dbeta, d);
+  Ctx* c = ctx();
+  if (b <= 0 || d <= 0 || !px || !pm || !pr || !pd || !pg || !pb || !c) return -1;
+  k_colsum<<<blocks(d, 32), dim3(32, 8), 0, c->s>>>(px, pd, pm, pr, pg, pb, b, d, 0);
+  return launched("layer_norm_backward_params");
+}
+AE_API int aether_op_rms_norm_f32_cuda(int64_t x, int64_t gamma, int64_t out, float eps, int rows, int d) {
+  const size_t n = (size_t)rows * d;
+  float* px = F(x, n);
+  const float* pg = F(gamma, d);
+  float* po = F(out, n);
+  if (rows <= 0 || d <= 0 || !px || !pg || !po) return -1;
+  ROW_LAUNCH(k_rmsnorm, rows, px, nullptr, pg, po, eps, d);
+}
+// x += residual (in place); out = rmsnorm(x) * gamma
+AE_API int aether_op_fused_add_rmsnorm_f32_cuda(int64_t x, int64_t residual, int64_t gamma, int64_t out, float eps,
+                                                int rows, int d) {
+  const size_t n = (size_t)rows * d;
+  float* px = F(x, n);
+  const float *pr = F(residual, n), *pg = F(gamma, d);
+  float* po = F(out, n);
+  if (rows <= 0 || d <= 0 || !px || !pr || !pg || !po) return -1;
+  ROW_LAUNCH(k_rmsnorm, rows, px, pr, pg, po, eps, d);
+}
+AE_API int aether_op_rms_norm_backward_dx_f32_cuda(int64_t x, int64_t gamma, int64_t dy, int64_t dx, int64_t inv_rms,
+                                                   float eps, int rows, int d) {
+  const size_t n = (size_t)rows * d;
+  const float *px = F(x, n), *pg = F(gamma, d), *pd = F(dy, n);
+  float *po = F(dx, n), *pi = F(inv_rms, rows);
+  if (rows <= 0 || d <= 0 || !px || !pg || !pd || !po || !pi) return -1;
+  ROW_LAUNCH(k_rmsnorm_bwd_dx, rows, px, pg, pd, po, pi, eps, d);
+}
+AE_API int aether_op_rms_norm_backward_gamma_f32_cuda(int64_t x, int64_t dy, int64_t inv_rms, int64_t dgamma, int rows,
+                                                      int d) {
+  const size_t n = (size_t)rows * d;
+  const float *px = F(x, n), *pd = F(dy, n), *pi = F(inv_rms, rows);
+  float* pg = F(dgamma, d);
+  Ctx* c = ctx();
+  if (rows <= 0 || d <= 0 || !px || !pd || !pi || !pg || !c) return -1;
+  k_colsum<<<blocks(d, 32), dim3(32, 8), 0, c->s>>>(px, pd, nullptr, pi, pg, nullptr, rows, d, 1);
+  return launched("rms_norm_backward_gamma");
+}
+// Mean cross-entropy over b rows (per-row losses summed on the host in double);
+// probs_out gets the softmax. Returns NaN on a bad handle.
+AE_API float aether_op_cross_entropy_f32_cuda(int64_t logits, int64_t labels, int64_t probs, int b, int v) {
+  const size_t n = (size_t)b * v;
+  const float* pl = F(logits, n);
+  const int* pt = I(labels, b);
+  float* pp = F(probs, n);
+  Ctx* c = ctx();
+  if (b <= 0 || v <= 0 || !pl || !pt || !pp || !c) return NAN;
+  float* loss = nullptr;
+  if (cudaMallocAsync(&loss, (size_t)b * 4, c->s) != cudaSuccess) return NAN;
+  k_ce_fwd<<<(unsigned)b, kRowThreads, 0, c->s>>>(pl, pt, pp, loss, v);
+  std::vector<float> h(b);
+  cudaMemcpyAsync(h.data(), loss, (size_t)b * 4, cudaMemcpyDeviceToHost, c->s);
+  cudaFreeAsync(loss, c->s);
+  if (cudaStreamSynchronize(c->s) != cudaSuccess) return NAN;
+  double s = 0.0;
+  for (float x : h) s += x;
+  return (float)(s / b);
+}
+// dlogits = (probs - onehot(label)) / b
+AE_API int aether_op_cross_entropy_backward_f32_cuda(int64_t probs, int64_t labels, int64_t dlogits, int b, int v) {
+  const size_t n = (size_t)b * v;
+  const float* pp = F(probs, n);
+  const int* pt = I(labels, b);
+  float* pd = F(dlogits, n);
+  if (b <= 0 || v <= 0 || !pp || !pt || !pd) return -1;
+  EW_LAUNCH(k_ce_bwd, n, pp, pt, pd, b, v);
+}
+
+// ================================================================================================ attention
+// Causal SDPA over [bh, s, d] with the [bh, s, s] probabilities kept for the
+// backward: two strided-batched GEMMs around a causal row softmax, scale 1/sqrt(d).
+AE_API int aether_op_sdpa_causal_forward_f32_cuda(int64_t q, int64_t k, int64_t v, int64_t out, int64_t attn, int bh,
+                                                  int s, int d) {
+  if (bh <= 0 || s <= 0 || d <= 0) return -1;
+  const size_t nq = (size_t)bh * s * d, na = (size_t)bh * s * s;
+  const float *pq = F(q, nq), *pk = F(k, nq), *pv = F(v, nq);
+  float *po = F(out, nq), *pa = F(attn, na);
+  Ctx* c = ctx();
+  if (!pq || !pk || !pv || !po || !pa || !c) return -1;
+  const float scale = 1.f / std::sqrt((float)d);
+  const long long sq = (long long)s * d, ss = (long long)s * s;
+  int r = gemm_rm(false, true, s, s, d, scale, pq, d, pk, d, 0.f, pa, s, bh, sq, sq, ss);
+  if (r) return r;
+  k_causal_softmax<<<(unsigned)(bh * s), kRowThreads, 0, c->s>>>(pa, s);
+  if ((r = launched("causal_softmax"))) return r;
+  return gemm_rm(false, false, s, d, s, 1.f, pa, s, pv, d, 0.f, po, d, bh, ss, sq, sq);
+}
+
+AE_API int aether_op_sdpa_causal_backward_f32_cuda(int64_t q, int64_t k, int64_t v, int64_t attn, int64_t dout,
+                                                   int64_t dq, int64_t dk, int64_t dv, int64_t dscores, int bh, int s,
+                                                   int d) {
+  if (bh <= 0 || s <= 0 || d <= 0) return -1;
+  const size_t nq = (size_t)bh * s * d, na = (size_t)bh * s * s;
+  const float *pq = F(q, nq), *pk = F(k, nq), *pv = F(v, nq), *pa = F(attn, na), *pg = F(dout, nq);
+  float *gq = F(dq, nq), *gk = F(dk, nq), *gv = F(dv, nq), *ps = F(dscores, na);
+  Ctx* c = ctx();
+  if (!pq || !pk || !pv || !pa || !pg || !gq || !gk || !gv || !ps || !c) return -1;
+  const float scale = 1.f / std::sqrt((float)d);
+  const long long sq = (long long)s * d, ss = (long long)s * s;
+  int r;
+  // dV = P^T dO ; dP = dO V^T
+  if ((r = gemm_rm(true, false, s, d, s, 1.f, pa, s, pg, d, 0.f, gv, d, bh, ss, sq, sq))) return r;
+  if ((r = gemm_rm(false, true, s, s, d, 1.f, pg, d, pv, d, 0.f, ps, s, bh, sq, sq, ss))) return r;
+  // dS = scale * P * (dP - rowsum(dP * P))  (zero above the diagonal since P is)
+  k_softmax_bwd<<<(unsigned)(bh * s), kRowThreads, 0, c->s>>>(pa, ps, ps, s, scale);
+  if ((r = launched("sdpa_softmax_bwd"))) return r;
+  // dQ = dS K ; dK = dS^T Q
+  if ((r = gemm_rm(false, false, s, d, s, 1.f, ps, s, pk, d, 0.f, gq, d, bh, ss, sq, sq))) return r;
+  return gemm_rm(true, false, s, d, s, 1.f, ps, s, pq, d, 0.f, gk, d, bh, ss, sq, sq);
+}
+
+// One decode token: q [hq * hd] against the first cur_seq rows of the KV cache.
+AE_API int aether_op_attention_seq1_f32_cuda(int64_t q, int64_t kc, int64_t vc, int64_t out, int cur, int hq, int hkv,
+                                             int hd, float scale) {
+  if (cur <= 0 || hq <= 0 || hkv <= 0 || hd <= 0 || hq % hkv) return -1;
+  const size_t smem = (size_t)cur * 4;
+  if (smem > 200 * 1024) return -1;  // scores live in shared memory
+  const float* pq = F(q, (size_t)hq * hd);
+  const float *pk = F(kc, (size_t)cur * hkv * hd), *pv = F(vc, (size_t)cur * hkv * hd);
+  float* po = F(out, (size_t)hq * hd);
+  Ctx* c = ctx();
+  if (!pq || !pk || !pv || !po || !c) return -1;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_seq1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_attn_seq1<<<(unsigned)hq, 256, smem, c->s>>>(pq, pk, pv, po, cur, hq, hkv, hd, scale);
+  return launched("attention_seq1");
+}
+
+// ================================================================================================ quantised weights
+// Dequantise n_blocks GGUF blocks (u8 handle) into f32 (256 values per K-quant super-block).
+AE_API int aether_op_dequant_q4_k_m_f32_cuda(int64_t blk, int64_t out, int n) { return dequant_handle(TQ4_K, blk, out, n); }
+AE_API int aether_op_dequant_q6_k_f32_cuda(int64_t blk, int64_t out, int n) { return dequant_handle(TQ6_K, blk, out, n); }
+// Any supported GGML type number (Q4_0, Q5_0, Q8_0, Q3_K..Q6_K, IQ4_NL, IQ4_XS).
+AE_API int aether_op_dequant_f32_cuda(int dt, int64_t blk, int64_t out, int n) { return dequant_handle(dt, blk, out, n); }
+
+// out[n] = W[n, k] a[k] with W in GGUF blocks (k = n_blocks * block elements)
+AE_API int aether_op_fused_q4k_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q4_0_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_0, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q5_0_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ5_0, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q8_0_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ8_0, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q5_k_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ5_K, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q3_k_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ3_K, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_iq4_nl_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TIQ4_NL, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_iq4_xs_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TIQ4_XS, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q6k_matmul_seq1_v2_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ6_K, a, w, o, n, nb);
+}
+// The reference's successive Q4_K kernel versions share one interface; all run the kernel above.
+AE_API int aether_op_fused_q4k_matmul_seq1_v2_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q4k_matmul_seq1_v3_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q4k_matmul_seq1_v4_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q4k_matmul_seq1_v5_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_q4k_matmul_seq1_v6_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, w, o, n, nb);
+}
+// out[n] = silu(W_gate a) * (W_up a), both Q4_K, in one pass over a
+AE_API int aether_op_fused_q4k_ffn_gate_up_silu_mul_cuda(int64_t a, int64_t wg, int64_t wu, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, wg, o, n, nb, 0, wu);
+}
+AE_API int aether_op_fused_q4k_ffn_gate_up_silu_mul_v2_cuda(int64_t a, int64_t wg, int64_t wu, int64_t o, int n,
+                                                           int nb) {
+  return qmatvec(TQ4_K, a, wg, o, n, nb, 0, wu);
+}
+// y[o] = sum_i x[i] W[o, i] for F16 / F32 weights held in u8 buffers
+AE_API int aether_op_fused_f16_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_in, int n_out) {
+  return qmatvec(TF16, x, w, y, n_out, n_in);
+}
+AE_API int aether_op_fused_f32_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_in, int n_out) {
+  return qmatvec(TF32, x, w, y, n_out, n_in);
+}
+// Expert e of a stacked [E, n_out, k] quantised expert tensor
+AE_API int aether_op_fused_q4k_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TQ4_K, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_fused_q8_0_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TQ8_0, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_fused_q5_0_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TQ5_0, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_fused_q3_k_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TQ3_K, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_fused_q6_k_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TQ6_K, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_fused_q5_k_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TQ5_K, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_fused_iq4_xs_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TIQ4_XS, x, w, y, n_out, bpr, e);
+}
