@@ -168,6 +168,73 @@ SIGNATURES = {
     "aether_prof_reset": (I, []),
     "aether_timer_start": (L, []),
     "aether_timer_elapsed_us": (L, [L]),
+    # scalar helpers, extra losses, witnesses, GGUF reader (float arguments / results)
+    "aether_init_normal_f32": (I, [P, I, Fl, L]),
+    "aether_fill_labels_i32": (I, [P, I, I, L]),
+    "aether_fill_f32": (None, [P, I, Fl]),
+    "aether_init_constant_f32": (None, [P, I, Fl]),
+    "aether_abs_f32": (Fl, [Fl]),
+    "aether_cos_f32": (Fl, [Fl]),
+    "aether_sin_f32": (Fl, [Fl]),
+    "aether_exp_f32": (Fl, [Fl]),
+    "aether_log_f32": (Fl, [Fl]),
+    "aether_sqrt_f32": (Fl, [Fl]),
+    "aether_max_f32": (Fl, [Fl, Fl]),
+    "aether_min_f32": (Fl, [Fl, Fl]),
+    "aether_max_i64": (L, [L, L]),
+    "aether_min_i64": (L, [L, L]),
+    "aether_abs_i64": (L, [L]),
+    "aether_sum_f32": (Fl, [P, I]),
+    "aether_dot_f32_scalar": (Fl, [P, P, L]),
+    "aether_op_bce_f32": (Fl, [P, P, I]),
+    "aether_op_bce_backward_f32": (I, [P, P, P, I]),
+    "aether_op_kl_div_f32": (Fl, [P, P, I]),
+    "aether_op_kl_div_backward_f32": (I, [P, P, P, I]),
+    "aether_op_contrastive_f32": (Fl, [P, P, Fl, I, Fl]),
+    "aether_op_contrastive_backward_f32": (I, [P, P, P, Fl, I, Fl]),
+    "aether_op_smooth_l1_f32": (Fl, [P, P, I, Fl]),
+    "aether_op_smooth_l1_backward_f32": (I, [P, P, P, I, Fl]),
+    "aether_op_triplet_f32": (Fl, [P, P, P, I, Fl]),
+    "aether_op_triplet_backward_f32": (I, [P, P, P, P, I, Fl]),
+    "aether_op_matmul_bf16": (I, [P, P, P, I, I, I]),
+    "aether_print_loss": (I, [I, Fl]),
+    "aether_print_f32_default": (I, [Fl]),
+    "aether_print_kv_f32": (I, [C.c_char_p, Fl]),
+    "aether_print_kv_i64": (I, [C.c_char_p, L]),
+    "aether_f32_close_exit": (I, [Fl, Fl]),
+    "aether_f32_in_band_exit": (I, [Fl, Fl, Fl]),
+    "aether_bpe_tokenizer_new": (L, []),
+    "aether_bpe_tokenizer_free": (I, [L]),
+    "aether_bpe_add_token_with_id": (I, [L, I, P, I]),
+    "aether_bpe_add_merge": (I, [L, I, I, I, P, I]),
+    "aether_bpe_add_merge_by_id": (I, [L, I, I, I, I]),
+    "aether_bpe_encode": (I, [L, P, I, P, I]),
+    "aether_bpe_encode_ids": (I, [L, P, I, P, I]),
+    "aether_bpe_decode": (I, [L, P, I, P, I]),
+    "aether_bpe_lookup_bytes": (I, [L, P, I]),
+    "aether_tokenizer_json_load": (I, [L, P, I]),
+    "aether_safetensors_n_tensors": (I, [P, L]),
+    "aether_safetensors_get_dtype": (I, [P, L, P, L]),
+    "aether_safetensors_get_shape": (I, [P, L, P, L, P, I]),
+    "aether_gguf_open": (L, [P, I]),
+    "aether_gguf_close": (I, [L]),
+    "aether_gguf_version": (I, [L]),
+    "aether_gguf_n_tensors": (I, [L]),
+    "aether_gguf_get_tensor_name": (I, [L, I, P, I]),
+    "aether_gguf_get_tensor_dtype": (I, [L, I]),
+    "aether_gguf_get_tensor_shape": (I, [L, I, P, I]),
+    "aether_gguf_get_tensor_abs_offset": (L, [L, I]),
+    "aether_gguf_get_tensor_data_ptr": (L, [L, I]),
+    "aether_gguf_find_tensor_by_name": (I, [L, P, I]),
+    "aether_gguf_get_tensor_n_elems": (L, [L, I]),
+    "aether_gguf_get_metadata_u32": (L, [L, P, I]),
+    "aether_gguf_get_metadata_bool": (L, [L, P, I]),
+    "aether_gguf_get_metadata_f32": (C.c_double, [L, P, I]),
+    "aether_gguf_get_metadata_string": (I, [L, P, I, P, I]),
+    "aether_gguf_get_metadata_array_string_n": (I, [L, P, I]),
+    "aether_gguf_get_metadata_array_string_get": (I, [L, P, I, I, P, I]),
+    "aether_gguf_get_metadata_array_f32_n": (I, [L, P, I]),
+    "aether_gguf_get_metadata_array_f32": (I, [L, P, I, P, I]),
     # AetherLM-Nano
     "aether_nano_create": (P, [I, I, I, I, I, I, U64]),
     "aether_nano_destroy": (None, [P]),

@@ -90,9 +90,10 @@ void aether_free(int64_t p) {
   std::free(base);
 }
 
-// SplitMix64 + Box-Muller normal fill (same generator as the trainer).
-int aether_init_normal_f32(void* buf, int n, float mean, float std, uint64_t seed) {
-  uint64_t state = seed + 0x9E3779B97F4A7C15ull;
+// SplitMix64 + Box-Muller N(0, scale^2) fill (same generator as the trainer).
+int aether_init_normal_f32(void* buf, int n, float scale, int64_t seed) {
+  const float mean = 0.f, std = scale;
+  uint64_t state = (uint64_t)seed + 0x9E3779B97F4A7C15ull;
   auto next = [&]() {
     state += 0x9E3779B97F4A7C15ull;
     uint64_t z = state;
@@ -113,8 +114,8 @@ int aether_init_normal_f32(void* buf, int n, float mean, float std, uint64_t see
   return 0;
 }
 
-int aether_fill_labels_i32(void* buf, int n, int modulo, uint64_t seed) {
-  uint64_t s = seed;
+int aether_fill_labels_i32(void* buf, int n, int modulo, int64_t seed) {
+  uint64_t s = (uint64_t)seed;
   int32_t* o = static_cast<int32_t*>(buf);
   for (int i = 0; i < n; ++i) {
     s = s * 6364136223846793005ull + 1442695040888963407ull;

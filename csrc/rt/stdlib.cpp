@@ -1,0 +1,995 @@
+// Host pieces of the core C ABI that programs and tools call directly:
+// allocator and scalar helpers, the extra losses (BCE, KL, contrastive,
+// smooth-L1, triplet), the print / exit witnesses, a byte-level BPE tokenizer
+// table with a tokenizer.json loader, safetensors header queries over an
+// in-memory file, and a memory-mapped GGUF reader (metadata by key, tensor
+// table by index or name, raw block pointers for the dequantisers).
+//
+// Names, argument orders and return conventions follow the reference's
+// exports (runtime/src/lib.rs: allocator and scalar helpers 1-700, losses via
+// ops.rs, printing 2840-2960, BPE 3900-4150, safetensors 8500-8640, GGUF
+// 8647-9030); the bodies are this library's own.
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <fcntl.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+extern "C" {
+int64_t aether_alloc_bytes(int64_t n);
+void aether_free(int64_t p);
+}
+
+namespace {
+
+// ------------------------------------------------------------------------------------------ tiny JSON
+// Enough JSON for tokenizer.json and safetensors headers: objects keep their
+// key order, strings are unescaped to UTF-8 (\uXXXX with surrogate pairs).
+struct Json {
+  enum T { Null, Bool, Num, Str, Arr, Obj } t = Null;
+  bool b = false;
+  double num = 0;
+  std::string s;
+  std::vector<Json> a;
+  std::vector<std::pair<std::string, Json>> o;
+  const Json* get(const std::string& k) const {
+    for (auto& kv : o)
+      if (kv.first == k) return &kv.second;
+    return nullptr;
+  }
+};
+
+struct JsonParser {
+  const char* p;
+  const char* e;
+  bool ok = true;
+  void ws() {
+    while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
+  }
+  static void put_utf8(std::string& out, uint32_t cp) {
+    if (cp < 0x80) {
+      out += (char)cp;
+    } else if (cp < 0x800) {
+      out += (char)(0xC0 | (cp >> 6));
+      out += (char)(0x80 | (cp & 0x3F));
+    } else if (cp < 0x10000) {
+      out += (char)(0xE0 | (cp >> 12));
+      out += (char)(0x80 | ((cp >> 6) & 0x3F));
+      out += (char)(0x80 | (cp & 0x3F));
+    } else {
+      out += (char)(0xF0 | (cp >> 18));
+      out += (char)(0x80 | ((cp >> 12) & 0x3F));
+      out += (char)(0x80 | ((cp >> 6) & 0x3F));
+      out += (char)(0x80 | (cp & 0x3F));
+    }
+  }
+  bool hex4(uint32_t* v) {
+    if (e - p < 4) return false;
+    *v = 0;
+    for (int i = 0; i < 4; ++i) {
+      char c = *p++;
+      *v <<= 4;
+      if (c >= '0' && c <= '9') *v |= c - '0';
+      else if (c >= 'a' && c <= 'f') *v |= c - 'a' + 10;
+      else if (c >= 'A' && c <= 'F') *v |= c - 'A' + 10;
+      else return false;
+    }
+    return true;
+  }
+  bool str(std::string& out) {
+    if (p >= e || *p != '"') return false;
+    ++p;
+    while (p < e && *p != '"') {
+      if (*p != '\\') {
+        out += *p++;
+        continue;
+      }
+      if (++p >= e) return false;
+      char c = *p++;
+      switch (c) {
+        case 'n': out += '\n'; break;
+        case 't': out += '\t'; break;
+        case 'r': out += '\r'; break;
+        case 'b': out += '\b'; break;
+        case 'f': out += '\f'; break;
+        case 'u': {
+          uint32_t cp;
+          if (!hex4(&cp)) return false;
+          if (cp >= 0xD800 && cp < 0xDC00 && e - p >= 6 && p[0] == '\\' && p[1] == 'u') {
+            p += 2;
+            uint32_t lo;
+            if (!hex4(&lo)) return false;
+            cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
+          }
+          put_utf8(out, cp);
+          break;
+        }
+        default: out += c;  // \" \\ \/
+      }
+    }
+    if (p >= e) return false;
+    ++p;
+    return true;
+  }
+  Json value(int depth = 0) {
+    Json j;
+    ws();
+    if (p >= e || depth > 64) {
+      ok = false;
+      return j;
+    }
+    if (*p == '{') {
+      j.t = Json::Obj;
+      ++p;
+      ws();
+      if (p < e && *p == '}') {
+        ++p;
+        return j;
+      }
+      while (ok) {
+        ws();
+        std::string k;
+        if (!str(k)) {
+          ok = false;
+          break;
+        }
+        ws();
+        if (p >= e || *p != ':') {
+          ok = false;
+          break;
+        }
+        ++p;
+        j.o.emplace_back(std::move(k), value(depth + 1));
+        ws();
+        if (p < e && *p == ',') {
+          ++p;
+          continue;
+        }
+        if (p < e && *p == '}') {
+          ++p;
+          break;
+        }
+        ok = false;
+      }
+    } else if (*p == '[') {
+      j.t = Json::Arr;
+      ++p;
+      ws();
+      if (p < e && *p == ']') {
+        ++p;
+        return j;
+      }
+      while (ok) {
+        j.a.push_back(value(depth + 1));
+        ws();
+        if (p < e && *p == ',') {
+          ++p;
+          continue;
+        }
+        if (p < e && *p == ']') {
+          ++p;
+          break;
+        }
+        ok = false;
+      }
+    } else if (*p == '"') {
+      j.t = Json::Str;
+      if (!str(j.s)) ok = false;
+    } else if (e - p >= 4 && !strncmp(p, "true", 4)) {
+      j.t = Json::Bool;
+      j.b = true;
+      p += 4;
+    } else if (e - p >= 5 && !strncmp(p, "false", 5)) {
+      j.t = Json::Bool;
+      p += 5;
+    } else if (e - p >= 4 && !strncmp(p, "null", 4)) {
+      p += 4;
+    } else {
+      char* end = nullptr;
+      std::string tmp(p, std::min<ptrdiff_t>(e - p, 64));
+      j.t = Json::Num;
+      j.num = strtod(tmp.c_str(), &end);
+      if (end == tmp.c_str()) ok = false;
+      p += end - tmp.c_str();
+    }
+    return j;
+  }
+};
+
+bool parse_json(const char* s, size_t n, Json* out) {
+  JsonParser jp{s, s + n};
+  *out = jp.value();
+  jp.ws();
+  return jp.ok;
+}
+
+// ------------------------------------------------------------------------------------------ BPE
+struct Bpe {
+  std::vector<std::string> dec;                                 // id -> bytes
+  std::unordered_map<uint64_t, std::pair<uint32_t, uint32_t>> merges;  // (left, right) -> (merged, rank)
+};
+std::mutex g_bpe_mu;
+std::vector<std::unique_ptr<Bpe>> g_bpe;
+
+Bpe* bpe(int64_t h) {
+  std::lock_guard<std::mutex> l(g_bpe_mu);
+  return (h >= 0 && (size_t)h < g_bpe.size()) ? g_bpe[h].get() : nullptr;
+}
+
+uint64_t pair_key(uint32_t a, uint32_t b) { return ((uint64_t)a << 32) | b; }
+
+// Lowest-rank adjacent pair merged everywhere (left to right, non-overlapping), repeated.
+void bpe_merge(const Bpe& t, std::vector<uint32_t>& tok) {
+  std::vector<uint32_t> nxt;
+  while (tok.size() >= 2) {
+    uint32_t best_rank = UINT32_MAX, bl = 0, br = 0, bm = 0;
+    for (size_t i = 0; i + 1 < tok.size(); ++i) {
+      auto it = t.merges.find(pair_key(tok[i], tok[i + 1]));
+      if (it != t.merges.end() && it->second.second < best_rank) {
+        best_rank = it->second.second;
+        bl = tok[i];
+        br = tok[i + 1];
+        bm = it->second.first;
+      }
+    }
+    if (best_rank == UINT32_MAX) break;
+    nxt.clear();
+    for (size_t i = 0; i < tok.size();) {
+      if (i + 1 < tok.size() && tok[i] == bl && tok[i + 1] == br) {
+        nxt.push_back(bm);
+        i += 2;
+      } else {
+        nxt.push_back(tok[i++]);
+      }
+    }
+    tok.swap(nxt);
+  }
+}
+
+int emit_ids(const std::vector<uint32_t>& tok, void* out, int max_ids) {
+  if ((int)tok.size() > max_ids) return -1;
+  int32_t* o = static_cast<int32_t*>(out);
+  for (size_t i = 0; i < tok.size(); ++i) o[i] = (int32_t)tok[i];
+  return (int)tok.size();
+}
+
+// ------------------------------------------------------------------------------------------ GGUF
+struct GKv {
+  uint32_t type = 0;
+  size_t off = 0;       // value offset (arrays: first element)
+  uint32_t atype = 0;   // array element type
+  uint64_t count = 0;   // array length
+};
+struct GTensor {
+  std::string name;
+  std::vector<int64_t> dims;
+  uint32_t type = 0;
+  uint64_t off = 0;  // relative to the data section
+};
+struct Gguf {
+  uint8_t* base = nullptr;
+  size_t size = 0;
+  uint32_t version = 0;
+  size_t data = 0;
+  std::map<std::string, GKv> kv;
+  std::vector<GTensor> tensors;
+  ~Gguf() {
+    if (base) munmap(base, size);
+  }
+};
+std::mutex g_gguf_mu;
+std::vector<std::unique_ptr<Gguf>> g_gguf;
+
+Gguf* gguf(int64_t h) {
+  std::lock_guard<std::mutex> l(g_gguf_mu);
+  return (h >= 0 && (size_t)h < g_gguf.size()) ? g_gguf[h].get() : nullptr;
+}
+
+size_t scalar_size(uint32_t t) {
+  switch (t) {
+    case 0: case 1: case 7: return 1;
+    case 2: case 3: return 2;
+    case 4: case 5: case 6: return 4;
+    case 10: case 11: case 12: return 8;
+    default: return 0;
+  }
+}
+
+struct Cursor {
+  const uint8_t* b;
+  size_t n, i = 0;
+  bool ok = true;
+  template <class T>
+  T rd() {
+    T v{};
+    if (i + sizeof(T) > n) {
+      ok = false;
+      return v;
+    }
+    memcpy(&v, b + i, sizeof(T));
+    i += sizeof(T);
+    return v;
+  }
+  std::string str() {
+    uint64_t len = rd<uint64_t>();
+    if (!ok || len > n - i) {
+      ok = false;
+      return {};
+    }
+    std::string s((const char*)b + i, len);
+    i += len;
+    return s;
+  }
+  bool skip_value(uint32_t t) {
+    if (t == 8) {
+      str();
+      return ok;
+    }
+    if (t == 9) {
+      uint32_t at = rd<uint32_t>();
+      uint64_t cnt = rd<uint64_t>();
+      if (!ok) return false;
+      if (at == 8) {
+        for (uint64_t k = 0; k < cnt && ok; ++k) str();
+        return ok;
+      }
+      const size_t es = scalar_size(at);
+      if (!es || cnt > (n - i) / es) return ok = false;
+      i += cnt * es;
+      return true;
+    }
+    const size_t es = scalar_size(t);
+    if (!es || i + es > n) return ok = false;
+    i += es;
+    return true;
+  }
+};
+
+const GKv* gkv(Gguf* g, int64_t key, int key_len) {
+  if (!g || !key || key_len <= 0) return nullptr;
+  auto it = g->kv.find(std::string((const char*)key, key_len));
+  return it == g->kv.end() ? nullptr : &it->second;
+}
+
+// safetensors: the JSON header of an in-memory file
+bool st_header(int64_t buf, int64_t len, Json* j) {
+  if (!buf || len < 8) return false;
+  uint64_t hl;
+  memcpy(&hl, (const void*)buf, 8);
+  if (hl > (uint64_t)len - 8) return false;
+  return parse_json((const char*)buf + 8, hl, j) && j->t == Json::Obj;
+}
+
+void write_out(const std::string& s) { fwrite(s.data(), 1, s.size(), stdout); }
+
+}  // namespace
+
+extern "C" {
+
+// ================================================================================================ memory
+int aether_free_f32(int64_t p, int) {
+  aether_free(p);
+  return 0;
+}
+int aether_free_i32(int64_t p, int) {
+  aether_free(p);
+  return 0;
+}
+void aether_free_bytes(int64_t p, int64_t) { aether_free(p); }
+int64_t aether_realloc_bytes(int64_t p, int64_t old_n, int64_t new_n) {
+  int64_t q = aether_alloc_bytes(new_n);
+  if (q && p && old_n > 0) memcpy((void*)q, (const void*)p, (size_t)std::min(old_n, new_n));
+  if (p) aether_free(p);
+  return q;
+}
+void aether_fill_f32(int64_t p, int n, float v) {
+  if (p && n > 0) std::fill((float*)p, (float*)p + n, v);
+}
+void aether_init_constant_f32(int64_t p, int n, float v) { aether_fill_f32(p, n, v); }
+int64_t aether_load_i64(int64_t p, int64_t i) { return ((const int64_t*)p)[i]; }
+void aether_store_i32(int64_t p, int i, int v) { ((int32_t*)p)[i] = v; }
+void aether_store_i64(int64_t p, int64_t i, int64_t v) { ((int64_t*)p)[i] = v; }
+int64_t aether_byte_at(int64_t p, int64_t i) { return ((const uint8_t*)p)[i]; }
+void aether_byte_set(int64_t p, int64_t i, int64_t v) { ((uint8_t*)p)[i] = (uint8_t)v; }
+int64_t aether_bytes_eq(int64_t a, int64_t b, int64_t n) {
+  if (n <= 0) return 1;
+  if (!a || !b) return 0;
+  return memcmp((const void*)a, (const void*)b, (size_t)n) == 0;
+}
+int aether_copy_cstr(int64_t dst, int64_t cstr, int max_bytes) {
+  if (!dst || !cstr || max_bytes <= 0) return -1;
+  const char* s = (const char*)cstr;
+  int n = 0;
+  while (n < max_bytes && s[n]) {
+    ((char*)dst)[n] = s[n];
+    ++n;
+  }
+  return n;
+}
+int64_t aether_str_len(int64_t p) { return p ? (int64_t)strlen((const char*)p) : 0; }
+
+// ================================================================================================ scalars
+float aether_abs_f32(float x) { return std::fabs(x); }
+int64_t aether_abs_i64(int64_t x) { return x < 0 ? -x : x; }
+float aether_cos_f32(float x) { return std::cos(x); }
+float aether_sin_f32(float x) { return std::sin(x); }
+float aether_exp_f32(float x) { return std::exp(x); }
+float aether_log_f32(float x) { return std::log(x); }
+float aether_sqrt_f32(float x) { return std::sqrt(x); }
+float aether_max_f32(float a, float b) { return a > b ? a : b; }
+float aether_min_f32(float a, float b) { return a < b ? a : b; }
+int64_t aether_max_i64(int64_t a, int64_t b) { return a > b ? a : b; }
+int64_t aether_min_i64(int64_t a, int64_t b) { return a < b ? a : b; }
+float aether_sum_f32(int64_t p, int n) {
+  double s = 0;
+  for (int i = 0; i < n; ++i) s += ((const float*)p)[i];
+  return (float)s;
+}
+float aether_dot_f32_scalar(int64_t a, int64_t b, int64_t n) {
+  if (!a || !b || n <= 0) return 0.f;
+  float acc = 0.f;  // sequential f32, like a scalar loop in the calling program
+  for (int64_t i = 0; i < n; ++i) acc += ((const float*)a)[i] * ((const float*)b)[i];
+  return acc;
+}
+
+// ================================================================================================ losses
+// Mean binary cross-entropy of probabilities (clamped to [1e-7, 1 - 1e-7]).
+float aether_op_bce_f32(const void* pred, const void* target, int n) {
+  if (n <= 0) return 0.f;
+  const float *p = (const float*)pred, *t = (const float*)target;
+  double acc = 0;
+  for (int i = 0; i < n; ++i) {
+    const float q = std::min(std::max(p[i], 1e-7f), 1.f - 1e-7f);
+    acc -= t[i] * std::log(q) + (1.f - t[i]) * std::log(1.f - q);
+  }
+  return (float)(acc / n);
+}
+int aether_op_bce_backward_f32(const void* pred, const void* target, void* dpred, int n) {
+  if (n <= 0) return 0;
+  const float *p = (const float*)pred, *t = (const float*)target;
+  float* g = (float*)dpred;
+  for (int i = 0; i < n; ++i) {
+    const float q = std::min(std::max(p[i], 1e-7f), 1.f - 1e-7f);
+    g[i] = (q - t[i]) / (q * (1.f - q)) / n;
+  }
+  return 0;
+}
+// Mean over elements of t (log t - log p), both floored at 1e-12.
+float aether_op_kl_div_f32(const void* pred, const void* target, int n) {
+  if (n <= 0) return 0.f;
+  const float *p = (const float*)pred, *t = (const float*)target;
+  double acc = 0;
+  for (int i = 0; i < n; ++i) acc += t[i] * (std::log(std::max(t[i], 1e-12f)) - std::log(std::max(p[i], 1e-12f)));
+  return (float)(acc / n);
+}
+int aether_op_kl_div_backward_f32(const void* pred, const void* target, void* dpred, int n) {
+  if (n <= 0) return 0;
+  const float *p = (const float*)pred, *t = (const float*)target;
+  for (int i = 0; i < n; ++i) ((float*)dpred)[i] = -t[i] / std::max(p[i], 1e-12f) / n;
+  return 0;
+}
+// y |x1 - x2|^2 + (1 - y) max(0, margin - |x1 - x2|)^2
+float aether_op_contrastive_f32(const void* x1, const void* x2, float y, int d, float margin) {
+  const float *a = (const float*)x1, *b = (const float*)x2;
+  float d2 = 0.f;
+  for (int i = 0; i < d; ++i) d2 += (a[i] - b[i]) * (a[i] - b[i]);
+  const float neg = std::max(margin - std::sqrt(d2), 0.f);
+  return y * d2 + (1.f - y) * neg * neg;
+}
+int aether_op_contrastive_backward_f32(const void* x1, const void* x2, void* dx1, float y, int d, float margin) {
+  const float *a = (const float*)x1, *b = (const float*)x2;
+  float d2 = 0.f;
+  for (int i = 0; i < d; ++i) d2 += (a[i] - b[i]) * (a[i] - b[i]);
+  const float dist = std::max(std::sqrt(d2), 1e-12f);
+  const bool neg = margin - dist > 0.f;
+  for (int i = 0; i < d; ++i) {
+    const float u = a[i] - b[i];
+    ((float*)dx1)[i] = 2.f * y * u + (neg ? -2.f * (margin - dist) * u / dist * (1.f - y) : 0.f);
+  }
+  return 0;
+}
+// Mean smooth-L1: 0.5 d^2 / beta below beta, |d| - beta / 2 above.
+float aether_op_smooth_l1_f32(const void* pred, const void* target, int n, float beta) {
+  if (n <= 0) return 0.f;
+  const float *p = (const float*)pred, *t = (const float*)target;
+  double acc = 0;
+  for (int i = 0; i < n; ++i) {
+    const float dd = p[i] - t[i], ad = std::fabs(dd);
+    acc += ad < beta ? 0.5f * dd * dd / beta : ad - 0.5f * beta;
+  }
+  return (float)(acc / n);
+}
+int aether_op_smooth_l1_backward_f32(const void* pred, const void* target, void* dpred, int n, float beta) {
+  if (n <= 0) return 0;
+  const float *p = (const float*)pred, *t = (const float*)target;
+  for (int i = 0; i < n; ++i) {
+    const float dd = p[i] - t[i];
+    ((float*)dpred)[i] = (std::fabs(dd) < beta ? dd / beta : (dd > 0.f ? 1.f : -1.f)) / n;
+  }
+  return 0;
+}
+// max(0, |a - p|^2 - |a - n|^2 + margin) and its anchor gradient
+float aether_op_triplet_f32(const void* anchor, const void* positive, const void* negative, int d, float margin) {
+  const float *a = (const float*)anchor, *p = (const float*)positive, *q = (const float*)negative;
+  float dap = 0.f, dan = 0.f;
+  for (int i = 0; i < d; ++i) {
+    dap += (a[i] - p[i]) * (a[i] - p[i]);
+    dan += (a[i] - q[i]) * (a[i] - q[i]);
+  }
+  return std::max(dap - dan + margin, 0.f);
+}
+int aether_op_triplet_backward_f32(const void* anchor, const void* positive, const void* negative, void* d_anchor,
+                                   int d, float margin) {
+  const float *a = (const float*)anchor, *p = (const float*)positive, *q = (const float*)negative;
+  float dap = 0.f, dan = 0.f;
+  for (int i = 0; i < d; ++i) {
+    dap += (a[i] - p[i]) * (a[i] - p[i]);
+    dan += (a[i] - q[i]) * (a[i] - q[i]);
+  }
+  const bool active = dap - dan + margin > 0.f;
+  for (int i = 0; i < d; ++i) ((float*)d_anchor)[i] = active ? 2.f * (q[i] - p[i]) : 0.f;
+  return 0;
+}
+
+// bf16 [m,k] x [k,n] -> bf16 [m,n] on the host, fp32 accumulation, round to nearest even.
+int aether_op_matmul_bf16(const void* a, const void* b, void* out, int m, int k, int n) {
+  if (!a || !b || !out || m <= 0 || k <= 0 || n <= 0) return -1;
+  auto f = [](uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float x;
+    memcpy(&x, &u, 4);
+    return x;
+  };
+  const uint16_t *A = (const uint16_t*)a, *B = (const uint16_t*)b;
+  std::vector<float> bf((size_t)k * n), row(n);
+  for (size_t i = 0; i < bf.size(); ++i) bf[i] = f(B[i]);
+  for (int i = 0; i < m; ++i) {
+    std::fill(row.begin(), row.end(), 0.f);
+    for (int p = 0; p < k; ++p) {
+      const float av = f(A[(size_t)i * k + p]);
+      const float* br = &bf[(size_t)p * n];
+      for (int j = 0; j < n; ++j) row[j] += av * br[j];
+    }
+    for (int j = 0; j < n; ++j) {
+      uint32_t u;
+      memcpy(&u, &row[j], 4);
+      if ((u & 0x7F800000u) != 0x7F800000u) u += 0x7FFFu + ((u >> 16) & 1u);  // NaN / inf pass through
+      ((uint16_t*)out)[(size_t)i * n + j] = (uint16_t)(u >> 16);
+    }
+  }
+  return 0;
+}
+// Which host matmul body a shape takes: 1 = cache-blocked (every shape here), -1 = invalid.
+int aether_op_matmul_f32_auto_kernel(int m, int k, int n) { return (m > 0 && k > 0 && n > 0) ? 1 : -1; }
+
+// ================================================================================================ printing
+int aether_print_loss(int step, float loss) {
+  printf("step=%d loss=%.6f\n", step, loss);
+  fflush(stdout);
+  return 0;
+}
+int aether_print_f32_default(float v) {
+  char buf[64];
+  snprintf(buf, sizeof(buf), "%.9g", v);
+  write_out(buf);
+  return 0;
+}
+int aether_print_i64(int64_t v) {
+  printf("%lld", (long long)v);
+  return 0;
+}
+int aether_print_kv_f32(const char* label, float v) {
+  if (label) printf("%s: %.9g\n", label, v);
+  else printf("%.9g\n", v);
+  return 0;
+}
+int aether_print_kv_i64(const char* label, int64_t v) {
+  if (label) printf("%s: %lld\n", label, (long long)v);
+  else printf("%lld\n", (long long)v);
+  return 0;
+}
+int aether_print_newline() {
+  putchar('\n');
+  fflush(stdout);
+  return 0;
+}
+int aether_print_str_n(const char* p, int64_t n) {
+  if (p && n > 0) fwrite(p, 1, (size_t)n, stdout);
+  return 0;
+}
+void aether_print_bytes(int64_t p, int64_t n) {
+  if (p && n > 0) fwrite((const void*)p, 1, (size_t)n, stdout);
+}
+// Witness exits: 42 when the check holds, 1 otherwise.
+int aether_f32_close_exit(float a, float b) {
+  const float mag = std::max(std::max(std::fabs(a), std::fabs(b)), 1.f);
+  return std::fabs(a - b) / mag < 1e-3f ? 42 : 1;
+}
+int aether_f32_in_band_exit(float v, float lo, float hi) {
+  if (!std::isfinite(v)) return 1;
+  const float a = std::fabs(v);
+  return (a > lo && a < hi) ? 42 : 1;
+}
+
+// ================================================================================================ BPE
+// A table starts with the 256 single-byte tokens; merges add (or name) ids.
+int64_t aether_bpe_tokenizer_new() {
+  auto t = std::make_unique<Bpe>();
+  t->dec.reserve(256);
+  for (int b = 0; b < 256; ++b) t->dec.emplace_back(1, (char)b);
+  std::lock_guard<std::mutex> l(g_bpe_mu);
+  for (size_t i = 0; i < g_bpe.size(); ++i)
+    if (!g_bpe[i]) {
+      g_bpe[i] = std::move(t);
+      return (int64_t)i;
+    }
+  g_bpe.push_back(std::move(t));
+  return (int64_t)g_bpe.size() - 1;
+}
+int aether_bpe_tokenizer_free(int64_t h) {
+  std::lock_guard<std::mutex> l(g_bpe_mu);
+  if (h < 0 || (size_t)h >= g_bpe.size()) return -1;
+  g_bpe[h].reset();
+  return 0;
+}
+int aether_bpe_add_token_with_id(int64_t h, int id, const void* bytes, int n) {
+  Bpe* t = bpe(h);
+  if (!t || !bytes || n <= 0 || id < 0) return -1;
+  if ((size_t)id >= t->dec.size()) t->dec.resize(id + 1);
+  t->dec[id].assign((const char*)bytes, n);
+  return 0;
+}
+int aether_bpe_add_merge(int64_t h, int left, int right, int rank, const void* bytes, int n) {
+  Bpe* t = bpe(h);
+  if (!t || left < 0 || right < 0 || rank < 0 || !bytes || n <= 0) return -1;
+  if ((size_t)left >= t->dec.size() || (size_t)right >= t->dec.size()) return -1;
+  if (t->merges.count(pair_key(left, right))) return -1;
+  const uint32_t id = (uint32_t)t->dec.size();
+  t->dec.emplace_back((const char*)bytes, n);
+  t->merges[pair_key(left, right)] = {id, (uint32_t)rank};
+  return (int)id;
+}
+int aether_bpe_add_merge_by_id(int64_t h, int left, int right, int rank, int merged) {
+  Bpe* t = bpe(h);
+  if (!t || left < 0 || right < 0 || rank < 0 || merged < 0) return -1;
+  if (t->merges.count(pair_key(left, right))) return -1;
+  t->merges[pair_key(left, right)] = {(uint32_t)merged, (uint32_t)rank};
+  return 0;
+}
+int aether_bpe_encode(int64_t h, const void* text, int n_text, void* out, int max_ids) {
+  Bpe* t = bpe(h);
+  if (!t || !text || !out || n_text < 0 || max_ids <= 0) return -1;
+  std::vector<uint32_t> tok((const uint8_t*)text, (const uint8_t*)text + n_text);
+  bpe_merge(*t, tok);
+  return emit_ids(tok, out, max_ids);
+}
+int aether_bpe_encode_ids(int64_t h, const void* ids, int n, void* out, int max_ids) {
+  Bpe* t = bpe(h);
+  if (!t || !ids || !out || n < 0 || max_ids <= 0) return -1;
+  std::vector<uint32_t> tok(n);
+  for (int i = 0; i < n; ++i) {
+    const int32_t v = ((const int32_t*)ids)[i];
+    if (v < 0 || (size_t)v >= t->dec.size()) return -1;
+    tok[i] = (uint32_t)v;
+  }
+  bpe_merge(*t, tok);
+  return emit_ids(tok, out, max_ids);
+}
+int aether_bpe_decode(int64_t h, const void* ids, int n, void* out, int max_bytes) {
+  Bpe* t = bpe(h);
+  if (!t || !ids || !out || n < 0) return -1;
+  int w = 0;
+  for (int i = 0; i < n; ++i) {
+    const int32_t v = ((const int32_t*)ids)[i];
+    if (v < 0 || (size_t)v >= t->dec.size()) return -1;
+    const std::string& s = t->dec[v];
+    if (w + (int)s.size() > max_bytes) return -1;
+    memcpy((char*)out + w, s.data(), s.size());
+    w += (int)s.size();
+  }
+  return w;
+}
+int aether_bpe_lookup_bytes(int64_t h, const void* bytes, int n) {
+  Bpe* t = bpe(h);
+  if (!t || !bytes || n <= 0) return -1;
+  const std::string needle((const char*)bytes, n);
+  for (size_t i = 0; i < t->dec.size(); ++i)
+    if (t->dec[i] == needle) return (int)i;
+  return -1;
+}
+// A Hugging Face tokenizer.json: model.vocab (surface string -> id), added
+// tokens, and model.merges ("a b" or ["a", "b"], rank = position). Returns the
+// number of merges, -1 on a JSON error, -2 when a merge names an unknown token.
+int aether_tokenizer_json_load(int64_t h, const void* json, int n) {
+  Bpe* t = bpe(h);
+  if (!t || !json || n <= 0) return -1;
+  Json j;
+  if (!parse_json((const char*)json, n, &j) || j.t != Json::Obj) return -1;
+  const Json* model = j.get("model");
+  const Json* vocab = model ? model->get("vocab") : nullptr;
+  const Json* merges = model ? model->get("merges") : nullptr;
+  if (!vocab || vocab->t != Json::Obj) return -1;
+  std::unordered_map<std::string, int> ids;
+  for (auto& kv : vocab->o) {
+    const int id = (int)kv.second.num;
+    if (kv.second.t != Json::Num || id < 0 || kv.first.empty()) continue;
+    ids[kv.first] = id;
+    aether_bpe_add_token_with_id(h, id, kv.first.data(), (int)kv.first.size());
+  }
+  if (const Json* added = j.get("added_tokens"))
+    for (auto& a : added->a) {
+      const Json *c = a.get("content"), *i = a.get("id");
+      if (c && i && !c->s.empty()) {
+        ids[c->s] = (int)i->num;
+        aether_bpe_add_token_with_id(h, (int)i->num, c->s.data(), (int)c->s.size());
+      }
+    }
+  int count = 0;
+  if (merges && merges->t == Json::Arr)
+    for (size_t r = 0; r < merges->a.size(); ++r) {
+      const Json& m = merges->a[r];
+      std::string l, rr;
+      if (m.t == Json::Str) {
+        const size_t sp = m.s.find(' ');
+        if (sp == std::string::npos) return -2;
+        l = m.s.substr(0, sp);
+        rr = m.s.substr(sp + 1);
+      } else if (m.t == Json::Arr && m.a.size() == 2) {
+        l = m.a[0].s;
+        rr = m.a[1].s;
+      } else {
+        return -1;
+      }
+      auto il = ids.find(l), ir = ids.find(rr), im = ids.find(l + rr);
+      if (il == ids.end() || ir == ids.end() || im == ids.end()) return -2;
+      if (aether_bpe_add_merge_by_id(h, il->second, ir->second, (int)r, im->second) == 0) ++count;
+    }
+  return count;
+}
+
+// ================================================================================================ safetensors
+// dtype codes: F32 0, F16 1, BF16 2, I32 3, I16 4, U8 5, I64 6; -1 unknown / missing.
+int aether_safetensors_n_tensors(int64_t buf, int64_t len) {
+  Json j;
+  if (!st_header(buf, len, &j)) return -1;
+  int n = 0;
+  for (auto& kv : j.o) n += kv.first != "__metadata__";
+  return n;
+}
+int aether_safetensors_get_dtype(int64_t buf, int64_t len, int64_t name, int64_t name_len) {
+  Json j;
+  if (!name || name_len <= 0 || !st_header(buf, len, &j)) return -1;
+  const Json* t = j.get(std::string((const char*)name, name_len));
+  const Json* d = t ? t->get("dtype") : nullptr;
+  if (!d) return -1;
+  static const char* names[] = {"F32", "F16", "BF16", "I32", "I16", "U8", "I64"};
+  for (int i = 0; i < 7; ++i)
+    if (d->s == names[i]) return i;
+  return -1;
+}
+int aether_safetensors_get_shape(int64_t buf, int64_t len, int64_t name, int64_t name_len, int64_t out_dims,
+                                 int max_dims) {
+  Json j;
+  if (!name || name_len <= 0 || !out_dims || !st_header(buf, len, &j)) return -1;
+  const Json* t = j.get(std::string((const char*)name, name_len));
+  const Json* s = t ? t->get("shape") : nullptr;
+  if (!s || s->t != Json::Arr || (int)s->a.size() > max_dims) return -1;
+  for (size_t i = 0; i < s->a.size(); ++i) ((int64_t*)out_dims)[i] = (int64_t)s->a[i].num;
+  return (int)s->a.size();
+}
+
+// ================================================================================================ GGUF
+// Handle >= 0; -1 file error, -2 bad magic, -3 bad metadata, -4 bad tensor table.
+int64_t aether_gguf_open(int64_t path, int n_path) {
+  if (!path || n_path <= 0) return -1;
+  const std::string p((const char*)path, n_path);
+  const int fd = open(p.c_str(), O_RDONLY);
+  if (fd < 0) return -1;
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size < 24) {
+    close(fd);
+    return -1;
+  }
+  void* m = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (m == MAP_FAILED) return -1;
+  auto g = std::make_unique<Gguf>();
+  g->base = (uint8_t*)m;
+  g->size = (size_t)st.st_size;
+  Cursor c{g->base, g->size};
+  if (memcmp(g->base, "GGUF", 4) != 0) return -2;
+  c.i = 4;
+  g->version = c.rd<uint32_t>();
+  if (g->version < 2) return -3;
+  const uint64_t nt = c.rd<uint64_t>(), nkv = c.rd<uint64_t>();
+  if (!c.ok || nt > g->size || nkv > g->size) return -3;
+  uint64_t align = 32;
+  for (uint64_t k = 0; k < nkv; ++k) {
+    std::string key = c.str();
+    GKv v;
+    v.type = c.rd<uint32_t>();
+    if (!c.ok) return -3;
+    if (v.type == 9) {
+      v.atype = c.rd<uint32_t>();
+      v.count = c.rd<uint64_t>();
+      v.off = c.i;
+      c.i -= 12;  // re-read the array header in skip_value
+    } else {
+      v.off = c.i;
+    }
+    if (!c.skip_value(v.type)) return -3;
+    if (key == "general.alignment" && (v.type == 4 || v.type == 5)) align = *(const uint32_t*)(g->base + v.off);
+    g->kv[key] = v;
+  }
+  for (uint64_t k = 0; k < nt; ++k) {
+    GTensor t;
+    t.name = c.str();
+    const uint32_t nd = c.rd<uint32_t>();
+    if (!c.ok || nd > 8) return -4;
+    for (uint32_t d = 0; d < nd; ++d) t.dims.push_back((int64_t)c.rd<uint64_t>());
+    t.type = c.rd<uint32_t>();
+    t.off = c.rd<uint64_t>();
+    if (!c.ok) return -4;
+    g->tensors.push_back(std::move(t));
+  }
+  if (!align) align = 32;
+  g->data = (c.i + align - 1) / align * align;
+  std::lock_guard<std::mutex> l(g_gguf_mu);
+  g_gguf.push_back(std::move(g));
+  return (int64_t)g_gguf.size() - 1;
+}
+int aether_gguf_close(int64_t h) {
+  std::lock_guard<std::mutex> l(g_gguf_mu);
+  if (h < 0 || (size_t)h >= g_gguf.size() || !g_gguf[h]) return -1;
+  g_gguf[h].reset();
+  return 0;
+}
+int aether_gguf_version(int64_t h) {
+  Gguf* g = gguf(h);
+  return g ? (int)g->version : -1;
+}
+int aether_gguf_n_tensors(int64_t h) {
+  Gguf* g = gguf(h);
+  return g ? (int)g->tensors.size() : -1;
+}
+int aether_gguf_get_tensor_name(int64_t h, int i, int64_t out, int max_out) {
+  Gguf* g = gguf(h);
+  if (!g || i < 0 || (size_t)i >= g->tensors.size() || !out) return -1;
+  const std::string& s = g->tensors[i].name;
+  if ((int)s.size() > max_out) return -1;
+  memcpy((void*)out, s.data(), s.size());
+  return (int)s.size();
+}
+int aether_gguf_get_tensor_dtype(int64_t h, int i) {
+  Gguf* g = gguf(h);
+  return (g && i >= 0 && (size_t)i < g->tensors.size()) ? (int)g->tensors[i].type : -1;
+}
+int aether_gguf_get_tensor_shape(int64_t h, int i, int64_t out_dims, int max_dims) {
+  Gguf* g = gguf(h);
+  if (!g || i < 0 || (size_t)i >= g->tensors.size() || !out_dims) return -1;
+  const auto& d = g->tensors[i].dims;
+  if ((int)d.size() > max_dims) return -1;
+  for (size_t k = 0; k < d.size(); ++k) ((int64_t*)out_dims)[k] = d[k];
+  return (int)d.size();
+}
+int64_t aether_gguf_get_tensor_abs_offset(int64_t h, int i) {
+  Gguf* g = gguf(h);
+  return (g && i >= 0 && (size_t)i < g->tensors.size()) ? (int64_t)(g->data + g->tensors[i].off) : -1;
+}
+int64_t aether_gguf_get_tensor_data_ptr(int64_t h, int i) {
+  Gguf* g = gguf(h);
+  if (!g || i < 0 || (size_t)i >= g->tensors.size()) return 0;
+  const size_t off = g->data + g->tensors[i].off;
+  return off < g->size ? (int64_t)(g->base + off) : 0;
+}
+int aether_gguf_find_tensor_by_name(int64_t h, int64_t name, int name_len) {
+  Gguf* g = gguf(h);
+  if (!g || !name || name_len <= 0) return -1;
+  const std::string n((const char*)name, name_len);
+  for (size_t i = 0; i < g->tensors.size(); ++i)
+    if (g->tensors[i].name == n) return (int)i;
+  return -1;
+}
+int64_t aether_gguf_get_tensor_n_elems(int64_t h, int i) {
+  Gguf* g = gguf(h);
+  if (!g || i < 0 || (size_t)i >= g->tensors.size()) return -1;
+  int64_t n = 1;
+  for (int64_t d : g->tensors[i].dims) n *= d;
+  return n;
+}
+// Integer metadata (any GGUF integer type) as i64; -1 missing / not an integer.
+int64_t aether_gguf_get_metadata_u32(int64_t h, int64_t key, int key_len) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  if (!v) return -1;
+  const uint8_t* p = g->base + v->off;
+  switch (v->type) {
+    case 0: return *p;
+    case 1: return (int8_t)*p;
+    case 2: { uint16_t x; memcpy(&x, p, 2); return x; }
+    case 3: { int16_t x; memcpy(&x, p, 2); return x; }
+    case 4: { uint32_t x; memcpy(&x, p, 4); return x; }
+    case 5: { int32_t x; memcpy(&x, p, 4); return x; }
+    case 10: case 11: { int64_t x; memcpy(&x, p, 8); return x; }
+    default: return -1;
+  }
+}
+int64_t aether_gguf_get_metadata_bool(int64_t h, int64_t key, int key_len) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  return (v && v->type == 7) ? (g->base[v->off] != 0) : -1;
+}
+double aether_gguf_get_metadata_f32(int64_t h, int64_t key, int key_len) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  if (!v) return NAN;
+  if (v->type == 6) {
+    float x;
+    memcpy(&x, g->base + v->off, 4);
+    return x;
+  }
+  if (v->type == 12) {
+    double x;
+    memcpy(&x, g->base + v->off, 8);
+    return x;
+  }
+  return NAN;
+}
+int aether_gguf_get_metadata_string(int64_t h, int64_t key, int key_len, int64_t out, int max) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  if (!v || v->type != 8 || !out) return -1;
+  uint64_t n;
+  memcpy(&n, g->base + v->off, 8);
+  if ((int64_t)n > max) return -2;
+  memcpy((void*)out, g->base + v->off + 8, n);
+  return (int)n;
+}
+int aether_gguf_get_metadata_array_string_n(int64_t h, int64_t key, int key_len) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  return (v && v->type == 9 && v->atype == 8) ? (int)v->count : -1;
+}
+int aether_gguf_get_metadata_array_string_get(int64_t h, int64_t key, int key_len, int idx, int64_t out, int max) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  if (!v || v->type != 9 || v->atype != 8 || idx < 0 || (uint64_t)idx >= v->count || !out) return -1;
+  size_t o = v->off;
+  for (int k = 0;; ++k) {  // strings are length-prefixed: walk to element idx
+    uint64_t n;
+    memcpy(&n, g->base + o, 8);
+    if (k == idx) {
+      if ((int64_t)n > max) return -2;
+      memcpy((void*)out, g->base + o + 8, n);
+      return (int)n;
+    }
+    o += 8 + n;
+  }
+}
+int aether_gguf_get_metadata_array_f32_n(int64_t h, int64_t key, int key_len) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  return (v && v->type == 9 && v->atype == 6) ? (int)v->count : -1;
+}
+int aether_gguf_get_metadata_array_f32(int64_t h, int64_t key, int key_len, int64_t out, int max) {
+  Gguf* g = gguf(h);
+  const GKv* v = gkv(g, key, key_len);
+  if (!v || v->type != 9 || v->atype != 6 || !out || max < 0) return -1;
+  const int n = (int)std::min<uint64_t>(v->count, (uint64_t)max);
+  memcpy((void*)out, g->base + v->off, (size_t)n * 4);
+  return n;
+}
+
+}  // extern "C"
