@@ -365,3 +365,48 @@ def test_f16_f32_weight_matvec():
     hw32 = d.upload(np.frombuffer(w.tobytes(), np.uint8).copy())
     d.call("aether_op_fused_f32_matmul_seq1_cuda", hx, hw32, hy, n_in, n_out)
     _close(d.download(hy, n_out), w.astype(np.float64) @ x, 1e-4)
+
+
+@pytest.mark.gpu
+def test_cuda_train_tiny_witness_matches_host_ops():
+    """The reference's cuda_train_tiny program (B=8, K=16, N=4 linear
+    classifier, 50 AdamW steps) driven through the device ABI, against the
+    same steps on the host ops of libaether_rt."""
+    from aether_b200 import runtime as rt
+
+    d = _dev()
+    B, K, N = 8, 16, 4
+    x = np.zeros(B * K, np.float32)
+    w0 = np.zeros(K * N, np.float32)
+    lab = np.zeros(B, np.int32)
+    rt.call("aether_init_normal_f32", rt.ptr(x), B * K, C.c_float(1.0), 1)
+    rt.call("aether_init_normal_f32", rt.ptr(w0), K * N, C.c_float(0.1), 7)
+    rt.call("aether_fill_labels_i32", rt.ptr(lab), B, N, 13)
+    hx, hw, hl = d.upload(x), d.upload(w0), d.upload(lab)
+    hy, hp, hdy, hdw, hm, hv = (d.alloc_f32(n) for n in (B * N, B * N, B * N, K * N, K * N, K * N))
+    dev_losses = []
+    for s in range(1, 51):
+        d.call("aether_op_matmul_f32_cuda", hx, hw, hy, B, K, N)
+        dev_losses.append(d.lib.aether_op_cross_entropy_f32_cuda(hy, hl, hp, B, N))
+        d.call("aether_op_cross_entropy_backward_f32_cuda", hp, hl, hdy, B, N)
+        d.call("aether_op_matmul_backward_rhs_f32_cuda", hx, hdy, hdw, B, K, N)
+        d.call("aether_op_adamw_step_f32_cuda", hw, hdw, hm, hv, C.c_float(0.05), C.c_float(0.9), C.c_float(0.999),
+               C.c_float(1e-8), C.c_float(0.0), s, K * N)
+    d.call("aether_dev_sync")
+    assert dev_losses[-1] < dev_losses[0]
+    # host ops, same program
+    w = w0.copy()
+    y, p, dy, dw, m, v = (np.zeros(n, np.float32) for n in (B * N, B * N, B * N, K * N, K * N, K * N))
+    lib = rt.lib()
+    for f in ("aether_op_cross_entropy_f32",):
+        getattr(lib, f).restype = C.c_float
+    lib.aether_op_adamw_step_f32.argtypes = [C.c_void_p] * 4 + [C.c_float] * 5 + [C.c_int64, C.c_int]
+    host_losses = []
+    for s in range(1, 51):
+        lib.aether_op_matmul_f32(rt.ptr(x), rt.ptr(w), rt.ptr(y), B, K, N)
+        host_losses.append(lib.aether_op_cross_entropy_f32(rt.ptr(y), rt.ptr(lab), rt.ptr(p), B, N))
+        lib.aether_op_cross_entropy_backward_f32(rt.ptr(p), rt.ptr(lab), rt.ptr(dy), B, N)
+        lib.aether_op_matmul_backward_rhs_f32(rt.ptr(x), rt.ptr(dy), rt.ptr(dw), B, K, N)
+        lib.aether_op_adamw_step_f32(rt.ptr(w), rt.ptr(dw), rt.ptr(m), rt.ptr(v), 0.05, 0.9, 0.999, 1e-8, 0.0, s, K * N)
+    np.testing.assert_allclose(dev_losses, host_losses, rtol=1e-4)
+    np.testing.assert_allclose(d.download(hw, K * N), w, rtol=1e-3, atol=1e-5)
