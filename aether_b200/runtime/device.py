@@ -108,6 +108,12 @@ SIGNATURES = {
     "aether_op_fused_q4k_ffn_gate_up_silu_mul_v2_cuda": (I, [L, L, L, L, I, I]),
     "aether_op_fused_f16_matmul_seq1_cuda": (I, [L, L, L, I, I]),
     "aether_op_fused_f32_matmul_seq1_cuda": (I, [L, L, L, I, I]),
+    "aether_nccl_real_init_multi_gpu": (I, [I]),
+    "aether_nccl_real_get_handle": (L, [I]),
+    "aether_nccl_real_all_reduce_f32": (I, [L, L, I, I, L]),
+    "aether_nccl_real_comm_world_size": (I, [L]),
+    "aether_nccl_real_comm_rank": (I, [L]),
+    "aether_nccl_real_finalize": (I, []),
 }
 for _n in ("q4k", "q4_0", "q5_0", "q8_0", "q5_k", "q3_k", "iq4_nl", "iq4_xs"):
     SIGNATURES[f"aether_op_fused_{_n}_matmul_seq1_cuda"] = (I, [L, L, L, I, I])

@@ -28,6 +28,7 @@
 #include <cublas_v2.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <chrono>
 #include <cmath>
@@ -1501,4 +1502,103 @@ AE_API int aether_op_fused_q5_k_expert_matmul_seq1_cuda(int64_t x, int64_t w, in
 }
 AE_API int aether_op_fused_iq4_xs_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
   return qmatvec(TIQ4_XS, x, w, y, n_out, bpr, e);
+}
+
+// ================================================================================================ NCCL clique
+// One process driving n local GPUs (ncclCommInitAll): comm handle i + 1 is
+// rank i on device i. A single thread drives every rank, so the per-rank
+// all-reduce calls are queued and issued together in one NCCL group once every
+// rank of the clique has called (in any order); a 1-GPU clique runs at once.
+// Buffers are device handles allocated on the rank's device
+// (aether_dev_set_device(i) first). Op codes: 0 sum, 1 max, 2 min, 3 prod.
+namespace {
+struct NComm {
+  ncclComm_t c;
+  int dev;
+};
+struct NPending {
+  const float* s;
+  float* r;
+  size_t n;
+  ncclRedOp_t op;
+  int rank;
+};
+std::vector<NComm> g_comms;
+std::vector<NPending> g_npend;
+std::mutex g_nmu;
+
+int nccl_flush_locked() {
+  int prev = cur_dev();
+  int rc = 0;
+  if (ncclGroupStart() != ncclSuccess) return -2;
+  for (const NPending& p : g_npend) {
+    Ctx* c = ctx_for(g_comms[p.rank].dev);
+    cudaSetDevice(g_comms[p.rank].dev);
+    if (!c || ncclAllReduce(p.s, p.r, p.n, ncclFloat, p.op, g_comms[p.rank].c, c->s) != ncclSuccess) rc = -2;
+  }
+  if (ncclGroupEnd() != ncclSuccess) rc = -2;
+  g_npend.clear();
+  if (prev >= 0) cudaSetDevice(prev);
+  return rc;
+}
+}  // namespace
+
+AE_API int aether_nccl_real_finalize() {
+  std::lock_guard<std::mutex> l(g_nmu);
+  for (NComm& c : g_comms) ncclCommDestroy(c.c);
+  g_comms.clear();
+  g_npend.clear();
+  return 0;
+}
+
+AE_API int aether_nccl_real_init_multi_gpu(int n) {
+  int have = 0;
+  if (n <= 0 || cudaGetDeviceCount(&have) != cudaSuccess || have < n) return -1;
+  aether_nccl_real_finalize();
+  std::vector<ncclComm_t> cs(n);
+  std::vector<int> devs(n);
+  for (int i = 0; i < n; ++i) {
+    devs[i] = i;
+    if (!ctx_for(i)) return -2;
+  }
+  if (ncclCommInitAll(cs.data(), n, devs.data()) != ncclSuccess) return -3;
+  std::lock_guard<std::mutex> l(g_nmu);
+  for (int i = 0; i < n; ++i) g_comms.push_back({cs[i], i});
+  return n;
+}
+
+AE_API int64_t aether_nccl_real_get_handle(int i) {
+  std::lock_guard<std::mutex> l(g_nmu);
+  return (i >= 0 && (size_t)i < g_comms.size()) ? (int64_t)i + 1 : 0;
+}
+
+AE_API int aether_nccl_real_comm_world_size(int64_t comm) {
+  std::lock_guard<std::mutex> l(g_nmu);
+  return (comm >= 1 && (size_t)comm <= g_comms.size()) ? (int)g_comms.size() : -1;
+}
+
+AE_API int aether_nccl_real_comm_rank(int64_t comm) {
+  std::lock_guard<std::mutex> l(g_nmu);
+  return (comm >= 1 && (size_t)comm <= g_comms.size()) ? (int)comm - 1 : -1;
+}
+
+AE_API int aether_nccl_real_all_reduce_f32(int64_t send, int64_t recv, int n, int op, int64_t comm) {
+  static const ncclRedOp_t ops[4] = {ncclSum, ncclMax, ncclMin, ncclProd};
+  if (n <= 0 || op < 0 || op > 3) return -1;
+  const float* s = F(send, n);
+  float* r = F(recv, n);
+  int sdev, rdev;
+  {
+    std::lock_guard<std::mutex> l(g_mu);
+    sdev = s ? g_bufs[send - 1].dev : -1;
+    rdev = r ? g_bufs[recv - 1].dev : -1;
+  }
+  std::lock_guard<std::mutex> l(g_nmu);
+  if (!s || !r || comm < 1 || (size_t)comm > g_comms.size()) return -1;
+  const int rank = (int)comm - 1;
+  if (sdev != g_comms[rank].dev || rdev != g_comms[rank].dev) return -1;  // buffers live on the rank's GPU
+  for (const NPending& p : g_npend)
+    if (p.rank == rank || p.n != (size_t)n || p.op != ops[op]) return -1;  // one call per rank, same shape
+  g_npend.push_back({s, r, (size_t)n, ops[op], rank});
+  return g_npend.size() == g_comms.size() ? nccl_flush_locked() : 0;
 }

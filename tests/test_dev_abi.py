@@ -24,6 +24,9 @@ def test_exports_bound_and_bad_handles_refused():
     assert lb.aether_dev_h2d_f32(0, bogus, 4) == -1
     assert np.isnan(lb.aether_op_cross_entropy_f32_cuda(bogus, bogus, bogus, 2, 4))
     assert lb.aether_wall_us() > 0
+    assert lb.aether_nccl_real_get_handle(0) == 0  # no clique yet
+    assert lb.aether_nccl_real_all_reduce_f32(bogus, bogus, 4, 0, 1) == -1
+    assert lb.aether_nccl_real_comm_world_size(5) == -1
 
 
 def _dev():
@@ -410,3 +413,29 @@ def test_cuda_train_tiny_witness_matches_host_ops():
         lib.aether_op_adamw_step_f32(rt.ptr(w), rt.ptr(dw), rt.ptr(m), rt.ptr(v), 0.05, 0.9, 0.999, 1e-8, 0.0, s, K * N)
     np.testing.assert_allclose(dev_losses, host_losses, rtol=1e-4)
     np.testing.assert_allclose(d.download(hw, K * N), w, rtol=1e-3, atol=1e-5)
+
+
+@pytest.mark.gpu
+def test_nccl_clique_on_the_visible_gpus():
+    """ncclCommInitAll over every visible GPU; each rank's buffer holds rank + 1
+    and the queued per-rank calls run as one group (a 1-GPU clique at once)."""
+    d = _dev()
+    n = d.lib.aether_dev_count()
+    assert d.lib.aether_nccl_real_init_multi_gpu(n) == n
+    sends, recvs = [], []
+    for r in range(n):
+        d.call("aether_dev_set_device", r)
+        sends.append(d.upload(np.full(1000, r + 1, np.float32)))
+        recvs.append(d.alloc_f32(1000))
+    assert d.lib.aether_nccl_real_all_reduce_f32(sends[0], recvs[0], 1000, 9, 1) == -1  # bad op
+    for r in range(n):
+        h = d.lib.aether_nccl_real_get_handle(r)
+        assert d.lib.aether_nccl_real_comm_rank(h) == r and d.lib.aether_nccl_real_comm_world_size(h) == n
+        d.call("aether_nccl_real_all_reduce_f32", sends[r], recvs[r], 1000, 0, h)
+    want = n * (n + 1) / 2
+    for r in range(n):
+        d.call("aether_dev_set_device", r)
+        d.call("aether_dev_sync")
+        assert (d.download(recvs[r], 1000) == want).all()
+    d.call("aether_nccl_real_finalize")
+    d.call("aether_dev_set_device", 0)
