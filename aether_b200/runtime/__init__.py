@@ -235,6 +235,26 @@ SIGNATURES = {
     "aether_gguf_get_metadata_array_string_get": (I, [L, P, I, I, P, I]),
     "aether_gguf_get_metadata_array_f32_n": (I, [L, P, I]),
     "aether_gguf_get_metadata_array_f32": (I, [L, P, I, P, I]),
+    # crypto and wire codecs
+    "aether_sha256": (I, [P, I, P]),
+    "aether_sha512": (I, [P, I, P]),
+    "aether_hmac_sha256": (I, [P, I, P, I, P]),
+    "aether_hkdf_extract": (I, [P, I, P, I, P]),
+    "aether_hkdf_expand": (I, [P, I, P, I, P, I]),
+    "aether_tls13_hkdf_expand_label": (I, [P, I, P, I, P, I, P, I]),
+    "aether_chacha20_poly1305_encrypt": (I, [P, P, P, I, P, I, P, I]),
+    "aether_chacha20_poly1305_decrypt": (I, [P, P, P, I, P, I, P, I]),
+    "aether_x25519_derive_public": (I, [P, P]),
+    "aether_x25519_shared_secret": (I, [P, P, P]),
+    "aether_ed25519_derive_public": (I, [P, P]),
+    "aether_ed25519_sign": (I, [P, P, P, I, P]),
+    "aether_ed25519_verify": (I, [P, P, I, P]),
+    "aether_random_bytes": (I, [P, I]),
+    "aether_ws_encode_text_frame": (I, [P, I, P, I]),
+    "aether_ws_decode_frame_payload": (I, [P, I, P, I]),
+    "aether_http_parse_request": (I, [P, I, P, I, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "aether_http_write_response_200": (I, [P, I, P, I]),
+    "aether_openai_render_completion": (I, [P, I, P, I, P, I, I, I, P, I]),
     # AetherLM-Nano
     "aether_nano_create": (P, [I, I, I, I, I, I, U64]),
     "aether_nano_destroy": (None, [P]),
