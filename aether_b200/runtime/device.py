@@ -124,6 +124,47 @@ for _n in ("q4k", "q8_0", "q5_0", "q3_k", "q6_k", "q5_k", "iq4_xs"):
     SIGNATURES[f"aether_op_fused_{_n}_expert_matmul_seq1_cuda"] = (I, [L, L, L, I, I, I])
 
 
+SIGNATURES.update({
+    "aether_op_rope_apply_devarg_f32_cuda": (I, [L, I, I, I, Fl, L]),
+    "aether_op_batched_rope_apply_devarg_f32_cuda": (I, [L, I, I, I, Fl, L]),
+    "aether_op_qkv_bias_rope_devarg_f32_cuda": (I, [L, L, L, L, L, L, I, I, I, Fl, L]),
+    "aether_op_append_kv_devarg_f32_cuda": (I, [L, L, L, L, I, L]),
+    "aether_op_attention_seq1_devarg_f32_cuda": (I, [L, L, L, L, I, I, I, Fl, I, L]),
+    "aether_op_paged_append_kv_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, L]),
+    "aether_op_paged_append_kv_mla_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, I, L]),
+    "aether_op_paged_attention_seq1_v4_devarg_f32_cuda": (I, [L, L, L, L, L, L, L, L, I, I, I, I, Fl, I, I, L]),
+    "aether_op_paged_attention_flex_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, I, I, I, Fl, I, L]),
+    "aether_op_paged_attention_mla_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, I, I, Fl, I, L]),
+    "aether_op_batched_paged_append_kv_seqB_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, I, I, L]),
+    "aether_op_batched_paged_append_kv_hetero_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, I, I, L]),
+    "aether_op_batched_paged_attention_seqB_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, I, I, I, I, Fl, I, L]),
+    "aether_op_batched_paged_attention_hetero_devarg_f32_cuda": (I, [L, L, L, L, L, I, I, I, I, I, I, Fl, I, L]),
+    "aether_op_bert_self_attention_fwd_f32_cuda": (I, [L, L, L, L, I, I, I, Fl]),
+    "aether_op_bert_embed_sum_f32_cuda": (I, [L, L, L, L, L, L, I, I]),
+    "aether_op_dinov3_rope2d_f32_cuda": (I, [L, L, L, I, I, I, I, I]),
+    "aether_op_mla_split_kv_a_f32_cuda": (I, [L, L, L, I, I]),
+    "aether_op_mla_assemble_k_f32_cuda": (I, [L, L, L, I, I, I, I]),
+    "aether_op_mla_extract_v_f32_cuda": (I, [L, L, I, I, I]),
+    "aether_op_mla_broadcast_kv_for_mqa_f32_cuda": (I, [L, L, L, L, I, I, I]),
+    "aether_op_mla_rope_q_partial_f32_cuda": (I, [L, I, I, I, Fl, L]),
+    "aether_op_mla_rope_k_shared_f32_cuda": (I, [L, I, Fl, L]),
+    "aether_op_mla_rope_q_partial_yarn_f32_cuda": (I, [L, I, I, I, Fl, Fl, Fl, Fl, Fl, L]),
+    "aether_op_mla_rope_k_shared_yarn_f32_cuda": (I, [L, I, Fl, Fl, Fl, Fl, Fl, L]),
+    "aether_op_quantize_q8_1_llama_cuda": (I, [L, L, L, L, I]),
+    "aether_op_mmvq_q4k_q8_1_single_cuda": (I, [L, L, L, L, I, I]),
+    "aether_op_mmvq_q6k_q8_1_single_cuda": (I, [L, L, L, L, I, I]),
+    "aether_op_mmvq_q4k_q8_1_swiglu_cuda": (I, [L, L, L, L, L, I, I]),
+    "aether_op_fused_q4k_membw_probe_cuda": (I, [L, L, L, I, I]),
+})
+for _v in ("", "_v2", "_v3"):
+    SIGNATURES[f"aether_op_paged_attention_seq1{_v}_devarg_f32_cuda"] = (I, [L, L, L, L, L, I, I, I, I, Fl, I, L])
+for _n in ("q8_0", "q4_k", "q5_k", "q6_k", "iq4_nl", "f16"):
+    SIGNATURES[f"aether_op_mla_absorb_q_{_n}_cuda"] = (I, [L, L, L, I, I, I, I, I])
+    SIGNATURES[f"aether_op_mla_absorb_v_{_n}_cuda"] = (I, [L, L, L, I, I, I, I])
+for _n in ("q4k_matmul_seqB_v3", "q4k_matmul_seqB_fp16", "q6k_matmul_seqB_v3", "q6k_matmul_seqB_fp16"):
+    SIGNATURES[f"aether_op_fused_{_n}_cuda"] = (I, [L, L, L, I, I, I])
+
+
 def lib():
     global _LIB
     if _LIB is None:

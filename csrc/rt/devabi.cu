@@ -731,27 +731,50 @@ __global__ void k_dequant_flat(const uint8_t* w, float* out, size_t chunks) {
 }
 
 // y[r] = sum_k x[k] * W[r, k] (* silu gate variant): one warp per output row,
-// lane l takes 32-value chunks l, l+32, ...
+// lane l takes 32-value chunks l, l+32, ... Rows come in groups of `rpg`
+// (per-head weights): group g reads x + g * xg and writes y[g * yg + r % rpg];
+// grid.y walks a batch of inputs (x + b * xb, y + b * yb).
+struct MV {
+  const float* x;
+  const uint8_t* w;
+  float* y;
+  const uint8_t* w2;
+  int rows, chunks;
+  size_t row_bytes;
+  int rpg;
+  long long xg, yg, xb, yb;
+  const int8_t* xq;  // when set: x is q8_1 (int8 values xq, one scale xd per 32)
+  const float* xd;
+};
+
 template <int T>
-__global__ void k_matvec(const float* x, const uint8_t* w, float* y, int rows, int chunks, size_t row_bytes,
-                         const uint8_t* w2) {
+__global__ void k_matvec(MV p) {
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int l = threadIdx.x & 31;
-  if (r >= rows) return;
-  const uint8_t* wr = w + (size_t)r * row_bytes;
-  const uint8_t* wr2 = w2 ? w2 + (size_t)r * row_bytes : nullptr;
+  if (r >= p.rows) return;
+  const int g = r / p.rpg;
+  const float* x = p.x + blockIdx.y * p.xb + g * p.xg;
+  const uint8_t* wr = p.w + (size_t)r * p.row_bytes;
+  const uint8_t* wr2 = p.w2 ? p.w2 + (size_t)r * p.row_bytes : nullptr;
   float acc = 0.f, acc2 = 0.f;
   float v[32];
-  for (int c = l; c < chunks; c += 32) {
-    const float4* xv = (const float4*)(x + (size_t)c * 32);
+  for (int c = l; c < p.chunks; c += 32) {
     float xs[32];
+    if (p.xq) {
+      const int8_t* q = p.xq + (size_t)c * 32;
+      const float d = p.xd[c];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 t = __ldg(xv + i);
-      xs[4 * i] = t.x;
-      xs[4 * i + 1] = t.y;
-      xs[4 * i + 2] = t.z;
-      xs[4 * i + 3] = t.w;
+      for (int i = 0; i < 32; ++i) xs[i] = d * (float)q[i];
+    } else {
+      const float4* xv = (const float4*)(x + (size_t)c * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 t = __ldg(xv + i);
+        xs[4 * i] = t.x;
+        xs[4 * i + 1] = t.y;
+        xs[4 * i + 2] = t.z;
+        xs[4 * i + 3] = t.w;
+      }
     }
     chunk32<T>(wr, c, v);
 #pragma unroll
@@ -764,7 +787,7 @@ __global__ void k_matvec(const float* x, const uint8_t* w, float* y, int rows, i
   }
   acc = warp_sum(acc);
   if (wr2) acc2 = warp_sum(acc2);
-  if (l == 0) y[r] = wr2 ? acc / (1.f + expf(-acc)) * acc2 : acc;  // silu(gate) * up
+  if (l == 0) p.y[blockIdx.y * p.yb + g * p.yg + r % p.rpg] = wr2 ? acc / (1.f + expf(-acc)) * acc2 : acc;  // silu(gate) * up
 }
 
 // ---------------------------------------------------------------------------------------------- GEMM
@@ -788,46 +811,47 @@ int gemm_rm(bool ta, bool tb, int M, int N, int K, float alpha, const float* A, 
 }
 
 template <int T>
-int matvec_launch(const float* x, const uint8_t* w, float* y, int rows, int chunks, size_t row_bytes,
-                  const uint8_t* w2 = nullptr) {
+int matvec_launch(MV p, int batch) {
   Ctx* c = ctx();
   if (!c) return -1;
-  k_matvec<T><<<blocks(rows, 8), 256, 0, c->s>>>(x, w, y, rows, chunks, row_bytes, w2);
+  k_matvec<T><<<dim3(blocks(p.rows, 8), batch), 256, 0, c->s>>>(p);
   return launched("matvec");
 }
 
-int matvec_typed(int t, const float* x, const uint8_t* w, float* y, int rows, int chunks, size_t row_bytes,
-                 const uint8_t* w2 = nullptr) {
+int matvec_typed(int t, MV p, int batch = 1) {
   switch (t) {
-    case TF32: return matvec_launch<TF32>(x, w, y, rows, chunks, row_bytes, w2);
-    case TF16: return matvec_launch<TF16>(x, w, y, rows, chunks, row_bytes, w2);
-    case TQ4_0: return matvec_launch<TQ4_0>(x, w, y, rows, chunks, row_bytes, w2);
-    case TQ5_0: return matvec_launch<TQ5_0>(x, w, y, rows, chunks, row_bytes, w2);
-    case TQ8_0: return matvec_launch<TQ8_0>(x, w, y, rows, chunks, row_bytes, w2);
-    case TIQ4_NL: return matvec_launch<TIQ4_NL>(x, w, y, rows, chunks, row_bytes, w2);
-    case TQ3_K: return matvec_launch<TQ3_K>(x, w, y, rows, chunks, row_bytes, w2);
-    case TQ4_K: return matvec_launch<TQ4_K>(x, w, y, rows, chunks, row_bytes, w2);
-    case TQ5_K: return matvec_launch<TQ5_K>(x, w, y, rows, chunks, row_bytes, w2);
-    case TQ6_K: return matvec_launch<TQ6_K>(x, w, y, rows, chunks, row_bytes, w2);
-    case TIQ4_XS: return matvec_launch<TIQ4_XS>(x, w, y, rows, chunks, row_bytes, w2);
+    case TF32: return matvec_launch<TF32>(p, batch);
+    case TF16: return matvec_launch<TF16>(p, batch);
+    case TQ4_0: return matvec_launch<TQ4_0>(p, batch);
+    case TQ5_0: return matvec_launch<TQ5_0>(p, batch);
+    case TQ8_0: return matvec_launch<TQ8_0>(p, batch);
+    case TIQ4_NL: return matvec_launch<TIQ4_NL>(p, batch);
+    case TQ3_K: return matvec_launch<TQ3_K>(p, batch);
+    case TQ4_K: return matvec_launch<TQ4_K>(p, batch);
+    case TQ5_K: return matvec_launch<TQ5_K>(p, batch);
+    case TQ6_K: return matvec_launch<TQ6_K>(p, batch);
+    case TIQ4_XS: return matvec_launch<TIQ4_XS>(p, batch);
     default: return -2;
   }
 }
 
 // Quantised mat-vec by handle: `rows` output rows of `nblk` blocks each, the
-// weight starting `expert` whole matrices into the buffer.
-int qmatvec(int t, int64_t xh, int64_t wh, int64_t yh, int rows, int nblk, int expert = 0, int64_t w2h = 0) {
+// weight starting `expert` whole matrices into the buffer; `batch` inputs of
+// k values back to back give `batch` outputs of `rows` values.
+int qmatvec(int t, int64_t xh, int64_t wh, int64_t yh, int rows, int nblk, int expert = 0, int64_t w2h = 0,
+            int batch = 1) {
   int ne, nb;
-  if (!block_of(t, &ne, &nb) || rows <= 0 || nblk <= 0 || expert < 0) return -1;
+  if (!block_of(t, &ne, &nb) || rows <= 0 || nblk <= 0 || expert < 0 || batch <= 0) return -1;
   const size_t k = (size_t)nblk * ne;
   if (k % 32) return -1;
   const size_t row_bytes = (size_t)nblk * nb, mat = row_bytes * rows;
-  const float* x = F(xh, k);
+  const float* x = F(xh, k * batch);
   const uint8_t* w = U(wh, mat * (expert + 1));
-  float* y = F(yh, rows);
+  float* y = F(yh, (size_t)rows * batch);
   const uint8_t* w2 = w2h ? U(w2h, mat) : nullptr;
   if (!x || !w || !y || (w2h && !w2)) return -1;
-  return matvec_typed(t, x, w + mat * expert, y, rows, (int)(k / 32), row_bytes, w2);
+  MV p{x, w + mat * expert, y, w2, rows, (int)(k / 32), row_bytes, rows, 0, 0, (long long)k, rows, nullptr, nullptr};
+  return matvec_typed(t, p, batch);
 }
 
 template <int T>
@@ -1601,4 +1625,711 @@ AE_API int aether_nccl_real_all_reduce_f32(int64_t send, int64_t recv, int n, in
     if (p.rank == rank || p.n != (size_t)n || p.op != ops[op]) return -1;  // one call per rank, same shape
   g_npend.push_back({s, r, (size_t)n, ops[op], rank});
   return g_npend.size() == g_comms.size() ? nccl_flush_locked() : 0;
+}
+
+// ================================================================================================ decode-step ops
+// Variants of the decode ops that read the step's position / length from a
+// device i32 buffer (step_args[0] = position, step_args[1] = current length;
+// batched forms take one value per sequence), so a captured decode graph is
+// replayed with only that buffer rewritten. KV caches are contiguous
+// ([rows, d_row]) or paged pools ([physical blocks * block_size, d_row]) read
+// through a page table (row = table[t / block_size] * block_size + t % block_size).
+// Every device-side index is checked against the table length and the pool's
+// rows: an out-of-range entry is skipped (its key is masked, its write dropped).
+namespace {
+
+struct RopeArgs {
+  float* x;
+  int rows, heads, hs, off, rd;  // rows x heads slices of stride hs; RoPE on dims [off, off + rd)
+  float base;
+  const int* pos;  // per_row ? pos[r] : pos[0] + r
+  int per_row;
+  float ys, yctx, yfast, yslow;  // YaRN (ys > 1)
+};
+
+// YaRN per-pair frequency factor: 1 for fast-rotating pairs, 1 / s for slow
+// ones, linear in between over the pairs whose wavelength lies between
+// beta_fast and beta_slow rotations of the original context.
+__device__ float yarn_factor(int i, int rd, float base, float s, float ctx, float bfast, float bslow) {
+  if (s <= 1.f) return 1.f;
+  const float two_pi = 6.283185307179586f;
+  const float lo = fmaxf(floorf(rd * logf(ctx / (bfast * two_pi)) / (2.f * logf(base))), 0.f);
+  float hi = fminf(ceilf(rd * logf(ctx / (bslow * two_pi)) / (2.f * logf(base))), (float)(rd - 1));
+  if (lo == hi) hi += 0.001f;
+  const float ramp = fminf(fmaxf(((float)i - lo) / (hi - lo), 0.f), 1.f);
+  return ramp / s + (1.f - ramp);
+}
+
+__global__ void k_rope_dev(RopeArgs a) {
+  const int half = a.rd / 2;
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)a.rows * a.heads * half) return;
+  const int j = (int)(i % half);
+  const size_t rh = i / half;
+  const int h = (int)(rh % a.heads), r = (int)(rh / a.heads);
+  const int pos = a.per_row ? a.pos[r] : a.pos[0] + r;
+  const float ang = (float)pos * yarn_factor(j, a.rd, a.base, a.ys, a.yctx, a.yfast, a.yslow) *
+                    powf(a.base, -2.f * (float)j / (float)a.rd);
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  float* v = a.x + ((size_t)r * a.heads + h) * a.hs + a.off;
+  const float x0 = v[j], x1 = v[j + half];
+  v[j] = x0 * cs - x1 * sn;
+  v[j + half] = x0 * sn + x1 * cs;
+}
+
+// q, k, v += biases, then RoPE on q and k at step_args[0], in one launch.
+__global__ void k_qkv_bias_rope(float* q, float* k, float* v, const float* bq, const float* bk, const float* bv, int hq,
+                                int hkv, int hd, float base, const int* step) {
+  const int half = hd / 2;
+  const int nq = hq * half, nk = hkv * half, nv = hkv * hd;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq + nk + nv) return;
+  if (i >= nq + nk) {
+    const int e = i - nq - nk;
+    v[e] += bv[e];
+    return;
+  }
+  float* x = i < nq ? q : k;
+  const float* b = i < nq ? bq : bk;
+  const int pi = i < nq ? i : i - nq;
+  const int h = pi / half, j = pi % half;
+  const int o0 = h * hd + j, o1 = o0 + half;
+  const float x0 = x[o0] + b[o0], x1 = x[o1] + b[o1];
+  float sn, cs;
+  sincosf((float)step[0] * powf(base, -2.f * (float)j / (float)hd), &sn, &cs);
+  x[o0] = x0 * cs - x1 * sn;
+  x[o1] = x0 * sn + x1 * cs;
+}
+
+struct AppendArgs {
+  const float* kn;
+  const float* vn;
+  float* kp;
+  float* vp;
+  const int* pt;  // null: contiguous cache
+  int pt_stride, bs, dk, dv;
+  const int* pos;  // per_batch ? pos[b] : pos[0]
+  int per_batch;
+  long long rows_k, rows_v;
+};
+
+__device__ __forceinline__ long long kv_row(const int* pt, int pt_stride, int b, int bs, int t) {
+  if (!pt) return t;
+  const int blk = t / bs;
+  if (blk >= pt_stride) return -1;
+  const int phys = pt[(size_t)b * pt_stride + blk];
+  return phys < 0 ? -1 : (long long)phys * bs + t % bs;
+}
+
+__global__ void k_append_dev(AppendArgs a) {
+  const int b = blockIdx.y;
+  const int pos = a.per_batch ? a.pos[b] : a.pos[0];
+  if (pos < 0) return;
+  const long long row = kv_row(a.pt, a.pt_stride, b, a.bs, pos);
+  if (row < 0) return;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < a.dk && row < a.rows_k) a.kp[row * a.dk + i] = a.kn[(size_t)b * a.dk + i];
+  if (i < a.dv && row < a.rows_v) a.vp[row * a.dv + i] = a.vn[(size_t)b * a.dv + i];
+}
+
+struct AttnArgs {
+  const float* q;
+  const float* kp;
+  const float* vp;
+  const int* pt;
+  int pt_stride;
+  float* out;
+  int hq, hkv, dk, dv, bs;
+  float scale;
+  int window;        // > 0: only the last `window` positions
+  const int* cur;    // null: cur_const; else per_batch ? cur[b] : cur[1]
+  int cur_per_batch, cur_const, max_seq;
+  long long rows_k, rows_v;
+  long long q_bstride, o_bstride;
+  int n_split;       // > 1: partials to sm / sl / sv, merged by k_attn_combine
+  float* sm;
+  float* sl;
+  float* sv;
+};
+
+// One query token per (head, batch row[, split]): scores in shared memory (a
+// warp per key), softmax, then a thread per output dim sums over the keys.
+__global__ void k_attn_dev(AttnArgs a) {
+  extern __shared__ float sc[];
+  const int h = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
+  int cur = a.cur ? (a.cur_per_batch ? a.cur[b] : a.cur[1]) : a.cur_const;
+  cur = min(max(cur, 0), a.max_seq);
+  const int lo = a.window > 0 ? max(0, cur - a.window) : 0;
+  const int per = (cur - lo + a.n_split - 1) / a.n_split;
+  const int t0 = lo + sp * per, t1 = min(cur, t0 + per);
+  const int n = max(t1 - t0, 0);
+  const int kvh = h / (a.hq / a.hkv);
+  const float* q = a.q + b * a.q_bstride + (size_t)h * a.dk;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int t = w; t < n; t += nw) {
+    const long long row = kv_row(a.pt, a.pt_stride, b, a.bs, t0 + t);
+    float acc = 0.f;
+    const bool ok = row >= 0 && row < a.rows_k;
+    if (ok) {
+      const float* kr = a.kp + row * (long long)(a.hkv * a.dk) + (size_t)kvh * a.dk;
+      for (int d = l; d < a.dk; d += 32) acc += q[d] * kr[d];
+      acc = warp_sum(acc);
+    }
+    if (l == 0) sc[t] = ok ? acc * a.scale : -INFINITY;
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) m = fmaxf(m, sc[t]);
+  m = block_max(m);
+  float sum = 0.f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float e = m == -INFINITY ? 0.f : expf(sc[t] - m);
+    sc[t] = e;
+    sum += e;
+  }
+  sum = block_sum(sum);
+  for (int d = threadIdx.x; d < a.dv; d += blockDim.x) {
+    float acc = 0.f;
+    for (int t = 0; t < n; ++t) {
+      const long long row = kv_row(a.pt, a.pt_stride, b, a.bs, t0 + t);
+      if (row >= 0 && row < a.rows_v && sc[t] != 0.f)
+        acc += sc[t] * a.vp[row * (long long)(a.hkv * a.dv) + (size_t)kvh * a.dv + d];
+    }
+    if (a.n_split > 1) {
+      a.sv[((size_t)h * a.n_split + sp) * a.dv + d] = acc;
+    } else {
+      a.out[b * a.o_bstride + (size_t)h * a.dv + d] = sum > 0.f ? acc / sum : 0.f;
+    }
+  }
+  if (a.n_split > 1 && threadIdx.x == 0) {
+    a.sm[(size_t)h * a.n_split + sp] = m;
+    a.sl[(size_t)h * a.n_split + sp] = sum;
+  }
+}
+
+// Merge the splits of each head: out = sum_s v_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+__global__ void k_attn_combine(const float* sm, const float* sl, const float* sv, float* out, int n_split, int dv) {
+  const int h = blockIdx.x;
+  float M = -INFINITY;
+  for (int s = 0; s < n_split; ++s) M = fmaxf(M, sm[(size_t)h * n_split + s]);
+  float L = 0.f;
+  for (int s = 0; s < n_split; ++s) {
+    const float ms = sm[(size_t)h * n_split + s];
+    L += ms == -INFINITY ? 0.f : sl[(size_t)h * n_split + s] * expf(ms - M);
+  }
+  for (int d = threadIdx.x; d < dv; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < n_split; ++s) {
+      const float ms = sm[(size_t)h * n_split + s];
+      if (ms != -INFINITY) acc += sv[((size_t)h * n_split + s) * dv + d] * expf(ms - M);
+    }
+    out[(size_t)h * dv + d] = L > 0.f ? acc / L : 0.f;
+  }
+}
+
+int attn_launch(AttnArgs a, int batch) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  const size_t smem = (size_t)a.max_seq * 4;
+  if (a.max_seq <= 0 || smem > 200 * 1024 || a.hq % a.hkv) return -1;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_dev, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_attn_dev<<<dim3(a.hq, batch, a.n_split), 256, smem, c->s>>>(a);
+  int r = launched("attention_devarg");
+  if (r || a.n_split <= 1) return r;
+  k_attn_combine<<<a.hq, 128, 0, c->s>>>(a.sm, a.sl, a.sv, a.out, a.n_split, a.dv);
+  return launched("attention_combine");
+}
+
+int append_launch(AppendArgs a, int batch) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  k_append_dev<<<dim3(blocks(max(a.dk, a.dv)), batch), 256, 0, c->s>>>(a);
+  return launched("append_kv_devarg");
+}
+
+int rope_launch(RopeArgs a) {
+  Ctx* c = ctx();
+  if (!c) return -1;
+  k_rope_dev<<<blocks((size_t)a.rows * a.heads * (a.rd / 2)), 256, 0, c->s>>>(a);
+  return launched("rope_devarg");
+}
+
+// Paged single-sequence attention behind the reference's several entry points.
+int paged_attn(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out, int hq, int hkv, int dk, int dv, int bs,
+               float scale, int max_seq, int64_t step, int window = 0, int n_split = 1, int64_t hm = 0,
+               int64_t hl = 0, int64_t hv = 0) {
+  if (hq <= 0 || hkv <= 0 || dk <= 0 || dv <= 0 || bs <= 0 || max_seq <= 0 || n_split <= 0) return -1;
+  AttnArgs a{};
+  a.q = F(q, (size_t)hq * dk);
+  a.kp = F(kp, (size_t)hkv * dk);
+  a.vp = F(vp, (size_t)hkv * dv);
+  a.pt = I(pt, 1);
+  a.pt_stride = (int)capacity(pt, 4);
+  a.out = F(out, (size_t)hq * dv);
+  a.hq = hq; a.hkv = hkv; a.dk = dk; a.dv = dv; a.bs = bs; a.scale = scale; a.window = window;
+  a.cur = I(step, 2);
+  a.max_seq = max_seq;
+  a.rows_k = capacity(kp, 4) / ((size_t)hkv * dk);
+  a.rows_v = capacity(vp, 4) / ((size_t)hkv * dv);
+  a.n_split = n_split;
+  if (n_split > 1) {
+    a.sm = F(hm, (size_t)hq * n_split);
+    a.sl = F(hl, (size_t)hq * n_split);
+    a.sv = F(hv, (size_t)hq * n_split * dv);
+    if (!a.sm || !a.sl || !a.sv) return -1;
+  }
+  if (!a.q || !a.kp || !a.vp || !a.pt || !a.out || !a.cur) return -1;
+  return attn_launch(a, 1);
+}
+
+int paged_append(int64_t kn, int64_t vn, int64_t kp, int64_t vp, int64_t pt, int dk, int dv, int bs, int64_t step,
+                 int batch = 1, int pt_stride = 0, int per_batch = 0) {
+  if (dk <= 0 || dv <= 0 || bs <= 0 || batch <= 0) return -1;
+  AppendArgs a{};
+  a.kn = F(kn, (size_t)batch * dk);
+  a.vn = F(vn, (size_t)batch * dv);
+  a.kp = F(kp, dk);
+  a.vp = F(vp, dv);
+  a.pt = pt ? I(pt, 1) : nullptr;
+  a.pt_stride = pt ? (pt_stride ? pt_stride : (int)capacity(pt, 4)) : 0;
+  if (pt && (size_t)a.pt_stride * batch > capacity(pt, 4)) return -1;
+  a.bs = bs; a.dk = dk; a.dv = dv;
+  a.pos = I(step, per_batch ? batch : 1);
+  a.per_batch = per_batch;
+  a.rows_k = capacity(kp, 4) / dk;
+  a.rows_v = capacity(vp, 4) / dv;
+  if (!a.kn || !a.vn || !a.kp || !a.vp || (pt && !a.pt) || !a.pos) return -1;
+  return append_launch(a, batch);
+}
+
+int batched_attn(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out, int batch, int hq, int hkv, int hd, int bs,
+                 int pt_stride, float scale, int max_seq, int64_t cur, int per_batch) {
+  if (batch <= 0 || hq <= 0 || hkv <= 0 || hd <= 0 || bs <= 0 || pt_stride <= 0) return -1;
+  AttnArgs a{};
+  a.q = F(q, (size_t)batch * hq * hd);
+  a.kp = F(kp, (size_t)hkv * hd);
+  a.vp = F(vp, (size_t)hkv * hd);
+  a.pt = I(pt, (size_t)batch * pt_stride);
+  a.pt_stride = pt_stride;
+  a.out = F(out, (size_t)batch * hq * hd);
+  a.hq = hq; a.hkv = hkv; a.dk = hd; a.dv = hd; a.bs = bs; a.scale = scale;
+  a.cur = I(cur, per_batch ? batch : 2);
+  a.cur_per_batch = per_batch;
+  a.max_seq = max_seq;
+  a.rows_k = a.rows_v = capacity(kp, 4) / ((size_t)hkv * hd);
+  a.q_bstride = a.o_bstride = (long long)hq * hd;
+  a.n_split = 1;
+  if (!a.q || !a.kp || !a.vp || !a.pt || !a.out || !a.cur || capacity(vp, 4) < capacity(kp, 4)) return -1;
+  return attn_launch(a, batch);
+}
+
+// Gather / scatter helpers of the MLA step: out[i] = in[map(i)] over n elements.
+__global__ void k_mla_copy(const float* a, const float* b, float* out, int n_heads, int da, int db, int mode,
+                           int extra) {
+  // mode 0: split kv_a [da + db] -> a-part (out) and b-part (via `extra` as offset into out2 -- unused)
+  // mode 1: assemble K: out[h, :da] = a[h, :da] (row stride da + extra), out[h, da:] = b[:db]
+  // mode 2: extract V:  out[h, :db] = a[h, da : da + db] (row stride da + db)
+  // mode 3: broadcast:  out[h, :da] = a[:da], out[h, da:] = b[:db]
+  const int per = (mode == 2) ? db : da + db;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_heads * per) return;
+  const int h = i / per, j = i % per;
+  float v;
+  if (mode == 1) v = j < da ? a[(size_t)h * (da + extra) + j] : b[j - da];
+  else if (mode == 2) v = a[(size_t)h * (da + db) + da + j];
+  else v = j < da ? a[j] : b[j - da];
+  out[i] = v;
+}
+
+__global__ void k_copy_rows(const float* in, float* out, int rows, int n, long long in_stride, long long in_off,
+                            long long out_stride, long long out_off) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * n) return;
+  const int r = i / n, j = i % n;
+  out[r * out_stride + out_off + j] = in[r * in_stride + in_off + j];
+}
+
+// q8_1 activations: per 32 values, d = max|x| / 127, q = round(x / d), s = d * sum(q).
+__global__ void k_quant_q8_1(const float* x, int8_t* q, float* d, float* s, int nblk) {
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int l = threadIdx.x & 31;
+  if (b >= nblk) return;
+  const float v = x[(size_t)b * 32 + l];
+  const float amax = warp_max(fabsf(v));
+  const float dd = amax / 127.f;
+  const int qi = dd > 0.f ? __float2int_rn(v / dd) : 0;
+  q[(size_t)b * 32 + l] = (int8_t)qi;
+  const float sum = warp_sum((float)qi);
+  if (l == 0) {
+    d[b] = dd;
+    s[b] = dd * sum;
+  }
+}
+
+__global__ void k_bert_embed(const int* ids, const int* tt, const float* word, const float* pos, const float* type,
+                             float* out, int seq, int d, int vocab, int n_pos, int n_type) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)seq * d) return;
+  const int t = (int)(i / d), j = (int)(i % d);
+  const int id = ids[t], ty = tt ? tt[t] : 0;
+  float v = (id >= 0 && id < vocab) ? word[(size_t)id * d + j] : 0.f;
+  v += t < n_pos ? pos[(size_t)t * d + j] : 0.f;
+  v += (ty >= 0 && ty < n_type) ? type[(size_t)ty * d + j] : 0.f;
+  out[i] = v;
+}
+
+// Rotate-half 2-D RoPE of the patch tokens (after n_prefix tokens) with
+// per-patch cos / sin tables [n_patches, head_dim].
+__global__ void k_rope2d_tables(float* buf, const float* cs, const float* sn, int n_prefix, int heads, int hd,
+                                int n_patches) {
+  const int half = hd / 2;
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)n_patches * heads * half) return;
+  const int j = (int)(i % half);
+  const size_t ph = i / half;
+  const int h = (int)(ph % heads), p = (int)(ph / heads);
+  float* v = buf + ((size_t)(n_prefix + p) * heads + h) * hd;
+  const float* c = cs + (size_t)p * hd;
+  const float* s = sn + (size_t)p * hd;
+  const float x0 = v[j], x1 = v[j + half];
+  v[j] = x0 * c[j] - x1 * s[j];
+  v[j + half] = x1 * c[j + half] + x0 * s[j + half];
+}
+
+// Per-head absorbed-MLA mat-vecs: `heads` groups of `rows` weight rows of `k`
+// values; group h reads x + h * xg and writes y + h * yg.
+int absorb(int t, int64_t xh, int64_t wh, int64_t yh, int heads, int rows, int k, long long xg, long long yg,
+           size_t x_need, size_t y_need) {
+  int ne, nb;
+  if (!block_of(t, &ne, &nb) || heads <= 0 || rows <= 0 || k <= 0 || k % 32 || k % ne || xg % 4) return -1;
+  const size_t row_bytes = (size_t)(k / ne) * nb;
+  const float* x = F(xh, x_need);
+  const uint8_t* w = U(wh, row_bytes * rows * heads);
+  float* y = F(yh, y_need);
+  if (!x || !w || !y) return -1;
+  MV p{x, w, y, nullptr, heads * rows, k / 32, row_bytes, rows, xg, yg, 0, 0, nullptr, nullptr};
+  return matvec_typed(t, p, 1);
+}
+
+int absorb_q(int t, int64_t q, int64_t w, int64_t out, int heads, int key_mla, int qk_rope, int lora, int k_nope) {
+  const int q_nope = key_mla - qk_rope;
+  if (heads <= 0 || qk_rope < 0 || lora <= 0 || q_nope <= 0 || k_nope != q_nope) return -1;
+  const int per = lora + qk_rope;
+  int r = absorb(t, q, w, out, heads, lora, q_nope, key_mla, per, (size_t)heads * key_mla, (size_t)heads * per);
+  if (r || qk_rope == 0) return r;
+  // q_pe rides along: out[h, lora:] = q[h, q_nope:]
+  Ctx* c = ctx();
+  k_copy_rows<<<blocks((size_t)heads * qk_rope), 256, 0, c->s>>>(F(q, (size_t)heads * key_mla), F(out, (size_t)heads * per),
+                                                                  heads, qk_rope, key_mla, q_nope, per, lora);
+  return launched("mla_absorb_q");
+}
+
+int absorb_v(int t, int64_t av, int64_t w, int64_t out, int heads, int lora, int vdim, int k) {
+  if (heads <= 0 || lora <= 0 || vdim <= 0 || k != lora) return -1;
+  return absorb(t, av, w, out, heads, vdim, lora, lora, vdim, (size_t)heads * lora, (size_t)heads * vdim);
+}
+
+int elements_per_row(int t, int blocks_per_row) {
+  int ne, nb;
+  return block_of(t, &ne, &nb) ? blocks_per_row * ne : -1;
+}
+
+}  // namespace
+
+AE_API int aether_op_rope_apply_devarg_f32_cuda(int64_t x, int seq, int heads, int hd, float base, int64_t step) {
+  if (seq <= 0 || heads <= 0 || hd <= 0 || hd % 2) return -1;
+  RopeArgs a{F(x, (size_t)seq * heads * hd), seq, heads, hd, 0, hd, base, I(step, 1), 0, 1.f, 1.f, 1.f, 1.f};
+  return (!a.x || !a.pos) ? -1 : rope_launch(a);
+}
+// x [batch, heads, hd], row b at pos_batch[b]
+AE_API int aether_op_batched_rope_apply_devarg_f32_cuda(int64_t x, int batch, int heads, int hd, float base,
+                                                        int64_t pos_batch) {
+  if (batch <= 0 || heads <= 0 || hd <= 0 || hd % 2) return -1;
+  RopeArgs a{F(x, (size_t)batch * heads * hd), batch, heads, hd, 0, hd, base, I(pos_batch, batch), 1, 1.f, 1.f, 1.f,
+             1.f};
+  return (!a.x || !a.pos) ? -1 : rope_launch(a);
+}
+AE_API int aether_op_qkv_bias_rope_devarg_f32_cuda(int64_t q, int64_t k, int64_t v, int64_t bq, int64_t bk, int64_t bv,
+                                                   int hq, int hkv, int hd, float base, int64_t step) {
+  if (hq <= 0 || hkv <= 0 || hd <= 0 || hd % 2) return -1;
+  float *pq = F(q, (size_t)hq * hd), *pk = F(k, (size_t)hkv * hd), *pv = F(v, (size_t)hkv * hd);
+  const float *bq_ = F(bq, (size_t)hq * hd), *bk_ = F(bk, (size_t)hkv * hd), *bv_ = F(bv, (size_t)hkv * hd);
+  const int* st = I(step, 1);
+  if (!pq || !pk || !pv || !bq_ || !bk_ || !bv_ || !st) return -1;
+  const int n = hq * (hd / 2) + hkv * (hd / 2) + hkv * hd;
+  EW_LAUNCH(k_qkv_bias_rope, n, pq, pk, pv, bq_, bk_, bv_, hq, hkv, hd, base, st);
+}
+AE_API int aether_op_append_kv_devarg_f32_cuda(int64_t kn, int64_t vn, int64_t kc, int64_t vc, int dkv, int64_t step) {
+  return paged_append(kn, vn, kc, vc, 0, dkv, dkv, 1, step);
+}
+AE_API int aether_op_attention_seq1_devarg_f32_cuda(int64_t q, int64_t kc, int64_t vc, int64_t out, int hq, int hkv,
+                                                    int hd, float scale, int max_seq, int64_t step) {
+  if (hq <= 0 || hkv <= 0 || hd <= 0) return -1;
+  AttnArgs a{};
+  a.q = F(q, (size_t)hq * hd);
+  a.kp = F(kc, (size_t)hkv * hd);
+  a.vp = F(vc, (size_t)hkv * hd);
+  a.out = F(out, (size_t)hq * hd);
+  a.hq = hq; a.hkv = hkv; a.dk = hd; a.dv = hd; a.bs = 1; a.scale = scale;
+  a.cur = I(step, 2);
+  a.max_seq = max_seq;
+  a.rows_k = capacity(kc, 4) / ((size_t)hkv * hd);
+  a.rows_v = capacity(vc, 4) / ((size_t)hkv * hd);
+  a.n_split = 1;
+  if (!a.q || !a.kp || !a.vp || !a.out || !a.cur) return -1;
+  return attn_launch(a, 1);
+}
+AE_API int aether_op_paged_append_kv_devarg_f32_cuda(int64_t kn, int64_t vn, int64_t kp, int64_t vp, int64_t pt, int dkv,
+                                                     int bs, int64_t step) {
+  return pt ? paged_append(kn, vn, kp, vp, pt, dkv, dkv, bs, step) : -1;
+}
+AE_API int aether_op_paged_append_kv_mla_devarg_f32_cuda(int64_t kn, int64_t vn, int64_t kp, int64_t vp, int64_t pt,
+                                                         int dk, int dv, int bs, int64_t step) {
+  return pt ? paged_append(kn, vn, kp, vp, pt, dk, dv, bs, step) : -1;
+}
+AE_API int aether_op_paged_attention_seq1_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out,
+                                                          int hq, int hkv, int hd, int bs, float scale, int max_seq,
+                                                          int64_t step) {
+  return paged_attn(q, kp, vp, pt, out, hq, hkv, hd, hd, bs, scale, max_seq, step);
+}
+// The reference's successive versions of the paged kernel share one interface and one kernel here.
+AE_API int aether_op_paged_attention_seq1_v2_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out,
+                                                             int hq, int hkv, int hd, int bs, float scale, int max_seq,
+                                                             int64_t step) {
+  return paged_attn(q, kp, vp, pt, out, hq, hkv, hd, hd, bs, scale, max_seq, step);
+}
+AE_API int aether_op_paged_attention_seq1_v3_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out,
+                                                             int hq, int hkv, int hd, int bs, float scale, int max_seq,
+                                                             int64_t step) {
+  return paged_attn(q, kp, vp, pt, out, hq, hkv, hd, hd, bs, scale, max_seq, step);
+}
+// Split-K over the keys: partials (m, l, v) in caller scratch of hq * n_split * (2 + hd) floats.
+AE_API int aether_op_paged_attention_seq1_v4_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out,
+                                                             int64_t sm, int64_t sl, int64_t sv, int hq, int hkv, int hd,
+                                                             int bs, float scale, int max_seq, int n_split,
+                                                             int64_t step) {
+  if (n_split <= 0 || n_split > 256) return -1;
+  return paged_attn(q, kp, vp, pt, out, hq, hkv, hd, hd, bs, scale, max_seq, step, 0, n_split, sm, sl, sv);
+}
+// Any head_dim; sliding_window > 0 keeps only the last sliding_window positions.
+AE_API int aether_op_paged_attention_flex_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out,
+                                                          int hq, int hkv, int hd, int bs, int window, float scale,
+                                                          int max_seq, int64_t step) {
+  return paged_attn(q, kp, vp, pt, out, hq, hkv, hd, hd, bs, scale, max_seq, step, window);
+}
+// Per-head K of qk_head_dim and V of v_head_dim (non-absorbed MLA).
+AE_API int aether_op_paged_attention_mla_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt, int64_t out,
+                                                         int heads, int qk_hd, int v_hd, int bs, float scale,
+                                                         int max_seq, int64_t step) {
+  return paged_attn(q, kp, vp, pt, out, heads, heads, qk_hd, v_hd, bs, scale, max_seq, step);
+}
+// B sequences at one shared position step_args[0] (seqB) or their own pos_batch[b] (hetero).
+AE_API int aether_op_batched_paged_append_kv_seqB_devarg_f32_cuda(int64_t kn, int64_t vn, int64_t kp, int64_t vp,
+                                                                  int64_t pt, int batch, int dkv, int bs, int pt_stride,
+                                                                  int64_t step) {
+  return (pt && pt_stride > 0) ? paged_append(kn, vn, kp, vp, pt, dkv, dkv, bs, step, batch, pt_stride, 0) : -1;
+}
+AE_API int aether_op_batched_paged_append_kv_hetero_devarg_f32_cuda(int64_t kn, int64_t vn, int64_t kp, int64_t vp,
+                                                                    int64_t pt, int batch, int dkv, int bs,
+                                                                    int pt_stride, int64_t pos_batch) {
+  return (pt && pt_stride > 0) ? paged_append(kn, vn, kp, vp, pt, dkv, dkv, bs, pos_batch, batch, pt_stride, 1) : -1;
+}
+AE_API int aether_op_batched_paged_attention_seqB_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt,
+                                                                  int64_t out, int batch, int hq, int hkv, int hd, int bs,
+                                                                  int pt_stride, float scale, int max_seq,
+                                                                  int64_t step) {
+  return batched_attn(q, kp, vp, pt, out, batch, hq, hkv, hd, bs, pt_stride, scale, max_seq, step, 0);
+}
+AE_API int aether_op_batched_paged_attention_hetero_devarg_f32_cuda(int64_t q, int64_t kp, int64_t vp, int64_t pt,
+                                                                    int64_t out, int batch, int hq, int hkv, int hd,
+                                                                    int bs, int pt_stride, float scale, int max_seq,
+                                                                    int64_t cur_batch) {
+  return batched_attn(q, kp, vp, pt, out, batch, hq, hkv, hd, bs, pt_stride, scale, max_seq, cur_batch, 1);
+}
+
+// ------------------------------------------------------------------------------------------------ encoders
+// Bidirectional attention over [seq, heads, hd] (every query sees every key).
+AE_API int aether_op_bert_self_attention_fwd_f32_cuda(int64_t q, int64_t k, int64_t v, int64_t out, int seq, int heads,
+                                                      int hd, float scale) {
+  if (seq <= 0 || heads <= 0 || hd <= 0) return -1;
+  const size_t n = (size_t)seq * heads * hd;
+  AttnArgs a{};
+  a.q = F(q, n);
+  a.kp = F(k, n);
+  a.vp = F(v, n);
+  a.out = F(out, n);
+  a.hq = a.hkv = heads; a.dk = a.dv = hd; a.bs = 1; a.scale = scale;
+  a.cur_const = seq;
+  a.max_seq = seq;
+  a.rows_k = a.rows_v = seq;
+  a.q_bstride = a.o_bstride = (long long)heads * hd;
+  a.n_split = 1;
+  if (!a.q || !a.kp || !a.vp || !a.out) return -1;
+  return attn_launch(a, seq);
+}
+// out[t] = word[ids[t]] + pos[t] + type[token_type[t]] (type handle 0: type 0)
+AE_API int aether_op_bert_embed_sum_f32_cuda(int64_t ids, int64_t tt, int64_t word, int64_t pos, int64_t type,
+                                             int64_t out, int seq, int d) {
+  if (seq <= 0 || d <= 0) return -1;
+  const int* pi = I(ids, seq);
+  const int* pt = tt ? I(tt, seq) : nullptr;
+  const int vocab = (int)(capacity(word, 4) / d), n_pos = (int)(capacity(pos, 4) / d),
+            n_type = (int)(capacity(type, 4) / d);
+  const float *pw = F(word, (size_t)vocab * d), *pp = F(pos, (size_t)n_pos * d), *py = F(type, (size_t)n_type * d);
+  float* po = F(out, (size_t)seq * d);
+  if (!pi || (tt && !pt) || !pw || !pp || !py || !po || vocab <= 0 || n_type <= 0) return -1;
+  EW_LAUNCH(k_bert_embed, (size_t)seq * d, pi, pt, pw, pp, py, po, seq, d, vocab, n_pos, n_type);
+}
+// DINOv3 axial RoPE on the patch tokens of buf [seq, heads, hd] with tables [n_patches, hd].
+AE_API int aether_op_dinov3_rope2d_f32_cuda(int64_t buf, int64_t cosb, int64_t sinb, int seq, int n_prefix, int heads,
+                                            int hd, int n_patches) {
+  if (seq <= 0 || n_prefix < 0 || heads <= 0 || hd <= 0 || hd % 2 || n_patches < 0 || n_prefix + n_patches > seq)
+    return -1;
+  float* pb = F(buf, (size_t)seq * heads * hd);
+  const float *pc = F(cosb, (size_t)n_patches * hd), *ps = F(sinb, (size_t)n_patches * hd);
+  if (!pb || (n_patches && (!pc || !ps))) return -1;
+  if (!n_patches) return 0;
+  EW_LAUNCH(k_rope2d_tables, (size_t)n_patches * heads * (hd / 2), pb, pc, ps, n_prefix, heads, hd, n_patches);
+}
+
+// ------------------------------------------------------------------------------------------------ MLA
+// kv_a [lora + rope] -> c_kv [lora], k_rope [rope]
+AE_API int aether_op_mla_split_kv_a_f32_cuda(int64_t kv_a, int64_t c_kv, int64_t k_rope, int lora, int rope) {
+  if (lora <= 0 || rope < 0) return -1;
+  const float* pa = F(kv_a, (size_t)lora + rope);
+  float *pc = F(c_kv, lora), *pr = rope ? F(k_rope, rope) : nullptr;
+  Ctx* c = ctx();
+  if (!pa || !pc || (rope && !pr) || !c) return -1;
+  k_copy_rows<<<blocks(lora), 256, 0, c->s>>>(pa, pc, 1, lora, 0, 0, 0, 0);
+  if (rope) k_copy_rows<<<blocks(rope), 256, 0, c->s>>>(pa, pr, 1, rope, 0, lora, 0, 0);
+  return launched("mla_split_kv_a");
+}
+// k_row[h] = [kv_b_out[h, :nope] | k_rope]  (kv_b_out rows of nope + v_hd)
+AE_API int aether_op_mla_assemble_k_f32_cuda(int64_t kv_b, int64_t k_rope, int64_t k_row, int heads, int nope, int rope,
+                                             int v_hd) {
+  if (heads <= 0 || nope <= 0 || rope < 0 || v_hd < 0) return -1;
+  const float *pb = F(kv_b, (size_t)heads * (nope + v_hd)), *pr = F(k_rope, rope ? rope : 1);
+  float* po = F(k_row, (size_t)heads * (nope + rope));
+  if (!pb || !pr || !po) return -1;
+  EW_LAUNCH(k_mla_copy, (size_t)heads * (nope + rope), pb, pr, po, heads, nope, rope, 1, v_hd);
+}
+// v_row[h] = kv_b_out[h, nope : nope + v_hd]
+AE_API int aether_op_mla_extract_v_f32_cuda(int64_t kv_b, int64_t v_row, int heads, int nope, int v_hd) {
+  if (heads <= 0 || nope < 0 || v_hd <= 0) return -1;
+  const float* pb = F(kv_b, (size_t)heads * (nope + v_hd));
+  float* po = F(v_row, (size_t)heads * v_hd);
+  if (!pb || !po) return -1;
+  EW_LAUNCH(k_mla_copy, (size_t)heads * v_hd, pb, nullptr, po, heads, nope, v_hd, 2, 0);
+}
+// k_row[h] = [c_kv | k_pe], v_row[h] = c_kv for every head (MQA view of the latent)
+AE_API int aether_op_mla_broadcast_kv_for_mqa_f32_cuda(int64_t c_kv, int64_t k_pe, int64_t k_row, int64_t v_row,
+                                                       int heads, int lora, int rope) {
+  if (heads <= 0 || lora <= 0 || rope < 0) return -1;
+  const float *pc = F(c_kv, lora), *pp = F(k_pe, rope ? rope : 1);
+  float *pk = F(k_row, (size_t)heads * (lora + rope)), *pv = F(v_row, (size_t)heads * lora);
+  Ctx* c = ctx();
+  if (!pc || !pp || !pk || !pv || !c) return -1;
+  k_mla_copy<<<blocks((size_t)heads * (lora + rope)), 256, 0, c->s>>>(pc, pp, pk, heads, lora, rope, 3, 0);
+  k_mla_copy<<<blocks((size_t)heads * lora), 256, 0, c->s>>>(pc, pp, pv, heads, lora, 0, 3, 0);
+  return launched("mla_broadcast_kv");
+}
+// RoPE on the last (qk_hd - nope) dims of each head of q, at step_args[0].
+AE_API int aether_op_mla_rope_q_partial_f32_cuda(int64_t q, int heads, int qk_hd, int nope, float base, int64_t step) {
+  const int rd = qk_hd - nope;
+  if (heads <= 0 || nope < 0 || rd <= 0 || rd % 2) return -1;
+  RopeArgs a{F(q, (size_t)heads * qk_hd), 1, heads, qk_hd, nope, rd, base, I(step, 1), 0, 1.f, 1.f, 1.f, 1.f};
+  return (!a.x || !a.pos) ? -1 : rope_launch(a);
+}
+AE_API int aether_op_mla_rope_k_shared_f32_cuda(int64_t k_rope, int rd, float base, int64_t step) {
+  if (rd <= 0 || rd % 2) return -1;
+  RopeArgs a{F(k_rope, rd), 1, 1, rd, 0, rd, base, I(step, 1), 0, 1.f, 1.f, 1.f, 1.f};
+  return (!a.x || !a.pos) ? -1 : rope_launch(a);
+}
+AE_API int aether_op_mla_rope_q_partial_yarn_f32_cuda(int64_t q, int heads, int qk_hd, int nope, float base, float ys,
+                                                      float yctx, float yfast, float yslow, int64_t step) {
+  const int rd = qk_hd - nope;
+  if (heads <= 0 || nope < 0 || rd <= 0 || rd % 2) return -1;
+  RopeArgs a{F(q, (size_t)heads * qk_hd), 1, heads, qk_hd, nope, rd, base, I(step, 1), 0, ys, yctx, yfast, yslow};
+  return (!a.x || !a.pos) ? -1 : rope_launch(a);
+}
+AE_API int aether_op_mla_rope_k_shared_yarn_f32_cuda(int64_t k_rope, int rd, float base, float ys, float yctx,
+                                                     float yfast, float yslow, int64_t step) {
+  if (rd <= 0 || rd % 2) return -1;
+  RopeArgs a{F(k_rope, rd), 1, 1, rd, 0, rd, base, I(step, 1), 0, ys, yctx, yfast, yslow};
+  return (!a.x || !a.pos) ? -1 : rope_launch(a);
+}
+// Absorbed MLA: q_out[h] = [W_kb[h] q_nope[h] | q_pe[h]] and attn_out[h] = W_vb[h] attn_v[h],
+// per-head weights in GGUF blocks (rows of q_nope resp. kv_lora values).
+#define MLA_ABSORB(name, T)                                                                                        \
+  AE_API int aether_op_mla_absorb_q_##name##_cuda(int64_t q, int64_t w, int64_t out, int heads, int key_mla,         \
+                                                  int qk_rope, int lora, int bpr) {                                 \
+    return absorb_q(T, q, w, out, heads, key_mla, qk_rope, lora, elements_per_row(T, bpr));                         \
+  }                                                                                                                 \
+  AE_API int aether_op_mla_absorb_v_##name##_cuda(int64_t av, int64_t w, int64_t out, int heads, int lora, int vdim, \
+                                                  int bpr) {                                                        \
+    return absorb_v(T, av, w, out, heads, lora, vdim, elements_per_row(T, bpr));                                     \
+  }
+MLA_ABSORB(q8_0, TQ8_0)
+MLA_ABSORB(q4_k, TQ4_K)
+MLA_ABSORB(q5_k, TQ5_K)
+MLA_ABSORB(q6_k, TQ6_K)
+MLA_ABSORB(iq4_nl, TIQ4_NL)
+MLA_ABSORB(f16, TF16)  // F16: the last argument counts elements per row (block of one)
+
+// ------------------------------------------------------------------------------------------------ q8_1 activations
+// x [n_in] -> int8 values, per-32 scales d and d * sum(q) (n_in a multiple of 32).
+AE_API int aether_op_quantize_q8_1_llama_cuda(int64_t x, int64_t aq, int64_t ad, int64_t as, int n_in) {
+  if (n_in <= 0 || n_in % 32) return -1;
+  const int nblk = n_in / 32;
+  const float* px = F(x, n_in);
+  int8_t* pq = (int8_t*)U(aq, n_in);
+  float *pd = F(ad, nblk), *ps = F(as, nblk);
+  Ctx* c = ctx();
+  if (!px || !pq || !pd || !ps || !c) return -1;
+  k_quant_q8_1<<<blocks(nblk, 8), 256, 0, c->s>>>(px, pq, pd, ps, nblk);
+  return launched("quantize_q8_1");
+}
+namespace {
+int mmvq(int t, int64_t w, int64_t w2, int64_t aq, int64_t ad, int64_t out, int n_out, int bpr) {
+  int ne, nb;
+  if (!block_of(t, &ne, &nb) || n_out <= 0 || bpr <= 0) return -1;
+  const size_t k = (size_t)bpr * ne, row_bytes = (size_t)bpr * nb;
+  const uint8_t* pw = U(w, row_bytes * n_out);
+  const uint8_t* pw2 = w2 ? U(w2, row_bytes * n_out) : nullptr;
+  const int8_t* pq = (const int8_t*)U(aq, k);
+  const float* pd = F(ad, k / 32);
+  float* po = F(out, n_out);
+  if (!pw || (w2 && !pw2) || !pq || !pd || !po) return -1;
+  MV p{nullptr, pw, po, pw2, n_out, (int)(k / 32), row_bytes, n_out, 0, 0, 0, 0, pq, pd};
+  return matvec_typed(t, p, 1);
+}
+}  // namespace
+// out = W x for x given as q8_1 (quantize_q8_1_llama output); swiglu: silu(W_gate x) * (W_up x)
+AE_API int aether_op_mmvq_q4k_q8_1_single_cuda(int64_t w, int64_t aq, int64_t ad, int64_t out, int n_out, int bpr) {
+  return mmvq(TQ4_K, w, 0, aq, ad, out, n_out, bpr);
+}
+AE_API int aether_op_mmvq_q6k_q8_1_single_cuda(int64_t w, int64_t aq, int64_t ad, int64_t out, int n_out, int bpr) {
+  return mmvq(TQ6_K, w, 0, aq, ad, out, n_out, bpr);
+}
+AE_API int aether_op_mmvq_q4k_q8_1_swiglu_cuda(int64_t wg, int64_t wu, int64_t aq, int64_t ad, int64_t out, int n_out,
+                                               int bpr) {
+  return mmvq(TQ4_K, wg, wu, aq, ad, out, n_out, bpr);
+}
+// `batch` activation rows against one quantised weight: out [batch, n]
+AE_API int aether_op_fused_q4k_matmul_seqB_v3_cuda(int64_t a, int64_t w, int64_t o, int n, int nb, int batch) {
+  return qmatvec(TQ4_K, a, w, o, n, nb, 0, 0, batch);
+}
+AE_API int aether_op_fused_q4k_matmul_seqB_fp16_cuda(int64_t a, int64_t w, int64_t o, int n, int nb, int batch) {
+  return qmatvec(TQ4_K, a, w, o, n, nb, 0, 0, batch);
+}
+AE_API int aether_op_fused_q6k_matmul_seqB_v3_cuda(int64_t a, int64_t w, int64_t o, int n, int nb, int batch) {
+  return qmatvec(TQ6_K, a, w, o, n, nb, 0, 0, batch);
+}
+AE_API int aether_op_fused_q6k_matmul_seqB_fp16_cuda(int64_t a, int64_t w, int64_t o, int n, int nb, int batch) {
+  return qmatvec(TQ6_K, a, w, o, n, nb, 0, 0, batch);
+}
+// A Q4_K mat-vec kept under the reference's bandwidth-probe name.
+AE_API int aether_op_fused_q4k_membw_probe_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TQ4_K, a, w, o, n, nb);
 }

@@ -24,6 +24,12 @@ def test_exports_bound_and_bad_handles_refused():
     assert lb.aether_dev_h2d_f32(0, bogus, 4) == -1
     assert np.isnan(lb.aether_op_cross_entropy_f32_cuda(bogus, bogus, bogus, 2, 4))
     assert lb.aether_wall_us() > 0
+    assert lb.aether_op_paged_attention_seq1_devarg_f32_cuda(bogus, bogus, bogus, bogus, bogus, 8, 2, 64, 16, 1.0,
+                                                             128, bogus) == -1
+    assert lb.aether_op_paged_attention_seq1_v4_devarg_f32_cuda(bogus, bogus, bogus, bogus, bogus, bogus, bogus, bogus,
+                                                                8, 2, 64, 16, 1.0, 128, 0, bogus) == -1
+    assert lb.aether_op_mla_absorb_q_q4_k_cuda(bogus, bogus, bogus, 4, 192, 64, 512, 1) == -1
+    assert lb.aether_op_quantize_q8_1_llama_cuda(bogus, bogus, bogus, bogus, 33) == -1
     assert lb.aether_nccl_real_get_handle(0) == 0  # no clique yet
     assert lb.aether_nccl_real_all_reduce_f32(bogus, bogus, 4, 0, 1) == -1
     assert lb.aether_nccl_real_comm_world_size(5) == -1
