@@ -255,6 +255,10 @@ SIGNATURES = {
     "aether_http_parse_request": (I, [P, I, P, I, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "aether_http_write_response_200": (I, [P, I, P, I]),
     "aether_openai_render_completion": (I, [P, I, P, I, P, I, I, I, P, I]),
+    # TLS 1.3 sessions
+    "aether_tls13_server_new": (L, [P, P, P, P, I, P, I]),
+    "aether_tls13_client_new": (L, [P, P, P, I]),
+    "aether_tls13_self_loopback_smoke": (I, []),
     # AetherLM-Nano
     "aether_nano_create": (P, [I, I, I, I, I, I, U64]),
     "aether_nano_destroy": (None, [P]),
