@@ -118,8 +118,6 @@ class GPT:
         # chunk of every sequence; attention all-gathers K/V over the group
         self.cp = cp if cp is not None and cp.world > 1 else None
         tp_size = self.tp.world if self.tp else 1
-        # the shared q/k norm weights would get only this rank's heads' gradient
-        assert not (cfg.qk_norm and self.tp is not None), "qk_norm with tensor parallelism is not supported"
         if self.tp is not None and self.tp.sp:
             assert first and last and self.cp is None and shard is None, \
                 "sequence parallelism needs the whole model on a flat arena, without CP"
@@ -252,14 +250,16 @@ class GPT:
         return A.rmsnorm(x, a["final_norm"], cfg.norm_eps) if self.last else x
 
     def finish_grads(self) -> None:
-        """After the last backward of a step: under sequence parallelism each
-        TP rank holds the per-layer norm gradients of its own tokens only, so
-        they are summed over the TP group (one all-reduce of 2 * layers * d
-        floats). Everything else already holds the full gradient."""
-        if self.tp is None or not self.tp.sp:
+        """After the last backward of a step, sum over the TP group the
+        gradients that each rank holds only in part: the per-layer norms under
+        sequence parallelism (each rank saw its own tokens) and the shared q/k
+        norm weights under any TP (each rank normalised its own heads). One
+        all-reduce; everything else already holds the full gradient."""
+        if self.tp is None:
             return
-        gs = [getattr(self.arena[f"l{i}.{n}"], "main_grad", None) for i in self.layers
-              for n in ("attn_norm", "mlp_norm")]
+        names = [n for n in ("attn_norm", "mlp_norm") if self.tp.sp]
+        names += [n for n in ("q_norm", "k_norm") if self.cfg.qk_norm]
+        gs = [getattr(self.arena[f"l{i}.{n}"], "main_grad", None) for i in self.layers for n in names]
         gs = [g for g in gs if g is not None]  # frozen base weights (adapters) have none
         if not gs:
             return

@@ -25,7 +25,7 @@ def _tokens(step, n=4):
     return torch.randint(0, 128, (n, 17), generator=torch.Generator().manual_seed(50 + step))
 
 
-def _worker(rank, world, tp, port, q, sp=False):
+def _worker(rank, world, tp, port, q, sp=False, extra=None):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
                       MASTER_PORT=str(port))
     sys.path.insert(0, ROOT)
@@ -38,7 +38,7 @@ def _worker(rank, world, tp, port, q, sp=False):
     D.init(device="cpu", timeout_s=60)
     mesh = make_mesh(tp, sequence_parallel=sp)
     assert mesh.tp.sp == sp
-    m = GPT(GPTConfig(**CFG), device="cpu", seed=9, tp=mesh.tp, pad_multiple=mesh.dp_world)
+    m = GPT(GPTConfig(**CFG, **(extra or {})), device="cpu", seed=9, tp=mesh.tp, pad_multiple=mesh.dp_world)
     # one gradient for the checks against the unsharded model
     toks = _tokens(0)
     loss = m.loss(toks[:, :-1].contiguous(), toks[:, 1:].contiguous())
@@ -61,13 +61,13 @@ def _worker(rank, world, tp, port, q, sp=False):
     D.shutdown()
 
 
-def _run(world, tp, sp=False):
+def _run(world, tp, sp=False, extra=None):
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, tp, port, q, sp)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, tp, port, q, sp, extra)) for r in range(world)]
     for p in ps:
         p.start()
     got = {}
@@ -80,12 +80,12 @@ def _run(world, tp, sp=False):
     return got
 
 
-def _reference():
+def _reference(extra=None):
     from aether_b200.models.gpt import GPT, GPTConfig
     from aether_b200.parallel import dist as D
     from aether_b200.train import Trainer
 
-    m = GPT(GPTConfig(**CFG), device="cpu", seed=9)
+    m = GPT(GPTConfig(**CFG, **(extra or {})), device="cpu", seed=9)
     toks = _tokens(0)
     loss = m.loss(toks[:, :-1].contiguous(), toks[:, 1:].contiguous())
     loss.backward()
@@ -97,19 +97,19 @@ def _reference():
     return m, float(loss.detach()), grads
 
 
-def _init_master():
+def _init_master(extra=None):
     from aether_b200.models.gpt import GPT, GPTConfig
 
-    m = GPT(GPTConfig(**CFG), device="cpu", seed=9)
+    m = GPT(GPTConfig(**CFG, **(extra or {})), device="cpu", seed=9)
     return {n: m.arena.master_view(n).clone() for n in m.arena.names()}
 
 
-def _check(got, tp):
+def _check(got, tp, extra=None):
     from aether_b200.models.gpt import GPTConfig
     from aether_b200.parallel.tp_train import shard_tensor
 
-    cfg = GPTConfig(**CFG)
-    ref, lref, gref = _reference()
+    cfg = GPTConfig(**CFG, **(extra or {}))
+    ref, lref, gref = _reference(extra)
     for rank, (loss, grads, master) in got.items():
         assert abs(loss - lref) < 1e-4 * abs(lref), (loss, lref)
         tr = rank % tp
@@ -120,7 +120,7 @@ def _check(got, tp):
             assert err < 3e-2, (n, err)
         # Adam turns tiny, rounding-level gradient differences into full-size
         # steps, so compare the direction of each tensor's total update
-        init = _init_master()
+        init = _init_master(extra)
         for n, w in master.items():
             want = shard_tensor(cfg, n, ref.arena.master_view(n), tr, tp) - shard_tensor(cfg, n, init[n], tr, tp)
             got = torch.from_numpy(w) - shard_tensor(cfg, n, init[n], tr, tp)
@@ -142,3 +142,11 @@ def test_tp2_sequence_parallel_matches_single_process():
 
 def test_tp2_dp2_sequence_parallel_mesh_matches_single_process():
     _check(_run(4, 2, sp=True), 2)
+
+
+def test_tp2_qk_norm_matches_single_process():
+    """Qwen3-style q/k norms: each rank normalises its own heads, so the shared
+    norm weights' gradients are summed over the TP group."""
+    qk = {"qk_norm": True}
+    _check(_run(2, 2, extra=qk), 2, qk)
+    _check(_run(2, 2, sp=True, extra=qk), 2, qk)
