@@ -4,7 +4,6 @@ import pytest
 import torch
 
 from aether_b200.models.gpt import GPT, GPTConfig
-from aether_b200.optim import FlatAdamW
 from aether_b200.parallel import dist as D
 from aether_b200.train import Trainer
 from tests.util import rel_err

@@ -9,7 +9,7 @@ import torch
 from aether_b200 import _ext
 from aether_b200.ops import functional as F
 from aether_b200.ops import reference as ref
-from tests.util import assert_close, rel_err
+from tests.util import assert_close
 
 pytestmark = pytest.mark.gpu
 dev = "cuda"

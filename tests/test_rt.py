@@ -7,7 +7,6 @@ import ctypes
 import os
 
 import numpy as np
-import pytest
 import torch
 
 from aether_b200 import runtime as rt

@@ -1,6 +1,3 @@
-import torch
-
-
 def rel_err(out, ref):
     out = out.float()
     ref = ref.float()
