@@ -57,7 +57,6 @@ SIGNATURES = {
     "aether_nccl_comm_rank": (I, [L]),
     "aether_nccl_all_reduce_f32": (I, [P, P, I, I, L]),
     "aether_llm_inference_bench_tps": (Fl, [I, I, I, I, I]),
-    "aether_llm_inference_bench_tps_cuda": (Fl, [I, I, I, I, I]),
     "aether_print_bench": (I, [L, I, I, I, I, L]),
     "aether_img_normalize_f32": (I, [P, P, I, Fl, Fl]),
     "aether_img_patchify_f32": (I, [P, P, I, I, I]),

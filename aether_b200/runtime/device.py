@@ -155,6 +155,8 @@ SIGNATURES.update({
     "aether_op_mmvq_q6k_q8_1_single_cuda": (I, [L, L, L, L, I, I]),
     "aether_op_mmvq_q4k_q8_1_swiglu_cuda": (I, [L, L, L, L, L, I, I]),
     "aether_op_fused_q4k_membw_probe_cuda": (I, [L, L, L, I, I]),
+    "aether_llm_inference_bench_tps_cuda": (Fl, [I, I, I, I, I]),
+    "aether_llm_inference_bench_tps_cuda_resident": (Fl, [I, I, I, I, I]),
 })
 for _v in ("", "_v2", "_v3"):
     SIGNATURES[f"aether_op_paged_attention_seq1{_v}_devarg_f32_cuda"] = (I, [L, L, L, L, L, I, I, I, I, Fl, I, L])

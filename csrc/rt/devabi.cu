@@ -37,6 +37,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <algorithm>
 #include <vector>
 
 #define AE_API extern "C" __attribute__((visibility("default")))
@@ -2332,4 +2333,188 @@ AE_API int aether_op_fused_q6k_matmul_seqB_fp16_cuda(int64_t a, int64_t w, int64
 // A Q4_K mat-vec kept under the reference's bandwidth-probe name.
 AE_API int aether_op_fused_q4k_membw_probe_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
   return qmatvec(TQ4_K, a, w, o, n, nb);
+}
+
+// ================================================================================================ tiny-LM benches
+// Iterations per second of a pre-LayerNorm decoder block stack (LN -> Q/K/V ->
+// causal attention -> O + residual -> LN -> up -> SiLU -> down + residual) over
+// seq_len tokens in fp32, the weights drawn from the same fixed-seed SplitMix64
+// stream as the host library's CPU bench. -1 when no GPU is present.
+//   _cuda: every matmul is one round trip through the device (weights and
+//          activations uploaded, result downloaded, buffers allocated and
+//          freed per call); the other ops run on the host.
+//   _cuda_resident: weights uploaded once and every op on the device; one
+//          iteration is captured in a CUDA graph and replayed (eager launches
+//          when capture is not possible).
+namespace {
+struct TinyLM {
+  int d, f, s, layers;
+  std::vector<float> w, x;  // per layer: wq, wk, wv, wo (d x d), up (d x f), down (f x d)
+  TinyLM(int d_, int l_, int f_, int s_) : d(d_), f(f_), s(s_), layers(l_) {
+    uint64_t st = 0x2545F4914F6CDD1DULL;
+    auto rnd = [&]() {
+      st += 0x9E3779B97F4A7C15ULL;
+      uint64_t z = st;
+      z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+      z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+      z ^= z >> 31;
+      return ((float)(z >> 40) / (float)(1 << 24) - 0.5f) * 0.02f;
+    };
+    w.resize(per_layer() * layers);
+    for (auto& e : w) e = rnd();
+    x.resize((size_t)s * d);
+    for (auto& e : x) e = rnd();
+  }
+  size_t per_layer() const { return 4 * (size_t)d * d + 2 * (size_t)d * f; }
+  const float* W(int l, int i) const {  // i: 0..3 = q,k,v,o; 4 = up; 5 = down
+    const float* b = w.data() + per_layer() * l;
+    return i < 4 ? b + (size_t)i * d * d : b + 4 * (size_t)d * d + (size_t)(i - 4) * d * f;
+  }
+};
+
+void host_ln(const float* x, float* y, int s, int d) {
+  for (int r = 0; r < s; ++r) {
+    double m = 0, v = 0;
+    for (int j = 0; j < d; ++j) m += x[(size_t)r * d + j];
+    m /= d;
+    for (int j = 0; j < d; ++j) v += (x[(size_t)r * d + j] - m) * (x[(size_t)r * d + j] - m);
+    const float rs = (float)(1.0 / std::sqrt(v / d + 1e-5));
+    for (int j = 0; j < d; ++j) y[(size_t)r * d + j] = (float)(x[(size_t)r * d + j] - m) * rs;
+  }
+}
+void host_attn(const float* q, const float* k, const float* v, float* o, int s, int d) {
+  std::vector<float> p(s);
+  const float sc = 1.f / std::sqrt((float)d);
+  for (int i = 0; i < s; ++i) {
+    float m = -INFINITY, sum = 0.f;
+    for (int j = 0; j <= i; ++j) {
+      float a = 0.f;
+      for (int t = 0; t < d; ++t) a += q[(size_t)i * d + t] * k[(size_t)j * d + t];
+      p[j] = a * sc;
+      m = std::max(m, p[j]);
+    }
+    for (int j = 0; j <= i; ++j) sum += (p[j] = std::exp(p[j] - m));
+    for (int t = 0; t < d; ++t) {
+      float a = 0.f;
+      for (int j = 0; j <= i; ++j) a += p[j] * v[(size_t)j * d + t];
+      o[(size_t)i * d + t] = a / sum;
+    }
+  }
+}
+// One matmul as a self-contained device round trip.
+bool routed_matmul(Ctx* c, const float* a, const float* b, float* out, int m, int k, int n) {
+  float *da = nullptr, *db = nullptr, *dc = nullptr;
+  if (cudaMallocAsync(&da, (size_t)m * k * 4, c->s) || cudaMallocAsync(&db, (size_t)k * n * 4, c->s) ||
+      cudaMallocAsync(&dc, (size_t)m * n * 4, c->s))
+    return false;
+  cudaMemcpyAsync(da, a, (size_t)m * k * 4, cudaMemcpyHostToDevice, c->s);
+  cudaMemcpyAsync(db, b, (size_t)k * n * 4, cudaMemcpyHostToDevice, c->s);
+  const int r = gemm_rm(false, false, m, n, k, 1.f, da, k, db, n, 0.f, dc, n);
+  cudaMemcpyAsync(out, dc, (size_t)m * n * 4, cudaMemcpyDeviceToHost, c->s);
+  cudaFreeAsync(da, c->s);
+  cudaFreeAsync(db, c->s);
+  cudaFreeAsync(dc, c->s);
+  return r == 0 && cudaStreamSynchronize(c->s) == cudaSuccess;
+}
+}  // namespace
+
+AE_API float aether_llm_inference_bench_tps_cuda(int iters, int d_model, int n_layers, int ff, int seq_len) {
+  if (iters <= 0 || d_model <= 0 || n_layers <= 0 || ff <= 0 || seq_len <= 0) return 0.f;
+  Ctx* c = ctx();
+  if (!c) return -1.f;
+  TinyLM m(d_model, n_layers, ff, seq_len);
+  const int s = seq_len, d = d_model, f = ff;
+  std::vector<float> x = m.x, h((size_t)s * d), q(h), k(h), v(h), o(h), proj(h), up((size_t)s * f);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0; it < iters; ++it)
+    for (int l = 0; l < n_layers; ++l) {
+      host_ln(x.data(), h.data(), s, d);
+      if (!routed_matmul(c, h.data(), m.W(l, 0), q.data(), s, d, d) ||
+          !routed_matmul(c, h.data(), m.W(l, 1), k.data(), s, d, d) ||
+          !routed_matmul(c, h.data(), m.W(l, 2), v.data(), s, d, d))
+        return 0.f;
+      host_attn(q.data(), k.data(), v.data(), o.data(), s, d);
+      if (!routed_matmul(c, o.data(), m.W(l, 3), proj.data(), s, d, d)) return 0.f;
+      for (size_t i = 0; i < x.size(); ++i) x[i] += proj[i];
+      host_ln(x.data(), h.data(), s, d);
+      if (!routed_matmul(c, h.data(), m.W(l, 4), up.data(), s, d, f)) return 0.f;
+      for (auto& e : up) e = e / (1.f + std::exp(-e));
+      if (!routed_matmul(c, up.data(), m.W(l, 5), proj.data(), s, f, d)) return 0.f;
+      for (size_t i = 0; i < x.size(); ++i) x[i] += proj[i];
+    }
+  const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  return sec > 0 ? (float)(iters / sec) : 0.f;
+}
+
+AE_API float aether_llm_inference_bench_tps_cuda_resident(int iters, int d_model, int n_layers, int ff,
+                                                          int seq_len) {
+  if (iters <= 0 || d_model <= 0 || n_layers <= 0 || ff <= 0 || seq_len <= 0) return 0.f;
+  Ctx* c = ctx();
+  if (!c) return -1.f;
+  TinyLM m(d_model, n_layers, ff, seq_len);
+  const int s = seq_len, d = d_model, f = ff;
+  const size_t sd = (size_t)s * d;
+  float* buf = nullptr;  // weights | x | h | q | k | v | o | proj | up | att | mean | rstd | ones | zeros
+  const size_t n_w = m.w.size(), total = n_w + 7 * sd + (size_t)s * f + (size_t)s * s + 2 * (size_t)s + 2 * (size_t)d;
+  if (cudaMallocAsync(&buf, total * 4, c->s) != cudaSuccess) return 0.f;
+  float* W = buf;
+  float *x = W + n_w, *h = x + sd, *q = h + sd, *k = q + sd, *v = k + sd, *o = v + sd, *proj = o + sd;
+  float *up = proj + sd, *att = up + (size_t)s * f, *mean = att + (size_t)s * s, *rstd = mean + s, *ones = rstd + s;
+  float* zeros = ones + d;
+  cudaMemcpyAsync(W, m.w.data(), n_w * 4, cudaMemcpyHostToDevice, c->s);
+  cudaMemcpyAsync(x, m.x.data(), sd * 4, cudaMemcpyHostToDevice, c->s);
+  std::vector<float> one(d, 1.f);
+  cudaMemcpyAsync(ones, one.data(), (size_t)d * 4, cudaMemcpyHostToDevice, c->s);
+  cudaMemsetAsync(zeros, 0, (size_t)d * 4, c->s);
+  cudaStreamSynchronize(c->s);
+  const float scale = 1.f / std::sqrt((float)d);
+  auto layer_w = [&](int l, int i) { return W + (m.W(l, i) - m.w.data()); };
+  auto iteration = [&]() {
+    for (int l = 0; l < n_layers; ++l) {
+      k_layernorm<<<s, kRowThreads, 0, c->s>>>(x, nullptr, ones, zeros, h, mean, rstd, 1e-5f, d);
+      gemm_rm(false, false, s, d, d, 1.f, h, d, layer_w(l, 0), d, 0.f, q, d);
+      gemm_rm(false, false, s, d, d, 1.f, h, d, layer_w(l, 1), d, 0.f, k, d);
+      gemm_rm(false, false, s, d, d, 1.f, h, d, layer_w(l, 2), d, 0.f, v, d);
+      gemm_rm(false, true, s, s, d, scale, q, d, k, d, 0.f, att, s);
+      k_causal_softmax<<<s, kRowThreads, 0, c->s>>>(att, s);
+      gemm_rm(false, false, s, d, s, 1.f, att, s, v, d, 0.f, o, d);
+      gemm_rm(false, false, s, d, d, 1.f, o, d, layer_w(l, 3), d, 1.f, x, d);  // residual in the GEMM (beta 1)
+      k_layernorm<<<s, kRowThreads, 0, c->s>>>(x, nullptr, ones, zeros, h, mean, rstd, 1e-5f, d);
+      gemm_rm(false, false, s, f, d, 1.f, h, d, layer_w(l, 4), f, 0.f, up, f);
+      k_silu<<<blocks((size_t)s * f), 256, 0, c->s>>>(up, (size_t)s * f);
+      gemm_rm(false, false, s, d, f, 1.f, up, f, layer_w(l, 5), d, 1.f, x, d);
+    }
+  };
+  iteration();  // one eager pass first: cuBLAS sets up its workspace outside the capture
+  cudaStreamSynchronize(c->s);
+  // capture one iteration; replay it
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  if (cudaStreamBeginCapture(c->s, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+    iteration();
+    if (cudaStreamEndCapture(c->s, &g) != cudaSuccess || !g || cudaGraphInstantiate(&ge, g, 0) != cudaSuccess)
+      ge = nullptr;
+  }
+  cudaGetLastError();  // a failed capture falls back to eager launches
+  auto run = [&]() {
+    if (ge) cudaGraphLaunch(ge, c->s);
+    else iteration();
+  };
+  for (int i = 0; i < 3; ++i) run();  // warm-up
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, c->s);
+  for (int i = 0; i < iters; ++i) run();
+  cudaEventRecord(e1, c->s);
+  const bool ok = cudaEventSynchronize(e1) == cudaSuccess;
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (ge) cudaGraphExecDestroy(ge);
+  if (g) cudaGraphDestroy(g);
+  cudaFreeAsync(buf, c->s);
+  cudaStreamSynchronize(c->s);
+  return (ok && ms > 0.f) ? (float)(iters / (ms * 1e-3)) : 0.f;
 }

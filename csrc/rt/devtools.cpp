@@ -406,10 +406,8 @@ AE_API int aether_nccl_all_reduce_f32(const void* send, void* recv, int n, int o
 // Forward passes per second of a pre-LayerNorm decoder (LN -> Q/K/V -> causal
 // attention -> O + residual -> LN -> up -> SiLU -> down + residual) over a
 // seq_len-token block, fp32 on this CPU through the C ABI's own ops; weights
-// are drawn once from a fixed-seed SplitMix64 stream, scaled to +-0.01. GPU
-// serving throughput is measured by the Python package (bench_serve): the
-// cuBLAS-routed and device-resident variants return 0 (not built into the
-// host library).
+// are drawn once from a fixed-seed SplitMix64 stream, scaled to +-0.01. The
+// GPU variants (_cuda, _cuda_resident) live in the device library.
 int aether_op_matmul_f32(const void*, const void*, void*, int, int, int);
 int aether_op_layer_norm_f32(const void*, const void*, const void*, float, void*, void*, void*, int, int);
 int aether_op_sdpa_causal_f32(const void*, const void*, const void*, void*, void*, int, int, int);
@@ -465,8 +463,6 @@ AE_API float aether_llm_inference_bench_tps(int n_iters, int d_model, int n_laye
   const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
   return sec > 0 ? (float)(n_iters / sec) : 0.f;
 }
-AE_API float aether_llm_inference_bench_tps_cuda(int, int, int, int, int) { return 0.f; }
-AE_API float aether_llm_inference_bench_tps_cuda_resident(int, int, int, int, int) { return 0.f; }
 
 // One bench line: "cpu|gpu  M= N= K= iters= us=".
 AE_API int aether_print_bench(int64_t which, int m, int n, int k, int iters, int64_t us) {

@@ -30,6 +30,9 @@ def test_exports_bound_and_bad_handles_refused():
                                                                 8, 2, 64, 16, 1.0, 128, 0, bogus) == -1
     assert lb.aether_op_mla_absorb_q_q4_k_cuda(bogus, bogus, bogus, 4, 192, 64, 512, 1) == -1
     assert lb.aether_op_quantize_q8_1_llama_cuda(bogus, bogus, bogus, bogus, 33) == -1
+    if not torch.cuda.is_available():  # the GPU benches say -1 without a device
+        assert lb.aether_llm_inference_bench_tps_cuda(3, 64, 2, 256, 8) == -1.0
+        assert lb.aether_llm_inference_bench_tps_cuda_resident(3, 64, 2, 256, 8) == -1.0
     assert lb.aether_nccl_real_get_handle(0) == 0  # no clique yet
     assert lb.aether_nccl_real_all_reduce_f32(bogus, bogus, 4, 0, 1) == -1
     assert lb.aether_nccl_real_comm_world_size(5) == -1
@@ -445,3 +448,15 @@ def test_nccl_clique_on_the_visible_gpus():
         assert (d.download(recvs[r], 1000) == want).all()
     d.call("aether_nccl_real_finalize")
     d.call("aether_dev_set_device", 0)
+
+
+@pytest.mark.gpu
+def test_tiny_lm_benches(capsys):
+    """The reference witnesses' tiny decoder (2 layers, d 64, ff 256, 8
+    tokens): per-call routing and the device-resident graph replay."""
+    d = _dev()
+    per_call = d.lib.aether_llm_inference_bench_tps_cuda(50, 64, 2, 256, 8)
+    resident = d.lib.aether_llm_inference_bench_tps_cuda_resident(2000, 64, 2, 256, 8)
+    with capsys.disabled():
+        print(f"\ntiny LM iterations/s: per-call {per_call:.0f}, resident {resident:.0f}")
+    assert per_call > 0 and resident > per_call
