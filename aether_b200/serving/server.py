@@ -236,6 +236,7 @@ def main():
     ap.add_argument("--max-seq", type=int, default=4096)
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--h2c", action="store_true", help="serve HTTP/2 over cleartext (prior knowledge) instead of HTTP/1.1")
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--embeddings", action="store_true", help="also serve a BGE-large-shape /v1/embeddings model")
     ap.add_argument("--vision", action="store_true", help="also serve a DINOv3 ViT-L/16-shape /v1/vision/embed")
@@ -337,7 +338,14 @@ def main():
     app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, template=template, vision=vision,
                     rate_limit=limiter)
     try:
-        uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+        if args.h2c:
+            import asyncio
+
+            from .h2 import serve as serve_h2
+
+            asyncio.run(serve_h2(app, args.host, args.port))
+        else:
+            uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
     finally:
         engine.shutdown()
         if tp is not None:  # release the replaying ranks, then the process group

@@ -217,3 +217,62 @@ def test_jinja_chat_template_tools_and_tool_call_parsing():
     # the sandbox refuses attribute access into Python internals
     with pytest.raises(Exception):
         JinjaChatTemplate("{{ messages.__class__.__mro__ }}").render(msgs)
+
+
+def test_http2_server_routes():
+    """The same OpenAI app over h2c (prior knowledge), driven by curl."""
+    import asyncio
+    import shutil
+    import subprocess
+
+    from aether_b200.serving.h2 import serve
+    from aether_b200.serving.server import build_app
+
+    if not shutil.which("curl"):
+        pytest.skip("curl not available")
+    eng = Engine(_model(seed=6), ByteTokenizer(), max_concurrent=2, use_graph=False)
+    app = build_app(eng, "tiny-h2")
+    port = _free_port()
+    loop = asyncio.new_event_loop()
+    started = threading.Event()
+
+    def run():
+        asyncio.set_event_loop(loop)
+        ev = asyncio.Event()
+
+        async def main():
+            task = asyncio.ensure_future(serve(app, "127.0.0.1", port, ev))
+            await ev.wait()
+            started.set()
+            await task
+
+        try:
+            loop.run_until_complete(main())
+        except BaseException:  # cancelled at the end of the test
+            pass
+
+    th = threading.Thread(target=run, daemon=True)
+    th.start()
+    assert started.wait(10)
+    base = f"http://127.0.0.1:{port}"
+
+    def curl(*args, data=None):
+        out = subprocess.run(["curl", "-s", "--http2-prior-knowledge", "--max-time", "60", *args], input=data,
+                             capture_output=True, timeout=90)
+        assert out.returncode == 0, out.stderr
+        return out.stdout
+
+    try:
+        assert json.loads(curl(base + "/v1/models"))["data"][0]["id"] == "tiny-h2"
+        body = json.dumps({"prompt": "abc", "max_tokens": 4}).encode()
+        out = json.loads(curl("-H", "content-type: application/json", "--data-binary", "@-", base + "/v1/completions",
+                              data=body))
+        assert out["object"] == "text_completion" and out["usage"]["completion_tokens"] >= 1
+        body = json.dumps({"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3, "stream": True}).encode()
+        sse = curl("-N", "-H", "content-type: application/json", "--data-binary", "@-", base + "/v1/chat/completions",
+                   data=body).decode()
+        assert sse.count("data: ") >= 2 and sse.rstrip().endswith("data: [DONE]")
+    finally:
+        eng.shutdown()
+        for t in asyncio.all_tasks(loop):
+            loop.call_soon_threadsafe(t.cancel)
