@@ -17,6 +17,9 @@ decode identically):
         sub-blocks of 32, 128 bytes of nibbles; x = d*sc*q - dmin*mn
   Q6_K  256 values: 128 bytes low 4 bits, 64 bytes high 2 bits, 16 x int8
         scales, f16 d; x = d * scale * (q - 32) over 16 sub-blocks of 16
+  IQ3_XXS / IQ3_S  256 values: codebook indices (4 magnitudes each), sign
+        patterns and 4-bit scales; decoded by the native library, which holds
+        the format's codebooks
 """
 from __future__ import annotations
 
@@ -32,10 +35,11 @@ _SCALAR = {T_U8: "<B", T_I8: "<b", T_U16: "<H", T_I16: "<h", T_U32: "<I", T_I32:
 
 F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 14, 30
 Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, IQ4_NL, IQ4_XS = 3, 6, 7, 10, 11, 13, 20, 23
+IQ3_XXS, IQ3_S = 18, 21
 # (block elements, block bytes) of every type the load-time dequantiser reads
 BLOCKS = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24),
           Q8_0: (32, 34), Q2_K: (256, 84), Q3_K: (256, 110), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
-          IQ4_NL: (32, 18), IQ4_XS: (256, 136)}
+          IQ4_NL: (32, 18), IQ4_XS: (256, 136), IQ3_XXS: (256, 98), IQ3_S: (256, 110)}
 # the 16 non-uniform levels of the IQ4_NL / IQ4_XS formats
 IQ4_LEVELS = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.float32)
 # (block elements, block bytes)
@@ -175,6 +179,14 @@ def dequantize(buf: np.ndarray, typ: int, n: int) -> np.ndarray:
         return _dequant_32(buf, typ)[:n]
     if typ in (Q2_K, Q3_K, Q5_K, IQ4_XS):
         return _dequant_k(buf, typ)[:n]
+    if typ in (IQ3_XXS, IQ3_S):  # codebook formats: the native dequantisers hold the grids
+        from .. import runtime as rt
+
+        b = np.ascontiguousarray(buf, dtype=np.uint8)
+        nblk = b.size // BLOCKS[typ][1]
+        out = np.empty(nblk * 256, np.float32)
+        rt.call("aether_dequant_iq3_xxs" if typ == IQ3_XXS else "aether_dequant_iq3_s", rt.ptr(b), rt.ptr(out), nblk)
+        return out[:n]
     raise NotImplementedError(f"GGUF tensor type {typ} is not supported by the load-time dequantiser")
 
 

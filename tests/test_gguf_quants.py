@@ -107,3 +107,19 @@ def test_native_q3_k_matches():
     out = np.zeros(4 * 256, np.float32)
     assert R.call("aether_dequant_q3_k", R.ptr(b), R.ptr(out), 4) == 0
     assert np.allclose(out, G.dequantize(b.reshape(-1), G.Q3_K, 1024), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["IQ3_XXS", "IQ3_S"])
+def test_iq3_matches_the_gguf_package(name):
+    """The IQ3 codebook formats through the load-time dequantiser, against the
+    pure-Python dequantiser of the `gguf` package on random blocks."""
+    gq = pytest.importorskip("gguf.quants")
+    gt = pytest.importorskip("gguf").GGMLQuantizationType
+    typ = getattr(G, name)
+    ne, nb = G.BLOCKS[typ]
+    rng = np.random.default_rng(typ)
+    b = rng.integers(0, 256, size=(40, nb), dtype=np.uint8)
+    b[:, 0:2] = np.frombuffer(np.float16(rng.uniform(0.01, 0.1)).tobytes(), np.uint8)
+    want = gq.dequantize(b.reshape(-1), getattr(gt, name)).reshape(-1)
+    got = G.dequantize(b.reshape(-1), typ, 40 * ne - 7)
+    np.testing.assert_array_equal(got, want[: 40 * ne - 7])
