@@ -9,6 +9,13 @@ on different streams of one connection run concurrently.
     python -m aether_b200.serving.server --model 7b --h2c --port 8000
     curl --http2-prior-knowledge http://127.0.0.1:8000/v1/models
 
+With ``tls=True`` the same sessions run inside the library's own TLS 1.3
+server sessions (ChaCha20-Poly1305, X25519, a self-signed Ed25519
+certificate generated at start-up, ALPN "h2"):
+
+    python -m aether_b200.serving.server --model 7b --h2-tls --port 8443
+    curl -k --http2 https://127.0.0.1:8443/v1/models
+
 Reference: the h2 path of aether-serve (trainer/src/bin/serve.rs:1059-1207,
 runtime/src/http2.rs).
 """
@@ -118,11 +125,80 @@ class H2Connection:
         await self.app(scope, receive, send)
 
 
-async def serve(app, host: str = "127.0.0.1", port: int = 8000, ready: asyncio.Event | None = None):
-    """Serve `app` over h2c until cancelled."""
+class _TlsStream:
+    """Reader / writer pair over a native TLS 1.3 server session: reads return
+    decrypted application data, writes are encrypted into records."""
+
+    def __init__(self, reader, writer, cn: bytes):
+        import os
+
+        lb = rt.lib()
+        L, P, I = C.c_int64, C.c_void_p, C.c_int
+        lb.aether_tls13_server_new.restype = L
+        lb.aether_tls13_server_new.argtypes = [P, P, P, P, I, P, I]
+        lb.aether_tls13_server_feed.argtypes = [L, P, I, P, I]
+        lb.aether_tls13_server_take_outbound.argtypes = [L, P, I]
+        lb.aether_tls13_server_send.argtypes = [L, P, I]
+        lb.aether_tls13_server_free.argtypes = [L]
+        lb.aether_tls13_server_is_done.argtypes = [L]
+        self.lib, self.reader, self.writer = lb, reader, writer
+        self.early = bytearray()  # plaintext written before the handshake completed
+        self.h = lb.aether_tls13_server_new(os.urandom(32), os.urandom(32), os.urandom(32), cn, len(cn),
+                                            os.urandom(8), 8)
+        self.buf = C.create_string_buffer(1 << 17)
+        self.app = C.create_string_buffer(1 << 17)
+
+    def _flush(self):
+        while True:
+            n = self.lib.aether_tls13_server_take_outbound(self.h, self.buf, len(self.buf))
+            if n <= 0:
+                return
+            self.writer.write(self.buf.raw[:n])
+
+    async def read(self, n: int) -> bytes:
+        while True:
+            data = await self.reader.read(65536)
+            if not data:
+                return b""
+            got = self.lib.aether_tls13_server_feed(self.h, data, len(data), self.app, len(self.app))
+            if self.early and self.lib.aether_tls13_server_is_done(self.h) == 1:
+                early, self.early = bytes(self.early), bytearray()
+                self.lib.aether_tls13_server_send(self.h, early, len(early))
+            self._flush()
+            await self.writer.drain()
+            if got < 0:
+                return b""
+            if got:
+                return self.app.raw[:got]
+
+    def write(self, data: bytes) -> None:
+        if self.lib.aether_tls13_server_is_done(self.h) != 1:
+            self.early += data
+            return
+        if self.lib.aether_tls13_server_send(self.h, data, len(data)) >= 0:
+            self._flush()
+
+    async def drain(self) -> None:
+        await self.writer.drain()
+
+    def close(self) -> None:
+        self.lib.aether_tls13_server_free(self.h)
+        self.writer.close()
+
+    def get_extra_info(self, key):
+        return self.writer.get_extra_info(key)
+
+
+async def serve(app, host: str = "127.0.0.1", port: int = 8000, ready: asyncio.Event | None = None,
+                tls: bool = False):
+    """Serve `app` over h2c (or HTTP/2 over the native TLS 1.3 with tls=True) until cancelled."""
 
     async def on_conn(reader, writer):
-        await H2Connection(app, reader, writer, (host, port)).run()
+        if tls:
+            stream = _TlsStream(reader, writer, host.encode())
+            await H2Connection(app, stream, stream, (host, port)).run()
+        else:
+            await H2Connection(app, reader, writer, (host, port)).run()
 
     server = await asyncio.start_server(on_conn, host, port)
     if ready is not None:

@@ -237,6 +237,8 @@ def main():
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--h2c", action="store_true", help="serve HTTP/2 over cleartext (prior knowledge) instead of HTTP/1.1")
+    ap.add_argument("--h2-tls", action="store_true",
+                    help="serve HTTP/2 over the native TLS 1.3 (self-signed Ed25519 certificate, ALPN h2)")
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--embeddings", action="store_true", help="also serve a BGE-large-shape /v1/embeddings model")
     ap.add_argument("--vision", action="store_true", help="also serve a DINOv3 ViT-L/16-shape /v1/vision/embed")
@@ -338,12 +340,12 @@ def main():
     app = build_app(engine, f"qwen2.5-{args.model}", embedder=embedder, template=template, vision=vision,
                     rate_limit=limiter)
     try:
-        if args.h2c:
+        if args.h2c or args.h2_tls:
             import asyncio
 
             from .h2 import serve as serve_h2
 
-            asyncio.run(serve_h2(app, args.host, args.port))
+            asyncio.run(serve_h2(app, args.host, args.port, tls=args.h2_tls))
         else:
             uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
     finally:

@@ -196,6 +196,7 @@ struct Session {
   // server identity
   uint8_t ed_seed[32], ed_pub[32];
   Bytes cert;
+  bool alpn_h2 = false;  // server: the client offered "h2" and it was selected
   uint8_t peer_ed[32];
   Bytes transcript, in, out, hs_buf;
   Bytes hs_secret, c_hs, s_hs, c_ap, s_ap, master;
@@ -381,6 +382,12 @@ struct Session {
           Bytes k = v.take(v.u(2));
           if (g == GROUP_X25519 && k.size() == 32) share = k;
         }
+      } else if (t == 16) {  // ALPN: select "h2" when offered
+        Rd v = e.sub(e.u(2));
+        while (v.ok && !v.end()) {
+          const Bytes proto = v.take(v.u(1));
+          if (proto.size() == 2 && proto[0] == 'h' && proto[1] == '2') alpn_h2 = true;
+        }
       }
     }
     if (!r.ok || !ext.ok || !have_suite || !v13 || !ed || share.empty()) return false;
@@ -409,7 +416,11 @@ struct Session {
     aether_x25519_shared_secret(x_priv, share.data(), shared);
     derive_handshake(shared);
     wr.set(s_hs);
-    hs_msg(HS_EE, {0, 0});
+    if (alpn_h2) {  // EncryptedExtensions carrying the selected protocol
+      hs_msg(HS_EE, {0, 9, 0, 16, 0, 5, 0, 3, 2, 'h', '2'});
+    } else {
+      hs_msg(HS_EE, {0, 0});
+    }
     Bytes c;
     put8(c, 0);
     Bytes entry;
@@ -625,6 +636,11 @@ int aether_tls13_client_is_done(int64_t h) {
   return s ? s->st == CONNECTED : -2;
 }
 int aether_tls13_server_free(int64_t h) { return release(h, true); }
+// 1 when ALPN selected "h2" on this server session, 0 otherwise.
+int aether_tls13_server_alpn_h2(int64_t h) {
+  Session* s = get(h, true);
+  return s ? (int)s->alpn_h2 : -2;
+}
 int aether_tls13_client_free(int64_t h) { return release(h, false); }
 
 // Client and server in one process, fixed keys: handshake and one exchange of

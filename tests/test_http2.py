@@ -155,3 +155,51 @@ def test_curl_h2c_requests(h2_server):
     urls = [f"http://127.0.0.1:{port}/r{i}" for i in range(6)]
     out = _curl(port, "--parallel", "--parallel-immediate", *urls)
     assert out.count(b'"version": "2"') == 6
+
+
+def test_curl_h2_over_native_tls():
+    """curl (OpenSSL + nghttp2) negotiates TLS 1.3 and ALPN h2 with the
+    library's own TLS server session, then speaks HTTP/2 through it."""
+    if not shutil.which("curl"):
+        pytest.skip("curl not available")
+    from aether_b200.serving.h2 import serve
+
+    async def app(scope, receive, send):
+        await receive()
+        body = (b"tls h2 " + scope["path"].encode()) * (1 if scope["path"] != "/big" else 20000)
+        await send({"type": "http.response.start", "status": 200, "headers": [(b"content-type", b"text/plain")]})
+        await send({"type": "http.response.body", "body": body, "more_body": False})
+
+    port = _free_port()
+    loop = asyncio.new_event_loop()
+    ready = threading.Event()
+
+    def run():
+        asyncio.set_event_loop(loop)
+        ev = asyncio.Event()
+
+        async def main():
+            task = asyncio.ensure_future(serve(app, "127.0.0.1", port, ev, tls=True))
+            await ev.wait()
+            ready.set()
+            await task
+
+        try:
+            loop.run_until_complete(main())
+        except BaseException:  # cancelled at the end of the test
+            pass
+
+    threading.Thread(target=run, daemon=True).start()
+    assert ready.wait(10)
+    try:
+        out = subprocess.run(["curl", "-s", "-k", "--http2", "--tlsv1.3", "-w", "\\n%{http_version}",
+                              f"https://127.0.0.1:{port}/hello"], capture_output=True, timeout=30)
+        assert out.returncode == 0, out.stderr
+        body, version = out.stdout.rsplit(b"\n", 1)
+        assert body == b"tls h2 /hello" and version == b"2"
+        big = subprocess.run(["curl", "-s", "-k", "--http2", f"https://127.0.0.1:{port}/big"], capture_output=True,
+                             timeout=30)
+        assert big.stdout == b"tls h2 /big" * 20000
+    finally:
+        for t in asyncio.all_tasks(loop):
+            loop.call_soon_threadsafe(t.cancel)
