@@ -20,12 +20,21 @@
 //     B * Hkv <= AETHER_NOALLOC_MAX_COUNTERS (1024); larger problems are
 //     rejected with AETHER_NOALLOC_ETOOBIG before anything is launched.
 //     The scratch costs 8192 * 129 * 4 bytes + 4 KB, about 4.2 MB per GPU.
-//   * D must be 128, Hq a multiple of Hkv with Hq / Hkv <= 8, 1 <= splits <= 64;
-//     out must be 8-byte aligned with out_rs a multiple of 4.
+//   * D must be 128, Hq a multiple of Hkv with Hq / Hkv <= 8, 1 <= splits <= 64.
+//   * Alignment, because the kernel moves K/V rows in 16-byte copies, q in
+//     4-byte loads and out in 8-byte stores: k_cache and v_cache 16-byte
+//     aligned with slot_stride and pos_stride multiples of 8 elements; q
+//     4-byte aligned with q_rs even; out 8-byte aligned with out_rs a multiple
+//     of 4. Anything else returns AETHER_NOALLOC_EINVAL and launches nothing.
+//   * `stream` must belong to the current device (the scratch address is the
+//     current device's); a stream of another device returns
+//     AETHER_NOALLOC_EINVAL.
 //   * The first call on each device does one-time set-up for that device: it
 //     looks up the scratch address, raises the kernel's shared-memory limit and
-//     clears the counters (a synchronous memset). Make that first call before
-//     any stream capture, for example with a tiny warm-up problem.
+//     clears the counters (a memset followed by a device synchronise). Make
+//     that first call before any stream capture, for example with a tiny
+//     warm-up problem. If the set-up fails, the call returns
+//     AETHER_NOALLOC_ECUDA and the next call on that device tries again.
 //   * The scratch is shared by all calls on a device. Two calls whose
 //     executions overlap (different streams, or different host threads without
 //     ordering between them) race on it and give wrong results. Order the

@@ -681,6 +681,7 @@ void finalize_residual_norm(at::Tensor acc, std::optional<at::Tensor> bias, std:
 // Allocation-free variant of decode_attention (fused combine). Declared, with
 // its rules and limits, in aether_noalloc.h. It has no counterpart in the
 // reference. Same kernel as above; only where the scratch comes from differs.
+#include <atomic>
 #include <mutex>
 
 #include "aether_noalloc.h"
@@ -703,24 +704,32 @@ struct DeviceScratch {
   float* part_o = nullptr;
   float* part_lse = nullptr;
   int* counters = nullptr;
-  int status = AETHER_NOALLOC_ECUDA;
 };
 static DeviceScratch g_dev[kMaxDevices];
-static std::once_flag g_once[kMaxDevices];
+static std::atomic<bool> g_ready[kMaxDevices];  // set (release) after g_dev[dev] is filled in
+static std::mutex g_setup_mu;
 
-static void setup(int dev) {
+// Set-up of one device, run with that device current. A device is marked
+// ready only when every step succeeded, so a failed set-up (for example a
+// memset refused during another stream's global-mode capture) is retried by
+// the next call instead of failing every later call.
+static int setup(int dev) {
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  if (g_ready[dev].load(std::memory_order_acquire)) return AETHER_NOALLOC_OK;
   DeviceScratch s;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_o), g_part_o) != cudaSuccess ||
       cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_lse), g_part_lse) != cudaSuccess ||
       cudaGetSymbolAddress(reinterpret_cast<void**>(&s.counters), g_counters) != cudaSuccess ||
       cudaFuncSetAttribute(dec::decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kKvSmem) !=
           cudaSuccess ||
-      cudaMemset(s.counters, 0, sizeof(int) * kMaxCounters) != cudaSuccess) {
-    g_dev[dev].status = AETHER_NOALLOC_ECUDA;
-    return;
+      cudaMemset(s.counters, 0, sizeof(int) * kMaxCounters) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();  // clear the failed call's error so the caller's next CUDA call does not see it
+    return AETHER_NOALLOC_ECUDA;
   }
-  s.status = AETHER_NOALLOC_OK;
   g_dev[dev] = s;
+  g_ready[dev].store(true, std::memory_order_release);
+  return AETHER_NOALLOC_OK;
 }
 
 }  // namespace noalloc
@@ -732,7 +741,14 @@ extern "C" __attribute__((visibility("default"))) int aether_decode_attention_no
     float scale, void* stream) {
   using namespace aether;
   if (!q || !k_cache || !v_cache || !slot || !seqlen || !out) return AETHER_NOALLOC_EINVAL;
+  // The kernel reads K/V rows with 16-byte copies and q with 4-byte loads, and
+  // writes out with 8-byte stores: a misaligned base or stride would be a GPU
+  // fault (which ends the context), so it is an argument error here.
   if (out_rs % 4 != 0 || reinterpret_cast<uintptr_t>(out) % 8 != 0) return AETHER_NOALLOC_EINVAL;
+  if (reinterpret_cast<uintptr_t>(k_cache) % 16 != 0 || reinterpret_cast<uintptr_t>(v_cache) % 16 != 0 ||
+      slot_stride % 8 != 0 || pos_stride % 8 != 0 || slot_stride < 0 || pos_stride < 0)
+    return AETHER_NOALLOC_EINVAL;
+  if (reinterpret_cast<uintptr_t>(q) % 4 != 0 || q_rs % 2 != 0 || q_rs < 0) return AETHER_NOALLOC_EINVAL;
   if (B < 0 || D != 128 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0 || Hq / Hkv > dec::kMaxGroup || splits < 1 ||
       splits > dec::kMaxSplits)
     return AETHER_NOALLOC_EINVAL;
@@ -740,9 +756,20 @@ extern "C" __attribute__((visibility("default"))) int aether_decode_attention_no
     return AETHER_NOALLOC_ETOOBIG;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= noalloc::kMaxDevices) return AETHER_NOALLOC_ECUDA;
-  std::call_once(noalloc::g_once[dev], noalloc::setup, dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (st != nullptr && st != cudaStreamLegacy && st != cudaStreamPerThread) {
+    int sdev = -1;  // the scratch address belongs to the current device: the stream must be on it too
+    if (cudaStreamGetDevice(st, &sdev) != cudaSuccess) {
+      cudaGetLastError();
+      return AETHER_NOALLOC_EINVAL;
+    }
+    if (sdev != dev) return AETHER_NOALLOC_EINVAL;
+  }
+  if (!noalloc::g_ready[dev].load(std::memory_order_acquire)) {
+    const int rc = noalloc::setup(dev);
+    if (rc != AETHER_NOALLOC_OK) return rc;
+  }
   const noalloc::DeviceScratch& s = noalloc::g_dev[dev];
-  if (s.status != AETHER_NOALLOC_OK) return s.status;
   if (B == 0) return AETHER_NOALLOC_OK;
   dec::DecParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -762,7 +789,13 @@ extern "C" __attribute__((visibility("default"))) int aether_decode_attention_no
   p.Hkv = Hkv;
   p.splits = splits;
   p.scale_log2 = scale * dec::kLog2e;
-  dec::decode_attn_kernel<<<dim3((unsigned)splits, (unsigned)(B * Hkv)), 128, dec::kKvSmem,
-                            static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? AETHER_NOALLOC_OK : AETHER_NOALLOC_ECUDA;
+  // cudaLaunchKernelEx reports this launch's own error (cudaGetLastError
+  // would also return, and clear, an unrelated earlier error of the thread).
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)splits, (unsigned)(B * Hkv));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = dec::kKvSmem;
+  cfg.stream = st;
+  return cudaLaunchKernelEx(&cfg, dec::decode_attn_kernel, p) == cudaSuccess ? AETHER_NOALLOC_OK
+                                                                               : AETHER_NOALLOC_ECUDA;
 }
