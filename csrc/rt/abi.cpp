@@ -394,7 +394,6 @@ int aether_op_sgd_step_f32(void* param, const void* grad, float lr, float moment
 }
 // Single-process fallbacks of the collective ABI (multi-rank programs use the
 // torch.distributed engines; these keep world-size-1 programs linking).
-int aether_op_all_reduce_sum_f32(void* /*buf*/, int world_size, int /*n*/) { return world_size <= 1 ? 0 : -1; }
-void aether_dist_all_reduce(void* /*buf*/, int /*world_size*/, int /*backend*/) {}
+// aether_op_all_reduce_sum_f32 and aether_dist_all_reduce: collectives.cpp
 
 }  // extern "C"

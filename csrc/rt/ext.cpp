@@ -991,27 +991,8 @@ AE_API int64_t aether_timer_start() {
 }
 AE_API int64_t aether_timer_elapsed_us(int64_t start) { return aether_timer_start() - start; }
 
-// ------------------------------------------------------------------ single-rank collective shapes
-// One process, one rank: the data already is the result. Multi-rank
-// collectives run through torch.distributed / this package's NVLink kernels.
-AE_API int aether_op_broadcast_f32(void* buf, int n, int /*root*/) { return buf && n >= 0 ? 0 : -1; }
-AE_API int aether_op_all_gather_f32(const void* src, void* dst, int n, int world) {
-  if (!src || !dst || n < 0 || world < 1) return -1;
-  std::memcpy(dst, src, sizeof(float) * (size_t)n);
-  return 0;
-}
-AE_API int aether_op_reduce_scatter_f32(const void* src, void* dst, int n, int /*world*/) {
-  if (!src || !dst || n < 0) return -1;
-  std::memcpy(dst, src, sizeof(float) * (size_t)n);
-  return 0;
-}
-AE_API int aether_op_send_f32(const void* buf, int n, int /*dst*/) { return buf && n >= 0 ? 0 : -1; }
-AE_API int aether_op_recv_f32(void* buf, int n, int /*src*/) { return buf && n >= 0 ? 0 : -1; }
-AE_API int aether_op_all_to_all_f32(const void* src, void* dst, int n, int /*world*/) {
-  if (!src || !dst || n < 0) return -1;
-  std::memcpy(dst, src, sizeof(float) * (size_t)n);
-  return 0;
-}
+// The generic collectives (aether_op_{broadcast,all_gather,reduce_scatter,
+// send,recv,all_to_all}_f32) live in collectives.cpp, real across processes.
 
 // ------------------------------------------------------------------ distributed algorithm shapes
 // Single-process versions of the parallel layouts, with the reference's
