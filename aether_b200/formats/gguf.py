@@ -346,6 +346,9 @@ def write_gguf(path: str, metadata: dict, tensors: dict, alignment: int = 32) ->
         if isinstance(v, list):
             if all(isinstance(i, str) for i in v):
                 return struct.pack("<I", T_ARR) + struct.pack("<IQ", T_STR, len(v)) + b"".join(s(i) for i in v)
+            if any(isinstance(i, float) for i in v):  # e.g. tokenizer.ggml.scores
+                return struct.pack("<I", T_ARR) + struct.pack("<IQ", T_F32, len(v)) + b"".join(
+                    struct.pack("<f", float(i)) for i in v)
             return struct.pack("<I", T_ARR) + struct.pack("<IQ", T_I32, len(v)) + b"".join(struct.pack("<i", i) for i in v)
         raise TypeError(type(v))
 
@@ -437,8 +440,20 @@ def load_qwen_weights(path: str, device="cuda"):
 
 
 def tokenizer_from_gguf(g: GGUFFile):
-    from ..serving.tokenizer import BPETokenizer
+    """The GGUF file's own tokenizer: SentencePiece (``tokenizer.ggml.model``
+    "llama": pieces, scores, token types, BOS / EOS, add-BOS and space-prefix
+    flags) or byte-level BPE (``gpt2``: tokens + merges)."""
+    from ..serving.tokenizer import BPETokenizer, SPMTokenizer
 
+    if g.meta.get("tokenizer.ggml.model") == "llama":
+        toks = g.meta.get("tokenizer.ggml.tokens", [])
+        scores = g.meta.get("tokenizer.ggml.scores", [0.0] * len(toks))
+        types = g.meta.get("tokenizer.ggml.token_type", [1] * len(toks))
+        get = lambda k: (int(g.meta[k]) if k in g.meta else None)  # noqa: E731
+        return SPMTokenizer(toks, scores, types, bos_id=get("tokenizer.ggml.bos_token_id"),
+                            eos_id=get("tokenizer.ggml.eos_token_id"), unk_id=get("tokenizer.ggml.unknown_token_id"),
+                            add_bos=bool(g.meta.get("tokenizer.ggml.add_bos_token", True)),
+                            add_space_prefix=bool(g.meta.get("tokenizer.ggml.add_space_prefix", True)))
     toks = g.meta.get("tokenizer.ggml.tokens", [])
     merges = g.meta.get("tokenizer.ggml.merges", [])
     types = g.meta.get("tokenizer.ggml.token_type", [1] * len(toks))

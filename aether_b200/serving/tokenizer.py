@@ -8,6 +8,10 @@ GPT-2 byte map in runtime/src/serving.rs:3614-4170) and its chat templates
     random-init models and the byte-level nano model);
   * ``BPETokenizer``   -- byte-level BPE from a Hugging Face ``tokenizer.json``
     (GPT-2 / Qwen2 family): byte-to-unicode map, merge ranks, added tokens;
+  * ``SPMTokenizer``   -- SentencePiece vocabularies (GGUF
+    ``tokenizer.ggml.model == "llama"``: Llama / Mistral SPM, Gemma): pieces
+    with scores, spaces as U+2581, symbol-pair merges by score, byte fallback
+    (reference: ``SpmModel``, runtime/src/serving.rs:2615-2700);
   * ``chat_template``  -- ChatML (Qwen2), Llama-3 and a plain fallback.
 """
 from __future__ import annotations
@@ -152,6 +156,159 @@ class BPETokenizer:
                     buf.append(b)
         text.append(buf.decode("utf-8", errors="replace"))
         return "".join(text)
+
+
+_SPACE = "\u2581"
+
+
+class SPMTokenizer:
+    """SentencePiece tokenizer of the score-merge kind llama.cpp uses for
+    ``llama``-model GGUF vocabularies.
+
+    Encoding: spaces become U+2581 (optionally one is prefixed), the text is
+    split into UTF-8 characters, and the adjacent pair whose concatenation is
+    the highest-scoring vocabulary piece is merged repeatedly (ties: the
+    leftmost pair) until no adjacent pair forms a piece; a symbol that is not
+    a piece falls back to its ``<0xNN>`` byte tokens. This is SentencePiece's
+    BPE-model encoding, which the Llama / Mistral / Gemma vocabularies use.
+    Control and unused entries (token types 3 and 5) take no part in merging;
+    user-defined / control strings (types 3, 4) are matched whole first.
+    """
+
+    NORMAL, UNKNOWN, CONTROL, USER, UNUSED, BYTE = 1, 2, 3, 4, 5, 6
+
+    def __init__(self, pieces: list, scores: list, types: list | None = None, bos_id: int | None = None,
+                 eos_id: int | None = None, add_bos: bool = False, add_space_prefix: bool = False,
+                 unk_id: int | None = None):
+        types = list(types) if types is not None else [self.NORMAL] * len(pieces)
+        self.pieces = list(pieces)
+        self.vocab_size = len(pieces)
+        self.piece_id: dict = {}
+        self.score: dict = {}
+        self.byte_id = [-1] * 256
+        self.special: dict = {}
+        for i, (p, sc, ty) in enumerate(zip(self.pieces, scores, types)):
+            if len(p) == 6 and p.startswith("<0x") and p.endswith(">"):
+                try:
+                    self.byte_id[int(p[3:5], 16)] = i
+                    continue
+                except ValueError:
+                    pass
+            if ty in (self.CONTROL, self.USER):
+                if p:
+                    self.special.setdefault(p, i)
+                continue
+            if ty == self.UNUSED or not p:
+                continue
+            if p not in self.piece_id:  # the lowest id wins for a repeated surface
+                self.piece_id[p] = i
+                self.score[p] = float(sc)
+        self.bos_id, self.eos_id, self.unk_id = bos_id, eos_id, unk_id
+        self.add_bos, self.add_space_prefix = add_bos, add_space_prefix
+        self._special_re = (re.compile("(" + "|".join(re.escape(t) for t in sorted(self.special, key=len,
+                                                                                    reverse=True)) + ")")
+                            if self.special else None)
+
+    @staticmethod
+    def from_sentencepiece(model_file: str, **kw) -> "SPMTokenizer":
+        """From a SentencePiece ``.model`` file (needs the ``sentencepiece`` package)."""
+        import sentencepiece as spm
+
+        sp = spm.SentencePieceProcessor(model_file=model_file)
+        n = sp.get_piece_size()
+        types = []
+        for i in range(n):
+            types.append(SPMTokenizer.CONTROL if sp.is_control(i) else SPMTokenizer.UNKNOWN if sp.is_unknown(i)
+                         else SPMTokenizer.UNUSED if sp.is_unused(i) else SPMTokenizer.BYTE if sp.is_byte(i)
+                         else SPMTokenizer.NORMAL)
+        return SPMTokenizer([sp.id_to_piece(i) for i in range(n)], [sp.get_score(i) for i in range(n)], types,
+                            bos_id=sp.bos_id() if sp.bos_id() >= 0 else None,
+                            eos_id=sp.eos_id() if sp.eos_id() >= 0 else None,
+                            unk_id=sp.unk_id() if sp.unk_id() >= 0 else None, **kw)
+
+    def _encode_fragment(self, text: str) -> list:
+        import heapq
+
+        if not text:
+            return []
+        text = text.replace(" ", _SPACE)
+        sym = list(text)  # one symbol per character; "" marks a symbol merged away
+        n = len(sym)
+        prev = list(range(-1, n - 1))
+        nxt = list(range(1, n + 1))
+        nxt[-1] = -1
+        heap = []
+
+        def push(i, j):
+            if i < 0 or j < 0:
+                return
+            cand = sym[i] + sym[j]
+            sc = self.score.get(cand)
+            if sc is not None:
+                heapq.heappush(heap, (-sc, i, j, cand))
+
+        for i in range(n - 1):
+            push(i, i + 1)
+        while heap:
+            _, i, j, cand = heapq.heappop(heap)
+            if not sym[i] or not sym[j] or nxt[i] != j or sym[i] + sym[j] != cand:
+                continue  # stale: one side was merged since this pair was queued
+            sym[i] = cand
+            sym[j] = ""
+            nxt[i] = nxt[j]
+            if nxt[j] >= 0:
+                prev[nxt[j]] = i
+            push(prev[i], i)
+            push(i, nxt[i])
+        out = []
+        i = 0
+        while i >= 0 and i < n:
+            s = sym[i]
+            tid = self.piece_id.get(s)
+            if tid is not None:
+                out.append(tid)
+            else:  # byte fallback
+                for b in s.encode("utf-8"):
+                    bid = self.byte_id[b]
+                    out.append(bid if bid >= 0 else (self.unk_id if self.unk_id is not None else 0))
+            i = nxt[i]
+        return out
+
+    def encode(self, text: str, allow_special: bool = True, add_bos: bool | None = None) -> list:
+        out = [self.bos_id] if (self.add_bos if add_bos is None else add_bos) and self.bos_id is not None else []
+        parts = self._special_re.split(text) if (allow_special and self._special_re) else [text]
+        after_special = True  # a text fragment at the start or after a special token gets the space prefix
+        for part in parts:
+            if not part:
+                continue
+            if allow_special and part in self.special:
+                out.append(self.special[part])
+                after_special = True
+                continue
+            if after_special and self.add_space_prefix:
+                part = " " + part
+            after_special = False
+            out.extend(self._encode_fragment(part))
+        return out
+
+    def decode(self, ids) -> str:
+        buf = bytearray()
+        for i in ids:
+            i = int(i)
+            if not 0 <= i < self.vocab_size:
+                continue
+            p = self.pieces[i]
+            if len(p) == 6 and p.startswith("<0x") and p.endswith(">") and self.byte_id[int(p[3:5], 16)] == i:
+                buf.append(int(p[3:5], 16))
+            elif i in (self.bos_id, self.eos_id) or (p in self.special and self.special[p] == i
+                                                      and p.startswith("<") and p.endswith(">")):
+                continue  # control tokens render as nothing
+            else:
+                buf.extend(p.replace(_SPACE, " ").encode("utf-8"))
+        text = buf.decode("utf-8", errors="replace")
+        if self.add_space_prefix and text.startswith(" "):
+            text = text[1:]  # the space the encoder prefixed
+        return text
 
 
 def chat_template(messages: list, style: str = "chatml", add_generation_prompt: bool = True) -> str:
