@@ -170,6 +170,7 @@ class QwenWeights:
 
         self.embed = rnd(cfg.vocab, d)
         self.lm_head = self.embed if cfg.tie_embeddings else rnd(cfg.vocab, d)
+        self._set_vocab_shard()
         self.final_norm = torch.ones(d, dtype=torch.bfloat16, device=self.device)
         self.attn_norm = [torch.ones(d, dtype=torch.bfloat16, device=self.device) for _ in range(L)]
         self.q_norm = [torch.ones(D, dtype=torch.bfloat16, device=self.device) for _ in range(L)] if cfg.qk_norm else None
@@ -202,6 +203,25 @@ class QwenWeights:
             self.wd.append(wd[:, f0:f1].contiguous())
             del wqkv, bqkv, wo, wgu, wd
 
+    def _set_vocab_shard(self) -> None:
+        """Vocabulary-parallel LM head under TP: rank r keeps rows
+        [r * per, r * per + n) of the head (zero-padded to ``per`` rows, a
+        multiple of 8), and an untied full head is dropped from the device."""
+        cfg, tp = self.cfg, self.tp_size
+        self.lm_head_shard = None
+        if tp == 1:
+            return
+        V, d = cfg.vocab, cfg.d_model
+        per = (-(-V // tp) + 7) // 8 * 8
+        col0 = self.tp_rank * per
+        n = max(0, min(per, V - col0))
+        assert n > 0, "more TP ranks than vocabulary slices"
+        shard = torch.zeros(per, d, dtype=torch.bfloat16, device=self.device)
+        shard[:n].copy_(self.lm_head[col0 : col0 + n])
+        self.lm_head_shard, self.vocab_col0, self.vocab_n, self.vocab_per = shard, col0, n, per
+        if not cfg.tie_embeddings:
+            self.lm_head = None  # each rank streams only its slice
+
     @staticmethod
     def shard(full: "QwenWeights", tp_rank: int, tp_size: int, device) -> "QwenWeights":
         """One rank's shard of full (e.g. GGUF- or HF-loaded) weights, in the
@@ -224,7 +244,8 @@ class QwenWeights:
 
         to = lambda t: None if t is None else t.to(dev)  # noqa: E731
         w.embed = to(full.embed)
-        w.lm_head = w.embed if cfg.tie_embeddings else to(full.lm_head)
+        w.lm_head = w.embed if cfg.tie_embeddings else full.lm_head
+        w._set_vocab_shard()
         w.final_norm = to(full.final_norm)
         w.attn_norm = [to(t) for t in full.attn_norm]
         w.mlp_norm = [to(t) for t in full.mlp_norm]
@@ -268,6 +289,11 @@ class QwenModel:
         tp_size = tp.world if tp is not None else 1
         self.w = weights or QwenWeights(cfg, device, seed, tp_rank, tp_size)
         self.hq, self.hkv, self.f = self.w.hq, self.w.hkv, self.w.f
+        # vocabulary-parallel head: needs the TP object's merge / gather and a sharded head
+        self.vp = (tp is not None and hasattr(tp, "vocab_argmax")
+                   and getattr(self.w, "lm_head_shard", None) is not None)
+        # one-shot push reduction of the decode row-parallel GEMMs (CUDA TP only)
+        self.push = tp is not None and getattr(tp, "mode", None) == "push"
         self.max_batch = max_batch
         self.max_seq = max_seq or cfg.max_seq
         # one extra slot absorbs the K/V writes of padded batch rows
@@ -303,6 +329,10 @@ class QwenModel:
         self.fused_decode = _os.environ.get("AETHER_UNFUSED_DECODE", "0") != "1" and not cfg.qk_norm
         self._graphs: dict[int, tuple] = {}
         self._alloc_decode_buffers()
+        if tp is not None and hasattr(tp, "prepare_decode"):
+            V = cfg.vocab
+            cols = tp.world * self.w.vocab_per if self.vp else V
+            tp.prepare_decode(max_batch + 1, cfg.d_model, cols)
 
     # ------------------------------------------------------------------ buffers
     def _auto_splits(self, B: int) -> int:
@@ -318,7 +348,7 @@ class QwenModel:
         cfg, B, dev = self.cfg, self.max_batch, self.device
         D = cfg.head_dim
         qkv_w = (self.hq + 2 * self.hkv) * D
-        widest = max(qkv_w, 2 * self.f, cfg.d_model, cfg.vocab)
+        widest = max(qkv_w, 2 * self.f, cfg.d_model, self.w.vocab_per if self.vp else cfg.vocab)
         bf = torch.bfloat16
         self.buf = {
             "tok": torch.zeros(B, dtype=torch.long, device=dev),
@@ -393,6 +423,12 @@ class QwenModel:
             x = self._ffn(i, h, x)
         last = x.view(B, S, cfg.d_model)[:, -1].contiguous()
         hl, _, _ = F.rmsnorm(last, w.final_norm, cfg.norm_eps)
+        if self.vp:
+            loc = F.gemm(hl, w.lm_head_shard, out_dtype=torch.float32)
+            nxt = self.tp.vocab_argmax(loc, w.vocab_n, w.vocab_col0)
+            if return_logits:
+                return nxt, self.tp.gather_vocab(loc, w.vocab_n, w.vocab_col0, cfg.vocab)
+            return nxt
         head = self._prefill_head()
         logits = F.gemm(hl, head, out_dtype=torch.float32)
         if head.shape[0] != cfg.vocab:
@@ -454,25 +490,45 @@ class QwenModel:
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
                                self._auto_splits(B), b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table,
                                window=self.win[i], softcap=self.softcap)
-            if self.tp is None:
+            if self.push:  # local GEMM, then one push-reduce + residual + RMSNorm kernel
                 F.skinny_gemm(o, w.wo[i], acc)
-                racc = acc
+                self.tp.push_reduce(acc, x2, res=x, w=w.mlp_norm[i], h=h, eps=cfg.norm_eps)
             else:
-                racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
-            F.finalize_residual_norm(racc, x2, w.mlp_norm[i], h, res=x, eps=cfg.norm_eps, wait=self._tp_wait())
+                if self.tp is None:
+                    F.skinny_gemm(o, w.wo[i], acc)
+                    racc = acc
+                else:
+                    racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
+                F.finalize_residual_norm(racc, x2, w.mlp_norm[i], h, res=x, eps=cfg.norm_eps, wait=self._tp_wait())
             F.skinny_gemm(h, w.wgu[i], acc)
             F.skinny_finalize(acc, act, swiglu=True)
+            nw = w.attn_norm[i + 1] if i + 1 < L else w.final_norm
+            if self.push:
+                F.skinny_gemm(act, w.wd[i], acc)
+                self.tp.push_reduce(acc, x, res=x2, w=nw, h=h, eps=cfg.norm_eps)
+                continue
             if self.tp is None:
                 F.skinny_gemm(act, w.wd[i], acc)
                 racc = acc
             else:
                 racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
-            nw = w.attn_norm[i + 1] if i + 1 < L else w.final_norm
             F.finalize_residual_norm(racc, x, nw, h, res=x2, eps=cfg.norm_eps, wait=self._tp_wait())
-        F.skinny_gemm(h, w.lm_head, acc)
-        if self._want_logits:
-            b["logits"][:B].copy_(acc[:, : cfg.vocab])
-        b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
+        self._decode_head(B, h, acc)
+
+    def _decode_head(self, B: int, h, acc) -> None:
+        """LM head GEMM and greedy pick (TP: this rank's vocabulary slice and
+        the cross-rank merge); fp32 logits copied out when asked for."""
+        cfg, w, b = self.cfg, self.w, self.buf
+        if self.vp:
+            F.skinny_gemm(h, w.lm_head_shard, acc)
+            if self._want_logits:
+                self.tp.gather_vocab(acc, w.vocab_n, w.vocab_col0, cfg.vocab, out=b["logits"][:B])
+            self.tp.vocab_argmax(acc, w.vocab_n, w.vocab_col0, out=b["next"][:B])
+        else:
+            F.skinny_gemm(h, w.lm_head, acc)
+            if self._want_logits:
+                b["logits"][:B].copy_(acc[:, : cfg.vocab])
+            b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
         acc.zero_()
 
     def _step_body(self, B: int) -> None:
@@ -496,7 +552,10 @@ class QwenModel:
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
                                self._auto_splits(B), b["part_o"], b["part_lse"], page_table=self.page_table,
                                window=self.win[i], softcap=self.softcap)
-            if self.tp is None:
+            if self.push:
+                F.skinny_gemm(o, w.wo[i], acc)
+                self.tp.push_reduce(acc, x2, res=x)
+            elif self.tp is None:
                 F.skinny_gemm(o, w.wo[i], acc)
                 F.skinny_finalize(acc, x2, res=x)
             else:
@@ -505,11 +564,7 @@ class QwenModel:
             F.rmsnorm_into(x2, w.mlp_norm[i], h, cfg.norm_eps)
             self._decode_ffn(i, h, x2, x, act, acc)
         F.rmsnorm_into(x, w.final_norm, h, cfg.norm_eps)
-        F.skinny_gemm(h, w.lm_head, acc)
-        if self._want_logits:
-            b["logits"][:B].copy_(acc[:, : cfg.vocab])
-        b["next"][:B].copy_(F.argmax(acc[:, : cfg.vocab]))
-        acc.zero_()
+        self._decode_head(B, h, acc)
 
     def _tp_wait(self):
         return self.tp.finalize_wait() if self.tp is not None else None
@@ -519,7 +574,10 @@ class QwenModel:
         w = self.w
         F.skinny_gemm(h, w.wgu[i], acc)
         F.skinny_finalize(acc, act, swiglu=True)
-        if self.tp is None:
+        if self.push:
+            F.skinny_gemm(act, w.wd[i], acc)
+            self.tp.push_reduce(acc, x, res=x2)
+        elif self.tp is None:
             F.skinny_gemm(act, w.wd[i], acc)
             F.skinny_finalize(acc, x, res=x2)
         else:
@@ -634,6 +692,7 @@ class QwenModel:
             h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.mlp_norm[i].float()
             x = x + self._reference_ffn(i, h)
         h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.final_norm.float()
+        assert w.lm_head is not None, "reference_logits needs the full LM head (a TP rank keeps only its slice)"
         return h @ w.lm_head.float().t()
 
     def _reference_ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:

@@ -54,6 +54,15 @@ void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, 
 void skinny_gemm(at::Tensor x, at::Tensor w, at::Tensor acc, int64_t splits, int64_t acc_mc,
                  std::optional<at::Tensor> sig_peers, std::optional<at::Tensor> sig_epoch,
                  std::optional<at::Tensor> sig_done, int64_t sig_rank, int64_t sig_world);
+// tp_decode.cu
+void tp_vocab_argmax(at::Tensor logits, int64_t n_loc, int64_t col0, at::Tensor flag_peers, at::Tensor ctr,
+                     int64_t rows_cap, at::Tensor out, int64_t rank, int64_t world, double timeout_s);
+void tp_put_cols(at::Tensor src, int64_t n_loc, int64_t col0, at::Tensor data_peers, int64_t ldd, int64_t rank,
+                 int64_t world);
+void tp_push_reduce(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bias, std::optional<at::Tensor> res,
+                    std::optional<at::Tensor> w, std::optional<at::Tensor> h, double eps, at::Tensor data_peers,
+                    int64_t data_mc, int64_t ld, at::Tensor flag_peers, at::Tensor ctr, int64_t rows_cap,
+                    int64_t rank, int64_t world, double timeout_s);
 // comm.cu
 void team_barrier(at::Tensor peer_sig_ptrs, at::Tensor my_sig, at::Tensor epoch, int64_t rank, int64_t world,
                   double timeout_s);
@@ -136,6 +145,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "sig_peers"_a = pybind11::none(), "sig_epoch"_a = pybind11::none(), "sig_done"_a = pybind11::none(),
         "sig_rank"_a = 0, "sig_world"_a = 0);
   m.def("team_barrier", &aether::team_barrier);
+  m.def("tp_vocab_argmax", &aether::tp_vocab_argmax);
+  m.def("tp_put_cols", &aether::tp_put_cols);
+  m.def("tp_push_reduce", &aether::tp_push_reduce, "acc"_a, "y"_a, "bias"_a, "res"_a, "w"_a, "h"_a, "eps"_a,
+        "data_peers"_a, "data_mc"_a, "ld"_a, "flag_peers"_a, "ctr"_a, "rows_cap"_a, "rank"_a, "world"_a,
+        "timeout_s"_a);
   m.def("allreduce_oneshot", &aether::allreduce_oneshot);
   m.def("allreduce_nvls", &aether::allreduce_nvls);
   m.def("dp_reduce_adamw", &aether::dp_reduce_adamw);

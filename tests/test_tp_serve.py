@@ -4,6 +4,7 @@ single-rank model."""
 import os
 import socket
 
+import pytest
 import torch
 
 TINY = dict(vocab=512, d_model=128, n_layers=2, n_heads=2, n_kv_heads=2, d_ff=256, max_seq=64)
@@ -42,8 +43,38 @@ class _GlooTP:
     def finalize_wait(self):
         return None
 
+    def vocab_argmax(self, logits, n_loc, col0, out=None):
+        import torch.distributed as dist
 
-def _worker(rank, world, port, q):
+        loc = logits[:, :n_loc].float()
+        best, idx = loc.max(-1)
+        cand = torch.stack([best, (idx + col0).float()], -1)
+        allc = [torch.empty_like(cand) for _ in range(self.world)]
+        dist.all_gather(allc, cand)
+        allc = torch.stack(allc)  # [world, rows, 2]; ties go to the lowest rank = lowest index
+        r = allc[..., 0].argmax(0)
+        res = allc[r, torch.arange(allc.shape[1]), 1].long()
+        if out is None:
+            return res
+        out.copy_(res)
+        return out
+
+    def gather_vocab(self, logits, n_loc, col0, V, out=None):
+        import torch.distributed as dist
+
+        per = logits[:, :n_loc].float().contiguous()
+        sizes = [None] * self.world
+        dist.all_gather_object(sizes, per.shape[1])
+        parts = [torch.empty(per.shape[0], n, dtype=torch.float32) for n in sizes]
+        dist.all_gather(parts, per)
+        full = torch.cat(parts, 1)[:, :V]
+        if out is None:
+            return full
+        out.copy_(full)
+        return out
+
+
+def _worker(rank, world, port, q, tie=True):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import torch.distributed as dist
 
@@ -52,7 +83,8 @@ def _worker(rank, world, port, q):
 
     dist.init_process_group("gloo", rank=rank, world_size=world)
     ctrl = dist.new_group(backend="gloo")
-    model = QwenModel(QwenConfig(**TINY), device="cpu", seed=4, max_batch=2, max_seq=64, tp=_GlooTP(rank, world))
+    model = QwenModel(QwenConfig(**TINY, tie_embeddings=tie), device="cpu", seed=4, max_batch=2, max_seq=64,
+                      tp=_GlooTP(rank, world))
     if rank == 0:
         from aether_b200.serving.engine import Engine
         from aether_b200.serving.sampling import SamplingParams
@@ -75,7 +107,10 @@ def _worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_tp_serving_matches_one_rank():
+@pytest.mark.parametrize("tie", [True, False])
+def test_tp_serving_matches_one_rank(tie):
+    """Tied head: the shard is a slice of the embedding; untied: each rank
+    keeps only its vocabulary slice of the head (vocabulary-parallel LM head)."""
     import multiprocessing as mp
 
     from aether_b200.models.qwen import QwenConfig, QwenModel
@@ -83,7 +118,7 @@ def test_tp_serving_matches_one_rank():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, tie)) for r in range(2)]
     for p in ps:
         p.start()
     got = dict(q.get(timeout=300) for _ in ps)
@@ -91,7 +126,7 @@ def test_tp_serving_matches_one_rank():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert got["replayed"] >= 2  # prefills and decode steps reached rank 1
-    ref = QwenModel(QwenConfig(**TINY), device="cpu", seed=4, max_batch=2, max_seq=64)
+    ref = QwenModel(QwenConfig(**TINY, tie_embeddings=tie), device="cpu", seed=4, max_batch=2, max_seq=64)
     for prompt, n, out in ((b"hello world", 5, got["outs"][0]), (b"tensor parallel", 4, got["outs"][1])):
         want = ref.generate(torch.tensor([list(prompt)]), n, use_graph=False)[0].tolist()
         assert out == want, (prompt, out, want)
