@@ -10,7 +10,11 @@ checkpoint readable.
 
 Loading concatenates all ranks' shards into the full master / moment vectors
 and slices the caller's own shard out of them, so a checkpoint written at one
-DP degree resumes at another. ZeRO-2 / ZeRO-3 arenas (``parallel.fsdp``)
+DP degree resumes at another. The bucketed DP engine
+(``OverlappedDataParallel``) owns one chunk of every layer instead of one
+range; its ranks save the list of (arena begin, end) chunks and their
+concatenated master / moments, which load into any engine the same way.
+ZeRO-2 / ZeRO-3 arenas (``parallel.fsdp``)
 save their per-layer-unit shards with the unit layout; loading rebuilds every
 parameter's full master and moments by name, so either kind of checkpoint
 resumes into either kind of arena at any world size. The bf16 compute copy is rebuilt from the fp32
@@ -54,19 +58,32 @@ def _sharded(arena) -> bool:
     return hasattr(arena, "units") and hasattr(arena, "scatter_full")
 
 
+def _slices(opt):
+    """[(arena begin, arena end, state offset)] of an engine that owns several
+    chunks (OverlappedDataParallel), else None."""
+    return getattr(getattr(opt, "opt", opt), "slices", None)
+
+
 def save(path: str, arena, opt, step: int, rank: int = 0, world: int = 1, extra: dict | None = None) -> None:
     os.makedirs(path, exist_ok=True)
     m, v, get_step, _, start, end = _opt_state(opt)
     end = arena.numel if end is None else end
     meta = {"step": step, "opt_step": get_step(), "start": start, "end": end, "numel": arena.numel,
             "rank": rank, "world": world, "cpu_rng": torch.get_rng_state().tolist()}
+    slices = _slices(opt)
     if _sharded(arena):
         meta.update(kind="sharded", layout=arena.layout(), start=0, end=arena.numel)
         start, end = 0, arena.numel
     if arena.device.type == "cuda":
         meta["cuda_rng"] = torch.cuda.get_rng_state(arena.device).tolist()
-    st.save_file({"master": arena.master[start:end], "m": m, "v": v}, os.path.join(path, f"rank{rank:05d}.safetensors"),
-                 metadata={"aether": json.dumps(meta)})
+    if slices is not None:
+        meta.update(slices=[[b, e] for b, e, _ in slices], start=0, end=0)
+        master = torch.cat([arena.master[b:e] for b, e, _ in slices]) if slices else arena.master[:0]
+        n = sum(e - b for b, e, _ in slices)
+        tensors = {"master": master, "m": m[:n], "v": v[:n]}
+    else:
+        tensors = {"master": arena.master[start:end], "m": m, "v": v}
+    st.save_file(tensors, os.path.join(path, f"rank{rank:05d}.safetensors"), metadata={"aether": json.dumps(meta)})
     if rank == 0:
         info = {"world": world, "numel": arena.numel, "step": step,
                 "slots": {n: [list(s.shape), s.offset, s.numel, s.decay] for n, s in arena.slots.items()},
@@ -98,11 +115,29 @@ def named_state(path: str) -> tuple:
         return info, out, metas
     full = {k: torch.zeros(info["numel"], dtype=torch.float32) for k in ("master", "m", "v")}
     for me, sh in zip(metas, shards):
-        for k in full:
-            full[k][me["start"] : me["end"]] = sh[k]
+        _place(full, me, sh)
     for n, (shape, off, numel, _) in info["slots"].items():
         out[n] = {k: full[k][off : off + numel].view(shape).clone() for k in full}
     return info, out, metas
+
+
+def _place(full: dict, meta: dict, shard: dict) -> None:
+    """Writes one rank's saved state into the full vectors."""
+    if "slices" in meta:
+        o = 0
+        for b, e in meta["slices"]:
+            for k in full:
+                full[k][b:e] = shard[k][o : o + e - b]
+            o += e - b
+        return
+    for k in full:
+        full[k][meta["start"] : meta["end"]] = shard[k]
+
+
+def _holds(meta: dict, at: int) -> bool:
+    if "slices" in meta:
+        return any(b <= at < e for b, e in meta["slices"])
+    return meta["start"] <= at < meta["end"]
 
 
 def _restore_rng(meta, device) -> None:
@@ -127,20 +162,24 @@ def load(path: str, arena, opt, restore_rng: bool = True) -> int:
     my_rank_meta = None
     m, v, _, put_step, start, end = _opt_state(opt)
     end = arena.numel if end is None else end
+    slices = _slices(opt)
+    first = slices[0][0] if slices else start
     for r in range(info["world"]):
         f = os.path.join(path, f"rank{r:05d}.safetensors")
         meta = json.loads(st.metadata(f)["aether"])
-        t = st.load_file(f)
-        s, e = meta["start"], meta["end"]
-        for k in full:
-            full[k][s:e] = t[k]
-        if my_rank_meta is None or s <= start < e:  # the shard that holds ours (rank 0's as a fallback)
+        _place(full, meta, st.load_file(f))
+        if my_rank_meta is None or _holds(meta, first):  # the shard that holds ours (rank 0's as a fallback)
             my_rank_meta = meta
     with torch.no_grad():
         arena.master.copy_(full["master"][: arena.numel].to(arena.master.device))
         arena.sync_bf16_from_master()
-        m.copy_(full["m"][start:end].to(m.device))
-        v.copy_(full["v"][start:end].to(v.device))
+        if slices is not None:
+            for b, e, o in slices:
+                m[o : o + e - b].copy_(full["m"][b:e].to(m.device))
+                v[o : o + e - b].copy_(full["v"][b:e].to(v.device))
+        else:
+            m.copy_(full["m"][start:end].to(m.device))
+            v.copy_(full["v"][start:end].to(v.device))
     put_step(int(my_rank_meta["opt_step"]))
     if restore_rng:
         torch.set_rng_state(torch.tensor(my_rank_meta["cpu_rng"], dtype=torch.uint8))
@@ -174,8 +213,14 @@ def _load_by_name(path: str, arena, opt, restore_rng: bool) -> int:
                     arena.master_view(n).copy_(t["master"].to(arena.master.device))
                     fm[s.offset : s.offset + s.numel] = t["m"].reshape(-1)
                     fv[s.offset : s.offset + s.numel] = t["v"].reshape(-1)
-            m.copy_(fm[start:end].to(m.device))
-            v.copy_(fv[start:end].to(v.device))
+            slices = _slices(opt)
+            if slices is not None:
+                for b, e, o in slices:
+                    m[o : o + e - b].copy_(fm[b:e].to(m.device))
+                    v[o : o + e - b].copy_(fv[b:e].to(v.device))
+            else:
+                m.copy_(fm[start:end].to(m.device))
+                v.copy_(fv[start:end].to(v.device))
         arena.sync_bf16_from_master()
     rank = getattr(arena, "rank", 0)
     me = metas[rank] if rank < len(metas) else metas[0]

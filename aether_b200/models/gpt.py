@@ -100,6 +100,18 @@ def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool 
     return specs
 
 
+class _ReadyHook:
+    """Gradient hook on a layer's input: tells the data-parallel engine that the
+    named parameter bucket's gradients are final (returns None: the gradient
+    passes through unchanged)."""
+
+    def __init__(self, fn, key: str):
+        self.fn, self.key = fn, key
+
+    def __call__(self, grad):
+        self.fn(self.key)
+
+
 class GPT:
     """The whole model, or one pipeline stage of it (``layers``, ``first``,
     ``last``): a first stage embeds token ids, a last stage ends in the final
@@ -228,7 +240,12 @@ class GPT:
             assert x.shape[0] % self.tp.world == 0, "sequence parallelism needs B*S divisible by the TP degree"
             x = T.sp_split(x, self.tp)
         lin = self._linear
+        ready = getattr(self, "grad_ready_hook", None) if torch.is_grad_enabled() else None
         for i in self.layers:
+            if ready is not None and x.requires_grad:
+                # x's gradient is complete only after every op of layer i has run
+                # backward, so layer i's parameter gradients are final then
+                x.register_hook(_ReadyHook(ready, f"l{i}"))
             h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
             qkv = lin(i, "wqkv", h)
             if cfg.qk_norm:
@@ -247,6 +264,8 @@ class GPT:
             x = lin(i, "wd", act, residual=x)
         if sp:
             x = T.sp_gather(x, self.tp)
+        if ready is not None and self.last and x.requires_grad:
+            x.register_hook(_ReadyHook(ready, "head"))  # after the LM head and final norm backward
         return A.rmsnorm(x, a["final_norm"], cfg.norm_eps) if self.last else x
 
     def finish_grads(self) -> None:

@@ -32,6 +32,8 @@ class Trainer:
                                                          weight_decay=weight_decay, max_grad_norm=max_grad_norm)
         self.step_idx = 0
         self._loss_acc = torch.zeros(1, dtype=torch.float32, device=model.device)
+        if hasattr(self.dp, "attach"):  # engines that reduce gradient buckets during the backward
+            self.dp.attach(model)
 
     def lr_at(self, step: int) -> float:
         if self.total <= 0:
@@ -61,6 +63,7 @@ class Trainer:
         n_tok = b * (tokens.shape[1] - 1)
         self.model.arena.zero_grad()
         self._loss_acc.zero_()
+        arm = getattr(self.dp, "arm", None)
         with self._section("fwd_bwd"):
             for i in range(n_mb):
                 chunk = tokens[i * mb : (i + 1) * mb]
@@ -69,6 +72,8 @@ class Trainer:
                 ids = chunk[:, :-1]
                 tgt = chunk[:, 1:]
                 loss = self.model.loss(ids.contiguous(), tgt.contiguous(), loss_scale=1.0 / n_tok)
+                if arm is not None and i == n_mb - 1:
+                    arm(self.lr_at(self.step_idx))  # the last backward reduces buckets as layers finish
                 loss.backward()
                 self._loss_acc += loss.detach()
             finish = getattr(self.model, "finish_grads", None)

@@ -4,7 +4,9 @@ Checks, on N ranks over NVLink:
   * team barrier + NVLS / P2P all-reduce (bf16 and fp32) against the plain sum;
   * fused data-parallel step (reduce + AdamW + broadcast kernel) against the
     NCCL reduce-scatter / AdamW / all-gather path from identical gradients;
-  * Qwen TP decode (multicast-reduce GEMM) and prefill against TP=1 tokens.
+  * the backward-overlapped bucketed DP engine against the NCCL engine;
+  * Qwen TP decode (push-reduce or multicast-reduce GEMM, vocabulary-parallel
+    LM head) and prefill against TP=1 tokens.
 Prints "OK <name>" lines; any mismatch raises (non-zero exit).
 """
 import os
@@ -64,6 +66,33 @@ def check_fused_dp(info):
         m2.arena.bf16.copy_(m1.arena.bf16)  # keep both forwards identical
     assert _ext.check_status() == 0
     print(f"OK fused_dp mc={team.has_multicast}", flush=True)
+
+
+def check_overlap_dp(info):
+    """Backward-overlapped bucketed DP (through Trainer, two micro-batches per
+    step) against the NCCL DataParallel engine from the same weights and data."""
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.parallel.dp import DataParallel, OverlappedDataParallel, team_alloc
+    from aether_b200.parallel.symm import SymmTeam
+    from aether_b200.train import Trainer
+
+    cfg = GPTConfig(vocab=512, d_model=256, n_layers=3, n_heads=2, n_kv_heads=2, d_ff=512, max_seq=128)
+    team = SymmTeam(info)
+    m1 = GPT(cfg, device=info.device, seed=5, pad_multiple=info.world, alloc=team_alloc(team))
+    m2 = GPT(cfg, device=info.device, seed=5, pad_multiple=info.world)
+    t1 = Trainer(m1, info, lr=1e-3, micro_batch=2, dp=OverlappedDataParallel(m1.arena, team, lr=1e-3))
+    t2 = Trainer(m2, info, lr=1e-3, micro_batch=2, dp=DataParallel(m2.arena, info, lr=1e-3))
+    toks = torch.randint(0, 512, (4, 129), device=info.device,
+                         generator=torch.Generator(device=info.device).manual_seed(info.rank))
+    for step in range(3):
+        l1 = float(t1.train_step(toks))
+        l2 = float(t2.train_step(toks))
+        torch.cuda.synchronize()
+        d = float((m1.arena.bf16.float() - m2.arena.bf16.float()).abs().max())
+        same = float((m1.arena.bf16.view(torch.int16) == m2.arena.bf16.view(torch.int16)).float().mean())
+        assert abs(l1 - l2) < 1e-3 * abs(l2) and d < 1e-2 and same > 0.99, (step, l1, l2, d, same)
+    assert _ext.check_status() == 0
+    print(f"OK overlap_dp mc={team.has_multicast} same={same:.4f}", flush=True)
 
 
 def check_tp_qwen(info):
@@ -263,11 +292,13 @@ def main():
     from aether_b200.parallel.symm import SymmTeam
 
     team = SymmTeam(info)
-    which = sys.argv[1:] or ["allreduce", "dp", "tp", "pp", "tp_train", "fsdp", "cp", "ep", "mla_tp"]
+    which = sys.argv[1:] or ["allreduce", "dp", "overlap_dp", "tp", "pp", "tp_train", "fsdp", "cp", "ep", "mla_tp"]
     if "allreduce" in which:
         check_allreduce(team, info)
     if "dp" in which:
         check_fused_dp(info)
+    if "overlap_dp" in which:
+        check_overlap_dp(info)
     if "tp" in which:
         check_tp_qwen(info)
     if "pp" in which:
