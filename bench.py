@@ -12,7 +12,16 @@ around exactly K steps (max over ranks) with device-resident synthetic inputs;
 with each step's token ids copied from pinned host memory and the loss read
 back to the host every step.
 
-``--impl reference`` reports why the reference implementation cannot run here.
+After training, the same processes serve the Qwen2.5-7B shape at TP = N (the
+other half of the headline): ``decode`` holds CUDA-event decode tokens/s and
+p50 time-to-first-token at batch 1 / 16 / 64 (prompt 2048, 256 greedy tokens,
+max over ranks). At N > 1 the line also carries ``params_in_sync`` (every
+data-parallel rank holds bit-identical bf16 parameters after the timed steps)
+and ``dp_check`` (one fused NVLink DP step against the NCCL path on a small
+model, relative difference of the updated parameters).
+
+``--impl reference`` probes for the reference's toolchain (cargo / rustc) and
+reports why the reference implementation cannot run here.
 """
 from __future__ import annotations
 
@@ -28,11 +37,42 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-REFERENCE_UNAVAILABLE = (
-    "the reference (suhteevah/aether) is a Rust cargo workspace with no setup.py/pyproject "
-    "(pip install of it fails) and this image has no cargo/rustc, so its NCCL+cuBLAS build "
-    "cannot be built offline"
-)
+def reference_status() -> str | None:
+    """Why the reference (a Rust cargo workspace) cannot run here, or None if
+    its toolchain and an installed build are present."""
+    import shutil
+
+    missing = [t for t in ("cargo", "rustc") if shutil.which(t) is None]
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    built = os.path.isdir(ref_dir) and any(os.scandir(ref_dir))
+    if not missing and built:
+        return None
+    why = []
+    if missing:
+        why.append("no " + "/".join(missing) + " on PATH")
+    if not built:
+        why.append("baseline/_ref is empty: pip install of the reference fails (a cargo workspace with no "
+                   "setup.py / pyproject.toml)")
+    return ("the reference (suhteevah/aether) is a Rust cargo workspace whose NCCL+cuBLAS build cannot be "
+            "produced offline here: " + "; ".join(why))
+
+
+def participating_gpus(world: int) -> list:
+    """nvidia-smi indices of the GPUs this job's ranks use (local ranks
+    0..world-1 on one node), through CUDA_VISIBLE_DEVICES when it is set."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if not vis:
+        return list(range(world))
+    items = [v.strip() for v in vis.split(",") if v.strip()][:world]
+    if all(v.isdigit() for v in items):
+        return [int(v) for v in items]
+    try:  # UUIDs: map through nvidia-smi's index,uuid table
+        out = subprocess.run(["nvidia-smi", "--query-gpu=index,uuid", "--format=csv,noheader"], capture_output=True,
+                             text=True, timeout=20).stdout
+        table = {u.strip(): int(i) for i, u in (line.split(",") for line in out.strip().splitlines())}
+        return [table[v] for v in items if v in table]
+    except (OSError, ValueError, subprocess.SubprocessError):
+        return []
 
 
 class ClockSampler:
@@ -115,22 +155,33 @@ def parse():
                     help="sequences per forward/backward pass (16: ~56 GB of activations on one GPU)")
     ap.add_argument("--layers", type=int, default=24, help="debug only; anything but 24 is not the benchmark config")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
-                    help="fused: one-kernel NVLink reduce + AdamW + broadcast; nccl: NCCL reduce-scatter/all-gather")
+    ap.add_argument("--dp", default="overlap", choices=["overlap", "fused", "nccl"],
+                    help="overlap: the fused NVLink reduce + AdamW + broadcast kernel per layer bucket, under the "
+                    "backward; fused: the same kernel once over the whole arena after the backward; "
+                    "nccl: NCCL reduce-scatter / all-gather")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (TP x DP mesh, e.g. --gpus 8 --tp 4)")
     ap.add_argument("--pp", type=int, default=1, help="pipeline stages (1F1B over NCCL p2p); --gpus must equal --pp")
     ap.add_argument("--sp", action="store_true",
                     help="sequence parallelism inside TP (residual stream split by token over the TP ranks)")
     ap.add_argument("--tp-comm", default="symm", choices=["symm", "nccl"],
                     help="TP all-reduce: in-kernel symmetric-memory (NVLS / peer loads) or NCCL")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Qwen2.5-7B TP=N serving section")
+    ap.add_argument("--decode-batches", default="1,16,64")
+    ap.add_argument("--decode-prompt", type=int, default=2048)
+    ap.add_argument("--decode-tokens", type=int, default=256)
     return ap.parse_args()
 
 
 def main():
     args = parse()
     if args.impl == "reference":
+        why = reference_status()
         if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}), flush=True)
+            if why is not None:
+                print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+            else:  # never reached on this image; kept so a toolchain that appears is not silently ignored
+                print(json.dumps({"impl": "reference", "unavailable": "cargo found, but no runner for the "
+                                  "reference's trainer is wired into this benchmark"}), flush=True)
         return 0
 
     import torch
@@ -165,14 +216,16 @@ def main():
 
         mesh = make_mesh(tp, use_symm=args.tp_comm == "symm", sequence_parallel=args.sp)
         dinfo = D.DistInfo(mesh.dp_rank, dp_world, info.local_rank, dev, info.backend)
-    if dp_world > 1 and args.dp == "fused":
-        from aether_b200.parallel.dp import FusedDataParallel, team_alloc
+    dp_mode = args.dp if (args.dp != "overlap" or mesh is None) else "fused"  # overlap: pure DP only
+    if dp_world > 1 and dp_mode in ("fused", "overlap"):
+        from aether_b200.parallel.dp import FusedDataParallel, OverlappedDataParallel, team_alloc
         from aether_b200.parallel.symm import SymmTeam
 
         team = SymmTeam(info, group=mesh.dp_group if mesh else None, timeout_s=60.0)
         model = GPT(cfg, device=dev, seed=1234, pad_multiple=dp_world, alloc=team_alloc(team),
                     tp=mesh.tp if mesh else None)
-        dp = FusedDataParallel(model.arena, team, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+        Engine = OverlappedDataParallel if dp_mode == "overlap" else FusedDataParallel
+        dp = Engine(model.arena, team, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
     else:
         model = GPT(cfg, device=dev, seed=1234, pad_multiple=dp_world, tp=mesh.tp if mesh else None)
         if mesh is not None:
@@ -188,13 +241,15 @@ def main():
             for _ in range(2)]
     dev_batch = host[0].to(dev)
 
+    dp_check = run_dp_check(info, dp_mode) if (dp_world > 1 and tp == 1 and dp_mode != "nccl") else None
+
     for _ in range(args.warmup):
         trainer.train_step(dev_batch)
     torch.cuda.synchronize()
     D.barrier()
 
     # ---------------------------------------------------------------- device-timed region
-    sampler = ClockSampler(range(torch.cuda.device_count())) if info.is_main else None
+    sampler = ClockSampler(participating_gpus(world)) if info.is_main else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
@@ -215,6 +270,7 @@ def main():
     ms = D.all_reduce_max(ms, dev)
     tokens_per_step = args.global_batch * S
     value = tokens_per_step / (ms / 1e3)
+    in_sync = params_in_sync(model.arena, mesh.dp_group if mesh else None, dev) if dp_world > 1 else None
 
     # ---------------------------------------------------------------- end-to-end region
     e2e = None
@@ -251,6 +307,15 @@ def main():
         pass
     peak_sus = peaks.get("bf16_tflops_sustained", 1400.0)
 
+    decode = None
+    if not args.no_decode:
+        del trainer, dp, model, dev_batch
+        import gc
+
+        gc.collect()
+        torch.cuda.empty_cache()
+        decode = run_decode(args, info)
+
     if info.is_main:
         out = {
             "metric": "train_tokens_per_s",
@@ -272,7 +337,9 @@ def main():
                 "seq_len": S,
                 "micro_batch": args.micro_batch,
                 "parallelism": (f"tp{tp}x" if tp > 1 else "") + f"dp{dp_world}"
-                + ((" zero1 " + ("fused-nvlink" if args.dp == "fused" else "nccl")) if dp_world > 1 else "")
+                + ((" zero1 " + {"overlap": "fused-nvlink bucketed, overlapped with backward",
+                                 "fused": "fused-nvlink after backward", "nccl": "nccl"}[dp_mode])
+                   if dp_world > 1 else "")
                 + (f" tp-allreduce-{args.tp_comm}" if tp > 1 else "") + (" sp" if tp > 1 and args.sp else ""),
                 "optimizer": "AdamW lr 3e-4 betas (0.9,0.95) wd 0.1, fp32 master",
                 "l2": "no flush needed: per-step working set (2.7 GB bf16 weights + activations) >> 126 MB L2",
@@ -282,12 +349,111 @@ def main():
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": launches,
+            "params_in_sync": in_sync,
+            "dp_check": dp_check,
+            "decode": decode,
             "impl": "aether",
         }
         print(json.dumps(out), flush=True)
     D.barrier()
     D.shutdown()
     return 0
+
+
+def params_in_sync(arena, group, dev) -> bool:
+    """True when every rank of the (data-parallel) group holds bit-identical
+    bf16 parameters: an exact integer checksum of the raw bits, compared
+    across ranks."""
+    import torch
+    import torch.distributed as dist
+
+    bits = arena.bf16.view(torch.int16).to(torch.int64)
+    w = torch.arange(1, bits.numel() + 1, device=dev, dtype=torch.int64) % 65521
+    mine = torch.stack([bits.sum(), (bits * w).sum()])
+    world = dist.get_world_size(group)
+    got = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(got, mine, group=group)
+    return bool(all(torch.equal(g, got[0]) for g in got))
+
+
+def run_dp_check(info, mode: str) -> dict:
+    """One optimiser step of a small GPT through the benchmark's NVLink DP
+    engine and through the NCCL reduce-scatter / AdamW / all-gather path from
+    the same weights and batches (two micro-batches): how far the updated
+    parameters differ (both paths sum the same fp32 gradients)."""
+    import torch
+
+    from aether_b200.models.gpt import GPT, GPTConfig
+    from aether_b200.parallel.dp import DataParallel, FusedDataParallel, OverlappedDataParallel, team_alloc
+    from aether_b200.parallel.symm import SymmTeam
+    from aether_b200.train import Trainer
+
+    cfg = GPTConfig(vocab=1024, d_model=256, n_layers=2, n_heads=2, n_kv_heads=2, d_ff=512, max_seq=256)
+    dev, world = info.device, info.world
+    gen = torch.Generator().manual_seed(77 + info.rank)
+    toks = torch.randint(0, cfg.vocab, (4, 129), generator=gen).to(dev)
+    team = SymmTeam(info, timeout_s=60.0)
+    m_f = GPT(cfg, device=dev, seed=5, pad_multiple=world, alloc=team_alloc(team))
+    Engine = OverlappedDataParallel if mode == "overlap" else FusedDataParallel
+    dp_f = Engine(m_f.arena, team, lr=1e-3, weight_decay=0.1)
+    m_n = GPT(cfg, device=dev, seed=5, pad_multiple=world)
+    dp_n = DataParallel(m_n.arena, info, lr=1e-3, weight_decay=0.1)
+    Trainer(m_f, info, lr=1e-3, weight_decay=0.1, micro_batch=2, dp=dp_f).train_step(toks)
+    Trainer(m_n, info, lr=1e-3, weight_decay=0.1, micro_batch=2, dp=dp_n).train_step(toks)
+    torch.cuda.synchronize()
+    a, b = m_f.arena, m_n.arena
+    # each engine updates only its own parts of the master copy: compare where both own
+    own = torch.zeros(a.numel, dtype=torch.bool, device=dev)
+    for s0, e0 in ([(x[0], x[1]) for x in dp_f.slices] if mode == "overlap" else [(dp_f.start, dp_f.end)]):
+        own[s0:e0] = True
+    own[: dp_n.start] = False
+    own[dp_n.end :] = False
+    # both paths sum the same fp32 gradients in a different order, so the step-1
+    # AdamW update (about lr * sign(g)) may differ only where a gradient is ~0
+    diff = ((a.master - b.master).abs() / 1e-3)[own] if bool(own.any()) else torch.zeros(1, device=dev)
+    frac = float((diff > 1e-2).float().mean())
+    bf_same = float((a.bf16.view(torch.int16) == b.bf16.view(torch.int16)).float().mean())
+    worst = D_max(float(diff.max()), dev)
+    frac = D_max(frac, dev)
+    bf_same = -D_max(-bf_same, dev)
+    del team
+    return {"model": "GPT-2L d256 (check only)", "engine": mode, "steps": 1, "max_update_diff_lr_units": worst,
+            "frac_updates_off_by_1pct_lr": frac, "frac_bf16_params_identical": bf_same,
+            "ok": frac < 1e-4 and bf_same > 0.999}
+
+
+def D_max(x: float, dev) -> float:
+    from aether_b200.parallel import dist as D
+
+    return D.all_reduce_max(x, dev)
+
+
+def run_decode(args, info) -> dict:
+    """Qwen2.5-7B shape served at TP = world: decode tokens/s and p50 TTFT per
+    batch (CUDA events, max over ranks; random-init bf16 weights, uniform-random
+    prompts, greedy, CUDA-graph decode step)."""
+    from aether_b200 import bench_serve
+
+    tp = None
+    if info.world > 1:
+        from aether_b200.parallel.tp import TensorParallel
+
+        tp = TensorParallel(info)
+    batches = [int(b) for b in args.decode_batches.split(",")]
+    recs = bench_serve.run("7b", batches, args.decode_prompt, args.decode_tokens, 3, tp, rank0=False)
+    if tp is not None:
+        tp.close()
+    rows = {str(r["batch"]): {"tokens_per_s": r["value"], "ms_per_step": r["ms_per_decode_step"],
+                              "ttft_p50_ms": r["ttft_p50_ms"]} for r in recs}
+    return {
+        "metric": "decode_tokens_per_s + p50 TTFT",
+        "model": "Qwen2.5-7B shape (28L d3584 28q/4kv heads, SwiGLU 18944, vocab 152064, untied head)",
+        "tp": info.world, "prompt": args.decode_prompt, "new_tokens": args.decode_tokens,
+        "batches": rows, "timing": "CUDA events: decode = 255 graph replays; TTFT = batched prefill + first token "
+        "(p50 of 3); max over ranks",
+        "lm_head": recs[0].get("lm_head") if recs else None,
+        "dtype": "bf16", "data": "synthetic uniform-random prompts, random-init weights",
+    }
 
 
 def run_pp(args, info, cfg):
@@ -319,7 +485,7 @@ def run_pp(args, info, cfg):
         step(dev)
     torch.cuda.synchronize()
     D.barrier()
-    sampler = ClockSampler(range(torch.cuda.device_count())) if info.is_main else None
+    sampler = ClockSampler(participating_gpus(world)) if info.is_main else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
