@@ -1,0 +1,1788 @@
+// aetherc: a compiler for the Aether language subset that the runtime
+// witnesses and training programs are written in, lowering to C and linking
+// against this package's C-ABI libraries (libaether_rt / libaether_dev).
+//
+// Reference: the aetherc CLI (compiler/src/main.rs:60-140: --emit kinds,
+// --check, --json-errors, -o), the `Tensor` method lowering of its asm
+// backend (compiler/src/codegen/asm/mod.rs:4195-4380: a method on a
+// shape-typed device tensor becomes one aether_op_*_cuda call with the shape
+// integers appended), its matmul -> gelu fusion peephole (compiler/src/mir/
+// fuse.rs:1-30) and the `--emit=c` backend (compiler/src/codegen/c/mod.rs).
+// The reference emits x86-64 assembly or C; this one always goes through C
+// (gcc / cc) and links the shared runtime libraries.
+//
+// Language covered: `use <module>;` (stdlib modules of extern declarations),
+// `const`, `extern fn`, `fn` with typed parameters and return type, `let` /
+// `let mut` with optional type, scalar types (bool, i8..i64, u8..u64, f32,
+// f64, &str), fixed arrays `[T; N]` (literal and repeat forms, indexing),
+// `Tensor<f32|i32, [dims]>` device tensors (allocated at `let`, freed when
+// the scope ends), `while`, `loop`, `for i in a..b` / `a..=b`, `break`,
+// `continue`, `return`, `if` / `else if` / `else` as statements and
+// expressions, block tail expressions, arithmetic / comparison / logical /
+// bitwise operators, compound assignment, `as` casts and the cast builtins
+// f32() f64() i32() i64(), println / print, float math builtins, and method
+// calls on tensors. Anything else (structs, traits, closures, macros,
+// generics) is a diagnostic, not a miscompile.
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <functional>
+#include <map>
+#include <memory>
+#include <set>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace ae {
+
+// ============================================================================ diagnostics
+struct Diag : std::runtime_error {
+  std::string code;
+  int line, col;
+  Diag(std::string c, int l, int k, const std::string& m) : std::runtime_error(m), code(std::move(c)), line(l), col(k) {}
+};
+[[noreturn]] void fail(const char* code, int line, int col, const std::string& msg) { throw Diag(code, line, col, msg); }
+
+// ============================================================================ lexer
+enum class T { Id, Int, Float, Str, Char, Op, Eof };
+struct Tok {
+  T t;
+  std::string s;
+  int line, col;
+};
+
+std::vector<Tok> lex(const std::string& src) {
+  std::vector<Tok> out;
+  size_t i = 0;
+  int line = 1, col = 1;
+  auto adv = [&](size_t n) {
+    for (size_t k = 0; k < n && i < src.size(); ++k, ++i) {
+      if (src[i] == '\n') {
+        ++line;
+        col = 1;
+      } else {
+        ++col;
+      }
+    }
+  };
+  static const char* ops3[] = {"..=", "<<=", ">>=", nullptr};
+  static const char* ops2[] = {"->", "=>", "==", "!=", "<=", ">=", "&&", "||", "+=", "-=", "*=", "/=", "%=",
+                               "&=", "|=", "^=", "<<", ">>", "::", "..", nullptr};
+  while (i < src.size()) {
+    const char c = src[i];
+    if (c == ' ' || c == '\t' || c == '\r' || c == '\n') {
+      adv(1);
+      continue;
+    }
+    if (c == '/' && i + 1 < src.size() && src[i + 1] == '/') {  // comments are dropped at lex time
+      while (i < src.size() && src[i] != '\n') adv(1);
+      continue;
+    }
+    if (c == '/' && i + 1 < src.size() && src[i + 1] == '*') {
+      int depth = 0;
+      do {
+        if (src.compare(i, 2, "/*") == 0) {
+          ++depth;
+          adv(2);
+        } else if (src.compare(i, 2, "*/") == 0) {
+          --depth;
+          adv(2);
+        } else {
+          adv(1);
+        }
+      } while (depth > 0 && i < src.size());
+      continue;
+    }
+    const int l0 = line, c0 = col;
+    if (isalpha((unsigned char)c) || c == '_') {
+      size_t j = i;
+      while (j < src.size() && (isalnum((unsigned char)src[j]) || src[j] == '_')) ++j;
+      out.push_back({T::Id, src.substr(i, j - i), l0, c0});
+      adv(j - i);
+      continue;
+    }
+    if (isdigit((unsigned char)c)) {
+      size_t j = i;
+      bool flt = false;
+      std::string text;
+      if (c == '0' && j + 1 < src.size() && (src[j + 1] == 'x' || src[j + 1] == 'X')) {
+        j += 2;
+        while (j < src.size() && (isxdigit((unsigned char)src[j]) || src[j] == '_')) {
+          if (src[j] != '_') text += src[j];
+          ++j;
+        }
+        text = std::to_string((long long)std::stoull(text, nullptr, 16));
+      } else if (c == '0' && j + 1 < src.size() && (src[j + 1] == 'o' || src[j + 1] == 'O')) {
+        j += 2;
+        while (j < src.size() && ((src[j] >= '0' && src[j] <= '7') || src[j] == '_')) {
+          if (src[j] != '_') text += src[j];
+          ++j;
+        }
+        text = std::to_string((long long)std::stoull(text, nullptr, 8));
+      } else if (c == '0' && j + 1 < src.size() && (src[j + 1] == 'b' || src[j + 1] == 'B')) {
+        j += 2;
+        while (j < src.size() && (src[j] == '0' || src[j] == '1' || src[j] == '_')) {
+          if (src[j] != '_') text += src[j];
+          ++j;
+        }
+        text = std::to_string((long long)std::stoull(text, nullptr, 2));
+      } else {
+        while (j < src.size() && (isdigit((unsigned char)src[j]) || src[j] == '_')) {
+          if (src[j] != '_') text += src[j];
+          ++j;
+        }
+        // a '.' starts a fraction unless it begins a range (`0..n`) or a method call (`1.max`)
+        if (j + 1 < src.size() && src[j] == '.' && isdigit((unsigned char)src[j + 1])) {
+          flt = true;
+          text += src[j++];
+          while (j < src.size() && (isdigit((unsigned char)src[j]) || src[j] == '_')) {
+            if (src[j] != '_') text += src[j];
+            ++j;
+          }
+        } else if (j < src.size() && src[j] == '.' && (j + 1 >= src.size() || (src[j + 1] != '.' &&
+                                                                                 !isalpha((unsigned char)src[j + 1]) &&
+                                                                                 src[j + 1] != '_'))) {
+          flt = true;  // `1.` literal
+          text += src[j++];
+        }
+        if (j < src.size() && (src[j] == 'e' || src[j] == 'E') && j + 1 < src.size() &&
+            (isdigit((unsigned char)src[j + 1]) || ((src[j + 1] == '-' || src[j + 1] == '+') && j + 2 < src.size() &&
+                                                    isdigit((unsigned char)src[j + 2])))) {
+          flt = true;
+          text += src[j++];
+          if (src[j] == '-' || src[j] == '+') text += src[j++];
+          while (j < src.size() && isdigit((unsigned char)src[j])) text += src[j++];
+        }
+      }
+      // type suffixes (1i32, 2.0f32, 3u8): kept as the literal's text after '#'
+      size_t k = j;
+      while (k < src.size() && (isalnum((unsigned char)src[k]) || src[k] == '_')) ++k;
+      std::string suffix = src.substr(j, k - j);
+      if (!suffix.empty()) {
+        if (suffix[0] == '_') suffix = suffix.substr(1);
+        if (suffix == "f32" || suffix == "f64") flt = true;
+        text += "#" + suffix;
+        j = k;
+      }
+      out.push_back({flt ? T::Float : T::Int, text, l0, c0});
+      adv(j - i);
+      continue;
+    }
+    if (c == '"') {
+      std::string s;
+      size_t j = i + 1;
+      while (j < src.size() && src[j] != '"') {
+        if (src[j] == '\\' && j + 1 < src.size()) {
+          const char e = src[j + 1];
+          s += e == 'n' ? '\n' : e == 't' ? '\t' : e == 'r' ? '\r' : e == '0' ? '\0' : e;
+          j += 2;
+        } else {
+          s += src[j++];
+        }
+      }
+      if (j >= src.size()) fail("AE0001", l0, c0, "unterminated string literal");
+      out.push_back({T::Str, s, l0, c0});
+      adv(j + 1 - i);
+      continue;
+    }
+    if (c == '\'' && i + 2 < src.size() && (src[i + 2] == '\'' || (src[i + 1] == '\\' && i + 3 < src.size()))) {
+      int v;
+      size_t len;
+      if (src[i + 1] == '\\') {
+        const char e = src[i + 2];
+        v = e == 'n' ? '\n' : e == 't' ? '\t' : e == 'r' ? '\r' : e == '0' ? 0 : e;
+        len = 4;
+      } else {
+        v = (unsigned char)src[i + 1];
+        len = 3;
+      }
+      out.push_back({T::Char, std::to_string(v), l0, c0});
+      adv(len);
+      continue;
+    }
+    std::string op;
+    for (int k = 0; ops3[k]; ++k)
+      if (src.compare(i, 3, ops3[k]) == 0) op = ops3[k];
+    if (op.empty())
+      for (int k = 0; ops2[k]; ++k)
+        if (src.compare(i, 2, ops2[k]) == 0) op = ops2[k];
+    if (op.empty()) op = std::string(1, c);
+    if (std::string("(){}[],;:.+-*/%<>=!&|^~#?@$").find(op[0]) == std::string::npos)
+      fail("AE0001", l0, c0, std::string("unexpected character '") + c + "'");
+    out.push_back({T::Op, op, l0, c0});
+    adv(op.size());
+  }
+  out.push_back({T::Eof, "", line, col});
+  return out;
+}
+
+// ============================================================================ types
+enum class B { Void, Bool, I8, I16, I32, I64, U8, U16, U32, U64, F32, F64, Str, Tensor, Array, Unknown };
+
+struct Ty {
+  B b = B::Unknown;
+  B elem = B::Unknown;           // tensor element (F32 / I32)
+  std::vector<int64_t> dims;     // tensor shape
+  std::shared_ptr<Ty> inner;     // array element
+  int64_t len = 0;               // array length
+  bool is_int() const { return b >= B::I8 && b <= B::U64; }
+  bool is_float() const { return b == B::F32 || b == B::F64; }
+  bool is_num() const { return is_int() || is_float(); }
+  int64_t numel() const {
+    int64_t n = 1;
+    for (int64_t d : dims) n *= d;
+    return n;
+  }
+};
+Ty prim(B b) {
+  Ty t;
+  t.b = b;
+  return t;
+}
+
+const std::map<std::string, B>& prim_names() {
+  static const std::map<std::string, B> m = {
+      {"bool", B::Bool}, {"i8", B::I8},   {"i16", B::I16}, {"i32", B::I32}, {"i64", B::I64}, {"isize", B::I64},
+      {"u8", B::U8},     {"u16", B::U16}, {"u32", B::U32}, {"u64", B::U64}, {"usize", B::U64}, {"f32", B::F32},
+      {"f64", B::F64},   {"str", B::Str}};
+  return m;
+}
+
+std::string ctype(const Ty& t) {
+  switch (t.b) {
+    case B::Void: return "void";
+    case B::Bool: return "int";
+    case B::I8: return "int8_t";
+    case B::I16: return "int16_t";
+    case B::I32: return "int32_t";
+    case B::I64: return "int64_t";
+    case B::U8: return "uint8_t";
+    case B::U16: return "uint16_t";
+    case B::U32: return "uint32_t";
+    case B::U64: return "uint64_t";
+    case B::F32: return "float";
+    case B::F64: return "double";
+    case B::Str: return "const char*";
+    case B::Tensor: return "int64_t";  // a device buffer handle
+    default: return "int64_t";
+  }
+}
+
+std::string tyname(const Ty& t) {
+  for (auto& kv : prim_names())
+    if (kv.second == t.b && kv.first != "isize" && kv.first != "usize") return t.b == B::Str ? "&str" : kv.first;
+  if (t.b == B::Void) return "()";
+  if (t.b == B::Tensor) {
+    std::string s = std::string("Tensor<") + (t.elem == B::I32 ? "i32" : "f32") + ", [";
+    for (size_t i = 0; i < t.dims.size(); ++i) s += (i ? ", " : "") + std::to_string(t.dims[i]);
+    return s + "]>";
+  }
+  if (t.b == B::Array) return "[" + tyname(*t.inner) + "; " + std::to_string(t.len) + "]";
+  return "?";
+}
+
+// ============================================================================ AST
+struct Expr;
+struct Stmt;
+struct Block;
+using EP = std::shared_ptr<Expr>;
+using SP = std::shared_ptr<Stmt>;
+using BP = std::shared_ptr<Block>;
+
+struct TyExpr {  // a type as written; tensor dims / array lengths may name constants
+  std::string name;              // primitive / "Tensor" / "[]" / "&str"
+  std::string elem;              // tensor element
+  std::vector<EP> dims;          // tensor dims or {array length}
+  std::shared_ptr<TyExpr> inner; // array element
+  int line = 0, col = 0;
+};
+
+struct Expr {
+  enum K { Int, Float, BoolL, Str, Char, Var, Unary, Binary, Call, Method, Cast, Ref, If, BlockE, Index, ArrayLit,
+           ArrayRep, LoopE } k;
+  std::string s;  // literal / name / operator / method
+  std::vector<EP> a;
+  BP blk, blk2;   // if: then / else block (else may be an `if` wrapped in a block)
+  std::shared_ptr<TyExpr> cast;
+  bool mut = false;
+  int line = 0, col = 0;
+};
+
+struct Block {
+  std::vector<SP> stmts;
+  EP tail;
+  int line = 0, col = 0;
+};
+
+struct Stmt {
+  enum K { Let, ExprS, Assign, While, Loop, For, Return, Break, Continue } k;
+  std::string name, op;
+  bool mut = false, inclusive = false;
+  std::shared_ptr<TyExpr> ty;
+  EP e, e2, e3;
+  BP body;
+  int line = 0, col = 0;
+};
+
+struct Param {
+  std::string name;
+  std::shared_ptr<TyExpr> ty;
+};
+struct Fn {
+  std::string name;
+  std::vector<Param> params;
+  std::shared_ptr<TyExpr> ret;
+  BP body;
+  bool is_extern = false;
+  int line = 0, col = 0;
+};
+struct Const {
+  std::string name;
+  std::shared_ptr<TyExpr> ty;
+  EP e;
+  int line = 0, col = 0;
+};
+struct Program {
+  std::vector<Fn> fns;
+  std::vector<Const> consts;
+  std::vector<std::string> uses;
+};
+
+// ============================================================================ parser
+class Parser {
+ public:
+  explicit Parser(std::vector<Tok> t) : t_(std::move(t)) {}
+
+  Program program() {
+    Program p;
+    while (!at(T::Eof)) {
+      if (is_id("pub")) next();
+      if (eat_id("use")) {
+        std::string path = ident();
+        while (eat_op("::")) path += "::" + ident();
+        expect_op(";");
+        p.uses.push_back(path);
+      } else if (eat_id("const") || eat_id("static")) {
+        Const c;
+        c.line = cur().line;
+        c.col = cur().col;
+        eat_id("mut");
+        c.name = ident();
+        expect_op(":");
+        c.ty = type();
+        expect_op("=");
+        c.e = expr();
+        expect_op(";");
+        p.consts.push_back(c);
+      } else if (is_id("extern") || is_id("fn") || is_id("unsafe")) {
+        p.fns.push_back(fn());
+      } else if (cur().t == T::Op && cur().s == "#") {  // attributes are accepted and ignored
+        next();
+        expect_op("[");
+        int depth = 1;
+        while (depth > 0 && !at(T::Eof)) {
+          if (cur().t == T::Op && cur().s == "[") ++depth;
+          if (cur().t == T::Op && cur().s == "]") --depth;
+          next();
+        }
+      } else {
+        fail("AE0100", cur().line, cur().col, "unsupported item '" + cur().s + "' (this compiler handles fn, extern fn, "
+                                              "const and use)");
+      }
+    }
+    return p;
+  }
+
+ private:
+  std::vector<Tok> t_;
+  size_t i_ = 0;
+  const Tok& cur() const { return t_[i_]; }
+  const Tok& peek(int k = 1) const { return t_[std::min(i_ + k, t_.size() - 1)]; }
+  void next() {
+    if (i_ + 1 < t_.size()) ++i_;
+  }
+  bool at(T t) const { return cur().t == t; }
+  bool is_op(const char* s) const { return cur().t == T::Op && cur().s == s; }
+  bool is_id(const char* s) const { return cur().t == T::Id && cur().s == s; }
+  bool eat_op(const char* s) {
+    if (!is_op(s)) return false;
+    next();
+    return true;
+  }
+  bool eat_id(const char* s) {
+    if (!is_id(s)) return false;
+    next();
+    return true;
+  }
+  void expect_op(const char* s) {
+    if (!eat_op(s)) fail("AE0002", cur().line, cur().col, std::string("expected '") + s + "', found '" + cur().s + "'");
+  }
+  std::string ident() {
+    if (!at(T::Id)) fail("AE0002", cur().line, cur().col, "expected an identifier, found '" + cur().s + "'");
+    std::string s = cur().s;
+    next();
+    return s;
+  }
+
+  std::shared_ptr<TyExpr> type() {
+    auto t = std::make_shared<TyExpr>();
+    t->line = cur().line;
+    t->col = cur().col;
+    if (eat_op("&")) {
+      eat_id("mut");
+      auto in = type();
+      if (in->name == "str") {
+        t->name = "str";
+        return t;
+      }
+      return in;  // references to scalars / tensors are passed by value (handles)
+    }
+    if (eat_op("[")) {
+      t->name = "[]";
+      t->inner = type();
+      expect_op(";");
+      t->dims.push_back(expr());
+      expect_op("]");
+      return t;
+    }
+    if (eat_op("(")) {
+      expect_op(")");
+      t->name = "()";
+      return t;
+    }
+    t->name = ident();
+    if (t->name == "Tensor") {
+      expect_op("<");
+      t->elem = ident();
+      expect_op(",");
+      expect_op("[");
+      while (!is_op("]")) {
+        t->dims.push_back(expr_prec(9));  // no comparison operators inside a shape
+        if (!eat_op(",")) break;
+      }
+      expect_op("]");
+      expect_op(">");
+    }
+    return t;
+  }
+
+  Fn fn() {
+    Fn f;
+    f.line = cur().line;
+    f.col = cur().col;
+    eat_id("unsafe");
+    if (eat_id("extern")) {
+      f.is_extern = true;
+      if (at(T::Str)) next();  // extern "C"
+    }
+    if (!eat_id("fn")) fail("AE0002", cur().line, cur().col, "expected 'fn'");
+    f.name = ident();
+    expect_op("(");
+    while (!is_op(")")) {
+      eat_id("mut");
+      Param p;
+      p.name = ident();
+      expect_op(":");
+      p.ty = type();
+      f.params.push_back(p);
+      if (!eat_op(",")) break;
+    }
+    expect_op(")");
+    if (eat_op("->")) f.ret = type();
+    if (f.is_extern) {
+      expect_op(";");
+    } else {
+      f.body = block();
+    }
+    return f;
+  }
+
+  BP block() {
+    auto b = std::make_shared<Block>();
+    b->line = cur().line;
+    b->col = cur().col;
+    expect_op("{");
+    while (!is_op("}")) {
+      if (at(T::Eof)) fail("AE0002", b->line, b->col, "unclosed block");
+      if (eat_op(";")) continue;
+      SP s = stmt();
+      if (!s) {  // a trailing expression without ';' ends the block
+        b->tail = last_expr_;
+        if (!is_op("}")) fail("AE0002", cur().line, cur().col, "expected ';' or '}' after an expression");
+        break;
+      }
+      b->stmts.push_back(s);
+    }
+    expect_op("}");
+    return b;
+  }
+
+  static bool block_like(const EP& e) {
+    return e->k == Expr::If || e->k == Expr::BlockE || e->k == Expr::LoopE;
+  }
+
+  EP last_expr_;
+
+  // A statement, or nullptr when an expression ends the block (its value is last_expr_).
+  SP stmt() {
+    auto s = std::make_shared<Stmt>();
+    s->line = cur().line;
+    s->col = cur().col;
+    if (eat_id("let")) {
+      s->k = Stmt::Let;
+      s->mut = eat_id("mut");
+      s->name = ident();
+      if (eat_op(":")) s->ty = type();
+      if (eat_op("=")) s->e = expr();
+      expect_op(";");
+      return s;
+    }
+    if (eat_id("while")) {
+      s->k = Stmt::While;
+      s->e = expr_nostruct();
+      s->body = block();
+      return s;
+    }
+    if (eat_id("for")) {
+      s->k = Stmt::For;
+      s->name = ident();
+      if (!eat_id("in")) fail("AE0002", cur().line, cur().col, "expected 'in'");
+      s->e = expr_prec(9);
+      if (eat_op("..=")) {
+        s->inclusive = true;
+      } else if (!eat_op("..")) {
+        fail("AE0100", cur().line, cur().col, "for loops iterate over ranges a..b or a..=b");
+      }
+      s->e2 = expr_prec(9);
+      s->body = block();
+      return s;
+    }
+    if (eat_id("return")) {
+      s->k = Stmt::Return;
+      if (!is_op(";") && !is_op("}")) s->e = expr();
+      eat_op(";");
+      return s;
+    }
+    if (eat_id("break")) {
+      s->k = Stmt::Break;
+      eat_op(";");
+      return s;
+    }
+    if (eat_id("continue")) {
+      s->k = Stmt::Continue;
+      eat_op(";");
+      return s;
+    }
+    EP e = expr();
+    static const std::set<std::string> assign = {"=", "+=", "-=", "*=", "/=", "%=", "&=", "|=", "^=", "<<=", ">>="};
+    if (cur().t == T::Op && assign.count(cur().s)) {
+      s->k = Stmt::Assign;
+      s->op = cur().s;
+      next();
+      s->e = e;
+      s->e2 = expr();
+      expect_op(";");
+      return s;
+    }
+    if (eat_op(";")) {
+      s->k = Stmt::ExprS;
+      s->e = e;
+      return s;
+    }
+    if (is_op("}")) {
+      last_expr_ = e;
+      return nullptr;
+    }
+    if (block_like(e)) {  // `if c { .. }` followed by more statements
+      s->k = Stmt::ExprS;
+      s->e = e;
+      return s;
+    }
+    fail("AE0002", cur().line, cur().col, "expected ';' after expression, found '" + cur().s + "'");
+  }
+
+  EP mk(Expr::K k, const Tok& at) {
+    auto e = std::make_shared<Expr>();
+    e->k = k;
+    e->line = at.line;
+    e->col = at.col;
+    return e;
+  }
+
+  EP expr() { return expr_prec(0); }
+  EP expr_nostruct() { return expr_prec(0); }
+
+  static int prec(const std::string& op) {
+    if (op == "||") return 1;
+    if (op == "&&") return 2;
+    if (op == "==" || op == "!=" || op == "<" || op == "<=" || op == ">" || op == ">=") return 3;
+    if (op == "|") return 4;
+    if (op == "^") return 5;
+    if (op == "&") return 6;
+    if (op == "<<" || op == ">>") return 7;
+    if (op == "+" || op == "-") return 8;
+    if (op == "*" || op == "/" || op == "%") return 9;
+    return -1;
+  }
+
+  EP expr_prec(int min) {
+    EP lhs = unary();
+    while (cur().t == T::Op) {
+      const std::string op = cur().s;
+      const int p = prec(op);
+      if (p < 0 || p < min) break;
+      const Tok at = cur();
+      next();
+      EP rhs = expr_prec(p + 1);
+      EP b = mk(Expr::Binary, at);
+      b->s = op;
+      b->a = {lhs, rhs};
+      lhs = b;
+    }
+    return lhs;
+  }
+
+  EP unary() {
+    const Tok at = cur();
+    if (eat_op("-") || eat_op("!")) {
+      EP e = mk(Expr::Unary, at);
+      e->s = at.s;
+      e->a = {unary()};
+      return e;
+    }
+    if (eat_op("&")) {
+      EP e = mk(Expr::Ref, at);
+      e->mut = eat_id("mut");
+      e->a = {unary()};
+      return e;
+    }
+    if (eat_op("*")) {  // dereference of a by-value binding: the value itself
+      return unary();
+    }
+    return cast_expr(postfix(primary()));
+  }
+
+  EP cast_expr(EP e) {
+    while (is_id("as")) {
+      const Tok at = cur();
+      next();
+      EP c = mk(Expr::Cast, at);
+      c->cast = type();
+      c->a = {e};
+      e = c;
+    }
+    return e;
+  }
+
+  EP postfix(EP e) {
+    for (;;) {
+      const Tok at = cur();
+      if (eat_op(".")) {
+        std::string m = ident();
+        EP c = mk(Expr::Method, at);
+        c->s = m;
+        c->a = {e};
+        expect_op("(");
+        while (!is_op(")")) {
+          c->a.push_back(expr());
+          if (!eat_op(",")) break;
+        }
+        expect_op(")");
+        e = c;
+      } else if (is_op("[")) {
+        next();
+        EP ix = mk(Expr::Index, at);
+        ix->a = {e, expr()};
+        expect_op("]");
+        e = ix;
+      } else {
+        return e;
+      }
+    }
+  }
+
+  EP primary() {
+    const Tok at = cur();
+    switch (at.t) {
+      case T::Int: {
+        next();
+        EP e = mk(Expr::Int, at);
+        e->s = at.s;
+        return e;
+      }
+      case T::Float: {
+        next();
+        EP e = mk(Expr::Float, at);
+        e->s = at.s;
+        return e;
+      }
+      case T::Str: {
+        next();
+        EP e = mk(Expr::Str, at);
+        e->s = at.s;
+        return e;
+      }
+      case T::Char: {
+        next();
+        EP e = mk(Expr::Char, at);
+        e->s = at.s;
+        return e;
+      }
+      default: break;
+    }
+    if (eat_op("(")) {
+      if (eat_op(")")) {
+        EP e = mk(Expr::BlockE, at);  // unit
+        e->blk = std::make_shared<Block>();
+        return e;
+      }
+      EP e = expr();
+      expect_op(")");
+      return e;
+    }
+    if (is_op("[")) {
+      next();
+      if (eat_op("]")) fail("AE0100", at.line, at.col, "empty array literal");
+      EP first = expr();
+      if (eat_op(";")) {
+        EP e = mk(Expr::ArrayRep, at);
+        e->a = {first, expr()};
+        expect_op("]");
+        return e;
+      }
+      EP e = mk(Expr::ArrayLit, at);
+      e->a = {first};
+      while (eat_op(",")) {
+        if (is_op("]")) break;
+        e->a.push_back(expr());
+      }
+      expect_op("]");
+      return e;
+    }
+    if (is_op("{")) {
+      EP e = mk(Expr::BlockE, at);
+      e->blk = block();
+      return e;
+    }
+    if (eat_id("if")) {
+      EP e = mk(Expr::If, at);
+      e->a = {expr_nostruct()};
+      e->blk = block();
+      if (eat_id("else")) {
+        if (is_id("if")) {
+          auto b = std::make_shared<Block>();
+          b->tail = primary();  // else if: the nested if is the else block's value
+          e->blk2 = b;
+        } else {
+          e->blk2 = block();
+        }
+      }
+      return e;
+    }
+    if (eat_id("unsafe")) {  // no borrow checker here: an unsafe block is a block
+      EP e = mk(Expr::BlockE, at);
+      e->blk = block();
+      return e;
+    }
+    if (eat_id("loop")) {
+      EP e = mk(Expr::LoopE, at);
+      e->blk = block();
+      return e;
+    }
+    if (eat_id("true") || eat_id("false")) {
+      EP e = mk(Expr::BoolL, at);
+      e->s = at.s;
+      return e;
+    }
+    if (at.t == T::Id) {
+      std::string name = ident();
+      while (is_op("::")) {  // paths: the last segment names the item
+        next();
+        name = ident();
+      }
+      if (eat_op("!")) fail("AE0100", at.line, at.col, "macros are not supported");
+      if (eat_op("(")) {
+        EP e = mk(Expr::Call, at);
+        e->s = name;
+        while (!is_op(")")) {
+          e->a.push_back(expr());
+          if (!eat_op(",")) break;
+        }
+        expect_op(")");
+        return e;
+      }
+      EP e = mk(Expr::Var, at);
+      e->s = name;
+      return e;
+    }
+    fail("AE0002", at.line, at.col, "unexpected '" + at.s + "'");
+  }
+};
+
+// ============================================================================ tensor method lowering
+// A method on a device tensor is one runtime call: (receiver, the call's
+// arguments in order, then the integers its shape recipe derives from the
+// receiver's and first argument's static shapes).
+struct MethodRule {
+  const char* fn;
+  int recipe;
+};
+enum Recipe { MKN_MATMUL, MKN_NT, MKN_TN, MKN_BWD_RHS, MKN_BWD_LHS, ROWS_COLS, NUMEL, MKN_2D };
+
+const std::map<std::string, MethodRule>& method_rules() {
+  static const std::map<std::string, MethodRule> m = {
+      {"matmul", {"aether_op_matmul_f32_cuda", MKN_MATMUL}},
+      {"matmul_gelu", {"aether_op_matmul_gelu_f32_cuda", MKN_2D}},
+      {"matmul_t", {"aether_op_matmul_nt_f32_cuda", MKN_NT}},
+      {"matmul_tn", {"aether_op_matmul_tn_f32_cuda", MKN_TN}},
+      {"matmul_backward_rhs", {"aether_op_matmul_backward_rhs_f32_cuda", MKN_BWD_RHS}},
+      {"matmul_backward_lhs", {"aether_op_matmul_backward_lhs_f32_cuda", MKN_BWD_LHS}},
+      {"cross_entropy", {"aether_op_cross_entropy_f32_cuda", ROWS_COLS}},
+      {"cross_entropy_backward", {"aether_op_cross_entropy_backward_f32_cuda", ROWS_COLS}},
+      {"softmax", {"aether_op_softmax_f32_cuda", ROWS_COLS}},
+      {"softmax_backward", {"aether_op_softmax_backward_f32_cuda", ROWS_COLS}},
+      {"softmax_backward_scaled", {"aether_op_softmax_backward_scaled_f32_cuda", ROWS_COLS}},
+      {"layer_norm", {"aether_op_layer_norm_f32_cuda", ROWS_COLS}},
+      {"add_layer_norm", {"aether_op_add_layer_norm_f32_cuda", ROWS_COLS}},
+      {"layer_norm_backward_dx", {"aether_op_layer_norm_backward_dx_f32_cuda", ROWS_COLS}},
+      {"layer_norm_backward_params", {"aether_op_layer_norm_backward_params_f32_cuda", ROWS_COLS}},
+      {"adamw_step", {"aether_op_adamw_step_f32_cuda", NUMEL}},
+      {"add", {"aether_op_add_f32_cuda", NUMEL}},
+      {"gelu", {"aether_op_gelu_f32_cuda", NUMEL}},
+      {"gelu_backward", {"aether_op_gelu_backward_f32_cuda", NUMEL}},
+      {"scale", {"aether_op_scale_f32_cuda", NUMEL}},
+  };
+  return m;
+}
+
+// ============================================================================ fusion peephole
+// `x.matmul(&w, &mut h); h.gelu(&mut h);` -> `x.matmul_gelu(&w, &mut h);`
+// (the intermediate is updated in place, so no later read can see the
+// unfused value). Applied to every block, nested blocks first.
+int fuse_block(Block& b);
+int fuse_expr(const EP& e) {
+  if (!e) return 0;
+  int n = 0;
+  if (e->blk) n += fuse_block(*e->blk);
+  if (e->blk2) n += fuse_block(*e->blk2);
+  for (auto& a : e->a) n += fuse_expr(a);
+  return n;
+}
+static std::string var_of(const EP& e) {
+  if (!e) return "";
+  if (e->k == Expr::Ref && !e->a.empty()) return var_of(e->a[0]);
+  return e->k == Expr::Var ? e->s : "";
+}
+int fuse_block(Block& b) {
+  int n = 0;
+  for (auto& s : b.stmts) {
+    if (s->body) n += fuse_block(*s->body);
+    n += fuse_expr(s->e) + fuse_expr(s->e2);
+  }
+  n += fuse_expr(b.tail);
+  for (size_t i = 0; i + 1 < b.stmts.size(); ++i) {
+    Stmt &s0 = *b.stmts[i], &s1 = *b.stmts[i + 1];
+    if (s0.k != Stmt::ExprS || s1.k != Stmt::ExprS || s0.e->k != Expr::Method || s1.e->k != Expr::Method) continue;
+    const Expr &m0 = *s0.e, &m1 = *s1.e;
+    if (m0.s != "matmul" || m1.s != "gelu" || m0.a.size() != 3 || m1.a.size() != 2) continue;
+    const std::string out = var_of(m0.a[2]);
+    if (out.empty() || var_of(m1.a[0]) != out || var_of(m1.a[1]) != out || m1.a[1]->k != Expr::Ref || !m1.a[1]->mut)
+      continue;
+    s0.e->s = "matmul_gelu";
+    b.stmts.erase(b.stmts.begin() + (long)i + 1);
+    ++n;
+  }
+  return n;
+}
+
+// ============================================================================ C code generation
+struct Local {
+  Ty ty;
+  std::string c;
+};
+struct FnSig {
+  std::vector<Ty> params;
+  Ty ret;
+  std::string c;
+  bool is_extern;
+};
+
+class Gen {
+ public:
+  Gen(Program& p, std::string stdlib_dir, std::string src_dir)
+      : p_(p), stdlib_(std::move(stdlib_dir)), srcdir_(std::move(src_dir)) {}
+
+  std::string run() {
+    for (auto& c : p_.consts) const_src_[c.name] = &c;
+    for (auto& f : p_.fns) declare(f);
+    std::ostringstream o;
+    o << "/* generated by aetherc */\n#include <stdint.h>\n#include <stdio.h>\n#include <math.h>\n\n";
+    o << "int64_t aether_dev_alloc_f32(int32_t);\nint64_t aether_dev_alloc_i32(int32_t);\n"
+         "int32_t aether_dev_free_f32(int64_t);\nint32_t aether_dev_free_i32(int64_t);\n";
+    o << "static void ae_drop_f32(int64_t* h) { if (*h > 0) aether_dev_free_f32(*h); }\n"
+         "static void ae_drop_i32(int64_t* h) { if (*h > 0) aether_dev_free_i32(*h); }\n\n";
+    std::set<std::string> pre = {"aether_dev_alloc_f32", "aether_dev_alloc_i32", "aether_dev_free_f32",
+                                 "aether_dev_free_i32"};
+    for (auto& kv : sigs_) {
+      const FnSig& s = kv.second;
+      if (!s.is_extern || pre.count(kv.first)) continue;
+      o << ctype(s.ret) << " " << s.c << "(" << plist(s) << ");\n";
+    }
+    o << "\n";
+    for (auto& c : p_.consts) {
+      Ty t = resolve(*c.ty);
+      o << "static const " << ctype(t) << " aec_" << c.name << " = " << lit_of(eval_const(c.e), t) << ";\n";
+    }
+    for (auto& f : p_.fns)
+      if (!f.is_extern) o << "static " << ctype(sigs_[f.name].ret) << " " << sigs_[f.name].c << "(" << plist(sigs_[f.name]) << ");\n";
+    o << "\n";
+    for (auto& f : p_.fns)
+      if (!f.is_extern) o << fn_def(f);
+    if (!sigs_.count("main") || sigs_["main"].is_extern) fail("AE0300", 1, 1, "program has no `fn main`");
+    const FnSig& m = sigs_["main"];
+    o << "int main(void) {\n";
+    if (m.ret.b == B::Void)
+      o << "  aef_main();\n  return 0;\n}\n";
+    else
+      o << "  return (int)aef_main();\n}\n";
+    return o.str();
+  }
+
+  // `use a::b;` loads <stdlib>/b.aether (or <source dir>/b.aether) and
+  // merges its extern declarations and constants.
+  static void resolve_uses(Program& p, const std::string& stdlib, const std::string& srcdir,
+                           std::set<std::string>& seen);
+
+ private:
+  Program& p_;
+  std::string stdlib_, srcdir_;
+  std::map<std::string, FnSig> sigs_;
+  std::map<std::string, const Const*> const_src_;
+  std::map<std::string, std::pair<Ty, double>> const_val_;
+  std::vector<std::map<std::string, Local>> scopes_;
+  Ty ret_;
+  int uniq_ = 0;
+  int indent_ = 1;
+
+  static std::string plist(const FnSig& s) {
+    if (s.params.empty()) return "void";
+    std::string r;
+    for (size_t i = 0; i < s.params.size(); ++i) r += (i ? ", " : "") + ctype(s.params[i]);
+    return r;
+  }
+
+  void declare(const Fn& f) {
+    FnSig s;
+    for (auto& p : f.params) s.params.push_back(resolve(*p.ty));
+    s.ret = f.ret ? resolve(*f.ret) : prim(B::Void);
+    s.is_extern = f.is_extern;
+    s.c = f.is_extern ? f.name : "aef_" + f.name;
+    auto it = sigs_.find(f.name);
+    if (it != sigs_.end()) {
+      if (f.is_extern && it->second.is_extern) return;  // the same extern declared twice (program + stdlib)
+      fail("AE0201", f.line, f.col, "function '" + f.name + "' is defined twice");
+    }
+    sigs_[f.name] = s;
+  }
+
+  // --------------------------------------------------------------- constants
+  std::pair<Ty, double> eval_const(const EP& e) {
+    switch (e->k) {
+      case Expr::Int: return {prim(B::I64), (double)std::stoll(e->s.substr(0, e->s.find('#')))};
+      case Expr::Float: return {prim(B::F32), std::stod(e->s.substr(0, e->s.find('#')))};
+      case Expr::BoolL: return {prim(B::Bool), e->s == "true" ? 1.0 : 0.0};
+      case Expr::Var: {
+        auto it = const_val_.find(e->s);
+        if (it != const_val_.end()) return it->second;
+        auto src = const_src_.find(e->s);
+        if (src == const_src_.end()) fail("AE0210", e->line, e->col, "'" + e->s + "' is not a constant");
+        const_val_[e->s] = {prim(B::Unknown), 0};  // cycle guard
+        auto v = eval_const(src->second->e);
+        v.first = resolve(*src->second->ty);
+        const_val_[e->s] = v;
+        return v;
+      }
+      case Expr::Unary: {
+        auto v = eval_const(e->a[0]);
+        if (e->s == "-") v.second = -v.second;
+        else v.second = v.second == 0;
+        return v;
+      }
+      case Expr::Cast: {
+        auto v = eval_const(e->a[0]);
+        v.first = resolve(*e->cast);
+        if (v.first.is_int()) v.second = (double)(int64_t)v.second;
+        return v;
+      }
+      case Expr::Binary: {
+        auto l = eval_const(e->a[0]), r = eval_const(e->a[1]);
+        const bool fl = l.first.is_float() || r.first.is_float();
+        const double a = l.second, b = r.second;
+        double v = 0;
+        const std::string& op = e->s;
+        if (op == "+") v = a + b;
+        else if (op == "-") v = a - b;
+        else if (op == "*") v = a * b;
+        else if (op == "/") {
+          if (b == 0) fail("AE0211", e->line, e->col, "division by zero in a constant");
+          v = fl ? a / b : (double)((int64_t)a / (int64_t)b);
+        } else if (op == "%") {
+          if (b == 0) fail("AE0211", e->line, e->col, "division by zero in a constant");
+          v = (double)((int64_t)a % (int64_t)b);
+        } else if (op == "<<") v = (double)((int64_t)a << (int64_t)b);
+        else if (op == ">>") v = (double)((int64_t)a >> (int64_t)b);
+        else if (op == "&") v = (double)((int64_t)a & (int64_t)b);
+        else if (op == "|") v = (double)((int64_t)a | (int64_t)b);
+        else if (op == "^") v = (double)((int64_t)a ^ (int64_t)b);
+        else fail("AE0210", e->line, e->col, "operator '" + op + "' is not allowed in a constant");
+        return {fl ? prim(B::F32) : l.first, v};
+      }
+      default: fail("AE0210", e->line, e->col, "not a constant expression");
+    }
+  }
+
+  static std::string lit_of(const std::pair<Ty, double>& v, const Ty& t) {
+    char buf[64];
+    if (t.is_float()) {
+      snprintf(buf, sizeof buf, "%.17g", v.second);
+      std::string s = buf;
+      if (s.find_first_of(".eEn") == std::string::npos) s += ".0";
+      return t.b == B::F32 ? "(float)" + s : s;
+    }
+    snprintf(buf, sizeof buf, "%lld", (long long)v.second);
+    return std::string(buf) + (t.b == B::I64 || t.b == B::U64 ? "LL" : "");
+  }
+
+  int64_t const_int(const EP& e) {
+    auto v = eval_const(e);
+    return (int64_t)v.second;
+  }
+
+  Ty resolve(const TyExpr& t) {
+    Ty r;
+    if (t.name == "()") return prim(B::Void);
+    if (t.name == "Tensor") {
+      r.b = B::Tensor;
+      if (t.elem == "f32") r.elem = B::F32;
+      else if (t.elem == "i32") r.elem = B::I32;
+      else fail("AE0220", t.line, t.col, "tensor elements must be f32 or i32");
+      for (auto& d : t.dims) {
+        const int64_t v = const_int(d);
+        if (v <= 0) fail("AE0221", t.line, t.col, "tensor dimensions must be positive");
+        r.dims.push_back(v);
+      }
+      return r;
+    }
+    if (t.name == "[]") {
+      r.b = B::Array;
+      r.inner = std::make_shared<Ty>(resolve(*t.inner));
+      r.len = const_int(t.dims[0]);
+      return r;
+    }
+    auto it = prim_names().find(t.name);
+    if (it == prim_names().end()) fail("AE0222", t.line, t.col, "unknown type '" + t.name + "'");
+    return prim(it->second);
+  }
+
+  // --------------------------------------------------------------- scopes
+  Local* lookup(const std::string& n) {
+    for (auto it = scopes_.rbegin(); it != scopes_.rend(); ++it) {
+      auto f = it->find(n);
+      if (f != it->end()) return &f->second;
+    }
+    return nullptr;
+  }
+  std::string bind(const std::string& n, const Ty& t) {
+    std::string c = n + "_" + std::to_string(++uniq_);
+    scopes_.back()[n] = {t, c};
+    return c;
+  }
+  std::string pad() const { return std::string(2 * indent_, ' '); }
+
+  // --------------------------------------------------------------- expressions
+  struct V {
+    std::string c;
+    Ty t;
+  };
+  static bool is_lit(const EP& e) {
+    return e->k == Expr::Int || e->k == Expr::Float || (e->k == Expr::Unary && e->s == "-" && is_lit(e->a[0]));
+  }
+
+  static std::string conv(const V& v, const Ty& to) {
+    if (to.b == B::Unknown || to.b == B::Void) return v.c;
+    if (v.t.b == to.b && to.b != B::Str) return v.c;
+    if (v.t.b == B::Str && (to.is_int())) return "((" + ctype(to) + ")(intptr_t)(" + v.c + "))";
+    if (v.t.b == B::Tensor && to.is_int()) return "((" + ctype(to) + ")(" + v.c + "))";
+    if (v.t.b == B::Array) return v.c;
+    return "((" + ctype(to) + ")(" + v.c + "))";
+  }
+
+  V gen(const EP& e, const Ty& hint) {
+    switch (e->k) {
+      case Expr::Int: {
+        const size_t h = e->s.find('#');
+        Ty t = hint.is_num() ? hint : prim(B::I64);
+        if (h != std::string::npos) t = prim(prim_names().at(e->s.substr(h + 1)));
+        const std::string num = e->s.substr(0, h);
+        if (t.is_float()) return {"((" + ctype(t) + ")" + num + ")", t};
+        return {"((" + ctype(t) + ")" + num + (t.b == B::I64 || t.b == B::U64 ? "LL" : "") + ")", t};
+      }
+      case Expr::Float: {
+        const size_t h = e->s.find('#');
+        Ty t = hint.b == B::F64 ? hint : prim(B::F32);
+        if (h != std::string::npos) t = prim(prim_names().at(e->s.substr(h + 1)));
+        std::string num = e->s.substr(0, h);
+        if (num.back() == '.') num += "0";
+        return {t.b == B::F32 ? num + "f" : num, t};
+      }
+      case Expr::BoolL: return {e->s == "true" ? "1" : "0", prim(B::Bool)};
+      case Expr::Char: return {"((uint8_t)" + e->s + ")", hint.is_int() ? hint : prim(B::U8)};
+      case Expr::Str: {
+        std::string s = "\"";
+        for (unsigned char c : e->s) {
+          if (c == '"' || c == '\\') s += '\\', s += (char)c;
+          else if (c == '\n') s += "\\n";
+          else if (c == '\t') s += "\\t";
+          else if (c < 32 || c >= 127) {
+            char b[8];
+            snprintf(b, sizeof b, "\\%03o", c);
+            s += b;
+          } else s += (char)c;
+        }
+        return {s + "\"", prim(B::Str)};
+      }
+      case Expr::Var: {
+        if (Local* l = lookup(e->s)) return {l->c, l->ty};
+        if (const_src_.count(e->s)) {
+          auto v = eval_const(e);
+          return {"aec_" + e->s, v.first};
+        }
+        fail("AE0210", e->line, e->col, "unknown name '" + e->s + "'");
+      }
+      case Expr::Unary: {
+        V a = gen(e->a[0], hint);
+        if (e->s == "!") return {"(!" + a.c + ")", prim(B::Bool)};  // `!` is a logical not (0 -> 1, else 0)
+        return {"(-" + a.c + ")", a.t};
+      }
+      case Expr::Ref: {
+        V a = gen(e->a[0], hint);
+        return a;  // tensors and scalars travel by value (a tensor's value is its handle)
+      }
+      case Expr::Cast: {
+        Ty to = resolve(*e->cast);
+        V a = gen(e->a[0], to);
+        return {"((" + ctype(to) + ")(" + a.c + "))", to};
+      }
+      case Expr::Binary: return binary(e, hint);
+      case Expr::Call: return call(e, hint);
+      case Expr::Method: return method(e);
+      case Expr::Index: {
+        V arr = gen(e->a[0], prim(B::Unknown));
+        if (arr.t.b != B::Array) fail("AE0230", e->line, e->col, "only arrays can be indexed");
+        V ix = gen(e->a[1], prim(B::I64));
+        return {arr.c + "[" + ix.c + "]", *arr.t.inner};
+      }
+      case Expr::If: {
+        V c = gen(e->a[0], prim(B::Bool));
+        std::string a = block_expr(*e->blk, hint);
+        Ty t = last_block_ty_;
+        if (!e->blk2) return {"({ if (" + c.c + ") " + a + "; })", prim(B::Void)};
+        std::string b = block_expr(*e->blk2, t.b != B::Void ? t : hint);
+        if (t.b == B::Void) t = last_block_ty_;
+        if (t.b == B::Void) return {"({ if (" + c.c + ") " + a + "; else " + b + "; })", t};
+        return {"((" + c.c + ") ? " + a + " : " + b + ")", t};
+      }
+      case Expr::BlockE: {
+        std::string s = block_expr(*e->blk, hint);
+        return {s, last_block_ty_};
+      }
+      case Expr::LoopE: {
+        std::ostringstream o;
+        o << "({ for (;;) ";
+        o << block_stmt(*e->blk);
+        o << " })";
+        return {o.str(), prim(B::Void)};
+      }
+      default: fail("AE0100", e->line, e->col, "array literals are only allowed as `let` initialisers");
+    }
+  }
+
+  V binary(const EP& e, const Ty& hint) {
+    const std::string& op = e->s;
+    const bool cmp = op == "==" || op == "!=" || op == "<" || op == "<=" || op == ">" || op == ">=";
+    const bool logic = op == "&&" || op == "||";
+    if (logic) {
+      V a = gen(e->a[0], prim(B::Bool)), b = gen(e->a[1], prim(B::Bool));
+      return {"(" + a.c + " " + op + " " + b.c + ")", prim(B::Bool)};
+    }
+    const bool shift = op == "<<" || op == ">>";
+    const Ty h = cmp ? prim(B::Unknown) : hint;
+    V a, b;
+    if (is_lit(e->a[0]) && !is_lit(e->a[1])) {
+      b = gen(e->a[1], h);
+      a = gen(e->a[0], shift ? h : b.t);
+    } else {
+      a = gen(e->a[0], h);
+      b = gen(e->a[1], shift ? prim(B::Unknown) : a.t);
+    }
+    Ty t = a.t;
+    if (!shift && a.t.is_num() && b.t.is_num() && a.t.b != b.t.b) {
+      // mixed operands: widen to the float / wider side, as the values compare
+      if (b.t.is_float() && !a.t.is_float()) t = b.t;
+      else if (a.t.is_float() == b.t.is_float() && (int)b.t.b > (int)a.t.b) t = b.t;
+    }
+    std::string ac = conv(a, t), bc = shift ? b.c : conv(b, t);
+    if (op == "%" && t.is_float())
+      return {(t.b == B::F32 ? "fmodf(" : "fmod(") + ac + ", " + bc + ")", t};
+    if (cmp) return {"(" + ac + " " + op + " " + bc + ")", prim(B::Bool)};
+    return {"((" + ctype(t) + ")(" + ac + " " + op + " " + bc + "))", t};
+  }
+
+  V call(const EP& e, const Ty& hint) {
+    const std::string& n = e->s;
+    auto one_arg = [&](const Ty& t) {
+      if (e->a.size() != 1) fail("AE0240", e->line, e->col, n + "() takes one argument");
+      return gen(e->a[0], t);
+    };
+    // casts written as calls
+    static const std::map<std::string, B> casts = {{"f32", B::F32}, {"f64", B::F64}, {"i32", B::I32},
+                                                   {"i64", B::I64}, {"u8", B::U8},   {"u32", B::U32},
+                                                   {"u64", B::U64}, {"i8", B::I8},   {"i16", B::I16}};
+    if (!sigs_.count(n) && casts.count(n)) {
+      Ty to = prim(casts.at(n));
+      V a = one_arg(to);
+      return {"((" + ctype(to) + ")(" + a.c + "))", to};
+    }
+    if (!sigs_.count(n) && (n == "println" || n == "print")) {
+      std::string fmt = n == "println" ? "\\n" : "";
+      if (e->a.empty()) return {"printf(\"" + fmt + "\")", prim(B::Void)};
+      V a = gen(e->a[0], prim(B::Unknown));
+      std::string f = a.t.b == B::Str ? "%s" : a.t.is_float() ? "%g" : "%lld";
+      std::string val = a.t.b == B::Str ? a.c : a.t.is_float() ? "(double)(" + a.c + ")" : "(long long)(" + a.c + ")";
+      return {"(printf(\"" + f + fmt + "\", " + val + "), fflush(stdout))", prim(B::Void)};
+    }
+    static const std::set<std::string> math = {"sqrt", "sin", "cos", "tan", "exp", "log", "abs", "floor", "ceil",
+                                               "tanh", "powf", "pow"};
+    if (!sigs_.count(n) && math.count(n)) {
+      if (n == "pow" || n == "powf") {
+        if (e->a.size() != 2) fail("AE0240", e->line, e->col, n + "() takes two arguments");
+        V a = gen(e->a[0], hint.is_float() ? hint : prim(B::F32));
+        V b = gen(e->a[1], a.t);
+        return {(a.t.b == B::F64 ? "pow(" : "powf(") + a.c + ", " + conv(b, a.t) + ")", a.t};
+      }
+      V a = one_arg(hint.is_float() ? hint : prim(B::F32));
+      if (a.t.is_int()) {
+        if (n == "abs") return {"((" + a.c + ") < 0 ? -(" + a.c + ") : (" + a.c + "))", a.t};
+        a = {"((float)(" + a.c + "))", prim(B::F32)};
+      }
+      const std::string cn = n == "abs" ? "fabs" : n;
+      return {(a.t.b == B::F32 ? cn + "f(" : cn + "(") + a.c + ")", a.t};
+    }
+    auto it = sigs_.find(n);
+    if (it == sigs_.end()) fail("AE0240", e->line, e->col, "unknown function '" + n + "'");
+    const FnSig& s = it->second;
+    if (s.params.size() != e->a.size())
+      fail("AE0241", e->line, e->col, "'" + n + "' takes " + std::to_string(s.params.size()) + " arguments, got " +
+                                           std::to_string(e->a.size()));
+    std::string args;
+    for (size_t i = 0; i < e->a.size(); ++i) {
+      V v = gen(e->a[i], s.params[i]);
+      if (v.t.b == B::Tensor && !s.params[i].is_int() && s.params[i].b != B::Tensor)
+        fail("AE0220", e->a[i]->line, e->a[i]->col, "a tensor passed where " + tyname(s.params[i]) + " is expected");
+      args += (i ? ", " : "") + conv(v, s.params[i]);
+    }
+    return {s.c + "(" + args + ")", s.ret};
+  }
+
+  V method(const EP& e) {
+    V r = gen(e->a[0], prim(B::Unknown));
+    if (r.t.b != B::Tensor)
+      fail("AE0250", e->line, e->col, "method '" + e->s + "' needs a Tensor receiver, not " + tyname(r.t));
+    auto it = method_rules().find(e->s);
+    if (it == method_rules().end()) fail("AE0251", e->line, e->col, "unknown tensor method '" + e->s + "'");
+    const MethodRule& rule = it->second;
+    std::vector<V> args;
+    std::vector<Ty> shapes;
+    for (size_t i = 1; i < e->a.size(); ++i) {
+      V v = gen(e->a[i], prim(B::Unknown));
+      args.push_back(v);
+      shapes.push_back(v.t);
+    }
+    const std::vector<int64_t>& s = r.t.dims;
+    auto arg_dims = [&](size_t k) -> const std::vector<int64_t>& {
+      if (k >= shapes.size() || shapes[k].b != B::Tensor)
+        fail("AE0252", e->line, e->col, e->s + ": argument " + std::to_string(k + 1) + " must be a Tensor");
+      return shapes[k].dims;
+    };
+    auto need2 = [&](const std::vector<int64_t>& d, const char* what) {
+      if (d.size() != 2) fail("AE0253", e->line, e->col, e->s + ": " + what + " must be 2-dimensional");
+    };
+    std::vector<int64_t> extra;
+    switch (rule.recipe) {
+      case MKN_MATMUL: {
+        const auto& w = arg_dims(0);
+        need2(w, "the weight");
+        if (s.size() == 2) extra = {s[0], s[1], w[1]};
+        else if (s.size() == 3) extra = {s[0] * s[1], s[2], w[1]};
+        else fail("AE0253", e->line, e->col, "matmul: the receiver must be 2- or 3-dimensional");
+        if (extra[1] != w[0]) fail("AE0254", e->line, e->col, "matmul: inner dimensions differ");
+        break;
+      }
+      case MKN_2D: {
+        const auto& w = arg_dims(0);
+        need2(s, "the receiver");
+        need2(w, "the weight");
+        extra = {s[0], s[1], w[1]};
+        break;
+      }
+      case MKN_NT: {
+        const auto& k = arg_dims(0);
+        need2(s, "the receiver");
+        need2(k, "the right operand");
+        extra = {s[0], s[1], k[0]};
+        break;
+      }
+      case MKN_TN: {
+        const auto& b = arg_dims(0);
+        need2(s, "the receiver");
+        need2(b, "the right operand");
+        extra = {s[1], s[0], b[1]};
+        break;
+      }
+      case MKN_BWD_RHS: {
+        const auto& dy = arg_dims(0);
+        need2(s, "the receiver");
+        need2(dy, "dy");
+        extra = {s[0], s[1], dy[1]};
+        break;
+      }
+      case MKN_BWD_LHS: {
+        const auto& w = arg_dims(0);
+        need2(s, "the receiver");
+        need2(w, "the weight");
+        extra = {s[0], w[0], s[1]};
+        break;
+      }
+      case ROWS_COLS:
+        need2(s, "the receiver");
+        extra = {s[0], s[1]};
+        break;
+      case NUMEL: extra = {r.t.numel()}; break;
+    }
+    // the runtime signature types the user's arguments and the appended shape ints
+    auto sit = sigs_.find(rule.fn);
+    std::string call = std::string(rule.fn) + "(" + r.c;
+    Ty ret = prim(B::I32);
+    if (sit != sigs_.end()) {
+      const FnSig& fs = sit->second;
+      ret = fs.ret;
+      if (fs.params.size() != 1 + args.size() + extra.size())
+        fail("AE0241", e->line, e->col, "tensor method '" + e->s + "' lowers to " + rule.fn + ", which takes " +
+                                            std::to_string(fs.params.size()) + " arguments; the call supplies " +
+                                            std::to_string(1 + args.size() + extra.size()));
+      for (size_t i = 0; i < args.size(); ++i) {
+        V v = args[i];
+        if (is_lit(e->a[i + 1])) v = gen(e->a[i + 1], fs.params[i + 1]);
+        call += ", " + conv(v, fs.params[i + 1]);
+      }
+    } else {
+      used_undeclared_.insert(rule.fn);
+      for (auto& v : args) call += ", " + v.c;
+    }
+    for (int64_t x : extra) call += ", " + std::to_string(x);
+    return {call + ")", ret};
+  }
+
+  std::set<std::string> used_undeclared_;
+  Ty last_block_ty_;
+
+  // A block as a GNU statement expression; its type lands in last_block_ty_.
+  std::string block_expr(const Block& b, const Ty& hint) {
+    scopes_.emplace_back();
+    std::ostringstream o;
+    o << "({ ";
+    ++indent_;
+    for (auto& s : b.stmts) o << stmt(*s) << " ";
+    Ty t = prim(B::Void);
+    if (b.tail) {
+      V v = gen(b.tail, hint);
+      t = v.t;
+      o << v.c << "; ";
+    }
+    --indent_;
+    o << "})";
+    scopes_.pop_back();
+    last_block_ty_ = t;
+    return o.str();
+  }
+
+  std::string block_stmt(const Block& b) {
+    scopes_.emplace_back();
+    std::ostringstream o;
+    o << "{\n";
+    ++indent_;
+    for (auto& s : b.stmts) o << pad() << stmt(*s) << "\n";
+    if (b.tail) {
+      V v = gen(b.tail, prim(B::Unknown));
+      o << pad() << v.c << ";\n";
+    }
+    --indent_;
+    o << pad() << "}";
+    scopes_.pop_back();
+    return o.str();
+  }
+
+  // --------------------------------------------------------------- statements
+  std::string stmt(const Stmt& s) {
+    switch (s.k) {
+      case Stmt::Let: return let(s);
+      case Stmt::ExprS: {
+        V v = gen(s.e, prim(B::Unknown));
+        return v.c + ";";
+      }
+      case Stmt::Assign: {
+        V lhs = gen(s.e, prim(B::Unknown));
+        if (s.e->k != Expr::Var && s.e->k != Expr::Index)
+          fail("AE0260", s.line, s.col, "can only assign to a variable or an array element");
+        if (lhs.t.b == B::Tensor) fail("AE0261", s.line, s.col, "tensor bindings cannot be reassigned");
+        V rhs = gen(s.e2, lhs.t);
+        if (s.op == "%=" && lhs.t.is_float())
+          return lhs.c + " = " + (lhs.t.b == B::F32 ? "fmodf(" : "fmod(") + lhs.c + ", " + conv(rhs, lhs.t) + ");";
+        return lhs.c + " " + s.op + " " + conv(rhs, lhs.t) + ";";
+      }
+      case Stmt::While: {
+        V c = gen(s.e, prim(B::Bool));
+        return "while (" + c.c + ") " + block_stmt(*s.body);
+      }
+      case Stmt::Loop: return "for (;;) " + block_stmt(*s.body);
+      case Stmt::For: {
+        V a = gen(s.e, prim(B::Unknown));
+        V b = gen(s.e2, a.t);
+        Ty t = a.t.is_int() ? a.t : prim(B::I64);
+        scopes_.emplace_back();
+        const std::string iv = bind(s.name, t), lim = "lim_" + std::to_string(++uniq_);
+        std::string r = "for (" + ctype(t) + " " + iv + " = " + conv(a, t) + ", " + lim + " = " + conv(b, t) + "; " + iv +
+                        (s.inclusive ? " <= " : " < ") + lim + "; ++" + iv + ") " + block_stmt(*s.body);
+        scopes_.pop_back();
+        return r;
+      }
+      case Stmt::Return: {
+        if (!s.e) return ret_.b == B::Void ? "return;" : "return 0;";
+        V v = gen(s.e, ret_);
+        return "return " + conv(v, ret_) + ";";
+      }
+      case Stmt::Break: return "break;";
+      case Stmt::Continue: return "continue;";
+    }
+    return "";
+  }
+
+  std::string let(const Stmt& s) {
+    if (s.name == "_" && s.e && !s.ty) {  // `let _ = e;` evaluates e and drops the value
+      V v = gen(s.e, prim(B::Unknown));
+      return "(void)(" + v.c + ");";
+    }
+    if (s.ty && s.ty->name == "Tensor") {
+      if (s.e) fail("AE0270", s.line, s.col, "a Tensor binding is allocated by its declaration and takes no initialiser");
+      Ty t = resolve(*s.ty);
+      const std::string c = bind(s.name, t);
+      const bool f = t.elem == B::F32;
+      return std::string("int64_t ") + c + " __attribute__((cleanup(" + (f ? "ae_drop_f32" : "ae_drop_i32") + "))) = " +
+             (f ? "aether_dev_alloc_f32(" : "aether_dev_alloc_i32(") + std::to_string(t.numel()) + ");";
+    }
+    Ty t = s.ty ? resolve(*s.ty) : prim(B::Unknown);
+    if (t.b == B::Array && !s.e) {  // zero-filled
+      const std::string c = bind(s.name, t);
+      return ctype(*t.inner) + " " + c + "[" + std::to_string(t.len) + "] = {0};";
+    }
+    if (t.b == B::Array || (s.e && (s.e->k == Expr::ArrayLit || s.e->k == Expr::ArrayRep))) {
+      Ty el = t.b == B::Array ? *t.inner : prim(B::Unknown);
+      std::vector<std::string> vals;
+      std::string rep_val, rep_len;
+      int64_t len = 0;
+      if (s.e->k == Expr::ArrayLit) {
+        for (auto& x : s.e->a) {
+          V v = gen(x, el);
+          if (el.b == B::Unknown) el = v.t;
+          vals.push_back(conv(v, el));
+        }
+        len = (int64_t)vals.size();
+      } else if (s.e->k == Expr::ArrayRep) {
+        V v = gen(s.e->a[0], el);
+        if (el.b == B::Unknown) el = v.t;
+        rep_val = conv(v, el);
+        len = const_int(s.e->a[1]);
+      } else {
+        fail("AE0271", s.line, s.col, "arrays are initialised from an array literal");
+      }
+      if (t.b == B::Array && t.len != len) fail("AE0220", s.line, s.col, "array length does not match its type");
+      Ty at;
+      at.b = B::Array;
+      at.inner = std::make_shared<Ty>(el);
+      at.len = len;
+      const std::string c = bind(s.name, at);
+      std::string r = ctype(el) + " " + c + "[" + std::to_string(len) + "]";
+      if (!vals.empty()) {
+        r += " = {";
+        for (size_t i = 0; i < vals.size(); ++i) r += (i ? ", " : "") + vals[i];
+        return r + "};";
+      }
+      const std::string k = "i_" + std::to_string(++uniq_);
+      return r + "; for (int64_t " + k + " = 0; " + k + " < " + std::to_string(len) + "; ++" + k + ") " + c + "[" + k +
+             "] = " + rep_val + ";";
+    }
+    std::string init;
+    if (s.e) {
+      V v = gen(s.e, t);
+      if (t.b == B::Unknown) t = v.t;
+      if (v.t.b == B::Tensor && t.b == B::Tensor)
+        fail("AE0272", s.line, s.col, "a Tensor binding cannot be copied (use the original binding)");
+      if (t.b == B::Void) fail("AE0273", s.line, s.col, "binding has no value");
+      init = conv(v, t);
+    } else {
+      if (t.b == B::Unknown) fail("AE0274", s.line, s.col, "a binding without initialiser needs a type");
+      init = t.is_float() ? "0" : "0";
+    }
+    const std::string c = bind(s.name, t);
+    return ctype(t) + " " + c + " = " + init + ";";
+  }
+
+  std::string fn_def(const Fn& f) {
+    const FnSig& sig = sigs_[f.name];
+    ret_ = sig.ret;
+    scopes_.clear();
+    scopes_.emplace_back();
+    std::string params;
+    for (size_t i = 0; i < f.params.size(); ++i) {
+      const std::string c = bind(f.params[i].name, sig.params[i]);
+      params += (i ? ", " : "") + ctype(sig.params[i]) + " " + c;
+    }
+    if (params.empty()) params = "void";
+    std::ostringstream o;
+    o << "static " << ctype(sig.ret) << " " << sig.c << "(" << params << ") {\n";
+    indent_ = 1;
+    const Block& b = *f.body;
+    for (auto& s : b.stmts) o << pad() << stmt(*s) << "\n";
+    if (b.tail) {
+      V v = gen(b.tail, ret_);
+      if (ret_.b == B::Void) o << pad() << v.c << ";\n";
+      else o << pad() << "return " << conv(v, ret_) << ";\n";
+    } else if (ret_.b != B::Void) {
+      o << pad() << "return 0;\n";
+    }
+    o << "}\n\n";
+    return o.str();
+  }
+};
+
+bool read_file(const std::string& path, std::string& out) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return false;
+  std::ostringstream s;
+  s << f.rdbuf();
+  out = s.str();
+  return true;
+}
+
+void Gen::resolve_uses(Program& p, const std::string& stdlib, const std::string& srcdir,
+                       std::set<std::string>& seen) {
+  std::vector<std::string> uses = p.uses;
+  for (const std::string& u : uses) {
+    const std::string leaf = u.substr(u.rfind(':') == std::string::npos ? 0 : u.rfind(':') + 1);
+    if (seen.count(leaf)) continue;
+    seen.insert(leaf);
+    std::string text;
+    if (!read_file(stdlib + "/" + leaf + ".aether", text) && !read_file(srcdir + "/" + leaf + ".aether", text) &&
+        !read_file(srcdir + "/_" + leaf + ".aether", text))
+      fail("AE0400", 1, 1, "cannot find module '" + u + "'");
+    Parser ps(lex(text));
+    Program m = ps.program();
+    resolve_uses(m, stdlib, srcdir, seen);
+    for (auto& f : m.fns) p.fns.push_back(f);
+    for (auto& c : m.consts) {
+      bool dup = false;
+      for (auto& e : p.consts) dup |= e.name == c.name;
+      if (!dup) p.consts.push_back(c);
+    }
+  }
+}
+
+// ============================================================================ AST dump
+void dump_expr(std::ostream& o, const EP& e);
+void dump_block(std::ostream& o, const Block& b) {
+  o << "(block";
+  for (auto& s : b.stmts) {
+    o << " (" << (s->k == Stmt::Let ? "let " + s->name : s->k == Stmt::Assign ? "assign" + s->op
+                : s->k == Stmt::While ? "while" : s->k == Stmt::For ? "for " + s->name
+                : s->k == Stmt::Return ? "return" : s->k == Stmt::Break ? "break" : s->k == Stmt::Continue ? "continue"
+                : "expr");
+    if (s->e) o << " ", dump_expr(o, s->e);
+    if (s->e2) o << " ", dump_expr(o, s->e2);
+    if (s->body) o << " ", dump_block(o, *s->body);
+    o << ")";
+  }
+  if (b.tail) o << " (tail ", dump_expr(o, b.tail), o << ")";
+  o << ")";
+}
+void dump_expr(std::ostream& o, const EP& e) {
+  static const char* names[] = {"int", "float", "bool", "str", "char", "var", "unary", "binary", "call", "method",
+                                "cast", "ref", "if", "block", "index", "array", "array-repeat", "loop"};
+  o << "(" << names[e->k];
+  if (!e->s.empty()) o << " " << e->s;
+  for (auto& a : e->a) o << " ", dump_expr(o, a);
+  if (e->blk) o << " ", dump_block(o, *e->blk);
+  if (e->blk2) o << " ", dump_block(o, *e->blk2);
+  o << ")";
+}
+
+}  // namespace ae
+
+// ============================================================================ driver
+namespace {
+std::string dirname_of(const std::string& p) {
+  const size_t s = p.rfind('/');
+  return s == std::string::npos ? "." : p.substr(0, s);
+}
+std::string self_dir() {
+  char buf[4096];
+  const ssize_t n = readlink("/proc/self/exe", buf, sizeof buf - 1);
+  if (n <= 0) return ".";
+  buf[n] = 0;
+  return dirname_of(buf);
+}
+std::string json_escape(const std::string& s) {
+  std::string r;
+  for (char c : s) {
+    if (c == '"' || c == '\\') r += '\\', r += c;
+    else if (c == '\n') r += "\\n";
+    else r += c;
+  }
+  return r;
+}
+void usage() {
+  std::puts(
+      "aetherc - compiler for Aether programs against the aether_b200 C-ABI runtime\n\n"
+      "USAGE:\n"
+      "  aetherc <input.aether> [-o <out>] [--emit=bin|c|ast|tokens] [--check] [--json-errors]\n"
+      "          [--no-fuse] [--O0|--O1|--O2] [--stdlib <dir>] [--libdir <dir>] [--cc <compiler>]\n\n"
+      "--emit=bin     lower to C, compile with the C compiler and link libaether_rt / libaether_dev (default)\n"
+      "--emit=c       write the generated C\n"
+      "--emit=ast     write the parsed program as an S-expression\n"
+      "--check        parse and type-check only\n"
+      "--no-fuse      keep `matmul` + in-place `gelu` as two runtime calls\n"
+      "The reference's other emit kinds (mir, llvm-ir, asm, asm-bin, aether-bin, pe-bin) are not produced.");
+}
+}  // namespace
+
+int main(int argc, char** argv) {
+  std::string input, output, emit = "bin", stdlib, libdir, cc = "cc", opt = "-O2";
+  bool check = false, json = false, fuse = true;
+  for (int i = 1; i < argc; ++i) {
+    const std::string a = argv[i];
+    if (a == "-o" && i + 1 < argc) output = argv[++i];
+    else if (a.rfind("--emit=", 0) == 0) emit = a.substr(7);
+    else if (a == "--check") check = true;
+    else if (a == "--json-errors") json = true;
+    else if (a == "--no-fuse") fuse = false;
+    else if (a == "--O0") opt = "-O0";
+    else if (a == "--O1") opt = "-O1";
+    else if (a == "--O2") opt = "-O2";
+    else if (a == "--stdlib" && i + 1 < argc) stdlib = argv[++i];
+    else if (a == "--libdir" && i + 1 < argc) libdir = argv[++i];
+    else if (a == "--cc" && i + 1 < argc) cc = argv[++i];
+    else if (a == "-h" || a == "--help") {
+      usage();
+      return 0;
+    } else if (a == "--version") {
+      std::puts("aetherc (aether_b200) 0.2");
+      return 0;
+    } else if (!a.empty() && a[0] != '-') input = a;
+    else {
+      std::fprintf(stderr, "aetherc: unknown argument %s\n", a.c_str());
+      return 2;
+    }
+  }
+  if (input.empty()) {
+    usage();
+    return 2;
+  }
+  const std::string here = self_dir();
+  if (stdlib.empty()) stdlib = here + "/../aetherc_stdlib";
+  if (libdir.empty()) libdir = here + "/..";
+  static const std::set<std::string> kinds = {"bin", "c", "ast", "tokens"};
+  if (!kinds.count(emit)) {
+    std::fprintf(stderr, "aetherc: --emit=%s is not produced by this compiler (bin, c, ast, tokens)\n", emit.c_str());
+    return 2;
+  }
+  std::string src;
+  if (!ae::read_file(input, src)) {
+    std::fprintf(stderr, "aetherc: cannot read %s\n", input.c_str());
+    return 2;
+  }
+  try {
+    std::vector<ae::Tok> toks = ae::lex(src);
+    if (emit == "tokens") {
+      for (auto& t : toks) std::printf("%d:%d %s\n", t.line, t.col, t.s.c_str());
+      return 0;
+    }
+    ae::Parser ps(toks);
+    ae::Program prog = ps.program();
+    if (emit == "ast") {
+      std::ostringstream o;
+      for (auto& f : prog.fns) {
+        o << "(fn " << f.name;
+        if (f.body) o << " ", ae::dump_block(o, *f.body);
+        o << ")\n";
+      }
+      if (output.empty()) std::fputs(o.str().c_str(), stdout);
+      else std::ofstream(output) << o.str();
+      return 0;
+    }
+    int fused = 0;
+    if (fuse)
+      for (auto& f : prog.fns)
+        if (f.body) fused += ae::fuse_block(*f.body);
+    std::set<std::string> seen;
+    ae::Gen::resolve_uses(prog, stdlib, dirname_of(input), seen);
+    ae::Gen g(prog, stdlib, dirname_of(input));
+    const std::string c = g.run();
+    if (check) return 0;
+    if (emit == "c") {
+      if (output.empty()) std::fputs(c.c_str(), stdout);
+      else std::ofstream(output) << c;
+      if (fused) std::fprintf(stderr, "aetherc: fused %d matmul+gelu pair(s)\n", fused);
+      return 0;
+    }
+    if (output.empty()) {
+      output = input;
+      const size_t dot = output.rfind(".aether");
+      if (dot != std::string::npos) output = output.substr(0, dot);
+    }
+    const std::string tmp = output + ".aetherc.c";
+    std::ofstream(tmp) << c;
+    const std::string cmd = cc + " " + opt + " -w -o '" + output + "' '" + tmp + "' -L'" + libdir +
+                            "' -Wl,--no-as-needed -laether_rt -Wl,--as-needed -laether_dev -Wl,--no-as-needed -lm "
+                            "-Wl,-rpath,'" + libdir + "'";
+    const int rc = std::system(cmd.c_str());
+    std::remove(tmp.c_str());
+    if (rc != 0) {
+      std::fprintf(stderr, "aetherc: C compiler failed (%s)\n", cmd.c_str());
+      return 1;
+    }
+    return 0;
+  } catch (const ae::Diag& d) {
+    if (json)
+      std::fprintf(stderr, "{\"code\":\"%s\",\"file\":\"%s\",\"line\":%d,\"col\":%d,\"message\":\"%s\"}\n",
+                   d.code.c_str(), json_escape(input).c_str(), d.line, d.col, json_escape(d.what()).c_str());
+    else
+      std::fprintf(stderr, "%s:%d:%d: error[%s]: %s\n", input.c_str(), d.line, d.col, d.code.c_str(), d.what());
+    return 1;
+  }
+}
