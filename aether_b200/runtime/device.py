@@ -10,7 +10,7 @@
     d.download(c, (4, 2))
 
 Every op checks its handles' kinds and sizes and returns -1 instead of
-launching when they do not fit; -2 means a CUDA or cuBLAS error, whose text
+launching when they do not fit; -2 means a CUDA error, whose text
 ``last_error()`` returns.
 
 Reference: the i64-handle device ABI of runtime/src/cuda.rs:7230-11760.

@@ -8,14 +8,15 @@
 // none of the reference's machinery:
 //   * one handle table for every element kind (f32 / i32 / u8), each entry
 //     holding a stream-ordered allocation (cudaMallocAsync) and its device;
-//   * a context per device (stream, cuBLAS handle, captured graph) instead of
+//   * a context per device (stream, GEMM scratch, captured graph) instead of
 //     one global device-0 context, so several GPUs can be driven from one
 //     process (aether_dev_set_device);
 //   * every op checks each handle's kind and that the extents it is about to
 //     touch fit the allocation, and returns -1 instead of launching;
-//   * ahead-of-time sm_100a kernels (no runtime compilation). GEMMs are plain
-//     f32 library GEMMs (cuBLAS, row-major through the transposed view; TF32
-//     tensor cores with AETHER_DEV_TF32=1); everything else is a kernel in
+//   * ahead-of-time sm_100a kernels (no runtime compilation, no cuBLAS). The
+//     f32 GEMM family runs on the tcgen05 tensor cores (kind::tf32 with a
+//     three-term hi / lo split for fp32-class accuracy) above ~96^3 and on a
+//     tiled SIMT kernel below; everything else is a kernel in
 //     this file: one CTA per row with shuffle reductions for norms / softmax /
 //     cross-entropy, column-tiled deterministic reductions for parameter
 //     gradients, and quantised mat-vecs that dequantise GGUF blocks in
@@ -25,8 +26,8 @@
 // training ops, graphs, sync), 8442-8480 (RoPE), 10185-10380 (GQA, embedding,
 // SiLU, transpose, in-place ops), 10388-11120 (dequant and fused quantised
 // mat-vecs), 11553 (d2d), 11609-11680 (KV append and one-token attention).
-#include <cublas_v2.h>
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <nccl.h>
 
@@ -39,6 +40,8 @@
 #include <mutex>
 #include <algorithm>
 #include <vector>
+
+#include "../common.cuh"  // tcgen05 / TMA / mbarrier shims (header-only)
 
 #define AE_API extern "C" __attribute__((visibility("default")))
 
@@ -56,10 +59,22 @@ struct Buf {
 struct Ctx {
   bool ready = false;
   cudaStream_t s = nullptr;
-  cublasHandle_t blas = nullptr;
+  float* ws = nullptr;  // split-operand scratch of the f32 GEMM
+  size_t ws_floats = 0;
+  int* status = nullptr;  // bounded-wait status word of this device's kernels
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
 };
+
+// IQ3 codebooks (format data, shared with the host dequantisers), copied to
+// every device when its context is created: global memory rather than
+// __constant__, since the lanes of a warp index different entries and
+// constant-cache reads of different addresses serialise.
+namespace iq3 {
+#include "iq3_grids.inc"
+}
+__device__ uint32_t g_iq3xxs_grid[256];
+__device__ uint32_t g_iq3s_grid[512];
 
 constexpr int kMaxDev = 64;
 std::mutex g_mu;
@@ -89,13 +104,11 @@ Ctx* ctx_for(int d) {
     set_err("stream", e);
     return nullptr;
   }
-  if (cublasCreate(&c.blas) != CUBLAS_STATUS_SUCCESS) {
-    snprintf(g_err, sizeof(g_err), "cublasCreate failed");
+  if ((e = cudaMemcpyToSymbol(g_iq3xxs_grid, iq3::IQ3XXS_GRID, sizeof(iq3::IQ3XXS_GRID))) != cudaSuccess ||
+      (e = cudaMemcpyToSymbol(g_iq3s_grid, iq3::IQ3S_GRID, sizeof(iq3::IQ3S_GRID))) != cudaSuccess) {
+    set_err("IQ3 codebooks", e);
     return nullptr;
   }
-  cublasSetStream(c.blas, c.s);
-  const char* tf32 = getenv("AETHER_DEV_TF32");
-  cublasSetMathMode(c.blas, (tf32 && tf32[0] == '1') ? CUBLAS_TF32_TENSOR_OP_MATH : CUBLAS_DEFAULT_MATH);
   c.ready = true;
   return &c;
 }
@@ -569,7 +582,7 @@ __global__ void k_attn_seq1(const float* q, const float* kc, const float* vc, fl
 // ---------------------------------------------------------------------------------------------- GGUF blocks
 // Element types by their GGML numbers; block = (elements, bytes).
 enum Q { TF32 = 0, TF16 = 1, TQ4_0 = 2, TQ5_0 = 6, TQ8_0 = 8, TQ3_K = 11, TQ4_K = 12, TQ5_K = 13, TQ6_K = 14,
-         TIQ4_NL = 20, TIQ4_XS = 23 };
+         TIQ3_XXS = 18, TIQ4_NL = 20, TIQ3_S = 21, TIQ4_XS = 23 };
 
 bool block_of(int t, int* ne, int* nb) {
   switch (t) {
@@ -584,11 +597,14 @@ bool block_of(int t, int* ne, int* nb) {
     case TQ5_K: *ne = 256; *nb = 176; return true;
     case TQ6_K: *ne = 256; *nb = 210; return true;
     case TIQ4_XS: *ne = 256; *nb = 136; return true;
+    case TIQ3_XXS: *ne = 256; *nb = 98; return true;
+    case TIQ3_S: *ne = 256; *nb = 110; return true;
     default: return false;
   }
 }
 
 __constant__ float c_iq4[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
 
 __device__ __forceinline__ float h2f(const uint8_t* p) {
   __half_raw r;
@@ -697,6 +713,44 @@ __device__ __forceinline__ void chunk32(const uint8_t* row, int c, float* v) {
       const int q = ((qs[i] >> (2 * sh)) & 3) - ((hm[i] & m) ? 0 : 4);
       v[i] = d * scl[i >> 4] * (float)q;
     }
+  } else if constexpr (T == TIQ3_XXS) {
+    // 32 values: 8 codebook indices (4 magnitudes each), one u32 with a 4-bit
+    // scale and four 7-bit sign-pattern indices (index + parity bit = 8 signs)
+    const int j = c & 7;
+    const uint8_t* b = row + (size_t)(c >> 3) * 98;
+    const float d = h2f(b);
+    const uint8_t* qs = b + 2 + 8 * j;
+    const uint32_t aux = b[66 + 4 * j] | (b[67 + 4 * j] << 8) | (b[68 + 4 * j] << 16) | ((uint32_t)b[69 + 4 * j] << 24);
+    const float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t i7 = (aux >> (7 * g)) & 127;
+      const uint32_t sg = i7 | ((__popc(i7) & 1) << 7);
+      const uint32_t e0 = __ldg(&g_iq3xxs_grid[qs[2 * g]]), e1 = __ldg(&g_iq3xxs_grid[qs[2 * g + 1]]);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float mag = (float)(((t < 4 ? e0 : e1) >> (8 * (t & 3))) & 0xff);
+        v[8 * g + t] = db * mag * ((sg >> t) & 1 ? -1.f : 1.f);
+      }
+    }
+  } else if constexpr (T == TIQ3_S) {
+    // 32 values: 8 nine-bit codebook indices (low bytes + one high-bit byte),
+    // 4 explicit sign bytes, one 4-bit scale d * (1 + 2 s)
+    const int j = c & 7;
+    const uint8_t* b = row + (size_t)(c >> 3) * 110;
+    const float d = h2f(b);
+    const uint8_t *qs = b + 2 + 8 * j, qh = b[66 + j], *sg = b + 74 + 4 * j;
+    const float db = d * (float)(1 + 2 * ((b[106 + j / 2] >> (4 * (j & 1))) & 15));
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t e0 = __ldg(&g_iq3s_grid[qs[2 * g] | (((qh >> (2 * g)) & 1) << 8)]);
+      const uint32_t e1 = __ldg(&g_iq3s_grid[qs[2 * g + 1] | (((qh >> (2 * g + 1)) & 1) << 8)]);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float mag = (float)(((t < 4 ? e0 : e1) >> (8 * (t & 3))) & 0xff);
+        v[8 * g + t] = db * mag * ((sg[g] >> t) & 1 ? -1.f : 1.f);
+      }
+    }
   } else if constexpr (T == TIQ4_XS) {
     const int j = c & 7;
     const uint8_t* b = row + (size_t)(c >> 3) * 136;
@@ -720,7 +774,8 @@ __global__ void k_dequant_flat(const uint8_t* w, float* out, size_t chunks) {
   size_t c = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (c >= chunks) return;
   float v[32];
-  if constexpr (T == TQ4_K || T == TQ5_K || T == TQ6_K || T == TQ3_K || T == TIQ4_XS) {
+  if constexpr (T == TQ4_K || T == TQ5_K || T == TQ6_K || T == TQ3_K || T == TIQ4_XS || T == TIQ3_XXS ||
+                T == TIQ3_S) {
     chunk32<T>(w, (int)c, v);  // super-block c / 8, sub-block c % 8
   } else {
     const int nb = T == TQ8_0 ? 34 : T == TQ5_0 ? 22 : 18;  // one 32-value block per chunk
@@ -792,23 +847,322 @@ __global__ void k_matvec(MV p) {
 }
 
 // ---------------------------------------------------------------------------------------------- GEMM
-// Row-major C[M,N] = alpha op(A) op(B) + beta C through cuBLAS's column-major
-// view (C^T = op(B)^T op(A)^T, the row-major buffers read as their transposes).
+// Row-major C[M,N] = alpha op(A)[M,K] op(B)[K,N] + beta C, strided-batched, in
+// fp32 -- the contract of the reference's cuBLAS sgemm family
+// (runtime/src/cuda.rs:7419-7760). Two kernels of this library, no cuBLAS:
+//   * large problems: a tcgen05 kernel of kind::tf32 with the three-term
+//     split x = hi + lo (hi = tf32(x), lo = tf32(x - hi)) and
+//     C = A_hi B_hi + A_lo B_hi + A_hi B_lo accumulated in TMEM, which keeps
+//     fp32-class accuracy (the dropped A_lo B_lo term is ~2^-22 relative).
+//     A pre-pass writes the hi / lo parts K-major and zero-padded to whole
+//     128 x 32 tiles, so every TMA box is in bounds and transposed operands
+//     need no second kernel; 128 x 128 output tile per CTA, 3-stage TMA ring,
+//     one thread issues the MMAs, four warps read TMEM back;
+//   * small problems: a 32 x 32-tiled SIMT kernel with fp32 FMAs.
+namespace tfg {
+constexpr int BM = 128, BN = 128, BK = 32;  // BK fp32 = 128 bytes: one 128B-swizzle row
+constexpr int STAGES = 3;
+constexpr int TILE = BM * BK * 4;           // 16 KB
+constexpr int STAGE_BYTES = 4 * TILE;       // A hi, A lo, B hi, B lo
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t kIdesc = (1u << 4)                // D: F32
+                            | (2u << 7) | (2u << 10)  // A, B: TF32 (both K-major)
+                            | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+struct Args {
+  float* C;
+  long long ldc, sC;
+  int M, N, K, kb;  // kb: K blocks of BK
+  int Mp, Np;       // padded rows of the split operands
+  float alpha, beta;
+  int* status;
+};
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// dst[(b * 2 + part) * rows_p * Kp + r * Kp + k] = part 0: tf32(x), part 1:
+// tf32(x - tf32(x)), x = op(src)[r][k] of batch b (0 outside the real shape).
+// op(src)[r][k] = src[r * ld + k] or, transposed, src[k * ld + r].
+__global__ void k_split(const float* __restrict__ src, long long ld, long long bstride, bool trans, int rows, int K,
+                        int rows_p, int Kp, float* __restrict__ dst) {
+  const long long n = (long long)rows_p * Kp;
+  const int b = blockIdx.y;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / Kp), k = (int)(i % Kp);
+    float x = 0.f;
+    if (r < rows && k < K) x = src[b * bstride + (trans ? (long long)k * ld + r : (long long)r * ld + k)];
+    const float hi = to_tf32(x);
+    dst[((long long)b * 2) * n + i] = hi;
+    dst[((long long)b * 2 + 1) * n + i] = to_tf32(x - hi);
+  }
+}
+
+__global__ void __launch_bounds__(128, 1) k_gemm(const __grid_constant__ CUtensorMap tA,
+                                                 const __grid_constant__ CUtensorMap tB, Args p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tn = blockIdx.x, tm = blockIdx.y, b = blockIdx.z;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      aether::mbar_init(&full[s], 1);
+      aether::mbar_init(&empty[s], 1);
+    }
+    aether::mbar_init(done, 1);
+    *abort_word = 0;
+    aether::fence_mbar_init();
+    aether::tma_prefetch_desc(&tA);
+    aether::tma_prefetch_desc(&tB);
+  }
+  if (warp == 1) {
+    aether::tmem_alloc(tmem_slot, BN);
+    aether::tmem_relinquish();
+  }
+  aether::tc_fence_before();
+  __syncthreads();
+  aether::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    // producer: the hi / lo tiles of A and B for each K block
+    const int a_hi = (2 * b) * p.Mp + tm * BM, a_lo = a_hi + p.Mp;
+    const int b_hi = (2 * b) * p.Np + tn * BN, b_lo = b_hi + p.Np;
+    uint32_t issued = 0;
+    for (int kb = 0; kb < p.kb; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+      if (!aether::mbar_wait(&empty[s], ph ^ 1u, abort_word)) {
+        ok = false;
+        break;
+      }
+      uint8_t* st = smem + s * STAGE_BYTES;
+      aether::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+      aether::tma_load_2d(st, &tA, &full[s], kb * BK, a_hi);
+      aether::tma_load_2d(st + TILE, &tA, &full[s], kb * BK, a_lo);
+      aether::tma_load_2d(st + 2 * TILE, &tB, &full[s], kb * BK, b_hi);
+      aether::tma_load_2d(st + 3 * TILE, &tB, &full[s], kb * BK, b_lo);
+      ++issued;
+    }
+    if (!ok) {
+      *abort_word = 1;
+      atomicExch(p.status, aether::kStatusTimeoutProducer);
+      volatile int never = 0;  // copies in flight land before the CTA exits
+      for (uint32_t j = 1; j <= (issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES); ++j) {
+        const uint32_t i = issued - j;
+        aether::mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: per 8-wide K step, hi*hi + lo*hi + hi*lo into one accumulator
+    for (int kb = 0; kb < p.kb && ok; ++kb) {
+      const int s = kb % STAGES;
+      if (!aether::mbar_wait(&full[s], (uint32_t)(kb / STAGES) & 1u, abort_word)) {
+        ok = false;
+        break;
+      }
+      aether::tc_fence_after();
+      const uint32_t base = aether::smem_u32(smem + s * STAGE_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint64_t ah = aether::sdesc_sw128(base + kk * 32, 16, 1024);
+        const uint64_t al = aether::sdesc_sw128(base + TILE + kk * 32, 16, 1024);
+        const uint64_t bh = aether::sdesc_sw128(base + 2 * TILE + kk * 32, 16, 1024);
+        const uint64_t bl = aether::sdesc_sw128(base + 3 * TILE + kk * 32, 16, 1024);
+        umma_tf32(tmem, ah, bh, (kb | kk) != 0 ? 1u : 0u);
+        umma_tf32(tmem, al, bh, 1u);
+        umma_tf32(tmem, ah, bl, 1u);
+      }
+      aether::umma_commit(&empty[s]);
+    }
+    if (!ok) {
+      *abort_word = 1;
+      atomicExch(p.status, aether::kStatusTimeoutMma);
+    }
+    aether::umma_commit(done);  // also the drain: fires once every MMA issued above has completed
+  }
+  __syncwarp();
+  // epilogue: warp w owns TMEM lanes (rows) 32w .. 32w + 31
+  {
+    // `done` fires once every MMA the issuer started has completed (it commits
+    // even after an abort), so TMEM is quiet whether or not the tile finished
+    volatile int never = 0;
+    const bool got = aether::mbar_wait(done, 0, &never);
+    aether::tc_fence_after();
+    const int m = tm * BM + warp * 32 + lane;
+    float* crow = p.C + b * p.sC + (long long)m * p.ldc;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      aether::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+      aether::tmem_ld_wait();
+      if (!got || *abort_word || m >= p.M) continue;
+      const int n0 = tn * BN + c * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = n0 + j;
+        if (n < p.N) {
+          const float v = p.alpha * __uint_as_float(r[j]);
+          crow[n] = p.beta != 0.f ? v + p.beta * crow[n] : v;
+        }
+      }
+    }
+  }
+  aether::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) aether::tmem_dealloc(tmem, BN);
+}
+
+// C = alpha op(A) op(B) + beta C, one thread per output, 32 x 32 shared tiles.
+__global__ void k_gemm_simt(bool ta, bool tb, int M, int N, int K, float alpha, const float* __restrict__ A,
+                            long long lda, const float* __restrict__ B, long long ldb, float beta, float* C,
+                            long long ldc, long long sA, long long sB, long long sC) {
+  __shared__ float As[32][33], Bs[32][33];
+  const int b = blockIdx.z;
+  A += b * sA;
+  B += b * sB;
+  C += b * sC;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads, 4 rows each
+  const int row0 = blockIdx.y * 32, col = blockIdx.x * 32 + tx;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < K; k0 += 32) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = ty + 8 * i;
+      const int m = row0 + r, k = k0 + tx;  // As[r][kk] = op(A)[m][k]
+      As[r][tx] = (m < M && k < K) ? (ta ? A[(long long)k * lda + m] : A[(long long)m * lda + k]) : 0.f;
+      const int kr = k0 + r, n = col;      // Bs[kk][c] = op(B)[k][n]
+      Bs[r][tx] = (kr < K && n < N) ? (tb ? B[(long long)n * ldb + kr] : B[(long long)kr * ldb + n]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < 32; ++kk) {
+      const float bv = Bs[kk][tx];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] += As[ty + 8 * i][kk] * bv;
+    }
+    __syncthreads();
+  }
+  if (col >= N) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = row0 + ty + 8 * i;
+    if (m < M) {
+      float* c = C + (long long)m * ldc + col;
+      *c = beta != 0.f ? alpha * acc[i] + beta * *c : alpha * acc[i];
+    }
+  }
+}
+}  // namespace tfg
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_tiled() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(f);
+  });
+  return fn;
+}
+
+// [rows, Kp] fp32 K-major operand, 128-row x 32-column boxes, 128B swizzle.
+bool tmap_f32(CUtensorMap* m, const float* base, int Kp, long long rows) {
+  EncodeTiled fn = encode_tiled();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
+  cuuint32_t box[2] = {tfg::BK, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Grow-only scratch for the split operands, one per device context (stream-ordered).
+float* gemm_scratch(Ctx* c, size_t floats) {
+  if (c->ws_floats < floats) {
+    if (c->ws) cudaFreeAsync(c->ws, c->s);
+    c->ws = nullptr;
+    c->ws_floats = 0;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&c->ws), floats * 4, c->s) != cudaSuccess) return nullptr;
+    c->ws_floats = floats;
+  }
+  return c->ws;
+}
+
+int* dev_status() {
+  Ctx* c = ctx();
+  if (!c) return nullptr;
+  if (!c->status) {
+    if (cudaMalloc(reinterpret_cast<void**>(&c->status), sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(c->status, 0, sizeof(int));
+  }
+  return c->status;
+}
+
 int gemm_rm(bool ta, bool tb, int M, int N, int K, float alpha, const float* A, int lda, const float* B, int ldb,
             float beta, float* C, int ldc, int batch = 1, long long sA = 0, long long sB = 0, long long sC = 0) {
   Ctx* c = ctx();
   if (!c) return -1;
-  const cublasOperation_t oa = ta ? CUBLAS_OP_T : CUBLAS_OP_N, ob = tb ? CUBLAS_OP_T : CUBLAS_OP_N;
-  cublasStatus_t st;
-  if (batch == 1)
-    st = cublasSgemm(c->blas, ob, oa, N, M, K, &alpha, B, ldb, A, lda, &beta, C, ldc);
-  else
-    st = cublasSgemmStridedBatched(c->blas, ob, oa, N, M, K, &alpha, B, ldb, sB, A, lda, sA, &beta, C, ldc, sC, batch);
-  if (st != CUBLAS_STATUS_SUCCESS) {
-    snprintf(g_err, sizeof(g_err), "cublas status %d", (int)st);
+  if (M <= 0 || N <= 0 || K <= 0 || batch <= 0) return -1;
+  // the tensor-core path pays a split pre-pass and 128 x 128 tiles: worth it above ~96^3
+  const bool tc = (long long)M * N * K >= (1ll << 20) * 3 / 4 && M >= 64 && N >= 64 && K >= 32 &&
+                  getenv("AETHER_DEV_SIMT_GEMM") == nullptr;
+  if (!tc) {
+    dim3 grid((N + 31) / 32, (M + 31) / 32, batch);
+    tfg::k_gemm_simt<<<grid, 256, 0, c->s>>>(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, sA, sB, sC);
+    return launched("gemm");
+  }
+  const int Mp = (M + 127) / 128 * 128, Np = (N + 127) / 128 * 128, Kp = (K + 31) / 32 * 32;
+  const size_t a_f = (size_t)batch * 2 * Mp * Kp, b_f = (size_t)batch * 2 * Np * Kp;
+  float* ws = gemm_scratch(c, a_f + b_f);
+  int* status = dev_status();
+  if (!ws || !status) {
+    snprintf(g_err, sizeof(g_err), "gemm: scratch allocation failed");
     return -2;
   }
-  return 0;
+  float *as = ws, *bs = ws + a_f;
+  const unsigned ga = (unsigned)std::min<long long>(((long long)Mp * Kp + 255) / 256, 4096);
+  const unsigned gb = (unsigned)std::min<long long>(((long long)Np * Kp + 255) / 256, 4096);
+  tfg::k_split<<<dim3(ga, batch), 256, 0, c->s>>>(A, lda, sA, ta, M, K, Mp, Kp, as);
+  tfg::k_split<<<dim3(gb, batch), 256, 0, c->s>>>(B, ldb, sB, !tb, N, K, Np, Kp, bs);  // B^T rows are op(B) columns
+  CUtensorMap ta_map, tb_map;
+  if (!tmap_f32(&ta_map, as, Kp, (long long)batch * 2 * Mp) || !tmap_f32(&tb_map, bs, Kp, (long long)batch * 2 * Np)) {
+    snprintf(g_err, sizeof(g_err), "gemm: tensor map encoding failed");
+    return -2;
+  }
+  static bool attr_set[kMaxDev] = {};
+  const int d = cur_dev();
+  if (!attr_set[d]) {
+    cudaFuncSetAttribute(tfg::k_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, tfg::SMEM);
+    attr_set[d] = true;
+  }
+  tfg::Args args{C, ldc, sC, M, N, K, Kp / tfg::BK, Mp, Np, alpha, beta, status};
+  tfg::k_gemm<<<dim3(Np / tfg::BN, Mp / tfg::BM, batch), 128, tfg::SMEM, c->s>>>(ta_map, tb_map, args);
+  return launched("gemm");
 }
 
 template <int T>
@@ -832,6 +1186,8 @@ int matvec_typed(int t, MV p, int batch = 1) {
     case TQ5_K: return matvec_launch<TQ5_K>(p, batch);
     case TQ6_K: return matvec_launch<TQ6_K>(p, batch);
     case TIQ4_XS: return matvec_launch<TIQ4_XS>(p, batch);
+    case TIQ3_XXS: return matvec_launch<TIQ3_XXS>(p, batch);
+    case TIQ3_S: return matvec_launch<TIQ3_S>(p, batch);
     default: return -2;
   }
 }
@@ -874,6 +1230,8 @@ int dequant_typed(int t, const uint8_t* w, float* out, size_t chunks) {
     case TQ3_K: return dequant_launch<TQ3_K>(w, out, chunks);
     case TIQ4_NL: return dequant_launch<TIQ4_NL>(w, out, chunks);
     case TIQ4_XS: return dequant_launch<TIQ4_XS>(w, out, chunks);
+    case TIQ3_XXS: return dequant_launch<TIQ3_XXS>(w, out, chunks);
+    case TIQ3_S: return dequant_launch<TIQ3_S>(w, out, chunks);
     default: return -2;
   }
 }
@@ -1527,6 +1885,23 @@ AE_API int aether_op_fused_q5_k_expert_matmul_seq1_cuda(int64_t x, int64_t w, in
 }
 AE_API int aether_op_fused_iq4_xs_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
   return qmatvec(TIQ4_XS, x, w, y, n_out, bpr, e);
+}
+// IQ3_XXS / IQ3_S (GLM-4.7-flash's quantisation): dense and expert mat-vecs, dequantiser
+AE_API int aether_op_fused_iq3_xxs_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TIQ3_XXS, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_iq3_s_matmul_seq1_cuda(int64_t a, int64_t w, int64_t o, int n, int nb) {
+  return qmatvec(TIQ3_S, a, w, o, n, nb);
+}
+AE_API int aether_op_fused_iq3_xxs_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr,
+                                                           int e) {
+  return qmatvec(TIQ3_XXS, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_fused_iq3_s_expert_matmul_seq1_cuda(int64_t x, int64_t w, int64_t y, int n_out, int bpr, int e) {
+  return qmatvec(TIQ3_S, x, w, y, n_out, bpr, e);
+}
+AE_API int aether_op_dequant_iq3_xxs_f32_cuda(int64_t blk, int64_t out, int n) {
+  return dequant_handle(TIQ3_XXS, blk, out, n);
 }
 
 // ================================================================================================ NCCL clique

@@ -76,28 +76,34 @@ def test_registry_copies_and_refusals():
 
 
 @pytest.mark.gpu
-def test_gemm_family():
+@pytest.mark.parametrize("m,k,n,tol", [
+    (67, 129, 45, 1e-5),      # small: the SIMT kernel
+    (300, 190, 257, 2e-5),    # tensor cores (tf32 x3), every dimension ragged against the 128 / 32 tiles
+    (1024, 1024, 1024, 2e-5),
+])
+def test_gemm_family(m, k, n, tol):
+    """The f32 GEMM family against fp64 numpy. A single tf32 pass would be off
+    by ~1e-3 relative; the three-term hi / lo split must stay at fp32 level."""
     d = _dev()
-    m, k, n = 67, 129, 45
     a, b = _rand(m, k, seed=1), _rand(k, n, seed=2)
     ha, hb, ho = d.upload(a), d.upload(b), d.alloc_f32(m * n)
     d.call("aether_op_matmul_f32_cuda", ha, hb, ho, m, k, n)
-    _close(d.download(ho, (m, n)), a @ b)
+    _close(d.download(ho, (m, n)), a.astype(np.float64) @ b, tol)
     d.call("aether_op_matmul_gelu_f32_cuda", ha, hb, ho, m, k, n)
-    ref = torch.nn.functional.gelu(torch.from_numpy(a @ b), approximate="tanh").numpy()
-    _close(d.download(ho, (m, n)), ref)
+    ref = torch.nn.functional.gelu(torch.from_numpy(a.astype(np.float64) @ b), approximate="tanh").numpy()
+    _close(d.download(ho, (m, n)), ref, max(tol, 1e-5))
     at = d.upload(np.ascontiguousarray(a.T))  # [k, m]
     d.call("aether_op_matmul_tn_f32_cuda", at, hb, ho, m, k, n)
-    _close(d.download(ho, (m, n)), a @ b)
+    _close(d.download(ho, (m, n)), a.astype(np.float64) @ b, tol)
     bt = d.upload(np.ascontiguousarray(b.T))  # [n, k]
     d.call("aether_op_matmul_nt_f32_cuda", ha, bt, ho, m, k, n)
-    _close(d.download(ho, (m, n)), a @ b)
+    _close(d.download(ho, (m, n)), a.astype(np.float64) @ b, tol)
     dy = _rand(m, n, seed=3)
     hdy, hdb, hda = d.upload(dy), d.alloc_f32(k * n), d.alloc_f32(m * k)
     d.call("aether_op_matmul_backward_rhs_f32_cuda", ha, hdy, hdb, m, k, n)
-    _close(d.download(hdb, (k, n)), a.T @ dy)
+    _close(d.download(hdb, (k, n)), a.T.astype(np.float64) @ dy, tol)
     d.call("aether_op_matmul_backward_lhs_f32_cuda", hdy, hb, hda, m, k, n)
-    _close(d.download(hda, (m, k)), dy @ b.T)
+    _close(d.download(hda, (m, k)), dy.astype(np.float64) @ b.T, tol)
     d.call("aether_bench_matmul_batch", ha, hb, ho, m, k, n, 3)
     d.call("aether_op_matmul_f32_cuda_profile", ha, hb, ho, m, k, n)
 
@@ -310,7 +316,7 @@ def test_sdpa_and_decode_attention_and_graphs():
 
 
 _HALVES = {G.Q4_0: (0,), G.Q8_0: (0,), G.Q5_0: (0,), G.IQ4_NL: (0,), G.Q4_K: (0, 2), G.Q5_K: (0, 2), G.Q3_K: (108,),
-           G.Q6_K: (208,), G.IQ4_XS: (0,)}
+           G.Q6_K: (208,), G.IQ4_XS: (0,), G.IQ3_XXS: (0,), G.IQ3_S: (0,)}
 
 
 def _qblocks(typ, n, seed):
@@ -325,10 +331,11 @@ def _qblocks(typ, n, seed):
 @pytest.mark.gpu
 @pytest.mark.parametrize("typ,name", [(G.Q4_0, "q4_0"), (G.Q5_0, "q5_0"), (G.Q8_0, "q8_0"), (G.IQ4_NL, "iq4_nl"),
                                       (G.Q3_K, "q3_k"), (G.Q4_K, "q4k"), (G.Q5_K, "q5_k"), (G.Q6_K, "q6k"),
-                                      (G.IQ4_XS, "iq4_xs")])
+                                      (G.IQ4_XS, "iq4_xs"), (G.IQ3_XXS, "iq3_xxs"), (G.IQ3_S, "iq3_s")])
 def test_quantised_dequant_and_matvec(typ, name):
-    """Device dequantisation and the fused mat-vec against the numpy load-time
-    dequantiser of the same GGUF blocks."""
+    """Device dequantisation and the fused mat-vec against the load-time
+    dequantiser of the same GGUF blocks (numpy, or the native host decoders of
+    the IQ3 codebook formats)."""
     d = _dev()
     ne, nb = G.BLOCKS[typ]
     rows, bpr = 24, (4 if ne == 256 else 32)
@@ -358,10 +365,17 @@ def test_quantised_dequant_and_matvec(typ, name):
         hdy, hdx = d.upload(dyv), d.alloc_f32(k)
         d.call("aether_op_quant_matmul_backward_lhs_f32_cuda", hw, typ, hdy, hdx, rows, k)
         _close(d.download(hdx, k), w.T.astype(np.float64) @ dyv, 1e-4)
-    if typ in (G.Q4_K, G.Q6_K):
-        fn = "aether_op_dequant_q4_k_m_f32_cuda" if typ == G.Q4_K else "aether_op_dequant_q6_k_f32_cuda"
+    if typ in (G.Q4_K, G.Q6_K, G.IQ3_XXS):
+        fn = {G.Q4_K: "aether_op_dequant_q4_k_m_f32_cuda", G.Q6_K: "aether_op_dequant_q6_k_f32_cuda",
+              G.IQ3_XXS: "aether_op_dequant_iq3_xxs_f32_cuda"}[typ]
         d.call(fn, hw, hout, rows * bpr)
         _close(d.download(hout, (rows, k)), w, 1e-6)
+    if typ in (G.IQ3_XXS, G.IQ3_S):  # expert e = 1 of a stacked pair
+        blk1 = _qblocks(typ, rows * bpr, seed=98).reshape(-1)
+        two = d.upload(np.concatenate([blk.reshape(-1), blk1]))
+        w1 = G.dequantize(blk1, typ, rows * k).reshape(rows, k)
+        d.call(f"aether_op_fused_{name}_expert_matmul_seq1_cuda", hx, two, hy, rows, bpr, 1)
+        _close(d.download(hy, rows), w1.astype(np.float64) @ x, 1e-4)
 
 
 @pytest.mark.gpu
