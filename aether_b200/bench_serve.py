@@ -24,6 +24,56 @@ from . import _ext
 from .models.qwen import QwenConfig, QwenModel
 
 
+class EmulatedTP:
+    """One tensor-parallel rank's share of the work on a single GPU, with the
+    cross-rank exchanges replaced by their local halves: the model holds rank
+    ``rank`` of ``world``'s shards and runs the same kernels as in a real TP
+    run (push-reduce mode), except that a reduction sums only this rank's
+    partial and the vocabulary argmax sees only this rank's slice. The time
+    per step is the TP compute floor; a real TP run minus it is the cost of
+    communication. Numerics are not those of the full model."""
+
+    mode = "push"
+
+    def __init__(self, rank: int, world: int):
+        self.rank, self.world = rank, world
+
+    def prepare_decode(self, rows_cap, width, vocab_cols):
+        pass
+
+    def all_reduce_(self, t):
+        return t
+
+    def reduce_gemm(self, x, w, which):
+        raise NotImplementedError("the emulation runs the push-reduce path only")
+
+    def finalize_wait(self):
+        return None
+
+    def push_reduce(self, acc, y, res=None, bias=None, w=None, h=None, eps=1e-6):
+        from .ops import functional as F
+
+        if w is None:
+            return F.skinny_finalize(acc, y, bias=bias, res=res)
+        F.finalize_residual_norm(acc, y, w, h, bias=bias, res=res, eps=eps)
+        return y
+
+    def vocab_argmax(self, logits, n_loc, col0, out=None):
+        from .ops import functional as F
+
+        r = F.argmax(logits[:, :n_loc].contiguous()) + col0
+        if out is None:
+            return r
+        out.copy_(r)
+        return out
+
+    def gather_vocab(self, logits, n_loc, col0, V, out=None):
+        raise NotImplementedError("the emulation keeps one vocabulary slice")
+
+    def max_over_ranks(self, x):
+        return x
+
+
 def events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
@@ -70,7 +120,7 @@ def run(model_name: str, batches, prompt: int, new_tokens: int, ttft_reps: int, 
             ms_step = tp.max_over_ranks(ms_step)
             tt = [tp.max_over_ranks(t) for t in tt]
         rec = {
-            "metric": "decode_tokens_per_s", "model": f"Qwen2.5-{model_name.upper()} shape", "tp": tp.world if tp else 1,
+            "metric": "decode_tokens_per_s", "model": f"Qwen2.5-{model_name.upper()} shape", "tp": tp.world if tp else 1, "emulated_tp": isinstance(tp, EmulatedTP),
             "batch": B, "prompt": prompt, "new_tokens": new_tokens, "value": B / (ms_step / 1e3), "unit": "tokens/s",
             "ms_per_decode_step": ms_step, "ttft_p50_ms": statistics.median(tt), "ttft_all_ms": tt,
             "decode_splits": m.decode_splits, "graph": True, "dtype": "bf16",
@@ -92,13 +142,17 @@ def main():
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--ttft-reps", type=int, default=5)
     ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--emulate-tp", type=int, default=0,
+                    help="one GPU runs one TP rank's shards without communication (the TP compute floor)")
     args = ap.parse_args()
     _ext.C()
     batches = [int(b) for b in (args.batches or ("1,8,32" if args.model == "1.5b" else "1,16,64")).split(",")]
     prompt = args.prompt or (512 if args.model == "1.5b" else 2048)
     tp = None
     rank0 = True
-    if args.tp > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    if args.emulate_tp > 1:
+        tp = EmulatedTP(0, args.emulate_tp)
+    elif args.tp > 1 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
         from .parallel import dist as D
         from .parallel.tp import TensorParallel
 
@@ -106,7 +160,7 @@ def main():
         tp = TensorParallel(info)
         rank0 = info.is_main
     run(args.model, batches, prompt, args.new_tokens, args.ttft_reps, tp, rank0)
-    if tp is not None:
+    if tp is not None and hasattr(tp, "close"):
         tp.close()
 
 

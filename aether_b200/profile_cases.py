@@ -15,6 +15,8 @@ once on its own:
     python -m aether_b200.profile_cases decode7b    # eager Qwen2.5-7B-shape decode steps (batch 1, 2048 cached)
                                                     # inside NVTX range "decode": for the launch list only
                                                     # (ncu --nvtx --nvtx-include "decode/" --metrics gpu__time_duration.sum)
+    python -m aether_b200.profile_cases decode7b_tp8 # the same for one TP=8 rank's shards, emulated on one GPU
+    python -m aether_b200.profile_cases rows 1      # one launch of each row / elementwise / loss / MoE / MLA / quant kernel
 """
 from __future__ import annotations
 
@@ -98,11 +100,11 @@ def adamw(reps):
         F.adamw_(p, g, m, v, pb, lr=1e-4, beta1=0.9, beta2=0.95, eps=1e-8, wd=0.1, step=i + 1)
 
 
-def decode7b(reps):
+def decode7b(reps, tp=None):
     from .models.qwen import QwenConfig, QwenModel
 
     cfg = QwenConfig.qwen25_7b()
-    m = QwenModel(cfg, device="cuda", seed=1, max_batch=1, max_seq=4096)
+    m = QwenModel(cfg, device="cuda", seed=1, max_batch=1, max_seq=4096, tp=tp)
     prompt = torch.randint(0, cfg.vocab, (1, 2048), device="cuda")
     tok = m.prefill(prompt)
     pos = torch.full((1,), 2048, dtype=torch.int32, device="cuda")
@@ -115,7 +117,66 @@ def decode7b(reps):
         torch.cuda.nvtx.range_pop()
 
 
-CASES = {f.__name__: f for f in (gemm, attn_fwd, attn_bwd, skinny, decode_attn, decode_attn_b1, adamw, decode7b)}
+def rows(reps):
+    """One launch each of the row / elementwise / loss / MoE / MLA / quant
+    kernels at training or serving sizes (inputs > L2 where the op streams):
+    rmsnorm fwd + bwd and layernorm fwd + bwd [16384, 2048], softmax
+    [16384, 4096], swiglu fwd + bwd [16384, 11264], RoPE on a [16384, 6144]
+    qkv, embedding fwd + bwd (vocab 32000), fused cross-entropy [4096, 152064],
+    the grouped MoE GEMM (8 experts, 8192 token rows x 1408 -> 2048), absorbed
+    MLA decode attention (16 heads, 4 sequences x 4096 latent rows), Q8_0
+    quantise + dequantise of 64M values."""
+    from .ops import reference as ref
+
+    T, d = 16384, 2048
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(T, d, device="cuda", generator=g).bfloat16()
+    w = torch.ones(d, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(d, device="cuda")
+    for _ in range(reps):
+        y, h, rstd = F.rmsnorm(x, w)
+        F.rmsnorm_bwd(y, h, w, rstd, dw)
+    out = F.layernorm(x, w, w)
+    F.layernorm_bwd(out[0], x, w, out[-2], out[-1], dw, dw.clone())
+    F.softmax(torch.randn(T, 4096, device="cuda", generator=g).bfloat16())
+    hgu = torch.randn(T, 2 * 5632, device="cuda", generator=g).bfloat16()
+    act = F.swiglu(hgu)
+    F.swiglu_bwd(hgu, act)
+    qkv = torch.randn(T, 3 * d, device="cuda", generator=g).bfloat16()
+    cos, sin = ref.rope_tables(2048, 128, 10000.0, device="cuda")
+    pos = torch.arange(2048, device="cuda", dtype=torch.int32).repeat(T // 2048)
+    F.rope_(qkv, pos, cos.contiguous(), sin.contiguous(), 32, 128)
+    table = torch.randn(32000, d, device="cuda", generator=g).bfloat16()
+    ids = torch.randint(0, 32000, (T,), device="cuda", generator=g)
+    e = F.embedding(table, ids)
+    F.embedding_bwd(e, ids, torch.zeros(32000, d, device="cuda"))
+    logits = torch.randn(4096, 152064, device="cuda", generator=g).bfloat16()
+    F.cross_entropy_fused(logits, torch.randint(0, 152064, (4096,), device="cuda", generator=g), grad_scale=1 / 4096)
+    del logits
+    E, Tm, K, N = 8, 8192, 2048, 1408
+    idx = torch.randint(0, E, (Tm, 1), device="cuda", generator=g, dtype=torch.int32)
+    row_of, src_row, tile_group = F.moe_permute(idx, E)
+    X = F.moe_gather(torch.randn(Tm, K, device="cuda", generator=g).bfloat16(), src_row)
+    F.gemm_grouped(X, torch.randn(E, N, K, device="cuda", generator=g).bfloat16() * 0.02, tile_group)
+    cache = torch.randn(4, 4096, 576, device="cuda", generator=g).bfloat16()
+    q_abs = torch.randn(4, 16, 576, device="cuda", generator=g).bfloat16()
+    F.mla_attention(q_abs, cache, torch.arange(4, device="cuda", dtype=torch.int32),
+                    torch.full((4,), 4096, device="cuda", dtype=torch.int32),
+                    torch.empty(4, 16, 512, device="cuda", dtype=torch.bfloat16), 576 ** -0.5, splits=8)
+    big = torch.randn(1 << 26, device="cuda", generator=g).bfloat16()
+    q = F.quantize_blocks(big)
+    F.dequantize_blocks(q, big.shape)
+
+
+def decode7b_tp8(reps):
+    """decode7b for one TP=8 rank's shards, emulated on one GPU (no exchanges)."""
+    from .bench_serve import EmulatedTP
+
+    decode7b(reps, tp=EmulatedTP(0, 8))
+
+
+CASES = {f.__name__: f for f in (gemm, attn_fwd, attn_bwd, skinny, decode_attn, decode_attn_b1, adamw, decode7b,
+                                 decode7b_tp8, rows)}
 
 
 def main():
