@@ -110,11 +110,14 @@ class LoRAGPT:
                 out, inp = base.arena.slots[f"l{i}.{t}"].shape
                 specs += [(f"l{i}.{t}.A", (cfg.rank, inp), False), (f"l{i}.{t}.B", (out, cfg.rank), False)]
         self.arena = ParamArena(specs, self.device, pad_multiple=pad_multiple, alloc=alloc)
-        g = torch.Generator(device="cpu").manual_seed(seed)
         with torch.no_grad():
             for name, slot in self.arena.slots.items():
                 mv = self.arena.master_view(name)
                 if name.endswith(".A"):
+                    # one generator per (layer, target): any pipeline split draws the same adapters
+                    layer, target = name.split(".")[:2]
+                    key = int(layer[1:]) * len(cfg.targets) + cfg.targets.index(target)
+                    g = torch.Generator(device="cpu").manual_seed(seed * 1000003 + key)
                     mv.copy_((torch.randn(slot.shape, generator=g) / math.sqrt(cfg.rank)).to(self.device))
                 else:
                     mv.zero_()
