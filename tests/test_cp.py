@@ -5,6 +5,7 @@ import os
 import socket
 import sys
 
+import pytest
 import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -23,7 +24,7 @@ def _tokens():
     return torch.randint(0, 128, (2, 33), generator=torch.Generator().manual_seed(11))
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, mode="allgather"):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
                       MASTER_PORT=str(port))
     sys.path.insert(0, ROOT)
@@ -34,7 +35,7 @@ def _worker(rank, world, port, q):
     from aether_b200.parallel.cp import CPGroup, shard_sequence
 
     D.init(device="cpu", timeout_s=60)
-    cp = CPGroup(rank, world, None)
+    cp = CPGroup(rank, world, None, mode)
     m = GPT(GPTConfig(**CFG), device="cpu", seed=4, cp=cp)
     ids, tgt = shard_sequence(_tokens(), cp)
     loss = m.loss(ids, tgt)
@@ -48,7 +49,11 @@ def _worker(rank, world, port, q):
     D.shutdown()
 
 
-def test_cp2_matches_full_sequence():
+@pytest.mark.parametrize("mode", ["allgather", "ring", "ulysses"])
+def test_cp2_matches_full_sequence(mode):
+    """All three attention schemes (K/V all-gather, ring attention with
+    log-sum-exp merging, Ulysses all-to-all over heads) reproduce the
+    one-process loss and gradients."""
     import multiprocessing as mp
 
     from aether_b200.models.gpt import GPT, GPTConfig
@@ -56,7 +61,7 @@ def test_cp2_matches_full_sequence():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in ps:
         p.start()
     got = dict((r, (l, g)) for r, l, g in (q.get(timeout=300) for _ in ps))
