@@ -37,6 +37,7 @@ class EmulatedTP:
 
     def __init__(self, rank: int, world: int):
         self.rank, self.world = rank, world
+        self._acc = None
 
     def prepare_decode(self, rows_cap, width, vocab_cols):
         pass
@@ -45,7 +46,13 @@ class EmulatedTP:
         return t
 
     def reduce_gemm(self, x, w, which):
-        raise NotImplementedError("the emulation runs the push-reduce path only")
+        """This rank's partial only (the multicast-reduce path without the exchange)."""
+        from .ops import functional as F
+
+        if self._acc is None or self._acc.shape[1] < w.shape[0]:
+            self._acc = torch.zeros(64, max(w.shape[0], 8192), dtype=torch.float32, device=x.device)
+        F.skinny_gemm(x, w, self._acc)
+        return self._acc[: x.shape[0]]
 
     def finalize_wait(self):
         return None

@@ -327,6 +327,12 @@ class QwenModel:
         import os as _os
         # the fused decode epilogue has no slot for Qwen3's q/k norm
         self.fused_decode = _os.environ.get("AETHER_UNFUSED_DECODE", "0") != "1" and not cfg.qk_norm
+        # QKV (bias + RoPE + KV append) and SwiGLU finished inside their decode GEMMs (opt-in:
+        # measured on a B200 the tile finisher serialises in the GEMM tail -- Qwen2.5-7B TP1
+        # batch 64: 7.43 ms per step against 5.72 with the separate finalize kernels; batch 1
+        # within noise of the separate kernels)
+        self.fused_epilogues = (self.fused_decode and cfg.head_dim == 128 and self.f % 64 == 0
+                                and _os.environ.get("AETHER_GEMM_EPILOGUES", "0") == "1")
         self._graphs: dict[int, tuple] = {}
         self._alloc_decode_buffers()
         if tp is not None and hasattr(tp, "prepare_decode"):
@@ -367,6 +373,8 @@ class QwenModel:
             "next": torch.zeros(B, dtype=torch.long, device=dev),
             "counters": torch.zeros(B * self.hkv, dtype=torch.int32, device=dev),
             "logits": torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev),
+            # per-tile K-block counters of the fused-epilogue GEMMs (they return to zero)
+            "tiles": torch.zeros(max(qkv_w // 128, self.f // 64) + 1, dtype=torch.int32, device=dev),
         }
         self._want_logits = False
 
@@ -483,14 +491,20 @@ class QwenModel:
         x.copy_(F.embedding(w.embed, b["tok"][:B]))
         F.rmsnorm_into(x, w.attn_norm[0], h, cfg.norm_eps)
         L = cfg.n_layers
+        fused_ep = self.fused_epilogues
+        push = self._push_for(B)
         for i in range(L):
-            F.skinny_gemm(h, w.wqkv[i], acc)
-            F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, *self.rope_cs[i], self.cache.k[i], self.cache.v[i],
-                                self.hq, self.hkv, D, page_table=self.page_table)
+            if fused_ep:  # bias + RoPE + KV append finished inside the GEMM
+                F.skinny_gemm_qkv(h, w.wqkv[i], acc, b["tiles"], w.bqkv[i], qkv, pos, slot, *self.rope_cs[i],
+                                  self.cache.k[i], self.cache.v[i], self.hq, self.hkv, page_table=self.page_table)
+            else:
+                F.skinny_gemm(h, w.wqkv[i], acc)
+                F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, *self.rope_cs[i], self.cache.k[i],
+                                    self.cache.v[i], self.hq, self.hkv, D, page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
                                self._auto_splits(B), b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table,
                                window=self.win[i], softcap=self.softcap)
-            if self.push:  # local GEMM, then one push-reduce + residual + RMSNorm kernel
+            if push:  # local GEMM, then one push-reduce + residual + RMSNorm kernel
                 F.skinny_gemm(o, w.wo[i], acc)
                 self.tp.push_reduce(acc, x2, res=x, w=w.mlp_norm[i], h=h, eps=cfg.norm_eps)
             else:
@@ -500,10 +514,13 @@ class QwenModel:
                 else:
                     racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
                 F.finalize_residual_norm(racc, x2, w.mlp_norm[i], h, res=x, eps=cfg.norm_eps, wait=self._tp_wait())
-            F.skinny_gemm(h, w.wgu[i], acc)
-            F.skinny_finalize(acc, act, swiglu=True)
+            if fused_ep:  # SwiGLU finished inside the gate/up GEMM
+                F.skinny_gemm_swiglu(h, w.wgu[i], acc, act, b["tiles"])
+            else:
+                F.skinny_gemm(h, w.wgu[i], acc)
+                F.skinny_finalize(acc, act, swiglu=True)
             nw = w.attn_norm[i + 1] if i + 1 < L else w.final_norm
-            if self.push:
+            if push:
                 F.skinny_gemm(act, w.wd[i], acc)
                 self.tp.push_reduce(acc, x, res=x2, w=nw, h=h, eps=cfg.norm_eps)
                 continue
@@ -552,7 +569,7 @@ class QwenModel:
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
                                self._auto_splits(B), b["part_o"], b["part_lse"], page_table=self.page_table,
                                window=self.win[i], softcap=self.softcap)
-            if self.push:
+            if self._push_for(B):
                 F.skinny_gemm(o, w.wo[i], acc)
                 self.tp.push_reduce(acc, x2, res=x)
             elif self.tp is None:
@@ -569,12 +586,25 @@ class QwenModel:
     def _tp_wait(self):
         return self.tp.finalize_wait() if self.tp is not None else None
 
+    def _push_for(self, B: int) -> bool:
+        """Push reduction for this batch bucket: measured on B200s (Qwen2.5-7B
+        shape) the multicast-reduce GEMM is faster for one or a few rows (TP8
+        batch 1: 1.76 vs 1.87 ms per step) and the push faster from 16 rows on
+        (TP8 batch 64: 3.46 vs 5.01 ms); AETHER_TP_REDUCE pins one mode."""
+        if not self.push:
+            return False
+        import os as _os
+
+        if _os.environ.get("AETHER_TP_REDUCE") == "push":
+            return True
+        return B > 4
+
     def _decode_ffn(self, i, h, x2, x, act, acc) -> None:
         """x = x2 + FFN(h) on the decode rows (static buffers)."""
         w = self.w
         F.skinny_gemm(h, w.wgu[i], acc)
         F.skinny_finalize(acc, act, swiglu=True)
-        if self.push:
+        if self._push_for(h.shape[0]):
             F.skinny_gemm(act, w.wd[i], acc)
             self.tp.push_reduce(acc, x, res=x2)
         elif self.tp is None:

@@ -471,6 +471,31 @@ def qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache,
     return rope_kv_append(qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, D, page_table)
 
 
+def skinny_gemm_swiglu(x, w, acc, act, tile_cnt, splits=0):
+    """act[M, F] = silu(x w_gate^T) * (x w_up^T), w = [gate; up] [2F, K], as one
+    decode GEMM whose tile finisher applies the SwiGLU (acc: zeroed fp32
+    scratch, left zeroed; tile_cnt: int32 counters, left zeroed)."""
+    if _cuda(x):
+        C().skinny_gemm_swiglu(x, w, acc, act, tile_cnt, int(splits))
+        return act
+    F_ = w.shape[0] // 2
+    z = x.float() @ w.float().t()
+    act[: x.shape[0], :F_].copy_((torch.nn.functional.silu(z[:, :F_]) * z[:, F_:]).to(act.dtype))
+    return act
+
+
+def skinny_gemm_qkv(x, w, acc, tile_cnt, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv,
+                    page_table=None, splits=0):
+    """The decode QKV projection and its epilogue in one GEMM (head_dim 128):
+    qkv = rope(bf16(x wqkv^T + bias)) with k / v appended to the caches."""
+    if _cuda(x):
+        C().skinny_gemm_qkv(x, w, acc, tile_cnt, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, int(Hq),
+                            int(Hkv), page_table, int(splits))
+        return qkv
+    skinny_gemm(x, w, acc)
+    return qkv_finalize_rope(acc, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv, 128, page_table)
+
+
 def finalize_residual_norm(acc, y, w, h, bias=None, res=None, eps=1e-6, wait=None):
     """y = bf16(acc + bias + res) (residual stream); h = rmsnorm(y) * w; acc zeroed.
     wait: as in skinny_finalize."""

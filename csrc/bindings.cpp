@@ -63,6 +63,12 @@ void tp_push_reduce(at::Tensor acc, at::Tensor y, std::optional<at::Tensor> bias
                     std::optional<at::Tensor> w, std::optional<at::Tensor> h, double eps, at::Tensor data_peers,
                     int64_t data_mc, int64_t ld, at::Tensor flag_peers, at::Tensor ctr, int64_t rows_cap,
                     int64_t rank, int64_t world, double timeout_s);
+void skinny_gemm_swiglu(at::Tensor x, at::Tensor w, at::Tensor acc, at::Tensor act, at::Tensor tile_cnt,
+                        int64_t splits);
+void skinny_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor acc, at::Tensor tile_cnt, std::optional<at::Tensor> bias,
+                     at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t,
+                     at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv,
+                     std::optional<at::Tensor> page_table, int64_t splits);
 // comm.cu
 void team_barrier(at::Tensor peer_sig_ptrs, at::Tensor my_sig, at::Tensor epoch, int64_t rank, int64_t world,
                   double timeout_s);
@@ -145,6 +151,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "sig_peers"_a = pybind11::none(), "sig_epoch"_a = pybind11::none(), "sig_done"_a = pybind11::none(),
         "sig_rank"_a = 0, "sig_world"_a = 0);
   m.def("team_barrier", &aether::team_barrier);
+  m.def("skinny_gemm_swiglu", &aether::skinny_gemm_swiglu);
+  m.def("skinny_gemm_qkv", &aether::skinny_gemm_qkv);
   m.def("tp_vocab_argmax", &aether::tp_vocab_argmax);
   m.def("tp_put_cols", &aether::tp_put_cols);
   m.def("tp_push_reduce", &aether::tp_push_reduce, "acc"_a, "y"_a, "bias"_a, "res"_a, "w"_a, "h"_a, "eps"_a,

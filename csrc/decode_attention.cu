@@ -20,6 +20,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "decode_common.cuh"
 #include "host_utils.h"
 
 namespace aether {
@@ -34,35 +35,6 @@ constexpr int kKeysPerBlock = 64;                      // keys per pipeline stag
 constexpr int kStages = 3;
 constexpr int kStageBytes = 2 * kKeysPerBlock * 256;   // K and V rows of one block
 constexpr int kKvSmem = kStages * kStageBytes;         // 96 KB
-
-__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
-  v[0] = bf16lo(u.x); v[1] = bf16hi(u.x); v[2] = bf16lo(u.y); v[3] = bf16hi(u.y);
-  v[4] = bf16lo(u.z); v[5] = bf16hi(u.z); v[6] = bf16lo(u.w); v[7] = bf16hi(u.w);
-}
-__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
-  uint4 u;
-  u.x = pack_bf16(v[0], v[1]); u.y = pack_bf16(v[2], v[3]);
-  u.z = pack_bf16(v[4], v[5]); u.w = pack_bf16(v[6], v[7]);
-  return u;
-}
-
-// Paged KV: with a page table, a cache is a pool [pages, page_size, Hkv, D]
-// and key t of the sequence in table row `seq` lives in physical page
-// table[seq * stride + t / page_size] at row t % page_size (page_size a power of
-// two). Without one, the cache is [slots, max_seq, Hkv, D] indexed by slot.
-struct PageMap {
-  const int* table = nullptr;
-  int stride = 0;
-  int shift = 0;
-};
-
-// element offset of (sequence row `seq`, position t) -- head 0, dim 0
-__device__ __forceinline__ int64_t kv_offset(const PageMap& pm, int seq, int t, int64_t slot_stride,
-                                             int64_t pos_stride) {
-  if (pm.table == nullptr) return (int64_t)seq * slot_stride + (int64_t)t * pos_stride;
-  const int64_t phys = pm.table[(int64_t)seq * pm.stride + (t >> pm.shift)];
-  return ((phys << pm.shift) | (int64_t)(t & ((1 << pm.shift) - 1))) * pos_stride;
-}
 
 // qkv: [T, row] with q heads [0,Hq), k heads [Hq, Hq+Hkv), v heads after.
 // One thread per (token, head, 8-wide chunk of the half head).
@@ -525,9 +497,6 @@ __global__ void __launch_bounds__(1024) finalize_residual_norm_kernel(float* __r
 
 }  // namespace dec
 
-namespace {
-// page_table: CUDA int32 [rows, max_pages] (rows indexed by `slot`), caches
-// [pages, page_size, Hkv, D] with page_size a power of two.
 dec::PageMap page_map(const std::optional<at::Tensor>& page_table, const at::Tensor& cache) {
   dec::PageMap pm;
   if (!page_table || !page_table->defined()) return pm;
@@ -543,7 +512,6 @@ dec::PageMap page_map(const std::optional<at::Tensor>& page_table, const at::Ten
   pm.shift = shift;
   return pm;
 }
-}  // namespace
 
 // qkv [T, row] bf16 (rotated in place), pos/slot int32 [T], cos/sin [max_pos, D/2],
 // k_cache/v_cache [slots, max_seq, Hkv, D] (or page pools with page_table).

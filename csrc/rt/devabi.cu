@@ -93,12 +93,27 @@ int cur_dev() {
   return d;
 }
 
+// Restores the calling thread's current device on scope exit.
+struct DeviceScope {
+  int prev = -1;
+  explicit DeviceScope(int d) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~DeviceScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
 Ctx* ctx_for(int d) {
   if (d < 0 || d >= kMaxDev) return nullptr;
   Ctx& c = g_ctx[d];
   if (c.ready) return &c;
   std::lock_guard<std::mutex> l(g_mu);
   if (c.ready) return &c;
+  // the stream and the codebook copies belong to device d, whichever device
+  // the caller has current (the NCCL clique creates every device's context)
+  DeviceScope on(d);
   cudaError_t e = cudaStreamCreateWithFlags(&c.s, cudaStreamNonBlocking);
   if (e != cudaSuccess) {
     set_err("stream", e);

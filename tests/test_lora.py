@@ -84,8 +84,9 @@ def test_qlora_cpu_close_to_bf16_base():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt", [F.Q8_0, F.Q4_0])
-def test_gpu_block_quant_matches_cpu(fmt):
-    x = (torch.randn(96, 256, generator=torch.Generator().manual_seed(0)) * 0.05).bfloat16()
+@pytest.mark.parametrize("shape", [(96, 256), (37, 96)])  # whole 32-block warp spans; a ragged last span
+def test_gpu_block_quant_matches_cpu(fmt, shape):
+    x = (torch.randn(*shape, generator=torch.Generator().manual_seed(0)) * 0.05).bfloat16()
     qc = F.quantize_blocks(x, fmt)
     qg = F.quantize_blocks(x.cuda(), fmt)
     assert torch.equal(qg.cpu(), qc)

@@ -47,7 +47,7 @@ def test_gpu_prefill_and_graph_decode():
 @pytest.mark.gpu
 def test_gpu_skinny_gemm_and_decode_attention():
     from aether_b200.ops import reference as ref
-    for M in (1, 7, 16, 33, 64):
+    for M in (1, 2, 3, 4, 7, 16, 33, 64):
         x = torch.randn(M, 3584, device="cuda").bfloat16()
         w = torch.randn(1000, 3584, device="cuda").bfloat16()
         acc = torch.zeros(M, 1024, device="cuda")
@@ -73,6 +73,60 @@ def test_gpu_skinny_gemm_and_decode_attention():
         o, _ = ref.attention(q[bi].view(1, 1, Hq, D), kc[s, :L][None], vc[s, :L][None], D ** -0.5, causal=False)
         e = (out[bi].float() - o.reshape(-1)).norm() / o.norm()
         assert e < 1e-2, (bi, float(e))
+
+
+@pytest.mark.gpu
+def test_gpu_fused_gemm_epilogues_match_separate_kernels():
+    """The decode GEMMs that finish QKV (bias + RoPE + KV append) and SwiGLU
+    inside their tiles give the same caches, activations and tokens as the
+    GEMM + finalize-kernel path, on contiguous and paged caches and at batch
+    sizes that exercise one and several 16-row MMA columns."""
+    from aether_b200.ops import reference as ref
+
+    # fused-epilogue GEMMs against the separate kernels, one call each
+    for M in (1, 5, 33):
+        Hq, Hkv, D, K = 4, 2, 128, 512
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = (torch.randn((Hq + 2 * Hkv) * D, K, device="cuda") * 0.05).bfloat16()
+        bias = torch.randn((Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+        cos, sin = ref.rope_tables(64, D, 1e4, device="cuda")
+        pos = torch.randint(0, 64, (M,), dtype=torch.int32, device="cuda")
+        slot = torch.randperm(M + 1, device="cuda")[:M].int()
+        outs = []
+        for fused in (True, False):
+            kc = torch.zeros(M + 1, 64, Hkv, D, dtype=torch.bfloat16, device="cuda")
+            vc = torch.zeros_like(kc)
+            qkv = torch.zeros(M, (Hq + 2 * Hkv) * D, dtype=torch.bfloat16, device="cuda")
+            acc = torch.zeros(M, (Hq + 2 * Hkv) * D, device="cuda")
+            tiles = torch.zeros(64, dtype=torch.int32, device="cuda")
+            if fused:
+                F.skinny_gemm_qkv(x, w, acc, tiles, bias, qkv, pos, slot, cos.contiguous(), sin.contiguous(), kc, vc,
+                                  Hq, Hkv)
+                assert int(tiles.abs().sum()) == 0 and float(acc.abs().max()) == 0.0
+            else:
+                F.skinny_gemm(x, w, acc)
+                F.qkv_finalize_rope(acc, bias, qkv, pos, slot, cos.contiguous(), sin.contiguous(), kc, vc, Hq, Hkv, D)
+            outs.append((qkv, kc, vc))
+        for a, b in zip(*outs):
+            assert float((a.float() - b.float()).abs().max()) <= 2e-2 * float(b.float().abs().max()) + 1e-6
+        Fh = 192
+        wgu = (torch.randn(2 * Fh, K, device="cuda") * 0.05).bfloat16()
+        acc = torch.zeros(M, 2 * Fh, device="cuda")
+        tiles = torch.zeros(64, dtype=torch.int32, device="cuda")
+        act = torch.empty(M, Fh, dtype=torch.bfloat16, device="cuda")
+        F.skinny_gemm_swiglu(x, wgu, acc, act, tiles)
+        z = x.float() @ wgu.float().t()
+        want = torch.nn.functional.silu(z[:, :Fh]) * z[:, Fh:]
+        assert float((act.float() - want).norm() / want.norm()) < 1e-2
+        assert int(tiles.abs().sum()) == 0 and float(acc.abs().max()) == 0.0
+    # and the whole decode step with and without them (contiguous and paged caches)
+    cfg = QwenConfig(**dict(TINY, d_model=512, n_heads=4, n_kv_heads=2, d_ff=1024))
+    toks = torch.randint(0, cfg.vocab, (3, 40), device="cuda")
+    for pages in (0, 64):
+        m1 = QwenModel(cfg, device="cuda", seed=2, max_batch=8, max_seq=256, kv_pages=pages)
+        m2 = QwenModel(cfg, device="cuda", seed=2, max_batch=8, max_seq=256, kv_pages=pages)
+        m1.fused_epilogues, m2.fused_epilogues = True, False
+        assert torch.equal(m1.generate(toks, 8), m2.generate(toks, 8))
 
 
 QWEN3 = dict(TINY, qkv_bias=False, qk_norm=True, head_dim_=128, tie_embeddings=False)  # head_dim != d / H
