@@ -246,7 +246,7 @@ class GPT:
                 # x's gradient is complete only after every op of layer i has run
                 # backward, so layer i's parameter gradients are final then
                 x.register_hook(_ReadyHook(ready, f"l{i}"))
-            h = A.rmsnorm(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
+            h, res = A.rmsnorm_residual(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
             qkv = lin(i, "wqkv", h)
             if cfg.qk_norm:
                 qkv = self._qk_norm(i, qkv, Hq, Hkv, D)
@@ -257,11 +257,11 @@ class GPT:
                 from ..parallel.cp import cp_attention
 
                 o = cp_attention(qkv, B, S, Hq, Hkv, D, scale, self.cp)
-            x = lin(i, "wo", o, residual=x)
-            h = A.rmsnorm(x, a[f"l{i}.mlp_norm"], cfg.norm_eps)
+            x = lin(i, "wo", o, residual=res)
+            h, res = A.rmsnorm_residual(x, a[f"l{i}.mlp_norm"], cfg.norm_eps)
             gu = lin(i, "wgu", h)
             act = A.swiglu(gu)
-            x = lin(i, "wd", act, residual=x)
+            x = lin(i, "wd", act, residual=res)
         if sp:
             x = T.sp_gather(x, self.tp)
         if ready is not None and self.last and x.requires_grad:

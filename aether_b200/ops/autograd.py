@@ -77,6 +77,38 @@ def rmsnorm(x, w, eps=1e-6):
     return RMSNormFn.apply(x, w, eps)
 
 
+class RMSNormResidualFn(torch.autograd.Function):
+    """(rmsnorm(x) * w, x) for a pre-norm residual block: the second output
+    is the residual branch (an alias of x). In backward both gradients arrive
+    in one call and the kernel adds the residual gradient into dx as it
+    writes it, so autograd never runs a separate [T, d] add for the two uses
+    of x."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        y, _, rstd = F.rmsnorm(x, w, eps)
+        ctx.save_for_backward(x, w, rstd)
+        return y, x.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy, dres):
+        x, w, rstd = ctx.saved_tensors
+        mg = _main_grad(w)
+        tmp = None
+        if mg is None:
+            tmp = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        if dy is None:
+            dy = torch.zeros_like(x)
+        dx = F.rmsnorm_bwd(dy.contiguous(), x, w, rstd, mg if mg is not None else tmp,
+                           dres=dres.contiguous() if dres is not None else None, accumulate=True)
+        return dx, (tmp.to(w.dtype) if tmp is not None and ctx.needs_input_grad[1] else None), None
+
+
+def rmsnorm_residual(x, w, eps=1e-6):
+    """-> (normed, residual alias of x); see RMSNormResidualFn."""
+    return RMSNormResidualFn.apply(x, w, eps)
+
+
 class LayerNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, eps):
