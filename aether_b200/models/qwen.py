@@ -339,6 +339,16 @@ class QwenModel:
             V = cfg.vocab
             cols = tp.world * self.w.vocab_per if self.vp else V
             tp.prepare_decode(max_batch + 1, cfg.d_model, cols)
+        # the whole decode step as one persistent kernel for batch buckets 1 / 2 / 4
+        self.mega = self._mega_supported()
+        self._mega = None
+        if self.mega:
+            self._mega_setup()
+        # batch buckets that take the one-kernel step by default: measured on a
+        # B200 (Qwen2.5-7B shapes) it wins where a rank's per-layer weights are
+        # small (TP >= 4, batch 1) and loses to the kernel chain at TP 1 and at
+        # batch 2 / 4, where its per-stage reductions bound the weight stream
+        self.mega_batches = {1} if (tp is not None and getattr(tp, "world", 1) >= 4) else set()
 
     # ------------------------------------------------------------------ buffers
     def _auto_splits(self, B: int) -> int:
@@ -549,7 +559,111 @@ class QwenModel:
         acc.zero_()
 
     def _step_body(self, B: int) -> None:
+        if self._mega_for(B):
+            self._decode_mega(B, self.buf["logits"][:B] if self._want_logits else None)
+            return
         (self._decode_body if self.fused_decode else self._decode_body_unfused)(B)
+
+    # ------------------------------------------------------------------ one-kernel decode step
+    def _mega_world(self) -> int:
+        """Ranks the kernel exchanges with: a real tensor-parallel team, else 1
+        (one GPU, or a single-GPU emulation of one rank's shards)."""
+        team = getattr(self.tp, "team", None)
+        return self.tp.world if team is not None else 1
+
+    def _mega_supported(self) -> bool:
+        """Whether the model fits the one-kernel decode step (csrc/decode_mega.cu):
+        head_dim 128, no q/k norm, sliding window or softcap, at most 8 query
+        heads per KV head, and -- under real tensor parallelism -- multicast
+        reduction buffers (the batch bucket must also fit its activation rows in
+        40 KB of shared memory, see _mega_for). AETHER_DECODE_MEGA=0 turns it off."""
+        import os as _os
+
+        cfg = self.cfg
+        if _os.environ.get("AETHER_DECODE_MEGA", "1") == "0" or self.device.type != "cuda":
+            return False
+        if not self.fused_decode or cfg.head_dim != 128 or self.softcap or any(self.win):
+            return False
+        d, f, hq, hkv = cfg.d_model, self.f, self.hq, self.hkv
+        if d % 8 or f % 8 or hq % hkv or hq // hkv > 8:
+            return False
+        if self._mega_world() > 1:
+            team = self.tp.team
+            if not getattr(team, "use_multicast", False) or self.tp.world > 8:
+                return False
+        return True
+
+    def _mega_for(self, B: int) -> bool:
+        if not self.mega or B not in (1, 2, 4) or B not in self.mega_batches:
+            return False
+        if self._want_logits and self._mega_world() > 1:
+            return False  # full logits need the cross-rank gather of the kernel chain
+        return B * max(self.cfg.d_model, self.hq * 128, self.f) * 2 <= 40 * 1024
+
+    def _mega_setup(self) -> None:
+        """Scratch, state and (tensor parallel: symmetric, collectively
+        allocated) exchange buffers of the one-kernel decode step, and the
+        device table of per-layer weight / cache / RoPE pointers."""
+        cfg, w, dev = self.cfg, self.w, self.device
+        L, d = cfg.n_layers, cfg.d_model
+        G = self.hq // self.hkv
+        nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+        bf = torch.bfloat16
+        rows = []
+        for i in range(L):
+            cos, sin = self.rope_cs[i]
+            ptrs = [w.wqkv[i], w.bqkv[i], w.wo[i], w.wgu[i], w.wd[i], w.attn_norm[i], w.mlp_norm[i],
+                    self.cache.k[i], self.cache.v[i], cos, sin]
+            rows.append([0 if t is None else t.data_ptr() for t in ptrs])
+        m = {
+            "table": torch.tensor(rows, dtype=torch.int64, device=dev),
+            "x": torch.zeros(4, d, dtype=bf, device=dev),
+            "x2": torch.zeros(4, d, dtype=bf, device=dev),
+            "q": torch.zeros(4, self.hq * 128, dtype=bf, device=dev),
+            "o": torch.zeros(4, self.hq * 128, dtype=bf, device=dev),
+            "act": torch.zeros(4, self.f, dtype=bf, device=dev),
+            "part": torch.zeros(4 * self.hkv * nsm * G * 130, dtype=torch.float32, device=dev),
+            "pair_ctr": torch.zeros(4 * self.hkv, dtype=torch.int32, device=dev),
+            "state": torch.zeros(64, dtype=torch.int32, device=dev),
+        }
+        world = self._mega_world()
+        if world > 1:
+            team = self.tp.team
+            r0, r1 = team.alloc(4 * d, torch.float32), team.alloc(4 * d, torch.float32)
+            fl, ky = team.alloc(8, torch.int32), team.alloc(8 * 4, torch.int64)
+            for buf in (r0, r1, fl, ky):
+                buf.tensor.zero_()
+            if not (r0.mc_ptr and r1.mc_ptr):  # no NVLS multicast on this system: keep the kernel chain
+                self.mega = False
+            m.update(red0=r0.tensor, red1=r1.tensor, red0_mc=r0.mc_ptr, red1_mc=r1.mc_ptr, flags=fl.tensor,
+                     flag_peers=torch.tensor(fl.peers_host, dtype=torch.int64), keys=ky.tensor,
+                     key_peers=torch.tensor(ky.peers_host, dtype=torch.int64), _bufs=(r0, r1, fl, ky))
+            torch.cuda.synchronize(dev)
+            import torch.distributed as _dist
+
+            _dist.barrier()
+        else:
+            m.update(red0=torch.zeros(4, d, dtype=torch.float32, device=dev),
+                     red1=torch.zeros(4, d, dtype=torch.float32, device=dev), red0_mc=0, red1_mc=0,
+                     flags=torch.zeros(8, dtype=torch.int32, device=dev), flag_peers=torch.zeros(8, dtype=torch.int64),
+                     keys=torch.zeros(32, dtype=torch.int64, device=dev), key_peers=torch.zeros(8, dtype=torch.int64))
+        self._mega = m
+
+    def _decode_mega(self, B: int, logits=None) -> None:
+        """One greedy decode step of B rows in one kernel launch; with logits
+        (fp32 [B, >= head rows]) this rank's head rows' logits are written too."""
+        cfg, w, b, m = self.cfg, self.w, self.buf, self._mega
+        if self.vp:
+            head, rows, col0 = w.lm_head_shard, w.vocab_n, w.vocab_col0
+        else:
+            head, rows, col0 = w.lm_head, cfg.vocab, 0
+        tp = self.tp
+        world = self._mega_world()
+        rank = tp.rank if world > 1 else 0
+        timeout = float(tp.team.timeout_s) if world > 1 else 2.0
+        F.decode_mega(m, w.embed, w.final_norm, head, rows, col0, cfg.d_model, self.hq, self.hkv, self.f,
+                      cfg.norm_eps, self.scale, b["tok"][:B], b["pos"][:B], b["slot"][:B], b["seqlen"][:B],
+                      b["next"][:B], logits, self.cache.k[0], self.page_table, rank, world, timeout)
 
     def _decode_body_unfused(self, B: int) -> None:
         """Decode step with separate norm / RoPE / combine kernels (13 per layer)."""

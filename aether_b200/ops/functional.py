@@ -484,6 +484,20 @@ def skinny_gemm_swiglu(x, w, acc, act, tile_cnt, splits=0):
     return act
 
 
+def decode_mega(m, embed, final_norm, head, vocab_rows, vocab_col0, d, hq, hkv, f, eps, scale, tok, pos, slot,
+                seqlen, next_tok, logits, cache0, page_table, rank, world, timeout_s):
+    """The whole greedy decode step in one persistent kernel (csrc/decode_mega.cu);
+    ``m`` holds the layer table, scratch, state and exchange buffers built by
+    QwenModel._mega_setup. CUDA only (the kernel chain is the portable path)."""
+    if not _cuda(embed):
+        raise RuntimeError("decode_mega runs on CUDA devices only")
+    C().decode_mega(m["table"], embed, final_norm, head, int(vocab_rows), int(vocab_col0), int(d), int(hq), int(hkv),
+                    int(f), float(eps), float(scale), tok, pos, slot, seqlen, next_tok, logits, cache0, page_table,
+                    m["x"], m["x2"], m["q"], m["o"], m["act"], m["part"], m["pair_ctr"], m["red0"], m["red1"],
+                    int(m["red0_mc"]), int(m["red1_mc"]), m["flags"], m["flag_peers"], m["keys"], m["key_peers"],
+                    int(rank), int(world), m["state"], float(timeout_s), m.get("trace"), int(m.get("debug", 0)))
+
+
 def skinny_gemm_qkv(x, w, acc, tile_cnt, bias, qkv, pos, slot, cos_t, sin_t, k_cache, v_cache, Hq, Hkv,
                     page_table=None, splits=0):
     """The decode QKV projection and its epilogue in one GEMM (head_dim 128):

@@ -12,7 +12,8 @@
 //                 row: tcgen05.ld of its S row, masking,
 //                 online softmax (max / exp2 / sum in registers), P written back
 //                 as bf16 over the S columns (tcgen05.st), and O rescaled in
-//                 TMEM only when the row maximum actually grew
+//                 TMEM only when the row maximum outgrows the exponent base
+//                 by more than 2^8 (lazy rescaling)
 // TMEM: per sub-tile an S/P region (128 columns) and an O accumulator (128).
 // The MMA issuer interleaves the sub-tiles (PV of one, QK of the other) so the
 // tensor core stays busy while each warpgroup runs its softmax.
@@ -42,6 +43,7 @@ constexpr int kThreads = 320;  // producer, MMA, two softmax warpgroups
 constexpr int TILE_BYTES = 128 * D * 2;  // 32 KB: [128 rows][128 d] as two 128B-swizzled halves
 constexpr int kSmem = TILE_BYTES * (2 + 2 * KV_STAGES) + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;  // base moves when the row max grows by > 2^8
 
 struct Params {
   __nv_bfloat16* out;
@@ -91,6 +93,32 @@ __device__ __forceinline__ float ex2_poly(float x) {
   const float f = x - (t - 12582912.f);
   const float p = fmaf(fmaf(fmaf(0.055008791f, f, 0.24221075f), f, 0.69328290f), f, 1.f);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Blackwell's three-input max and packed two-lane fp32 FMA / add: half the
+// issue slots of the scalar forms in the softmax's per-score work.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 template <bool kPoly>
@@ -256,20 +284,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       tc_fence_after();
+      // Scores stay in raw units (the softmax scale is folded into the
+      // exponent's FMA below); with a softcap they are capped logits in log2 units.
       float s[BN];
+      {
+        uint32_t r[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + lane_off + c * 32, r);
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
         tmem_ld_wait();
         if (p.cap_in > 0.f) {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) s[c * 32 + t] = p.cap_out * tanh_sfu(__uint_as_float(r[t]) * p.cap_in);
+          for (int t = 0; t < BN; ++t) s[t] = p.cap_out * tanh_sfu(__uint_as_float(r[t]) * p.cap_in);
         } else {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(r[t]) * p.scale_log2;
+          for (int t = 0; t < BN; ++t) s[t] = __uint_as_float(r[t]);
         }
       }
+      const float sc = p.cap_in > 0.f ? 1.f : p.scale_log2;
       const int key0 = j * BN;
       const bool need_mask = (key0 + BN > p.Sk) || (p.causal && key0 + BN - 1 > qsub0 + p.causal_offset);
       if (need_mask) {
@@ -286,36 +317,56 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (key0 + t < lo) s[t] = -INFINITY;
         }
       }
-      // row max and sum over eight independent accumulators (a single chain
-      // would serialise 128 dependent max / 64 dependent adds per tile)
+      // row max over eight independent accumulators (a single chain would
+      // serialise 128 dependent max operations per tile)
+      // (three-input max: two new scores per instruction)
       float m8[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
 #pragma unroll
-      for (int t = 0; t < BN; ++t) m8[t & 7] = fmaxf(m8[t & 7], s[t]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      const float mn = fmaxf(m, mx);
+      for (int t = 0; t < BN; t += 2) m8[(t >> 1) & 7] = max3f(m8[(t >> 1) & 7], s[t], s[t + 1]);
+      const float mx = sc * max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+      // Lazy rescaling: the exponent base only moves when the row maximum
+      // grows by more than 2^8 over it. Until then probabilities may reach
+      // 2^8 (exact in fp32 / bf16 range), and O and l share the stale base,
+      // so O / l is unchanged; the TMEM rescale of O (128 loads, multiplies
+      // and stores per row) drops out of nearly every tile.
+      const bool grow = mx > m + kRescaleLog2;
+      const float mn = grow ? mx : m;
+      const float alpha = grow ? ex2_sfu(m - mn) : 1.f;
       const float base = mn == -INFINITY ? 0.f : mn;
-      const float alpha = ex2_sfu(m - base);
-      float r8[8];
+      // exponent arguments and row sums two at a time (packed f32x2 FMA / add)
+      const uint64_t sc2 = pack_f32x2(sc, sc), nb2 = pack_f32x2(-base, -base);
+      uint64_t r4[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) r8[u] = 0.f;
-      uint32_t pk[BN / 2];
+      for (int u = 0; u < 4; ++u) r4[u] = 0ull;
+      // P_j goes over the S_j columns as each half is ready (S_j landing means
+      // PV_{j-1}, which read P_{j-1} there, has completed), which also frees
+      // the half's score registers early.
 #pragma unroll
-      for (int t = 0; t < BN; t += 2) {
-        float a0, a1;
-        if (kPoly && ((t >> 1) & 3) == 3) {  // a quarter of the exponentials on the FMA pipe
-          a0 = ex2_poly(s[t] - base);
-          a1 = ex2_poly(s[t + 1] - base);
-        } else {
-          a0 = ex2_sfu(s[t] - base);
-          a1 = ex2_sfu(s[t + 1] - base);
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int t = 64 * hf; t < 64 * hf + 64; t += 2) {
+          float x0, x1;
+          unpack_f32x2(fma_f32x2(pack_f32x2(s[t], s[t + 1]), sc2, nb2), x0, x1);
+          float a0, a1;
+          if (kPoly && ((t >> 1) & 3) == 3) {  // a quarter of the exponentials on the FMA pipe
+            a0 = ex2_poly(x0);
+            a1 = ex2_poly(x1);
+          } else {
+            a0 = ex2_sfu(x0);
+            a1 = ex2_sfu(x1);
+          }
+          r4[(t >> 1) & 3] = add_f32x2(r4[(t >> 1) & 3], pack_f32x2(a0, a1));
+          pk[(t - 64 * hf) / 2] = pack_bf16(a0, a1);
         }
-        r8[(t >> 1) & 7] += a0 + a1;
-        pk[t / 2] = pack_bf16(a0, a1);
+        tmem_st32(tS + lane_off + 32 * hf, pk);
       }
-      const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
+      const uint64_t r2 = add_f32x2(add_f32x2(r4[0], r4[1]), add_f32x2(r4[2], r4[3]));
+      float rs0, rs1;
+      unpack_f32x2(r2, rs0, rs1);
+      const float rs = rs0 + rs1;
       l = l * alpha + rs;
       m = mn;
       // PV_{j-1} must have landed before O may be touched; every PV completion
@@ -327,8 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         o_phase ^= 1u;
       }
-      // Rescale O only if some row of this warp saw its maximum grow.
-      const bool need = (j > 0) && (alpha != 1.f);
+      // Rescale O only if some row of this warp moved its base.
+      const bool need = (j > 0) && grow;
       if (__any_sync(0xffffffffu, need)) {
         __syncwarp();
         tc_fence_after();
@@ -341,15 +392,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
           tmem_st32(tO + lane_off + c * 32, r);
         }
-      }
-      {
-        uint32_t r[32];
-#pragma unroll
-        for (int t = 0; t < 32; ++t) r[t] = pk[t];
-        tmem_st32(tS + lane_off, r);
-#pragma unroll
-        for (int t = 0; t < 32; ++t) r[t] = pk[32 + t];
-        tmem_st32(tS + lane_off + 32, r);
       }
       tmem_st_wait();
       tc_fence_before();

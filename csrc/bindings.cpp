@@ -69,6 +69,16 @@ void skinny_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor acc, at::Tensor tile
                      at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t,
                      at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv,
                      std::optional<at::Tensor> page_table, int64_t splits);
+// decode_mega.cu
+void decode_mega(at::Tensor layers, at::Tensor embed, at::Tensor final_norm, at::Tensor head, int64_t vocab_rows,
+                 int64_t vocab_col0, int64_t d, int64_t hq, int64_t hkv, int64_t f, double eps, double scale,
+                 at::Tensor tok, at::Tensor pos, at::Tensor slot, at::Tensor seqlen, at::Tensor next,
+                 std::optional<at::Tensor> logits, at::Tensor cache0, std::optional<at::Tensor> page_table,
+                 at::Tensor x, at::Tensor x2, at::Tensor q, at::Tensor o, at::Tensor act, at::Tensor part,
+                 at::Tensor pair_ctr, at::Tensor red0, at::Tensor red1, int64_t red0_mc, int64_t red1_mc,
+                 at::Tensor flags, at::Tensor flag_peers, at::Tensor keys, at::Tensor key_peers, int64_t rank,
+                 int64_t world, at::Tensor state, double timeout_s, std::optional<at::Tensor> trace,
+                 int64_t debug);
 // comm.cu
 void team_barrier(at::Tensor peer_sig_ptrs, at::Tensor my_sig, at::Tensor epoch, int64_t rank, int64_t world,
                   double timeout_s);
@@ -153,6 +163,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("team_barrier", &aether::team_barrier);
   m.def("skinny_gemm_swiglu", &aether::skinny_gemm_swiglu);
   m.def("skinny_gemm_qkv", &aether::skinny_gemm_qkv);
+  m.def("decode_mega", &aether::decode_mega, "layers"_a, "embed"_a, "final_norm"_a, "head"_a, "vocab_rows"_a,
+        "vocab_col0"_a, "d"_a, "hq"_a, "hkv"_a, "f"_a, "eps"_a, "scale"_a, "tok"_a, "pos"_a, "slot"_a, "seqlen"_a,
+        "next"_a, "logits"_a, "cache0"_a, "page_table"_a, "x"_a, "x2"_a, "q"_a, "o"_a, "act"_a, "part"_a,
+        "pair_ctr"_a, "red0"_a, "red1"_a, "red0_mc"_a, "red1_mc"_a, "flags"_a, "flag_peers"_a, "keys"_a,
+        "key_peers"_a, "rank"_a, "world"_a, "state"_a, "timeout_s"_a, "trace"_a = pybind11::none(), "debug"_a = 0);
   m.def("tp_vocab_argmax", &aether::tp_vocab_argmax);
   m.def("tp_put_cols", &aether::tp_put_cols);
   m.def("tp_push_reduce", &aether::tp_push_reduce, "acc"_a, "y"_a, "bias"_a, "res"_a, "w"_a, "h"_a, "eps"_a,

@@ -117,6 +117,51 @@ def check_tp_qwen(info):
     print(f"OK tp_qwen agree={agree:.3f} mc={tp.team.has_multicast}", flush=True)
 
 
+def check_tp_mega(info):
+    """The one-kernel TP decode step (multimem reductions + flag barriers inside
+    the kernel) against the TP kernel chain: per-rank vocabulary-slice logits
+    and merged greedy tokens, batch buckets 1 / 2 / 4, teacher-forced."""
+    from aether_b200.models.qwen import QwenConfig, QwenModel
+    from aether_b200.parallel.tp import TensorParallel
+
+    cfg = QwenConfig(vocab=2048, d_model=1024, n_layers=3, n_heads=8, n_kv_heads=2, d_ff=2048, max_seq=512,
+                     init_std=0.05)
+    tp = TensorParallel(info)
+    ma = QwenModel(cfg, device=info.device, seed=5, max_batch=4, max_seq=512, tp=tp)
+    mb = QwenModel(cfg, device=info.device, seed=5, max_batch=4, max_seq=512, tp=tp)
+    ma.mega_batches = {1, 2, 4}
+    mb.mega = False
+    if not ma.mega:
+        print("OK tp_mega skipped: no multicast reduction buffers", flush=True)
+        return
+    w = ma.w
+    agree = []
+    for B in (1, 2, 4):
+        g = torch.Generator(device=info.device).manual_seed(20 + B)
+        prompts = torch.randint(0, cfg.vocab, (B, 130), device=info.device, generator=g)
+        tok = mb.prefill(prompts)
+        ma.prefill(prompts)
+        pos = torch.full((B,), 130, dtype=torch.int32, device=info.device)
+        for step in range(4):
+            b = ma.buf
+            b["tok"][:B].copy_(tok)
+            b["pos"][:B].copy_(pos)
+            b["seqlen"][:B].copy_(pos + 1)
+            b["slot"][:B].copy_(torch.arange(B, dtype=torch.int32, device=info.device))
+            loc = torch.zeros(B, w.vocab_per, device=info.device)
+            ma._decode_mega(B, loc)
+            na = b["next"][:B].clone()
+            nb = mb.decode_step(tok, pos, use_graph=step % 2 == 1, want_logits=True).clone()
+            full = mb.buf["logits"][:B, w.vocab_col0 : w.vocab_col0 + w.vocab_n]
+            err = float((loc[:, : w.vocab_n] - full).abs().max())
+            assert err <= 2e-2 * float(full.abs().max()) + 1e-5, (B, step, err)
+            agree.append(float((na == nb).float().mean()))
+            tok, pos = nb, pos + 1
+    assert sum(agree) / len(agree) > 0.9, agree
+    assert _ext.check_status() == 0
+    print(f"OK tp_mega agree={sum(agree) / len(agree):.3f}", flush=True)
+
+
 def check_pp(info):
     """1F1B pipeline over NCCL p2p (one stage per rank) against one GPU."""
     from aether_b200.models.gpt import GPT, GPTConfig
@@ -296,7 +341,8 @@ def main():
     from aether_b200.parallel.symm import SymmTeam
 
     team = SymmTeam(info)
-    which = sys.argv[1:] or ["allreduce", "dp", "overlap_dp", "tp", "pp", "tp_train", "fsdp", "cp", "ep", "mla_tp"]
+    which = sys.argv[1:] or ["allreduce", "dp", "overlap_dp", "tp", "tp_mega", "pp", "tp_train", "fsdp", "cp", "ep",
+                             "mla_tp"]
     if "allreduce" in which:
         check_allreduce(team, info)
     if "dp" in which:
@@ -305,6 +351,8 @@ def main():
         check_overlap_dp(info)
     if "tp" in which:
         check_tp_qwen(info)
+    if "tp_mega" in which:
+        check_tp_mega(info)
     if "pp" in which:
         check_pp(info)
     if "tp_train" in which:

@@ -32,7 +32,7 @@ def test_multigpu_nvlink_paths():
            os.path.join(ROOT, "tests", "multigpu_worker.py")]
     out = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert out.returncode == 0, out.stdout[-4000:] + out.stderr[-4000:]
-    assert out.stdout.count("OK ") >= 9 * n
+    assert out.stdout.count("OK ") >= 10 * n
 
 
 def _gloo_dp_worker(rank, world, port, q):

@@ -126,6 +126,7 @@ def test_gpu_fused_gemm_epilogues_match_separate_kernels():
         m1 = QwenModel(cfg, device="cuda", seed=2, max_batch=8, max_seq=256, kv_pages=pages)
         m2 = QwenModel(cfg, device="cuda", seed=2, max_batch=8, max_seq=256, kv_pages=pages)
         m1.fused_epilogues, m2.fused_epilogues = True, False
+        m1.mega = m2.mega = False  # exercise the kernel chain (the one-kernel step has its own tests)
         assert torch.equal(m1.generate(toks, 8), m2.generate(toks, 8))
 
 
