@@ -344,11 +344,16 @@ class QwenModel:
         self._mega = None
         if self.mega:
             self._mega_setup()
-        # batch buckets that take the one-kernel step by default: measured on a
-        # B200 (Qwen2.5-7B shapes) it wins where a rank's per-layer weights are
-        # small (TP >= 4, batch 1) and loses to the kernel chain at TP 1 and at
-        # batch 2 / 4, where its per-stage reductions bound the weight stream
-        self.mega_batches = {1} if (tp is not None and getattr(tp, "world", 1) >= 4) else set()
+        # batch buckets that take the one-kernel step: none unless
+        # AETHER_DECODE_MEGA=force. Measured on B200s at batch 1: one GPU
+        # holding one TP=8 rank's Qwen2.5-7B shards 1.245 ms per step against
+        # 1.367 for the kernel chain (TP=4 shards: +2 %), but Qwen2.5-7B whole
+        # 3.57 against 3.36, Qwen2.5-1.5B 1.72 against 1.53, real TP=8 2.21
+        # against 1.76 (its in-kernel cross-rank barriers cost more than the
+        # chain's push reductions), and batch 2 / 4 slower throughout.
+        import os as _os
+        forced = _os.environ.get("AETHER_DECODE_MEGA") == "force"
+        self.mega_batches = {1, 2, 4} if forced else set()
 
     # ------------------------------------------------------------------ buffers
     def _auto_splits(self, B: int) -> int:
@@ -576,7 +581,8 @@ class QwenModel:
         head_dim 128, no q/k norm, sliding window or softcap, at most 8 query
         heads per KV head, and -- under real tensor parallelism -- multicast
         reduction buffers (the batch bucket must also fit its activation rows in
-        40 KB of shared memory, see _mega_for). AETHER_DECODE_MEGA=0 turns it off."""
+        40 KB of shared memory, see _mega_for). AETHER_DECODE_MEGA=0 skips even
+        its buffers; =force makes decode use it for every bucket it supports."""
         import os as _os
 
         cfg = self.cfg
@@ -598,7 +604,8 @@ class QwenModel:
             return False
         if self._want_logits and self._mega_world() > 1:
             return False  # full logits need the cross-rank gather of the kernel chain
-        return B * max(self.cfg.d_model, self.hq * 128, self.f) * 2 <= 40 * 1024
+        return (B * max(self.cfg.d_model, self.hq * 128, self.f) * 2 <= 40 * 1024
+                and B * self.hq * 1024 <= 40 * 1024)
 
     def _mega_setup(self) -> None:
         """Scratch, state and (tensor parallel: symmetric, collectively

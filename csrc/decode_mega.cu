@@ -6,7 +6,7 @@
 // pays a launch, a ramp and a tail for each of ~9 dependent kernels per layer.
 // Here one CTA per SM lives for the whole step:
 //   warp 14     : producer -- streams this CTA's share of every weight matrix
-//                 (contiguous row ranges, 1-D cp.async.bulk) through a 4-stage
+//                 (contiguous row ranges, 1-D cp.async.bulk) through a 3-stage
 //                 shared-memory ring, in the exact order the consumers use
 //                 them, running ahead ACROSS phase boundaries: weights do not
 //                 depend on activations, so the next phase's rows are already
@@ -53,10 +53,10 @@ using bf16 = __nv_bfloat16;
 constexpr int kConsumerWarps = 14;
 constexpr int kConsumers = kConsumerWarps * 32;  // 448
 constexpr int kThreads = kConsumers + 32;        // + producer warp
-constexpr int kStages = 4;
-constexpr int kSlot = 40 * 1024;   // one ring stage: whole weight rows
+constexpr int kStages = 3;
+constexpr int kSlot = 56 * 1024;   // one ring stage: whole weight rows
 constexpr int kUnion = 40 * 1024;  // activation rows [B][K] bf16, or attention staging
-constexpr int kKeys = 64;          // keys per attention chunk
+constexpr int kKeys = 32;          // keys per attention chunk (one per lane in the softmax)
 constexpr int kMaxG = 8;           // query heads per KV head
 constexpr int kMaxB = 4;
 constexpr int kPartStride = 2 + 128;  // attention partial: m, l, o[128]
@@ -366,13 +366,20 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
 }
 
 template <int B>
+__device__ void attn_prefetch(const Smem& s, const Params& p, int layer);
+
+template <int B>
 __device__ void producer(const Smem& s, const Params& p) {
   Cursor ld{0, 0, -1, 0}, pf{0, 0, -1, 0};
   int64_t ld_bytes = 0, pf_bytes = 0;
   bool pf_more = true;
   Block b{}, q{};
-  int it = 0;
+  int it = 0, layer_seen = -1;
   while (cursor_next<B>(p, ld, b)) {
+    if (ld.layer < p.L && ld.layer != layer_seen) {  // a new layer: its attention K / V into L2
+      layer_seen = ld.layer;
+      attn_prefetch<B>(s, p, layer_seen);
+    }
     while (pf_more && !(p.debug & 1) && pf_bytes < ld_bytes + kPrefetch) {
       pf_more = cursor_next<B>(p, pf, q);
       if (pf_more) {
@@ -604,109 +611,156 @@ __device__ void zero_slice(const Params& p, float* buf) {
 }
 
 // ---------------------------------------------------------------- attention
+// Split-K decode attention. Each (row, KV head) pair gets S = CTAs / pairs
+// CTAs (or, with more pairs than CTAs, a CTA takes whole pairs), each a
+// contiguous range of 32-key chunks; the next chunk's K / V are loaded into
+// registers while the current one is scored, then stored to the other half of
+// a double buffer. Every working CTA writes one partial (running max m, sum l
+// and unnormalised o for each of its G query heads); the o_proj prologue
+// merges them (merge_attention), so no CTA waits on another here.
+struct AttnSplit {
+  int S;     // CTAs per pair (1 when pairs >= CTAs)
+  bool many;
+};
+template <int B>
+__device__ __forceinline__ AttnSplit attn_split(const Params& p) {
+  const int P = B * p.hkv, nb = gridDim.x;
+  AttnSplit a;
+  a.many = P >= nb;
+  a.S = a.many ? 1 : nb / P;
+  return a;
+}
+__device__ __forceinline__ int attn_used(int S, int n) {  // splits that get keys: >= 2 chunks each
+  return max(1, min(S, (n + 2 * kKeys - 1) / (2 * kKeys)));
+}
+
+// Producer side: pull this CTA's K / V chunks of layer `layer`'s attention
+// into L2 while the QKV phase runs (the row that phase appends is re-read
+// from L2 anyway). Only where a KV head's keys are contiguous (one KV head
+// per rank); runs split at page boundaries.
+template <int B>
+__device__ void attn_prefetch(const Smem& s, const Params& p, int layer) {
+  if (p.hkv != 1) return;
+  const Layer& ly = p.layers[layer];
+  const AttnSplit as = attn_split<B>(p);
+  const int P = B * p.hkv, nb = gridDim.x;
+  int pi = as.many ? (int)blockIdx.x : (int)blockIdx.x / as.S;
+  const int sidx = as.many ? 0 : (int)blockIdx.x % as.S;
+  const int run = p.pm.table != nullptr ? (1 << p.pm.shift) : 1 << 30;
+  for (; pi < P; pi += as.many ? nb : P) {
+    const int b = pi / p.hkv;
+    const int n = s.rows[3 * kMaxB + b], seq = s.rows[2 * kMaxB + b];
+    const int nch = (n + kKeys - 1) / kKeys, Su = attn_used(as.S, n);
+    if (sidx < Su) {
+      const int t1 = min(n, (sidx + 1) * nch / Su * kKeys);
+      for (int t = sidx * nch / Su * kKeys; t < t1;) {
+        const int len = min(t1 - t, run - (t & (run - 1)));
+        const int64_t off = dec::kv_offset(p.pm, seq, t, p.slot_stride, p.pos_stride);
+        prefetch_l2(ly.kc + off, (uint32_t)len * 256);
+        prefetch_l2(ly.vc + off, (uint32_t)len * 256);
+        t += len;
+      }
+    }
+    if (!as.many) break;
+  }
+}
+
 template <int B>
 __device__ bool attention_phase(const Smem& s, const Params& p, const Layer& ly) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = p.hq / p.hkv, P = B * p.hkv, nb = gridDim.x;
-  bf16* sK = reinterpret_cast<bf16*>(s.uni);
-  bf16* sV = sK + kKeys * 128;
-  float* sq = reinterpret_cast<float*>(sV + kKeys * 128);  // [G][128]
-  float* sp = sq + kMaxG * 128;                            // [G][64] scores / probabilities
-  float* sm = sp + kMaxG * kKeys;                          // m [G], l [G], alpha [G]
-  // P >= CTAs: each CTA takes whole (row, KV head) pairs; otherwise each pair
-  // gets S = CTAs / P CTAs, each a contiguous range of 64-key chunks
-  const bool many = P >= nb;
-  const int S = many ? 1 : nb / P;
-  int pi = many ? (int)blockIdx.x : (int)blockIdx.x / S;
-  const int sidx = many ? 0 : (int)blockIdx.x % S;
-  for (; pi < P; pi += many ? nb : P) {
+  bf16* kvbuf = reinterpret_cast<bf16*>(s.uni);  // [2 buffers][K | V][kKeys][128]
+  float* sq = reinterpret_cast<float*>(kvbuf + 2 * 2 * kKeys * 128);  // [G][128]
+  float* sp = sq + kMaxG * 128;                                      // [G][kKeys]
+  float* sm = sp + kMaxG * kKeys;                                    // m [G], l [G], alpha [G]
+  const AttnSplit as = attn_split<B>(p);
+  int pi = as.many ? (int)blockIdx.x : (int)blockIdx.x / as.S;
+  const int sidx = as.many ? 0 : (int)blockIdx.x % as.S;
+  constexpr int kPieces = 2 * kKeys * 16, kPer = (kPieces + kConsumers - 1) / kConsumers;
+  for (; pi < P; pi += as.many ? nb : P) {
     const int b = pi / p.hkv, kvh = pi % p.hkv;
-    const int n = s.rows[3 * kMaxB + b];
+    const int n = s.rows[3 * kMaxB + b], seq = s.rows[2 * kMaxB + b];
     const int nch = (n + kKeys - 1) / kKeys;
-    const int Su = min(S, nch);
+    const int Su = attn_used(as.S, n);
     if (sidx < Su) {
       const int c0 = sidx * nch / Su, c1 = (sidx + 1) * nch / Su;
-      const int seq = s.rows[2 * kMaxB + b];
-      for (int i = tid; i < G * 16; i += kConsumers) {
-        const int g = i >> 4, c = i & 15;
-        float v[8];
-        unpack8f(ldcg16(p.q + (int64_t)b * p.hq * 128 + (kvh * G + g) * 128 + 8 * c), v);
+      uint4 qreg = make_uint4(0u, 0u, 0u, 0u);
+      if (tid < G * 16) qreg = ldcg16(p.q + (int64_t)b * p.hq * 128 + (kvh * G + (tid >> 4)) * 128 + 8 * (tid & 15));
+      auto load_chunk = [&](int ch, uint4 (&vb)[kPer]) {
+        const int t0 = ch * kKeys;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) sq[g * 128 + 8 * c + e] = v[e] * p.scale_log2;
-      }
+        for (int j = 0; j < kPer; ++j) {
+          const int i = tid + j * kConsumers;
+          vb[j] = make_uint4(0u, 0u, 0u, 0u);
+          if (i < kPieces) {
+            const int kv = i / (kKeys * 16), rem = i % (kKeys * 16), key = rem >> 4, c = rem & 15;
+            const int t = t0 + key;
+            if (t < n)
+              vb[j] = ldcg16((kv ? ly.vc : ly.kc) + dec::kv_offset(p.pm, seq, t, p.slot_stride, p.pos_stride) +
+                             kvh * 128 + 8 * c);
+          }
+        }
+      };
+      auto store_chunk = [&](int buf, const uint4 (&vb)[kPer]) {
+        uint4* dst = reinterpret_cast<uint4*>(kvbuf + buf * 2 * kKeys * 128);
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int i = tid + j * kConsumers;
+          if (i < kPieces) dst[i] = vb[j];  // K pieces then V pieces, [key][16] each
+        }
+      };
+      uint4 vb[kPer];
+      load_chunk(c0, vb);
       if (tid < G) {
         sm[tid] = -INFINITY;
         sm[kMaxG + tid] = 0.f;
       }
+      if (tid < G * 16) {
+        float v[8];
+        unpack8f(qreg, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sq[(tid >> 4) * 128 + 8 * (tid & 15) + e] = v[e] * p.scale_log2;
+      }
+      store_chunk(0, vb);
       ev(p, s.misc, 5);
       float2 oacc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       for (int ch = c0; ch < c1; ++ch) {
-        const int t0 = ch * kKeys;
-        consumer_bar();  // previous chunk's K / V / probabilities fully used
-        {
-          // 2 x 64 keys x 16 pieces of 16 B: every load of this thread is in
-          // flight before the first store into shared memory
-          constexpr int kPieces = 2 * kKeys * 16, kPer = (kPieces + kConsumers - 1) / kConsumers;
-          uint4 vb[kPer];
-#pragma unroll
-          for (int j = 0; j < kPer; ++j) {
-            const int i = tid + j * kConsumers;
-            vb[j] = make_uint4(0u, 0u, 0u, 0u);
-            if (i < kPieces) {
-              const int kv = i / (kKeys * 16), rem = i % (kKeys * 16), key = rem >> 4, c = rem & 15;
-              const int t = t0 + key;
-              if (t < n)
-                vb[j] = ldcg16((kv ? ly.vc : ly.kc) + dec::kv_offset(p.pm, seq, t, p.slot_stride, p.pos_stride) +
-                               kvh * 128 + 8 * c);
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < kPer; ++j) {
-            const int i = tid + j * kConsumers;
-            if (i < kPieces) {
-              const int kv = i / (kKeys * 16), rem = i % (kKeys * 16);
-              reinterpret_cast<uint4*>(kv ? sV : sK)[rem] = vb[j];
-            }
-          }
-        }
+        const int buf = (ch - c0) & 1, t0 = ch * kKeys;
+        if (ch + 1 < c1) load_chunk(ch + 1, vb);  // in flight while this chunk is scored
         consumer_bar();
+        const bf16* sK = kvbuf + buf * 2 * kKeys * 128;
+        const bf16* sV = sK + kKeys * 128;
         ev(p, s.misc, 6);
-        // one thread per (query head, key): a 128-long dot product from shared
-        // memory, its 16-B pieces visited in a key-rotated order (fewer bank
-        // conflicts between the threads of a warp, which read different keys)
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int item = tid + k * kConsumers;
-          if (item < G * kKeys) {
-            const int g = item / kKeys, key = item % kKeys;
-            const uint4* kr = reinterpret_cast<const uint4*>(sK + key * 128);
-            const float4* qg = reinterpret_cast<const float4*>(sq + g * 128);
-            float a0 = 0.f, a1 = 0.f;
+        // one thread per (query head, key): a 128-long dot product, 16-B pieces
+        // in a key-rotated order (fewer bank conflicts between a warp's keys)
+        for (int item = tid; item < G * kKeys; item += kConsumers) {
+          const int g = item / kKeys, key = item % kKeys;
+          const uint4* kr = reinterpret_cast<const uint4*>(sK + key * 128);
+          const float4* qg = reinterpret_cast<const float4*>(sq + g * 128);
+          float a0 = 0.f, a1 = 0.f;
 #pragma unroll 4
-            for (int c = 0; c < 16; ++c) {
-              const int cc = (c + key) & 15;
-              float kf[8];
-              unpack8f(kr[cc], kf);
-              const float4 q0 = qg[2 * cc], q1 = qg[2 * cc + 1];
-              a0 = fmaf(kf[0], q0.x, a0); a1 = fmaf(kf[1], q0.y, a1);
-              a0 = fmaf(kf[2], q0.z, a0); a1 = fmaf(kf[3], q0.w, a1);
-              a0 = fmaf(kf[4], q1.x, a0); a1 = fmaf(kf[5], q1.y, a1);
-              a0 = fmaf(kf[6], q1.z, a0); a1 = fmaf(kf[7], q1.w, a1);
-            }
-            sp[g * kKeys + key] = (t0 + key < n) ? a0 + a1 : -INFINITY;
+          for (int c = 0; c < 16; ++c) {
+            const int cc = (c + key) & 15;
+            float kf[8];
+            unpack8f(kr[cc], kf);
+            const float4 q0 = qg[2 * cc], q1 = qg[2 * cc + 1];
+            a0 = fmaf(kf[0], q0.x, a0); a1 = fmaf(kf[1], q0.y, a1);
+            a0 = fmaf(kf[2], q0.z, a0); a1 = fmaf(kf[3], q0.w, a1);
+            a0 = fmaf(kf[4], q1.x, a0); a1 = fmaf(kf[5], q1.y, a1);
+            a0 = fmaf(kf[6], q1.z, a0); a1 = fmaf(kf[7], q1.w, a1);
           }
+          sp[g * kKeys + key] = (t0 + key < n) ? a0 + a1 : -INFINITY;
         }
         consumer_bar();
         ev(p, s.misc, 7);
-        if (warp < G) {
+        if (warp < G) {  // kKeys == 32: one score per lane
           const int g = warp;
-          const float s0 = sp[g * kKeys + lane], s1 = sp[g * kKeys + lane + 32];
-          const float cm = warp_max(fmaxf(s0, s1));
+          const float sc = sp[g * kKeys + lane];
+          const float cm = warp_max(sc);
           const float mo = sm[g], mn = fmaxf(mo, cm);
-          const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
-          sp[g * kKeys + lane] = p0;
-          sp[g * kKeys + lane + 32] = p1;
-          const float ls = warp_sum(p0 + p1);
+          const float pr = exp2f(sc - mn);
+          sp[g * kKeys + lane] = pr;
+          const float ls = warp_sum(pr);
           if (lane == 0) {
             const float al = exp2f(mo - mn);
             sm[2 * kMaxG + g] = al;
@@ -734,103 +788,110 @@ __device__ bool attention_phase(const Smem& s, const Params& p, const Layer& ly)
             oacc[k] = make_float2(ox, oy);
           }
         }
+        if (ch + 1 < c1) store_chunk(buf ^ 1, vb);  // the other buffer: last read two chunks ago
       }
       consumer_bar();
       ev(p, s.misc, 9);
-      const int64_t obase = (int64_t)b * p.hq * 128 + (int64_t)kvh * G * 128;
-      if (Su == 1) {
+      float* part = p.part + ((int64_t)pi * nb + sidx) * G * kPartStride;
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int item = tid + k * kConsumers;
-          if (item < G * 64) {
-            const int g = item >> 6, d2 = item & 63;
-            const float inv = 1.f / sm[kMaxG + g];
-            reinterpret_cast<uint32_t*>(p.o + obase + g * 128)[d2] = pack_bf16(oacc[k].x * inv, oacc[k].y * inv);
-          }
-        }
-      } else {
-        float* part = p.part + ((int64_t)pi * nb + sidx) * G * kPartStride;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int item = tid + k * kConsumers;
-          if (item < G * 64) {
-            const int g = item >> 6, d2 = item & 63;
-            reinterpret_cast<float2*>(part + g * kPartStride + 2)[d2] = oacc[k];
-          }
-        }
-        if (tid < G) {
-          part[tid * kPartStride] = sm[tid];
-          part[tid * kPartStride + 1] = sm[kMaxG + tid];
-        }
-        __threadfence();
-        consumer_bar();
-        if (tid == 0) {
-          const int prev = atomicAdd(&p.pair_ctr[pi], 1);
-          s.misc[1] = prev == Su - 1;
-          if (prev == Su - 1) p.pair_ctr[pi] = 0;
-          __threadfence();
-        }
-        consumer_bar();
-        if (s.misc[1]) {
-          // log-sum-exp merge of the Su partials: split weights first (all
-          // loads issued together), then each (head, dim pair) sums Su rows
-          const float* p0 = p.part + (int64_t)pi * nb * G * kPartStride;
-          float* wts = reinterpret_cast<float*>(sK);  // [G][Su] weights, then [G][Su] l
-          float* lsb = wts + G * Su;
-          for (int i = tid; i < G * Su; i += kConsumers) {
-            const int g = i / Su, sp2 = i - g * Su;
-            const float* pe = p0 + (sp2 * G + g) * kPartStride;
-            wts[i] = ldcg_f(pe);
-            lsb[i] = ldcg_f(pe + 1);
-          }
-          consumer_bar();
-          if (warp < G) {
-            const int g = warp;
-            float M = -INFINITY;
-            for (int sp2 = lane; sp2 < Su; sp2 += 32) M = fmaxf(M, wts[g * Su + sp2]);
-            M = warp_max(M);
-            float L = 0.f;
-            for (int sp2 = lane; sp2 < Su; sp2 += 32) {
-              const float w = exp2f(wts[g * Su + sp2] - M);
-              wts[g * Su + sp2] = w;
-              L += w * lsb[g * Su + sp2];
-            }
-            L = warp_sum(L);
-            if (lane == 0) sm[2 * kMaxG + g] = 1.f / L;
-          }
-          consumer_bar();
-          for (int item = tid; item < G * 64; item += kConsumers) {
-            const int g = item >> 6, d2 = item & 63;
-            float ox = 0.f, oy = 0.f;
-            const float* pe = p0 + g * kPartStride + 2 + 2 * d2;
-            int sp2 = 0;
-            for (; sp2 + 4 <= Su; sp2 += 4) {
-              float2 v[4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) v[j] = ldcg_f2(pe + (sp2 + j) * G * kPartStride);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float w = wts[g * Su + sp2 + j];
-                ox = fmaf(w, v[j].x, ox);
-                oy = fmaf(w, v[j].y, oy);
-              }
-            }
-            for (; sp2 < Su; ++sp2) {
-              const float2 v = ldcg_f2(pe + sp2 * G * kPartStride);
-              const float w = wts[g * Su + sp2];
-              ox = fmaf(w, v.x, ox);
-              oy = fmaf(w, v.y, oy);
-            }
-            const float inv = sm[2 * kMaxG + g];
-            reinterpret_cast<uint32_t*>(p.o + obase + g * 128)[d2] = pack_bf16(ox * inv, oy * inv);
-          }
-        }
-        ev(p, s.misc, 10);
+      for (int k = 0; k < 2; ++k) {
+        const int item = tid + k * kConsumers;
+        if (item < G * 64) reinterpret_cast<float2*>(part + (item >> 6) * kPartStride + 2)[item & 63] = oacc[k];
       }
+      if (tid < G) {
+        part[tid * kPartStride] = sm[tid];
+        part[tid * kPartStride + 1] = sm[kMaxG + tid];
+      }
+      consumer_bar();  // the shared buffers of this pair are free for the next one
     }
-    if (!many) break;
+    if (!as.many) break;
   }
   return true;
+}
+
+// o_proj prologue: the activation rows are the attention output, merged here
+// from the partials by log-sum-exp (every CTA merges all of them -- a few
+// hundred KB from L2 at most -- instead of one CTA merging while the others
+// wait). T threads share each (pair, head, 4-dim chunk) item: each loads the
+// m, l and o of every T-th split in one round of loads (up to 12 splits in
+// flight), folds them relative to its own running max, and the T results are
+// combined through shared memory. Writes bf16 o [B][hq * 128] into s.uni.
+template <int B>
+__device__ void merge_attention(const Smem& s, const Params& p) {
+  const int tid = threadIdx.x;
+  const int G = p.hq / p.hkv, P = B * p.hkv, nb = gridDim.x;
+  const AttnSplit as = attn_split<B>(p);
+  const int items = P * G * 32;
+  const int T = max(1, kConsumers / items);
+  bf16* xs = reinterpret_cast<bf16*>(s.uni);
+  // [T][items] (acc, then M and L) right after the bf16 rows (B * hq * 768
+  // bytes in all, checked by the host against the 40 KB area)
+  float4* pacc = reinterpret_cast<float4*>(s.uni + B * p.hq * 256);
+  float2* pml = reinterpret_cast<float2*>(pacc + T * items);
+  for (int w0 = tid; w0 < items * T; w0 += kConsumers) {
+    const int item = w0 % items, j0 = w0 / items;
+    const int d4 = item & 31, pg = item >> 5, pi = pg / G, g = pg % G;
+    const int Su = attn_used(as.S, s.rows[3 * kMaxB + pi / p.hkv]);
+    const float* p0 = p.part + (int64_t)pi * nb * G * kPartStride + g * kPartStride;
+    float M = -INFINITY, L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sb = j0; sb < Su; sb += 12 * T) {
+      float2 ml[12];
+      float4 v[12];
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        const int sp2 = sb + j * T;
+        ml[j] = make_float2(-INFINITY, 0.f);
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (sp2 < Su) {
+          const float* pe = p0 + (int64_t)sp2 * G * kPartStride;
+          ml[j] = ldcg_f2(pe);
+          const float2 a = ldcg_f2(pe + 2 + 4 * d4), c = ldcg_f2(pe + 4 + 4 * d4);
+          v[j] = make_float4(a.x, a.y, c.x, c.y);
+        }
+      }
+      float bm = M;
+#pragma unroll
+      for (int j = 0; j < 12; ++j) bm = fmaxf(bm, ml[j].x);
+      const float sc = exp2f(M - bm);  // 0 on the first batch (M = -inf)
+      acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+      L *= sc;
+      M = bm;
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        const float w = exp2f(ml[j].x - M);  // 0 for missing splits
+        L = fmaf(w, ml[j].y, L);
+        acc.x = fmaf(w, v[j].x, acc.x);
+        acc.y = fmaf(w, v[j].y, acc.y);
+        acc.z = fmaf(w, v[j].z, acc.z);
+        acc.w = fmaf(w, v[j].w, acc.w);
+      }
+    }
+    pacc[j0 * items + item] = acc;
+    pml[j0 * items + item] = make_float2(M, L);
+  }
+  consumer_bar();
+  for (int item = tid; item < items; item += kConsumers) {
+    float M = -INFINITY;
+    for (int j = 0; j < T; ++j) M = fmaxf(M, pml[j * items + item].x);
+    float L = 0.f;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < T; ++j) {
+      const float2 ml = pml[j * items + item];
+      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+      const float4 c = pacc[j * items + item];
+      L = fmaf(w, ml.y, L);
+      a.x = fmaf(w, c.x, a.x); a.y = fmaf(w, c.y, a.y); a.z = fmaf(w, c.z, a.z); a.w = fmaf(w, c.w, a.w);
+    }
+    const int d4 = item & 31, pg = item >> 5, pi = pg / G, g = pg % G;
+    const int b = pi / p.hkv, kvh = pi % p.hkv;
+    const float iL = 1.f / L;
+    uint2 o;
+    o.x = pack_bf16(a.x * iL, a.y * iL);
+    o.y = pack_bf16(a.z * iL, a.w * iL);
+    reinterpret_cast<uint2*>(xs + (int64_t)b * p.hq * 128 + (kvh * G + g) * 128)[d4] = o;
+  }
+  consumer_bar();
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -957,7 +1018,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mega_kernel(Params p) {
       trace_at(p, 2 + 5 * i);
       ev(p, s.misc, 4);
       // ---- C: o_proj, reduced over the ranks
-      copy_rows<B>(s, p.o, p.hq * 128);
+      merge_attention<B>(s, p);
       ev(p, s.misc, 1);
       {
         const Phase& P1 = ph[1];
@@ -1150,7 +1211,8 @@ void decode_mega(at::Tensor layers, at::Tensor embed, at::Tensor final_norm, at:
   TORCH_CHECK(B == 1 || B == 2 || B == 4, "decode_mega: batch 1, 2 or 4");
   TORCH_CHECK(layers.is_cuda() && layers.scalar_type() == at::kLong && layers.dim() == 2 && layers.size(1) == 11,
               "decode_mega: layers int64 [L, 11]");
-  TORCH_CHECK(d % 8 == 0 && f % 8 == 0 && hq % hkv == 0 && hq / hkv <= mk::kMaxG, "decode_mega: shapes");
+  TORCH_CHECK(d % 8 == 0 && f % 8 == 0 && hq % hkv == 0 && hq / hkv <= mk::kMaxG && B * hq * 1024 <= mk::kUnion,
+              "decode_mega: shapes (query heads x batch rows too many for the attention merge)");
   TORCH_CHECK(B * std::max({d, hq * 128, f}) * 2 <= mk::kUnion, "decode_mega: activation rows exceed shared memory");
   TORCH_CHECK(world >= 1 && world <= 8 && (world == 1 || (red0_mc != 0 && red1_mc != 0)),
               "decode_mega: tensor parallel needs multicast reduction buffers");
