@@ -45,10 +45,12 @@ class GPTConfig:
     init_std: float = 0.02
     tie_embeddings: bool = False
     qk_norm: bool = False  # Qwen3: per-head RMSNorm of q and k before RoPE
+    qkv_bias: bool = False  # Qwen2: bias on the q / k / v projections
+    head_dim_: int = 0  # explicit head dimension (0: d_model / n_heads)
 
     @property
     def head_dim(self) -> int:
-        return self.d_model // self.n_heads
+        return self.head_dim_ or self.d_model // self.n_heads
 
     @staticmethod
     def gpt_24l() -> "GPTConfig":
@@ -81,10 +83,12 @@ def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool 
             (f"l{i}.attn_norm", (d,), False),
             (f"l{i}.wqkv", (qkv, d), True),
         ]
+        if cfg.qkv_bias:
+            specs.append((f"l{i}.bqkv", (qkv,), False))
         if cfg.qk_norm:
             specs += [(f"l{i}.q_norm", (cfg.head_dim,), False), (f"l{i}.k_norm", (cfg.head_dim,), False)]
         specs += [
-            (f"l{i}.wo", (d, d), True),
+            (f"l{i}.wo", (d, cfg.n_heads * cfg.head_dim), True),
             (f"l{i}.mlp_norm", (d,), False),
             (f"l{i}.wgu", (2 * f, d), True),
             (f"l{i}.wd", (d, f), True),
@@ -96,6 +100,7 @@ def gpt_param_specs(cfg: GPTConfig, layers=None, first: bool = True, last: bool 
     if tp_size > 1:
         from ..parallel.tp_train import shard_shape
 
+        assert not cfg.qkv_bias, "tensor-parallel training shards no qkv bias"
         specs = [(n, shard_shape(cfg, n, shp, tp_size), dec) for n, shp, dec in specs]
     return specs
 
@@ -118,13 +123,20 @@ class GPT:
     norm, LM head and loss, other stages map hidden states to hidden states."""
 
     def __init__(self, cfg: GPTConfig, device="cuda", seed: int = 0, pad_multiple: int = 1, alloc=None,
-                 layers=None, first: bool = True, last: bool = True, tp=None, cp=None, shard=None):
+                 layers=None, first: bool = True, last: bool = True, tp=None, cp=None, shard=None,
+                 external: frozenset = frozenset(), loss_chunk: int = 0):
         """tp: a ``parallel.tp_train.TPGroup`` -- this rank then holds its
         Megatron shard of every layer (and the same values as the matching
         slice of the unsharded model with the same seed).
         shard: a ``parallel.fsdp.ShardSpec`` -- ZeRO-2 / ZeRO-3 (FSDP) storage:
-        the arena holds only this rank's slice of every layer."""
+        the arena holds only this rank's slice of every layer.
+        external: projection names ("wqkv", "wo", "wgu", "wd") whose weights
+        live outside the arena (a frozen quantised base: adapters replace
+        ``_linear`` and supply them); their shapes are in ``external_shapes``.
+        loss_chunk > 0: the LM head + cross-entropy runs over that many tokens
+        at a time (peak memory [loss_chunk, vocab] instead of [tokens, vocab])."""
         self.cfg = cfg
+        self.loss_chunk = loss_chunk
         self.tp = tp if tp is not None and tp.world > 1 else None
         # context parallel (parallel.cp.CPGroup): this rank holds one contiguous
         # chunk of every sequence; attention all-gathers K/V over the group
@@ -138,6 +150,8 @@ class GPT:
         self.layers = list(range(cfg.n_layers) if layers is None else layers)
         self.first, self.last = first, last
         specs = gpt_param_specs(cfg, self.layers, first, last, tp_size)
+        self.external_shapes = {n: shp for n, shp, _ in specs if n.split(".")[-1] in external}
+        specs = [sp for sp in specs if sp[0] not in self.external_shapes]
         if shard is not None:
             from ..parallel.fsdp import ShardedArena
 
@@ -161,6 +175,8 @@ class GPT:
             for name in a.names():
                 if name.endswith("norm"):
                     t = torch.ones(full_shape[name], dtype=torch.float32)
+                elif name.endswith("bqkv"):
+                    t = torch.zeros(full_shape[name], dtype=torch.float32)
                 else:
                     g = torch.Generator(device="cpu").manual_seed(seed * 1000003 + index[name])
                     t = torch.empty(full_shape[name], dtype=torch.float32)
@@ -248,6 +264,8 @@ class GPT:
                 x.register_hook(_ReadyHook(ready, f"l{i}"))
             h, res = A.rmsnorm_residual(x, a[f"l{i}.attn_norm"], cfg.norm_eps)
             qkv = lin(i, "wqkv", h)
+            if cfg.qkv_bias:
+                qkv = A.add_bias(qkv, a[f"l{i}.bqkv"])
             if cfg.qk_norm:
                 qkv = self._qk_norm(i, qkv, Hq, Hkv, D)
             qkv = A.rope_(qkv, pos, self.rope_cos, self.rope_sin, Hq + Hkv, D)
@@ -296,6 +314,8 @@ class GPT:
         w = self.arena["tok_emb"] if self.cfg.tie_embeddings else self.arena["lm_head"]
         if loss_scale is None:
             loss_scale = 1.0 / targets.numel()
+        if self.loss_chunk and h.shape[0] > self.loss_chunk:
+            return A.lm_head_cross_entropy_chunked(h, w, targets.reshape(-1), loss_scale, self.loss_chunk)
         return A.lm_head_cross_entropy(h, w, targets.reshape(-1), loss_scale)
 
     def loss(self, ids: torch.Tensor, targets: torch.Tensor, loss_scale: float | None = None,

@@ -61,11 +61,28 @@ class _QuantWeight:
 
 
 def _weight(w):
-    return w.bf16() if isinstance(w, _QuantWeight) else w
+    """A frozen weight object (quantised blocks) expanded to bf16, or the tensor itself."""
+    return w.bf16() if hasattr(w, "bf16") and not isinstance(w, torch.Tensor) else w
 
 
 def _acc(mg, a, b, a_mn, b_mn, alpha):
     F.gemm(a, b, a_mn=a_mn, b_mn=b_mn, out=mg, accumulate=True, alpha=alpha)
+
+
+class FrozenLinearFn(torch.autograd.Function):
+    """y = x W^T (+ residual) for a frozen base weight object that expands to
+    bf16 on demand (it is expanded again in backward: the shared scratch it
+    expands into holds another weight by then)."""
+
+    @staticmethod
+    def forward(ctx, x, residual, w):
+        ctx.w, ctx.has_res = w, residual is not None
+        return F.gemm(x, _weight(w), residual=residual)
+
+    @staticmethod
+    def backward(ctx, dy):
+        dx = F.gemm(dy.contiguous(), _weight(ctx.w), b_mn=True)
+        return dx, (dy if ctx.has_res else None), None
 
 
 class LoRALinearFn(torch.autograd.Function):
@@ -99,15 +116,20 @@ class LoRAGPT:
     ``device`` so ``Trainer`` and the DP engines drive it like a full model."""
 
     def __init__(self, base, cfg: LoRAConfig = LoRAConfig(), seed: int = 0, pad_multiple: int = 1, alloc=None,
-                 quant: str | None = None):
+                 quant: str | None = None, weights: dict | None = None):
+        """weights: prebuilt frozen base weights {(layer, target): weight} for
+        projections that live outside the base arena (a GGUF base kept in its
+        own quantised blocks, see ``models.qlora_gguf``)."""
         self.base, self.lcfg = base, cfg
         self.cfg, self.device = base.cfg, base.device
         assert cfg.rank % 8 == 0, "LoRA rank must be a multiple of 8 (tensor-core tile granularity)"
         base.freeze()
+        ext = getattr(base, "external_shapes", {})
         specs = []
         for i in base.layers:
             for t in cfg.targets:
-                out, inp = base.arena.slots[f"l{i}.{t}"].shape
+                key = f"l{i}.{t}"
+                out, inp = ext[key] if key in ext else base.arena.slots[key].shape
                 specs += [(f"l{i}.{t}.A", (cfg.rank, inp), False), (f"l{i}.{t}.B", (out, cfg.rank), False)]
         self.arena = ParamArena(specs, self.device, pad_multiple=pad_multiple, alloc=alloc)
         with torch.no_grad():
@@ -123,7 +145,10 @@ class LoRAGPT:
                     mv.zero_()
         self.arena.sync_bf16_from_master()
         self._scratch = None
-        self.qweights: dict = {}
+        self.qweights: dict = dict(weights or {})
+        for w in self.qweights.values():
+            if hasattr(w, "scratch") and w.scratch is None:
+                w.scratch = self._scratch_buf
         if quant is not None:
             fmt = {"q8_0": F.Q8_0, "q4_0": F.Q4_0}[quant]
             for i in base.layers:
@@ -142,8 +167,13 @@ class LoRAGPT:
         if name not in self.lcfg.targets:
             from ..ops import autograd as A
 
+            w = self.qweights.get((i, name))
+            if w is not None:
+                return FrozenLinearFn.apply(x, residual, w)
             return A.linear(x, self.base.arena[f"l{i}.{name}"], residual=residual)
-        w = self.qweights.get((i, name), self.base.arena[f"l{i}.{name}"])
+        w = self.qweights.get((i, name))
+        if w is None:
+            w = self.base.arena[f"l{i}.{name}"]
         a, b = self.arena[f"l{i}.{name}.A"], self.arena[f"l{i}.{name}.B"]
         return LoRALinearFn.apply(x, a, b, residual, w, self.lcfg.scale)
 

@@ -55,6 +55,31 @@ def linear(x, w, residual=None):
     return LinearFn.apply(x, w, residual)
 
 
+class AddBiasFn(torch.autograd.Function):
+    """y = x + b (b broadcast over rows); the bias gradient (column sums of
+    dy, fp32) accumulates into b's main_grad like every arena weight."""
+
+    @staticmethod
+    def forward(ctx, x, b):
+        ctx.b = b
+        return x + b
+
+    @staticmethod
+    def backward(ctx, dy):
+        b = ctx.b
+        mg = _main_grad(b)
+        db = None
+        if mg is not None:
+            mg.add_(dy.float().sum(0))
+        elif ctx.needs_input_grad[1]:
+            db = dy.float().sum(0).to(b.dtype)
+        return dy, db
+
+
+def add_bias(x, b):
+    return AddBiasFn.apply(x, b)
+
+
 class RMSNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, eps):
@@ -280,3 +305,53 @@ class LMHeadCrossEntropyFn(torch.autograd.Function):
 
 def lm_head_cross_entropy(x, w, targets, loss_scale, ignore_index=-100):
     return LMHeadCrossEntropyFn.apply(x, w, targets, float(loss_scale), ignore_index)
+
+
+class ChunkedLMHeadCrossEntropyFn(torch.autograd.Function):
+    """LMHeadCrossEntropyFn over ``chunk`` tokens at a time: each chunk's
+    logits [chunk, V] are computed, turned into their gradient by the fused
+    cross-entropy kernel and consumed at once -- the input gradient of the
+    chunk (dlogits W) and, when the head trains, its weight gradient
+    (dlogits^T x, accumulated in fp32) -- so no [tokens, V] tensor exists.
+    Backward scales the stored gradients by the incoming one. Reference: the
+    QLoRA stage's chunked LM-head loss (trainer/src/qwen_qlora_stage.rs)."""
+
+    @staticmethod
+    def forward(ctx, x, w, targets, loss_scale, chunk, ignore_index):
+        T = x.shape[0]
+        dx = torch.empty_like(x)
+        train_w = ctx.needs_input_grad[1]
+        dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device) if train_w else None
+        total = torch.zeros((), dtype=torch.float32, device=x.device)
+        for t0 in range(0, T, chunk):
+            xs, ts = x[t0 : t0 + chunk], targets[t0 : t0 + chunk]
+            logits = F.gemm(xs, w)
+            rows, _ = F.cross_entropy_fused(logits, ts, grad_scale=loss_scale, ignore_index=ignore_index,
+                                            write_grad=True)
+            total = total + rows.sum()
+            F.gemm(logits, w, b_mn=True, out=dx[t0 : t0 + chunk])
+            if train_w:
+                F.gemm(logits, xs, a_mn=True, b_mn=True, out=dw, accumulate=True)
+            del logits
+        ctx.save_for_backward(dx, dw if train_w else torch.empty(0))
+        ctx.train_w, ctx.wref = train_w, w
+        return total * loss_scale
+
+    @staticmethod
+    def backward(ctx, dloss):
+        dx, dw = ctx.saved_tensors
+        g = dloss.float()
+        gx = (dx.float() * g).to(dx.dtype)
+        gw = None
+        if ctx.train_w:
+            w = ctx.wref
+            mg = _main_grad(w)
+            if mg is not None:
+                mg.add_(dw * g)
+            else:
+                gw = (dw * g).to(w.dtype)
+        return gx, gw, None, None, None, None
+
+
+def lm_head_cross_entropy_chunked(x, w, targets, loss_scale, chunk, ignore_index=-100):
+    return ChunkedLMHeadCrossEntropyFn.apply(x, w, targets, float(loss_scale), int(chunk), ignore_index)

@@ -550,6 +550,23 @@ def quantize_blocks(x, fmt=Q8_0):
     return torch.frombuffer(bytearray(q(x.float().numpy().reshape(-1))), dtype=torch.uint8)
 
 
+GGUF_DEVICE_TYPES = frozenset({0, 1, 2, 6, 8, 12, 13, 14, 30})  # F32 F16 Q4_0 Q5_0 Q8_0 Q4_K Q5_K Q6_K BF16
+
+
+def gguf_dequant(blocks, typ, rows, K, out):
+    """``rows`` rows of K elements stored back to back as GGUF type ``typ``
+    (uint8 blocks) -> out[:rows, :K] (bf16). CUDA: one kernel for every type
+    in GGUF_DEVICE_TYPES; CPU: the host dequantiser."""
+    if _cuda(blocks):
+        C().gguf_dequant(blocks, int(typ), int(rows), int(K), out)
+        return out
+    from ..formats import gguf
+
+    x = gguf.dequantize(blocks.numpy(), int(typ), int(rows) * int(K)).reshape(int(rows), int(K))
+    out[:rows, :K].copy_(torch.from_numpy(x).to(out.dtype))
+    return out
+
+
 def dequantize_blocks(q, shape, fmt=Q8_0, out=None):
     """uint8 GGUF blocks -> bf16 tensor of ``shape``."""
     n = 1

@@ -2,6 +2,7 @@
 
     python -m aether_b200.pp_worker --rank R --world-size W --layers L \\
         [--base-port P] [--host H] [--epochs N] [--seed S] [--lr LR] [--microbatch M] [--qlora q8_0|q4_0]
+        [--gguf MODEL.gguf]
 
 Ranks meet at ``host:base-port`` (torch.distributed rendezvous; NCCL on GPUs,
 gloo on the CPU), each takes its contiguous share of ``--layers`` Qwen3-style
@@ -9,7 +10,9 @@ blocks (RMSNorm, fused QKV with per-head q/k RMSNorm, RoPE, causal attention,
 SwiGLU; the first rank embeds, the last owns the final norm, LM head and loss)
 and trains them with the 1F1B schedule over synthetic token batches. With
 ``--qlora`` the stage's base projections are frozen and kept as GGUF Q8_0 /
-Q4_0 blocks, and only LoRA adapters train (the QLoRA stage). The last rank
+Q4_0 blocks, and only LoRA adapters train (the QLoRA stage); with ``--gguf``
+the stage is that GGUF model's share of layers, in the file's own blocks
+(``--layers`` is then the model's). The last rank
 prints ``EPOCH <e> <mean loss>`` per epoch, every rank prints a checksum of
 its trained parameters, and the last rank ends with
 ``RESULT rank=<R> world=<W> final_loss=<x>``. A ``--world-size 1`` run holds
@@ -39,9 +42,12 @@ def model_config(layers: int):
 
 class QLoRAPipelineStage:
     """A pipeline stage whose base projections are frozen GGUF blocks and whose
-    LoRA adapters train (the QLoRA stage), with the GPTPipelineStage contract."""
+    LoRA adapters train (the QLoRA stage), with the GPTPipelineStage contract.
+    The base is a random GPT re-quantised to ``quant`` (Q8_0 / Q4_0), or --
+    with ``gguf`` -- this stage's layers of a GGUF model file, kept in the
+    file's own blocks (models/qlora_gguf.py)."""
 
-    def __init__(self, cfg, rank, world, device, seed=0, lr=1e-3, quant="q8_0", lora_rank=8):
+    def __init__(self, cfg, rank, world, device, seed=0, lr=1e-3, quant="q8_0", lora_rank=8, gguf=None):
         from .models.gpt import GPT
         from .models.lora import LoRAConfig, LoRAGPT
         from .optim import FlatAdamW
@@ -51,8 +57,15 @@ class QLoRAPipelineStage:
         self.layers = list(range(bounds[rank], bounds[rank + 1]))
         self.rank, self.world = rank, world
         self.first, self.last = rank == 0, rank == world - 1
-        base = GPT(cfg, device=device, seed=seed, layers=self.layers, first=self.first, last=self.last)
-        self.lora = LoRAGPT(base, LoRAConfig(rank=lora_rank, alpha=2.0 * lora_rank), seed=seed + 1, quant=quant)
+        lcfg = LoRAConfig(rank=lora_rank, alpha=2.0 * lora_rank)
+        if gguf is not None:
+            from .models.qlora_gguf import qlora_from_gguf
+
+            self.lora = qlora_from_gguf(gguf, device=device, lora=lcfg, seed=seed, layers=self.layers,
+                                        first=self.first, last=self.last, max_seq=cfg.max_seq)
+        else:
+            base = GPT(cfg, device=device, seed=seed, layers=self.layers, first=self.first, last=self.last)
+            self.lora = LoRAGPT(base, lcfg, seed=seed + 1, quant=quant)
         self.model = self.lora
         self.opt = FlatAdamW(self.lora.arena, lr=lr, weight_decay=0.0)
         self.device = torch.device(device)
@@ -96,6 +109,7 @@ def main(argv=None) -> int:
     ap.add_argument("--micro-batches", type=int, default=4, help="micro-batches per optimiser step")
     ap.add_argument("--seq", type=int, default=32)
     ap.add_argument("--qlora", choices=["q8_0", "q4_0"], default=None)
+    ap.add_argument("--gguf", default=None, help="QLoRA over this GGUF model's layers (its quantised blocks)")
     ap.add_argument("--device", default=None, help="cpu or cuda (default: cuda when available)")
     a = ap.parse_args(argv)
     if not 0 <= a.rank < a.world_size:
@@ -112,7 +126,15 @@ def main(argv=None) -> int:
     info = D.init(device=None if use_cuda else "cpu", timeout_s=120)
     dev = info.device
     cfg = model_config(a.layers)
-    if a.qlora:
+    if a.gguf:
+        from .formats.gguf import GGUFFile
+        from .models.qlora_gguf import config_from_gguf
+
+        cfg = config_from_gguf(GGUFFile(a.gguf), max_seq=max(64, a.seq))
+        if cfg.n_layers < a.world_size:
+            ap.error("the GGUF model has fewer layers than --world-size")
+        stage = QLoRAPipelineStage(cfg, a.rank, a.world_size, dev, seed=a.seed, lr=a.lr, gguf=a.gguf)
+    elif a.qlora:
         stage = QLoRAPipelineStage(cfg, a.rank, a.world_size, dev, seed=a.seed, lr=a.lr, quant=a.qlora)
     else:
         stage = GPTPipelineStage(cfg, a.rank, a.world_size, dev, seed=a.seed, lr=a.lr, weight_decay=0.0)

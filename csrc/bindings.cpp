@@ -69,6 +69,9 @@ void skinny_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor acc, at::Tensor tile
                      at::Tensor qkv, at::Tensor pos, at::Tensor slot, at::Tensor cos_t, at::Tensor sin_t,
                      at::Tensor k_cache, at::Tensor v_cache, int64_t Hq, int64_t Hkv,
                      std::optional<at::Tensor> page_table, int64_t splits);
+// gguf_dequant.cu
+bool gguf_device_type(int64_t type);
+void gguf_dequant(at::Tensor blocks, int64_t type, int64_t rows, int64_t K, at::Tensor out);
 // decode_mega.cu
 void decode_mega(at::Tensor layers, at::Tensor embed, at::Tensor final_norm, at::Tensor head, int64_t vocab_rows,
                  int64_t vocab_col0, int64_t d, int64_t hq, int64_t hkv, int64_t f, double eps, double scale,
@@ -163,6 +166,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("team_barrier", &aether::team_barrier);
   m.def("skinny_gemm_swiglu", &aether::skinny_gemm_swiglu);
   m.def("skinny_gemm_qkv", &aether::skinny_gemm_qkv);
+  m.def("gguf_device_type", &aether::gguf_device_type);
+  m.def("gguf_dequant", &aether::gguf_dequant);
   m.def("decode_mega", &aether::decode_mega, "layers"_a, "embed"_a, "final_norm"_a, "head"_a, "vocab_rows"_a,
         "vocab_col0"_a, "d"_a, "hq"_a, "hkv"_a, "f"_a, "eps"_a, "scale"_a, "tok"_a, "pos"_a, "slot"_a, "seqlen"_a,
         "next"_a, "logits"_a, "cache0"_a, "page_table"_a, "x"_a, "x2"_a, "q"_a, "o"_a, "act"_a, "part"_a,
