@@ -181,3 +181,13 @@ def test_gpu_qlora_gguf_matches_cpu(tmp_path):
     lg.backward()
     assert abs(float(lg) - a) < 2e-2 * abs(a), (float(lg), a)
     assert float(gpu.arena.grad.abs().sum()) > 0  # the adapters receive gradients
+
+
+def test_qlora_smoke_command_line(tmp_path):
+    """qlora-smoke over a layer range: loss falls, adapters grow; bad ranges exit 2."""
+    from aether_b200 import qlora_smoke
+
+    path = _write_base(str(tmp_path / "base.gguf"))
+    assert qlora_smoke.main(["--gguf", path, "--lo", "0", "--hi", "2", "--steps", "8", "--device", "cpu"]) == 0
+    assert qlora_smoke.main(["--gguf", path, "--lo", "1", "--hi", "2", "--steps", "8", "--device", "cpu"]) == 0
+    assert qlora_smoke.main(["--gguf", path, "--lo", "1", "--hi", "5", "--device", "cpu"]) == 2
