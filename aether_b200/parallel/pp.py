@@ -5,9 +5,9 @@ Reference: trainer/src/pipeline.rs -- ``trait Stage {forward, backward, step}``
 (:180) and ``run_1f1b`` (:199-290): rank r runs (world-1-r) warm-up forwards,
 then alternates one forward and one backward, then drains the remaining
 backwards; activations travel device -> host -> TCP -> host -> device. Here
-activations and gradients stay on the GPU and move with NCCL send/recv
-(isend/irecv, so a rank's send overlaps its next compute); the schedule and
-the stage contract are the same.
+activations and gradients stay on the GPU and move with NCCL isend / irecv
+(a rank's send overlaps its next compute, and every receive is posted one
+micro-batch ahead); the schedule and the stage contract are the same.
 """
 from __future__ import annotations
 
@@ -64,13 +64,30 @@ def run_1f1b(stage: GPTPipelineStage, batches: list, group=None) -> torch.Tensor
     total = torch.zeros((), dtype=torch.float32, device=dev)
     prev, nxt = rank - 1, rank + 1
 
+    # Receives are posted one micro-batch ahead (irecv), so the transfer of the
+    # next activation / gradient overlaps the compute of the current one. Per
+    # peer the posts stay in schedule order, matching the sender's isends.
+    posted = {}
+
+    def post(kind, i):
+        if i >= n or (kind, i) in posted or (stage.first if kind == "x" else stage.last):
+            return
+        t = torch.empty(batches[i][1].numel(), d, dtype=act_dtype, device=dev)
+        posted[(kind, i)] = (t, dist.irecv(t, src=prev if kind == "x" else nxt, group=group))
+
+    def take(kind, i):
+        post(kind, i)
+        t, work = posted.pop((kind, i))
+        work.wait()
+        return t
+
     def fwd(i):
         ids, tgt = batches[i]
         ids, tgt = ids.to(dev), tgt.to(dev)
         x = None
         if not stage.first:
-            x = torch.empty(tgt.numel(), d, dtype=act_dtype, device=dev)
-            dist.recv(x, src=prev, group=group)
+            x = take("x", i)
+            post("x", i + 1)
             x.requires_grad_(True)
             inputs[i] = x
         out = stage.forward(ids, tgt, x, loss_scale)
@@ -85,8 +102,8 @@ def run_1f1b(stage: GPTPipelineStage, batches: list, group=None) -> torch.Tensor
             out.backward()
             total = total + out.detach()
         else:
-            g = torch.empty_like(out)
-            dist.recv(g, src=nxt, group=group)
+            g = take("g", i)
+            post("g", i + 1)
             out.backward(g)
         if not stage.first:
             x = inputs.pop(i)
