@@ -27,12 +27,24 @@ def _main_grad(w: torch.Tensor) -> torch.Tensor | None:
     return mg
 
 
+def _gemm_w(x, w, b_mn=False, residual=None):
+    """x . w^T (b_mn: x . w) where w may be a ZeRO-3 weight whose unit is still
+    to be gathered: then this GEMM is the unit's first consumer and gathers it
+    inside the same kernel (parallel.fsdp, fused mode)."""
+    pg = getattr(w, "_fsdp_pg", None)
+    if pg is not None:
+        y = pg[0].pg_gemm(pg[1], x, w, b_mn=b_mn, residual=residual)
+        if y is not None:
+            return y
+    return F.gemm(x, w, b_mn=b_mn, residual=residual)
+
+
 class LinearFn(torch.autograd.Function):
     """y = x @ w^T (+ residual). x: [T, K], w: [N, K]."""
 
     @staticmethod
     def forward(ctx, x, w, residual=None):
-        y = F.gemm(x, w, residual=residual)
+        y = _gemm_w(x, w, residual=residual)
         ctx.save_for_backward(x, w)
         ctx.has_res = residual is not None
         return y
@@ -41,7 +53,7 @@ class LinearFn(torch.autograd.Function):
     def backward(ctx, dy):
         x, w = ctx.saved_tensors
         dy = dy.contiguous()
-        dx = F.gemm(dy, w, b_mn=True) if ctx.needs_input_grad[0] else None
+        dx = _gemm_w(dy, w, b_mn=True) if ctx.needs_input_grad[0] else None
         mg = _main_grad(w)
         dw = None
         if mg is not None:

@@ -43,6 +43,23 @@ def gemm(a, b, *, a_mn=False, b_mn=False, out=None, out_dtype=BF16, bias=None, r
     return out
 
 
+def gemm_tp(*args):
+    """The tensor-parallel training GEMM with its collective inside
+    (csrc/gemm_tp.cu; arguments as the extension's gemm_tp). A refused
+    argument set comes back as a message and is raised here."""
+    msg = C().gemm_tp(*args)
+    if msg:
+        raise RuntimeError(msg)
+
+
+def gemm_param_gather(*args):
+    """The GEMM whose weight unit (ZeRO-3) is all-gathered inside the same
+    kernel (csrc/gemm_tp.cu); raises a refused argument set."""
+    msg = C().gemm_param_gather(*args)
+    if msg:
+        raise RuntimeError(msg)
+
+
 def linear(x, w, bias=None, residual=None, out=None):
     """y = x @ w^T (+ bias) (+ residual); x [..., K], w [N, K]."""
     shp = x.shape

@@ -53,9 +53,20 @@ class ShardSpec:
     world: int
     stage: int = 3  # 2: gradients + optimiser state sharded; 3: parameters too
     group: object = None
+    # stage 3 on GPUs: a parallel.symm.SymmTeam over `group`. Each layer's
+    # parameter all-gather then runs inside its first consuming GEMM (the
+    # gemm_param_gather kernel) instead of an NCCL call.
+    fused: object = None
 
 
-def _unit_of(name: str) -> int:
+# elements per flag of the fused parameter gather (a layer unit is padded to
+# a multiple of world * FUSED_CHUNK)
+FUSED_CHUNK = 16384
+
+
+def _unit_of(name: str, fused: bool = False) -> int:
+    if fused and name.split(".")[-1].endswith("norm"):
+        return ROOT  # norm weights are read by row kernels before any GEMM: keep them gathered
     if name.startswith("l") and "." in name:
         head = name.split(".", 1)[0][1:]
         if head.isdigit():
@@ -64,7 +75,7 @@ def _unit_of(name: str) -> int:
 
 
 class _Unit:
-    def __init__(self, uid: int, specs, world: int):
+    def __init__(self, uid: int, specs, world: int, quantum: int = ALIGN):
         self.uid = uid
         self.slots: dict[str, Slot] = {}
         off = 0
@@ -74,10 +85,20 @@ class _Unit:
                 n *= int(s)
             self.slots[name] = Slot(name, tuple(int(s) for s in shape), off, n, decay)
             off += (n + ALIGN - 1) // ALIGN * ALIGN
-        unit = ALIGN * world
+        unit = quantum * world
         self.numel = max(unit, (off + unit - 1) // unit * unit)
         self.shard = self.numel // world
         self.offset = 0  # of this unit's slice inside the rank's flat shard
+
+
+class _StreamWork:
+    """Completion of work queued on a side stream (the wait is on the device)."""
+
+    def __init__(self, event):
+        self.event = event
+
+    def wait(self):
+        torch.cuda.current_stream().wait_event(self.event)
 
 
 class ShardedArena:
@@ -90,14 +111,17 @@ class ShardedArena:
         self.rank, self.world, self.stage, self.group = spec.rank, spec.world, spec.stage, spec.group
         assert self.stage in (2, 3)
         self.device = torch.device(device)
+        self.team = spec.fused if (spec.fused is not None and self.stage == 3 and self.world > 1
+                                   and self.device.type == "cuda") else None
+        fused = self.team is not None
         by_unit: dict[int, list] = {}
         for sp in specs:
-            by_unit.setdefault(_unit_of(sp[0]), []).append(sp)
+            by_unit.setdefault(_unit_of(sp[0], fused), []).append(sp)
         order = sorted(u for u in by_unit if u != ROOT) + ([ROOT] if ROOT in by_unit else [])
         self.units: dict[int, _Unit] = {}
         off = 0
         for u in order:
-            unit = _Unit(u, by_unit[u], self.world)
+            unit = _Unit(u, by_unit[u], self.world, FUSED_CHUNK if (fused and u != ROOT) else ALIGN)
             unit.offset = off
             off += unit.shard
             self.units[u] = unit
@@ -127,10 +151,35 @@ class ShardedArena:
             for u, unit in self.units.items():
                 self._pbuf[u] = self._full[base : base + unit.numel]
                 base += unit.numel
+        elif fused:
+            # symmetric memory: every rank's unit buffers, gather flags and
+            # readiness words, mapped into every peer
+            t = self.team
+            self._psym = [t.alloc(layer_max, torch.bfloat16) for _ in range(2)]
+            self._pslots = [b.tensor for b in self._psym]
+            self._pflags = [t.alloc(max(1, layer_max // FUSED_CHUNK), torch.int32) for _ in range(2)]
+            self._pready = [t.alloc(self.world, torch.int32) for _ in range(2)]
+            for b in self._pflags + self._pready:
+                b.tensor.zero_()
+            self._pctr = [torch.zeros(2, dtype=torch.int32, device=dev) for _ in range(2)]
+            self._puses = [0, 0]
+            self._proot = torch.zeros(root_n, dtype=torch.bfloat16, device=dev)
+            torch.cuda.synchronize(dev)
+            dist.barrier(group=self.group)  # every rank's flags are zero before anyone signals
         else:
             self._pslots = [torch.zeros(layer_max, dtype=torch.bfloat16, device=dev) for _ in range(2)]
             self._proot = torch.zeros(root_n, dtype=torch.bfloat16, device=dev)
-        self._gslots = [torch.zeros(layer_max, dtype=torch.float32, device=dev) for _ in range(2)]
+        if fused:
+            # layer gradients in symmetric memory: each rank sums its shard range
+            # out of every peer's buffer with its own kernel (no NCCL per layer)
+            self._gsym = [self.team.alloc(layer_max, torch.float32) for _ in range(2)]
+            self._gslots = [b.tensor for b in self._gsym]
+            for g in self._gslots:
+                g.zero_()
+            self._rs_stream = torch.cuda.Stream(device=dev)
+            self._rs_peers = {}
+        else:
+            self._gslots = [torch.zeros(layer_max, dtype=torch.float32, device=dev) for _ in range(2)]
         self._groot = torch.zeros(root_n, dtype=torch.float32, device=dev)
         self._scratch = {i: torch.zeros(layer_max // self.world, dtype=torch.float32, device=dev) for i in (0, 1)}
         self._scratch[ROOT] = torch.zeros(max(1, root_n // self.world), dtype=torch.float32, device=dev)
@@ -139,6 +188,7 @@ class ShardedArena:
     # ------------------------------------------------------------ bookkeeping
     def _reset_state(self):
         self._resident = {}  # unit -> (param buffer, pending gather work or None)
+        self._pending = {}  # fused mode: unit -> slot whose gather waits for the unit's first GEMM
         self._pslot_owner = [None, None]
         self._cur_fwd = None
         self._gslot_owner = [None, None]  # unit whose gradient sits in the slot
@@ -233,8 +283,14 @@ class ShardedArena:
             old = self._pslot_owner[k]
             if old is not None:
                 self._resident.pop(old, None)
+                self._pending.pop(old, None)
             self._pslot_owner[k] = u
             buf = self._pslots[k]
+            if self.team is not None:
+                # no transfer now: the unit's first GEMM gathers it (pg_gemm)
+                self._pending[u] = k
+                self._resident[u] = (buf, None)
+                return
         work = self._all_gather(buf[: unit.numel], self._shard_of(u, self.bf16), async_op)
         self._resident[u] = (buf, work)
 
@@ -250,14 +306,50 @@ class ShardedArena:
         return buf
 
     def _prefetch(self, u: int | None) -> None:
+        if self.team is not None:
+            return  # fused mode gathers inside the consuming GEMM, overlapped there
         if self.stage == 3 and u is not None and u not in self._resident:
             self._gather(u, async_op=self.device.type == "cuda")
+
+    def pg_gemm(self, u: int, x: torch.Tensor, w: torch.Tensor, b_mn: bool = False, residual=None):
+        """x . w^T (b_mn: x . w) as the first consumer of unit u's still-pending
+        gather: one kernel moves every rank's shard into every rank's unit
+        buffer and multiplies as the weight's chunks arrive. None when u is
+        already gathered (the caller runs a plain GEMM)."""
+        k = self._pending.get(u)
+        if k is None:
+            return None
+        if residual is not None or not x.is_contiguous():
+            self._complete(u)  # a form the gather kernel does not take: plain gather first
+            return None
+        del self._pending[u]
+        from ..ops import functional as F
+
+        unit = self.units[u]
+        self._puses[k] += 1
+        out = torch.empty(x.shape[0], w.shape[1] if b_mn else w.shape[0], dtype=torch.bfloat16, device=x.device)
+        sym, fl, rd = self._psym[k], self._pflags[k], self._pready[k]
+        F.gemm_param_gather([x], [w], [out], [self._shard_of(u, self.bf16)], [self._pctr[k]], [self.rank],
+                              self.world, FUSED_CHUNK, b_mn, sym.peers_host, fl.peers_host, rd.peers_host,
+                              sym.mc_ptr, self._puses[k], 10.0)
+        return out
+
+    def _complete(self, u: int) -> None:
+        """Gathers a pending unit without a GEMM (NCCL) -- for consumers the
+        fused kernel does not cover."""
+        k = self._pending.pop(u, None)
+        if k is not None:
+            unit = self.units[u]
+            self._all_gather(self._pslots[k][: unit.numel], self._shard_of(u, self.bf16), False)
 
     def _view(self, name: str, buf: torch.Tensor) -> torch.Tensor:
         s = self.slots[name]
         v = buf[s.offset : s.offset + s.numel].view(s.shape)
         v.requires_grad_(True)
         v._fsdp_name = name
+        u = self.unit_of[name]
+        if u in self._pending:
+            v._fsdp_pg = (self, u)  # its GEMM gathers the unit (ops.autograd._gemm_w)
         return v
 
     def __getitem__(self, name: str) -> torch.Tensor:
@@ -320,7 +412,38 @@ class ShardedArena:
                 return
             key, full = ks[0], self._gslots[ks[0]]
         out = self._scratch[key][: unit.shard]
+        if self.team is not None and key != ROOT:
+            self._gpending[key] = (self._reduce_scatter_fused(key, u, out), u)
+            return
         self._gpending[key] = (self._reduce_scatter(out, full[: unit.numel]), u)
+
+    def _reduce_scatter_fused(self, key: int, u: int, out: torch.Tensor) -> "_StreamWork":
+        """Unit u's gradient (slot `key`) reduce-scattered by this library's
+        kernels on a side stream, overlapped with the backward of the layers
+        below: a bounded barrier (every rank's unit gradient is complete), a
+        one-shot sum of this rank's shard range over every peer's buffer (P2P
+        loads), a second barrier (every peer has read this rank's buffer, so
+        the slot may be zeroed again)."""
+        from .._ext import C
+
+        unit = self.units[u]
+        tab = self._rs_peers.get((key, u))
+        if tab is None:
+            off = self.rank * unit.shard * 4
+            tab = torch.tensor([p + off for p in self._gsym[key].peers_host], dtype=torch.int64, device=self.device)
+            self._rs_peers[(key, u)] = tab
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(self.device))
+        side = self._rs_stream
+        with torch.cuda.stream(side):
+            side.wait_event(ready)
+            self.team.barrier()
+            C().allreduce_oneshot(tab, out, self.world)
+            self.team.barrier()
+            done = torch.cuda.Event()
+            done.record(side)
+        out.record_stream(side)
+        return _StreamWork(done)
 
     def _drain(self, key) -> None:
         """Wait for slot ``key``'s reduce-scatter and add it into the gradient shard."""

@@ -25,7 +25,10 @@ and the final norm, LM head and loss run on the all-gathered rows.
 
 The all-reduce is pluggable: NCCL over the TP process group (the baseline), or
 the in-kernel symmetric-memory all-reduce (``parallel.symm.SymmTeam``, NVLS
-``multimem.ld_reduce`` / ``multimem.st`` or one-shot peer loads).
+``multimem.ld_reduce`` / ``multimem.st`` or one-shot peer loads). With
+``make_mesh(..., sequence_parallel=True, fused=True)`` each sequence-parallel
+projection is instead one ``gemm_tp`` kernel (``parallel.tp_fused``): the
+all-gather or reduce-scatter runs inside the GEMM over NVLink, tile by tile.
 
 Reference: the Megatron plan of runtime/src/tensor_parallel.rs:8-29
 (column-parallel QKV and gate/up, row-parallel o_proj and down_proj, 2
@@ -50,6 +53,7 @@ class TPGroup:
     team: object = None  # SymmTeam for the in-kernel all-reduce (None: NCCL / gloo)
     _bufs: dict = None
     sp: bool = False  # sequence parallelism: the residual stream split by token
+    fused: object = None  # parallel.tp_fused.FusedTP: projections with the collective inside the GEMM
 
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -79,7 +83,9 @@ class Mesh:
     dp_group: object
 
 
-def make_mesh(tp_size: int, use_symm: bool = False, sequence_parallel: bool = False) -> Mesh:
+def make_mesh(tp_size: int, use_symm: bool = False, sequence_parallel: bool = False, fused: bool = False) -> Mesh:
+    """fused: (with sequence_parallel) every projection is one gemm_tp kernel with
+    its all-gather / reduce-scatter over NVLink inside it -- no NCCL call per layer."""
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
     assert world % tp_size == 0, "world size must be a multiple of the TP degree"
@@ -94,14 +100,21 @@ def make_mesh(tp_size: int, use_symm: bool = False, sequence_parallel: bool = Fa
             g = dist.new_group(list(range(t, world, tp_size)))
             if t == rank % tp_size:
                 dp_group = g
+    assert not fused or sequence_parallel, "the fused projections work on token-split rows (sequence parallelism)"
     team = None
-    if use_symm and tp_size > 1:
+    if (use_symm or fused) and tp_size > 1:
         from .symm import SymmTeam
         from .dist import DistInfo
 
         info = DistInfo(rank, world, rank, torch.device("cuda", torch.cuda.current_device()), "nccl")
         team = SymmTeam(info, group=tp_group)
-    return Mesh(TPGroup(rank % tp_size, tp_size, tp_group, team, sp=sequence_parallel and tp_size > 1),
+    fused_tp = None
+    if fused and tp_size > 1:
+        from .tp_fused import FusedTP
+
+        fused_tp = FusedTP(team)
+    return Mesh(TPGroup(rank % tp_size, tp_size, tp_group, team if use_symm else None,
+                        sp=sequence_parallel and tp_size > 1, fused=fused_tp),
                 rank // tp_size, dp_size, dp_group)
 
 
@@ -288,10 +301,18 @@ class _SPGather(torch.autograd.Function):
 
 
 def sp_column_linear(h, w, tp):
+    if tp.fused is not None and h.is_cuda and tp.fused.supports(h.shape[0]):
+        from .tp_fused import fused_column_linear
+
+        return fused_column_linear(h, w, tp)
     return _SPColumnLinear.apply(h, w, tp)
 
 
 def sp_row_linear(o, w, r, tp):
+    if tp.fused is not None and o.is_cuda and tp.fused.supports(o.shape[0] // tp.world):
+        from .tp_fused import fused_row_linear
+
+        return fused_row_linear(o, w, r, tp)
     return _SPRowLinear.apply(o, w, r, tp)
 
 

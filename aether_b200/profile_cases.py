@@ -17,6 +17,7 @@ once on its own:
                                                     # (ncu --nvtx --nvtx-include "decode/" --metrics gpu__time_duration.sum)
     python -m aether_b200.profile_cases decode7b_tp8 # the same for one TP=8 rank's shards, emulated on one GPU
     python -m aether_b200.profile_cases rows 1      # one launch of each row / elementwise / loss / MoE / MLA / quant kernel
+    python -m aether_b200.profile_cases gemm_tp     # fused TP-training GEMMs, two ranks emulated on one GPU
 """
 from __future__ import annotations
 
@@ -175,8 +176,62 @@ def decode7b_tp8(reps):
     decode7b(reps, tp=EmulatedTP(0, 8))
 
 
+def gemm_tp(reps):
+    """The fused TP-training GEMM with two TP ranks emulated on one GPU (one
+    cooperative launch, 74 SMs per rank): all-gather -> qkv GEMM (8192 x 3072 x
+    2048) and o_proj GEMM -> reduce-scatter (8192 x 2048 x 1024), against the
+    plain tcgen05 GEMM doing the same math on the whole GPU. Prints CUDA-event
+    times (the emulated ranks share the GPU, so the fused launch does both
+    ranks' work)."""
+    tp, Ml, d, nq, nin = 2, 4096, 2048, 3072, 1024
+    M = tp * Ml
+    bf = dict(dtype=torch.bfloat16, device="cuda")
+    h = [torch.randn(Ml, d, **bf) for _ in range(tp)]
+    wq = [torch.randn(nq, d, **bf) * 0.02 for _ in range(tp)]
+    o = [torch.randn(M, nin, **bf) for _ in range(tp)]
+    wo = [torch.randn(d, nin, **bf) * 0.02 for _ in range(tp)]
+    ag = [[torch.zeros(M, d, **bf) for _ in range(tp)] for _ in range(2)]
+    agf = [[torch.zeros(tp * (Ml // 128), dtype=torch.int32, device="cuda") for _ in range(tp)] for _ in range(2)]
+    rs = [[torch.zeros(tp * Ml * d, **bf) for _ in range(tp)] for _ in range(2)]
+    rsf = [[torch.zeros((Ml // 128) * (d // 256) * 4, dtype=torch.int32, device="cuda") for _ in range(tp)]
+           for _ in range(2)]
+    y = [torch.empty(M, nq, **bf) for _ in range(tp)]
+    x = [torch.empty(Ml, d, **bf) for _ in range(tp)]
+    ptr = lambda ts: [t.data_ptr() for t in ts]
+    n = [0]
+
+    def fused():
+        k, e = n[0] & 1, (n[0] >> 1) + 1
+        n[0] += 1
+        F.gemm_tp(h, ag[k], wq, y, [], h, list(range(tp)), tp, Ml, False, 1, False, False, ptr(ag[k]), ptr(agf[k]),
+                    0, [], [], e, 0, 5.0)
+        F.gemm_tp(o, [], wo, x, [], [], list(range(tp)), tp, Ml, False, 0, True, False, [], [], 0, ptr(rs[k]),
+                    ptr(rsf[k]), 0, e, 5.0)
+
+    hf = torch.cat(h)
+
+    def plain():
+        for r in range(tp):
+            F.gemm(hf, wq[r])
+            F.gemm(o[r], wo[r])
+
+    for fn, tag in ((fused, "fused (2 emulated ranks)"), (plain, "plain gemm_bf16 x2")):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        flops = 2 * tp * (M * nq * d + M * d * nin)
+        ms = e0.elapsed_time(e1) / reps
+        print(f"gemm_tp {tag}: {ms * 1e3:.1f} us per AG-GEMM + GEMM-RS pair, {flops / ms / 1e9:.0f} TFLOP/s")
+
+
 CASES = {f.__name__: f for f in (gemm, attn_fwd, attn_bwd, skinny, decode_attn, decode_attn_b1, adamw, decode7b,
-                                 decode7b_tp8, rows)}
+                                 decode7b_tp8, rows, gemm_tp)}
 
 
 def main():

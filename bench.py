@@ -163,8 +163,17 @@ def parse():
     ap.add_argument("--pp", type=int, default=1, help="pipeline stages (1F1B over NCCL p2p); --gpus must equal --pp")
     ap.add_argument("--sp", action="store_true",
                     help="sequence parallelism inside TP (residual stream split by token over the TP ranks)")
-    ap.add_argument("--tp-comm", default="symm", choices=["symm", "nccl"],
-                    help="TP all-reduce: in-kernel symmetric-memory (NVLS / peer loads) or NCCL")
+    ap.add_argument("--tp-comm", default="fused", choices=["fused", "symm", "nccl"],
+                    help="TP communication. fused (default; implies --sp): every projection is one gemm_tp kernel "
+                    "with its all-gather / reduce-scatter over NVLink inside; symm: in-kernel symmetric-memory "
+                    "all-reduce after each row-parallel GEMM; nccl: NCCL collectives")
+    ap.add_argument("--zero", type=int, default=1, choices=[1, 2, 3],
+                    help="ZeRO stage of the data-parallel engine (2 / 3: sharded gradients and optimiser state, "
+                    "3 also parameters)")
+    ap.add_argument("--zero-comm", default="fused", choices=["fused", "nccl"],
+                    help="ZeRO-3 on GPUs. fused: each layer's parameter all-gather inside its first consuming "
+                    "GEMM and the gradient reduce-scatter by this library's kernels (no NCCL call per layer); "
+                    "nccl: NCCL all-gathers / reduce-scatters with prefetch")
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen2.5-7B TP=N serving section")
     ap.add_argument("--decode-batches", default="1,16,64")
     ap.add_argument("--decode-prompt", type=int, default=2048)
@@ -214,10 +223,25 @@ def main():
     if tp > 1:
         from aether_b200.parallel.tp_train import make_mesh
 
-        mesh = make_mesh(tp, use_symm=args.tp_comm == "symm", sequence_parallel=args.sp)
+        if args.tp_comm == "fused":
+            args.sp = True
+        mesh = make_mesh(tp, use_symm=args.tp_comm == "symm", sequence_parallel=args.sp,
+                         fused=args.tp_comm == "fused")
         dinfo = D.DistInfo(mesh.dp_rank, dp_world, info.local_rank, dev, info.backend)
     dp_mode = args.dp if (args.dp != "overlap" or mesh is None) else "fused"  # overlap: pure DP only
-    if dp_world > 1 and dp_mode in ("fused", "overlap"):
+    if args.zero > 1:
+        assert mesh is None, "--zero 2/3 with --tp is not wired into this benchmark"
+        from aether_b200.parallel.fsdp import ShardedDataParallel, ShardSpec
+
+        team = None
+        if args.zero == 3 and args.zero_comm == "fused" and world > 1:
+            from aether_b200.parallel.symm import SymmTeam
+
+            team = SymmTeam(info, timeout_s=60.0)
+        model = GPT(cfg, device=dev, seed=1234, shard=ShardSpec(info.rank, world, args.zero, fused=team))
+        dp = ShardedDataParallel(model.arena, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+        dp_mode = f"zero{args.zero}" + ("-fused" if team is not None else "")
+    elif dp_world > 1 and dp_mode in ("fused", "overlap"):
         from aether_b200.parallel.dp import FusedDataParallel, OverlappedDataParallel, team_alloc
         from aether_b200.parallel.symm import SymmTeam
 
@@ -241,7 +265,7 @@ def main():
             for _ in range(2)]
     dev_batch = host[0].to(dev)
 
-    dp_check = run_dp_check(info, dp_mode) if (dp_world > 1 and tp == 1 and dp_mode != "nccl") else None
+    dp_check = run_dp_check(info, dp_mode) if (dp_world > 1 and tp == 1 and dp_mode in ("fused", "overlap")) else None
 
     for _ in range(args.warmup):
         trainer.train_step(dev_batch)
@@ -270,7 +294,8 @@ def main():
     ms = D.all_reduce_max(ms, dev)
     tokens_per_step = args.global_batch * S
     value = tokens_per_step / (ms / 1e3)
-    in_sync = params_in_sync(model.arena, mesh.dp_group if mesh else None, dev) if dp_world > 1 else None
+    in_sync = (params_in_sync(model.arena, mesh.dp_group if mesh else None, dev)
+               if dp_world > 1 and args.zero == 1 else None)  # ZeRO-2/3 ranks hold different shards
 
     # ---------------------------------------------------------------- end-to-end region
     e2e = None
@@ -339,8 +364,9 @@ def main():
                 "parallelism": (f"tp{tp}x" if tp > 1 else "") + f"dp{dp_world}"
                 + ((" zero1 " + {"overlap": "fused-nvlink bucketed, overlapped with backward",
                                  "fused": "fused-nvlink after backward", "nccl": "nccl"}[dp_mode])
-                   if dp_world > 1 else "")
-                + (f" tp-allreduce-{args.tp_comm}" if tp > 1 else "") + (" sp" if tp > 1 and args.sp else ""),
+                   if dp_world > 1 and args.zero == 1 else "")
+                + (f" {dp_mode}" if args.zero > 1 else "")
+                + ((" tp-fused-gemm-ag-rs" if args.tp_comm == "fused" else f" tp-allreduce-{args.tp_comm}") if tp > 1 else "") + (" sp" if tp > 1 and args.sp else ""),
                 "optimizer": "AdamW lr 3e-4 betas (0.9,0.95) wd 0.1, fp32 master",
                 "l2": "no flush needed: per-step working set (2.7 GB bf16 weights + activations) >> 126 MB L2",
             },

@@ -7,6 +7,18 @@ namespace aether {
 // gemm_sm100.cu
 void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn, std::optional<at::Tensor> bias,
                std::optional<at::Tensor> residual, double alpha, bool accumulate, std::optional<at::Tensor> alpha_t);
+// gemm_tp.cu
+std::string gemm_tp(std::vector<at::Tensor> a_local, std::vector<at::Tensor> a_ag, std::vector<at::Tensor> b,
+             std::vector<at::Tensor> out, std::vector<at::Tensor> residual, std::vector<at::Tensor> push_src,
+             std::vector<int64_t> ranks, int64_t tp, int64_t Ml, bool b_mn, int64_t ag_mode, bool rs,
+             bool local_copy, std::vector<int64_t> ag_buf, std::vector<int64_t> ag_flag, int64_t ag_mc,
+             std::vector<int64_t> rs_buf, std::vector<int64_t> rs_flag, int64_t ag_epoch, int64_t rs_epoch,
+             double timeout_s);
+std::string gemm_param_gather(std::vector<at::Tensor> a, std::vector<at::Tensor> b, std::vector<at::Tensor> out,
+                       std::vector<at::Tensor> shard, std::vector<at::Tensor> ctr, std::vector<int64_t> ranks,
+                       int64_t world, int64_t chunk, bool b_mn, std::vector<int64_t> unit_buf,
+                       std::vector<int64_t> flags, std::vector<int64_t> ready, int64_t mc, int64_t epoch,
+                       double timeout_s);
 // norm.cu
 void rmsnorm_fwd(at::Tensor x, std::optional<at::Tensor> res, at::Tensor w, at::Tensor y,
                  std::optional<at::Tensor> h_out, std::optional<at::Tensor> rstd, double eps);
@@ -136,6 +148,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &aether::gemm_bf16, "a"_a, "b"_a, "out"_a, "a_mn"_a, "b_mn"_a, "bias"_a = pybind11::none(),
         "residual"_a = pybind11::none(), "alpha"_a = 1.0, "accumulate"_a = false,
         "alpha_t"_a = pybind11::none());
+  m.def("gemm_tp", &aether::gemm_tp, "a_local"_a, "a_ag"_a, "b"_a, "out"_a, "residual"_a, "push_src"_a, "ranks"_a,
+        "tp"_a, "Ml"_a, "b_mn"_a, "ag_mode"_a, "rs"_a, "local_copy"_a, "ag_buf"_a, "ag_flag"_a, "ag_mc"_a,
+        "rs_buf"_a, "rs_flag"_a, "ag_epoch"_a, "rs_epoch"_a, "timeout_s"_a,
+        "tcgen05 GEMM with the TP all-gather / reduce-scatter fused in (sequence-parallel training)");
+  m.def("gemm_param_gather", &aether::gemm_param_gather, "a"_a, "b"_a, "out"_a, "shard"_a, "ctr"_a, "ranks"_a,
+        "world"_a, "chunk"_a, "b_mn"_a, "unit_buf"_a, "flags"_a, "ready"_a, "mc"_a, "epoch"_a, "timeout_s"_a,
+        "tcgen05 GEMM whose weight operand is all-gathered (ZeRO-3) inside the same kernel");
   m.def("rmsnorm_fwd", &aether::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &aether::rmsnorm_bwd);
   m.def("layernorm_fwd", &aether::layernorm_fwd);

@@ -199,19 +199,21 @@ def check_pp(info):
     print(f"OK pp losses={[round(float(x), 4) for x in t]}", flush=True)
 
 
-def check_tp_train(info, sp=False):
+def check_tp_train(info, sp=False, fused=False):
     """Megatron TP over all ranks (in-kernel symmetric-memory all-reduce; with
-    sp, NCCL reduce-scatter / all-gather around a token-split residual) against
-    one GPU."""
+    sp, NCCL reduce-scatter / all-gather around a token-split residual; with
+    fused, every projection one gemm_tp kernel with its all-gather /
+    reduce-scatter inside) against one GPU."""
     from aether_b200.models.gpt import GPT, GPTConfig
     from aether_b200.parallel.tp_train import make_mesh, shard_tensor
 
     w = info.world
     cfg = GPTConfig(vocab=512, d_model=128 * w, n_layers=2, n_heads=w, n_kv_heads=w, d_ff=256 * w, max_seq=128)
-    mesh = make_mesh(w, use_symm=True, sequence_parallel=sp)
+    mesh = make_mesh(w, use_symm=not fused, sequence_parallel=sp, fused=fused)
     m = GPT(cfg, device=info.device, seed=13, tp=mesh.tp)
     ref = GPT(cfg, device=info.device, seed=13)
-    toks = torch.randint(0, 512, (2, 129), generator=torch.Generator().manual_seed(2))
+    # fused: 256 token rows per rank (a multiple of the kernel's 128-row tiles)
+    toks = torch.randint(0, 512, (2 * w if fused else 2, 129), generator=torch.Generator().manual_seed(2))
     ids, tg = toks[:, :-1].contiguous().to(info.device), toks[:, 1:].contiguous().to(info.device)
     lt = m.loss(ids, tg)
     lt.backward()
@@ -227,7 +229,9 @@ def check_tp_train(info, sp=False):
         assert err < 5e-2, (n, err)
     torch.cuda.synchronize()
     assert _ext.check_status() == 0
-    print(f"OK tp_train{'_sp' if sp else ''} loss={float(lt.detach()):.4f}", flush=True)
+    if fused:
+        assert all(r.n_ag > 0 and r.n_rs > 0 for r in mesh.tp.fused.rings.values()), "fused path not taken"
+    print(f"OK tp_train{'_sp' if sp else ''}{'_fused' if fused else ''} loss={float(lt.detach()):.4f}", flush=True)
 
 
 def check_fsdp(info):
@@ -244,8 +248,12 @@ def check_fsdp(info):
     for t in toks:
         ref.loss(t[:, :-1].contiguous(), t[:, 1:].contiguous()).backward()
     dist.all_reduce(ref.arena.grad)
-    for stage in (2, 3):
-        m = GPT(cfg, device=info.device, seed=5, shard=ShardSpec(r, w, stage))
+    from aether_b200.parallel.symm import SymmTeam
+
+    for stage in (2, 3, "3-fused"):
+        # 3-fused: every layer's parameter all-gather inside its first consuming GEMM
+        spec = ShardSpec(r, w, 3, fused=SymmTeam(info)) if stage == "3-fused" else ShardSpec(r, w, stage)
+        m = GPT(cfg, device=info.device, seed=5, shard=spec)
         for t in toks:
             m.loss(t[:, :-1].contiguous(), t[:, 1:].contiguous()).backward()
         a = m.arena
@@ -262,8 +270,16 @@ def check_fsdp(info):
         eng.step()
         loss = m.loss(toks[0][:, :-1].contiguous(), toks[0][:, 1:].contiguous())
         assert torch.isfinite(loss)
+        if stage == "3-fused":
+            loss.backward()  # a second backward on the same slots (flags' use counts advance)
+            a._finish_grads()
+            assert sum(a._puses) >= 2 * cfg.n_layers, a._puses  # gathers ran inside the GEMMs
+            losses = [float(loss.detach())]
+            dist.all_gather_object(losses_all := [None] * w, losses[0])
+            assert all(abs(x - losses_all[0]) < 1e-6 for x in losses_all), losses_all
+            assert _ext.check_status() == 0
     torch.cuda.synchronize()
-    print(f"OK fsdp stages=2,3 world={w}", flush=True)
+    print(f"OK fsdp stages=2,3,3-fused world={w}", flush=True)
 
 
 def check_cp(info):
@@ -358,6 +374,7 @@ def main():
     if "tp_train" in which:
         check_tp_train(info)
         check_tp_train(info, sp=True)
+        check_tp_train(info, sp=True, fused=True)
     if "fsdp" in which:
         check_fsdp(info)
     if "cp" in which:
