@@ -47,6 +47,8 @@ class GPTConfig:
     qk_norm: bool = False  # Qwen3: per-head RMSNorm of q and k before RoPE
     qkv_bias: bool = False  # Qwen2: bias on the q / k / v projections
     head_dim_: int = 0  # explicit head dimension (0: d_model / n_heads)
+    attn_window: int = 0  # > 0: sliding-window attention (query i sees keys (i - window, i])
+    attn_softcap: float = 0.0  # > 0: attention logits soft-capped by softcap * tanh(s / softcap)
 
     @property
     def head_dim(self) -> int:
@@ -270,7 +272,8 @@ class GPT:
                 qkv = self._qk_norm(i, qkv, Hq, Hkv, D)
             qkv = A.rope_(qkv, pos, self.rope_cos, self.rope_sin, Hq + Hkv, D)
             if self.cp is None:
-                o = A.attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True)
+                o = A.attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True, window=cfg.attn_window,
+                                       softcap=cfg.attn_softcap)
             else:
                 from ..parallel.cp import cp_attention
 

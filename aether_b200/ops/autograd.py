@@ -199,21 +199,21 @@ class AttentionFn(torch.autograd.Function):
     """Causal attention over a packed qkv [B*S, (Hq + 2*Hkv) * D] buffer -> o [B*S, Hq*D]."""
 
     @staticmethod
-    def forward(ctx, qkv, B, S, Hq, Hkv, D, scale, causal):
+    def forward(ctx, qkv, B, S, Hq, Hkv, D, scale, causal, window=0, softcap=0.0):
         row = qkv.shape[1]
         q = qkv.view(B, S, row)[:, :, : Hq * D].view(B, S, Hq, D)
         k = qkv.view(B, S, row)[:, :, Hq * D : (Hq + Hkv) * D].view(B, S, Hkv, D)
         v = qkv.view(B, S, row)[:, :, (Hq + Hkv) * D :].view(B, S, Hkv, D)
         o = torch.empty(B, S, Hq, D, dtype=qkv.dtype, device=qkv.device)
-        o, lse = F.attention(q, k, v, scale, causal, 0, out=o)
+        o, lse = F.attention(q, k, v, scale, causal, 0, out=o, window=window, softcap=softcap)
         ctx.save_for_backward(qkv, o, lse)
-        ctx.cfg = (B, S, Hq, Hkv, D, scale, causal)
+        ctx.cfg = (B, S, Hq, Hkv, D, scale, causal, window, softcap)
         return o.view(B * S, Hq * D)
 
     @staticmethod
     def backward(ctx, do):
         qkv, o, lse = ctx.saved_tensors
-        B, S, Hq, Hkv, D, scale, causal = ctx.cfg
+        B, S, Hq, Hkv, D, scale, causal, window, softcap = ctx.cfg
         row = qkv.shape[1]
         v3 = qkv.view(B, S, row)
         q = v3[:, :, : Hq * D].view(B, S, Hq, D)
@@ -224,12 +224,15 @@ class AttentionFn(torch.autograd.Function):
         dq = d3[:, :, : Hq * D].view(B, S, Hq, D)
         dk = d3[:, :, Hq * D : (Hq + Hkv) * D].view(B, S, Hkv, D)
         dv = d3[:, :, (Hq + Hkv) * D :].view(B, S, Hkv, D)
-        F.attention_bwd(q, k, v, o, do.contiguous().view(B, S, Hq, D), lse, scale, causal, 0, dq=dq, dk=dk, dv=dv)
-        return dqkv, None, None, None, None, None, None, None
+        F.attention_bwd(q, k, v, o, do.contiguous().view(B, S, Hq, D), lse, scale, causal, 0, dq=dq, dk=dk, dv=dv,
+                        window=window, softcap=softcap)
+        return dqkv, None, None, None, None, None, None, None, None, None
 
 
-def attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True):
-    return AttentionFn.apply(qkv, B, S, Hq, Hkv, D, scale, causal)
+def attention_packed(qkv, B, S, Hq, Hkv, D, scale, causal=True, window=0, softcap=0.0):
+    """window > 0: sliding-window attention; softcap > 0: soft-capped logits
+    (forward and backward)."""
+    return AttentionFn.apply(qkv, B, S, Hq, Hkv, D, scale, causal, window, softcap)
 
 
 class SwiGLUFn(torch.autograd.Function):

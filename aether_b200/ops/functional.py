@@ -282,7 +282,7 @@ def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=T
     impl: "auto" (tcgen05 kernel when it applies, else the mma.sync kernel),
     "tc" or "fa2". Flex attention: ``window`` > 0 (sliding window: query i
     sees keys (i + offset - window, i + offset]) and ``softcap`` > 0 (logits
-    soft-capped by softcap * tanh(s / softcap)); forward only."""
+    soft-capped by softcap * tanh(s / softcap)); ``attention_bwd`` takes the same."""
     B, Sq, Hq, D = q.shape
     if _cuda(q):
         o = out if out is not None else torch.empty(B, Sq, Hq, D, dtype=q.dtype, device=q.device)
@@ -303,19 +303,22 @@ def attention(q, k, v, scale, causal=True, causal_offset=0, out=None, want_lse=T
 
 
 def attention_bwd(q, k, v, o, do, lse, scale, causal=True, causal_offset=0, dq=None, dk=None, dv=None,
-                  impl="auto"):
+                  impl="auto", window=0, softcap=0.0):
+    """Gradients of ``attention`` (same window / softcap; those forms run on
+    the mma.sync kernel)."""
     if _cuda(q):
         dq = dq if dq is not None else torch.empty_like(q)
         dk = dk if dk is not None else torch.empty(k.shape, dtype=k.dtype, device=k.device)
         dv = dv if dv is not None else torch.empty(v.shape, dtype=v.dtype, device=v.device)
         use_tc = impl == "tc" or (impl == "auto" and _tc_ok(q, k, v) and _tc_ok(do, dk, dv))
-        C().attention_bwd(q, k, v, o, do, lse, dq, dk, dv, float(scale), bool(causal), int(causal_offset), use_tc)
+        C().attention_bwd(q, k, v, o, do, lse, dq, dk, dv, float(scale), bool(causal), int(causal_offset), use_tc,
+                          int(window), float(softcap))
         return dq, dk, dv
     with torch.enable_grad():
         qf = q.detach().float().requires_grad_(True)
         kf = k.detach().float().requires_grad_(True)
         vf = v.detach().float().requires_grad_(True)
-        of, _ = ref.attention(qf, kf, vf, scale, causal, causal_offset)
+        of, _ = ref.attention(qf, kf, vf, scale, causal, causal_offset, window, softcap)
         gq, gk, gv = torch.autograd.grad(of, (qf, kf, vf), do.float())
     res = []
     for g, buf, like in ((gq, dq, q), (gk, dk, k), (gv, dv, v)):

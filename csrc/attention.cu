@@ -14,7 +14,7 @@
 //   * GQA is native (kv_head = q_head / group) -- no K/V copies;
 //   * `causal_offset` lets query i see keys <= i + offset (prefill on top of a
 //     KV cache);
-//   * flex attention (forward): `window` > 0 also hides keys < i + offset -
+//   * flex attention (forward and backward): `window` > 0 also hides keys < i + offset -
 //     window + 1 (sliding window), `softcap` > 0 maps the scaled logits
 //     through cap * tanh(s / cap).
 // Tiles live in shared memory with a 16-byte-chunk XOR swizzle so every
@@ -299,6 +299,8 @@ struct BwdParams {
   float scale;  // softmax scale
   int causal;
   int causal_offset;
+  int window;             // > 0: sliding window, as in the forward
+  float cap_in, cap_out;  // softcap > 0: scale / cap and cap * log2(e), as in the forward
 };
 
 // D[b,h,i] = sum_d dO[b,i,h,d] * O[b,i,h,d]; one warp per row.
@@ -467,9 +469,17 @@ __global__ void __launch_bounds__(256, 1) attn_bwd_kernel(BwdParams p) {
         const float lrow = (e >> 1) ? lb : la;
         bool ok = col < p.Sk && row < p.Sq;
         if (p.causal && col > row + p.causal_offset) ok = false;
-        const float pe = ok ? exp2f(s[nt][e] * scale_log2 - lrow) : 0.f;
+        if (p.window > 0 && col < row + p.causal_offset - p.window + 1) ok = false;
+        // soft-capped logits: z = cap tanh(s scale / cap), dz / d(s scale) = 1 - tanh^2
+        float logit2 = s[nt][e] * scale_log2, dcap = 1.f;
+        if (p.cap_in > 0.f) {
+          const float th = tanh_sfu(s[nt][e] * p.cap_in);
+          logit2 = p.cap_out * th;
+          dcap = 1.f - th * th;
+        }
+        const float pe = ok ? exp2f(logit2 - lrow) : 0.f;
         pv[e] = pe;
-        ds[e] = pe * (dp[nt][e] - ((e >> 1) ? db : da));
+        ds[e] = pe * (dp[nt][e] - ((e >> 1) ? db : da)) * dcap;
       }
       const int ch = colb >> 3, off = (colb & 7) * 2;
       *reinterpret_cast<uint32_t*>(sPp + swz<128>(ra, ch) + off) = pack_bf16(pv[0], pv[1]);
@@ -630,7 +640,7 @@ void attention_bwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor dout,
 // attention_bwd_sm100.cu; the rowsum(dO*O) pre-pass and the dQ conversion are shared.
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
                    at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset,
-                   bool use_tc) {
+                   bool use_tc, int64_t window, double softcap) {
   const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), D = q.size(3);
   const int64_t Sk = k.size(1), Hkv = k.size(2);
   attn::check_bshd(q, Hq, D, "attention_bwd q");
@@ -660,6 +670,8 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at:
         dsum.data_ptr<float>(), out.stride(0), out.stride(1), dout.stride(0), dout.stride(1), (int)B, (int)Hq, (int)Sq);
   AETHER_CUDA_CHECK(cudaGetLastError());
 
+  TORCH_CHECK(window >= 0 && softcap >= 0.0, "attention_bwd: window and softcap must be >= 0");
+  if (window > 0 || softcap > 0.0) use_tc = false;  // the flex forms run on the mma.sync kernel
   if (use_tc) {
     TORCH_CHECK(D == 128, "attention_bwd: the tcgen05 path needs head_dim 128");
     attention_bwd_tc(q, k, v, dout, lse, dsum, dq_acc, dk, dv, scale, causal, causal_offset);
@@ -685,6 +697,11 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at:
   p.scale = (float)scale;
   p.causal = causal ? 1 : 0;
   p.causal_offset = (int)causal_offset;
+  p.window = (int)window;
+  if (softcap > 0.0) {
+    p.cap_in = (float)(scale / softcap);
+    p.cap_out = (float)softcap * attn::kLog2e;
+  }
   dim3 grid((unsigned)((Sk + 63) / 64), (unsigned)(B * Hkv));
   if (D == 128) {
     constexpr int sm = attn::bwd_smem<128>();

@@ -58,7 +58,7 @@ void attention_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std
                    double scale, bool causal, int64_t causal_offset, int64_t window, double softcap);
 void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor dout, at::Tensor lse,
                    at::Tensor dq, at::Tensor dk, at::Tensor dv, double scale, bool causal, int64_t causal_offset,
-                   bool use_tc);
+                   bool use_tc, int64_t window, double softcap);
 // attention_sm100.cu
 void attention_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, std::optional<at::Tensor> lse,
                       double scale, bool causal, int64_t causal_offset, int64_t window, double softcap);
@@ -176,7 +176,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &aether::attention_fwd, "q"_a, "k"_a, "v"_a, "out"_a, "lse"_a, "scale"_a, "causal"_a,
         "causal_offset"_a, "window"_a = 0, "softcap"_a = 0.0);
   m.def("attention_bwd", &aether::attention_bwd, "q"_a, "k"_a, "v"_a, "out"_a, "dout"_a, "lse"_a, "dq"_a, "dk"_a,
-        "dv"_a, "scale"_a, "causal"_a, "causal_offset"_a, "use_tc"_a = false);
+        "dv"_a, "scale"_a, "causal"_a, "causal_offset"_a, "use_tc"_a = false, "window"_a = 0, "softcap"_a = 0.0);
   m.def("attention_fwd_tc", &aether::attention_fwd_tc, "q"_a, "k"_a, "v"_a, "out"_a, "lse"_a, "scale"_a, "causal"_a,
         "causal_offset"_a, "window"_a = 0, "softcap"_a = 0.0);
   m.def("skinny_gemm", &aether::skinny_gemm, "x"_a, "w"_a, "acc"_a, "splits"_a = 0, "acc_mc"_a = 0,

@@ -157,18 +157,21 @@ __device__ __forceinline__ bool flag_wait_ge(const uint32_t* f, uint32_t target,
   }
 }
 
-// Virtual tile t -> (tm, tn). The raster walks groups of gm M-tiles across N;
-// the M index is rotated so ag_mode 1 starts at this rank's rows and rs starts
-// at the next rank's rows (its own rows come last). gm divides Ml / BM, so a
-// group never mixes two ranks' rows and an rs CTA meets every foreign tile of
-// its sequence before any own tile.
+// Virtual tile t -> (tm, tn). The raster walks groups of gm M-tiles across N
+// (the last group possibly shorter); the M index is rotated so ag_mode 1
+// starts at this rank's rows and rs starts at the next rank's rows (its own
+// rows come last). In those modes gm divides Ml / BM, so a group never mixes
+// two ranks' rows and an rs CTA meets every foreign tile of its sequence
+// before any own tile.
 __device__ __forceinline__ void tile_coords(const Params& p, int rank, int t, int num_m, int num_n, int& tm,
                                             int& tn) {
   const int per_group = p.gm * num_n;
   const int g = t / per_group;
+  const int first = g * p.gm;
+  const int gsize = min(num_m - first, p.gm);  // the last group may be short (pg mode)
   const int r = t - g * per_group;
-  const int tv = g * p.gm + r % p.gm;
-  tn = r / p.gm;
+  const int tv = first + r % gsize;
+  tn = r / gsize;
   const int mt = p.Ml / BM;
   int start = 0;
   if (p.ag_mode == 1) start = rank * mt;

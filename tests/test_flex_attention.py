@@ -105,3 +105,39 @@ def test_gpu_flex_model_prefill_and_graph_decode():
     eager = m.generate(toks, 6, use_graph=False)
     graph = m.generate(toks, 6, use_graph=True)
     assert float((eager == graph).float().mean()) > 0.9
+
+
+def _fp32_grads(q, k, v, do, scale, window, softcap):
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    o, _ = ref.attention(qf, kf, vf, scale, True, 0, window, softcap)
+    return torch.autograd.grad(o, (qf, kf, vf), do.float())
+
+
+@pytest.mark.parametrize("window,softcap", [(0, 30.0), (48, 0.0), (33, 15.0)])
+def test_backward_flex_cpu(window, softcap):
+    """The CPU path of attention_bwd is autograd through the fp32 oracle with
+    the same window / softcap."""
+    q, k, v = _qkv(1, 40, 40, 2, 1, 16, seed=5)
+    do = torch.randn(1, 40, 2, 16, generator=torch.Generator().manual_seed(6)).bfloat16()
+    o, lse = F.attention(q, k, v, 0.25, True, window=window, softcap=softcap)
+    dq, dk, dv = F.attention_bwd(q, k, v, o, do, lse, 0.25, True, window=window, softcap=softcap)
+    for got, want in zip((dq, dk, dv), _fp32_grads(q, k, v, do, 0.25, window, softcap)):
+        assert float((got.float() - want).norm() / want.norm()) < 2e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("window,softcap", [(0, 30.0), (96, 0.0), (77, 20.0)])
+def test_gpu_backward_flex(D, window, softcap):
+    """Training backward with a sliding window and / or soft-capped logits (the
+    mma.sync kernel) against fp32 autograd through the oracle: GQA 4:2, a
+    ragged key count."""
+    q, k, v = _qkv(2, 200, 200, 4, 2, D, seed=7, device="cuda")
+    do = torch.randn(2, 200, 4, D, generator=torch.Generator().manual_seed(8)).bfloat16().cuda()
+    scale = D ** -0.5
+    o, lse = F.attention(q, k, v, scale, True, window=window, softcap=softcap)
+    dq, dk, dv = F.attention_bwd(q, k, v, o, do, lse, scale, True, window=window, softcap=softcap)
+    torch.cuda.synchronize()
+    for name, got, want in zip("qkv", (dq, dk, dv), _fp32_grads(q, k, v, do, scale, window, softcap)):
+        err = float((got.float() - want).norm() / want.norm())
+        assert err < 2e-2, (name, err)

@@ -134,18 +134,6 @@ def test_backward_modes(tp, Ml, n, d):
     _status_ok()
 
 
-def test_argument_checks():
-    """Shapes the kernel cannot tile are refused before anything launches."""
-    grp = Group(2, 128, 256, "cuda")
-    a = [torch.zeros(100, 256, dtype=torch.bfloat16, device="cuda")] * 2
-    w = [torch.zeros(256, 256, dtype=torch.bfloat16, device="cuda")] * 2
-    y = [torch.zeros(256, 256, dtype=torch.bfloat16, device="cuda")] * 2
-    with pytest.raises(RuntimeError, match="a_local"):
-        grp.call(a, grp.ag[0], w, y, [], a, False, 1, False, False, ag_slot=0, ag_ep=1)
-    with pytest.raises(RuntimeError, match="multiple of 128"):
-        F.gemm_tp(a, [], w, y, [], [], [0, 1], 2, 100, False, 0, True, False, [], [], 0, [1, 1], [1, 1], 0, 1, 1.0)
-
-
 @pytest.mark.parametrize("world,b_mn", [(2, False), (2, True), (4, False)])
 def test_param_gather_gemm(world, b_mn):
     """ZeRO-3 form: the weight lives in a flat parameter unit sharded over the

@@ -150,3 +150,23 @@ def test_tp2_qk_norm_matches_single_process():
     qk = {"qk_norm": True}
     _check(_run(2, 2, extra=qk), 2, qk)
     _check(_run(2, 2, sp=True, extra=qk), 2, qk)
+
+
+def test_fused_tp_gemm_refusals():
+    """The fused TP / ZeRO-3 GEMM entry points refuse what they cannot tile
+    with a message (raised by the Python wrappers), before touching a device."""
+    import pytest as _pytest
+
+    from aether_b200.ops import functional as F
+
+    a = [torch.zeros(100, 256, dtype=torch.bfloat16)] * 2
+    with _pytest.raises(RuntimeError, match="multiple of 128"):
+        F.gemm_tp(a, [], a, a, [], [], [0, 1], 2, 100, False, 0, True, False, [], [], 0, [16, 16], [16, 16], 0, 1, 1.0)
+    with _pytest.raises(RuntimeError, match="nothing to fuse"):
+        F.gemm_tp(a, [], a, a, [], [], [0, 1], 2, 128, False, 0, False, False, [], [], 0, [], [], 0, 0, 1.0)
+    sq = [torch.zeros(256, 256, dtype=torch.bfloat16)] * 2
+    with _pytest.raises(RuntimeError, match="CUDA tensors"):
+        F.gemm_tp(sq, sq, sq, sq, [], sq, [0, 1], 2, 128, False, 1, False, False, [16, 32], [16, 32], 0, [], [], 1, 0,
+                  1.0)
+    with _pytest.raises(RuntimeError, match="world unit buffers"):
+        F.gemm_param_gather(a, a, a, a, a, [0, 1], 2, 2048, False, [16], [16], [16], 0, 1, 1.0)
