@@ -16,6 +16,10 @@
    rank's accumulator and whose last CTA signals completion to the consuming
    finalize kernel, against the same GEMM followed by an NCCL all-reduce. Roofline: max(weight bytes / HBM bandwidth,
    output bytes over NVLink / link bandwidth).
+3. Tensor-parallel training projections (`--only tp_train`): the fused
+   all-gather -> GEMM and GEMM -> reduce-scatter kernels against NCCL around
+   the plain GEMM; roofline max(FLOPs / measured GEMM peak, NVLink bytes /
+   link bandwidth).
 Times are CUDA-event device times, max over ranks, after warm-up.
 """
 from __future__ import annotations
@@ -116,14 +120,84 @@ def tp_reduce(info, out):
     tp.close()
 
 
+def bf16_tflops():
+    try:
+        with open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")) as f:
+            return json.load(f)["bf16_tflops"]
+    except (OSError, KeyError, ValueError):
+        return 1590.0
+
+
+def tp_train(info, out):
+    """Fused tensor-parallel training projections (csrc/gemm_tp.cu) at the
+    GPT-24L micro-batch (16 x 2048 tokens, d 2048): the qkv all-gather -> GEMM
+    and the o_proj GEMM -> reduce-scatter (+ residual) of one layer, against
+    NCCL all-gather / reduce-scatter around the plain tcgen05 GEMM. Roofline of
+    the fused pair: the slower of its FLOPs at the measured GEMM peak and the
+    bytes this GPU must send over NVLink (its rows once, multicast where NVLS
+    is there, else once per peer; its partial sums of the other ranks' rows)
+    at the measured link rate."""
+    from .ops import functional as F
+    from .parallel.symm import SymmTeam
+    from .parallel.tp_fused import FusedTP
+
+    tp, d, M = info.world, 2048, 16 * 2048
+    Ml, nq, nin = M // tp, 3 * d // tp, d // tp
+    g = torch.Generator(device="cuda").manual_seed(info.rank)
+    bf = dict(dtype=torch.bfloat16, device="cuda")
+    h = torch.randn(Ml, d, generator=g, **bf)
+    wq = torch.randn(nq, d, generator=g, **bf) * 0.02
+    o = torch.randn(M, nin, generator=g, **bf)
+    wo = torch.randn(d, nin, generator=g, **bf) * 0.02
+    r = torch.randn(Ml, d, generator=g, **bf)
+    team = SymmTeam(info, timeout_s=60.0)
+    f = FusedTP(team)
+
+    def fused():
+        f.column(h, wq)
+        f.row(o, wo, r)
+
+    hf = torch.empty(M, d, **bf)
+    xs = torch.empty(Ml, d, **bf)
+
+    def nccl():
+        dist.all_gather_into_tensor(hf, h)
+        F.gemm(hf, wq)
+        y = F.gemm(o, wo)
+        dist.reduce_scatter_tensor(xs, y)
+        xs.add_(r)
+
+    t_f = timed(fused)
+    t_n = timed(nccl)
+    flops = 2.0 * M * nq * d + 2.0 * M * d * nin
+    mc = team.has_multicast
+    ag_bytes = Ml * d * 2 * (1 if mc else tp - 1)
+    rs_bytes = (tp - 1) * Ml * d * 2
+    t_comp = flops / (bf16_tflops() * 1e12) * 1e3
+    t_link = (ag_bytes + rs_bytes) / (LINK_GBS * 1e9) * 1e3
+    roof = max(t_comp, t_link)
+    out.append({"path": "tp_train_fused_ag_gemm_rs", "tp": tp, "tokens": M, "d_model": d, "multicast": mc,
+                "fused_ms": t_f, "nccl_ms": t_n, "speedup_vs_nccl": t_n / t_f, "roofline_ms": roof,
+                "roofline_compute_ms": t_comp, "roofline_nvlink_ms": t_link, "frac_of_roofline": roof / t_f})
+    del team
+
+
 def main():
+    import sys
+
     from .parallel import dist as D
 
+    only = sys.argv[sys.argv.index("--only") + 1].split(",") if "--only" in sys.argv else ["dp", "tp", "tp_train"]
     info = D.init(timeout_s=300)
     out = []
-    dp_step(info, out)
-    torch.cuda.empty_cache()
-    tp_reduce(info, out)
+    if "dp" in only:
+        dp_step(info, out)
+        torch.cuda.empty_cache()
+    if "tp" in only:
+        tp_reduce(info, out)
+        torch.cuda.empty_cache()
+    if "tp_train" in only:
+        tp_train(info, out)
     if info.rank == 0:
         for r in out:
             print(json.dumps(r), flush=True)
