@@ -406,9 +406,13 @@ def qwen_config_from_gguf(g: GGUFFile):
                       attn_softcap=float(m("attn_logit_softcapping", 0.0)))
 
 
-def load_qwen_weights(path: str, device="cuda"):
+def load_qwen_weights(path: str, device="cuda", keep_quant: bool = False):
     """GGUF (llama.cpp tensor names; architectures qwen2, qwen3, llama, mistral)
-    -> QwenWeights on `device` (bf16)."""
+    -> QwenWeights on `device` (bf16). keep_quant: the four projection groups
+    of every layer stay in the file's own blocks on the device (each part its
+    own type) and are expanded to bf16 into one shared scratch right before
+    each GEMM -- the weights take the file's size in memory, at the cost of an
+    expansion per use; embeddings, norms, biases and the LM head are bf16."""
     from ..models.qwen import QwenWeights
 
     g = GGUFFile(path)
@@ -417,6 +421,22 @@ def load_qwen_weights(path: str, device="cuda"):
     w.cfg, w.device, w.tp_rank, w.tp_size = cfg, torch.device(device), 0, 1
     w.hq, w.hkv, w.f = cfg.n_heads, cfg.n_kv_heads, cfg.d_ff
     t = lambda n: g.tensor(n).to(device)  # noqa: E731
+    if keep_quant:
+        from ..models.qlora_gguf import GGUFPart, GGUFWeight
+
+        holder = {}
+
+        def scratch(n):
+            buf = holder.get("buf")
+            if buf is None or buf.numel() < n:
+                buf = holder["buf"] = torch.empty(n, dtype=torch.bfloat16, device=device)
+            return buf[:n]
+
+        def q(*names):
+            return GGUFWeight([GGUFPart(g, nm, device) for nm in names], scratch)
+    else:
+        def q(*names):
+            return torch.cat([t(nm) for nm in names]).contiguous() if len(names) > 1 else t(names[0])
     w.embed = t("token_embd.weight")
     w.lm_head = w.embed if cfg.tie_embeddings else t("output.weight")
     w.final_norm = t("output_norm.weight")
@@ -430,12 +450,12 @@ def load_qwen_weights(path: str, device="cuda"):
             w.k_norm.append(t(p + "attn_k_norm.weight"))
         w.attn_norm.append(t(p + "attn_norm.weight"))
         w.mlp_norm.append(t(p + "ffn_norm.weight"))
-        w.wqkv.append(torch.cat([t(p + "attn_q.weight"), t(p + "attn_k.weight"), t(p + "attn_v.weight")]).contiguous())
+        w.wqkv.append(q(p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"))
         w.bqkv.append(torch.cat([t(p + "attn_q.bias"), t(p + "attn_k.bias"), t(p + "attn_v.bias")]).contiguous()
                       if cfg.qkv_bias else None)
-        w.wo.append(t(p + "attn_output.weight"))
-        w.wgu.append(torch.cat([t(p + "ffn_gate.weight"), t(p + "ffn_up.weight")]).contiguous())
-        w.wd.append(t(p + "ffn_down.weight"))
+        w.wo.append(q(p + "attn_output.weight"))
+        w.wgu.append(q(p + "ffn_gate.weight", p + "ffn_up.weight"))
+        w.wd.append(q(p + "ffn_down.weight"))
     return cfg, w
 
 

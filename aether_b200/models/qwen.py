@@ -356,6 +356,12 @@ class QwenModel:
         self.mega_batches = {1, 2, 4} if forced else set()
 
     # ------------------------------------------------------------------ buffers
+    def _mat(self, t):
+        """A projection as a bf16 [N, K] tensor: GGUF-quantised weights kept on
+        the device (``load_qwen_weights(..., keep_quant=True)``) are expanded
+        into the weights' shared scratch right before their GEMM."""
+        return t if isinstance(t, torch.Tensor) else t.bf16()
+
     def _auto_splits(self, B: int) -> int:
         """Key splits of the decode attention for batch size B: enough
         (sequence, KV head, split) CTAs for about two per SM, and no more --
@@ -413,7 +419,7 @@ class QwenModel:
         row = (self.hq + 2 * self.hkv) * D
         for i in range(cfg.n_layers):
             h, _, _ = F.rmsnorm(x, w.attn_norm[i], cfg.norm_eps)
-            qkv = F.gemm(h, w.wqkv[i], bias=w.bqkv[i])
+            qkv = F.gemm(h, self._mat(w.wqkv[i]), bias=w.bqkv[i])
             self._qk_norm(i, qkv)
             F.rope_kv_append(qkv, pos, slot_t, *self.rope_cs[i], self.cache.k[i], self.cache.v[i], self.hq,
                              self.hkv, D, page_table=self.page_table)
@@ -437,9 +443,9 @@ class QwenModel:
                                    softcap=self.softcap)
             o2 = o.view(T, self.hq * D)
             if self.tp is None:
-                x = F.gemm(o2, w.wo[i], residual=x)
+                x = F.gemm(o2, self._mat(w.wo[i]), residual=x)
             else:
-                y = F.gemm(o2, w.wo[i])
+                y = F.gemm(o2, self._mat(w.wo[i]))
                 self.tp.all_reduce_(y)
                 x = x + y
             h, _, _ = F.rmsnorm(x, w.mlp_norm[i], cfg.norm_eps)
@@ -468,10 +474,10 @@ class QwenModel:
     def _ffn(self, i: int, h: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         """x + FFN(h) for token rows (prefill); subclasses swap the FFN."""
         w = self.w
-        act = F.swiglu(F.gemm(h, w.wgu[i]))
+        act = F.swiglu(F.gemm(h, self._mat(w.wgu[i])))
         if self.tp is None:
-            return F.gemm(act, w.wd[i], residual=x)
-        y = F.gemm(act, w.wd[i])
+            return F.gemm(act, self._mat(w.wd[i]), residual=x)
+        y = F.gemm(act, self._mat(w.wd[i]))
         self.tp.all_reduce_(y)
         return x + y
 
@@ -510,40 +516,40 @@ class QwenModel:
         push = self._push_for(B)
         for i in range(L):
             if fused_ep:  # bias + RoPE + KV append finished inside the GEMM
-                F.skinny_gemm_qkv(h, w.wqkv[i], acc, b["tiles"], w.bqkv[i], qkv, pos, slot, *self.rope_cs[i],
+                F.skinny_gemm_qkv(h, self._mat(w.wqkv[i]), acc, b["tiles"], w.bqkv[i], qkv, pos, slot, *self.rope_cs[i],
                                   self.cache.k[i], self.cache.v[i], self.hq, self.hkv, page_table=self.page_table)
             else:
-                F.skinny_gemm(h, w.wqkv[i], acc)
+                F.skinny_gemm(h, self._mat(w.wqkv[i]), acc)
                 F.qkv_finalize_rope(acc, w.bqkv[i], qkv, pos, slot, *self.rope_cs[i], self.cache.k[i],
                                     self.cache.v[i], self.hq, self.hkv, D, page_table=self.page_table)
             F.decode_attention(qkv, self.cache.k[i], self.cache.v[i], slot, seqlen, o, self.hq, self.scale,
                                self._auto_splits(B), b["part_o"], b["part_lse"], b["counters"], page_table=self.page_table,
                                window=self.win[i], softcap=self.softcap)
             if push:  # local GEMM, then one push-reduce + residual + RMSNorm kernel
-                F.skinny_gemm(o, w.wo[i], acc)
+                F.skinny_gemm(o, self._mat(w.wo[i]), acc)
                 self.tp.push_reduce(acc, x2, res=x, w=w.mlp_norm[i], h=h, eps=cfg.norm_eps)
             else:
                 if self.tp is None:
-                    F.skinny_gemm(o, w.wo[i], acc)
+                    F.skinny_gemm(o, self._mat(w.wo[i]), acc)
                     racc = acc
                 else:
-                    racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)  # GEMM + all-reduce in one kernel
+                    racc = self.tp.reduce_gemm(o, self._mat(w.wo[i]), 2 * i)  # GEMM + all-reduce in one kernel
                 F.finalize_residual_norm(racc, x2, w.mlp_norm[i], h, res=x, eps=cfg.norm_eps, wait=self._tp_wait())
             if fused_ep:  # SwiGLU finished inside the gate/up GEMM
-                F.skinny_gemm_swiglu(h, w.wgu[i], acc, act, b["tiles"])
+                F.skinny_gemm_swiglu(h, self._mat(w.wgu[i]), acc, act, b["tiles"])
             else:
-                F.skinny_gemm(h, w.wgu[i], acc)
+                F.skinny_gemm(h, self._mat(w.wgu[i]), acc)
                 F.skinny_finalize(acc, act, swiglu=True)
             nw = w.attn_norm[i + 1] if i + 1 < L else w.final_norm
             if push:
-                F.skinny_gemm(act, w.wd[i], acc)
+                F.skinny_gemm(act, self._mat(w.wd[i]), acc)
                 self.tp.push_reduce(acc, x, res=x2, w=nw, h=h, eps=cfg.norm_eps)
                 continue
             if self.tp is None:
-                F.skinny_gemm(act, w.wd[i], acc)
+                F.skinny_gemm(act, self._mat(w.wd[i]), acc)
                 racc = acc
             else:
-                racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
+                racc = self.tp.reduce_gemm(act, self._mat(w.wd[i]), 2 * i + 1)
             F.finalize_residual_norm(racc, x, nw, h, res=x2, eps=cfg.norm_eps, wait=self._tp_wait())
         self._decode_head(B, h, acc)
 
@@ -590,6 +596,8 @@ class QwenModel:
             return False
         if not self.fused_decode or cfg.head_dim != 128 or self.softcap or any(self.win):
             return False
+        if not isinstance(self.w.wqkv[0], torch.Tensor):
+            return False  # quantised weights are expanded per projection; the one-kernel step streams bf16
         d, f, hq, hkv = cfg.d_model, self.f, self.hq, self.hkv
         if d % 8 or f % 8 or hq % hkv or hq // hkv > 8:
             return False
@@ -682,7 +690,7 @@ class QwenModel:
         x.copy_(F.embedding(w.embed, b["tok"][:B]))
         for i in range(cfg.n_layers):
             F.rmsnorm_into(x, w.attn_norm[i], h, cfg.norm_eps)
-            F.skinny_gemm(h, w.wqkv[i], acc)
+            F.skinny_gemm(h, self._mat(w.wqkv[i]), acc)
             F.skinny_finalize(acc, qkv, bias=w.bqkv[i])
             self._qk_norm(i, qkv)
             F.rope_kv_append(qkv, pos, slot, *self.rope_cs[i], self.cache.k[i], self.cache.v[i], self.hq, self.hkv, D,
@@ -691,13 +699,13 @@ class QwenModel:
                                self._auto_splits(B), b["part_o"], b["part_lse"], page_table=self.page_table,
                                window=self.win[i], softcap=self.softcap)
             if self._push_for(B):
-                F.skinny_gemm(o, w.wo[i], acc)
+                F.skinny_gemm(o, self._mat(w.wo[i]), acc)
                 self.tp.push_reduce(acc, x2, res=x)
             elif self.tp is None:
-                F.skinny_gemm(o, w.wo[i], acc)
+                F.skinny_gemm(o, self._mat(w.wo[i]), acc)
                 F.skinny_finalize(acc, x2, res=x)
             else:
-                racc = self.tp.reduce_gemm(o, w.wo[i], 2 * i)
+                racc = self.tp.reduce_gemm(o, self._mat(w.wo[i]), 2 * i)
                 F.skinny_finalize(racc, x2, res=x, wait=self._tp_wait())
             F.rmsnorm_into(x2, w.mlp_norm[i], h, cfg.norm_eps)
             self._decode_ffn(i, h, x2, x, act, acc)
@@ -723,16 +731,16 @@ class QwenModel:
     def _decode_ffn(self, i, h, x2, x, act, acc) -> None:
         """x = x2 + FFN(h) on the decode rows (static buffers)."""
         w = self.w
-        F.skinny_gemm(h, w.wgu[i], acc)
+        F.skinny_gemm(h, self._mat(w.wgu[i]), acc)
         F.skinny_finalize(acc, act, swiglu=True)
         if self._push_for(h.shape[0]):
-            F.skinny_gemm(act, w.wd[i], acc)
+            F.skinny_gemm(act, self._mat(w.wd[i]), acc)
             self.tp.push_reduce(acc, x, res=x2)
         elif self.tp is None:
-            F.skinny_gemm(act, w.wd[i], acc)
+            F.skinny_gemm(act, self._mat(w.wd[i]), acc)
             F.skinny_finalize(acc, x, res=x2)
         else:
-            racc = self.tp.reduce_gemm(act, w.wd[i], 2 * i + 1)
+            racc = self.tp.reduce_gemm(act, self._mat(w.wd[i]), 2 * i + 1)
             F.skinny_finalize(racc, x, res=x2, wait=self._tp_wait())
 
     def _bucket(self, B: int) -> int:
@@ -823,7 +831,7 @@ class QwenModel:
         pos = torch.arange(S, device=self.device)
         for i in range(cfg.n_layers):
             h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.attn_norm[i].float()
-            qkv = h @ w.wqkv[i].float().t()
+            qkv = h @ self._mat(w.wqkv[i]).float().t()
             if w.bqkv[i] is not None:
                 qkv = qkv + w.bqkv[i].float()
             if cfg.qk_norm:
@@ -839,7 +847,7 @@ class QwenModel:
             k = qkv[..., self.hq * D : (self.hq + self.hkv) * D].view(B, S, self.hkv, D)
             v = qkv[..., (self.hq + self.hkv) * D :].view(B, S, self.hkv, D)
             o, _ = ref.attention(q, k, v, self.scale, True, 0, self.win[i], self.softcap)
-            x = x + o.reshape(B, S, -1) @ w.wo[i].float().t()
+            x = x + o.reshape(B, S, -1) @ self._mat(w.wo[i]).float().t()
             h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.mlp_norm[i].float()
             x = x + self._reference_ffn(i, h)
         h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w.final_norm.float()
@@ -848,5 +856,5 @@ class QwenModel:
 
     def _reference_ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:
         w = self.w
-        g, u = (h @ w.wgu[i].float().t()).chunk(2, -1)
-        return (torch.nn.functional.silu(g) * u) @ w.wd[i].float().t()
+        g, u = (h @ self._mat(w.wgu[i]).float().t()).chunk(2, -1)
+        return (torch.nn.functional.silu(g) * u) @ self._mat(w.wd[i]).float().t()

@@ -244,6 +244,9 @@ def main():
     ap.add_argument("--vision", action="store_true", help="also serve a DINOv3 ViT-L/16-shape /v1/vision/embed")
     ap.add_argument("--rate-limit", type=float, default=0.0, help="POST requests per second per client (0 = off)")
     ap.add_argument("--gguf", default=None, help="load Qwen2 weights (and tokenizer) from a GGUF file")
+    ap.add_argument("--keep-quant", action="store_true",
+                    help="with --gguf: keep the projections in the file's quantised blocks on the device (the "
+                    "file's size in memory) and expand each right before its GEMM")
     ap.add_argument("--hf", default=None, help="load Qwen2 weights from a Hugging Face directory")
     ap.add_argument("--tp", type=int, default=1,
                     help="tensor-parallel degree; launch with torchrun --nproc-per-node N (rank 0 serves HTTP)")
@@ -280,7 +283,9 @@ def main():
                 raise SystemExit("--tp with a deepseek2 GGUF is not supported yet (random-init presets are)")
             cfg, weights = gguf.load_deepseek_weights(args.gguf, device=args.device)
         else:
-            cfg, weights = gguf.load_qwen_weights(args.gguf, device=load_dev)
+            if args.keep_quant and args.tp > 1:
+                raise SystemExit("--keep-quant serves one GPU (the TP shards are bf16)")
+            cfg, weights = gguf.load_qwen_weights(args.gguf, device=load_dev, keep_quant=args.keep_quant)
         if not args.tokenizer:
             tok = gguf.tokenizer_from_gguf(g)
         template = JinjaChatTemplate.from_gguf(g) or template

@@ -191,3 +191,41 @@ def test_qlora_smoke_command_line(tmp_path):
     assert qlora_smoke.main(["--gguf", path, "--lo", "0", "--hi", "2", "--steps", "8", "--device", "cpu"]) == 0
     assert qlora_smoke.main(["--gguf", path, "--lo", "1", "--hi", "2", "--steps", "8", "--device", "cpu"]) == 0
     assert qlora_smoke.main(["--gguf", path, "--lo", "1", "--hi", "5", "--device", "cpu"]) == 2
+
+
+def _serve_pair(path, device):
+    from aether_b200.models.qwen import QwenModel
+
+    cfg_d, w_d = G.load_qwen_weights(path, device=device)
+    cfg_q, w_q = G.load_qwen_weights(path, device=device, keep_quant=True)
+    assert not isinstance(w_q.wqkv[0], torch.Tensor) and w_q.wqkv[0].parts[0].blocks is not None
+    md = QwenModel(cfg_d, device=device, weights=w_d, max_batch=2, max_seq=64)
+    mq = QwenModel(cfg_q, device=device, weights=w_q, max_batch=2, max_seq=64)
+    return md, mq
+
+
+def test_serving_keeps_gguf_weights_quantised(tmp_path):
+    """Serving a GGUF model with its projections kept in the file's blocks
+    (expanded per GEMM) gives the same logits and tokens as serving the
+    dequantised bf16 weights."""
+    path = _write_base(str(tmp_path / "base.gguf"), seed=5)
+    md, mq = _serve_pair(path, "cpu")
+    toks = torch.randint(0, V, (2, 11), generator=torch.Generator().manual_seed(6))
+    _, ld = md.prefill(toks, return_logits=True)
+    _, lq = mq.prefill(toks, return_logits=True)
+    assert torch.equal(ld, lq)
+    assert torch.equal(md.generate(toks, 4, use_graph=False), mq.generate(toks, 4, use_graph=False))
+
+
+@pytest.mark.gpu
+def test_gpu_serving_keeps_gguf_weights_quantised(tmp_path):
+    """The same on the device, with CUDA-graph decode (the per-projection
+    expansions are captured with the GEMMs)."""
+    path = _write_base(str(tmp_path / "base.gguf"), seed=7)
+    md, mq = _serve_pair(path, "cuda")
+    toks = torch.randint(0, V, (2, 11), generator=torch.Generator().manual_seed(8)).cuda()
+    _, ld = md.prefill(toks, return_logits=True)
+    _, lq = mq.prefill(toks, return_logits=True)
+    assert float((ld.float() - lq.float()).abs().max()) < 1e-2 * float(ld.float().abs().max())
+    gd, gq = md.generate(toks, 6, use_graph=True), mq.generate(toks, 6, use_graph=True)
+    assert float((gd == gq).float().mean()) >= 0.9
