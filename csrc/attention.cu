@@ -303,11 +303,12 @@ struct BwdParams {
   float cap_in, cap_out;  // softcap > 0: scale / cap and cap * log2(e), as in the forward
 };
 
-// D[b,h,i] = sum_d dO[b,i,h,d] * O[b,i,h,d]; one warp per row.
+// D[b,h,i] = sum_d dO[b,i,h,d] * O[b,i,h,d]; one warp per row. The same warp
+// zeroes the row's fp32 dQ accumulator dq_acc[b,i,h,:] (no separate memset).
 template <int D>
 __global__ void attn_bwd_dsum_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
-                                     float* __restrict__ dsum, int64_t o_bs, int64_t o_rs, int64_t do_bs,
-                                     int64_t do_rs, int B, int Hq, int Sq) {
+                                     float* __restrict__ dsum, float* __restrict__ dq_acc, int64_t o_bs,
+                                     int64_t o_rs, int64_t do_bs, int64_t do_rs, int B, int Hq, int Sq) {
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (wid >= (int64_t)B * Hq * Sq) return;
@@ -324,6 +325,8 @@ __global__ void attn_bwd_dsum_kernel(const __nv_bfloat16* __restrict__ o, const 
   }
   s = warp_sum(s);
   if (lane == 0) dsum[wid] = s;
+  float* q_acc = dq_acc + (((int64_t)b * Sq + i) * Hq + h) * D;
+  for (int c = lane * 4; c < D; c += 128) *reinterpret_cast<float4*>(q_acc + c) = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 template <int D>
@@ -657,17 +660,19 @@ void attention_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at:
   auto stream = at::cuda::getCurrentCUDAStream();
   if (B == 0 || Sq == 0) return;
   auto dsum = at::empty({B, Hq, Sq}, q.options().dtype(at::kFloat));
-  auto dq_acc = at::zeros({B, Sq, Hq, D}, q.options().dtype(at::kFloat));
+  auto dq_acc = at::empty({B, Sq, Hq, D}, q.options().dtype(at::kFloat));  // zeroed by the dsum pre-pass
   const int64_t rows = B * Hq * Sq;
   const unsigned dgrid = (unsigned)((rows * 32 + 255) / 256);
   if (D == 128)
     attn::attn_bwd_dsum_kernel<128><<<dgrid, 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
-        dsum.data_ptr<float>(), out.stride(0), out.stride(1), dout.stride(0), dout.stride(1), (int)B, (int)Hq, (int)Sq);
+        dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), out.stride(0), out.stride(1), dout.stride(0), dout.stride(1),
+        (int)B, (int)Hq, (int)Sq);
   else
     attn::attn_bwd_dsum_kernel<64><<<dgrid, 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
-        dsum.data_ptr<float>(), out.stride(0), out.stride(1), dout.stride(0), dout.stride(1), (int)B, (int)Hq, (int)Sq);
+        dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), out.stride(0), out.stride(1), dout.stride(0), dout.stride(1),
+        (int)B, (int)Hq, (int)Sq);
   AETHER_CUDA_CHECK(cudaGetLastError());
 
   TORCH_CHECK(window >= 0 && softcap >= 0.0, "attention_bwd: window and softcap must be >= 0");

@@ -180,7 +180,10 @@ __device__ __forceinline__ void tile_coords(const Params& p, int rank, int t, in
   if (tm >= num_m) tm -= num_m;
 }
 
-template <bool B_MN>
+// EMU: ranks emulated on one GPU (rank = blockIdx.y, descriptors picked at run
+// time); otherwise one rank per GPU and every descriptor at a fixed parameter
+// address, as in the plain GEMM.
+template <bool B_MN, bool EMU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tp_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   __shared__ int s_ticket;
 
-  const int y = blockIdx.y;
+  const int y = EMU ? (int)blockIdx.y : 0;
   const RankArgs& ra = p.r[y];
   const int rank = ra.rank;
   const CUtensorMap* tmA = &maps.a_local[y];
@@ -789,11 +792,13 @@ std::string gemm_tp(std::vector<at::Tensor> a_local, std::vector<at::Tensor> a_a
     }
   }
 
-  auto kern = b_mn ? gemm_tp_kernel<true> : gemm_tp_kernel<false>;
-  static bool attr_set[2][64] = {};
-  if (!attr_set[b_mn][dev]) {
+  auto kern = ne > 1 ? (b_mn ? gemm_tp_kernel<true, true> : gemm_tp_kernel<false, true>)
+                     : (b_mn ? gemm_tp_kernel<true, false> : gemm_tp_kernel<false, false>);
+  static bool attr_set[4][64] = {};
+  const int variant = (b_mn ? 1 : 0) + (ne > 1 ? 2 : 0);
+  if (!attr_set[variant][dev]) {
     AETHER_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    attr_set[b_mn][dev] = true;
+    attr_set[variant][dev] = true;
   }
   const int64_t tiles = (M / BM) * ((N + BN - 1) / BN);
   const int per_rank = std::max(1, num_sms(dev) / ne);
@@ -927,11 +932,13 @@ std::string gemm_param_gather(std::vector<at::Tensor> a, std::vector<at::Tensor>
     maps.c[y] = make_tmap_2d(out[y].data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, out[y].stride(0) * 2, 64, 32,
                              CU_TENSOR_MAP_SWIZZLE_128B);
   }
-  auto kern = b_mn ? gemm_tp_kernel<true> : gemm_tp_kernel<false>;
-  static bool attr_set[2][64] = {};
-  if (!attr_set[b_mn][dev]) {
+  auto kern = ne > 1 ? (b_mn ? gemm_tp_kernel<true, true> : gemm_tp_kernel<false, true>)
+                     : (b_mn ? gemm_tp_kernel<true, false> : gemm_tp_kernel<false, false>);
+  static bool attr_set[4][64] = {};
+  const int variant = (b_mn ? 1 : 0) + (ne > 1 ? 2 : 0);
+  if (!attr_set[variant][dev]) {
     AETHER_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    attr_set[b_mn][dev] = true;
+    attr_set[variant][dev] = true;
   }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int per_rank = std::max(1, num_sms(dev) / ne);

@@ -17,7 +17,7 @@ from aether_b200.optim import FlatAdamW
 V, D, L, H, HKV, FF = 256, 128, 2, 2, 1, 256
 
 
-def _write_base(path, seed=0):
+def _write_base(path, seed=0, D=D, H=H, HKV=HKV, FF=FF):
     g = torch.Generator().manual_seed(seed)
     rnd = lambda *s: torch.randn(*s, generator=g) * 0.05  # noqa: E731
     hd = D // H
@@ -220,8 +220,9 @@ def test_serving_keeps_gguf_weights_quantised(tmp_path):
 @pytest.mark.gpu
 def test_gpu_serving_keeps_gguf_weights_quantised(tmp_path):
     """The same on the device, with CUDA-graph decode (the per-projection
-    expansions are captured with the GEMMs)."""
-    path = _write_base(str(tmp_path / "base.gguf"), seed=7)
+    expansions are captured with the GEMMs); head_dim 128, as the decode
+    attention kernel needs."""
+    path = _write_base(str(tmp_path / "base.gguf"), seed=7, D=256, H=2, HKV=1, FF=512)
     md, mq = _serve_pair(path, "cuda")
     toks = torch.randint(0, V, (2, 11), generator=torch.Generator().manual_seed(8)).cuda()
     _, ld = md.prefill(toks, return_logits=True)
