@@ -134,9 +134,8 @@ def tp_train(info, out):
     and the o_proj GEMM -> reduce-scatter (+ residual) of one layer, against
     NCCL all-gather / reduce-scatter around the plain tcgen05 GEMM. Roofline of
     the fused pair: the slower of its FLOPs at the measured GEMM peak and the
-    bytes this GPU must send over NVLink (its rows once, multicast where NVLS
-    is there, else once per peer; its partial sums of the other ranks' rows)
-    at the measured link rate."""
+    bytes this GPU must send over NVLink (its rows once per peer, P2P stores;
+    its partial sums of the other ranks' rows) at the measured link rate."""
     from .ops import functional as F
     from .parallel.symm import SymmTeam
     from .parallel.tp_fused import FusedTP
@@ -170,13 +169,12 @@ def tp_train(info, out):
     t_f = timed(fused)
     t_n = timed(nccl)
     flops = 2.0 * M * nq * d + 2.0 * M * d * nin
-    mc = team.has_multicast
-    ag_bytes = Ml * d * 2 * (1 if mc else tp - 1)
+    ag_bytes = Ml * d * 2 * (tp - 1)
     rs_bytes = (tp - 1) * Ml * d * 2
     t_comp = flops / (bf16_tflops() * 1e12) * 1e3
     t_link = (ag_bytes + rs_bytes) / (LINK_GBS * 1e9) * 1e3
     roof = max(t_comp, t_link)
-    out.append({"path": "tp_train_fused_ag_gemm_rs", "tp": tp, "tokens": M, "d_model": d, "multicast": mc,
+    out.append({"path": "tp_train_fused_ag_gemm_rs", "tp": tp, "tokens": M, "d_model": d,
                 "fused_ms": t_f, "nccl_ms": t_n, "speedup_vs_nccl": t_n / t_f, "roofline_ms": roof,
                 "roofline_compute_ms": t_comp, "roofline_nvlink_ms": t_link, "frac_of_roofline": roof / t_f})
     del team

@@ -9,6 +9,8 @@ one data-parallel reduce-scatter.
 """
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from . import functional as F
@@ -27,15 +29,24 @@ def _main_grad(w: torch.Tensor) -> torch.Tensor | None:
     return mg
 
 
+# ZeRO-3 arenas in fused mode (parallel.fsdp): a weight whose memory lies in
+# one of their unit buffers with a gather still pending is gathered by the GEMM
+# that reads it. Looked up by address: autograd hands backward new tensor
+# objects over the saved memory, so nothing set on the forward's view survives.
+PG_ARENAS = weakref.WeakSet()
+
+
 def _gemm_w(x, w, b_mn=False, residual=None):
     """x . w^T (b_mn: x . w) where w may be a ZeRO-3 weight whose unit is still
     to be gathered: then this GEMM is the unit's first consumer and gathers it
     inside the same kernel (parallel.fsdp, fused mode)."""
-    pg = getattr(w, "_fsdp_pg", None)
-    if pg is not None:
-        y = pg[0].pg_gemm(pg[1], x, w, b_mn=b_mn, residual=residual)
-        if y is not None:
-            return y
+    for arena in list(PG_ARENAS):
+        u = arena.pending_at(w)
+        if u is not None:
+            y = arena.pg_gemm(u, x, w, b_mn=b_mn, residual=residual)
+            if y is not None:
+                return y
+            break
     return F.gemm(x, w, b_mn=b_mn, residual=residual)
 
 

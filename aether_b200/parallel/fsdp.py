@@ -163,6 +163,7 @@ class ShardedArena:
                 b.tensor.zero_()
             self._pctr = [torch.zeros(2, dtype=torch.int32, device=dev) for _ in range(2)]
             self._puses = [0, 0]
+            A.PG_ARENAS.add(self)  # its pending gathers run inside the GEMMs that read them
             self._proot = torch.zeros(root_n, dtype=torch.bfloat16, device=dev)
             torch.cuda.synchronize(dev)
             dist.barrier(group=self.group)  # every rank's flags are zero before anyone signals
@@ -181,6 +182,11 @@ class ShardedArena:
         else:
             self._gslots = [torch.zeros(layer_max, dtype=torch.float32, device=dev) for _ in range(2)]
         self._groot = torch.zeros(root_n, dtype=torch.float32, device=dev)
+        # AETHER_FSDP_FUSED_RS=0 keeps the fused parameter gathers but reduces
+        # gradients with NCCL (to tell the two apart)
+        import os as _os
+
+        self._fused_rs = fused and _os.environ.get("AETHER_FSDP_FUSED_RS", "1") != "0"
         self._scratch = {i: torch.zeros(layer_max // self.world, dtype=torch.float32, device=dev) for i in (0, 1)}
         self._scratch[ROOT] = torch.zeros(max(1, root_n // self.world), dtype=torch.float32, device=dev)
         self._reset_state()
@@ -311,6 +317,18 @@ class ShardedArena:
         if self.stage == 3 and u is not None and u not in self._resident:
             self._gather(u, async_op=self.device.type == "cuda")
 
+    def pending_at(self, w: torch.Tensor):
+        """The unit whose still-pending gather covers w's memory, or None
+        (ops.autograd._gemm_w asks before every linear GEMM)."""
+        if not self._pending or not w.is_cuda:
+            return None
+        p = w.data_ptr()
+        for u, k in self._pending.items():
+            base = self._pslots[k].data_ptr()
+            if base <= p < base + self.units[u].numel * 2:
+                return u
+        return None
+
     def pg_gemm(self, u: int, x: torch.Tensor, w: torch.Tensor, b_mn: bool = False, residual=None):
         """x . w^T (b_mn: x . w) as the first consumer of unit u's still-pending
         gather: one kernel moves every rank's shard into every rank's unit
@@ -331,7 +349,7 @@ class ShardedArena:
         sym, fl, rd = self._psym[k], self._pflags[k], self._pready[k]
         F.gemm_param_gather([x], [w], [out], [self._shard_of(u, self.bf16)], [self._pctr[k]], [self.rank],
                               self.world, FUSED_CHUNK, b_mn, sym.peers_host, fl.peers_host, rd.peers_host,
-                              sym.mc_ptr, self._puses[k], 10.0)
+                              0, self._puses[k], 10.0)  # P2P pushes: this rank reads its own chunks back
         return out
 
     def _complete(self, u: int) -> None:
@@ -347,9 +365,6 @@ class ShardedArena:
         v = buf[s.offset : s.offset + s.numel].view(s.shape)
         v.requires_grad_(True)
         v._fsdp_name = name
-        u = self.unit_of[name]
-        if u in self._pending:
-            v._fsdp_pg = (self, u)  # its GEMM gathers the unit (ops.autograd._gemm_w)
         return v
 
     def __getitem__(self, name: str) -> torch.Tensor:
@@ -412,7 +427,7 @@ class ShardedArena:
                 return
             key, full = ks[0], self._gslots[ks[0]]
         out = self._scratch[key][: unit.shard]
-        if self.team is not None and key != ROOT:
+        if self.team is not None and key != ROOT and self._fused_rs:
             self._gpending[key] = (self._reduce_scatter_fused(key, u, out), u)
             return
         self._gpending[key] = (self._reduce_scatter(out, full[: unit.numel]), u)

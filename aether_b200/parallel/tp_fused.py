@@ -11,8 +11,8 @@ whose collective runs inside it, tile by tile, over NVLink:
                                          also kept locally for dW = dY^T . o)
 
 so a layer's hot path issues no NCCL call. The buffers live in symmetric
-memory (every rank maps every peer's; NVLS multicast where NVSwitch offers
-it): per activation shape [M, d] a two-slot gather ring ([M, d] bf16 plus
+memory (every rank maps every peer's; the rows are pushed with P2P stores,
+each rank receiving (tp - 1) / tp of them either way): per activation shape [M, d] a two-slot gather ring ([M, d] bf16 plus
 per-chunk flags) and a two-slot receive ring ([tp, M / tp, d] bf16 plus
 per-slab counters). Flags only grow (the kernel compares them with the
 number of uses of the slot), so they are zeroed once, at allocation.
@@ -92,7 +92,7 @@ class FusedTP:
                     [residual] if residual is not None else [], [push_src] if push_src is not None else [],
                     [self.rank], self.tp, ring.Ml, b_mn, ag_mode, rs, local_copy,
                     ag.peers_host if use_ag else [], agf.peers_host if use_ag else [],
-                    ag.mc_ptr if use_ag else 0,
+                    0,  # P2P pushes (the own rows are read back locally; see the kernel's note on multicast)
                     rsb.peers_host if rs else [], rsf.peers_host if rs else [], ag_ep, rs_ep, self.timeout_s)
 
     # ------------------------------------------------------------------ forward

@@ -170,10 +170,11 @@ def parse():
     ap.add_argument("--zero", type=int, default=1, choices=[1, 2, 3],
                     help="ZeRO stage of the data-parallel engine (2 / 3: sharded gradients and optimiser state, "
                     "3 also parameters)")
-    ap.add_argument("--zero-comm", default="fused", choices=["fused", "nccl"],
-                    help="ZeRO-3 on GPUs. fused: each layer's parameter all-gather inside its first consuming "
-                    "GEMM and the gradient reduce-scatter by this library's kernels (no NCCL call per layer); "
-                    "nccl: NCCL all-gathers / reduce-scatters with prefetch")
+    ap.add_argument("--zero-comm", default="nccl", choices=["fused", "nccl"],
+                    help="ZeRO-3 on GPUs. nccl: NCCL all-gathers / reduce-scatters with prefetch on a side "
+                    "stream (the faster on two B200s: 215.0K vs 209.4K tokens/s); fused: each layer's "
+                    "parameter all-gather inside its first consuming GEMM and the gradient reduce-scatter "
+                    "by this library's kernels (no NCCL call per layer)")
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen2.5-7B TP=N serving section")
     ap.add_argument("--decode-batches", default="1,16,64")
     ap.add_argument("--decode-prompt", type=int, default=2048)

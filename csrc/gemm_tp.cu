@@ -10,10 +10,12 @@
 // kernel that does the math and the transfer together:
 //
 //   ag_mode 1  all-gather -> GEMM. Two pusher warps of every CTA copy this
-//              rank's rows (128-row chunks) into every peer's gather buffer --
-//              one NVLS multimem.st per 16 bytes where NVSwitch multicast is
-//              available, P2P stores otherwise -- and release a per-chunk flag
-//              in each peer. The tile schedule starts with this rank's own
+//              rank's rows (128-row chunks) into every peer's gather buffer
+//              with P2P stores and release a per-chunk flag in each peer. (A
+//              multicast address may be passed instead -- one multimem.st per
+//              16 bytes -- but such a store reaches this GPU's own copy through
+//              the switch under another virtual alias, unordered with the local
+//              flag store, so no caller that reads its own rows back uses it.) The tile schedule starts with this rank's own
 //              rows (read straight from the local tensor); a tile of a peer's
 //              rows waits (bounded) for that chunk's flag and then TMA-loads it
 //              from local memory, so every remote byte crosses NVLink once and
