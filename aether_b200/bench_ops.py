@@ -91,6 +91,40 @@ def bench_gemm(iters):
                   "speedup_vs_cublas": c / t, "l2_flush": small})
 
 
+def bench_gemm_pair(iters):
+    """The CTA-pair (cta_group::2, 256 x 256 tile) GEMM against the one-CTA
+    kernel and torch (cuBLAS), square sizes and the GPT-24L training shapes
+    (micro-batch 16 x 2048 tokens): forward x.W^T, dgrad dy.W, wgrad dy^T.x
+    into fp32."""
+    hbm, tf, src = peaks()
+    C = _ext.C()
+    T = 16 * 2048
+    shapes = [(n, n, n) for n in (4096, 8192)] + [(T, 6144, 2048), (T, 2048, 2048), (T, 11264, 2048), (T, 2048, 5632)]
+    for M, N, K in shapes:
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = torch.randn(N, K, device="cuda").bfloat16()
+        dy = torch.randn(M, N, device="cuda").bfloat16()
+        gw = torch.zeros(N, K, device="cuda")
+        flops = 2.0 * M * N * K
+        cases = (("fwd", lambda: F.gemm(x, w), lambda: x @ w.t()),
+                 ("dgrad", lambda: F.gemm(dy, w, b_mn=True), lambda: dy @ w),
+                 ("wgrad_f32acc", lambda: F.gemm(dy, x, a_mn=True, b_mn=True, out=gw, accumulate=True),
+                  lambda: gw.add_((dy.t() @ x).float())))
+        for name, fn, tfn in cases:
+            res = {}
+            for mode in (0, 1):
+                old = C.gemm_pair_mode(mode)
+                try:
+                    res[mode] = time_fn(fn, iters)
+                finally:
+                    C.gemm_pair_mode(old)
+            c = time_fn(tfn, iters)
+            emit({"op": f"matmul_{name}_pair", "shape": [M, N, K], "one_cta_ms": res[0], "pair_ms": res[1],
+                  "one_cta_tflops": flops / res[0] / 1e9, "pair_tflops": flops / res[1] / 1e9,
+                  "pair_frac_of_peak": flops / res[1] / 1e9 / tf, "peak": src, "torch_cublas_ms": c,
+                  "pair_speedup_vs_cublas": c / res[1], "pair_speedup_vs_one_cta": res[0] / res[1]})
+
+
 def bench_sdpa(iters):
     hbm, tf, src = peaks()
     B, H, D = 8, 32, 128
@@ -245,7 +279,7 @@ def main():
     args = ap.parse_args()
     _ext.C()
     sel = set(args.only.split(","))
-    for name, fn in (("gemm", bench_gemm), ("sdpa", bench_sdpa), ("attn_bwd", bench_attn_bwd), ("rows", bench_rows),
+    for name, fn in (("gemm", bench_gemm), ("gemm_pair", bench_gemm_pair), ("sdpa", bench_sdpa), ("attn_bwd", bench_attn_bwd), ("rows", bench_rows),
                      ("rms_bwd", bench_rms_bwd), ("ce", bench_ce), ("adamw", bench_adamw)):
         if name in sel:
             fn(args.iters)

@@ -5,6 +5,7 @@
 
 namespace aether {
 // gemm_sm100.cu
+int64_t gemm_pair_mode(int64_t mode);
 void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn, std::optional<at::Tensor> bias,
                std::optional<at::Tensor> residual, double alpha, bool accumulate, std::optional<at::Tensor> alpha_t);
 // gemm_tp.cu
@@ -145,6 +146,8 @@ void dequantize_blocks(at::Tensor in, at::Tensor y, int64_t fmt);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace pybind11::literals;
   m.doc() = "aether_b200 sm_100a kernels";
+  m.def("gemm_pair_mode", &aether::gemm_pair_mode, "mode"_a,
+        "GEMM kernel choice: 0 one-CTA, 1 CTA pair for M, N >= 256, -1 measured default; returns the previous");
   m.def("gemm_bf16", &aether::gemm_bf16, "a"_a, "b"_a, "out"_a, "a_mn"_a, "b_mn"_a, "bias"_a = pybind11::none(),
         "residual"_a = pybind11::none(), "alpha"_a = 1.0, "accumulate"_a = false,
         "alpha_t"_a = pybind11::none());

@@ -22,6 +22,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <ATen/ATen.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host_utils.h"
 
@@ -75,6 +77,93 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
   const int r = t - g * per_group;
   tm = first_m + r % gsize;
   tn = r / gsize;
+}
+
+// One accumulator tile of 128 rows x BN columns from TMEM to global memory:
+// tcgen05.ld, alpha, bias, residual, bf16 / fp32 conversion, then 32-row x
+// 128-byte slabs staged through 128B-swizzled shared memory and written (or
+// reduce-added) by TMA. Run by the four epilogue warps; `quad` is the TMEM lane
+// quadrant of this warp, `tmem_acc` the accumulator's first column, m_base /
+// n_base the tile's first output row / column.
+template <int OUT>
+__device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tmC, uint8_t* sStage,
+                                              uint32_t tmem_acc, int m_base, int n_base, int quad, int lane,
+                                              float alpha, uint32_t& stage_ctr) {
+  const int row = quad * 32 + lane;
+  const int m = m_base + row;
+  const bool row_ok = m < p.M;
+  const int m_warp = m_base + quad * 32;  // first output row of this warp's slab
+  // Output chunks are 128 bytes wide per row: 32 fp32 or 64 bf16 columns.
+  constexpr int CW = (OUT == OUT_BF16) ? 64 : 32;
+#pragma unroll 1
+  for (int c = 0; c < BN / CW; ++c) {
+    const int n0 = n_base + c * CW;
+    float v[CW];
+#pragma unroll
+    for (int h = 0; h < CW / 32; ++h) {
+      uint32_t r[32];
+      tmem_ld32(tmem_acc + (static_cast<uint32_t>(quad * 32) << 16) + c * CW + h * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[h * 32 + j] = __uint_as_float(r[j]) * alpha;
+    }
+    if (n0 >= p.N) continue;  // whole chunk beyond N (warp-uniform)
+    if (p.bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+      for (int q = 0; q < CW / 8; ++q) {
+        if (n0 + q * 8 < p.N) {
+          const uint4 b = bp[q];
+          v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
+          v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
+          v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
+          v[q * 8 + 6] += bf16lo(b.w); v[q * 8 + 7] += bf16hi(b.w);
+        }
+      }
+    }
+    if (p.residual != nullptr && row_ok) {
+      const uint4* rp = reinterpret_cast<const uint4*>(p.residual + (int64_t)m * p.ldr + n0);
+#pragma unroll
+      for (int q = 0; q < CW / 8; ++q) {
+        if (n0 + q * 8 < p.N) {
+          const uint4 b = rp[q];
+          v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
+          v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
+          v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
+          v[q * 8 + 6] += bf16lo(b.w); v[q * 8 + 7] += bf16hi(b.w);
+        }
+      }
+    }
+    // Stage this warp's 32 x 128-byte slab (128B-swizzled) and hand it to TMA.
+    uint8_t* stage_buf = sStage + (quad * 2 + (stage_ctr & 1)) * kStageBytes;
+    if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+    __syncwarp();
+    uint8_t* my_row = stage_buf + lane * 128;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      uint4 o;
+      if constexpr (OUT == OUT_BF16) {
+        o.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+        o.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+        o.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+        o.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+      } else {
+        o.x = __float_as_uint(v[q * 4 + 0]);
+        o.y = __float_as_uint(v[q * 4 + 1]);
+        o.z = __float_as_uint(v[q * 4 + 2]);
+        o.w = __float_as_uint(v[q * 4 + 3]);
+      }
+      *reinterpret_cast<uint4*>(my_row + ((q ^ (lane & 7)) << 4)) = o;
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (OUT == OUT_F32_ACCUM) tma_reduce_add_2d(tmC, stage_buf, n0, m_warp);
+      else tma_store_2d(tmC, stage_buf, n0, m_warp);
+      bulk_commit();
+    }
+    ++stage_ctr;
+  }
 }
 
 template <bool A_MN, bool B_MN, int OUT>
@@ -235,7 +324,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // -------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row = quad * 32 + lane;
     const float alpha = p.alpha * (p.alpha_ptr != nullptr ? *p.alpha_ptr : 1.f);
     uint32_t stage_ctr = 0;
     int acc = 0;
@@ -251,80 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       tc_fence_after();
-      const int m = tm * BM + row;
-      const bool row_ok = m < p.M;
-      const int m_warp = tm * BM + quad * 32;  // first output row of this warp's slab
-      // Output chunks are 128 bytes wide per row: 32 fp32 or 64 bf16 columns.
-      constexpr int CW = (OUT == OUT_BF16) ? 64 : 32;
-#pragma unroll 1
-      for (int c = 0; c < BN / CW; ++c) {
-        const int n0 = tn * BN + c * CW;
-        float v[CW];
-#pragma unroll
-        for (int h = 0; h < CW / 32; ++h) {
-          uint32_t r[32];
-          tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c * CW + h * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[h * 32 + j] = __uint_as_float(r[j]) * alpha;
-        }
-        if (n0 >= p.N) continue;  // whole chunk beyond N (warp-uniform)
-        if (p.bias != nullptr) {
-          const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n0);
-#pragma unroll
-          for (int q = 0; q < CW / 8; ++q) {
-            if (n0 + q * 8 < p.N) {
-              const uint4 b = bp[q];
-              v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
-              v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
-              v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
-              v[q * 8 + 6] += bf16lo(b.w); v[q * 8 + 7] += bf16hi(b.w);
-            }
-          }
-        }
-        if (p.residual != nullptr && row_ok) {
-          const uint4* rp = reinterpret_cast<const uint4*>(p.residual + (int64_t)m * p.ldr + n0);
-#pragma unroll
-          for (int q = 0; q < CW / 8; ++q) {
-            if (n0 + q * 8 < p.N) {
-              const uint4 b = rp[q];
-              v[q * 8 + 0] += bf16lo(b.x); v[q * 8 + 1] += bf16hi(b.x);
-              v[q * 8 + 2] += bf16lo(b.y); v[q * 8 + 3] += bf16hi(b.y);
-              v[q * 8 + 4] += bf16lo(b.z); v[q * 8 + 5] += bf16hi(b.z);
-              v[q * 8 + 6] += bf16lo(b.w); v[q * 8 + 7] += bf16hi(b.w);
-            }
-          }
-        }
-        // Stage this warp's 32 x 128-byte slab (128B-swizzled) and hand it to TMA.
-        uint8_t* stage_buf = sStage + (quad * 2 + (stage_ctr & 1)) * kStageBytes;
-        if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
-        __syncwarp();
-        uint8_t* my_row = stage_buf + lane * 128;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint4 o;
-          if constexpr (OUT == OUT_BF16) {
-            o.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
-            o.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
-            o.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
-            o.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
-          } else {
-            o.x = __float_as_uint(v[q * 4 + 0]);
-            o.y = __float_as_uint(v[q * 4 + 1]);
-            o.z = __float_as_uint(v[q * 4 + 2]);
-            o.w = __float_as_uint(v[q * 4 + 3]);
-          }
-          *reinterpret_cast<uint4*>(my_row + ((q ^ (lane & 7)) << 4)) = o;
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if constexpr (OUT == OUT_F32_ACCUM) tma_reduce_add_2d(&tmC, stage_buf, n0, m_warp);
-          else tma_store_2d(&tmC, stage_buf, n0, m_warp);
-          bulk_commit();
-        }
-        ++stage_ctr;
-      }
+      epilogue_tile<OUT>(p, &tmC, sStage, tmem_base + acc * BN, tm * BM, tn * BN, quad, lane, alpha, stage_ctr);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
@@ -338,6 +353,218 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256). Each CTA loads its own 128 rows
+// of A and its own 128 rows of B (half of the tile's N) per 64-deep K block, so
+// a stage is 32 KB instead of 48 KB and six stages fit; the tensor core reads
+// half as many B bytes per FLOP from each SM's shared memory as the one-CTA
+// M128 x N256 form. The even CTA's MMA thread issues every MMA; TMA copies of
+// both CTAs count their bytes on the even CTA's `full` barriers; MMA
+// completion (stage free, accumulator ready) is committed to the barriers of
+// both CTAs; each CTA's epilogue drains its own 128 accumulator rows and
+// releases the accumulator on the even CTA's barrier. All loads are local (no
+// cluster multicast), so the kernel is usable inside multi-GPU training.
+constexpr int P_BM = 256;  // rows per pair tile (128 per CTA)
+constexpr int P_BN = 256;  // columns per pair tile (B rows: 128 per CTA)
+constexpr int P_STAGES = 6;
+constexpr int P_HALF_BYTES = 128 * BK * 2;  // 16 KB: one CTA's A or B rows of a K block
+constexpr int P_STAGE_BYTES = 2 * P_HALF_BYTES;
+constexpr int kPairSmemBytes = P_STAGES * P_STAGE_BYTES + kStageTotal + 1024 + 256;
+constexpr int kPairEpiArrivals = 8;  // 4 epilogue warps x 2 CTAs release an accumulator
+static_assert(kPairSmemBytes <= 232448, "pair GEMM shared memory");
+static_assert(P_BN == BN, "the pair epilogue drains BN accumulator columns per CTA");
+
+template <bool A_MN, bool B_MN, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + P_STAGES * P_HALF_BYTES;
+  uint8_t* sStage = sB + P_STAGES * P_HALF_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStage + kStageTotal);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
+  const int pair = (int)cluster_id_x();
+  const int npairs = (int)cluster_count_x();
+  const int num_m = (p.M + P_BM - 1) / P_BM;
+  const int num_n = (p.N + P_BN - 1) / P_BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);   // the even CTA's producer (expect_tx for both CTAs' bytes)
+      mbar_init(&empty[s], 1);  // one MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kPairEpiArrivals);
+    }
+    mbar_init(drain, 1);
+    *abort_word = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  // Both CTAs' barriers are initialised before either CTA signals the other's.
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        const int m0 = tm * P_BM + (int)rank * 128;
+        const int n0 = tn * P_BN + (int)rank * 128;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_word)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * P_HALF_BYTES;
+          uint8_t* b_dst = sB + stage * P_HALF_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, bar, kb * BK, m0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, bar, m0, kb * BK);
+            tma_load_2d_pair(a_dst + 8192, &tmA, bar, m0 + 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, bar, kb * BK, n0);
+          } else {
+            tma_load_2d_pair(b_dst, &tmB, bar, n0, kb * BK);
+            tma_load_2d_pair(b_dst + 8192, &tmB, bar, n0 + 64, kb * BK);
+          }
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutProducer);
+        // Copies in flight complete on the even CTA's barriers, which this CTA
+        // cannot observe: give them a fixed time to land before leaving.
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------------------ MMA issuer (even CTA)
+      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, P_BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_word)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * P_BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * P_HALF_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * P_HALF_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? sdesc_sw128(a_base + kk * 2048, 8192, 1024) : sdesc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? sdesc_sw128(b_base + kk * 2048, 8192, 1024) : sdesc_sw128(b_base + kk * 32, 16, 1024);
+            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);  // the stage is free in both CTAs
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);  // both CTAs' accumulator rows are final
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok) {
+        *abort_word = 1;
+        atomicExch(p.status, kStatusTimeoutMma);
+      }
+      // Drain: every MMA issued has completed before either CTA frees TMEM.
+      volatile int never = 0;
+      umma_commit_pair(drain, 0x1);
+      mbar_wait(drain, 0, &never);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int quad = warp & 3;
+    const float alpha = p.alpha * (p.alpha_ptr != nullptr ? *p.alpha_ptr : 1.f);
+    uint32_t stage_ctr = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < num_tiles; t += npairs) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_word)) {
+        *abort_word = 1;
+        if (lane == 0) atomicExch(p.status, kStatusTimeoutEpilogue);
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      epilogue_tile<OUT>(p, &tmC, sStage, tmem_base + acc * P_BN, tm * P_BM + (int)rank * 128, tn * P_BN, quad,
+                         lane, alpha, stage_ctr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait<0>();
+  }
+
+  // Neither CTA frees TMEM or leaves while the pair's MMAs, copies or
+  // barrier signals may still reach it.
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -357,7 +584,74 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   AETHER_CUDA_CHECK(cudaGetLastError());
 }
 
+template <bool A_MN, bool B_MN, int OUT>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
+                        cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, OUT>;
+  static bool attr_set[64] = {false};
+  const int dev = current_device();
+  if (!attr_set[dev]) {
+    AETHER_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
+    attr_set[dev] = true;
+  }
+  const int num_tiles = ((p.M + P_BM - 1) / P_BM) * ((p.N + P_BN - 1) / P_BN);
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Persistent: no more pairs than can be resident at once (an SM pair must
+  // share a GPC, so this can be below half the SM count), or the pairs that
+  // start late would each add a whole share of tiles to the tail.
+  static int resident[64] = {0};
+  if (resident[dev] == 0) {
+    cfg.gridDim = dim3(2 * (num_sms(dev) / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = num_sms(dev) / 2;
+    }
+    resident[dev] = std::min(n, num_sms(dev) / 2);
+  }
+  const int pairs = std::min(num_tiles, resident[dev]);
+  cfg.gridDim = dim3(2 * pairs);
+  AETHER_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p));
+}
+
+// Which kernel a GEMM runs on: 0 the one-CTA kernel, 1 the CTA-pair kernel
+// for every problem with M, N >= 256, -1 (default) the pair kernel whenever its
+// 256 x 256 tiles keep at least as many SMs busy as the one-CTA kernel's
+// 128 x 256 tiles would (measured on a B200: 4-18 % faster than the one-CTA
+// kernel from 4096^3 to the GPT-24L training shapes, every layout).
+// Initialised from AETHER_GEMM_PAIR; gemm_pair_mode() changes it at run time.
+static int g_pair_mode = [] {
+  const char* e = std::getenv("AETHER_GEMM_PAIR");
+  return e == nullptr ? -1 : std::atoi(e);
+}();
+
+static bool use_pair(int64_t M, int64_t N) {
+  if (g_pair_mode == 0 || M < P_BM || N < P_BN) return false;
+  if (g_pair_mode == 1) return true;
+  const int64_t pair_tiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+  const int64_t one_tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int64_t sms = num_sms(current_device());
+  return 2 * std::min<int64_t>(pair_tiles, sms / 2) >= std::min<int64_t>(one_tiles, sms);
+}
+
 }  // namespace gemm
+
+// Sets the GEMM kernel choice (see use_pair) and returns the previous one.
+int64_t gemm_pair_mode(int64_t mode) {
+  const int old = gemm::g_pair_mode;
+  gemm::g_pair_mode = (int)mode;
+  return old;
+}
 
 // Python-facing entry: out (+)= alpha * opA(a) . opB(b)^T (+ bias) (+ residual).
 //   a_mn == false: a is [M, K] (row stride a.stride(0));  true: a is [K, M].
@@ -410,10 +704,12 @@ void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn,
     p.ldr = residual->stride(0);
   }
 
+  const bool pair = gemm::use_pair(M, N);
   CUtensorMap ta, tb;
   if (!a_mn) ta = make_tmap_2d_bf16(a.data_ptr(), K, M, a.stride(0) * 2, gemm::BK, gemm::BM);
   else ta = make_tmap_2d_bf16(a.data_ptr(), M, K, a.stride(0) * 2, 64, gemm::BK);
-  if (!b_mn) tb = make_tmap_2d_bf16(b.data_ptr(), K, N, b.stride(0) * 2, gemm::BK, gemm::BN);
+  // K-major B: a pair kernel's CTA loads 128 of the tile's 256 B rows
+  if (!b_mn) tb = make_tmap_2d_bf16(b.data_ptr(), K, N, b.stride(0) * 2, gemm::BK, pair ? 128 : gemm::BN);
   else tb = make_tmap_2d_bf16(b.data_ptr(), N, K, b.stride(0) * 2, 64, gemm::BK);
 
   // Output map: 128-byte wide boxes (32 fp32 or 64 bf16 columns) x 32 rows, 128B swizzle.
@@ -429,7 +725,8 @@ void gemm_bf16(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn,
   const int mode = accumulate ? gemm::OUT_F32_ACCUM : (out_f32 ? gemm::OUT_F32 : gemm::OUT_BF16);
 #define AETHER_GEMM_CASE(AM, BMN, OM)                                         \
   if (a_mn == AM && b_mn == BMN && mode == OM) {                              \
-    gemm::launch<AM, BMN, OM>(ta, tb, tc, p, stream);                         \
+    if (pair) gemm::launch_pair<AM, BMN, OM>(ta, tb, tc, p, stream);          \
+    else gemm::launch<AM, BMN, OM>(ta, tb, tc, p, stream);                    \
     return;                                                                   \
   }
   AETHER_GEMM_CASE(false, false, gemm::OUT_BF16)

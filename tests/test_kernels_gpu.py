@@ -273,3 +273,53 @@ def test_attention_packed_strided():
     o, _ = F.attention(q, k, v, 1 / math.sqrt(D), True)
     o_r, _ = ref.attention(q, k, v, 1 / math.sqrt(D), True)
     assert_close(o, o_r, 1e-2, "packed attention")
+
+
+@pytest.fixture
+def pair_gemm():
+    """Every GEMM of M, N >= 256 on the CTA-pair (cta_group::2) kernel."""
+    old = _ext.C().gemm_pair_mode(1)
+    yield
+    _ext.C().gemm_pair_mode(old)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (312, 520, 200), (1000, 776, 328), (2048, 1536, 1024)])
+def test_gemm_pair_layouts(pair_gemm, a_mn, b_mn, M, N, K):
+    a = bf(K, M, seed=1) if a_mn else bf(M, K, seed=1)
+    b = bf(K, N, seed=2) if b_mn else bf(N, K, seed=2)
+    out = F.gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+    assert_close(out, ref.gemm(a, b, a_mn, b_mn), 1e-2, f"pair gemm a_mn={a_mn} b_mn={b_mn} {M}x{N}x{K}")
+
+
+def test_gemm_pair_epilogues(pair_gemm):
+    M, N, K = 520, 1032, 264
+    a, b = bf(M, K, seed=3), bf(N, K, seed=4)
+    bias, res = bf(N, seed=5), bf(M, N, seed=6)
+    out = F.gemm(a, b, bias=bias, residual=res, alpha=0.5)
+    assert_close(out, ref.gemm(a, b, bias=bias, residual=res, alpha=0.5), 1e-2, "pair gemm epilogue")
+    acc0 = torch.randn(M, N, device=dev)
+    acc = acc0.clone()
+    F.gemm(a, b, out=acc, accumulate=True)
+    assert_close(acc, acc0 + ref.gemm(a, b), 1e-3, "pair gemm fp32 accumulate")
+    f32 = F.gemm(a, b, out_dtype=torch.float32)
+    assert_close(f32, ref.gemm(a, b), 1e-4, "pair gemm fp32 out")
+    # a problem with more 256 x 256 tiles than SM pairs: every pair walks several tiles
+    a, b = bf(4096, 512, seed=7), bf(3072, 512, seed=8)
+    out = F.gemm(a, b)
+    idx = torch.arange(0, 4096, 61, device=dev)
+    assert_close(out[idx], ref.gemm(a[idx], b), 1e-2, "pair gemm persistent")
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+def test_gemm_one_cta_large(a_mn, b_mn):
+    """The one-CTA kernel on a problem the default would give to the pair kernel."""
+    old = _ext.C().gemm_pair_mode(0)
+    try:
+        M, N, K = 1536, 1280, 520
+        a = bf(K, M, seed=9) if a_mn else bf(M, K, seed=9)
+        b = bf(K, N, seed=10) if b_mn else bf(N, K, seed=10)
+        out = F.gemm(a, b, a_mn=a_mn, b_mn=b_mn)
+        assert_close(out, ref.gemm(a, b, a_mn, b_mn), 1e-2, f"one-CTA gemm a_mn={a_mn} b_mn={b_mn}")
+    finally:
+        _ext.C().gemm_pair_mode(old)
