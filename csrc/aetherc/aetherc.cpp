@@ -297,7 +297,8 @@ using SP = std::shared_ptr<Stmt>;
 using BP = std::shared_ptr<Block>;
 
 struct TyExpr {  // a type as written; tensor dims / array lengths may name constants
-  std::string name;              // primitive / "Tensor" / "[]" / "&str"
+  std::string name;              // primitive / "Tensor" / "[]" / "&str" / a struct name
+  bool generic = false;          // written with generic arguments (Vec<T>, ...)
   std::string elem;              // tensor element
   std::vector<EP> dims;          // tensor dims or {array length}
   std::shared_ptr<TyExpr> inner; // array element
@@ -306,7 +307,7 @@ struct TyExpr {  // a type as written; tensor dims / array lengths may name cons
 
 struct Expr {
   enum K { Int, Float, BoolL, Str, Char, Var, Unary, Binary, Call, Method, Cast, Ref, If, BlockE, Index, ArrayLit,
-           ArrayRep, LoopE } k;
+           ArrayRep, LoopE, Field, Deref } k;
   std::string s;  // literal / name / operator / method
   std::vector<EP> a;
   BP blk, blk2;   // if: then / else block (else may be an `if` wrapped in a block)
@@ -337,10 +338,28 @@ struct Param {
 };
 struct Fn {
   std::string name;
-  std::vector<Param> params;
+  std::vector<Param> params;  // a method's receiver is the parameter `self` (no type)
   std::shared_ptr<TyExpr> ret;
-  BP body;
+  BP body;                    // null: extern, or a trait method without a default body
   bool is_extern = false;
+  int line = 0, col = 0;
+};
+struct StructDef {
+  std::string name;
+  std::vector<std::string> generics;
+  std::vector<Param> fields;
+  int line = 0, col = 0;
+};
+struct TraitDef {
+  std::string name;
+  std::vector<std::string> supers;  // `trait Pet: Animal + Named`
+  std::vector<Fn> methods;
+  int line = 0, col = 0;
+};
+struct ImplDef {
+  std::string trait;  // empty: an inherent impl
+  std::string type;
+  std::vector<Fn> methods;
   int line = 0, col = 0;
 };
 struct Const {
@@ -353,6 +372,9 @@ struct Program {
   std::vector<Fn> fns;
   std::vector<Const> consts;
   std::vector<std::string> uses;
+  std::vector<StructDef> structs;
+  std::vector<TraitDef> traits;
+  std::vector<ImplDef> impls;
 };
 
 // ============================================================================ parser
@@ -383,18 +405,17 @@ class Parser {
         p.consts.push_back(c);
       } else if (is_id("extern") || is_id("fn") || is_id("unsafe")) {
         p.fns.push_back(fn());
-      } else if (cur().t == T::Op && cur().s == "#") {  // attributes are accepted and ignored
-        next();
-        expect_op("[");
-        int depth = 1;
-        while (depth > 0 && !at(T::Eof)) {
-          if (cur().t == T::Op && cur().s == "[") ++depth;
-          if (cur().t == T::Op && cur().s == "]") --depth;
-          next();
-        }
+      } else if (is_op("#")) {
+        attribute();
+      } else if (is_id("struct")) {
+        p.structs.push_back(struct_def());
+      } else if (is_id("trait")) {
+        p.traits.push_back(trait_def());
+      } else if (is_id("impl")) {
+        p.impls.push_back(impl_def());
       } else {
-        fail("AE0100", cur().line, cur().col, "unsupported item '" + cur().s + "' (this compiler handles fn, extern fn, "
-                                              "const and use)");
+        fail("AE0002", cur().line, cur().col, "expected an item (fn, extern fn, const, static, struct, trait, impl, "
+                                              "use), found '" + cur().s + "'");
       }
     }
     return p;
@@ -431,6 +452,170 @@ class Parser {
     return s;
   }
 
+  // `#[...]` before an item or a method: accepted and ignored.
+  void attribute() {
+    expect_op("#");
+    expect_op("[");
+    int depth = 1;
+    while (depth > 0 && !at(T::Eof)) {
+      if (is_op("[")) ++depth;
+      if (is_op("]")) --depth;
+      next();
+    }
+  }
+
+  // Closes a generic argument list; `>>` closes two.
+  void close_angle() {
+    if (is_op(">>")) {
+      t_[i_].s = ">";
+      return;
+    }
+    if (is_op(">=")) {
+      t_[i_].s = "=";
+      return;
+    }
+    expect_op(">");
+  }
+
+  // `<T, U: Bound, const N: usize>` after an item name: the parameter names.
+  std::vector<std::string> generic_params() {
+    std::vector<std::string> names;
+    if (!eat_op("<")) return names;
+    while (!is_op(">") && !is_op(">>")) {
+      eat_id("const");
+      names.push_back(ident());
+      if (eat_op(":")) {  // bounds / const type: skip to the next top-level ',' or '>'
+        int depth = 0;
+        while (!at(T::Eof)) {
+          if (is_op("<")) ++depth;
+          if ((is_op(">") || is_op(">>")) && depth == 0) break;
+          if (is_op(">")) --depth;
+          if (is_op(">>")) depth -= 2;
+          if (is_op(",") && depth == 0) break;
+          next();
+        }
+      }
+      if (!eat_op(",")) break;
+    }
+    close_angle();
+    return names;
+  }
+
+  StructDef struct_def() {
+    StructDef d;
+    d.line = cur().line;
+    d.col = cur().col;
+    next();  // struct
+    d.name = ident();
+    d.generics = generic_params();
+    if (eat_op(";")) return d;  // unit struct
+    if (eat_op("(")) {          // tuple struct
+      int k = 0;
+      while (!is_op(")")) {
+        eat_id("pub");
+        Param f;
+        f.name = std::to_string(k++);
+        f.ty = type();
+        d.fields.push_back(f);
+        if (!eat_op(",")) break;
+      }
+      expect_op(")");
+      expect_op(";");
+      return d;
+    }
+    expect_op("{");
+    while (!is_op("}")) {
+      if (is_op("#")) {
+        attribute();
+        continue;
+      }
+      eat_id("pub");
+      Param f;
+      f.name = ident();
+      expect_op(":");
+      f.ty = type();
+      d.fields.push_back(f);
+      if (!eat_op(",")) break;
+    }
+    expect_op("}");
+    return d;
+  }
+
+  TraitDef trait_def() {
+    TraitDef d;
+    d.line = cur().line;
+    d.col = cur().col;
+    next();  // trait
+    d.name = ident();
+    generic_params();
+    if (eat_op(":")) {
+      do {
+        d.supers.push_back(ident());
+      } while (eat_op("+"));
+    }
+    expect_op("{");
+    while (!is_op("}")) {
+      if (at(T::Eof)) fail("AE0002", d.line, d.col, "unclosed trait body");
+      if (is_op("#")) {
+        attribute();
+        continue;
+      }
+      d.methods.push_back(fn(true));
+    }
+    expect_op("}");
+    return d;
+  }
+
+  ImplDef impl_def() {
+    ImplDef d;
+    d.line = cur().line;
+    d.col = cur().col;
+    next();  // impl
+    generic_params();
+    std::string first = ident();
+    if (is_op("<")) type_args();
+    if (eat_id("for")) {
+      d.trait = first;
+      d.type = ident();
+      if (is_op("<")) type_args();
+    } else {
+      d.type = first;
+    }
+    expect_op("{");
+    while (!is_op("}")) {
+      if (at(T::Eof)) fail("AE0002", d.line, d.col, "unclosed impl body");
+      if (is_op("#")) {
+        attribute();
+        continue;
+      }
+      eat_id("pub");
+      d.methods.push_back(fn());
+    }
+    expect_op("}");
+    return d;
+  }
+
+  // `<T, [M, K], 3>` after a type name: types, shapes or constants, skipped.
+  void type_args() {
+    expect_op("<");
+    while (!is_op(">") && !is_op(">>") && !is_op(">=")) {
+      if (is_op("[")) {
+        next();
+        while (!is_op("]")) {
+          expr_prec(9);
+          if (!eat_op(",")) break;
+        }
+        expect_op("]");
+      } else if (at(T::Int)) {
+        next();
+      } else {
+        type();
+      }
+      if (!eat_op(",")) break;
+    }
+    close_angle();
+  }
+
   std::shared_ptr<TyExpr> type() {
     auto t = std::make_shared<TyExpr>();
     t->line = cur().line;
@@ -458,7 +643,11 @@ class Parser {
       return t;
     }
     t->name = ident();
-    if (t->name == "Tensor") {
+    while (is_op("::")) {  // a path: the last segment names the type
+      next();
+      t->name = ident();
+    }
+    if (t->name == "Tensor" && is_op("<") && peek().t == T::Id && peek(2).t == T::Op && peek(2).s == ",") {
       expect_op("<");
       t->elem = ident();
       expect_op(",");
@@ -468,35 +657,50 @@ class Parser {
         if (!eat_op(",")) break;
       }
       expect_op("]");
-      expect_op(">");
+      close_angle();
+    } else if (is_op("<")) {
+      type_args();
+      t->generic = true;
     }
     return t;
   }
 
-  Fn fn() {
+  // A function; in a trait (`trait_method`) the body may be left out.
+  Fn fn(bool trait_method = false) {
     Fn f;
     f.line = cur().line;
     f.col = cur().col;
     eat_id("unsafe");
+    eat_id("async");
     if (eat_id("extern")) {
       f.is_extern = true;
       if (at(T::Str)) next();  // extern "C"
     }
     if (!eat_id("fn")) fail("AE0002", cur().line, cur().col, "expected 'fn'");
     f.name = ident();
+    generic_params();
     expect_op("(");
     while (!is_op(")")) {
-      eat_id("mut");
       Param p;
-      p.name = ident();
-      expect_op(":");
-      p.ty = type();
+      if (is_op("&") && (peek().s == "self" || (peek().s == "mut" && peek(2).s == "self"))) {
+        next();
+        eat_id("mut");
+        next();  // self
+        p.name = "self";
+      } else {
+        eat_id("mut");
+        p.name = ident();
+        if (p.name != "self" || is_op(":")) {
+          expect_op(":");
+          p.ty = type();
+        }
+      }
       f.params.push_back(p);
       if (!eat_op(",")) break;
     }
     expect_op(")");
     if (eat_op("->")) f.ret = type();
-    if (f.is_extern) {
+    if (f.is_extern || (trait_method && is_op(";"))) {
       expect_op(";");
     } else {
       f.body = block();
@@ -550,6 +754,16 @@ class Parser {
       s->body = block();
       return s;
     }
+    if (is_id("parallel") && peek().t == T::Id && peek().s == "for") next();  // `parallel for`: a for loop here
+    if ((is_id("warp") || is_id("block")) && peek().t == T::Op && peek().s == "{") {
+      // a warp / block region: its statements, in order, as a block
+      const Tok at = cur();
+      next();
+      s->k = Stmt::ExprS;
+      s->e = mk(Expr::BlockE, at);
+      s->e->blk = block();
+      return s;
+    }
     if (eat_id("for")) {
       s->k = Stmt::For;
       s->name = ident();
@@ -558,7 +772,7 @@ class Parser {
       if (eat_op("..=")) {
         s->inclusive = true;
       } else if (!eat_op("..")) {
-        fail("AE0100", cur().line, cur().col, "for loops iterate over ranges a..b or a..=b");
+        fail("AE0500", cur().line, cur().col, "for loops iterate over ranges a..b or a..=b");
       }
       s->e2 = expr_prec(9);
       s->body = block();
@@ -663,8 +877,10 @@ class Parser {
       e->a = {unary()};
       return e;
     }
-    if (eat_op("*")) {  // dereference of a by-value binding: the value itself
-      return unary();
+    if (eat_op("*")) {  // dereference (of a by-value binding: the value itself)
+      EP e = mk(Expr::Deref, at);
+      e->a = {unary()};
+      return e;
     }
     return cast_expr(postfix(primary()));
   }
@@ -685,6 +901,14 @@ class Parser {
     for (;;) {
       const Tok at = cur();
       if (eat_op(".")) {
+        if (at_field_name()) {  // field access: `x.field` / `x.0`
+          EP f = mk(Expr::Field, at);
+          f->s = cur().s;
+          next();
+          f->a = {e};
+          e = f;
+          continue;
+        }
         std::string m = ident();
         EP c = mk(Expr::Method, at);
         c->s = m;
@@ -706,6 +930,11 @@ class Parser {
         return e;
       }
     }
+  }
+
+  bool at_field_name() const {
+    if (cur().t == T::Int) return true;
+    return cur().t == T::Id && !(peek().t == T::Op && (peek().s == "(" || peek().s == "::"));
   }
 
   EP primary() {
@@ -749,7 +978,7 @@ class Parser {
     }
     if (is_op("[")) {
       next();
-      if (eat_op("]")) fail("AE0100", at.line, at.col, "empty array literal");
+      if (eat_op("]")) fail("AE0500", at.line, at.col, "empty array literal");
       EP first = expr();
       if (eat_op(";")) {
         EP e = mk(Expr::ArrayRep, at);
@@ -807,7 +1036,7 @@ class Parser {
         next();
         name = ident();
       }
-      if (eat_op("!")) fail("AE0100", at.line, at.col, "macros are not supported");
+      if (eat_op("!")) fail("AE0500", at.line, at.col, "macros are not supported");
       if (eat_op("(")) {
         EP e = mk(Expr::Call, at);
         e->s = name;
@@ -945,7 +1174,7 @@ class Gen {
     o << "\n";
     for (auto& f : p_.fns)
       if (!f.is_extern) o << fn_def(f);
-    if (!sigs_.count("main") || sigs_["main"].is_extern) fail("AE0300", 1, 1, "program has no `fn main`");
+    if (!sigs_.count("main") || sigs_["main"].is_extern) fail("AE0580", 1, 1, "program has no `fn main`");
     const FnSig& m = sigs_["main"];
     o << "int main(void) {\n";
     if (m.ret.b == B::Void)
@@ -987,7 +1216,7 @@ class Gen {
     auto it = sigs_.find(f.name);
     if (it != sigs_.end()) {
       if (f.is_extern && it->second.is_extern) return;  // the same extern declared twice (program + stdlib)
-      fail("AE0201", f.line, f.col, "function '" + f.name + "' is defined twice");
+      fail("AE0501", f.line, f.col, "function '" + f.name + "' is defined twice");
     }
     sigs_[f.name] = s;
   }
@@ -1002,7 +1231,7 @@ class Gen {
         auto it = const_val_.find(e->s);
         if (it != const_val_.end()) return it->second;
         auto src = const_src_.find(e->s);
-        if (src == const_src_.end()) fail("AE0210", e->line, e->col, "'" + e->s + "' is not a constant");
+        if (src == const_src_.end()) fail("AE0510", e->line, e->col, "'" + e->s + "' is not a constant");
         const_val_[e->s] = {prim(B::Unknown), 0};  // cycle guard
         auto v = eval_const(src->second->e);
         v.first = resolve(*src->second->ty);
@@ -1031,20 +1260,20 @@ class Gen {
         else if (op == "-") v = a - b;
         else if (op == "*") v = a * b;
         else if (op == "/") {
-          if (b == 0) fail("AE0211", e->line, e->col, "division by zero in a constant");
+          if (b == 0) fail("AE0511", e->line, e->col, "division by zero in a constant");
           v = fl ? a / b : (double)((int64_t)a / (int64_t)b);
         } else if (op == "%") {
-          if (b == 0) fail("AE0211", e->line, e->col, "division by zero in a constant");
+          if (b == 0) fail("AE0511", e->line, e->col, "division by zero in a constant");
           v = (double)((int64_t)a % (int64_t)b);
         } else if (op == "<<") v = (double)((int64_t)a << (int64_t)b);
         else if (op == ">>") v = (double)((int64_t)a >> (int64_t)b);
         else if (op == "&") v = (double)((int64_t)a & (int64_t)b);
         else if (op == "|") v = (double)((int64_t)a | (int64_t)b);
         else if (op == "^") v = (double)((int64_t)a ^ (int64_t)b);
-        else fail("AE0210", e->line, e->col, "operator '" + op + "' is not allowed in a constant");
+        else fail("AE0510", e->line, e->col, "operator '" + op + "' is not allowed in a constant");
         return {fl ? prim(B::F32) : l.first, v};
       }
-      default: fail("AE0210", e->line, e->col, "not a constant expression");
+      default: fail("AE0510", e->line, e->col, "not a constant expression");
     }
   }
 
@@ -1072,10 +1301,10 @@ class Gen {
       r.b = B::Tensor;
       if (t.elem == "f32") r.elem = B::F32;
       else if (t.elem == "i32") r.elem = B::I32;
-      else fail("AE0220", t.line, t.col, "tensor elements must be f32 or i32");
+      else fail("AE0520", t.line, t.col, "tensor elements must be f32 or i32");
       for (auto& d : t.dims) {
         const int64_t v = const_int(d);
-        if (v <= 0) fail("AE0221", t.line, t.col, "tensor dimensions must be positive");
+        if (v <= 0) fail("AE0521", t.line, t.col, "tensor dimensions must be positive");
         r.dims.push_back(v);
       }
       return r;
@@ -1087,7 +1316,7 @@ class Gen {
       return r;
     }
     auto it = prim_names().find(t.name);
-    if (it == prim_names().end()) fail("AE0222", t.line, t.col, "unknown type '" + t.name + "'");
+    if (it == prim_names().end()) fail("AE0522", t.line, t.col, "unknown type '" + t.name + "'");
     return prim(it->second);
   }
 
@@ -1164,7 +1393,7 @@ class Gen {
           auto v = eval_const(e);
           return {"aec_" + e->s, v.first};
         }
-        fail("AE0210", e->line, e->col, "unknown name '" + e->s + "'");
+        fail("AE0510", e->line, e->col, "unknown name '" + e->s + "'");
       }
       case Expr::Unary: {
         V a = gen(e->a[0], hint);
@@ -1185,7 +1414,7 @@ class Gen {
       case Expr::Method: return method(e);
       case Expr::Index: {
         V arr = gen(e->a[0], prim(B::Unknown));
-        if (arr.t.b != B::Array) fail("AE0230", e->line, e->col, "only arrays can be indexed");
+        if (arr.t.b != B::Array) fail("AE0530", e->line, e->col, "only arrays can be indexed");
         V ix = gen(e->a[1], prim(B::I64));
         return {arr.c + "[" + ix.c + "]", *arr.t.inner};
       }
@@ -1210,7 +1439,7 @@ class Gen {
         o << " })";
         return {o.str(), prim(B::Void)};
       }
-      default: fail("AE0100", e->line, e->col, "array literals are only allowed as `let` initialisers");
+      default: fail("AE0500", e->line, e->col, "array literals are only allowed as `let` initialisers");
     }
   }
 
@@ -1248,7 +1477,7 @@ class Gen {
   V call(const EP& e, const Ty& hint) {
     const std::string& n = e->s;
     auto one_arg = [&](const Ty& t) {
-      if (e->a.size() != 1) fail("AE0240", e->line, e->col, n + "() takes one argument");
+      if (e->a.size() != 1) fail("AE0540", e->line, e->col, n + "() takes one argument");
       return gen(e->a[0], t);
     };
     // casts written as calls
@@ -1272,7 +1501,7 @@ class Gen {
                                                "tanh", "powf", "pow"};
     if (!sigs_.count(n) && math.count(n)) {
       if (n == "pow" || n == "powf") {
-        if (e->a.size() != 2) fail("AE0240", e->line, e->col, n + "() takes two arguments");
+        if (e->a.size() != 2) fail("AE0540", e->line, e->col, n + "() takes two arguments");
         V a = gen(e->a[0], hint.is_float() ? hint : prim(B::F32));
         V b = gen(e->a[1], a.t);
         return {(a.t.b == B::F64 ? "pow(" : "powf(") + a.c + ", " + conv(b, a.t) + ")", a.t};
@@ -1286,16 +1515,16 @@ class Gen {
       return {(a.t.b == B::F32 ? cn + "f(" : cn + "(") + a.c + ")", a.t};
     }
     auto it = sigs_.find(n);
-    if (it == sigs_.end()) fail("AE0240", e->line, e->col, "unknown function '" + n + "'");
+    if (it == sigs_.end()) fail("AE0540", e->line, e->col, "unknown function '" + n + "'");
     const FnSig& s = it->second;
     if (s.params.size() != e->a.size())
-      fail("AE0241", e->line, e->col, "'" + n + "' takes " + std::to_string(s.params.size()) + " arguments, got " +
+      fail("AE0541", e->line, e->col, "'" + n + "' takes " + std::to_string(s.params.size()) + " arguments, got " +
                                            std::to_string(e->a.size()));
     std::string args;
     for (size_t i = 0; i < e->a.size(); ++i) {
       V v = gen(e->a[i], s.params[i]);
       if (v.t.b == B::Tensor && !s.params[i].is_int() && s.params[i].b != B::Tensor)
-        fail("AE0220", e->a[i]->line, e->a[i]->col, "a tensor passed where " + tyname(s.params[i]) + " is expected");
+        fail("AE0520", e->a[i]->line, e->a[i]->col, "a tensor passed where " + tyname(s.params[i]) + " is expected");
       args += (i ? ", " : "") + conv(v, s.params[i]);
     }
     return {s.c + "(" + args + ")", s.ret};
@@ -1304,9 +1533,9 @@ class Gen {
   V method(const EP& e) {
     V r = gen(e->a[0], prim(B::Unknown));
     if (r.t.b != B::Tensor)
-      fail("AE0250", e->line, e->col, "method '" + e->s + "' needs a Tensor receiver, not " + tyname(r.t));
+      fail("AE0550", e->line, e->col, "method '" + e->s + "' needs a Tensor receiver, not " + tyname(r.t));
     auto it = method_rules().find(e->s);
-    if (it == method_rules().end()) fail("AE0251", e->line, e->col, "unknown tensor method '" + e->s + "'");
+    if (it == method_rules().end()) fail("AE0551", e->line, e->col, "unknown tensor method '" + e->s + "'");
     const MethodRule& rule = it->second;
     std::vector<V> args;
     std::vector<Ty> shapes;
@@ -1318,11 +1547,11 @@ class Gen {
     const std::vector<int64_t>& s = r.t.dims;
     auto arg_dims = [&](size_t k) -> const std::vector<int64_t>& {
       if (k >= shapes.size() || shapes[k].b != B::Tensor)
-        fail("AE0252", e->line, e->col, e->s + ": argument " + std::to_string(k + 1) + " must be a Tensor");
+        fail("AE0552", e->line, e->col, e->s + ": argument " + std::to_string(k + 1) + " must be a Tensor");
       return shapes[k].dims;
     };
     auto need2 = [&](const std::vector<int64_t>& d, const char* what) {
-      if (d.size() != 2) fail("AE0253", e->line, e->col, e->s + ": " + what + " must be 2-dimensional");
+      if (d.size() != 2) fail("AE0553", e->line, e->col, e->s + ": " + what + " must be 2-dimensional");
     };
     std::vector<int64_t> extra;
     switch (rule.recipe) {
@@ -1331,8 +1560,8 @@ class Gen {
         need2(w, "the weight");
         if (s.size() == 2) extra = {s[0], s[1], w[1]};
         else if (s.size() == 3) extra = {s[0] * s[1], s[2], w[1]};
-        else fail("AE0253", e->line, e->col, "matmul: the receiver must be 2- or 3-dimensional");
-        if (extra[1] != w[0]) fail("AE0254", e->line, e->col, "matmul: inner dimensions differ");
+        else fail("AE0553", e->line, e->col, "matmul: the receiver must be 2- or 3-dimensional");
+        if (extra[1] != w[0]) fail("AE0554", e->line, e->col, "matmul: inner dimensions differ");
         break;
       }
       case MKN_2D: {
@@ -1384,7 +1613,7 @@ class Gen {
       const FnSig& fs = sit->second;
       ret = fs.ret;
       if (fs.params.size() != 1 + args.size() + extra.size())
-        fail("AE0241", e->line, e->col, "tensor method '" + e->s + "' lowers to " + rule.fn + ", which takes " +
+        fail("AE0541", e->line, e->col, "tensor method '" + e->s + "' lowers to " + rule.fn + ", which takes " +
                                             std::to_string(fs.params.size()) + " arguments; the call supplies " +
                                             std::to_string(1 + args.size() + extra.size()));
       for (size_t i = 0; i < args.size(); ++i) {
@@ -1450,8 +1679,8 @@ class Gen {
       case Stmt::Assign: {
         V lhs = gen(s.e, prim(B::Unknown));
         if (s.e->k != Expr::Var && s.e->k != Expr::Index)
-          fail("AE0260", s.line, s.col, "can only assign to a variable or an array element");
-        if (lhs.t.b == B::Tensor) fail("AE0261", s.line, s.col, "tensor bindings cannot be reassigned");
+          fail("AE0560", s.line, s.col, "can only assign to a variable or an array element");
+        if (lhs.t.b == B::Tensor) fail("AE0561", s.line, s.col, "tensor bindings cannot be reassigned");
         V rhs = gen(s.e2, lhs.t);
         if (s.op == "%=" && lhs.t.is_float())
           return lhs.c + " = " + (lhs.t.b == B::F32 ? "fmodf(" : "fmod(") + lhs.c + ", " + conv(rhs, lhs.t) + ");";
@@ -1490,7 +1719,7 @@ class Gen {
       return "(void)(" + v.c + ");";
     }
     if (s.ty && s.ty->name == "Tensor") {
-      if (s.e) fail("AE0270", s.line, s.col, "a Tensor binding is allocated by its declaration and takes no initialiser");
+      if (s.e) fail("AE0570", s.line, s.col, "a Tensor binding is allocated by its declaration and takes no initialiser");
       Ty t = resolve(*s.ty);
       const std::string c = bind(s.name, t);
       const bool f = t.elem == B::F32;
@@ -1520,9 +1749,9 @@ class Gen {
         rep_val = conv(v, el);
         len = const_int(s.e->a[1]);
       } else {
-        fail("AE0271", s.line, s.col, "arrays are initialised from an array literal");
+        fail("AE0571", s.line, s.col, "arrays are initialised from an array literal");
       }
-      if (t.b == B::Array && t.len != len) fail("AE0220", s.line, s.col, "array length does not match its type");
+      if (t.b == B::Array && t.len != len) fail("AE0520", s.line, s.col, "array length does not match its type");
       Ty at;
       at.b = B::Array;
       at.inner = std::make_shared<Ty>(el);
@@ -1543,11 +1772,11 @@ class Gen {
       V v = gen(s.e, t);
       if (t.b == B::Unknown) t = v.t;
       if (v.t.b == B::Tensor && t.b == B::Tensor)
-        fail("AE0272", s.line, s.col, "a Tensor binding cannot be copied (use the original binding)");
-      if (t.b == B::Void) fail("AE0273", s.line, s.col, "binding has no value");
+        fail("AE0572", s.line, s.col, "a Tensor binding cannot be copied (use the original binding)");
+      if (t.b == B::Void) fail("AE0573", s.line, s.col, "binding has no value");
       init = conv(v, t);
     } else {
-      if (t.b == B::Unknown) fail("AE0274", s.line, s.col, "a binding without initialiser needs a type");
+      if (t.b == B::Unknown) fail("AE0574", s.line, s.col, "a binding without initialiser needs a type");
       init = t.is_float() ? "0" : "0";
     }
     const std::string c = bind(s.name, t);
@@ -1601,16 +1830,384 @@ void Gen::resolve_uses(Program& p, const std::string& stdlib, const std::string&
     std::string text;
     if (!read_file(stdlib + "/" + leaf + ".aether", text) && !read_file(srcdir + "/" + leaf + ".aether", text) &&
         !read_file(srcdir + "/_" + leaf + ".aether", text))
-      fail("AE0400", 1, 1, "cannot find module '" + u + "'");
+      fail("AE0003", 1, 1, "cannot find module '" + u + "'");
     Parser ps(lex(text));
     Program m = ps.program();
     resolve_uses(m, stdlib, srcdir, seen);
     for (auto& f : m.fns) p.fns.push_back(f);
+    for (auto& d : m.structs) p.structs.push_back(d);
+    for (auto& d : m.traits) p.traits.push_back(d);
+    for (auto& d : m.impls) p.impls.push_back(d);
     for (auto& c : m.consts) {
       bool dup = false;
       for (auto& e : p.consts) dup |= e.name == c.name;
       if (!dup) p.consts.push_back(c);
     }
+  }
+}
+
+// ============================================================================ front-end checks
+// The checks the reference's `aetherc --check` runs before code generation
+// (compiler/src/main.rs:330-540): trait completeness (mir/traits_drive.rs:
+// AE0210 a required method missing from an impl, AE0211 an impl of an
+// undeclared trait, AE0212 a supertrait not implemented for the type), scalar
+// type conflicts (mir/infer.rs: AE0220 a `let` annotation, AE0221 a call
+// argument, AE0222 a returned value, AE0224 a reassignment -- only where both
+// sides are concrete scalars of different classes: integer, float, bool) and
+// borrows (mir/lifetimes.rs: AE0200 a `&mut` while the place is borrowed,
+// AE0201 a `&` while it is mutably borrowed). The codes and what they flag are
+// the reference's; the passes are written here over this compiler's AST. A
+// `let`-bound borrow lives from its `let` to the last statement that names
+// its binding; a borrow inside an expression lives for its statement.
+
+void check_traits(const Program& p) {
+  std::map<std::string, const TraitDef*> traits;
+  for (auto& t : p.traits) traits[t.name] = &t;
+  std::set<std::pair<std::string, std::string>> impls;  // (trait, type)
+  for (auto& im : p.impls)
+    if (!im.trait.empty()) impls.insert({im.trait, im.type});
+  for (auto& im : p.impls) {
+    if (im.trait.empty()) continue;
+    auto it = traits.find(im.trait);
+    if (it == traits.end())
+      fail("AE0211", im.line, im.col, "`impl " + im.trait + " for " + im.type + "`: no trait `" + im.trait + "` is declared");
+    std::set<std::string> have;
+    for (auto& m : im.methods) have.insert(m.name);
+    for (auto& m : it->second->methods)
+      if (!m.body && !have.count(m.name))
+        fail("AE0210", im.line, im.col, "`impl " + im.trait + " for " + im.type + "` is missing the required method `" +
+                                            m.name + "`");
+    for (auto& sup : it->second->supers)
+      if (!impls.count({sup, im.type}))
+        fail("AE0212", im.line, im.col, "`" + im.type + "` implements `" + im.trait + "` but not its supertrait `" +
+                                            sup + "`");
+  }
+}
+
+// ---------------------------------------------------------------- scalar classes
+enum class SC { Unknown, Int, Float, Bool, Str, Unit };
+
+const char* sc_name(SC c) {
+  switch (c) {
+    case SC::Int: return "an integer";
+    case SC::Float: return "a float";
+    case SC::Bool: return "a bool";
+    case SC::Str: return "a string";
+    case SC::Unit: return "()";
+    default: return "unknown";
+  }
+}
+bool sc_scalar(SC c) { return c == SC::Int || c == SC::Float || c == SC::Bool; }
+bool sc_clash(SC a, SC b) { return sc_scalar(a) && sc_scalar(b) && a != b; }
+
+SC sc_of(const std::shared_ptr<TyExpr>& t) {
+  if (!t) return SC::Unknown;
+  static const std::set<std::string> ints = {"i8", "i16", "i32", "i64", "i128", "isize",
+                                             "u8", "u16", "u32", "u64", "u128", "usize"};
+  if (ints.count(t->name)) return SC::Int;
+  if (t->name == "f32" || t->name == "f64") return SC::Float;
+  if (t->name == "bool") return SC::Bool;
+  if (t->name == "str") return SC::Str;
+  if (t->name == "()") return SC::Unit;
+  return SC::Unknown;
+}
+
+class TypeCheck {
+ public:
+  explicit TypeCheck(const Program& p) : p_(p) {
+    for (auto& f : p.fns) sigs_[f.name] = &f;
+  }
+  void run() {
+    for (auto& f : p_.fns) {
+      if (!f.body) continue;
+      check_fn(f);
+    }
+    for (auto& im : p_.impls)
+      for (auto& f : im.methods)
+        if (f.body) check_fn(f);
+  }
+
+ private:
+  const Program& p_;
+  std::map<std::string, const Fn*> sigs_;
+  std::vector<std::map<std::string, SC>> env_;
+  const Fn* fn_ = nullptr;
+
+  void check_fn(const Fn& f) {
+    fn_ = &f;
+    env_.assign(1, {});
+    for (auto& prm : f.params) env_.back()[prm.name] = sc_of(prm.ty);
+    const SC body = block(*f.body);
+    const SC want = f.ret ? sc_of(f.ret) : SC::Unit;
+    if (f.body->tail && sc_clash(body, want))
+      fail("AE0222", f.body->tail->line, f.body->tail->col,
+           "`" + f.name + "` returns " + sc_name(want) + ", but its body yields " + sc_name(body));
+  }
+  SC lookup(const std::string& n) const {
+    for (auto it = env_.rbegin(); it != env_.rend(); ++it) {
+      auto f = it->find(n);
+      if (f != it->end()) return f->second;
+    }
+    return SC::Unknown;
+  }
+  SC block(const Block& b) {
+    env_.emplace_back();
+    for (auto& st : b.stmts) stmt(*st);
+    const SC t = b.tail ? expr(b.tail) : SC::Unit;
+    env_.pop_back();
+    return t;
+  }
+  void stmt(const Stmt& st) {
+    switch (st.k) {
+      case Stmt::Let: {
+        const SC v = st.e ? expr(st.e) : SC::Unknown;
+        const SC ann = sc_of(st.ty);
+        if (st.ty && st.e && sc_clash(ann, v))
+          fail("AE0220", st.line, st.col, "type mismatch in `let " + st.name + "`: annotation is " + sc_name(ann) +
+                                              ", but the value is " + sc_name(v));
+        env_.back()[st.name] = st.ty ? ann : v;
+        break;
+      }
+      case Stmt::Assign: {
+        const SC v = expr(st.e2);
+        if (st.op == "=" && st.e->k == Expr::Var) {
+          const SC have = lookup(st.e->s);
+          if (sc_clash(have, v))
+            fail("AE0224", st.line, st.col, "cannot assign " + std::string(sc_name(v)) + " to `" + st.e->s +
+                                                "`, which is " + sc_name(have));
+        } else {
+          expr(st.e);
+        }
+        break;
+      }
+      case Stmt::Return:
+        if (st.e) {
+          const SC v = expr(st.e);
+          const SC want = fn_->ret ? sc_of(fn_->ret) : SC::Unit;
+          if (sc_clash(v, want))
+            fail("AE0222", st.line, st.col, "returned value is " + std::string(sc_name(v)) + ", but `" + fn_->name +
+                                                "` returns " + sc_name(want));
+        }
+        break;
+      case Stmt::For:
+        expr(st.e);
+        expr(st.e2);
+        env_.emplace_back();
+        env_.back()[st.name] = SC::Int;
+        block(*st.body);
+        env_.pop_back();
+        break;
+      case Stmt::While:
+        expr(st.e);
+        block(*st.body);
+        break;
+      case Stmt::Loop:
+        if (st.body) block(*st.body);
+        break;
+      case Stmt::ExprS:
+        expr(st.e);
+        break;
+      default: break;
+    }
+  }
+  SC expr(const EP& e) {
+    if (!e) return SC::Unknown;
+    switch (e->k) {
+      case Expr::Int: return SC::Int;
+      case Expr::Float: return SC::Float;
+      case Expr::BoolL: return SC::Bool;
+      case Expr::Str: return SC::Str;
+      case Expr::Char: return SC::Unknown;
+      case Expr::Var: return lookup(e->s);
+      case Expr::Unary: {
+        const SC t = expr(e->a[0]);
+        return e->s == "!" ? (t == SC::Int ? SC::Int : SC::Bool) : t;
+      }
+      case Expr::Binary: {
+        const SC l = expr(e->a[0]);
+        const SC r = expr(e->a[1]);
+        static const std::set<std::string> rel = {"==", "!=", "<", "<=", ">", ">=", "&&", "||"};
+        if (rel.count(e->s)) return SC::Bool;
+        return sc_scalar(l) ? l : r;
+      }
+      case Expr::Call: {
+        std::vector<SC> args;
+        for (auto& a : e->a) args.push_back(expr(a));
+        auto it = sigs_.find(e->s);
+        if (it == sigs_.end()) return SC::Unknown;
+        const Fn& f = *it->second;
+        for (size_t i = 0; i < args.size() && i < f.params.size(); ++i) {
+          const SC want = sc_of(f.params[i].ty);
+          if (sc_clash(args[i], want))
+            fail("AE0221", e->a[i]->line, e->a[i]->col,
+                 "argument " + std::to_string(i + 1) + " to `" + f.name + "` is " + sc_name(args[i]) +
+                     ", but the parameter is " + sc_name(want));
+        }
+        return f.ret ? sc_of(f.ret) : SC::Unit;
+      }
+      case Expr::Cast:
+        expr(e->a[0]);
+        return sc_of(e->cast);
+      case Expr::If: {
+        expr(e->a[0]);
+        const SC a = block(*e->blk);
+        const SC b = e->blk2 ? block(*e->blk2) : SC::Unit;
+        return a == b ? a : SC::Unknown;
+      }
+      case Expr::BlockE: return e->blk ? block(*e->blk) : SC::Unit;
+      case Expr::LoopE:
+        block(*e->blk);
+        return SC::Unknown;
+      default:
+        for (auto& a : e->a) expr(a);
+        if (e->blk) block(*e->blk);
+        return SC::Unknown;
+    }
+  }
+};
+
+// ---------------------------------------------------------------- borrows
+class BorrowCheck {
+ public:
+  void run(const Program& p) {
+    for (auto& f : p.fns)
+      if (f.body) fn(*f.body);
+    for (auto& im : p.impls)
+      for (auto& f : im.methods)
+        if (f.body) fn(*f.body);
+  }
+
+ private:
+  struct Borrow {
+    std::string place, binding;  // binding empty: lives for its statement only
+    bool mut;
+    int from, until;
+  };
+  std::vector<Borrow> live_;
+  std::map<std::string, int> last_use_;
+  int pos_ = 0;
+
+  // Pass 1: the statement index of each name's last mention.
+  void uses_block(const Block& b) {
+    for (auto& s : b.stmts) uses_stmt(*s);
+    if (b.tail) {
+      ++pos_;
+      uses_expr(b.tail);
+    }
+  }
+  void uses_stmt(const Stmt& s) {
+    ++pos_;
+    uses_expr(s.e);
+    uses_expr(s.e2);
+    uses_expr(s.e3);
+    if (s.body) uses_block(*s.body);
+  }
+  void uses_expr(const EP& e) {
+    if (!e) return;
+    if (e->k == Expr::Var) last_use_[e->s] = pos_;
+    for (auto& a : e->a) uses_expr(a);
+    if (e->blk) uses_block(*e->blk);
+    if (e->blk2) uses_block(*e->blk2);
+  }
+
+  // Pass 2: borrows in statement order.
+  void fn(const Block& body) {
+    last_use_.clear();
+    pos_ = 0;
+    uses_block(body);
+    live_.clear();
+    pos_ = 0;
+    walk_block(body);
+  }
+  void walk_block(const Block& b) {
+    for (auto& s : b.stmts) walk_stmt(*s);
+    if (b.tail) {
+      ++pos_;
+      drop_dead();
+      walk_expr(b.tail, "");
+    }
+  }
+  void drop_dead() {
+    std::vector<Borrow> keep;
+    for (auto& b : live_)
+      if (b.until >= pos_) keep.push_back(b);
+    live_.swap(keep);
+  }
+  void walk_stmt(const Stmt& s) {
+    ++pos_;
+    drop_dead();
+    if (s.k == Stmt::Let && s.e && s.e->k == Expr::Ref) {
+      walk_expr(s.e, s.name);
+    } else {
+      walk_expr(s.e, "");
+      walk_expr(s.e2, "");
+      walk_expr(s.e3, "");
+    }
+    if (s.body) walk_block(*s.body);
+  }
+  void walk_expr(const EP& e, const std::string& binding) {
+    if (!e) return;
+    if (e->k == Expr::Ref && !e->a.empty() && e->a[0]->k == Expr::Var) {
+      const std::string& place = e->a[0]->s;
+      for (auto& b : live_) {
+        if (b.place != place) continue;
+        if (e->mut)
+          fail("AE0200", e->line, e->col, "cannot borrow `" + place + "` as mutable: already borrowed");
+        if (b.mut)
+          fail("AE0201", e->line, e->col, "cannot borrow `" + place + "` as shared: already mutably borrowed");
+      }
+      int until = pos_;
+      if (!binding.empty()) {
+        auto it = last_use_.find(binding);
+        until = it == last_use_.end() ? pos_ : std::max(pos_, it->second);
+      }
+      live_.push_back({place, binding, e->mut, pos_, until});
+      return;
+    }
+    for (auto& a : e->a) walk_expr(a, "");
+    if (e->blk) walk_block(*e->blk);
+    if (e->blk2) walk_block(*e->blk2);
+  }
+};
+
+// The code generator takes no structs, traits, impls or field accesses, and
+// reads `*x` of a by-value binding as `x`.
+void strip_deref(EP& e) {
+  if (!e) return;
+  while (e->k == Expr::Deref) e = e->a[0];
+  if (e->k == Expr::Field) fail("AE0500", e->line, e->col, "field access is checked but not compiled by this compiler");
+  for (auto& a : e->a) strip_deref(a);
+  auto blk = [](const BP& b) {
+    if (!b) return;
+    for (auto& st : b->stmts) {
+      strip_deref(st->e);
+      strip_deref(st->e2);
+      strip_deref(st->e3);
+      if (st->body) {
+        EP tmp = std::make_shared<Expr>();
+        tmp->k = Expr::BlockE;
+        tmp->blk = st->body;
+        strip_deref(tmp);
+      }
+    }
+    strip_deref(b->tail);
+  };
+  blk(e->blk);
+  blk(e->blk2);
+}
+void prepare_codegen(Program& p) {
+  if (!p.structs.empty())
+    fail("AE0500", p.structs[0].line, p.structs[0].col, "structs are checked but not compiled by this compiler");
+  if (!p.traits.empty())
+    fail("AE0500", p.traits[0].line, p.traits[0].col, "traits are checked but not compiled by this compiler");
+  if (!p.impls.empty())
+    fail("AE0500", p.impls[0].line, p.impls[0].col, "impls are checked but not compiled by this compiler");
+  for (auto& f : p.fns) {
+    if (!f.body) continue;
+    EP tmp = std::make_shared<Expr>();
+    tmp->k = Expr::BlockE;
+    tmp->blk = f.body;
+    strip_deref(tmp);
   }
 }
 
@@ -1675,7 +2272,7 @@ void usage() {
       "--emit=bin     lower to C, compile with the C compiler and link libaether_rt / libaether_dev (default)\n"
       "--emit=c       write the generated C\n"
       "--emit=ast     write the parsed program as an S-expression\n"
-      "--check        parse and type-check only\n"
+      "--check        parse, resolve `use`, check traits, scalar types and borrows; no code\n"
       "--no-fuse      keep `matmul` + in-place `gelu` as two runtime calls\n"
       "The reference's other emit kinds (mir, llvm-ir, asm, asm-bin, aether-bin, pe-bin) are not produced.");
 }
@@ -1723,7 +2320,11 @@ int main(int argc, char** argv) {
   }
   std::string src;
   if (!ae::read_file(input, src)) {
-    std::fprintf(stderr, "aetherc: cannot read %s\n", input.c_str());
+    if (json)
+      std::fprintf(stderr, "{\"code\":\"AE0100\",\"file\":\"%s\",\"line\":0,\"col\":0,\"message\":\"cannot read input\"}\n",
+                   json_escape(input).c_str());
+    else
+      std::fprintf(stderr, "%s: error[AE0100]: cannot read input\n", input.c_str());
     return 2;
   }
   try {
@@ -1745,15 +2346,23 @@ int main(int argc, char** argv) {
       else std::ofstream(output) << o.str();
       return 0;
     }
+    std::set<std::string> seen;
+    ae::Gen::resolve_uses(prog, stdlib, dirname_of(input), seen);
+    // The reference's order: traits always; scalar types under --check; borrows on both paths.
+    ae::check_traits(prog);
+    if (check) {
+      ae::TypeCheck(prog).run();
+      ae::BorrowCheck().run(prog);
+      return 0;
+    }
+    ae::BorrowCheck().run(prog);
+    ae::prepare_codegen(prog);
     int fused = 0;
     if (fuse)
       for (auto& f : prog.fns)
         if (f.body) fused += ae::fuse_block(*f.body);
-    std::set<std::string> seen;
-    ae::Gen::resolve_uses(prog, stdlib, dirname_of(input), seen);
     ae::Gen g(prog, stdlib, dirname_of(input));
     const std::string c = g.run();
-    if (check) return 0;
     if (emit == "c") {
       if (output.empty()) std::fputs(c.c_str(), stdout);
       else std::ofstream(output) << c;

@@ -66,20 +66,101 @@ def test_tensor_methods_lower_to_shaped_abi_calls():
 
 @pytest.mark.parametrize("src,code", [
     ("fn main() -> i32 { let t: Tensor<f32, [4, 3]>; let w: Tensor<f32, [2, 5]>; "
-     "let y: Tensor<f32, [4, 5]>; t.matmul(&w, &mut y); 0 }", "AE0254"),          # inner dims differ
-    ("fn main() -> i32 { let t: Tensor<f32, [4]>; t.transpose(); 0 }", "AE0251"),  # unknown method
-    ("fn main() -> i32 { let x: i32 = 1; x.gelu(); 0 }", "AE0250"),              # not a tensor
-    ("fn main() -> i32 { undefined_fn(1) }", "AE0240"),
-    ("fn main() -> i32 { let t: Tensor<f32, [0]>; 0 }", "AE0221"),
-    ("struct S { a: i32 }\nfn main() -> i32 { 0 }", "AE0100"),
+     "let y: Tensor<f32, [4, 5]>; t.matmul(&w, &mut y); 0 }", "AE0554"),          # inner dims differ
+    ("fn main() -> i32 { let t: Tensor<f32, [4]>; t.transpose(); 0 }", "AE0551"),  # unknown method
+    ("fn main() -> i32 { let x: i32 = 1; x.gelu(); 0 }", "AE0550"),              # not a tensor
+    ("fn main() -> i32 { undefined_fn(1) }", "AE0540"),
+    ("fn main() -> i32 { let t: Tensor<f32, [0]>; 0 }", "AE0521"),
+    ("struct S { a: i32 }\nfn main() -> i32 { 0 }", "AE0500"),                  # checked, not compiled
 ])
-def test_diagnostics_carry_codes(tmp_path, src, code):
+def test_codegen_diagnostics_carry_codes(tmp_path, src, code):
+    """Errors found while lowering to C (this compiler's own AE05xx codes)."""
     f = tmp_path / "bad.aether"
     f.write_text(src)
-    r = subprocess.run([AEC, str(f), "--check", "--json-errors"], capture_output=True, text=True, timeout=60)
+    r = subprocess.run([AEC, str(f), "--emit=c", "-o", str(tmp_path / "bad.c"), "--json-errors"],
+                       capture_output=True, text=True, timeout=60)
     assert r.returncode == 1
     d = json.loads(r.stderr.strip().splitlines()[-1])
     assert d["code"] == code and d["line"] >= 1, d
+
+
+# `--check` programs and the code each must fail with (None: must check clean).
+CHECK_CASES = [
+    ("fn main() -> i32 { return 0; }", None),
+    ("#[autodiff]\n#[distributed(world_size=4, backend=\"nccl\")]\nfn step() { let h = encode(); "
+     "let l = h.mse(target); l.backward(); }", None),                              # names resolve at codegen only
+    ("pub struct Pair<A, B> { a: A, b: B, }\nconst N: i64 = 64;\n"
+     "extern fn mm(x: &Tensor<f32, [R, C]>, y: &mut Tensor<f32, [C, R]>) -> i32;\n"
+     "fn go(x: &Tensor<f32, [R, C]>, y: &mut Tensor<f32, [C, R]>) { mm(x, y); }", None),
+    ("fn k() { parallel for i in 0..32 { warp { let v = 1; } block { let w = 2; } } "
+     "if 2 > 1 { let a = 1; } else { let b = 2; } }", None),
+    ("fn main() -> i64 { let v: i64 = 9; let p = &v; let q = &v; let r = &v; v }", None),
+    ("fn main() -> i64 { let mut v: i64 = 1; let p = &mut v; *p = 2; let q = &mut v; *q = 3; v }", None),
+    ("trait Area { fn area(&self) -> i32; fn twice(&self) -> i32 { 2 } }\nstruct Sq { s: i32 }\n"
+     "impl Area for Sq { fn area(&self) -> i32 { 1 } }\nfn main() -> i32 { 0 }", None),
+    ("extern fn f(a: i32) -> i32 { 0 }", "AE0002"),                               # extern with a body
+    ("fn g() { h(1 2); }", "AE0002"),
+    ("fn main() -> i32 { 0", "AE0002"),
+    ("fn main() -> i32 { let s = \"open; 0 }", "AE0001"),
+    ("use no_such_module;\nfn main() -> i32 { 0 }", "AE0003"),
+    ("fn main() -> i64 { let mut v: i64 = 1; let p = &mut v; let q = &mut v; *p = 2; *q = 3; v }", "AE0200"),
+    ("fn main() -> i64 { let mut v: i64 = 1; let p = &mut v; let q = &v; let t = *q; *p = 2; t }", "AE0201"),
+    ("fn main() -> i64 { let mut v: i64 = 1; f(&mut v, &v) }\nfn f(a: &mut i64, b: &i64) -> i64 { 0 }", "AE0201"),
+    ("trait Area { fn area(&self) -> i32; }\nstruct Sq { s: i32 }\nimpl Area for Sq { }\n"
+     "fn main() -> i32 { 0 }", "AE0210"),
+    ("struct Sq { s: i32 }\nimpl Paint for Sq { fn paint(&self) -> i32 { 0 } }\nfn main() -> i32 { 0 }", "AE0211"),
+    ("trait Base { fn b(&self) -> i32; }\ntrait Top: Base { fn t(&self) -> i32; }\nstruct C { i: i32 }\n"
+     "impl Top for C { fn t(&self) -> i32 { 0 } }\nfn main() -> i32 { 0 }", "AE0212"),
+    ("fn main() -> i32 { let x: i32 = 2.5; x }", "AE0220"),
+    ("fn main() -> i32 { let f: f64 = 2; 0 }", "AE0220"),
+    ("fn main() -> i32 { let b: bool = 1; 0 }", "AE0220"),
+    ("fn half(v: i64) -> i64 { v / 2 }\nfn main() -> i32 { half(1.5) as i32 }", "AE0221"),
+    ("fn r() -> i64 { 0.5 }\nfn main() -> i32 { 0 }", "AE0222"),
+    ("fn r() -> i64 { return 0.5; }\nfn main() -> i32 { 0 }", "AE0222"),
+    ("fn main() -> i32 { let mut n: i32 = 0; n = 0.5; n }", "AE0224"),
+]
+
+
+@pytest.mark.parametrize("src,code", CHECK_CASES)
+def test_check_mode(tmp_path, src, code):
+    """`--check` runs the reference's front-end checks: parse, `use`, traits,
+    scalar type conflicts and borrows, with the reference's AE codes."""
+    f = tmp_path / "p.aether"
+    f.write_text(src)
+    r = subprocess.run([AEC, str(f), "--check", "--json-errors"], capture_output=True, text=True, timeout=60)
+    if code is None:
+        assert r.returncode == 0, r.stderr
+        return
+    assert r.returncode == 1, (src, r.stderr)
+    d = json.loads(r.stderr.strip().splitlines()[-1])
+    assert d["code"] == code and d["line"] >= 1, (src, d)
+
+
+REF_CONFORMANCE = "/root/reference/tests/aether"
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_CONFORMANCE), reason="reference conformance suite not on this machine")
+def test_reference_conformance_suite():
+    """The reference's conformance suite, run the way its audit tool runs it
+    (tools/audit/src/conformance.rs): every file under positive/ must
+    `--check` clean, every negative/expect_AE####_*.aether must fail with
+    that code."""
+    bad = []
+    for kind in ("positive", "negative"):
+        d = os.path.join(REF_CONFORMANCE, kind)
+        for name in sorted(os.listdir(d)):
+            if not name.endswith(".aether"):
+                continue
+            r = subprocess.run([AEC, os.path.join(d, name), "--check", "--json-errors"], capture_output=True,
+                               text=True, timeout=60)
+            if kind == "positive":
+                if r.returncode != 0:
+                    bad.append((name, r.stderr[-300:]))
+                continue
+            want = re.search(r"_(AE\d{4})_", name).group(1)
+            if r.returncode == 0 or f'"code":"{want}"' not in r.stderr:
+                bad.append((name, r.stderr[-300:]))
+    assert not bad, bad
 
 
 @pytest.mark.skipif(not os.path.isdir(REF_WITNESSES), reason="reference witnesses not on this machine")
