@@ -19,7 +19,7 @@
 //       The `///` comment run right above each fn / extern fn / struct / enum
 //       / trait / impl / const, as a markdown (or HTML) index grouped by file.
 //       Reference: tools/aetherdoc/src/main.rs.
-//   aether-audit [--json] [--only sloc|markers|witnesses|abi] [--root DIR]
+//   aether-audit [--json] [--only sloc|markers|witnesses|conformance|abi] [--root DIR]
 //       Repository audit: source lines per component (code / comment /
 //       blank), unfinished-work markers in product sources, the .aether
 //       witnesses compiled with aetherc and run against their
@@ -732,6 +732,47 @@ int main_audit(const std::vector<std::string>& args) {
     }
     js += "]";
     std::fprintf(stderr, "witnesses: %d pass, %d fail, %d skipped\n", pass, fail, skip);
+  }
+  if (want("conformance")) {
+    // tests/aether/positive/*.aether must `--check` clean; tests/aether/negative/
+    // expect_AE####_*.aether must fail with that code (the reference's
+    // conformance layout, tools/audit/src/conformance.rs).
+    key("conformance");
+    js += "[";
+    bool f1 = true;
+    const std::string aec = bin + "/aetherc";
+    int pass = 0, fail = 0;
+    for (const char* kind : {"positive", "negative"}) {
+      std::vector<std::string> progs;
+      walk(root + "/tests/aether/" + kind, progs);
+      std::sort(progs.begin(), progs.end());
+      for (const std::string& p : progs) {
+        if (ext_of(p) != ".aether") continue;
+        const std::string name = p.substr(p.rfind('/') + 1);
+        std::string want;
+        if (std::string(kind) == "negative") {
+          const size_t k = name.find("_AE");
+          if (k == std::string::npos || k + 7 > name.size()) continue;
+          want = name.substr(k + 1, 6);
+        }
+        std::string log;
+        const int rc = run_cmd({aec, p, "--check", "--json-errors"}, &log, 60);
+        std::string status;
+        if (want.empty()) status = rc == 0 ? "pass" : "unexpected failure";
+        else if (rc == 0) status = "unexpected success";
+        else status = log.find("\"code\":\"" + want + "\"") != std::string::npos ? "pass" : "wrong code";
+        if (status == "pass") ++pass;
+        else {
+          ++fail;
+          errors.push_back("conformance " + name + ": " + status);
+        }
+        std::fprintf(stderr, "conformance %-44s %s\n", name.c_str(), status.c_str());
+        js += (f1 ? "" : ",") + std::string("{\"name\":") + json_str(name) + ",\"status\":" + json_str(status) + "}";
+        f1 = false;
+      }
+    }
+    js += "]";
+    std::fprintf(stderr, "conformance: %d pass, %d fail\n", pass, fail);
   }
   if (want("abi")) {
     key("abi");

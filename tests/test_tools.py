@@ -87,6 +87,17 @@ def test_audit_runs_witnesses():
     assert cpu and all(w["status"] == "pass" for w in cpu), rep
 
 
+def test_audit_runs_conformance():
+    """The package's conformance suite: positive files check clean, each
+    negative file fails with the code its name carries."""
+    r = run("aether-audit", "--json", "--root", ROOT, "--only", "conformance")
+    rep = json.loads(r.stdout)
+    assert r.returncode == 0, rep["errors"]
+    names = [c["name"] for c in rep["conformance"]]
+    assert len(names) >= 18 and all(c["status"] == "pass" for c in rep["conformance"]), rep
+    assert sum(n.startswith("expect_AE02") for n in names) >= 9
+
+
 def test_witness_stamper(tmp_path):
     d = tmp_path / "w"
     d.mkdir()
