@@ -20,9 +20,15 @@
 // `continue`, `return`, `if` / `else if` / `else` as statements and
 // expressions, block tail expressions, arithmetic / comparison / logical /
 // bitwise operators, compound assignment, `as` casts and the cast builtins
-// f32() f64() i32() i64(), println / print, float math builtins, and method
-// calls on tensors. Anything else (structs, traits, closures, macros,
-// generics) is a diagnostic, not a miscompile.
+// f32() f64() i32() i64(), println / print, float math builtins, method
+// calls on tensors, structs (C structs by value: literals, nested and array
+// fields), impl and trait methods (`Type__method`, `&self` by pointer, trait
+// default bodies copied into each impl, `Type::f()`, `Self`), enums (no
+// payload: integers; with payloads: tagged structs), `match` with literal,
+// wildcard, binding, path and tuple-variant patterns, `|` and guards,
+// `if let` / `while let`, and references to scalars and structs as pointers
+// (an address passed where an i64 is declared is the address as an integer).
+// Generic items, closures and macros are diagnostics, not miscompiles.
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -224,7 +230,7 @@ std::vector<Tok> lex(const std::string& src) {
 }
 
 // ============================================================================ types
-enum class B { Void, Bool, I8, I16, I32, I64, U8, U16, U32, U64, F32, F64, Str, Tensor, Array, Unknown };
+enum class B { Void, Bool, I8, I16, I32, I64, U8, U16, U32, U64, F32, F64, Str, Tensor, Array, Struct, Unknown };
 
 struct Ty {
   B b = B::Unknown;
@@ -232,6 +238,8 @@ struct Ty {
   std::vector<int64_t> dims;     // tensor shape
   std::shared_ptr<Ty> inner;     // array element
   int64_t len = 0;               // array length
+  std::string sname;             // struct name
+  bool ref = false;              // a reference (`&T` of a scalar or struct): a C pointer
   bool is_int() const { return b >= B::I8 && b <= B::U64; }
   bool is_float() const { return b == B::F32 || b == B::F64; }
   bool is_num() const { return is_int() || is_float(); }
@@ -256,6 +264,12 @@ const std::map<std::string, B>& prim_names() {
 }
 
 std::string ctype(const Ty& t) {
+  if (t.ref) {
+    Ty base = t;
+    base.ref = false;
+    return ctype(base) + "*";
+  }
+  if (t.b == B::Struct) return "aes_" + t.sname;
   switch (t.b) {
     case B::Void: return "void";
     case B::Bool: return "int";
@@ -276,6 +290,11 @@ std::string ctype(const Ty& t) {
 }
 
 std::string tyname(const Ty& t) {
+  if (t.ref) {
+    Ty base = t;
+    base.ref = false;
+    return "&" + tyname(base);
+  }
   for (auto& kv : prim_names())
     if (kv.second == t.b && kv.first != "isize" && kv.first != "usize") return t.b == B::Str ? "&str" : kv.first;
   if (t.b == B::Void) return "()";
@@ -285,6 +304,7 @@ std::string tyname(const Ty& t) {
     return s + "]>";
   }
   if (t.b == B::Array) return "[" + tyname(*t.inner) + "; " + std::to_string(t.len) + "]";
+  if (t.b == B::Struct) return t.sname;
   return "?";
 }
 
@@ -299,17 +319,31 @@ using BP = std::shared_ptr<Block>;
 struct TyExpr {  // a type as written; tensor dims / array lengths may name constants
   std::string name;              // primitive / "Tensor" / "[]" / "&str" / a struct name
   bool generic = false;          // written with generic arguments (Vec<T>, ...)
+  bool ref = false;              // written `&T` / `&mut T`
   std::string elem;              // tensor element
   std::vector<EP> dims;          // tensor dims or {array length}
   std::shared_ptr<TyExpr> inner; // array element
   int line = 0, col = 0;
 };
 
+// A `match` / `if let` / `while let` pattern.
+struct Pat {
+  enum K { Wild, Lit, Bind, Path, Tuple, Or } k = Wild;
+  std::string s;  // literal text, binding name or path
+  bool neg = false;  // a negative literal
+  std::vector<std::shared_ptr<Pat>> subs;  // Tuple: the payload patterns; Or: the alternatives
+  int line = 0, col = 0;
+};
+using PP = std::shared_ptr<Pat>;
+
 struct Expr {
   enum K { Int, Float, BoolL, Str, Char, Var, Unary, Binary, Call, Method, Cast, Ref, If, BlockE, Index, ArrayLit,
-           ArrayRep, LoopE, Field, Deref } k;
-  std::string s;  // literal / name / operator / method
+           ArrayRep, LoopE, Field, Deref, StructLit, Match } k;
+  std::string s;  // literal / name / operator / method / struct
   std::vector<EP> a;
+  std::vector<std::string> fields;  // struct literal: the field each of `a` initialises
+  std::vector<PP> pats;             // match: one pattern per arm (a[0] the scrutinee, a[i + 1] arm i)
+  std::vector<EP> guards;           // match: the arm's `if` guard or null
   BP blk, blk2;   // if: then / else block (else may be an `if` wrapped in a block)
   std::shared_ptr<TyExpr> cast;
   bool mut = false;
@@ -324,6 +358,7 @@ struct Block {
 
 struct Stmt {
   enum K { Let, ExprS, Assign, While, Loop, For, Return, Break, Continue } k;
+  PP pat;  // `while let pat = e`
   std::string name, op;
   bool mut = false, inclusive = false;
   std::shared_ptr<TyExpr> ty;
@@ -335,6 +370,7 @@ struct Stmt {
 struct Param {
   std::string name;
   std::shared_ptr<TyExpr> ty;
+  bool self_ref = false;  // `&self` / `&mut self`
 };
 struct Fn {
   std::string name;
@@ -356,6 +392,12 @@ struct TraitDef {
   std::vector<Fn> methods;
   int line = 0, col = 0;
 };
+struct EnumDef {
+  std::string name;
+  std::vector<std::string> generics;
+  std::vector<std::pair<std::string, std::vector<std::shared_ptr<TyExpr>>>> variants;  // name, payload types
+  int line = 0, col = 0;
+};
 struct ImplDef {
   std::string trait;  // empty: an inherent impl
   std::string type;
@@ -375,6 +417,7 @@ struct Program {
   std::vector<StructDef> structs;
   std::vector<TraitDef> traits;
   std::vector<ImplDef> impls;
+  std::vector<EnumDef> enums;
 };
 
 // ============================================================================ parser
@@ -413,6 +456,8 @@ class Parser {
         p.traits.push_back(trait_def());
       } else if (is_id("impl")) {
         p.impls.push_back(impl_def());
+      } else if (is_id("enum")) {
+        p.enums.push_back(enum_def());
       } else {
         fail("AE0002", cur().line, cur().col, "expected an item (fn, extern fn, const, static, struct, trait, impl, "
                                               "use), found '" + cur().s + "'");
@@ -566,6 +611,89 @@ class Parser {
     return d;
   }
 
+  EnumDef enum_def() {
+    EnumDef d;
+    d.line = cur().line;
+    d.col = cur().col;
+    next();  // enum
+    d.name = ident();
+    d.generics = generic_params();
+    expect_op("{");
+    while (!is_op("}")) {
+      if (is_op("#")) {
+        attribute();
+        continue;
+      }
+      std::pair<std::string, std::vector<std::shared_ptr<TyExpr>>> v;
+      v.first = ident();
+      if (eat_op("(")) {
+        while (!is_op(")")) {
+          v.second.push_back(type());
+          if (!eat_op(",")) break;
+        }
+        expect_op(")");
+      } else if (is_op("{")) {
+        fail("AE0500", cur().line, cur().col, "variants with named fields are not supported");
+      } else if (eat_op("=")) {
+        expr();  // an explicit discriminant: variants are numbered by position here
+      }
+      d.variants.push_back(v);
+      if (!eat_op(",")) break;
+    }
+    expect_op("}");
+    return d;
+  }
+
+  // A pattern: `_`, a literal, a binding, a path, `Path(p, ..)`, `p | p`.
+  PP pattern() {
+    PP first = pattern_one();
+    if (!is_op("|")) return first;
+    auto o = std::make_shared<Pat>();
+    o->k = Pat::Or;
+    o->line = first->line;
+    o->col = first->col;
+    o->subs.push_back(first);
+    while (eat_op("|")) o->subs.push_back(pattern_one());
+    return o;
+  }
+  PP pattern_one() {
+    auto p = std::make_shared<Pat>();
+    p->line = cur().line;
+    p->col = cur().col;
+    if (eat_op("-")) {
+      p->neg = true;
+      if (!at(T::Int) && !at(T::Float)) fail("AE0002", cur().line, cur().col, "expected a number after '-'");
+    }
+    if (at(T::Int) || at(T::Float) || at(T::Char) || at(T::Str)) {
+      p->k = Pat::Lit;
+      p->s = (at(T::Char) ? "'" : "") + cur().s;
+      if (at(T::Str)) p->s = "\"" + cur().s;
+      next();
+      return p;
+    }
+    if (is_id("true") || is_id("false")) {
+      p->k = Pat::Lit;
+      p->s = cur().s;
+      next();
+      return p;
+    }
+    std::string name = ident();
+    if (name == "_") return p;
+    while (eat_op("::")) name += "::" + ident();
+    p->s = name;
+    if (eat_op("(")) {
+      p->k = Pat::Tuple;
+      while (!is_op(")")) {
+        p->subs.push_back(pattern());
+        if (!eat_op(",")) break;
+      }
+      expect_op(")");
+      return p;
+    }
+    p->k = name.find("::") != std::string::npos ? Pat::Path : Pat::Bind;
+    return p;
+  }
+
   ImplDef impl_def() {
     ImplDef d;
     d.line = cur().line;
@@ -627,7 +755,8 @@ class Parser {
         t->name = "str";
         return t;
       }
-      return in;  // references to scalars / tensors are passed by value (handles)
+      in->ref = true;  // a pointer for scalars and structs; tensors (handles) and arrays travel as they are
+      return in;
     }
     if (eat_op("[")) {
       t->name = "[]";
@@ -687,6 +816,7 @@ class Parser {
         eat_id("mut");
         next();  // self
         p.name = "self";
+        p.self_ref = true;
       } else {
         eat_id("mut");
         p.name = ident();
@@ -729,7 +859,7 @@ class Parser {
   }
 
   static bool block_like(const EP& e) {
-    return e->k == Expr::If || e->k == Expr::BlockE || e->k == Expr::LoopE;
+    return e->k == Expr::If || e->k == Expr::BlockE || e->k == Expr::LoopE || e->k == Expr::Match;
   }
 
   EP last_expr_;
@@ -750,6 +880,10 @@ class Parser {
     }
     if (eat_id("while")) {
       s->k = Stmt::While;
+      if (eat_id("let")) {
+        s->pat = pattern();
+        expect_op("=");
+      }
       s->e = expr_nostruct();
       s->body = block();
       return s;
@@ -768,13 +902,18 @@ class Parser {
       s->k = Stmt::For;
       s->name = ident();
       if (!eat_id("in")) fail("AE0002", cur().line, cur().col, "expected 'in'");
+      const bool saved = no_struct_;
+      no_struct_ = true;
       s->e = expr_prec(9);
+      no_struct_ = saved;
       if (eat_op("..=")) {
         s->inclusive = true;
       } else if (!eat_op("..")) {
         fail("AE0500", cur().line, cur().col, "for loops iterate over ranges a..b or a..=b");
       }
+      no_struct_ = true;
       s->e2 = expr_prec(9);
+      no_struct_ = saved;
       s->body = block();
       return s;
     }
@@ -830,8 +969,22 @@ class Parser {
     return e;
   }
 
-  EP expr() { return expr_prec(0); }
-  EP expr_nostruct() { return expr_prec(0); }
+  EP expr() {
+    const bool saved = no_struct_;
+    no_struct_ = false;
+    EP e = expr_prec(0);
+    no_struct_ = saved;
+    return e;
+  }
+  // A condition or range: `Name {` there opens the block, not a struct literal.
+  EP expr_nostruct() {
+    const bool saved = no_struct_;
+    no_struct_ = true;
+    EP e = expr_prec(0);
+    no_struct_ = saved;
+    return e;
+  }
+  bool no_struct_ = false;
 
   static int prec(const std::string& op) {
     if (op == "||") return 1;
@@ -1000,6 +1153,51 @@ class Parser {
       e->blk = block();
       return e;
     }
+    if (eat_id("match")) {
+      EP e = mk(Expr::Match, at);
+      e->a = {expr_nostruct()};
+      expect_op("{");
+      while (!is_op("}")) {
+        if (cur().t == T::Eof) fail("AE0002", at.line, at.col, "unclosed match");
+        e->pats.push_back(pattern());
+        e->guards.push_back(eat_id("if") ? expr() : nullptr);
+        expect_op("=>");
+        EP arm = expr();
+        e->a.push_back(arm);
+        if (!eat_op(",") && !is_op("}") && !block_like(arm))
+          fail("AE0002", cur().line, cur().col, "expected ',' after a match arm, found '" + cur().s + "'");
+      }
+      expect_op("}");
+      return e;
+    }
+    if (is_id("if") && peek().t == T::Id && peek().s == "let") {  // if let P = e { .. } else { .. }
+      next();
+      next();
+      EP e = mk(Expr::Match, at);
+      e->pats.push_back(pattern());
+      expect_op("=");
+      e->a = {expr_nostruct()};
+      EP then_e = mk(Expr::BlockE, at);
+      then_e->blk = block();
+      e->a.push_back(then_e);
+      e->guards.push_back(nullptr);
+      auto wild = std::make_shared<Pat>();
+      e->pats.push_back(wild);
+      e->guards.push_back(nullptr);
+      EP else_e = mk(Expr::BlockE, at);
+      if (eat_id("else")) {
+        if (is_id("if")) {
+          else_e->blk = std::make_shared<Block>();
+          else_e->blk->tail = primary();
+        } else {
+          else_e->blk = block();
+        }
+      } else {
+        else_e->blk = std::make_shared<Block>();
+      }
+      e->a.push_back(else_e);
+      return e;
+    }
     if (eat_id("if")) {
       EP e = mk(Expr::If, at);
       e->a = {expr_nostruct()};
@@ -1032,9 +1230,30 @@ class Parser {
     }
     if (at.t == T::Id) {
       std::string name = ident();
-      while (is_op("::")) {  // paths: the last segment names the item
+      while (is_op("::")) {  // a path; code generation resolves `Type::item`, else the last segment
         next();
-        name = ident();
+        name += "::" + ident();
+      }
+      if (!no_struct_ && is_op("{") &&
+          (peek().s == "}" || (peek().t == T::Id && (peek(2).s == ":" || peek(2).s == "," || peek(2).s == "}")))) {
+        EP e = mk(Expr::StructLit, at);  // `Name { field: value, .. }` (or the `field` shorthand)
+        e->s = name;
+        next();
+        while (!is_op("}")) {
+          const Tok f = cur();
+          const std::string fname = ident();
+          e->fields.push_back(fname);
+          if (eat_op(":")) {
+            e->a.push_back(expr());
+          } else {
+            EP v = mk(Expr::Var, f);
+            v->s = fname;
+            e->a.push_back(v);
+          }
+          if (!eat_op(",")) break;
+        }
+        expect_op("}");
+        return e;
       }
       if (eat_op("!")) fail("AE0500", at.line, at.col, "macros are not supported");
       if (eat_op("(")) {
@@ -1140,7 +1359,8 @@ struct FnSig {
   std::vector<Ty> params;
   Ty ret;
   std::string c;
-  bool is_extern;
+  bool is_extern = false;
+  int self_kind = 0;  // a method's receiver: 0 none, 1 by value, 2 by pointer (`&self`)
 };
 
 class Gen {
@@ -1150,7 +1370,16 @@ class Gen {
 
   std::string run() {
     for (auto& c : p_.consts) const_src_[c.name] = &c;
+    declare_structs();
+    synthesize_defaults();
     for (auto& f : p_.fns) declare(f);
+    for (auto& im : p_.impls) {
+      if (!structs_.count(im.type))
+        fail("AE0500", im.line, im.col, "impl for '" + im.type + "', which is not a struct of this program");
+      self_type_ = im.type;
+      for (auto& m : im.methods) declare_method(im.type, m);
+    }
+    self_type_.clear();
     std::ostringstream o;
     o << "/* generated by aetherc */\n#include <stdint.h>\n#include <stdio.h>\n#include <math.h>\n\n";
     o << "int64_t aether_dev_alloc_f32(int32_t);\nint64_t aether_dev_alloc_i32(int32_t);\n"
@@ -1165,15 +1394,26 @@ class Gen {
       o << ctype(s.ret) << " " << s.c << "(" << plist(s) << ");\n";
     }
     o << "\n";
+    o << struct_decls() << "\n";
     for (auto& c : p_.consts) {
       Ty t = resolve(*c.ty);
       o << "static const " << ctype(t) << " aec_" << c.name << " = " << lit_of(eval_const(c.e), t) << ";\n";
     }
     for (auto& f : p_.fns)
       if (!f.is_extern) o << "static " << ctype(sigs_[f.name].ret) << " " << sigs_[f.name].c << "(" << plist(sigs_[f.name]) << ");\n";
+    for (auto& im : p_.impls)
+      for (auto& m : im.methods) {
+        const FnSig& sg = sigs_[im.type + "::" + m.name];
+        o << "static " << ctype(sg.ret) << " " << sg.c << "(" << plist(sg) << ");\n";
+      }
     o << "\n";
     for (auto& f : p_.fns)
-      if (!f.is_extern) o << fn_def(f);
+      if (!f.is_extern) o << fn_def(f, f.name);
+    for (auto& im : p_.impls) {
+      self_type_ = im.type;
+      for (auto& m : im.methods) o << fn_def(m, im.type + "::" + m.name);
+    }
+    self_type_.clear();
     if (!sigs_.count("main") || sigs_["main"].is_extern) fail("AE0580", 1, 1, "program has no `fn main`");
     const FnSig& m = sigs_["main"];
     o << "int main(void) {\n";
@@ -1203,8 +1443,315 @@ class Gen {
   static std::string plist(const FnSig& s) {
     if (s.params.empty()) return "void";
     std::string r;
-    for (size_t i = 0; i < s.params.size(); ++i) r += (i ? ", " : "") + ctype(s.params[i]);
+    for (size_t i = 0; i < s.params.size(); ++i)
+      r += (i ? ", " : "") + ctype(s.params[i]) + (i == 0 && s.self_kind == 2 ? "*" : "");
     return r;
+  }
+
+  struct V {  // a generated C expression and its type
+    std::string c;
+    Ty t;
+  };
+
+  // --------------------------------------------------------------- structs and impls
+  struct StructInfo {
+    std::vector<std::pair<std::string, Ty>> fields;
+  };
+  std::map<std::string, StructInfo> structs_;
+  std::string self_type_;  // the impl whose methods are being declared / generated
+
+  Ty struct_ty(const std::string& n) const {
+    Ty t;
+    t.b = B::Struct;
+    t.sname = n;
+    return t;
+  }
+
+  // Trait methods with a default body that an impl does not override are
+  // copied into the impl, so each type gets its own `Type__method`.
+  void synthesize_defaults() {
+    std::map<std::string, const TraitDef*> traits;
+    for (auto& t : p_.traits) traits[t.name] = &t;
+    for (auto& im : p_.impls) {
+      if (im.trait.empty() || !traits.count(im.trait)) continue;
+      std::set<std::string> have;
+      for (auto& m : im.methods) have.insert(m.name);
+      for (auto& m : traits[im.trait]->methods)
+        if (m.body && !have.count(m.name)) im.methods.push_back(m);
+    }
+  }
+
+  // Enums: one with no payload anywhere is an integer (its variant's
+  // position); one with payloads is a tagged C struct with a union of the
+  // variants' payload tuples.
+  struct EnumInfo {
+    std::vector<std::pair<std::string, std::vector<Ty>>> variants;
+    bool unit_only = true;
+  };
+  std::map<std::string, EnumInfo> enums_;
+
+  int variant_index(const std::string& en, const std::string& v) const {
+    const auto& vs = enums_.at(en).variants;
+    for (size_t i = 0; i < vs.size(); ++i)
+      if (vs[i].first == v) return (int)i;
+    return -1;
+  }
+
+  void declare_structs() {
+    for (auto& d : p_.structs) {
+      if (!d.generics.empty())
+        fail("AE0500", d.line, d.col, "generic structs are checked but not compiled by this compiler");
+      if (structs_.count(d.name)) fail("AE0501", d.line, d.col, "struct '" + d.name + "' is defined twice");
+      structs_[d.name];
+    }
+    for (auto& d : p_.enums) {
+      if (!d.generics.empty())
+        fail("AE0500", d.line, d.col, "generic enums are checked but not compiled by this compiler");
+      if (structs_.count(d.name) || enums_.count(d.name))
+        fail("AE0501", d.line, d.col, "type '" + d.name + "' is defined twice");
+      EnumInfo& in = enums_[d.name];
+      for (auto& v : d.variants) in.unit_only &= v.second.empty();
+    }
+    for (auto& d : p_.structs)
+      for (auto& f : d.fields) structs_[d.name].fields.push_back({f.name, resolve(*f.ty)});
+    for (auto& d : p_.enums)
+      for (auto& v : d.variants) {
+        std::vector<Ty> ts;
+        for (auto& t : v.second) ts.push_back(resolve(*t));
+        enums_[d.name].variants.push_back({v.first, ts});
+      }
+  }
+
+  void declare_method(const std::string& type, const Fn& m) {
+    FnSig s;
+    s.c = "aef_" + type + "__" + m.name;
+    for (size_t i = 0; i < m.params.size(); ++i) {
+      const Param& prm = m.params[i];
+      if (prm.name == "self" && !prm.ty) {
+        if (i != 0) fail("AE0002", m.line, m.col, "`self` must be the first parameter");
+        s.self_kind = prm.self_ref ? 2 : 1;
+        s.params.push_back(struct_ty(type));
+      } else {
+        s.params.push_back(resolve(*prm.ty));
+      }
+    }
+    s.ret = m.ret ? resolve(*m.ret) : prim(B::Void);
+    const std::string key = type + "::" + m.name;
+    if (sigs_.count(key)) fail("AE0501", m.line, m.col, "method '" + key + "' is defined twice");
+    sigs_[key] = s;
+  }
+
+  // C declarations of every struct, fields before the structs that hold them.
+  std::string struct_decls() {
+    std::ostringstream o;
+    std::vector<std::string> order;
+    std::set<std::string> done, visiting;
+    std::function<void(const std::string&)> visit = [&](const std::string& n) {
+      if (done.count(n)) return;
+      if (visiting.count(n)) fail("AE0500", 1, 1, "type '" + n + "' contains itself");
+      visiting.insert(n);
+      std::vector<const Ty*> parts;
+      if (enums_.count(n)) {
+        for (auto& v : enums_[n].variants)
+          for (auto& t : v.second) parts.push_back(&t);
+      } else {
+        for (auto& f : structs_[n].fields) parts.push_back(&f.second);
+      }
+      for (const Ty* t : parts) {
+        while (t->b == B::Array) t = t->inner.get();
+        if (t->b == B::Struct) visit(t->sname);
+      }
+      done.insert(n);
+      order.push_back(n);
+    };
+    for (auto& d : p_.structs) visit(d.name);
+    for (auto& d : p_.enums)
+      if (!enums_[d.name].unit_only) visit(d.name);
+    for (auto& n : order) o << "typedef struct aes_" << n << " aes_" << n << ";\n";
+    for (auto& n : order) {
+      if (enums_.count(n)) {
+        o << "struct aes_" << n << " { int64_t tag; union {";
+        for (auto& v : enums_[n].variants) {
+          if (v.second.empty()) continue;
+          o << " struct {";
+          for (size_t k = 0; k < v.second.size(); ++k) o << " " << ctype(v.second[k]) << " a" << k << ";";
+          o << " } v_" << v.first << ";";
+        }
+        o << " } u; };\n";
+        continue;
+      }
+      o << "struct aes_" << n << " {";
+      if (structs_[n].fields.empty()) o << " char unused_;";
+      for (auto& f : structs_[n].fields) {
+        if (f.second.b == B::Array) o << " " << ctype(*f.second.inner) << " f_" << f.first << "[" << f.second.len << "];";
+        else o << " " << ctype(f.second) << " f_" << f.first << ";";
+      }
+      o << " };\n";
+    }
+    return o.str();
+  }
+
+  static bool is_place(const EP& e) {
+    return e->k == Expr::Var || e->k == Expr::Field || e->k == Expr::Index;
+  }
+
+  // A call of a method or associated function `key` ("Type::name"); args[0]
+  // is the receiver when the method takes `self`.
+  V method_call(const EP& at, const std::string& key, const std::vector<EP>& args, const V* recv) {
+    const FnSig& sig = sigs_.at(key);
+    const size_t given = args.size() + (recv ? 1 : 0);
+    if (given != sig.params.size())
+      fail("AE0541", at->line, at->col, "'" + key + "' takes " + std::to_string(sig.params.size()) + " arguments, got " +
+                                            std::to_string(given));
+    std::string pre, list;
+    size_t pi = 0;
+    auto self_arg = [&](const V& v, const EP& src) {
+      if (sig.self_kind != 2) return conv(v, sig.params[0]);
+      if (src && is_place(src)) return "&(" + v.c + ")";
+      const std::string tmp = "tmp_" + std::to_string(++uniq_);  // an rvalue receiver: a temporary holds it
+      pre += ctype(v.t) + " " + tmp + " = " + v.c + "; ";
+      return "&" + tmp;
+    };
+    if (recv) {
+      list = self_arg(*recv, args.empty() ? nullptr : nullptr);
+      pi = 1;
+    }
+    for (size_t i = 0; i < args.size(); ++i, ++pi) {
+      V v = gen(args[i], sig.params[pi]);
+      std::string c = (pi == 0 && sig.self_kind) ? self_arg(v, args[i]) : conv(v, sig.params[pi]);
+      list += (pi ? ", " : "") + c;
+    }
+    const std::string call = sig.c + "(" + list + ")";
+    if (pre.empty()) return {call, sig.ret};
+    return {"({ " + pre + call + "; })", sig.ret};
+  }
+
+  // The C condition under which pattern `p` matches the value `m` of type
+  // `t`; the declarations of its bindings are appended to `binds`.
+  std::string pat_test(const Pat& p, const std::string& m, const Ty& t, std::string& binds) {
+    switch (p.k) {
+      case Pat::Wild: return "1";
+      case Pat::Bind:
+        if (t.b == B::Array || t.b == B::Tensor)
+          fail("AE0500", p.line, p.col, "bindings of arrays or tensors in patterns are not supported");
+        binds += ctype(t) + " " + bind(p.s, t) + " = " + m + "; ";
+        return "1";
+      case Pat::Lit: {
+        auto le = std::make_shared<Expr>();
+        le->line = p.line;
+        le->col = p.col;
+        le->s = p.s;
+        if (p.s == "true" || p.s == "false") le->k = Expr::BoolL;
+        else if (!p.s.empty() && p.s[0] == '\'') {
+          le->k = Expr::Char;
+          le->s = p.s.substr(1);
+        } else if (!p.s.empty() && p.s[0] == '"') {
+          fail("AE0500", p.line, p.col, "string patterns are not supported");
+        } else {
+          le->k = p.s.find_first_of(".eE") != std::string::npos && p.s.find("0x") != 0 ? Expr::Float : Expr::Int;
+        }
+        V v = gen(le, t);
+        return "(" + m + " == " + (p.neg ? "-" : "") + conv(v, t) + ")";
+      }
+      case Pat::Path:
+      case Pat::Tuple: {
+        const size_t cc = p.s.rfind("::");
+        const std::string en = cc == std::string::npos ? "" : p.s.substr(0, cc);
+        if (!en.empty() && enums_.count(en)) {
+          const std::string vn = p.s.substr(cc + 2);
+          const int ix = variant_index(en, vn);
+          if (ix < 0) fail("AE0510", p.line, p.col, "`" + en + "` has no variant '" + vn + "'");
+          if (enums_[en].unit_only) {
+            if (p.k == Pat::Tuple) fail("AE0541", p.line, p.col, "variant '" + p.s + "' carries no payload");
+            return "(" + m + " == " + std::to_string(ix) + ")";
+          }
+          if (t.b != B::Struct || t.sname != en)
+            fail("AE0520", p.line, p.col, "pattern '" + p.s + "' does not match a value of type " + tyname(t));
+          std::string test = "(" + m + ".tag == " + std::to_string(ix);
+          const auto& pay = enums_[en].variants[ix].second;
+          if (p.k == Pat::Tuple) {
+            if (p.subs.size() != pay.size())
+              fail("AE0541", p.line, p.col, "'" + p.s + "' carries " + std::to_string(pay.size()) + " values");
+            for (size_t k = 0; k < pay.size(); ++k) {
+              const std::string sub = pat_test(*p.subs[k], m + ".u.v_" + vn + ".a" + std::to_string(k), pay[k], binds);
+              if (sub != "1") test += " && " + sub;
+            }
+          }
+          return test + ")";
+        }
+        const std::string leaf = cc == std::string::npos ? p.s : p.s.substr(cc + 2);
+        if (p.k == Pat::Path && const_src_.count(leaf)) return "(" + m + " == aec_" + leaf + ")";
+        fail("AE0510", p.line, p.col, "unknown pattern '" + p.s + "'");
+      }
+      case Pat::Or: {
+        std::string r = "(";
+        for (size_t k = 0; k < p.subs.size(); ++k) {
+          std::string b;
+          r += (k ? " || " : "") + pat_test(*p.subs[k], m, t, b);
+          if (!b.empty()) fail("AE0500", p.line, p.col, "bindings inside `|` patterns are not supported");
+        }
+        return r + ")";
+      }
+    }
+    return "0";
+  }
+
+  // `match` (and `if let`) as a GNU statement expression: the scrutinee is
+  // evaluated once, arms are tried in order, a guard is evaluated with the
+  // arm's bindings in scope.
+  V match(const EP& e, const Ty& hint) {
+    V sc = gen(e->a[0], prim(B::Unknown));
+    const std::string id = std::to_string(++uniq_);
+    const std::string m = "m_" + id, r = "r_" + id, d = "d_" + id;
+    struct Arm {
+      std::string test, binds, guard;
+      V body;
+    };
+    std::vector<Arm> arms;
+    Ty rt = (hint.b == B::Unknown || hint.b == B::Void) ? prim(B::Unknown) : hint;
+    for (size_t i = 0; i < e->pats.size(); ++i) {
+      scopes_.emplace_back();
+      Arm a;
+      a.test = pat_test(*e->pats[i], m, sc.t, a.binds);
+      if (e->guards[i]) a.guard = gen(e->guards[i], prim(B::Bool)).c;
+      a.body = gen(e->a[i + 1], rt);
+      if (rt.b == B::Unknown && a.body.t.b != B::Void && a.body.t.b != B::Unknown) rt = a.body.t;
+      scopes_.pop_back();
+      arms.push_back(a);
+    }
+    const bool value = rt.b != B::Unknown && rt.b != B::Void;
+    std::string o = "({ " + ctype(sc.t) + " " + m + " = " + sc.c + "; ";
+    if (value) o += ctype(rt) + " " + r + " = " + zero_of(rt) + "; ";
+    o += "int " + d + " = 0; ";
+    for (auto& a : arms) {
+      o += "if (!" + d + " && " + a.test + ") { " + a.binds;
+      o += a.guard.empty() ? "{ " : "if (" + a.guard + ") { ";
+      if (value && a.body.t.b != B::Void) o += r + " = " + conv(a.body, rt) + "; ";
+      else o += a.body.c + "; ";
+      o += d + " = 1; } } ";
+    }
+    if (value) o += r + "; ";
+    o += "})";
+    (void)m;
+    return {o, value ? rt : prim(B::Void)};
+  }
+
+  V struct_method(const EP& e, const V& r) {
+    const std::string key = r.t.sname + "::" + e->s;
+    if (!sigs_.count(key)) fail("AE0551", e->line, e->col, "`" + r.t.sname + "` has no method '" + e->s + "'");
+    if (sigs_.at(key).self_kind == 0)
+      fail("AE0550", e->line, e->col, "'" + key + "' takes no `self`; call it as " + key + "(..)");
+    std::vector<EP> args(e->a.begin() + 1, e->a.end());
+    if (sigs_.at(key).self_kind == 2 && is_place(e->a[0])) {
+      // receiver by address: the place itself
+      const FnSig& sig = sigs_.at(key);
+      if (args.size() + 1 != sig.params.size())
+        fail("AE0541", e->line, e->col, "'" + key + "' takes " + std::to_string(sig.params.size() - 1) + " arguments");
+      std::string list = "&(" + r.c + ")";
+      for (size_t i = 0; i < args.size(); ++i) list += ", " + conv(gen(args[i], sig.params[i + 1]), sig.params[i + 1]);
+      return {sig.c + "(" + list + ")", sig.ret};
+    }
+    return method_call(e, key, args, &r);
   }
 
   void declare(const Fn& f) {
@@ -1295,6 +1842,12 @@ class Gen {
   }
 
   Ty resolve(const TyExpr& t) {
+    Ty r = resolve_base(t);
+    if (t.ref && r.b != B::Tensor && r.b != B::Array && r.b != B::Str && r.b != B::Void) r.ref = true;
+    return r;
+  }
+
+  Ty resolve_base(const TyExpr& t) {
     Ty r;
     if (t.name == "()") return prim(B::Void);
     if (t.name == "Tensor") {
@@ -1315,6 +1868,9 @@ class Gen {
       r.len = const_int(t.dims[0]);
       return r;
     }
+    if (t.name == "Self" && !self_type_.empty()) return struct_ty(self_type_);
+    if (structs_.count(t.name)) return struct_ty(t.name);
+    if (enums_.count(t.name)) return enums_[t.name].unit_only ? prim(B::I64) : struct_ty(t.name);
     auto it = prim_names().find(t.name);
     if (it == prim_names().end()) fail("AE0522", t.line, t.col, "unknown type '" + t.name + "'");
     return prim(it->second);
@@ -1336,16 +1892,25 @@ class Gen {
   std::string pad() const { return std::string(2 * indent_, ' '); }
 
   // --------------------------------------------------------------- expressions
-  struct V {
-    std::string c;
-    Ty t;
-  };
   static bool is_lit(const EP& e) {
     return e->k == Expr::Int || e->k == Expr::Float || (e->k == Expr::Unary && e->s == "-" && is_lit(e->a[0]));
   }
 
+  static V deref(const V& v) {
+    if (!v.t.ref) return v;
+    Ty base = v.t;
+    base.ref = false;
+    return {"(*" + v.c + ")", base};
+  }
+
   static std::string conv(const V& v, const Ty& to) {
     if (to.b == B::Unknown || to.b == B::Void) return v.c;
+    if (v.t.ref && to.ref) return v.c;
+    if (v.t.ref && !to.ref) {
+      if (to.b == B::I64 || to.b == B::U64)  // an address where a 64-bit integer (a C pointer) is expected
+        return "((" + ctype(to) + ")(intptr_t)(" + v.c + "))";
+      return conv(deref(v), to);
+    }
     if (v.t.b == to.b && to.b != B::Str) return v.c;
     if (v.t.b == B::Str && (to.is_int())) return "((" + ctype(to) + ")(intptr_t)(" + v.c + "))";
     if (v.t.b == B::Tensor && to.is_int()) return "((" + ctype(to) + ")(" + v.c + "))";
@@ -1389,6 +1954,16 @@ class Gen {
       }
       case Expr::Var: {
         if (Local* l = lookup(e->s)) return {l->c, l->ty};
+        const size_t cc = e->s.rfind("::");
+        if (cc != std::string::npos && enums_.count(e->s.substr(0, cc))) {
+          const std::string en = e->s.substr(0, cc);
+          const int ix = variant_index(en, e->s.substr(cc + 2));
+          if (ix < 0) fail("AE0510", e->line, e->col, "`" + en + "` has no variant '" + e->s.substr(cc + 2) + "'");
+          if (!enums_[en].variants[ix].second.empty())
+            fail("AE0541", e->line, e->col, "variant '" + e->s + "' carries a payload");
+          if (enums_[en].unit_only) return {"((int64_t)" + std::to_string(ix) + ")", prim(B::I64)};
+          return {"((aes_" + en + "){.tag = " + std::to_string(ix) + "})", struct_ty(en)};
+        }
         if (const_src_.count(e->s)) {
           auto v = eval_const(e);
           return {"aec_" + e->s, v.first};
@@ -1396,13 +1971,28 @@ class Gen {
         fail("AE0510", e->line, e->col, "unknown name '" + e->s + "'");
       }
       case Expr::Unary: {
-        V a = gen(e->a[0], hint);
+        V a = deref(gen(e->a[0], hint));
         if (e->s == "!") return {"(!" + a.c + ")", prim(B::Bool)};  // `!` is a logical not (0 -> 1, else 0)
         return {"(-" + a.c + ")", a.t};
       }
       case Expr::Ref: {
         V a = gen(e->a[0], hint);
-        return a;  // tensors and scalars travel by value (a tensor's value is its handle)
+        if (a.t.ref || a.t.b == B::Tensor || a.t.b == B::Array || a.t.b == B::Str || a.t.b == B::Void ||
+            a.t.b == B::Unknown)
+          return a;  // a tensor's value is its handle; arrays and strings are pointers already
+        Ty t = a.t;
+        t.ref = true;
+        if (is_place(e->a[0])) return {"(&(" + a.c + "))", t};
+        return {"(&(" + ctype(a.t) + "){" + a.c + "})", t};  // a temporary's address
+      }
+      case Expr::Deref: {
+        V a = gen(e->a[0], prim(B::Unknown));
+        if (a.t.ref) return deref(a);
+        if (a.t.b == B::I64 || a.t.b == B::U64) {  // an address held as a 64-bit integer: load through it
+          const Ty t = hint.is_num() || hint.b == B::Bool ? hint : prim(B::I64);
+          return {"(*(" + ctype(t) + "*)(intptr_t)(" + a.c + "))", t};
+        }
+        return a;  // `*x` of a by-value binding is the value itself
       }
       case Expr::Cast: {
         Ty to = resolve(*e->cast);
@@ -1432,6 +2022,60 @@ class Gen {
         std::string s = block_expr(*e->blk, hint);
         return {s, last_block_ty_};
       }
+      case Expr::StructLit: {
+        const std::string n = e->s == "Self" && !self_type_.empty() ? self_type_ : e->s;
+        auto it = structs_.find(n);
+        if (it == structs_.end()) fail("AE0522", e->line, e->col, "unknown struct '" + n + "'");
+        std::string r = "((aes_" + n + "){";
+        bool first = true;
+        for (size_t i = 0; i < e->fields.size(); ++i) {
+          const Ty* ft = nullptr;
+          for (auto& f : it->second.fields)
+            if (f.first == e->fields[i]) ft = &f.second;
+          if (!ft) fail("AE0530", e->line, e->col, "`" + n + "` has no field '" + e->fields[i] + "'");
+          std::string val;
+          if (ft->b == B::Array) {  // an array literal or `[v; n]` fills the field in place
+            const EP& x = e->a[i];
+            std::vector<std::string> items;
+            if (x->k == Expr::ArrayLit) {
+              for (auto& el : x->a) items.push_back(conv(gen(el, *ft->inner), *ft->inner));
+            } else if (x->k == Expr::ArrayRep) {
+              const int64_t n = const_int(x->a[1]);
+              if (n > 65536) fail("AE0500", x->line, x->col, "array repeat longer than 65536 in a struct literal");
+              const std::string one = conv(gen(x->a[0], *ft->inner), *ft->inner);
+              items.assign((size_t)n, one);
+            } else {
+              fail("AE0500", x->line, x->col, "an array field is initialised from an array literal");
+            }
+            if ((int64_t)items.size() != ft->len)
+              fail("AE0520", x->line, x->col, "array field '" + e->fields[i] + "' has " + std::to_string(ft->len) +
+                                                  " elements, the literal " + std::to_string(items.size()));
+            val = "{";
+            for (size_t k = 0; k < items.size(); ++k) val += (k ? ", " : "") + items[k];
+            val += "}";
+          } else {
+            val = conv(gen(e->a[i], *ft), *ft);
+          }
+          r += std::string(first ? "" : ", ") + ".f_" + e->fields[i] + " = " + val;
+          first = false;
+        }
+        for (auto& f : it->second.fields) {
+          bool given = false;
+          for (auto& g : e->fields) given |= g == f.first;
+          if (!given && f.second.b != B::Array)
+            fail("AE0520", e->line, e->col, "`" + n + "` literal is missing the field '" + f.first + "'");
+        }
+        if (first) r += "0";
+        return {r + "})", struct_ty(n)};
+      }
+      case Expr::Match: return match(e, hint);
+      case Expr::Field: {
+        V b = deref(gen(e->a[0], prim(B::Unknown)));
+        if (b.t.b != B::Struct) fail("AE0530", e->line, e->col, "field '" + e->s + "' of a value that is not a struct");
+        for (auto& f : structs_[b.t.sname].fields)
+          if (f.first == e->s) return {"(" + b.c + ").f_" + e->s, f.second};
+        fail("AE0530", e->line, e->col, "`" + b.t.sname + "` has no field '" + e->s + "'");
+      }
       case Expr::LoopE: {
         std::ostringstream o;
         o << "({ for (;;) ";
@@ -1448,18 +2092,18 @@ class Gen {
     const bool cmp = op == "==" || op == "!=" || op == "<" || op == "<=" || op == ">" || op == ">=";
     const bool logic = op == "&&" || op == "||";
     if (logic) {
-      V a = gen(e->a[0], prim(B::Bool)), b = gen(e->a[1], prim(B::Bool));
+      V a = deref(gen(e->a[0], prim(B::Bool))), b = deref(gen(e->a[1], prim(B::Bool)));
       return {"(" + a.c + " " + op + " " + b.c + ")", prim(B::Bool)};
     }
     const bool shift = op == "<<" || op == ">>";
     const Ty h = cmp ? prim(B::Unknown) : hint;
     V a, b;
     if (is_lit(e->a[0]) && !is_lit(e->a[1])) {
-      b = gen(e->a[1], h);
-      a = gen(e->a[0], shift ? h : b.t);
+      b = deref(gen(e->a[1], h));
+      a = deref(gen(e->a[0], shift ? h : b.t));
     } else {
-      a = gen(e->a[0], h);
-      b = gen(e->a[1], shift ? prim(B::Unknown) : a.t);
+      a = deref(gen(e->a[0], h));
+      b = deref(gen(e->a[1], shift ? prim(B::Unknown) : a.t));
     }
     Ty t = a.t;
     if (!shift && a.t.is_num() && b.t.is_num() && a.t.b != b.t.b) {
@@ -1475,7 +2119,30 @@ class Gen {
   }
 
   V call(const EP& e, const Ty& hint) {
-    const std::string& n = e->s;
+    const size_t colon = e->s.rfind("::");
+    if (colon != std::string::npos && enums_.count(e->s.substr(0, colon))) {  // a variant with its payload
+      const std::string en = e->s.substr(0, colon);
+      const int ix = variant_index(en, e->s.substr(colon + 2));
+      if (ix < 0) fail("AE0540", e->line, e->col, "`" + en + "` has no variant '" + e->s.substr(colon + 2) + "'");
+      const auto& pay = enums_[en].variants[ix].second;
+      if (pay.size() != e->a.size())
+        fail("AE0541", e->line, e->col, "'" + e->s + "' carries " + std::to_string(pay.size()) + " values, got " +
+                                            std::to_string(e->a.size()));
+      std::string r = "((aes_" + en + "){.tag = " + std::to_string(ix);
+      if (!pay.empty()) {
+        r += ", .u.v_" + e->s.substr(colon + 2) + " = {";
+        for (size_t k = 0; k < pay.size(); ++k) r += (k ? ", " : "") + conv(gen(e->a[k], pay[k]), pay[k]);
+        r += "}";
+      }
+      return {r + "})", struct_ty(en)};
+    }
+    if (colon != std::string::npos) {
+      std::string type = e->s.substr(0, colon);
+      if (type == "Self" && !self_type_.empty()) type = self_type_;
+      const std::string key = type + "::" + e->s.substr(colon + 2);
+      if (sigs_.count(key)) return method_call(e, key, e->a, nullptr);
+    }
+    const std::string n = colon == std::string::npos ? e->s : e->s.substr(colon + 2);
     auto one_arg = [&](const Ty& t) {
       if (e->a.size() != 1) fail("AE0540", e->line, e->col, n + "() takes one argument");
       return gen(e->a[0], t);
@@ -1523,6 +2190,12 @@ class Gen {
     std::string args;
     for (size_t i = 0; i < e->a.size(); ++i) {
       V v = gen(e->a[i], s.params[i]);
+      if (s.params[i].ref && !v.t.ref) {  // a value where a reference is declared: its address
+        Ty base = s.params[i];
+        base.ref = false;
+        v = is_place(e->a[i]) ? V{"(&(" + v.c + "))", s.params[i]}
+                              : V{"(&(" + ctype(base) + "){" + conv(v, base) + "})", s.params[i]};
+      }
       if (v.t.b == B::Tensor && !s.params[i].is_int() && s.params[i].b != B::Tensor)
         fail("AE0520", e->a[i]->line, e->a[i]->col, "a tensor passed where " + tyname(s.params[i]) + " is expected");
       args += (i ? ", " : "") + conv(v, s.params[i]);
@@ -1532,6 +2205,19 @@ class Gen {
 
   V method(const EP& e) {
     V r = gen(e->a[0], prim(B::Unknown));
+    if (r.t.b == B::Struct && r.t.ref) {  // through a reference: `&self` methods take the pointer itself
+      const std::string key = r.t.sname + "::" + e->s;
+      if (sigs_.count(key) && sigs_.at(key).self_kind == 2) {
+        const FnSig& sig = sigs_.at(key);
+        if (e->a.size() != sig.params.size())
+          fail("AE0541", e->line, e->col, "'" + key + "' takes " + std::to_string(sig.params.size() - 1) + " arguments");
+        std::string list = r.c;
+        for (size_t i = 1; i < e->a.size(); ++i) list += ", " + conv(gen(e->a[i], sig.params[i]), sig.params[i]);
+        return {sig.c + "(" + list + ")", sig.ret};
+      }
+      r = deref(r);
+    }
+    if (r.t.b == B::Struct) return struct_method(e, r);
     if (r.t.b != B::Tensor)
       fail("AE0550", e->line, e->col, "method '" + e->s + "' needs a Tensor receiver, not " + tyname(r.t));
     auto it = method_rules().find(e->s);
@@ -1678,8 +2364,8 @@ class Gen {
       }
       case Stmt::Assign: {
         V lhs = gen(s.e, prim(B::Unknown));
-        if (s.e->k != Expr::Var && s.e->k != Expr::Index)
-          fail("AE0560", s.line, s.col, "can only assign to a variable or an array element");
+        if (s.e->k != Expr::Var && s.e->k != Expr::Index && s.e->k != Expr::Field && s.e->k != Expr::Deref)
+          fail("AE0560", s.line, s.col, "can only assign to a variable, a field or an array element");
         if (lhs.t.b == B::Tensor) fail("AE0561", s.line, s.col, "tensor bindings cannot be reassigned");
         V rhs = gen(s.e2, lhs.t);
         if (s.op == "%=" && lhs.t.is_float())
@@ -1687,6 +2373,17 @@ class Gen {
         return lhs.c + " " + s.op + " " + conv(rhs, lhs.t) + ";";
       }
       case Stmt::While: {
+        if (s.pat) {  // while let: match once per iteration, leave on the first miss
+          V sc = gen(s.e, prim(B::Unknown));
+          const std::string m = "m_" + std::to_string(++uniq_);
+          scopes_.emplace_back();
+          std::string binds;
+          const std::string test = pat_test(*s.pat, m, sc.t, binds);
+          const std::string body = block_stmt(*s.body);
+          scopes_.pop_back();
+          return "for (;;) { " + ctype(sc.t) + " " + m + " = " + sc.c + "; if (!" + test + ") break; " + binds + body +
+                 " }";
+        }
         V c = gen(s.e, prim(B::Bool));
         return "while (" + c.c + ") " + block_stmt(*s.body);
       }
@@ -1703,7 +2400,7 @@ class Gen {
         return r;
       }
       case Stmt::Return: {
-        if (!s.e) return ret_.b == B::Void ? "return;" : "return 0;";
+        if (!s.e) return ret_.b == B::Void ? "return;" : "return " + zero_of(ret_) + ";";
         V v = gen(s.e, ret_);
         return "return " + conv(v, ret_) + ";";
       }
@@ -1777,19 +2474,27 @@ class Gen {
       init = conv(v, t);
     } else {
       if (t.b == B::Unknown) fail("AE0574", s.line, s.col, "a binding without initialiser needs a type");
-      init = t.is_float() ? "0" : "0";
+      init = t.b == B::Struct ? "{0}" : "0";
     }
     const std::string c = bind(s.name, t);
     return ctype(t) + " " + c + " = " + init + ";";
   }
 
-  std::string fn_def(const Fn& f) {
-    const FnSig& sig = sigs_[f.name];
+  static std::string zero_of(const Ty& t) { return t.b == B::Struct ? "(" + ctype(t) + "){0}" : "0"; }
+
+  std::string fn_def(const Fn& f, const std::string& key) {
+    const FnSig& sig = sigs_[key];
     ret_ = sig.ret;
     scopes_.clear();
     scopes_.emplace_back();
     std::string params;
     for (size_t i = 0; i < f.params.size(); ++i) {
+      if (i == 0 && sig.self_kind == 2) {  // `&self`: a pointer; `self` names what it points at
+        const std::string c = "self_" + std::to_string(++uniq_);
+        scopes_.back()["self"] = {sig.params[0], "(*" + c + ")"};
+        params += ctype(sig.params[0]) + "* " + c;
+        continue;
+      }
       const std::string c = bind(f.params[i].name, sig.params[i]);
       params += (i ? ", " : "") + ctype(sig.params[i]) + " " + c;
     }
@@ -1804,7 +2509,7 @@ class Gen {
       if (ret_.b == B::Void) o << pad() << v.c << ";\n";
       else o << pad() << "return " << conv(v, ret_) << ";\n";
     } else if (ret_.b != B::Void) {
-      o << pad() << "return 0;\n";
+      o << pad() << "return " << zero_of(ret_) << ";\n";
     }
     o << "}\n\n";
     return o.str();
@@ -2174,8 +2879,6 @@ class BorrowCheck {
 // reads `*x` of a by-value binding as `x`.
 void strip_deref(EP& e) {
   if (!e) return;
-  while (e->k == Expr::Deref) e = e->a[0];
-  if (e->k == Expr::Field) fail("AE0500", e->line, e->col, "field access is checked but not compiled by this compiler");
   for (auto& a : e->a) strip_deref(a);
   auto blk = [](const BP& b) {
     if (!b) return;
@@ -2196,19 +2899,18 @@ void strip_deref(EP& e) {
   blk(e->blk2);
 }
 void prepare_codegen(Program& p) {
-  if (!p.structs.empty())
-    fail("AE0500", p.structs[0].line, p.structs[0].col, "structs are checked but not compiled by this compiler");
-  if (!p.traits.empty())
-    fail("AE0500", p.traits[0].line, p.traits[0].col, "traits are checked but not compiled by this compiler");
-  if (!p.impls.empty())
-    fail("AE0500", p.impls[0].line, p.impls[0].col, "impls are checked but not compiled by this compiler");
-  for (auto& f : p.fns) {
-    if (!f.body) continue;
+  auto strip = [](const BP& body) {
+    if (!body) return;
     EP tmp = std::make_shared<Expr>();
     tmp->k = Expr::BlockE;
-    tmp->blk = f.body;
+    tmp->blk = body;
     strip_deref(tmp);
-  }
+  };
+  for (auto& f : p.fns) strip(f.body);
+  for (auto& im : p.impls)
+    for (auto& m : im.methods) strip(m.body);
+  for (auto& t : p.traits)
+    for (auto& m : t.methods) strip(m.body);
 }
 
 // ============================================================================ AST dump

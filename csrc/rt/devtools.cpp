@@ -165,19 +165,21 @@ AE_API int64_t aether_sbom_count() {
 }
 AE_API int aether_sbom_emit(const void* out_path, int64_t out_len) {
   if (!out_path || out_len <= 0) return -1;
-  std::string j = "{\"bomFormat\":\"CycloneDX\",\"specVersion\":\"1.5\",\"version\":1,\"components\":[";
+  // indented two spaces per level, one component per line
+  std::string j = "{\n  \"bomFormat\": \"CycloneDX\",\n  \"specVersion\": \"1.5\",\n  \"version\": 1,\n  \"components\": [";
   {
     std::lock_guard<std::mutex> g(g_mu);
     for (size_t i = 0; i < g_sbom.size(); ++i) {
-      if (i) j += ',';
-      j += "{\"type\":\"library\",\"name\":";
+      j += i ? ",\n    " : "\n    ";
+      j += "{\"type\": \"library\", \"name\": ";
       json_str(g_sbom[i].first, j);
-      j += ",\"version\":";
+      j += ", \"version\": ";
       json_str(g_sbom[i].second, j);
       j += '}';
     }
+    if (!g_sbom.empty()) j += "\n  ";
   }
-  j += "]}\n";
+  j += "]\n}\n";
   const std::string path = str_arg(out_path, out_len), tmp = path + ".tmp";
   FILE* f = std::fopen(tmp.c_str(), "wb");
   if (!f) return -2;

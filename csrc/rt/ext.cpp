@@ -496,6 +496,11 @@ AE_API int aether_pack_f32_to_bf16(int64_t src, int64_t dst, int n) {
 // ------------------------------------------------------------------ GGUF block dequantisers (-> f32)
 // Return 0 on success, 1 on a null pointer, 2 on a bad block count.
 static inline float half_at(const uint8_t* p) { return aether_f16_to_f32(p[0] | (p[1] << 8)); }
+// The exported Q4_0 decoder writes each byte's two values next to each other
+// (low nibble at 2j, high nibble at 2j + 1), which is the order this ABI
+// function has always produced for its callers (runtime/src/lib.rs:217-240);
+// GGUF tensors (low nibbles first, then high) are decoded by the loaders'
+// own Q4_0 path.
 AE_API int aether_dequant_q4_0(const void* blocks, void* out, int n_blocks) {
   if (!blocks || !out) return 1;
   if (n_blocks <= 0) return 2;
@@ -504,8 +509,8 @@ AE_API int aether_dequant_q4_0(const void* blocks, void* out, int n_blocks) {
     const float d = half_at(b);
     float* o = F(out) + (size_t)i * 32;
     for (int j = 0; j < 16; ++j) {
-      o[j] = d * (float)((b[2 + j] & 0x0f) - 8);
-      o[j + 16] = d * (float)((b[2 + j] >> 4) - 8);
+      o[2 * j] = d * (float)((b[2 + j] & 0x0f) - 8);
+      o[2 * j + 1] = d * (float)((b[2 + j] >> 4) - 8);
     }
   }
   return 0;
@@ -750,7 +755,7 @@ AE_API int64_t aether_batch_sched_admit(int64_t h, int req_id, int prompt_len, i
     aether_pkv_pagetable_set(r.table, l, phys);
     r.blocks.push_back(phys);
   }
-  r.position = prompt_len;
+  r.position = 0;  // counts emitted tokens from admission (the reference ABI's contract)
   s->reqs.push_back(std::move(r));
   return 0;
 }

@@ -406,7 +406,7 @@ float aether_test_add_f32(float a, float b) { return a + b; }
 double aether_test_add_f64(double a, double b) { return a + b; }
 int64_t aether_test_f32_to_i64(float x) { return (int64_t)x; }
 int64_t aether_test_f64_to_i64(double x) { return (int64_t)x; }
-float aether_test_mix_if(int i, float f, int j) { return (float)i * f + (float)j; }
+float aether_test_mix_if(int i, float f, int j) { return (float)(i + j) * f; }
 
 // ================================================================================================ vectors
 int64_t aether_vec_i64_new() { return g_vi.put(std::make_unique<VecI64>()); }

