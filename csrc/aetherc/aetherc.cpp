@@ -1954,6 +1954,10 @@ class Gen {
       }
       case Expr::Var: {
         if (Local* l = lookup(e->s)) return {l->c, l->ty};
+        if (sigs_.count(e->s) && e->s.find("::") == std::string::npos) {  // a function as a value: its address
+          fn_values_[e->s] = true;
+          return {"((int64_t)(intptr_t)&" + sigs_[e->s].c + ")", prim(B::I64)};
+        }
         const size_t cc = e->s.rfind("::");
         if (cc != std::string::npos && enums_.count(e->s.substr(0, cc))) {
           const std::string en = e->s.substr(0, cc);
@@ -2001,7 +2005,11 @@ class Gen {
       }
       case Expr::Binary: return binary(e, hint);
       case Expr::Call: return call(e, hint);
-      case Expr::Method: return method(e);
+      case Expr::Method:
+        if (e->s == "into" && e->a.size() == 1 && hint.b == B::Struct && !hint.ref &&
+            sigs_.count(hint.sname + "::from"))  // `v.into()` where a struct is expected: Type::from(v)
+          return method_call(e, hint.sname + "::from", {e->a[0]}, nullptr);
+        return method(e);
       case Expr::Index: {
         V arr = gen(e->a[0], prim(B::Unknown));
         if (arr.t.b != B::Array) fail("AE0530", e->line, e->col, "only arrays can be indexed");
@@ -2143,6 +2151,24 @@ class Gen {
       if (sigs_.count(key)) return method_call(e, key, e->a, nullptr);
     }
     const std::string n = colon == std::string::npos ? e->s : e->s.substr(colon + 2);
+    const size_t us = n.find("__");
+    if (us != std::string::npos && us > 0 && !sigs_.count(n)) {  // a flattened `Type__method` name
+      const std::string key = n.substr(0, us) + "::" + n.substr(us + 2);
+      if (sigs_.count(key)) return method_call(e, key, e->a, nullptr);
+    }
+    if (Local* fp = lookup(n)) {  // a local or parameter holding a function's address: an indirect call
+      if (!fp->ty.is_int()) fail("AE0540", e->line, e->col, "'" + n + "' is not a function");
+      std::vector<V> args;
+      std::string types, list;
+      for (size_t i = 0; i < e->a.size(); ++i) {
+        V v = deref(gen(e->a[i], prim(B::Unknown)));
+        types += (i ? ", " : "") + ctype(v.t);
+        list += (i ? ", " : "") + v.c;
+      }
+      const Ty rt = hint.is_num() ? hint : prim(B::I64);
+      return {"((" + ctype(rt) + " (*)(" + (types.empty() ? "void" : types) + "))(intptr_t)(" + fp->c + "))(" + list + ")",
+              rt};
+    }
     auto one_arg = [&](const Ty& t) {
       if (e->a.size() != 1) fail("AE0540", e->line, e->col, n + "() takes one argument");
       return gen(e->a[0], t);
@@ -2316,6 +2342,7 @@ class Gen {
   }
 
   std::set<std::string> used_undeclared_;
+  std::map<std::string, bool> fn_values_;  // functions whose address was taken
   Ty last_block_ty_;
 
   // A block as a GNU statement expression; its type lands in last_block_ty_.
@@ -2565,6 +2592,15 @@ void Gen::resolve_uses(Program& p, const std::string& stdlib, const std::string&
 // `let`-bound borrow lives from its `let` to the last statement that names
 // its binding; a borrow inside an expression lives for its statement.
 
+// Traits of the language's standard prelude: an impl of one needs no declaration here.
+bool prelude_trait(const std::string& n) {
+  static const std::set<std::string> names = {"From", "Into", "Clone", "Copy", "Debug", "Default", "Display",
+                                              "PartialEq", "Eq", "PartialOrd", "Ord", "Hash", "Send", "Sync",
+                                              "Drop", "Iterator", "Add", "Sub", "Mul", "Div", "Neg", "Deref",
+                                              "AsRef", "ToString"};
+  return names.count(n) != 0;
+}
+
 void check_traits(const Program& p) {
   std::map<std::string, const TraitDef*> traits;
   for (auto& t : p.traits) traits[t.name] = &t;
@@ -2574,6 +2610,7 @@ void check_traits(const Program& p) {
   for (auto& im : p.impls) {
     if (im.trait.empty()) continue;
     auto it = traits.find(im.trait);
+    if (it == traits.end() && prelude_trait(im.trait)) continue;
     if (it == traits.end())
       fail("AE0211", im.line, im.col, "`impl " + im.trait + " for " + im.type + "`: no trait `" + im.trait + "` is declared");
     std::set<std::string> have;
