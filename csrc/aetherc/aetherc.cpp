@@ -26,12 +26,17 @@
 // default bodies copied into each impl, `Type::f()`, `Self`), enums (no
 // payload: integers; with payloads: tagged structs), `match` with literal,
 // wildcard, binding, path and tuple-variant patterns, `|` and guards,
-// `if let` / `while let`, and references to scalars and structs as pointers
-// (an address passed where an i64 is declared is the address as an integer).
-// Generic items, closures and macros are diagnostics, not miscompiles.
+// `if let` / `while let`, references to scalars and structs as pointers
+// (an address passed where an i64 is declared is the address as an integer),
+// tuples and tuple structs, functions as values, and closures: one without
+// captures is a static function (its address an i64), one with captures a
+// heap object [function, captured values...] of type `Closure`, called with
+// the object as its first argument. Generic items and macros are
+// diagnostics, not miscompiles.
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cctype>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -320,11 +325,14 @@ struct TyExpr {  // a type as written; tensor dims / array lengths may name cons
   std::string name;              // primitive / "Tensor" / "[]" / "&str" / a struct name
   bool generic = false;          // written with generic arguments (Vec<T>, ...)
   bool ref = false;              // written `&T` / `&mut T`
+  std::vector<std::shared_ptr<TyExpr>> elems;  // a tuple type's element types
   std::string elem;              // tensor element
   std::vector<EP> dims;          // tensor dims or {array length}
   std::shared_ptr<TyExpr> inner; // array element
   int line = 0, col = 0;
 };
+
+struct Fn;
 
 // A `match` / `if let` / `while let` pattern.
 struct Pat {
@@ -338,12 +346,13 @@ using PP = std::shared_ptr<Pat>;
 
 struct Expr {
   enum K { Int, Float, BoolL, Str, Char, Var, Unary, Binary, Call, Method, Cast, Ref, If, BlockE, Index, ArrayLit,
-           ArrayRep, LoopE, Field, Deref, StructLit, Match } k;
+           ArrayRep, LoopE, Field, Deref, StructLit, Match, TupleLit, Closure } k;
   std::string s;  // literal / name / operator / method / struct
   std::vector<EP> a;
   std::vector<std::string> fields;  // struct literal: the field each of `a` initialises
   std::vector<PP> pats;             // match: one pattern per arm (a[0] the scrutinee, a[i + 1] arm i)
   std::vector<EP> guards;           // match: the arm's `if` guard or null
+  std::shared_ptr<Fn> closure;      // closure: parameters, optional return type, body (its tail)
   BP blk, blk2;   // if: then / else block (else may be an `if` wrapped in a block)
   std::shared_ptr<TyExpr> cast;
   bool mut = false;
@@ -359,6 +368,7 @@ struct Block {
 struct Stmt {
   enum K { Let, ExprS, Assign, While, Loop, For, Return, Break, Continue } k;
   PP pat;  // `while let pat = e`
+  std::vector<std::string> names;  // `let (a, b, _) = e`
   std::string name, op;
   bool mut = false, inclusive = false;
   std::shared_ptr<TyExpr> ty;
@@ -767,8 +777,17 @@ class Parser {
       return t;
     }
     if (eat_op("(")) {
+      if (eat_op(")")) {
+        t->name = "()";
+        return t;
+      }
+      t->name = "tuple";
+      while (!is_op(")")) {
+        t->elems.push_back(type());
+        if (!eat_op(",")) break;
+      }
       expect_op(")");
-      t->name = "()";
+      if (t->elems.size() == 1) return t->elems[0];  // `(T)` is T
       return t;
     }
     t->name = ident();
@@ -872,6 +891,19 @@ class Parser {
     if (eat_id("let")) {
       s->k = Stmt::Let;
       s->mut = eat_id("mut");
+      if (eat_op("(")) {  // let (a, b, _) = e
+        while (!is_op(")")) {
+          eat_id("mut");
+          s->names.push_back(ident());
+          if (!eat_op(",")) break;
+        }
+        expect_op(")");
+        if (eat_op(":")) s->ty = type();
+        expect_op("=");
+        s->e = expr();
+        expect_op(";");
+        return s;
+      }
       s->name = ident();
       if (eat_op(":")) s->ty = type();
       if (eat_op("=")) s->e = expr();
@@ -1126,7 +1158,39 @@ class Parser {
         return e;
       }
       EP e = expr();
+      if (is_op(",")) {  // a tuple
+        EP t = mk(Expr::TupleLit, at);
+        t->a = {e};
+        while (eat_op(",")) {
+          if (is_op(")")) break;
+          t->a.push_back(expr());
+        }
+        expect_op(")");
+        return t;
+      }
       expect_op(")");
+      return e;
+    }
+    if (is_op("|") || is_op("||")) {  // a closure: |a: T, b| body  /  || body
+      EP e = mk(Expr::Closure, at);
+      e->closure = std::make_shared<Fn>();
+      e->closure->line = at.line;
+      e->closure->col = at.col;
+      if (eat_op("|")) {
+        while (!is_op("|")) {
+          Param prm;
+          prm.name = ident();
+          if (eat_op(":")) prm.ty = type();
+          e->closure->params.push_back(prm);
+          if (!eat_op(",")) break;
+        }
+        expect_op("|");
+      } else {
+        next();  // ||
+      }
+      if (eat_op("->")) e->closure->ret = type();
+      e->closure->body = std::make_shared<Block>();
+      e->closure->body->tail = expr();
       return e;
     }
     if (is_op("[")) {
@@ -1381,7 +1445,7 @@ class Gen {
     }
     self_type_.clear();
     std::ostringstream o;
-    o << "/* generated by aetherc */\n#include <stdint.h>\n#include <stdio.h>\n#include <math.h>\n\n";
+    o << "/* generated by aetherc */\n#include <stdint.h>\n#include <stdio.h>\n#include <stdlib.h>\n#include <math.h>\n\n";
     o << "int64_t aether_dev_alloc_f32(int32_t);\nint64_t aether_dev_alloc_i32(int32_t);\n"
          "int32_t aether_dev_free_f32(int64_t);\nint32_t aether_dev_free_i32(int64_t);\n";
     o << "static void ae_drop_f32(int64_t* h) { if (*h > 0) aether_dev_free_f32(*h); }\n"
@@ -1394,6 +1458,16 @@ class Gen {
       o << ctype(s.ret) << " " << s.c << "(" << plist(s) << ");\n";
     }
     o << "\n";
+    // Bodies first: they can add tuple types and lifted closures, whose
+    // declarations the file needs ahead of every body.
+    std::ostringstream defs;
+    for (auto& f : p_.fns)
+      if (!f.is_extern) defs << fn_def(f, f.name);
+    for (auto& im : p_.impls) {
+      self_type_ = im.type;
+      for (auto& m : im.methods) defs << fn_def(m, im.type + "::" + m.name);
+    }
+    self_type_.clear();
     o << struct_decls() << "\n";
     for (auto& c : p_.consts) {
       Ty t = resolve(*c.ty);
@@ -1406,14 +1480,7 @@ class Gen {
         const FnSig& sg = sigs_[im.type + "::" + m.name];
         o << "static " << ctype(sg.ret) << " " << sg.c << "(" << plist(sg) << ");\n";
       }
-    o << "\n";
-    for (auto& f : p_.fns)
-      if (!f.is_extern) o << fn_def(f, f.name);
-    for (auto& im : p_.impls) {
-      self_type_ = im.type;
-      for (auto& m : im.methods) o << fn_def(m, im.type + "::" + m.name);
-    }
-    self_type_.clear();
+    o << lifted_protos_ << "\n" << lifted_defs_ << defs.str();
     if (!sigs_.count("main") || sigs_["main"].is_extern) fail("AE0580", 1, 1, "program has no `fn main`");
     const FnSig& m = sigs_["main"];
     o << "int main(void) {\n";
@@ -1465,6 +1532,127 @@ class Gen {
     t.b = B::Struct;
     t.sname = n;
     return t;
+  }
+
+  // Tuples: one C struct per element-type list, fields f_0, f_1, ...
+  std::vector<std::string> tuple_names_;
+  Ty tuple_ty(const std::vector<Ty>& elems) {
+    std::string n = "T";
+    for (auto& t : elems) {
+      std::string c = ctype(t);
+      for (char& ch : c)
+        if (!std::isalnum((unsigned char)ch)) ch = '_';
+      n += "_" + c;
+    }
+    if (!structs_.count(n)) {
+      StructInfo& in = structs_[n];
+      for (size_t i = 0; i < elems.size(); ++i) in.fields.push_back({std::to_string(i), elems[i]});
+      tuple_names_.push_back(n);
+    }
+    return struct_ty(n);
+  }
+
+  // Closures without captures become static functions; the value is the
+  // function's address (as the reference passes function pointers: an i64).
+  std::string lifted_protos_, lifted_defs_;
+
+  // Names a closure body reads that are locals of the enclosing function.
+  void free_vars(const EP& e, const std::set<std::string>& params, std::vector<std::string>& out) {
+    if (!e) return;
+    if (e->k == Expr::Var && !params.count(e->s) && lookup(e->s) &&
+        std::find(out.begin(), out.end(), e->s) == out.end())
+      out.push_back(e->s);
+    if (e->k == Expr::Call && !params.count(e->s) && lookup(e->s) &&
+        std::find(out.begin(), out.end(), e->s) == out.end())
+      out.push_back(e->s);  // a captured closure called inside
+    for (auto& a : e->a) free_vars(a, params, out);
+    auto blk = [&](const BP& b) {
+      if (!b) return;
+      for (auto& st : b->stmts) {
+        free_vars(st->e, params, out);
+        free_vars(st->e2, params, out);
+        free_vars(st->e3, params, out);
+        if (st->body) {
+          auto tmp = std::make_shared<Expr>();
+          tmp->k = Expr::BlockE;
+          tmp->blk = st->body;
+          free_vars(tmp, params, out);
+        }
+      }
+      free_vars(b->tail, params, out);
+    };
+    blk(e->blk);
+    blk(e->blk2);
+  }
+
+  V lift_closure(const EP& e) {
+    const Fn& f = *e->closure;
+    std::set<std::string> pnames;
+    for (auto& prm : f.params) pnames.insert(prm.name);
+    std::vector<std::string> caps;
+    free_vars(f.body->tail, pnames, caps);
+    std::vector<Local> cap_locals;
+    for (auto& c : caps) cap_locals.push_back(*lookup(c));
+    auto saved_scopes = scopes_;
+    const Ty saved_ret = ret_;
+    const int saved_indent = indent_;
+    scopes_.assign(1, {});
+    const std::string name = "aecl_" + std::to_string(++uniq_);
+    const std::string env_t = name + "_env";
+    std::string params = caps.empty() ? "" : "int64_t env";
+    std::vector<Ty> pts;
+    for (size_t i = 0; i < caps.size(); ++i)  // captures: read from the environment object
+      scopes_.back()[caps[i]] = {cap_locals[i].ty, "(((" + env_t + "*)(intptr_t)env)->c_" + caps[i] + ")"};
+    for (auto& prm : f.params) {
+      const Ty t = prm.ty ? resolve(*prm.ty) : prim(B::I64);
+      pts.push_back(t);
+      params += (params.empty() ? "" : ", ") + ctype(t) + " " + bind(prm.name, t);
+    }
+    Ty rt = f.ret ? resolve(*f.ret) : prim(B::Unknown);
+    ret_ = rt;
+    indent_ = 1;
+    V body;
+    try {
+      body = gen(f.body->tail, rt);
+    } catch (const Diag& d) {
+      if (d.code == "AE0510")  // a name of the enclosing function: a capture
+        for (auto& sc : saved_scopes)
+          for (auto& kv : sc)
+            if (std::string(d.what()).find("'" + kv.first + "'") != std::string::npos)
+              fail("AE0500", e->line, e->col, "closures that capture `" + kv.first + "` are not compiled; pass it as a parameter");
+      throw;
+    }
+    if (rt.b == B::Unknown) rt = body.t;
+    const std::string sig = "static " + ctype(rt) + " " + name + "(" + (params.empty() ? "void" : params) + ")";
+    lifted_protos_ += sig + ";\n";
+    lifted_defs_ += sig + " {\n  " + (rt.b == B::Void ? body.c + ";\n" : "return " + conv(body, rt) + ";\n") + "}\n\n";
+    scopes_ = saved_scopes;
+    ret_ = saved_ret;
+    indent_ = saved_indent;
+    if (caps.empty()) {
+      // a plain function; where a `Closure` is expected, a static object
+      // [adapter] whose adapter drops the environment argument
+      std::string ap = "int64_t env", aa;
+      for (size_t i = 0; i < pts.size(); ++i) {
+        ap += ", " + ctype(pts[i]) + " p" + std::to_string(i);
+        aa += (i ? ", " : "") + std::string("p") + std::to_string(i);
+      }
+      lifted_protos_ += "static " + ctype(rt) + " " + name + "_adapt(" + ap + ") { (void)env; return " + name + "(" +
+                        aa + "); }\nstatic int64_t " + name + "_obj[1] = {(int64_t)(intptr_t)&" + name + "_adapt};\n";
+      Ty t = prim(B::I64);
+      t.sname = "fn:" + name;
+      return {"((int64_t)(intptr_t)&" + name + ")", t};
+    }
+    std::string decl = "typedef struct { int64_t fn;";
+    for (size_t i = 0; i < caps.size(); ++i) decl += " " + ctype(cap_locals[i].ty) + " c_" + caps[i] + ";";
+    lifted_protos_ = decl + " } " + env_t + ";\n" + lifted_protos_;
+    std::string make = "({ " + env_t + "* ep = (" + env_t + "*)malloc(sizeof(" + env_t + ")); ep->fn = (int64_t)(intptr_t)&" +
+                       name + ";";
+    for (size_t i = 0; i < caps.size(); ++i) make += " ep->c_" + caps[i] + " = " + cap_locals[i].c + ";";
+    make += " (int64_t)(intptr_t)ep; })";
+    Ty t = prim(B::I64);
+    t.sname = "Closure";
+    return {make, t};
   }
 
   // Trait methods with a default body that an impl does not override are
@@ -1565,6 +1753,7 @@ class Gen {
       order.push_back(n);
     };
     for (auto& d : p_.structs) visit(d.name);
+    for (auto& n : tuple_names_) visit(n);
     for (auto& d : p_.enums)
       if (!enums_[d.name].unit_only) visit(d.name);
     for (auto& n : order) o << "typedef struct aes_" << n << " aes_" << n << ";\n";
@@ -1850,6 +2039,11 @@ class Gen {
   Ty resolve_base(const TyExpr& t) {
     Ty r;
     if (t.name == "()") return prim(B::Void);
+    if (t.name == "tuple") {
+      std::vector<Ty> el;
+      for (auto& x : t.elems) el.push_back(resolve(*x));
+      return tuple_ty(el);
+    }
     if (t.name == "Tensor") {
       r.b = B::Tensor;
       if (t.elem == "f32") r.elem = B::F32;
@@ -1869,6 +2063,11 @@ class Gen {
       return r;
     }
     if (t.name == "Self" && !self_type_.empty()) return struct_ty(self_type_);
+    if (t.name == "Closure") {  // a closure object: the address of [function, captures...]
+      Ty c = prim(B::I64);
+      c.sname = "Closure";
+      return c;
+    }
     if (structs_.count(t.name)) return struct_ty(t.name);
     if (enums_.count(t.name)) return enums_[t.name].unit_only ? prim(B::I64) : struct_ty(t.name);
     auto it = prim_names().find(t.name);
@@ -1905,6 +2104,8 @@ class Gen {
 
   static std::string conv(const V& v, const Ty& to) {
     if (to.b == B::Unknown || to.b == B::Void) return v.c;
+    if (to.sname == "Closure" && v.t.sname.rfind("fn:", 0) == 0)  // a plain closure as a closure object
+      return "((int64_t)(intptr_t)" + v.t.sname.substr(3) + "_obj)";
     if (v.t.ref && to.ref) return v.c;
     if (v.t.ref && !to.ref) {
       if (to.b == B::I64 || to.b == B::U64)  // an address where a 64-bit integer (a C pointer) is expected
@@ -2077,6 +2278,23 @@ class Gen {
         return {r + "})", struct_ty(n)};
       }
       case Expr::Match: return match(e, hint);
+      case Expr::Closure: return lift_closure(e);
+      case Expr::TupleLit: {
+        std::vector<Ty> want;
+        if (hint.b == B::Struct && structs_.count(hint.sname) && !structs_[hint.sname].fields.empty() &&
+            structs_[hint.sname].fields[0].first == "0" && structs_[hint.sname].fields.size() == e->a.size())
+          for (auto& f : structs_[hint.sname].fields) want.push_back(f.second);
+        std::vector<V> vs;
+        std::vector<Ty> el;
+        for (size_t i = 0; i < e->a.size(); ++i) {
+          vs.push_back(gen(e->a[i], want.empty() ? prim(B::Unknown) : want[i]));
+          el.push_back(want.empty() ? vs.back().t : want[i]);
+        }
+        const Ty t = tuple_ty(el);
+        std::string r = "((" + ctype(t) + "){";
+        for (size_t i = 0; i < vs.size(); ++i) r += (i ? ", " : "") + conv(vs[i], el[i]);
+        return {r + "})", t};
+      }
       case Expr::Field: {
         V b = deref(gen(e->a[0], prim(B::Unknown)));
         if (b.t.b != B::Struct) fail("AE0530", e->line, e->col, "field '" + e->s + "' of a value that is not a struct");
@@ -2151,6 +2369,15 @@ class Gen {
       if (sigs_.count(key)) return method_call(e, key, e->a, nullptr);
     }
     const std::string n = colon == std::string::npos ? e->s : e->s.substr(colon + 2);
+    if (structs_.count(n) && !structs_[n].fields.empty() && structs_[n].fields[0].first == "0") {  // Name(a, b)
+      const auto& fs = structs_[n].fields;
+      if (fs.size() != e->a.size())
+        fail("AE0541", e->line, e->col, "'" + n + "' has " + std::to_string(fs.size()) + " fields, got " +
+                                            std::to_string(e->a.size()));
+      std::string r = "((aes_" + n + "){";
+      for (size_t i = 0; i < fs.size(); ++i) r += (i ? ", " : "") + conv(gen(e->a[i], fs[i].second), fs[i].second);
+      return {r + "})", struct_ty(n)};
+    }
     const size_t us = n.find("__");
     if (us != std::string::npos && us > 0 && !sigs_.count(n)) {  // a flattened `Type__method` name
       const std::string key = n.substr(0, us) + "::" + n.substr(us + 2);
@@ -2166,6 +2393,10 @@ class Gen {
         list += (i ? ", " : "") + v.c;
       }
       const Ty rt = hint.is_num() ? hint : prim(B::I64);
+      if (fp->ty.sname == "Closure")  // [function, captures...]: the object itself is the first argument
+        return {"((" + ctype(rt) + " (*)(int64_t" + (types.empty() ? "" : ", " + types) + "))(intptr_t)(((int64_t*)(intptr_t)(" +
+                    fp->c + "))[0]))(" + fp->c + (list.empty() ? "" : ", " + list) + ")",
+                rt};
       return {"((" + ctype(rt) + " (*)(" + (types.empty() ? "void" : types) + "))(intptr_t)(" + fp->c + "))(" + list + ")",
               rt};
     }
@@ -2438,6 +2669,21 @@ class Gen {
   }
 
   std::string let(const Stmt& s) {
+    if (!s.names.empty()) {  // let (a, b, _) = e: a temporary, then one binding per element
+      V v = gen(s.e, s.ty ? resolve(*s.ty) : prim(B::Unknown));
+      if (v.t.b != B::Struct || structs_[v.t.sname].fields.size() != s.names.size() ||
+          structs_[v.t.sname].fields[0].first != "0")
+        fail("AE0520", s.line, s.col, "destructuring needs a tuple of " + std::to_string(s.names.size()) + " elements");
+      const std::string tmp = "tup_" + std::to_string(++uniq_);
+      std::string r = ctype(v.t) + " " + tmp + " = " + v.c + ";";
+      const auto fs = structs_[v.t.sname].fields;
+      for (size_t i = 0; i < s.names.size(); ++i) {
+        if (s.names[i] == "_") continue;
+        const std::string c = bind(s.names[i], fs[i].second);
+        r += " " + ctype(fs[i].second) + " " + c + " = " + tmp + ".f_" + std::to_string(i) + ";";
+      }
+      return r;
+    }
     if (s.name == "_" && s.e && !s.ty) {  // `let _ = e;` evaluates e and drops the value
       V v = gen(s.e, prim(B::Unknown));
       return "(void)(" + v.c + ");";
