@@ -31,8 +31,12 @@
 // tuples and tuple structs, functions as values, and closures: one without
 // captures is a static function (its address an i64), one with captures a
 // heap object [function, captured values...] of type `Closure`, called with
-// the object as its first argument. Generic items and macros are
-// diagnostics, not miscompiles.
+// the object as its first argument. Generic functions, structs and impls are
+// specialised per use (`id__int64_t`, `Pair__float`): type parameters bind
+// from argument types, then from the expected type, and a generic impl's
+// methods are generated for each instance that calls them. Shape generics
+// (`Tensor<f32, [M, K]>` with M a parameter) and macros are diagnostics, not
+// miscompiles.
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -326,6 +330,7 @@ struct TyExpr {  // a type as written; tensor dims / array lengths may name cons
   bool generic = false;          // written with generic arguments (Vec<T>, ...)
   bool ref = false;              // written `&T` / `&mut T`
   std::vector<std::shared_ptr<TyExpr>> elems;  // a tuple type's element types
+  std::vector<std::shared_ptr<TyExpr>> targs;  // generic arguments: `W<i64>`
   std::string elem;              // tensor element
   std::vector<EP> dims;          // tensor dims or {array length}
   std::shared_ptr<TyExpr> inner; // array element
@@ -387,6 +392,7 @@ struct Fn {
   std::vector<Param> params;  // a method's receiver is the parameter `self` (no type)
   std::shared_ptr<TyExpr> ret;
   BP body;                    // null: extern, or a trait method without a default body
+  std::vector<std::string> generics;  // type parameters: specialised per use
   bool is_extern = false;
   int line = 0, col = 0;
 };
@@ -733,8 +739,10 @@ class Parser {
     return d;
   }
 
-  // `<T, [M, K], 3>` after a type name: types, shapes or constants, skipped.
-  void type_args() {
+  // `<T, [M, K], 3>` after a type name: the type arguments (shapes and
+  // constants are skipped).
+  std::vector<std::shared_ptr<TyExpr>> type_args() {
+    std::vector<std::shared_ptr<TyExpr>> out;
     expect_op("<");
     while (!is_op(">") && !is_op(">>") && !is_op(">=")) {
       if (is_op("[")) {
@@ -747,11 +755,12 @@ class Parser {
       } else if (at(T::Int)) {
         next();
       } else {
-        type();
+        out.push_back(type());
       }
       if (!eat_op(",")) break;
     }
     close_angle();
+    return out;
   }
 
   std::shared_ptr<TyExpr> type() {
@@ -807,7 +816,7 @@ class Parser {
       expect_op("]");
       close_angle();
     } else if (is_op("<")) {
-      type_args();
+      t->targs = type_args();
       t->generic = true;
     }
     return t;
@@ -826,7 +835,7 @@ class Parser {
     }
     if (!eat_id("fn")) fail("AE0002", cur().line, cur().col, "expected 'fn'");
     f.name = ident();
-    generic_params();
+    f.generics = generic_params();
     expect_op("(");
     while (!is_op(")")) {
       Param p;
@@ -1438,6 +1447,10 @@ class Gen {
     synthesize_defaults();
     for (auto& f : p_.fns) declare(f);
     for (auto& im : p_.impls) {
+      if (gstructs_.count(im.type)) {
+        gimpls_[im.type].push_back(&im);
+        continue;
+      }
       if (!structs_.count(im.type))
         fail("AE0500", im.line, im.col, "impl for '" + im.type + "', which is not a struct of this program");
       self_type_ = im.type;
@@ -1462,8 +1475,9 @@ class Gen {
     // declarations the file needs ahead of every body.
     std::ostringstream defs;
     for (auto& f : p_.fns)
-      if (!f.is_extern) defs << fn_def(f, f.name);
+      if (!f.is_extern && f.generics.empty()) defs << fn_def(f, f.name);
     for (auto& im : p_.impls) {
+      if (gstructs_.count(im.type)) continue;
       self_type_ = im.type;
       for (auto& m : im.methods) defs << fn_def(m, im.type + "::" + m.name);
     }
@@ -1474,8 +1488,10 @@ class Gen {
       o << "static const " << ctype(t) << " aec_" << c.name << " = " << lit_of(eval_const(c.e), t) << ";\n";
     }
     for (auto& f : p_.fns)
-      if (!f.is_extern) o << "static " << ctype(sigs_[f.name].ret) << " " << sigs_[f.name].c << "(" << plist(sigs_[f.name]) << ");\n";
+      if (!f.is_extern && f.generics.empty())
+        o << "static " << ctype(sigs_[f.name].ret) << " " << sigs_[f.name].c << "(" << plist(sigs_[f.name]) << ");\n";
     for (auto& im : p_.impls)
+      if (!gstructs_.count(im.type))
       for (auto& m : im.methods) {
         const FnSig& sg = sigs_[im.type + "::" + m.name];
         o << "static " << ctype(sg.ret) << " " << sg.c << "(" << plist(sg) << ");\n";
@@ -1532,6 +1548,118 @@ class Gen {
     t.b = B::Struct;
     t.sname = n;
     return t;
+  }
+
+  // Generics: functions, structs and impls are specialised per use;
+  // tsubst_ maps the type parameters of the item being specialised.
+  std::map<std::string, const Fn*> gfns_;
+  std::map<std::string, const StructDef*> gstructs_;
+  std::map<std::string, std::vector<const ImplDef*>> gimpls_;
+  std::map<std::string, std::pair<std::string, std::map<std::string, Ty>>> spec_of_;  // W__i64 -> (W, {T: i64})
+  std::map<std::string, Ty> tsubst_;
+
+  static std::string mangle(const Ty& t) {
+    std::string c = ctype(t);
+    if (c.rfind("aes_", 0) == 0) c = c.substr(4);
+    for (char& ch : c)
+      if (!std::isalnum((unsigned char)ch)) ch = '_';
+    return c;
+  }
+
+  Ty specialize_struct(const std::string& base, const std::vector<Ty>& args, int line, int col) {
+    const StructDef& d = *gstructs_.at(base);
+    if (args.size() != d.generics.size())
+      fail("AE0522", line, col, "`" + base + "` takes " + std::to_string(d.generics.size()) + " type arguments");
+    std::string name = base;
+    std::map<std::string, Ty> sub;
+    for (size_t i = 0; i < args.size(); ++i) {
+      name += "__" + mangle(args[i]);
+      sub[d.generics[i]] = args[i];
+    }
+    if (!structs_.count(name)) {
+      auto saved = tsubst_;
+      tsubst_ = sub;
+      StructInfo in;
+      for (auto& f : d.fields) in.fields.push_back({f.name, resolve(*f.ty)});
+      tsubst_ = saved;
+      structs_[name] = in;
+      tuple_names_.push_back(name);
+      spec_of_[name] = {base, sub};
+    }
+    return struct_ty(name);
+  }
+
+  // Declares and generates `method` of a specialised generic struct.
+  bool specialize_method(const std::string& sname, const std::string& method) {
+    auto sp = spec_of_.find(sname);
+    if (sp == spec_of_.end() || !gimpls_.count(sp->second.first)) return false;
+    for (const ImplDef* im : gimpls_[sp->second.first])
+      for (auto& m : im->methods) {
+        if (m.name != method) continue;
+        auto saved_sub = tsubst_;
+        auto saved_self = self_type_;
+        tsubst_ = sp->second.second;
+        self_type_ = sname;
+        declare_method(sname, m);
+        emit_lazy(m, sname + "::" + m.name);
+        tsubst_ = saved_sub;
+        self_type_ = saved_self;
+        return true;
+      }
+    return false;
+  }
+
+  // Generates a function body now, outside the one being generated.
+  void emit_lazy(const Fn& f, const std::string& key) {
+    auto saved_scopes = scopes_;
+    const Ty saved_ret = ret_;
+    const int saved_indent = indent_;
+    const FnSig& sg = sigs_[key];
+    lifted_protos_ += "static " + ctype(sg.ret) + " " + sg.c + "(" + plist(sg) + ");\n";
+    lifted_defs_ += fn_def(f, key);
+    scopes_ = saved_scopes;
+    ret_ = saved_ret;
+    indent_ = saved_indent;
+  }
+
+  // A call of generic function `n`: type parameters bound from the
+  // arguments' types (then from the expected type), specialised once.
+  V generic_call(const EP& e, const std::string& n, const Ty& hint) {
+    const Fn& f = *gfns_.at(n);
+    if (f.params.size() != e->a.size())
+      fail("AE0541", e->line, e->col, "'" + n + "' takes " + std::to_string(f.params.size()) + " arguments, got " +
+                                          std::to_string(e->a.size()));
+    std::vector<V> args;
+    std::map<std::string, Ty> sub;
+    const std::set<std::string> gs(f.generics.begin(), f.generics.end());
+    for (size_t i = 0; i < e->a.size(); ++i) {
+      args.push_back(gen(e->a[i], prim(B::Unknown)));
+      const auto& pt = f.params[i].ty;
+      if (pt && gs.count(pt->name) && !sub.count(pt->name)) {
+        Ty t = args.back().t;
+        t.ref = false;
+        sub[pt->name] = t;
+      }
+    }
+    for (auto& g : f.generics)
+      if (!sub.count(g)) sub[g] = (f.ret && f.ret->name == g && hint.b != B::Unknown && hint.b != B::Void) ? hint : prim(B::I64);
+    std::string key = n;
+    for (auto& g : f.generics) key += "__" + mangle(sub[g]);
+    if (!sigs_.count(key)) {
+      auto saved = tsubst_;
+      tsubst_ = sub;
+      FnSig s;
+      for (auto& prm : f.params) s.params.push_back(resolve(*prm.ty));
+      s.ret = f.ret ? resolve(*f.ret) : prim(B::Void);
+      s.c = "aef_" + key;
+      sigs_[key] = s;
+      emit_lazy(f, key);
+      tsubst_ = saved;
+    }
+    const FnSig& s = sigs_[key];
+    std::string list;
+    for (size_t i = 0; i < args.size(); ++i) list += (i ? ", " : "") + conv(args[i], s.params[i]);
+    return {s.c + "(" + list + ")", s.ret};
   }
 
   // Tuples: one C struct per element-type list, fields f_0, f_1, ...
@@ -1687,10 +1815,10 @@ class Gen {
 
   void declare_structs() {
     for (auto& d : p_.structs) {
-      if (!d.generics.empty())
-        fail("AE0500", d.line, d.col, "generic structs are checked but not compiled by this compiler");
-      if (structs_.count(d.name)) fail("AE0501", d.line, d.col, "struct '" + d.name + "' is defined twice");
-      structs_[d.name];
+      if (structs_.count(d.name) || gstructs_.count(d.name))
+        fail("AE0501", d.line, d.col, "struct '" + d.name + "' is defined twice");
+      if (!d.generics.empty()) gstructs_[d.name] = &d;
+      else structs_[d.name];
     }
     for (auto& d : p_.enums) {
       if (!d.generics.empty())
@@ -1701,7 +1829,8 @@ class Gen {
       for (auto& v : d.variants) in.unit_only &= v.second.empty();
     }
     for (auto& d : p_.structs)
-      for (auto& f : d.fields) structs_[d.name].fields.push_back({f.name, resolve(*f.ty)});
+      if (d.generics.empty())
+        for (auto& f : d.fields) structs_[d.name].fields.push_back({f.name, resolve(*f.ty)});
     for (auto& d : p_.enums)
       for (auto& v : d.variants) {
         std::vector<Ty> ts;
@@ -1752,8 +1881,9 @@ class Gen {
       done.insert(n);
       order.push_back(n);
     };
-    for (auto& d : p_.structs) visit(d.name);
-    for (auto& n : tuple_names_) visit(n);
+    for (auto& d : p_.structs)
+      if (d.generics.empty()) visit(d.name);
+    for (size_t i = 0; i < tuple_names_.size(); ++i) visit(tuple_names_[i]);
     for (auto& d : p_.enums)
       if (!enums_[d.name].unit_only) visit(d.name);
     for (auto& n : order) o << "typedef struct aes_" << n << " aes_" << n << ";\n";
@@ -1927,6 +2057,7 @@ class Gen {
 
   V struct_method(const EP& e, const V& r) {
     const std::string key = r.t.sname + "::" + e->s;
+    if (!sigs_.count(key)) specialize_method(r.t.sname, e->s);
     if (!sigs_.count(key)) fail("AE0551", e->line, e->col, "`" + r.t.sname + "` has no method '" + e->s + "'");
     if (sigs_.at(key).self_kind == 0)
       fail("AE0550", e->line, e->col, "'" + key + "' takes no `self`; call it as " + key + "(..)");
@@ -1944,6 +2075,12 @@ class Gen {
   }
 
   void declare(const Fn& f) {
+    if (!f.generics.empty()) {
+      if (gfns_.count(f.name) || sigs_.count(f.name))
+        fail("AE0501", f.line, f.col, "function '" + f.name + "' is defined twice");
+      gfns_[f.name] = &f;
+      return;
+    }
     FnSig s;
     for (auto& p : f.params) s.params.push_back(resolve(*p.ty));
     s.ret = f.ret ? resolve(*f.ret) : prim(B::Void);
@@ -2062,7 +2199,13 @@ class Gen {
       r.len = const_int(t.dims[0]);
       return r;
     }
+    if (tsubst_.count(t.name)) return tsubst_.at(t.name);
     if (t.name == "Self" && !self_type_.empty()) return struct_ty(self_type_);
+    if (gstructs_.count(t.name)) {
+      std::vector<Ty> args;
+      for (auto& a : t.targs) args.push_back(resolve(*a));
+      return specialize_struct(t.name, args, t.line, t.col);
+    }
     if (t.name == "Closure") {  // a closure object: the address of [function, captures...]
       Ty c = prim(B::I64);
       c.sname = "Closure";
@@ -2232,7 +2375,23 @@ class Gen {
         return {s, last_block_ty_};
       }
       case Expr::StructLit: {
-        const std::string n = e->s == "Self" && !self_type_.empty() ? self_type_ : e->s;
+        std::string n = e->s == "Self" && !self_type_.empty() ? self_type_ : e->s;
+        if (gstructs_.count(n)) {  // the expected type's instance, else one bound from the field values
+          if (hint.b == B::Struct && spec_of_.count(hint.sname) && spec_of_[hint.sname].first == n) {
+            n = hint.sname;
+          } else {
+            const StructDef& d = *gstructs_[n];
+            std::map<std::string, Ty> sub;
+            for (size_t i = 0; i < e->fields.size(); ++i)
+              for (auto& f : d.fields)
+                if (f.name == e->fields[i] && f.ty && std::count(d.generics.begin(), d.generics.end(), f.ty->name) &&
+                    !sub.count(f.ty->name))
+                  sub[f.ty->name] = gen(e->a[i], prim(B::Unknown)).t;
+            std::vector<Ty> args;
+            for (auto& g : d.generics) args.push_back(sub.count(g) ? sub[g] : prim(B::I64));
+            n = specialize_struct(n, args, e->line, e->col).sname;
+          }
+        }
         auto it = structs_.find(n);
         if (it == structs_.end()) fail("AE0522", e->line, e->col, "unknown struct '" + n + "'");
         std::string r = "((aes_" + n + "){";
@@ -2438,6 +2597,7 @@ class Gen {
       const std::string cn = n == "abs" ? "fabs" : n;
       return {(a.t.b == B::F32 ? cn + "f(" : cn + "(") + a.c + ")", a.t};
     }
+    if (gfns_.count(n)) return generic_call(e, n, hint);
     auto it = sigs_.find(n);
     if (it == sigs_.end()) fail("AE0540", e->line, e->col, "unknown function '" + n + "'");
     const FnSig& s = it->second;
