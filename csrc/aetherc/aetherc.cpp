@@ -207,6 +207,12 @@ std::vector<Tok> lex(const std::string& src) {
       adv(j + 1 - i);
       continue;
     }
+    if (c == '\'' && i + 1 < src.size() && (std::isalpha((unsigned char)src[i + 1]) || src[i + 1] == '_') &&
+        !(i + 2 < src.size() && src[i + 2] == '\'')) {  // a lifetime (`'a`): no meaning here, dropped
+      adv(1);
+      while (i < src.size() && (std::isalnum((unsigned char)src[i]) || src[i] == '_')) adv(1);
+      continue;
+    }
     if (c == '\'' && i + 2 < src.size() && (src[i + 2] == '\'' || (src[i + 1] == '\\' && i + 3 < src.size()))) {
       int v;
       size_t len;
@@ -462,6 +468,9 @@ class Parser {
         c.e = expr();
         expect_op(";");
         p.consts.push_back(c);
+      } else if (is_id("unsafe") && peek().t == T::Id && peek().s == "impl") {
+        next();
+        p.impls.push_back(impl_def());
       } else if (is_id("extern") || is_id("fn") || is_id("unsafe")) {
         p.fns.push_back(fn());
       } else if (is_op("#")) {
@@ -777,6 +786,12 @@ class Parser {
       in->ref = true;  // a pointer for scalars and structs; tensors (handles) and arrays travel as they are
       return in;
     }
+    if (eat_id("impl")) {  // `impl Trait (+ Trait)`: an anonymous type parameter of the function
+      ident();
+      while (eat_op("+")) ident();
+      t->name = "impl$" + std::to_string(++impl_params_);
+      return t;
+    }
     if (eat_op("[")) {
       t->name = "[]";
       t->inner = type();
@@ -858,6 +873,9 @@ class Parser {
     }
     expect_op(")");
     if (eat_op("->")) f.ret = type();
+    for (auto& prm : f.params)  // `impl Trait` parameters / result: type parameters of their own
+      if (prm.ty && prm.ty->name.rfind("impl$", 0) == 0) f.generics.push_back(prm.ty->name);
+    if (f.ret && f.ret->name.rfind("impl$", 0) == 0) f.generics.push_back(f.ret->name);
     if (f.is_extern || (trait_method && is_op(";"))) {
       expect_op(";");
     } else {
@@ -1026,6 +1044,7 @@ class Parser {
     return e;
   }
   bool no_struct_ = false;
+  int impl_params_ = 0;
 
   static int prec(const std::string& op) {
     if (op == "||") return 1;
@@ -2607,11 +2626,14 @@ class Gen {
     std::string args;
     for (size_t i = 0; i < e->a.size(); ++i) {
       V v = gen(e->a[i], s.params[i]);
-      if (s.params[i].ref && !v.t.ref) {  // a value where a reference is declared: its address
+      if (s.params[i].ref && !v.t.ref) {
         Ty base = s.params[i];
         base.ref = false;
-        v = is_place(e->a[i]) ? V{"(&(" + v.c + "))", s.params[i]}
-                              : V{"(&(" + ctype(base) + "){" + conv(v, base) + "})", s.params[i]};
+        if (v.t.b == B::I64 || v.t.b == B::U64)  // an address held as an integer: the pointer itself
+          v = V{"((" + ctype(s.params[i]) + ")(intptr_t)(" + v.c + "))", s.params[i]};
+        else  // a value where a reference is declared: its address
+          v = is_place(e->a[i]) ? V{"(&(" + v.c + "))", s.params[i]}
+                                : V{"(&(" + ctype(base) + "){" + conv(v, base) + "})", s.params[i]};
       }
       if (v.t.b == B::Tensor && !s.params[i].is_int() && s.params[i].b != B::Tensor)
         fail("AE0520", e->a[i]->line, e->a[i]->col, "a tensor passed where " + tyname(s.params[i]) + " is expected");
