@@ -34,8 +34,10 @@
 // the object as its first argument. Generic functions, structs and impls are
 // specialised per use (`id__int64_t`, `Pair__float`): type parameters bind
 // from argument types, then from the expected type, and a generic impl's
-// methods are generated for each instance that calls them. Shape generics
-// (`Tensor<f32, [M, K]>` with M a parameter) and macros are diagnostics, not
+// methods are generated for each instance that calls them. `macro_rules!`
+// macros expand at parse time (captures, one level of repetition, rules in
+// order) and `println!` / `print!` take `{}` holes. Shape generics
+// (`Tensor<f32, [M, K]>` with M a parameter) are diagnostics, not
 // miscompiles.
 #include <sys/stat.h>
 #include <unistd.h>
@@ -468,6 +470,8 @@ class Parser {
         c.e = expr();
         expect_op(";");
         p.consts.push_back(c);
+      } else if (is_id("macro_rules") && peek().t == T::Op && peek().s == "!") {
+        macro_def();
       } else if (is_id("unsafe") && peek().t == T::Id && peek().s == "impl") {
         next();
         p.impls.push_back(impl_def());
@@ -1046,6 +1050,276 @@ class Parser {
   bool no_struct_ = false;
   int impl_params_ = 0;
 
+  // ------------------------------------------------------------- macro_rules
+  // Declarative macros expanded at parse time: `$x:frag` captures (an expr
+  // fragment is substituted in parentheses), one level of `$( .. ) sep *`
+  // repetition, rules tried in order; the expansion is parsed as a block
+  // expression by a parser that shares this one's macro table.
+  struct MacroRule {
+    std::vector<Tok> matcher, body;
+  };
+  std::shared_ptr<std::map<std::string, std::vector<MacroRule>>> macros_ =
+      std::make_shared<std::map<std::string, std::vector<MacroRule>>>();
+
+  static bool opens(const Tok& t) { return t.t == T::Op && (t.s == "(" || t.s == "[" || t.s == "{"); }
+  static bool closes(const Tok& t) { return t.t == T::Op && (t.s == ")" || t.s == "]" || t.s == "}"); }
+
+  // The tokens between an opening delimiter here and its match (consumed).
+  std::vector<Tok> group() {
+    if (!opens(cur())) fail("AE0002", cur().line, cur().col, "expected '(', '[' or '{', found '" + cur().s + "'");
+    std::vector<Tok> out;
+    const Tok start = cur();
+    next();
+    int depth = 1;
+    while (true) {
+      if (at(T::Eof)) fail("AE0002", start.line, start.col, "unclosed macro group");
+      if (opens(cur())) ++depth;
+      if (closes(cur()) && --depth == 0) break;
+      out.push_back(cur());
+      next();
+    }
+    next();
+    return out;
+  }
+
+  void macro_def() {
+    next();  // macro_rules
+    next();  // !
+    const std::string name = ident();
+    std::vector<MacroRule> rules;
+    const bool paren = is_op("(");
+    if (!is_op("{") && !paren) fail("AE0002", cur().line, cur().col, "expected '{' after the macro name");
+    next();
+    while (!is_op("}") && !is_op(")")) {
+      if (at(T::Eof)) fail("AE0002", cur().line, cur().col, "unclosed macro_rules");
+      MacroRule r;
+      r.matcher = group();
+      expect_op("=>");
+      r.body = group();
+      rules.push_back(r);
+      if (!eat_op(";")) break;
+    }
+    next();
+    if (paren) eat_op(";");
+    (*macros_)[name] = rules;
+  }
+
+  using Caps = std::map<std::string, std::vector<std::vector<Tok>>>;
+
+  // Tokens of one fragment starting at in[i]: up to the next `follow`
+  // token at depth 0 (or the end); `ident` / `tt` take one token or group.
+  static size_t take_fragment(const std::vector<Tok>& in, size_t i, const std::string& frag, const Tok* follow) {
+    if (frag == "ident" || frag == "literal" || frag == "lifetime") return i < in.size() ? i + 1 : i;
+    if (frag == "tt") {
+      if (i >= in.size()) return i;
+      if (!opens(in[i])) return i + 1;
+      int d = 0;
+      for (size_t k = i; k < in.size(); ++k) {
+        if (opens(in[k])) ++d;
+        if (closes(in[k]) && --d == 0) return k + 1;
+      }
+      return in.size();
+    }
+    int d = 0;
+    size_t k = i;
+    for (; k < in.size(); ++k) {
+      if (d == 0 && follow && in[k].t == follow->t && in[k].s == follow->s) break;
+      if (d == 0 && in[k].t == T::Op && (in[k].s == "," || in[k].s == ";" || in[k].s == "=>")) break;  // never inside an expr
+      if (opens(in[k])) ++d;
+      if (closes(in[k])) --d;
+    }
+    return k;
+  }
+
+  // Matches matcher m against in; captures into caps. One level of repetition.
+  static bool macro_match(const std::vector<Tok>& m, const std::vector<Tok>& in, Caps& caps) {
+    size_t mi = 0, ii = 0;
+    while (mi < m.size()) {
+      if (m[mi].s == "$" && mi + 1 < m.size() && m[mi + 1].s == "(") {  // $( inner ) sep? *
+        size_t close = mi + 2;
+        int d = 1;
+        for (; close < m.size(); ++close) {
+          if (opens(m[close])) ++d;
+          if (closes(m[close]) && --d == 0) break;
+        }
+        std::vector<Tok> inner(m.begin() + (long)mi + 2, m.begin() + (long)close);
+        size_t after = close + 1;
+        const Tok* sep = nullptr;
+        if (after < m.size() && m[after].s != "*" && m[after].s != "+" && m[after].s != "?") sep = &m[after++];
+        if (after >= m.size()) return false;
+        const std::string kind = m[after].s;
+        const Tok* follow = after + 1 < m.size() ? &m[after + 1] : nullptr;
+        for (size_t k = 0; k + 1 < inner.size(); ++k)
+          if (inner[k].s == "$") caps[inner[k + 1].s];  // repeated variables exist even when empty
+        int count = 0;
+        while (ii < in.size() && !(follow && in[ii].t == follow->t && in[ii].s == follow->s)) {
+          size_t j = 0;
+          while (j < inner.size()) {
+            if (inner[j].s == "$" && j + 3 < inner.size() + 1 && inner[j + 2].s == ":") {
+              const Tok* f = sep ? sep : follow;
+              if (j + 4 < inner.size()) f = &inner[j + 4];
+              const size_t end = take_fragment(in, ii, inner[j + 3].s, f);
+              if (end == ii) return false;
+              caps[inner[j + 1].s].push_back(std::vector<Tok>(in.begin() + (long)ii, in.begin() + (long)end));
+              ii = end;
+              j += 4;
+            } else {
+              if (ii >= in.size() || in[ii].s != inner[j].s) return false;
+              ++ii;
+              ++j;
+            }
+          }
+          ++count;
+          if (sep) {
+            if (ii < in.size() && in[ii].s == sep->s) ++ii;
+            else break;
+          }
+        }
+        if (kind == "+" && count == 0) return false;
+        mi = after + 1;
+        continue;
+      }
+      if (m[mi].s == "$" && mi + 3 < m.size() + 1 && m[mi + 2].s == ":") {  // $name:frag
+        const Tok* follow = mi + 4 < m.size() ? &m[mi + 4] : nullptr;
+        const size_t end = take_fragment(in, ii, m[mi + 3].s, follow);
+        if (end == ii) return false;
+        caps[m[mi + 1].s].push_back(std::vector<Tok>(in.begin() + (long)ii, in.begin() + (long)end));
+        ii = end;
+        mi += 4;
+        continue;
+      }
+      if (ii >= in.size() || in[ii].s != m[mi].s) return false;
+      ++ii;
+      ++mi;
+    }
+    return ii == in.size();
+  }
+
+  static void macro_emit(const std::vector<Tok>& body, const Caps& caps, size_t rep, bool in_rep,
+                         std::vector<Tok>& out) {
+    for (size_t k = 0; k < body.size(); ++k) {
+      const Tok& t = body[k];
+      if (t.s == "$" && k + 1 < body.size() && body[k + 1].s == "(") {
+        size_t close = k + 2;
+        int d = 1;
+        for (; close < body.size(); ++close) {
+          if (opens(body[close])) ++d;
+          if (closes(body[close]) && --d == 0) break;
+        }
+        std::vector<Tok> inner(body.begin() + (long)k + 2, body.begin() + (long)close);
+        size_t after = close + 1;
+        const Tok* sep = nullptr;
+        if (after < body.size() && body[after].s != "*" && body[after].s != "+" && body[after].s != "?")
+          sep = &body[after++];
+        size_t n = 0;
+        for (size_t j = 0; j + 1 < inner.size(); ++j)
+          if (inner[j].s == "$" && caps.count(inner[j + 1].s)) n = std::max(n, caps.at(inner[j + 1].s).size());
+        for (size_t r = 0; r < n; ++r) {
+          if (r && sep) out.push_back(*sep);
+          macro_emit(inner, caps, r, true, out);
+        }
+        k = after;
+        continue;
+      }
+      if (t.s == "$" && k + 1 < body.size() && caps.count(body[k + 1].s)) {
+        const auto& v = caps.at(body[k + 1].s);
+        const size_t idx = in_rep ? rep : 0;
+        if (idx < v.size()) {
+          Tok lp = t, rp = t;
+          lp.t = rp.t = T::Op;
+          lp.s = "(";
+          rp.s = ")";
+          out.push_back(lp);
+          out.insert(out.end(), v[idx].begin(), v[idx].end());
+          out.push_back(rp);
+        }
+        ++k;
+        continue;
+      }
+      out.push_back(t);
+    }
+  }
+
+  EP expand_macro(const Tok& at, const std::string& name) {
+    std::vector<Tok> in = group();
+    for (const MacroRule& r : (*macros_)[name]) {
+      Caps caps;
+      if (!macro_match(r.matcher, in, caps)) continue;
+      std::vector<Tok> toks;
+      Tok lb = at, rb = at;
+      lb.t = rb.t = T::Op;
+      lb.s = "{";
+      rb.s = "}";
+      toks.push_back(lb);
+      macro_emit(r.body, caps, 0, false, toks);
+      toks.push_back(rb);
+      Tok eof = at;
+      eof.t = T::Eof;
+      eof.s = "";
+      toks.push_back(eof);
+      Parser sub(toks);
+      sub.macros_ = macros_;
+      return sub.expr();
+    }
+    fail("AE0002", at.line, at.col, "no rule of macro `" + name + "!` matches this invocation");
+  }
+
+  // println! / print!: the format string's `{}` / `{:..}` holes take the
+  // arguments in order; literal text between them is printed as is.
+  EP format_macro(const Tok& at, bool newline) {
+    expect_op("(");
+    if (cur().t != T::Str) fail("AE0002", cur().line, cur().col, "expected a format string");
+    const std::string fmt = cur().s;
+    next();
+    std::vector<EP> args;
+    while (eat_op(",")) {
+      if (is_op(")")) break;
+      args.push_back(expr());
+    }
+    expect_op(")");
+    EP blk = mk(Expr::BlockE, at);
+    blk->blk = std::make_shared<Block>();
+    auto print = [&](EP arg) {
+      auto st = std::make_shared<Stmt>();
+      st->k = Stmt::ExprS;
+      EP c = mk(Expr::Call, at);
+      c->s = "print";
+      c->a = {arg};
+      st->e = c;
+      blk->blk->stmts.push_back(st);
+    };
+    auto lit = [&](const std::string& text) {
+      if (text.empty()) return;
+      EP sx = mk(Expr::Str, at);
+      sx->s = text;
+      print(sx);
+    };
+    std::string text;
+    size_t ai = 0;
+    for (size_t i = 0; i < fmt.size(); ++i) {
+      if (fmt[i] == '{' && i + 1 < fmt.size() && fmt[i + 1] == '{') {
+        text += '{';
+        ++i;
+      } else if (fmt[i] == '}' && i + 1 < fmt.size() && fmt[i + 1] == '}') {
+        text += '}';
+        ++i;
+      } else if (fmt[i] == '{') {
+        const size_t close = fmt.find('}', i);
+        if (close == std::string::npos) fail("AE0002", at.line, at.col, "unclosed '{' in a format string");
+        lit(text);
+        text.clear();
+        if (ai >= args.size()) fail("AE0541", at.line, at.col, "format string has more holes than arguments");
+        print(args[ai++]);
+        i = close;
+      } else {
+        text += fmt[i];
+      }
+    }
+    if (newline) text += '\n';
+    lit(text);
+    return blk;
+  }
+
   static int prec(const std::string& op) {
     if (op == "||") return 1;
     if (op == "&&") return 2;
@@ -1347,7 +1621,12 @@ class Parser {
         expect_op("}");
         return e;
       }
-      if (eat_op("!")) fail("AE0500", at.line, at.col, "macros are not supported");
+      if (is_op("!") && (peek().s == "(" || peek().s == "[" || peek().s == "{")) {
+        next();  // !
+        if ((name == "println" || name == "print") && !macros_->count(name)) return format_macro(at, name == "println");
+        if (!macros_->count(name)) fail("AE0500", at.line, at.col, "macro `" + name + "!` is not defined here");
+        return expand_macro(at, name);
+      }
       if (eat_op("(")) {
         EP e = mk(Expr::Call, at);
         e->s = name;

@@ -71,7 +71,7 @@ def test_tensor_methods_lower_to_shaped_abi_calls():
     ("fn main() -> i32 { let x: i32 = 1; x.gelu(); 0 }", "AE0550"),              # not a tensor
     ("fn main() -> i32 { undefined_fn(1) }", "AE0540"),
     ("fn main() -> i32 { let t: Tensor<f32, [0]>; 0 }", "AE0521"),
-    ("fn main() -> i32 { let v = twice!(1); 0 }", "AE0500"),                    # macros are not compiled
+    ("fn main() -> i32 { let v = twice!(1); 0 }", "AE0500"),                    # an undefined macro
 ])
 def test_codegen_diagnostics_carry_codes(tmp_path, src, code):
     """Errors found while lowering to C (this compiler's own AE05xx codes)."""

@@ -139,7 +139,7 @@ def test_jit_page_and_probes():
     assert list((C.c_float * 64).from_address(b)) == list(vals)
     assert lb.aether_test_add_f32(1.5, 2.25) == 3.75 and lb.aether_test_add_f64(1e300, 1e300) == 2e300
     assert lb.aether_test_f32_to_i64(-3.7) == -3 and lb.aether_test_f64_to_i64(2.0**40) == 2**40
-    assert lb.aether_test_mix_if(3, 0.5, 4) == 5.5
+    assert lb.aether_test_mix_if(3, 0.5, 4) == 3.5  # (i + j) * f
 
 
 def test_containers_and_iterators():
