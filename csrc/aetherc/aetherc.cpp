@@ -402,6 +402,7 @@ struct Fn {
   BP body;                    // null: extern, or a trait method without a default body
   std::vector<std::string> generics;  // type parameters: specialised per use
   bool is_extern = false;
+  bool is_test = false;  // #[test]: run by the `--test` harness
   int line = 0, col = 0;
 };
 struct StructDef {
@@ -452,7 +453,7 @@ class Parser {
   Program program() {
     Program p;
     while (!at(T::Eof)) {
-      if (is_id("pub")) next();
+      if (eat_id("pub") && is_op("(")) group();  // pub(crate) / pub(super) / pub(in path): all public here
       if (eat_id("use")) {
         std::string path = ident();
         while (eat_op("::")) path += "::" + ident();
@@ -477,8 +478,10 @@ class Parser {
         p.impls.push_back(impl_def());
       } else if (is_id("extern") || is_id("fn") || is_id("unsafe")) {
         p.fns.push_back(fn());
+        p.fns.back().is_test = pending_test_;
+        pending_test_ = false;
       } else if (is_op("#")) {
-        attribute();
+        if (attribute() == "test") pending_test_ = true;
       } else if (is_id("struct")) {
         p.structs.push_back(struct_def());
       } else if (is_id("trait")) {
@@ -527,16 +530,20 @@ class Parser {
   }
 
   // `#[...]` before an item or a method: accepted and ignored.
-  void attribute() {
+  // `#[...]`: skipped; returns the attribute's name (`test`, `inline`, ...).
+  std::string attribute() {
     expect_op("#");
     expect_op("[");
+    const std::string name = at(T::Id) ? cur().s : "";
     int depth = 1;
     while (depth > 0 && !at(T::Eof)) {
       if (is_op("[")) ++depth;
       if (is_op("]")) --depth;
       next();
     }
+    return name;
   }
+  bool pending_test_ = false;  // the next fn carries #[test]
 
   // Closes a generic argument list; `>>` closes two.
   void close_angle() {
@@ -1795,6 +1802,19 @@ class Gen {
         o << "static " << ctype(sg.ret) << " " << sg.c << "(" << plist(sg) << ");\n";
       }
     o << lifted_protos_ << "\n" << lifted_defs_ << defs.str();
+    if (test_mode_) {  // --test: every #[test] fn in source order; 0 = pass
+      o << "int main(void) {\n  int failed = 0, total = 0;\n";
+      for (auto& f : p_.fns) {
+        if (!f.is_test) continue;
+        const FnSig& sg = sigs_[f.name];
+        if (!sg.params.empty()) fail("AE0541", f.line, f.col, "#[test] fn '" + f.name + "' takes no arguments");
+        o << "  { int r = " << (sg.ret.b == B::Void ? "(" + sg.c + "(), 0)" : "(int)" + sg.c + "()") << "; ++total; "
+          << "printf(\"%s " << f.name << "\\n\", r == 0 ? \"PASS\" : \"FAIL\"); if (r) ++failed; }\n";
+      }
+      o << "  if (failed == 0) printf(\"ALL PASSED (%d tests)\\n\", total);\n"
+           "  else printf(\"%d of %d tests FAILED\\n\", failed, total);\n  return failed != 0;\n}\n";
+      return o.str();
+    }
     if (!sigs_.count("main") || sigs_["main"].is_extern) fail("AE0580", 1, 1, "program has no `fn main`");
     const FnSig& m = sigs_["main"];
     o << "int main(void) {\n";
@@ -1813,6 +1833,11 @@ class Gen {
  private:
   Program& p_;
   std::string stdlib_, srcdir_;
+
+ public:
+  bool test_mode_ = false;
+
+ private:
   std::map<std::string, FnSig> sigs_;
   std::map<std::string, const Const*> const_src_;
   std::map<std::string, std::pair<Ty, double>> const_val_;
@@ -3720,13 +3745,14 @@ void usage() {
       "--emit=ast     write the parsed program as an S-expression\n"
       "--check        parse, resolve `use`, check traits, scalar types and borrows; no code\n"
       "--no-fuse      keep `matmul` + in-place `gelu` as two runtime calls\n"
+      "--test         main runs every #[test] fn (0 = pass), prints PASS / FAIL and a summary\n"
       "The reference's other emit kinds (mir, llvm-ir, asm, asm-bin, aether-bin, pe-bin) are not produced.");
 }
 }  // namespace
 
 int main(int argc, char** argv) {
   std::string input, output, emit = "bin", stdlib, libdir, cc = "cc", opt = "-O2";
-  bool check = false, json = false, fuse = true;
+  bool check = false, json = false, fuse = true, test_mode = false;
   for (int i = 1; i < argc; ++i) {
     const std::string a = argv[i];
     if (a == "-o" && i + 1 < argc) output = argv[++i];
@@ -3734,6 +3760,7 @@ int main(int argc, char** argv) {
     else if (a == "--check") check = true;
     else if (a == "--json-errors") json = true;
     else if (a == "--no-fuse") fuse = false;
+    else if (a == "--test") test_mode = true;
     else if (a == "--O0") opt = "-O0";
     else if (a == "--O1") opt = "-O1";
     else if (a == "--O2") opt = "-O2";
@@ -3808,6 +3835,7 @@ int main(int argc, char** argv) {
       for (auto& f : prog.fns)
         if (f.body) fused += ae::fuse_block(*f.body);
     ae::Gen g(prog, stdlib, dirname_of(input));
+    g.test_mode_ = test_mode;
     const std::string c = g.run();
     if (emit == "c") {
       if (output.empty()) std::fputs(c.c_str(), stdout);

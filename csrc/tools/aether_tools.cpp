@@ -714,7 +714,9 @@ int main_audit(const std::vector<std::string>& args) {
         const char* td = mkdtemp(tmpl);
         const std::string exe = std::string(td ? td : "/tmp") + "/w";
         std::string log;
-        if (run_cmd({aec, p, "-o", exe}, &log, 300) != 0) {
+        std::vector<std::string> cmd = {aec, p, "-o", exe};
+        if (src.find("build-mode: aether-bin-test") != std::string::npos) cmd.push_back("--test");  // #[test] harness
+        if (run_cmd(cmd, &log, 300) != 0) {
           status = "compile error";
         } else {
           const int rc = run_cmd({exe}, &log, 600);

@@ -30,10 +30,13 @@ def _expect(path):
 
 def _run_program(path, tmp_path):
     out = str(tmp_path / os.path.basename(path)[: -len(".aether")])
-    c = _compile(path, out)
+    harness = re.search(r"build-mode:\s*aether-bin-test", open(path).read()) is not None
+    c = _compile(path, out, *(["--test"] if harness else []))
     assert c.returncode == 0, c.stderr
     r = subprocess.run([out], capture_output=True, text=True, timeout=300, cwd=str(tmp_path))
     assert r.returncode == _expect(path), (path, r.returncode, r.stdout[-2000:], r.stderr[-2000:])
+    if harness:  # one line per test, then the summary
+        assert "PASS adds" in r.stdout and "FAIL fails_on_purpose" in r.stdout and "1 of 3 tests FAILED" in r.stdout
 
 
 @pytest.mark.parametrize("name", sorted(f for f in os.listdir(PROGS) if f.startswith("cpu_")))
@@ -178,7 +181,8 @@ def test_reference_runtime_witnesses(tmp_path):
             continue
         cuda = "requires: cuda" in text
         out = str(tmp_path / name[:-7])
-        if _compile(path, out).returncode != 0:
+        extra = ["--test"] if re.search(r"build-mode:\s*aether-bin-test", text) else []  # the #[test] harness
+        if _compile(path, out, *extra).returncode != 0:
             if name.startswith("cuda_train_"):
                 train_missing.append(name)
             continue
@@ -191,4 +195,4 @@ def test_reference_runtime_witnesses(tmp_path):
         else:
             wrong.append(name)
     assert not train_missing, train_missing
-    assert cuda_compiled >= 21 and passed >= 257, (cuda_compiled, passed, wrong)
+    assert cuda_compiled >= 21 and passed >= 259, (cuda_compiled, passed, wrong)
