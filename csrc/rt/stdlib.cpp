@@ -15,6 +15,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cctype>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -993,3 +994,104 @@ int aether_gguf_get_metadata_array_f32(int64_t h, int64_t key, int key_len, int6
 }
 
 }  // extern "C"
+
+#ifndef AE_API
+#define AE_API extern "C" __attribute__((visibility("default")))
+#endif
+
+// ------------------------------------------------------------------ unprefixed file-format helpers
+// Exports the runtime module declares without the `aether_` prefix
+// (runtime/src/lib.rs:1220-1260, 1780-1880): header checks on an in-memory
+// GGUF / safetensors image (a pointer held as an int64) and a one-tensor
+// safetensors file named "data" written through a temporary file and a
+// rename, so a crash never leaves the destination half written.
+namespace {
+uint64_t le_u64(const uint8_t* p, int n) {
+  uint64_t v = 0;
+  for (int i = 0; i < n; ++i) v |= (uint64_t)p[i] << (8 * i);
+  return v;
+}
+const uint8_t* bytes_of(int64_t a) { return reinterpret_cast<const uint8_t*>((intptr_t)a); }
+}  // namespace
+
+AE_API int64_t gguf_parse_magic(int64_t buf, int64_t len) {
+  if (!buf || len < 4) return 0;
+  return std::memcmp(bytes_of(buf), "GGUF", 4) == 0 ? 1 : 0;
+}
+AE_API int64_t gguf_version(int64_t buf, int64_t len) {
+  return (!buf || len < 8) ? -1 : (int64_t)le_u64(bytes_of(buf) + 4, 4);
+}
+AE_API int64_t gguf_tensor_count(int64_t buf, int64_t len) {
+  return (!buf || len < 16) ? -1 : (int64_t)le_u64(bytes_of(buf) + 8, 8);
+}
+AE_API int64_t gguf_metadata_count(int64_t buf, int64_t len) {
+  return (!buf || len < 24) ? -1 : (int64_t)le_u64(bytes_of(buf) + 16, 8);
+}
+
+// Byte count of the JSON header after the 8-byte little-endian length, or -1.
+AE_API int64_t safetensors_parse_header(int64_t buf, int64_t len) {
+  if (!buf || len < 8) return -1;
+  const uint64_t h = le_u64(bytes_of(buf), 8);
+  return 8 + h > (uint64_t)len ? -1 : (int64_t)h;
+}
+
+// Address of tensor `name`'s payload in the image (its first data offset
+// past the header), or 0 when the name is not a key of the header.
+AE_API int64_t safetensors_get_tensor_f32(int64_t buf, int64_t len, int64_t name, int64_t name_len) {
+  const int64_t h = safetensors_parse_header(buf, len);
+  if (h < 0 || !name || name_len <= 0) return 0;
+  const std::string json(reinterpret_cast<const char*>(bytes_of(buf) + 8), (size_t)h);
+  const std::string key = "\"" + std::string(reinterpret_cast<const char*>(bytes_of(name)), (size_t)name_len) + "\"";
+  size_t at = 0;
+  for (;;) {  // the name as a key: a colon follows its closing quote
+    at = json.find(key, at);
+    if (at == std::string::npos) return 0;
+    size_t k = at + key.size();
+    while (k < json.size() && std::isspace((unsigned char)json[k])) ++k;
+    if (k < json.size() && json[k] == ':') break;
+    at += key.size();
+  }
+  const size_t off = json.find("\"data_offsets\":[", at);
+  if (off == std::string::npos) return 0;
+  const long long start = std::atoll(json.c_str() + off + 16);
+  if (start < 0 || 8 + h + start > len) return 0;
+  return buf + 8 + h + start;
+}
+
+AE_API int safetensors_save_f32(int64_t path, int64_t ptr, int64_t n) {
+  if (!path || !ptr || n < 0) return -1;
+  const std::string p(reinterpret_cast<const char*>(bytes_of(path)));
+  const std::string json = "{\"data\":{\"dtype\":\"F32\",\"shape\":[" + std::to_string(n) +
+                           "],\"data_offsets\":[0," + std::to_string(n * 4) + "]}}";
+  uint8_t len8[8];
+  for (int i = 0; i < 8; ++i) len8[i] = (uint8_t)((uint64_t)json.size() >> (8 * i));
+  const std::string tmp = p + ".tmp";
+  FILE* f = std::fopen(tmp.c_str(), "wb");
+  if (!f) return -2;
+  bool ok = std::fwrite(len8, 1, 8, f) == 8 && std::fwrite(json.data(), 1, json.size(), f) == json.size() &&
+            std::fwrite(bytes_of(ptr), 4, (size_t)n, f) == (size_t)n;
+  ok = (std::fclose(f) == 0) && ok;
+  if (!ok) return -2;
+  return std::rename(tmp.c_str(), p.c_str()) == 0 ? 0 : -3;
+}
+
+// Reads the first tensor's first n floats of a safetensors file into dst.
+AE_API int safetensors_load_f32(int64_t path, int64_t dst, int64_t n) {
+  if (!path || !dst || n < 0) return -1;
+  FILE* f = std::fopen(reinterpret_cast<const char*>(bytes_of(path)), "rb");
+  if (!f) return -2;
+  std::string all;
+  char chunk[65536];
+  size_t got;
+  while ((got = std::fread(chunk, 1, sizeof chunk, f)) > 0) all.append(chunk, got);
+  std::fclose(f);
+  const int64_t h = safetensors_parse_header((int64_t)(intptr_t)all.data(), (int64_t)all.size());
+  if (h < 0) return -3;
+  const std::string json = all.substr(8, (size_t)h);
+  const size_t off = json.find("\"data_offsets\":[");
+  if (off == std::string::npos) return -5;
+  const long long start = std::atoll(json.c_str() + off + 16);
+  if (start < 0 || 8 + (size_t)h + (size_t)start + (size_t)n * 4 > all.size()) return -6;
+  std::memcpy(reinterpret_cast<void*>((intptr_t)dst), all.data() + 8 + h + start, (size_t)n * 4);
+  return 0;
+}

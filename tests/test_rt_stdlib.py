@@ -218,3 +218,39 @@ def test_gguf_reader(tmp_path):
     bad = str(tmp_path / "bad.gguf")
     open(bad, "wb").write(b"NOPE" + b"\0" * 40)
     assert rt.call("aether_gguf_open", bad.encode(), len(bad)) == -2
+
+
+def test_unprefixed_file_format_exports(tmp_path):
+    """gguf_* header queries on an in-memory image and the one-tensor
+    safetensors save / load / lookup exports (the runtime module declares
+    them without the aether_ prefix)."""
+    lib = rt.lib()
+    for n in ("gguf_parse_magic", "gguf_version", "gguf_tensor_count", "gguf_metadata_count",
+              "safetensors_parse_header", "safetensors_get_tensor_f32"):
+        getattr(lib, n).restype = C.c_int64
+    for n in ("safetensors_save_f32", "safetensors_load_f32"):
+        getattr(lib, n).restype = C.c_int
+    head = np.frombuffer(b"GGUF" + (3).to_bytes(4, "little") + (7).to_bytes(8, "little") + (11).to_bytes(8, "little"),
+                         np.uint8).copy()
+    p, n = C.c_int64(head.ctypes.data), C.c_int64(head.size)
+    assert lib.gguf_parse_magic(p, n) == 1 and lib.gguf_version(p, n) == 3
+    assert lib.gguf_tensor_count(p, n) == 7 and lib.gguf_metadata_count(p, n) == 11
+    assert lib.gguf_tensor_count(p, C.c_int64(12)) == -1  # too short for the field
+    vals = np.arange(6, dtype=np.float32) * 1.5
+    path = str(tmp_path / "w.safetensors").encode()
+    assert lib.safetensors_save_f32(C.c_int64(C.cast(C.c_char_p(path), C.c_void_p).value),
+                                    C.c_int64(vals.ctypes.data), C.c_int64(6)) == 0
+    got = np.zeros(6, np.float32)
+    assert lib.safetensors_load_f32(C.c_int64(C.cast(C.c_char_p(path), C.c_void_p).value),
+                                    C.c_int64(got.ctypes.data), C.c_int64(6)) == 0
+    assert np.array_equal(got, vals)
+    blob = np.frombuffer(open(path.decode(), "rb").read(), np.uint8).copy()
+    b, bn = C.c_int64(blob.ctypes.data), C.c_int64(blob.size)
+    hdr = lib.safetensors_parse_header(b, bn)
+    assert hdr > 0 and json.loads(bytes(blob[8:8 + hdr]))["data"]["shape"] == [6]
+    name = b"data"
+    addr = lib.safetensors_get_tensor_f32(b, bn, C.c_int64(C.cast(C.c_char_p(name), C.c_void_p).value), C.c_int64(4))
+    assert addr == blob.ctypes.data + 8 + hdr
+    assert np.array_equal(np.frombuffer((C.c_float * 6).from_address(addr), np.float32), vals)
+    miss = b"nope"
+    assert lib.safetensors_get_tensor_f32(b, bn, C.c_int64(C.cast(C.c_char_p(miss), C.c_void_p).value), C.c_int64(4)) == 0
