@@ -36,7 +36,10 @@
 // from argument types, then from the expected type, and a generic impl's
 // methods are generated for each instance that calls them. `macro_rules!`
 // macros expand at parse time (captures, one level of repetition, rules in
-// order) and `println!` / `print!` take `{}` holes. Shape generics
+// order) and `println!` / `print!` take `{}` holes. Slices `&[T]` are
+// (pointer, length) structs: `slice_from_raw`, `&s[a..b]` of a slice, a
+// fixed array or a runtime vector / string handle, `len()`, indexing and
+// `for x in s`. Shape generics
 // (`Tensor<f32, [M, K]>` with M a parameter) are diagnostics, not
 // miscompiles.
 #include <sys/stat.h>
@@ -806,6 +809,10 @@ class Parser {
     if (eat_op("[")) {
       t->name = "[]";
       t->inner = type();
+      if (eat_op("]")) {  // `[T]` (written `&[T]`): a slice
+        t->name = "slice";
+        return t;
+      }
       expect_op(";");
       t->dims.push_back(expr());
       expect_op("]");
@@ -978,8 +985,9 @@ class Parser {
       no_struct_ = saved;
       if (eat_op("..=")) {
         s->inclusive = true;
-      } else if (!eat_op("..")) {
-        fail("AE0500", cur().line, cur().col, "for loops iterate over ranges a..b or a..=b");
+      } else if (!eat_op("..")) {  // `for x in slice`
+        s->body = block();
+        return s;
       }
       no_struct_ = true;
       s->e2 = expr_prec(9);
@@ -1417,7 +1425,28 @@ class Parser {
       } else if (is_op("[")) {
         next();
         EP ix = mk(Expr::Index, at);
-        ix->a = {e, expr()};
+        if (is_op("..")) {  // [..b] / [..]
+          next();
+          ix->s = "..";
+          ix->a = {e, nullptr, is_op("]") ? nullptr : expr()};
+        } else {
+          EP first = expr_prec(9);
+          if (eat_op("..")) {  // [a..b] / [a..]
+            ix->s = "..";
+            ix->a = {e, first, is_op("]") ? nullptr : expr()};
+          } else {
+            ix->a = {e, first};
+            while (cur().t == T::Op && prec(cur().s) >= 0) {  // the rest of a full expression
+              const std::string op = cur().s;
+              const Tok o = cur();
+              next();
+              EP b = mk(Expr::Binary, o);
+              b->s = op;
+              b->a = {ix->a[1], expr_prec(prec(op) + 1)};
+              ix->a[1] = b;
+            }
+          }
+        }
         expect_op("]");
         e = ix;
       } else {
@@ -1985,6 +2014,55 @@ class Gen {
     return {s.c + "(" + list + ")", s.ret};
   }
 
+  // Slices `&[T]`: a C struct {T* ptr; int64_t len}.
+  std::map<std::string, Ty> slice_elem_;
+  Ty slice_ty(const Ty& elem) {
+    const std::string n = "S_" + mangle(elem);
+    if (!structs_.count(n)) {
+      Ty pt = elem;
+      pt.ref = true;
+      StructInfo& in = structs_[n];
+      in.fields = {{"ptr", pt}, {"len", prim(B::I64)}};
+      tuple_names_.push_back(n);
+      slice_elem_[n] = elem;
+    }
+    return struct_ty(n);
+  }
+  bool is_slice(const Ty& t) const { return t.b == B::Struct && !t.ref && slice_elem_.count(t.sname); }
+
+  // `&h[a..b]`: a slice of a slice, or of a runtime vector / string handle
+  // (an i64) read through the handle's pointer and length accessors.
+  V slice_range(const EP& e, const Ty& hint) {
+    V b = deref(gen(e->a[0], prim(B::Unknown)));
+    Ty st;
+    std::string ptr, len, pre;
+    const std::string t = "sl_" + std::to_string(++uniq_);
+    if (is_slice(b.t)) {
+      st = b.t;
+      pre = ctype(st) + " " + t + " = " + b.c + "; ";
+      ptr = t + ".f_ptr";
+      len = t + ".f_len";
+    } else if (b.t.b == B::Array) {  // a fixed array: its storage and length
+      st = slice_ty(*b.t.inner);
+      ptr = "(" + b.c + ")";
+      len = std::to_string(b.t.len);
+    } else if (b.t.is_int() && is_slice(hint)) {
+      st = hint;
+      const Ty el = slice_elem_[hint.sname];
+      std::string acc = el.b == B::U8 || el.b == B::I8 ? "aether_string" : el.b == B::F32 ? "aether_vec_f32" : "aether_vec_i64";
+      pre = "int64_t " + t + " = " + b.c + "; ";
+      ptr = "((" + ctype(el) + "*)(intptr_t)" + acc + "_as_ptr(" + t + "))";
+      len = "((int64_t)" + acc + "_len(" + t + "))";
+    } else {
+      fail("AE0530", e->line, e->col, "a range index needs a slice, or a vector / string handle where a slice is expected");
+    }
+    const std::string lo = e->a[1] ? conv(gen(e->a[1], prim(B::I64)), prim(B::I64)) : "0";
+    const std::string hi = e->a.size() > 2 && e->a[2] ? conv(gen(e->a[2], prim(B::I64)), prim(B::I64)) : len;
+    return {"({ " + pre + "int64_t lo_" + t + " = " + lo + "; (" + ctype(st) + "){" + ptr + " + lo_" + t + ", (" + hi +
+                ") - lo_" + t + "}; })",
+            st};
+  }
+
   // Tuples: one C struct per element-type list, fields f_0, f_1, ...
   std::vector<std::string> tuple_names_;
   Ty tuple_ty(const std::vector<Ty>& elems) {
@@ -2492,13 +2570,15 @@ class Gen {
 
   Ty resolve(const TyExpr& t) {
     Ty r = resolve_base(t);
-    if (t.ref && r.b != B::Tensor && r.b != B::Array && r.b != B::Str && r.b != B::Void) r.ref = true;
+    if (t.ref && r.b != B::Tensor && r.b != B::Array && r.b != B::Str && r.b != B::Void && t.name != "slice")
+      r.ref = true;  // a slice is a (pointer, length) value already
     return r;
   }
 
   Ty resolve_base(const TyExpr& t) {
     Ty r;
     if (t.name == "()") return prim(B::Void);
+    if (t.name == "slice") return slice_ty(resolve(*t.inner));
     if (t.name == "tuple") {
       std::vector<Ty> el;
       for (auto& x : t.elems) el.push_back(resolve(*x));
@@ -2647,7 +2727,9 @@ class Gen {
         return {"(-" + a.c + ")", a.t};
       }
       case Expr::Ref: {
+        if (e->a[0]->k == Expr::Index && e->a[0]->s == "..") return slice_range(e->a[0], hint);
         V a = gen(e->a[0], hint);
+        if (is_slice(a.t)) return a;
         if (a.t.ref || a.t.b == B::Tensor || a.t.b == B::Array || a.t.b == B::Str || a.t.b == B::Void ||
             a.t.b == B::Unknown)
           return a;  // a tensor's value is its handle; arrays and strings are pointers already
@@ -2678,7 +2760,12 @@ class Gen {
           return method_call(e, hint.sname + "::from", {e->a[0]}, nullptr);
         return method(e);
       case Expr::Index: {
-        V arr = gen(e->a[0], prim(B::Unknown));
+        if (e->s == "..") return slice_range(e, hint);
+        V arr = deref(gen(e->a[0], prim(B::Unknown)));
+        if (is_slice(arr.t)) {
+          V ix = gen(e->a[1], prim(B::I64));
+          return {"(" + arr.c + ").f_ptr[" + ix.c + "]", slice_elem_[arr.t.sname]};
+        }
         if (arr.t.b != B::Array) fail("AE0530", e->line, e->col, "only arrays can be indexed");
         V ix = gen(e->a[1], prim(B::I64));
         return {arr.c + "[" + ix.c + "]", *arr.t.inner};
@@ -2921,6 +3008,14 @@ class Gen {
       return {(a.t.b == B::F32 ? cn + "f(" : cn + "(") + a.c + ")", a.t};
     }
     if (gfns_.count(n)) return generic_call(e, n, hint);
+    if (n == "slice_from_raw" && !sigs_.count(n)) {  // (pointer as i64, length) -> the expected slice type
+      if (!is_slice(hint)) fail("AE0520", e->line, e->col, "slice_from_raw needs an expected `&[T]` type");
+      if (e->a.size() != 2) fail("AE0541", e->line, e->col, "slice_from_raw takes a pointer and a length");
+      const Ty el = slice_elem_[hint.sname];
+      return {"((" + ctype(hint) + "){(" + ctype(el) + "*)(intptr_t)(" + conv(gen(e->a[0], prim(B::I64)), prim(B::I64)) +
+                  "), " + conv(gen(e->a[1], prim(B::I64)), prim(B::I64)) + "})",
+              hint};
+    }
     auto it = sigs_.find(n);
     if (it == sigs_.end()) fail("AE0540", e->line, e->col, "unknown function '" + n + "'");
     const FnSig& s = it->second;
@@ -2948,6 +3043,7 @@ class Gen {
 
   V method(const EP& e) {
     V r = gen(e->a[0], prim(B::Unknown));
+    if (is_slice(deref(r).t) && e->s == "len" && e->a.size() == 1) return {"(" + deref(r).c + ").f_len", prim(B::I64)};
     if (r.t.b == B::Struct && r.t.ref) {  // through a reference: `&self` methods take the pointer itself
       const std::string key = r.t.sname + "::" + e->s;
       if (sigs_.count(key) && sigs_.at(key).self_kind == 2) {
@@ -3133,6 +3229,19 @@ class Gen {
       }
       case Stmt::Loop: return "for (;;) " + block_stmt(*s.body);
       case Stmt::For: {
+        if (!s.e2) {  // for x in slice
+          V c = deref(gen(s.e, prim(B::Unknown)));
+          if (!is_slice(c.t)) fail("AE0500", s.line, s.col, "for loops iterate over ranges a..b, a..=b or slices");
+          const Ty el = slice_elem_[c.t.sname];
+          const std::string sv = "it_" + std::to_string(++uniq_), k = "k_" + std::to_string(uniq_);
+          scopes_.emplace_back();
+          const std::string x = bind(s.name, el);
+          std::string r = "{ " + ctype(c.t) + " " + sv + " = " + c.c + "; for (int64_t " + k + " = 0; " + k + " < " + sv +
+                          ".f_len; ++" + k + ") { " + ctype(el) + " " + x + " = " + sv + ".f_ptr[" + k + "]; " +
+                          block_stmt(*s.body) + " } }";
+          scopes_.pop_back();
+          return r;
+        }
         V a = gen(s.e, prim(B::Unknown));
         V b = gen(s.e2, a.t);
         Ty t = a.t.is_int() ? a.t : prim(B::I64);
