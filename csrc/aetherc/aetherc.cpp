@@ -39,7 +39,9 @@
 // order) and `println!` / `print!` take `{}` holes. Slices `&[T]` are
 // (pointer, length) structs: `slice_from_raw`, `&s[a..b]` of a slice, a
 // fixed array or a runtime vector / string handle, `len()`, indexing and
-// `for x in s`. Shape generics
+// `for x in s`. Generic enums are specialised like generic structs, and
+// `e?` yields the `Ok` / `Some` value or returns the enum from the enclosing
+// function. Shape generics
 // (`Tensor<f32, [M, K]>` with M a parameter) are diagnostics, not
 // miscompiles.
 #include <sys/stat.h>
@@ -362,7 +364,7 @@ using PP = std::shared_ptr<Pat>;
 
 struct Expr {
   enum K { Int, Float, BoolL, Str, Char, Var, Unary, Binary, Call, Method, Cast, Ref, If, BlockE, Index, ArrayLit,
-           ArrayRep, LoopE, Field, Deref, StructLit, Match, TupleLit, Closure } k;
+           ArrayRep, LoopE, Field, Deref, StructLit, Match, TupleLit, Closure, Try } k;
   std::string s;  // literal / name / operator / method / struct
   std::vector<EP> a;
   std::vector<std::string> fields;  // struct literal: the field each of `a` initialises
@@ -1422,6 +1424,11 @@ class Parser {
         }
         expect_op(")");
         e = c;
+      } else if (is_op("?")) {  // early return unless the Ok / Some variant
+        next();
+        EP t = mk(Expr::Try, at);
+        t->a = {e};
+        e = t;
       } else if (is_op("[")) {
         next();
         EP ix = mk(Expr::Index, at);
@@ -1918,6 +1925,54 @@ class Gen {
     return c;
   }
 
+  std::map<std::string, const EnumDef*> genums_;
+
+  // A generic enum's instance: a tagged struct like any enum with payloads.
+  Ty specialize_enum(const std::string& base, const std::vector<Ty>& args, int line, int col) {
+    const EnumDef& d = *genums_.at(base);
+    if (args.size() != d.generics.size())
+      fail("AE0522", line, col, "`" + base + "` takes " + std::to_string(d.generics.size()) + " type arguments");
+    std::string name = base;
+    std::map<std::string, Ty> sub;
+    for (size_t i = 0; i < args.size(); ++i) {
+      name += "__" + mangle(args[i]);
+      sub[d.generics[i]] = args[i];
+    }
+    if (!enums_.count(name)) {
+      auto saved = tsubst_;
+      tsubst_ = sub;
+      EnumInfo in;
+      in.unit_only = false;
+      for (auto& v : d.variants) {
+        std::vector<Ty> ts;
+        for (auto& t : v.second) ts.push_back(resolve(*t));
+        in.variants.push_back({v.first, ts});
+      }
+      tsubst_ = saved;
+      enums_[name] = in;
+      tuple_names_.push_back(name);
+      spec_of_[name] = {base, sub};
+    }
+    return struct_ty(name);
+  }
+
+  // The instance of generic enum `base` a path names: the expected type's,
+  // else one bound from the payload values (unbound parameters: i64).
+  std::string enum_instance(const std::string& base, const std::string& variant, const std::vector<EP>& payload,
+                            const Ty& hint, int line, int col) {
+    if (hint.b == B::Struct && spec_of_.count(hint.sname) && spec_of_[hint.sname].first == base) return hint.sname;
+    const EnumDef& d = *genums_.at(base);
+    std::map<std::string, Ty> sub;
+    for (auto& v : d.variants)
+      if (v.first == variant)
+        for (size_t k = 0; k < v.second.size() && k < payload.size(); ++k)
+          if (std::count(d.generics.begin(), d.generics.end(), v.second[k]->name) && !sub.count(v.second[k]->name))
+            sub[v.second[k]->name] = gen(payload[k], prim(B::Unknown)).t;
+    std::vector<Ty> args;
+    for (auto& g : d.generics) args.push_back(sub.count(g) ? sub[g] : prim(B::I64));
+    return specialize_enum(base, args, line, col).sname;
+  }
+
   Ty specialize_struct(const std::string& base, const std::vector<Ty>& args, int line, int col) {
     const StructDef& d = *gstructs_.at(base);
     if (args.size() != d.generics.size())
@@ -2222,10 +2277,12 @@ class Gen {
       else structs_[d.name];
     }
     for (auto& d : p_.enums) {
-      if (!d.generics.empty())
-        fail("AE0500", d.line, d.col, "generic enums are checked but not compiled by this compiler");
-      if (structs_.count(d.name) || enums_.count(d.name))
+      if (structs_.count(d.name) || enums_.count(d.name) || genums_.count(d.name))
         fail("AE0501", d.line, d.col, "type '" + d.name + "' is defined twice");
+      if (!d.generics.empty()) {
+        genums_[d.name] = &d;
+        continue;
+      }
       EnumInfo& in = enums_[d.name];
       for (auto& v : d.variants) in.unit_only &= v.second.empty();
     }
@@ -2233,6 +2290,7 @@ class Gen {
       if (d.generics.empty())
         for (auto& f : d.fields) structs_[d.name].fields.push_back({f.name, resolve(*f.ty)});
     for (auto& d : p_.enums)
+      if (d.generics.empty())
       for (auto& v : d.variants) {
         std::vector<Ty> ts;
         for (auto& t : v.second) ts.push_back(resolve(*t));
@@ -2286,7 +2344,7 @@ class Gen {
       if (d.generics.empty()) visit(d.name);
     for (size_t i = 0; i < tuple_names_.size(); ++i) visit(tuple_names_[i]);
     for (auto& d : p_.enums)
-      if (!enums_[d.name].unit_only) visit(d.name);
+      if (d.generics.empty() && !enums_[d.name].unit_only) visit(d.name);
     for (auto& n : order) o << "typedef struct aes_" << n << " aes_" << n << ";\n";
     for (auto& n : order) {
       if (enums_.count(n)) {
@@ -2376,7 +2434,9 @@ class Gen {
       case Pat::Path:
       case Pat::Tuple: {
         const size_t cc = p.s.rfind("::");
-        const std::string en = cc == std::string::npos ? "" : p.s.substr(0, cc);
+        std::string en = cc == std::string::npos ? "" : p.s.substr(0, cc);
+        if (genums_.count(en) && t.b == B::Struct && spec_of_.count(t.sname) && spec_of_[t.sname].first == en)
+          en = t.sname;  // Option::Some(x) against an Option<i64> value
         if (!en.empty() && enums_.count(en)) {
           const std::string vn = p.s.substr(cc + 2);
           const int ix = variant_index(en, vn);
@@ -2604,10 +2664,11 @@ class Gen {
     }
     if (tsubst_.count(t.name)) return tsubst_.at(t.name);
     if (t.name == "Self" && !self_type_.empty()) return struct_ty(self_type_);
-    if (gstructs_.count(t.name)) {
+    if (gstructs_.count(t.name) || genums_.count(t.name)) {
       std::vector<Ty> args;
       for (auto& a : t.targs) args.push_back(resolve(*a));
-      return specialize_struct(t.name, args, t.line, t.col);
+      return gstructs_.count(t.name) ? specialize_struct(t.name, args, t.line, t.col)
+                                     : specialize_enum(t.name, args, t.line, t.col);
     }
     if (t.name == "Closure") {  // a closure object: the address of [function, captures...]
       Ty c = prim(B::I64);
@@ -2706,6 +2767,12 @@ class Gen {
           return {"((int64_t)(intptr_t)&" + sigs_[e->s].c + ")", prim(B::I64)};
         }
         const size_t cc = e->s.rfind("::");
+        if (cc != std::string::npos && genums_.count(e->s.substr(0, cc))) {
+          EP inst = std::make_shared<Expr>(*e);
+          inst->s = enum_instance(e->s.substr(0, cc), e->s.substr(cc + 2), {}, hint, e->line, e->col) + "::" +
+                    e->s.substr(cc + 2);
+          return gen(inst, hint);
+        }
         if (cc != std::string::npos && enums_.count(e->s.substr(0, cc))) {
           const std::string en = e->s.substr(0, cc);
           const int ix = variant_index(en, e->s.substr(cc + 2));
@@ -2864,6 +2931,22 @@ class Gen {
         for (size_t i = 0; i < vs.size(); ++i) r += (i ? ", " : "") + conv(vs[i], el[i]);
         return {r + "})", t};
       }
+      case Expr::Try: {
+        V v = gen(e->a[0], prim(B::Unknown));
+        if (v.t.b != B::Struct || !enums_.count(v.t.sname))
+          fail("AE0520", e->line, e->col, "`?` needs an enum value (Ok / Some and a failure variant)");
+        int ok = variant_index(v.t.sname, "Ok");
+        if (ok < 0) ok = variant_index(v.t.sname, "Some");
+        if (ok < 0 || enums_[v.t.sname].variants[ok].second.size() != 1)
+          fail("AE0520", e->line, e->col, "`?` needs an `Ok(..)` or `Some(..)` variant with one value");
+        if (ret_.b != B::Struct || ret_.sname != v.t.sname)
+          fail("AE0520", e->line, e->col, "`?` returns the failure itself, so the function must return " + tyname(v.t));
+        const std::string t = "try_" + std::to_string(++uniq_);
+        const std::string vn = enums_[v.t.sname].variants[ok].first;
+        return {"({ " + ctype(v.t) + " " + t + " = " + v.c + "; if (" + t + ".tag != " + std::to_string(ok) + ") return " + t +
+                    "; " + t + ".u.v_" + vn + ".a0; })",
+                enums_[v.t.sname].variants[ok].second[0]};
+      }
       case Expr::Field: {
         V b = deref(gen(e->a[0], prim(B::Unknown)));
         if (b.t.b != B::Struct) fail("AE0530", e->line, e->col, "field '" + e->s + "' of a value that is not a struct");
@@ -2915,6 +2998,12 @@ class Gen {
 
   V call(const EP& e, const Ty& hint) {
     const size_t colon = e->s.rfind("::");
+    if (colon != std::string::npos && genums_.count(e->s.substr(0, colon))) {  // a generic enum's variant
+      EP inst = std::make_shared<Expr>(*e);
+      inst->s = enum_instance(e->s.substr(0, colon), e->s.substr(colon + 2), e->a, hint, e->line, e->col) + "::" +
+                e->s.substr(colon + 2);
+      return call(inst, hint);
+    }
     if (colon != std::string::npos && enums_.count(e->s.substr(0, colon))) {  // a variant with its payload
       const std::string en = e->s.substr(0, colon);
       const int ix = variant_index(en, e->s.substr(colon + 2));
