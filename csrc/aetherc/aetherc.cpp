@@ -41,7 +41,10 @@
 // fixed array or a runtime vector / string handle, `len()`, indexing and
 // `for x in s`. Generic enums are specialised like generic structs, and
 // `e?` yields the `Ok` / `Some` value or returns the enum from the enclosing
-// function. Shape generics
+// function. `async fn` is compiled as a plain function that runs to
+// completion where it is awaited (`.await` yields its value, `yield_now()`
+// does nothing): with a single task this gives the result polling would.
+// Shape generics
 // (`Tensor<f32, [M, K]>` with M a parameter) are diagnostics, not
 // miscompiles.
 #include <sys/stat.h>
@@ -481,7 +484,7 @@ class Parser {
       } else if (is_id("unsafe") && peek().t == T::Id && peek().s == "impl") {
         next();
         p.impls.push_back(impl_def());
-      } else if (is_id("extern") || is_id("fn") || is_id("unsafe")) {
+      } else if (is_id("extern") || is_id("fn") || is_id("unsafe") || is_id("async")) {
         p.fns.push_back(fn());
         p.fns.back().is_test = pending_test_;
         pending_test_ = false;
@@ -1405,6 +1408,10 @@ class Parser {
     for (;;) {
       const Tok at = cur();
       if (eat_op(".")) {
+        if (is_id("await") && !(peek().t == T::Op && peek().s == "(")) {
+          next();  // `f().await`: an async fn runs to completion where it is awaited (one task)
+          continue;
+        }
         if (at_field_name()) {  // field access: `x.field` / `x.0`
           EP f = mk(Expr::Field, at);
           f->s = cur().s;
@@ -3097,6 +3104,7 @@ class Gen {
       return {(a.t.b == B::F32 ? cn + "f(" : cn + "(") + a.c + ")", a.t};
     }
     if (gfns_.count(n)) return generic_call(e, n, hint);
+    if (n == "yield_now" && !sigs_.count(n) && e->a.empty()) return {"((void)0)", prim(B::Void)};  // one task: nothing to yield to
     if (n == "slice_from_raw" && !sigs_.count(n)) {  // (pointer as i64, length) -> the expected slice type
       if (!is_slice(hint)) fail("AE0520", e->line, e->col, "slice_from_raw needs an expected `&[T]` type");
       if (e->a.size() != 2) fail("AE0541", e->line, e->col, "slice_from_raw takes a pointer and a length");

@@ -196,4 +196,4 @@ def test_reference_runtime_witnesses(tmp_path):
         else:
             wrong.append(name)
     assert not train_missing, train_missing
-    assert cuda_compiled >= 21 and passed >= 268, (cuda_compiled, passed, wrong)
+    assert cuda_compiled >= 21 and passed >= 270, (cuda_compiled, passed, wrong)
