@@ -512,7 +512,7 @@ void walk(const std::string& dir, std::vector<std::string>& files) {
   while (dirent* e = readdir(d)) {
     const std::string n = e->d_name;
     if (n == "." || n == ".." || n[0] == '.' || n == "__pycache__" || n == "_build" || n == "build" ||
-        n == "_work" || n == "gpurun_out" || n == "baseline")
+        n == "_work" || (n.size() > 4 && n.compare(n.size() - 4, 4, "_out") == 0) || n == "baseline")
       continue;
     const std::string p = dir + "/" + n;
     struct stat st;
